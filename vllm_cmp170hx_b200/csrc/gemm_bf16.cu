@@ -1,0 +1,398 @@
+// Dense bf16 GEMM on tcgen05:  C[M, N] = A[M, K] . B[N, K]^T  (fp32 accumulate).
+//
+// This is the dense projection engine of the package (the role cuBLAS plays
+// for upstream vLLM's `F.linear`; the reference's thin-M BF16 GEMM family,
+// vllm_sm80/kernels/thin_gemm/thin_gemm_v74.py:616, solves the same problem
+// on sm_80 with split-K mma.sync).  B200 design:
+//
+//   * persistent grid, one CTA per SM, 6 warps:
+//       warp 0      TMA producer (A and B tiles, 128-byte swizzle, K step 64)
+//       warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//       warps 2..5  epilogue: tcgen05.ld 32x32b, convert, store
+//   * two TMEM accumulators (2 x BN fp32 columns) so the epilogue of tile i
+//     overlaps the MMAs of tile i+1;
+//   * split-K over the grid for decode shapes (few output tiles): each split
+//     writes fp32 partials, a second kernel sums them in a fixed order
+//     (deterministic);
+//   * "swap" mode for small M: the host passes the weight as A (its output
+//     features fill the 128-row MMA M dimension) and the activations as B, and
+//     the epilogue writes the transposed tile (coalesced along the lanes).
+//
+// Every wait is bounded (common.cuh); a timed-out wait records an error bit
+// in `status` and the CTA unwinds after draining its own in-flight copies.
+#include "common.cuh"
+#include <algorithm>
+
+#include "launch.h"
+#include "tma_host.h"
+
+namespace b200 {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;  // power of two for BN in {16..256}
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+};
+
+struct Params {
+  int M, N, K;
+  int ldc;            // row stride of C (elements)
+  int transpose_out;  // 1: tile (m, n) is stored at C[n * ldc + m]
+  int splits;         // K splits; >1 writes fp32 partials to `partial`
+  int k_blocks_per_split;
+  int m_tiles, n_tiles;
+  __nv_bfloat16* C;
+  float* partial;  // [splits, M, N] (in the output's orientation) when splits > 1
+  const __nv_bfloat16* bias;  // optional [N] (out features), added in the epilogue when splits == 1
+  uint32_t* status;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                        Params p) {
+  using C_ = Cfg<BN>;
+  constexpr int S = C_::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + S * C_::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C_::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* drain = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C_::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_mn = p.m_tiles * p.n_tiles;
+  const int total = tiles_mn * p.splits;
+  const int kb_total = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int split = t / tiles_mn;
+        const int mn = t % tiles_mn;
+        const int mt = mn % p.m_tiles;
+        const int nt = mn / p.m_tiles;
+        const int kb0 = split * p.k_blocks_per_split;
+        const int kb1 = min(kb_total, kb0 + p.k_blocks_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+          tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
+          tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // Drain: the most recent load of every stage must land before exit.
+        const uint32_t n = issued < (uint32_t)S ? issued : (uint32_t)S;
+        for (uint32_t i = 0; i < n; ++i) {
+          const uint32_t k = issued - 1 - i;
+          mbar_wait(&full[k % S], (k / S) & 1, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, 1 /*bf16*/);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
+        const int split = t / tiles_mn;
+        const int kb0 = split * p.k_blocks_per_split;
+        const int kb1 = min(kb_total, kb0 + p.k_blocks_per_split);
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_or_abort(&tempty[acc], acc_phase ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_or_abort(&full[stage], phase, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = desc_kmajor_sw128(smem_a + stage * C_::A_BYTES);
+          const uint64_t db = desc_kmajor_sw128(smem_b + stage * C_::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // +32 bytes per 16-element K step inside the 128-byte swizzle row.
+            umma_f16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (!ok) *abort_flag = 1;
+      // Every MMA this thread issued has completed once `drain` flips.
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+      const int split = t / tiles_mn;
+      const int mn = t % tiles_mn;
+      const int mt = mn % p.m_tiles;
+      const int nt = mn / p.m_tiles;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_or_abort(&tfull[acc], acc_phase, p.status, abort_flag)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mt * BM + q * 32 + lane;  // A row == TMEM lane
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c, r);
+        tmem_wait_ld();
+        const int col0 = nt * BN + c;
+        if (row < p.M) {
+          if (p.splits > 1) {
+            // fp32 partials in output orientation
+            float* dst = p.partial + (size_t)split * p.M * p.N;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int col = col0 + j;
+              if (col < p.N) {
+                const size_t off = p.transpose_out ? (size_t)col * p.M + row : (size_t)row * p.N + col;
+                dst[off] = __uint_as_float(r[j]);
+              }
+            }
+          } else if (p.transpose_out) {
+            const float bias = p.bias ? __bfloat162float(p.bias[row]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int col = col0 + j;
+              if (col < p.N) p.C[(size_t)col * p.ldc + row] = __float2bfloat16(__uint_as_float(r[j]) + bias);
+            }
+          } else {
+            __nv_bfloat16* dst = p.C + (size_t)row * p.ldc + col0;
+            if (col0 + 16 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) && p.bias == nullptr) {
+              uint4 v0, v1;
+              v0.x = pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1]));
+              v0.y = pack_bf16x2(__uint_as_float(r[2]), __uint_as_float(r[3]));
+              v0.z = pack_bf16x2(__uint_as_float(r[4]), __uint_as_float(r[5]));
+              v0.w = pack_bf16x2(__uint_as_float(r[6]), __uint_as_float(r[7]));
+              v1.x = pack_bf16x2(__uint_as_float(r[8]), __uint_as_float(r[9]));
+              v1.y = pack_bf16x2(__uint_as_float(r[10]), __uint_as_float(r[11]));
+              v1.z = pack_bf16x2(__uint_as_float(r[12]), __uint_as_float(r[13]));
+              v1.w = pack_bf16x2(__uint_as_float(r[14]), __uint_as_float(r[15]));
+              reinterpret_cast<uint4*>(dst)[0] = v0;
+              reinterpret_cast<uint4*>(dst)[1] = v1;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int col = col0 + j;
+                if (col < p.N) {
+                  const float bias = p.bias ? __bfloat162float(p.bias[col]) : 0.f;
+                  dst[j] = __float2bfloat16(__uint_as_float(r[j]) + bias);
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+}
+
+// Sum of split-K partials in split order, plus optional bias, to bf16.
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ C, int rows,
+                                     int cols, int ldc, int splits, const __nv_bfloat16* __restrict__ bias,
+                                     int bias_on_rows) {
+  const size_t n = (size_t)rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += partial[(size_t)k * n + i];
+    const int r = i / cols, c = i % cols;
+    if (bias) s += __bfloat162float(bias[bias_on_rows ? r : c]);
+    C[(size_t)r * ldc + c] = __float2bfloat16(s);
+  }
+}
+
+template <int BN>
+cudaError_t launch(const void* A, int64_t lda, int rows_a, const void* B, int64_t ldb, int rows_b, int K,
+                   const Params& p, cudaStream_t stream, int grid) {
+  using C_ = Cfg<BN>;
+  CUtensorMap ta = make_tma_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_a, K, lda, BM, BK,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_b, K, ldb, BN, BK,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kern = gemm_bf16_tn_kernel<BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, C_::SMEM_BYTES, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace gemm
+
+int device_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// Number of K splits the launcher uses for this shape (splits_req > 0 forces it).
+int gemm_bf16_splits(int M, int N, int K, int splits_req) {
+  using namespace gemm;
+  const bool swap = M <= 128;
+  const int Ma = swap ? N : M;
+  const int Nb = swap ? M : N;
+  const int bn = swap ? (Nb <= 16 ? 16 : Nb <= 32 ? 32 : Nb <= 64 ? 64 : 128) : 256;
+  const int tiles = ((Ma + BM - 1) / BM) * ((Nb + bn - 1) / bn);
+  const int kb_total = (K + BK - 1) / BK;
+  const int sms = device_sm_count();
+  int splits = 1;
+  if (splits_req > 0) {
+    splits = splits_req;
+  } else if (tiles < sms) {
+    splits = std::max(1, std::min(sms / tiles, kb_total / 4));
+  }
+  splits = std::max(1, std::min(splits, kb_total));
+  const int per = (kb_total + splits - 1) / splits;
+  return (kb_total + per - 1) / per;
+}
+
+cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
+  using namespace gemm;
+  if (a.M == 0 || a.N == 0) return cudaSuccess;
+  if (a.K % 8 != 0) return cudaErrorInvalidValue;
+  const int sms = device_sm_count();
+  // Small M: weights fill the 128-row MMA dimension, tokens the N dimension.
+  const bool swap = a.M <= 128;
+  const void* A = swap ? a.w : a.x;
+  const void* B = swap ? a.x : a.w;
+  const int64_t lda = swap ? a.ldw : a.ldx;
+  const int64_t ldb = swap ? a.ldx : a.ldw;
+  const int Ma = swap ? a.N : a.M;
+  const int Nb = swap ? a.M : a.N;
+  const int bn = swap ? (Nb <= 16 ? 16 : Nb <= 32 ? 32 : Nb <= 64 ? 64 : 128) : 256;
+  Params p{};
+  p.M = Ma;
+  p.N = Nb;
+  p.K = a.K;
+  p.ldc = (int)a.ldc;
+  p.transpose_out = swap ? 1 : 0;
+  p.m_tiles = (Ma + BM - 1) / BM;
+  p.n_tiles = (Nb + bn - 1) / bn;
+  const int kb_total = (a.K + BK - 1) / BK;
+  const int splits = gemm_bf16_splits(a.M, a.N, a.K, a.splits);
+  p.k_blocks_per_split = (kb_total + splits - 1) / splits;
+  p.splits = splits;
+  p.C = reinterpret_cast<__nv_bfloat16*>(a.c);
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  p.status = a.status;
+  if (splits > 1) {
+    if (a.partial == nullptr || a.partial_cap < (int64_t)splits * a.M * a.N) return cudaErrorInvalidValue;
+    p.partial = a.partial;
+    p.bias = nullptr;
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = std::min(tiles * splits, sms);
+  cudaError_t e;
+  switch (bn) {
+    case 16: e = launch<16>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid); break;
+    case 32: e = launch<32>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid); break;
+    case 64: e = launch<64>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid); break;
+    case 128: e = launch<128>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid); break;
+    default: e = launch<256>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid); break;
+  }
+  if (e != cudaSuccess || splits == 1) return e;
+  // partial is [splits, M, N] in output orientation.
+  const int threads = 256;
+  const int blocks = (int)std::min<int64_t>(((int64_t)a.M * a.N + threads - 1) / threads, (int64_t)sms * 8);
+  splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(p.partial, p.C, a.M, a.N, (int)a.ldc, splits,
+                                                       reinterpret_cast<const __nv_bfloat16*>(a.bias), 0);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -1,0 +1,12 @@
+// pybind11 bindings of the host-side C++ runtime (no device code here).
+#include <torch/extension.h>
+
+#include "ops.h"
+
+namespace b200 {
+
+void register_host_bindings(pybind11::module_& m) {
+  m.attr("ARCH") = "sm_100a";
+}
+
+}  // namespace b200

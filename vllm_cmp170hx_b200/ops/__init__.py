@@ -1,0 +1,62 @@
+"""Python entry points of the sm_100a kernels.
+
+Each function takes CUDA tensors to the native kernel (``torch.ops.b200.*``,
+built from ``csrc/``) and CPU tensors to the plain-PyTorch oracle of the same
+op (``vllm_cmp170hx_b200.oracle``), which is how the engine runs in CPU tests.
+There is no third path: a CUDA tensor never falls back to eager PyTorch, and a
+missing extension raises on first use.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _ext
+from ..oracle import basic as _ref
+
+
+def _native(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         splits: int = 0) -> torch.Tensor:
+    """y = x @ w^T (+ bias), bf16 in/out, fp32 accumulate (tcgen05 on GPU)."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    if not _native(x2):
+        y = _ref.linear(x2, w, bias)
+        if out is not None:
+            out.view(-1, w.shape[0]).copy_(y)
+            return out
+        return y.view(*lead, w.shape[0])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(*lead, w.shape[0], dtype=torch.bfloat16, device=x.device)
+    o2 = out.view(-1, w.shape[0])
+    _ext.ops().gemm_bf16_out(x2, w, bias, o2, _ext.status_word(x.device), splits)
+    return out
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    if not _native(x):
+        y = _ref.rms_norm(x2, w, eps)
+        if out is not None:
+            out.reshape(-1, x.shape[-1]).copy_(y)
+            return out
+        return y.view(*lead, x.shape[-1])
+    if out is None:
+        out = torch.empty(*lead, x.shape[-1], dtype=x.dtype, device=x.device)
+    _ext.ops().rms_norm_out(out.view(-1, x.shape[-1]) if out.dim() != 2 else out, x2, w, eps)
+    return out
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+    """In place: residual += x; x = rms_norm(residual) * w."""
+    if not _native(x):
+        _ref.fused_add_rms_norm(x, residual, w, eps)
+        return
+    _ext.ops().fused_add_rms_norm(x, residual, w, eps)
