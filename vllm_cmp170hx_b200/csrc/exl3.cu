@@ -1,0 +1,603 @@
+// EXL3 trellis-quantised linear layers and MoE experts on tcgen05.
+//
+// Reference behaviour: csrc/exl3/{dense.cu,moe.cu,moe_v2.cu,reference.cu} of
+// the reference (y = H128(H128(x*suh) @ W) * svh; routed experts with SwiGLU
+// and a weighted combine).  The reference decodes the trellis into mma.sync
+// register fragments (dense_mma.cu:249, moe_v2.cu:443); on sm_100 the MMA
+// reads its operands from shared memory, so here:
+//
+//   * 8 decoder warps read trellis words straight from global memory (one
+//     coalesced 128-byte row per 16x16 tile at 4 bits), decode 8 states per
+//     lane and store fp16 pairs into the UMMA "no swizzle" K-major layout
+//     (8x16-byte core matrices; bank-conflict-free: lane L writes word L);
+//   * a TMA warp stages the (Hadamard-rotated, fp16) activation rows of the
+//     work item with 128-byte swizzle;
+//   * one thread issues tcgen05.mma (M = 128 output features, N = rows of the
+//     item rounded to 16, K = 64 per stage) into TMEM;
+//   * the decoder warps then run the epilogue from TMEM: the output H128 is a
+//     butterfly across the 128 TMEM lanes (shuffles + one shared exchange),
+//     svh scaling, and for the gate/up pass SwiGLU plus the down projection's
+//     input rotation, so the intermediate is written once, already in the
+//     form the down pass consumes.
+//
+// A work item is (local expert, first row, rows <= tile_rows) of the
+// expert-sorted assignment list (router.cu); a dense EXL3 linear is the same
+// kernel with one "expert" whose rows are all tokens.
+#include "common.cuh"
+#include "launch.h"
+#include "tma_host.h"
+
+namespace b200 {
+namespace exl3 {
+
+constexpr int kDecodeWarps = 8;
+constexpr int kThreads = (kDecodeWarps + 2) * 32;  // + TMA warp + MMA warp
+constexpr int BK = 64;                              // K per pipeline stage (4 tile rows)
+constexpr int A_BYTES = 128 * BK * 2;               // one 128 x 64 fp16 operand tile
+constexpr int A_LBO = 2048;                         // bytes between K-adjacent core matrices
+constexpr int A_SBO = 128;                          // bytes between M-adjacent core matrices
+constexpr float kH128 = 0.08838834764831845f;       // 1/sqrt(128)
+
+struct GemmParams {
+  const uint16_t* trellis[2];
+  int64_t trellis_estride[2];  // int16 elements between experts
+  const __half* svh[2];
+  int64_t svh_estride[2];
+  const __half* suh_next;  // gate/up pass: the down matrix's suh (rotation of the intermediate)
+  int64_t suh_next_estride;
+  int K;        // padded input features (multiple of 128)
+  int N;        // padded output features of these matrices (multiple of 128)
+  int bits_x2;
+  int codebook;
+  int tile_rows;  // TMA box rows == max rows per item
+  const int4* items;
+  const int* num_items;
+  void* out;
+  int64_t ld_out;
+  int out_mode;        // 0: fp16 (gate/up intermediate), 1: fp32, 2: bf16
+  float swiglu_limit;  // <= 0: none
+  uint32_t* status;
+};
+
+// ----------------------------------------------------------------------------- codebooks
+template <int CB>
+__device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
+  if constexpr (CB == 2) {
+    const uint32_t p0 = s0 * 0x83DCD12Du, p1 = s1 * 0x83DCD12Du;
+    const uint32_t t0 = __dp4a(p0, 0x01010101u, 0x6400u);
+    const uint32_t t1 = __dp4a(p1, 0x01010101u, 0x6400u);
+    const uint32_t h = __byte_perm(t0, t1, 0x5410);
+    const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x1eee), __ushort_as_half(0x1eee)),
+                              __halves2half2(__ushort_as_half(0xc931), __ushort_as_half(0xc931)));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  } else {
+    const uint32_t p0 = ((s0 * 0xCBAC1FEDu) & 0x8fff8fffu) ^ 0x3b603b60u;
+    const uint32_t p1 = ((s1 * 0xCBAC1FEDu) & 0x8fff8fffu) ^ 0x3b603b60u;
+    const uint32_t lo = __byte_perm(p0, p1, 0x5410);
+    const uint32_t hi = __byte_perm(p0, p1, 0x7632);
+    const __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+}
+
+// 8 states of lane L in a 16x16 tile at 4 bits per weight (bits_x2 = 8):
+// the lane's window is word L-1 (low bits) and word L of the 32-word ring.
+__device__ __forceinline__ void states_b8(uint32_t w_prev, uint32_t w_self, uint32_t (&s)[8]) {
+  s[0] = __funnelshift_r(w_self, w_prev, 28) & 0xffffu;
+  s[1] = __funnelshift_r(w_self, w_prev, 24) & 0xffffu;
+  s[2] = __funnelshift_r(w_self, w_prev, 20) & 0xffffu;
+  s[3] = w_self >> 16;
+  s[4] = (w_self >> 12) & 0xffffu;
+  s[5] = __byte_perm(w_self, 0, 0x4421);
+  s[6] = (w_self >> 4) & 0xffffu;
+  s[7] = w_self & 0xffffu;
+}
+
+// Generic bitrate: lane L's state j starts at ring bit (L*4*b + c_j) mod (128 b)
+// with c_j = (j+1)*(b/2) + (b odd ? (j+1)/2 : 0) - 16.
+__device__ __forceinline__ void states_generic(const uint32_t* __restrict__ words, int b, int lane,
+                                               uint32_t (&s)[8]) {
+  const int ring = 128 * b;
+  const int nwords = 4 * b;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    int c = (j + 1) * (b >> 1) + ((b & 1) ? ((j + 1) >> 1) : 0) - 16;
+    int pos = lane * 4 * b + c;
+    pos = pos < 0 ? pos + ring : pos;
+    pos = pos >= ring ? pos - ring : pos;
+    const int lo = pos >> 5;
+    const int hi = lo + 1 == nwords ? 0 : lo + 1;
+    const uint32_t w0 = __ldg(words + lo), w1 = __ldg(words + hi);
+    s[j] = __funnelshift_l(w1, w0, pos & 31) >> 16;
+  }
+}
+
+// Decode one 16x16 tile (trellis tile words `tw`) and store it into the A
+// operand stage: tile column `tc` (output features 16*tc..), tile row `tr`
+// (K 16*tr..) of the 64-wide stage.
+template <int CB, bool FAST>
+__device__ __forceinline__ void decode_tile_store(const uint32_t* __restrict__ tw, uint32_t w_self, int b, int lane,
+                                                  uint8_t* a_stage, int tc, int tr) {
+  uint32_t s[8];
+  if constexpr (FAST) {
+    const uint32_t w_prev = __shfl_sync(0xffffffffu, w_self, (lane + 31) & 31);
+    states_b8(w_prev, w_self, s);
+  } else {
+    states_generic(tw, b, lane, s);
+  }
+  const uint32_t v01 = cb_pair<CB>(s[0], s[1]);  // rows 2a, 2a+1   col b
+  const uint32_t v23 = cb_pair<CB>(s[2], s[3]);  // rows 2a+8, 2a+9 col b
+  const uint32_t v45 = cb_pair<CB>(s[4], s[5]);  // rows 2a, 2a+1   col b+8
+  const uint32_t v67 = cb_pair<CB>(s[6], s[7]);  // rows 2a+8, 2a+9 col b+8
+  const uint32_t base = (uint32_t)(tr * 2) * A_LBO + (uint32_t)(tc * 2) * A_SBO + lane * 4;
+  *reinterpret_cast<uint32_t*>(a_stage + base) = v01;
+  *reinterpret_cast<uint32_t*>(a_stage + base + A_LBO) = v23;
+  *reinterpret_cast<uint32_t*>(a_stage + base + A_SBO) = v45;
+  *reinterpret_cast<uint32_t*>(a_stage + base + A_LBO + A_SBO) = v67;
+}
+
+// In-register butterfly over the 128 features held one per thread of a
+// 4-warp group (feature f = 32*q + lane), for NV columns at once.
+template <int NV>
+__device__ __forceinline__ void h128_group(float (&v)[NV], int lane, int q, float* xbuf, int bar_id) {
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+      v[i] = (lane & d) ? (o - v[i]) : (v[i] + o);
+    }
+  }
+  const int f = q * 32 + lane;
+#pragma unroll
+  for (int qb = 1; qb <= 2; qb <<= 1) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) xbuf[i * 128 + f] = v[i];
+    asm volatile("bar.sync %0, 128;" ::"r"(bar_id));
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float o = xbuf[i * 128 + (f ^ (qb * 32))];
+      v[i] = (q & qb) ? (o - v[i]) : (v[i] + o);
+    }
+    asm volatile("bar.sync %0, 128;" ::"r"(bar_id));
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] *= kH128;
+}
+
+template <int NMAT>
+struct Smem {
+  // per stage: NMAT A tiles then NMAT B tiles
+  static int stage_bytes(int tile_rows) { return NMAT * (A_BYTES + tile_rows * 128); }
+  static int stages(int tile_rows) {
+    int s = (200 * 1024 - 16 * 1024) / stage_bytes(tile_rows);
+    return s > 6 ? 6 : s;
+  }
+  static int total(int tile_rows) {
+    return 1024 + stages(tile_rows) * stage_bytes(tile_rows) + 2 * 16 * 128 * 4 /*xbuf*/ + 256 /*barriers*/;
+  }
+};
+
+// NMAT = 2: gate/up pass (writes the rotated SwiGLU intermediate), 1: down / dense.
+template <int NMAT, int CB, bool FAST>
+__global__ void __launch_bounds__(kThreads, 1)
+    exl3_gemm_kernel(const __grid_constant__ CUtensorMap tma_b0, const __grid_constant__ CUtensorMap tma_b1,
+                     GemmParams p, int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int tile_rows = p.tile_rows;
+  const int b_bytes = tile_rows * 128;
+  const int stage_bytes = NMAT * (A_BYTES + b_bytes);
+  float* xbuf = reinterpret_cast<float*>(smem + stages * stage_bytes);  // [2 groups][16][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xbuf + 2 * 16 * 128);
+  uint64_t* full = bars;            // [stages] 8 decoder warps + 1 TMA arrival + tx
+  uint64_t* empty = bars + 6;       // [stages] MMA commit
+  uint64_t* tfull = bars + 12;      // accumulator ready
+  uint64_t* drain = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int tmem_cols_needed = NMAT * tile_rows;
+  const uint32_t tmem_cols = tmem_cols_needed <= 32 ? 32 : tmem_cols_needed <= 64 ? 64 : tmem_cols_needed <= 128 ? 128
+                             : tmem_cols_needed <= 256 ? 256 : 512;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], kDecodeWarps + 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kDecodeWarps + 1) {
+    tmem_alloc(tmem_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = p.N / 128;
+  const int n_items = *p.num_items;
+  const int total = n_items * n_tiles;
+  const int kchunks = p.K / BK;
+  const int kt_per_row = p.N / 16;  // trellis tiles per tile row
+
+  auto a_tile = [&](int stage, int m) { return smem + stage * stage_bytes + m * A_BYTES; };
+  auto b_tile = [&](int stage, int m) { return smem + stage * stage_bytes + NMAT * A_BYTES + m * b_bytes; };
+
+  if (warp < kDecodeWarps) {
+    // =================================================================== decoders + epilogue
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    const int g = warp / 4;  // epilogue warp group
+    const int q = warp % 4;  // TMEM lane quarter
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
+      const int4 it = p.items[u / n_tiles];
+      const int tile = u % n_tiles;
+      const int e = it.x;
+      bool ok = true;
+      for (int kc = 0; kc < kchunks; ++kc) {
+        if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+          const uint32_t* tw_base =
+              reinterpret_cast<const uint32_t*>(p.trellis[m] + (int64_t)e * p.trellis_estride[m]);
+          const int words_per_tile = 4 * p.bits_x2;
+          uint32_t w[4];
+          const uint32_t* tws[4];
+#pragma unroll
+          for (int tr = 0; tr < 4; ++tr) {
+            const int kt = kc * 4 + tr;
+            const int nt = tile * 8 + warp;
+            tws[tr] = tw_base + (int64_t)(kt * kt_per_row + nt) * words_per_tile;
+            if constexpr (FAST) w[tr] = __ldg(tws[tr] + lane);
+          }
+#pragma unroll
+          for (int tr = 0; tr < 4; ++tr)
+            decode_tile_store<CB, FAST>(tws[tr], FAST ? w[tr] : 0u, p.bits_x2, lane, a_tile(stage, m), warp, tr);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[stage]);
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------------- epilogue
+      if (!mbar_wait_or_abort(tfull, local & 1, p.status, abort_flag)) break;
+      tc_fence_after();
+      const int rows = it.z;
+      const int row0 = it.y;
+      const int f = q * 32 + lane;
+      const int feat = tile * 128 + f;
+      float* xb = xbuf + g * 16 * 128;
+      const int nchunks = (rows + 15) / 16;
+      // column chunks alternate between the two warp groups; each group's
+      // named barrier spans its own 4 warps only
+      for (int c = g; c < nchunks; c += 2) {
+        const bool active = true;
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c * 16;
+        if constexpr (NMAT == 2) {
+          uint32_t rg[16], ru[16];
+          tmem_ld16(taddr, rg);
+          tmem_ld16(taddr + tile_rows, ru);
+          tmem_wait_ld();
+          float gv[16], uv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            gv[i] = __uint_as_float(rg[i]);
+            uv[i] = __uint_as_float(ru[i]);
+          }
+          h128_group<16>(gv, lane, q, xb, 1 + g);
+          h128_group<16>(uv, lane, q, xb, 1 + g);
+          const float sg = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
+          const float su = __half2float(p.svh[1][(int64_t)e * p.svh_estride[1] + feat]);
+          const float sn = __half2float(p.suh_next[(int64_t)e * p.suh_next_estride + feat]);
+          const float L = p.swiglu_limit;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float gg = gv[i] * sg, uu = uv[i] * su;
+            if (L > 0.f) {
+              gg = fminf(gg, L);
+              uu = fminf(fmaxf(uu, -L), L);
+            }
+            gv[i] = siluf_(gg) * uu * sn;
+          }
+          h128_group<16>(gv, lane, q, xb, 1 + g);
+          if (active) {
+            __half* out = reinterpret_cast<__half*>(p.out);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int r = c * 16 + i;
+              if (r < rows) out[(int64_t)(row0 + r) * p.ld_out + feat] = __float2half_rn(gv[i]);
+            }
+          }
+        } else {
+          uint32_t ra[16];
+          tmem_ld16(taddr, ra);
+          tmem_wait_ld();
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
+          h128_group<16>(v, lane, q, xb, 1 + g);
+          const float s = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
+          if (active) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int r = c * 16 + i;
+              if (r >= rows) continue;
+              const int64_t o = (int64_t)(row0 + r) * p.ld_out + feat;
+              if (p.out_mode == 1)
+                reinterpret_cast<float*>(p.out)[o] = v[i] * s;
+              else
+                reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(v[i] * s);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  } else if (warp == kDecodeWarps) {
+    // =================================================================== TMA producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tma_b0);
+      if (NMAT == 2) tma_prefetch_desc(&tma_b1);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int4 it = p.items[u / n_tiles];
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], NMAT * b_bytes);
+          tma_load_2d(b_tile(stage, 0), &tma_b0, &full[stage], kc * BK, it.y);
+          if (NMAT == 2) tma_load_2d(b_tile(stage, 1), &tma_b1, &full[stage], kc * BK, it.y);
+          ++issued;
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        const uint32_t n = issued < (uint32_t)stages ? issued : (uint32_t)stages;
+        for (uint32_t i = 0; i < n; ++i) {
+          const uint32_t k = issued - 1 - i;
+          mbar_wait(&full[k % stages], (k / stages) & 1, nullptr);
+        }
+      }
+    }
+  } else {
+    // =================================================================== MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int4 it = p.items[u / n_tiles];
+        const int n_pad = (it.z + 15) / 16 * 16;
+        const uint32_t idesc = make_idesc_f16(128, n_pad, 0 /*f16*/);
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!mbar_wait_or_abort(&full[stage], phase, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m) {
+            const uint32_t d = tmem_base + m * tile_rows;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t da = make_smem_desc(smem_u32(a_tile(stage, m)) + k * 2 * A_LBO, A_LBO, A_SBO,
+                                                 kSwizzleNone);
+              const uint64_t db = desc_kmajor_sw128(b_tile(stage, m)) + 2 * k;
+              umma_f16(d, da, db, idesc, (kc > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull);
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kDecodeWarps + 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tmem_cols);
+  }
+}
+
+// ----------------------------------------------------------------------------- input rotation
+// out[r, :] = fp16( H128( x[src_row(r), :] * suh ) ) for each of NMAT suh
+// vectors (per expert).  One warp per (row, 128-block): 4 values per lane,
+// 2 in-register butterfly stages + 5 shuffle stages.
+__global__ void input_rotate_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, int in_features, int K,
+                                    const int* __restrict__ sorted_token, const int* __restrict__ expert_offsets,
+                                    int E_local, const __half* __restrict__ suh0, const __half* __restrict__ suh1,
+                                    int64_t suh_estride, __half* __restrict__ out0, __half* __restrict__ out1,
+                                    int rows) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  const int nblk = K / 128;
+  if (gw >= rows * nblk) return;
+  const int r = gw / nblk, blk = gw % nblk;
+  int e = 0;
+  if (expert_offsets) {  // expert of row r: binary search in offsets
+    int lo = 0, hi = E_local;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) / 2;
+      if (expert_offsets[mid] <= r) lo = mid; else hi = mid;
+    }
+    e = lo;
+  }
+  const int tok = sorted_token ? sorted_token[r] : r;
+  const int c0 = blk * 128 + lane * 4;
+  float xv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = c0 + i;
+    xv[i] = c < in_features ? __bfloat162float(x[(int64_t)tok * ld_x + c]) : 0.f;
+  }
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    const __half* suh = m == 0 ? suh0 : suh1;
+    __half* out = m == 0 ? out0 : out1;
+    if (suh == nullptr) break;
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = xv[i] * __half2float(suh[(int64_t)e * suh_estride + c0 + i]);
+    // in-register: features 4*lane + {0,1,2,3}: distances 1, 2
+    float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+    v[0] = a0 + a2;
+    v[1] = a1 + a3;
+    v[2] = a0 - a2;
+    v[3] = a1 - a3;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+        v[i] = (lane & d) ? (o - v[i]) : (v[i] + o);
+      }
+    }
+    __half2 h01 = __floats2half2_rn(v[0] * kH128, v[1] * kH128);
+    __half2 h23 = __floats2half2_rn(v[2] * kH128, v[3] * kH128);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&h01);
+    pk.y = *reinterpret_cast<uint32_t*>(&h23);
+    *reinterpret_cast<uint2*>(out + (int64_t)r * K + c0) = pk;
+  }
+}
+
+// out[t, :] = sum_j w[t, j] * y[slot[t, j], :]  (+ add[t, :]), fp32 math, fixed j order.
+__global__ void combine_kernel(const float* __restrict__ y, int64_t ld_y, const int* __restrict__ slot_of,
+                               const float* __restrict__ sorted_weight, int k, int H,
+                               const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out,
+                               int64_t ld_out, float* __restrict__ out_f32) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int s = slot_of[(int64_t)t * k + j];
+      if (s >= 0) acc += sorted_weight[s] * y[(int64_t)s * ld_y + c];
+    }
+    if (add) acc += __bfloat162float(add[(int64_t)t * ld_out + c]);
+    if (out_f32)
+      out_f32[(int64_t)t * H + c] = acc;
+    else
+      out[(int64_t)t * ld_out + c] = __float2bfloat16(acc);
+  }
+}
+
+template <int NMAT, int CB, bool FAST>
+cudaError_t launch_gemm(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, cudaStream_t stream,
+                        int grid) {
+  const int stages = Smem<NMAT>::stages(p.tile_rows);
+  if (stages < 1) return cudaErrorInvalidValue;
+  const int smem = Smem<NMAT>::total(p.tile_rows);
+  CUtensorMap m0 = make_tma_2d(b0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b_rows, p.K, p.K, p.tile_rows, BK,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap m1 = NMAT == 2 ? make_tma_2d(b1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b_rows, p.K, p.K, p.tile_rows,
+                                           BK, CU_TENSOR_MAP_SWIZZLE_128B)
+                             : m0;
+  auto kern = exl3_gemm_kernel<NMAT, CB, FAST>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, smem, stream>>>(m0, m1, p, stages);
+  return cudaGetLastError();
+}
+
+template <int NMAT>
+cudaError_t dispatch(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, cudaStream_t s, int grid) {
+  const bool fast = p.bits_x2 == 8;
+  if (p.codebook == 1) {
+    return fast ? launch_gemm<NMAT, 1, true>(p, b0, b1, b_rows, s, grid)
+                : launch_gemm<NMAT, 1, false>(p, b0, b1, b_rows, s, grid);
+  }
+  return fast ? launch_gemm<NMAT, 2, true>(p, b0, b1, b_rows, s, grid)
+              : launch_gemm<NMAT, 2, false>(p, b0, b1, b_rows, s, grid);
+}
+
+}  // namespace exl3
+
+cudaError_t exl3_input_rotate(const void* x, int64_t ld_x, int in_features, int K, const int* sorted_token,
+                              const int* expert_offsets, int E_local, const void* suh0, const void* suh1,
+                              int64_t suh_estride, void* out0, void* out1, int rows, cudaStream_t stream) {
+  if (K % 128) return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  const int warps = rows * (K / 128);
+  const int threads = 256;
+  exl3::input_rotate_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ld_x, in_features, K, sorted_token, expert_offsets, E_local,
+      reinterpret_cast<const __half*>(suh0), reinterpret_cast<const __half*>(suh1), suh_estride,
+      reinterpret_cast<__half*>(out0), reinterpret_cast<__half*>(out1), rows);
+  return cudaGetLastError();
+}
+
+cudaError_t exl3_gemm(const Exl3GemmArgs& a, cudaStream_t stream) {
+  using namespace exl3;
+  if (a.K % 128 || a.N % 128 || a.tile_rows % 16 || a.tile_rows < 16 || a.tile_rows > 256) return cudaErrorInvalidValue;
+  if (a.nmat == 2 && a.tile_rows > 128) return cudaErrorInvalidValue;
+  if (a.bits_x2 < 2 || a.bits_x2 > 16) return cudaErrorInvalidValue;
+  GemmParams p{};
+  for (int m = 0; m < a.nmat; ++m) {
+    p.trellis[m] = reinterpret_cast<const uint16_t*>(a.trellis[m]);
+    p.trellis_estride[m] = a.trellis_estride;
+    p.svh[m] = reinterpret_cast<const __half*>(a.svh[m]);
+    p.svh_estride[m] = a.svh_estride;
+  }
+  p.suh_next = reinterpret_cast<const __half*>(a.suh_next);
+  p.suh_next_estride = a.suh_next_estride;
+  p.K = a.K;
+  p.N = a.N;
+  p.bits_x2 = a.bits_x2;
+  p.codebook = a.codebook;
+  p.tile_rows = a.tile_rows;
+  p.items = reinterpret_cast<const int4*>(a.items);
+  p.num_items = a.num_items;
+  p.out = a.out;
+  p.ld_out = a.ld_out;
+  p.out_mode = a.out_mode;
+  p.swiglu_limit = a.swiglu_limit;
+  p.status = a.status;
+  const int grid = std::max(1, std::min(a.max_work, device_sm_count()));
+  if (a.nmat == 2) return dispatch<2>(p, a.b0, a.b1, a.b_rows, stream, grid);
+  return dispatch<1>(p, a.b0, nullptr, a.b_rows, stream, grid);
+}
+
+cudaError_t moe_combine(const float* y, int64_t ld_y, const int* slot_of, const float* sorted_weight, int T, int k,
+                        int H, const void* add, void* out, int64_t ld_out, float* out_f32, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  exl3::combine_kernel<<<T, 256, 0, stream>>>(y, ld_y, slot_of, sorted_weight, k, H,
+                                              reinterpret_cast<const __nv_bfloat16*>(add),
+                                              reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_f32);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -4,6 +4,7 @@
 // pointers and a stream and return a cudaError_t; the glue turns errors into
 // exceptions.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -38,5 +39,79 @@ cudaError_t rms_norm(void* out, int64_t ld_out, const void* x, int64_t ld_x, con
                      cudaStream_t stream);
 cudaError_t fused_add_rms_norm(void* x, int64_t ld_x, void* residual, int64_t ld_res, const void* w, int T, int H,
                                float eps, cudaStream_t stream);
+
+// ---------------------------------------------------------------- router.cu
+// mode 0 softmax+renorm, 1 sigmoid(+bias select), 2 sqrt(softplus)(+bias select)
+cudaError_t moe_topk(const float* logits, int T, int E, int k, int mode, const float* bias, float scale, int renorm,
+                     int* ids, float* weights, cudaStream_t stream);
+cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, int k, const int* expert_map,
+                                  int E_local, int tile_rows, int* sorted_token, float* sorted_weight, int* slot_of,
+                                  int4* items, int* num_items, int* expert_offsets, int max_items,
+                                  cudaStream_t stream);
+
+// ---------------------------------------------------------------- exl3.cu
+struct Exl3GemmArgs {
+  int nmat;                 // 2: gate/up pass, 1: down / dense
+  const void* trellis[2];   // int16 [E, K/16, N/16, 8*bits_x2]
+  int64_t trellis_estride;  // elements between experts
+  const void* svh[2];       // fp16 [E, N]
+  int64_t svh_estride;
+  const void* suh_next;     // fp16 [E, N] (gate/up pass only): suh of the down matrix
+  int64_t suh_next_estride;
+  int K, N, bits_x2, codebook;
+  const void* b0;           // fp16 [b_rows, K] rotated activations (matrix 0)
+  const void* b1;           // fp16 [b_rows, K] (matrix 1, gate/up pass)
+  int64_t b_rows;
+  int tile_rows;            // rows per work item (<= 128 gate/up, <= 256 down)
+  const int* items;         // int4 [max_items] {expert, row0, rows, 0}
+  const int* num_items;
+  int max_work;             // upper bound of items * (N / 128) (grid size)
+  void* out;
+  int64_t ld_out;
+  int out_mode;             // 0 fp16, 1 fp32, 2 bf16
+  float swiglu_limit;
+  uint32_t* status;
+};
+cudaError_t exl3_gemm(const Exl3GemmArgs& a, cudaStream_t stream);
+cudaError_t exl3_input_rotate(const void* x, int64_t ld_x, int in_features, int K, const int* sorted_token,
+                              const int* expert_offsets, int E_local, const void* suh0, const void* suh1,
+                              int64_t suh_estride, void* out0, void* out1, int rows, cudaStream_t stream);
+cudaError_t moe_combine(const float* y, int64_t ld_y, const int* slot_of, const float* sorted_weight, int T, int k,
+                        int H, const void* add, void* out, int64_t ld_out, float* out_f32, cudaStream_t stream);
+
+// ---------------------------------------------------------------- kda.cu
+struct KdaArgs {
+  int full;  // 1: GLM layer semantics (bf16 inputs, conv, gates, gated norm); 0: core recurrence (fp32)
+  int H, D, num_seqs;
+  const int* cu_seqlens;  // [num_seqs + 1] token ranges
+  const int* state_idx;   // [num_seqs] state slot per sequence (nullptr: identity)
+  const int* has_init;    // [num_seqs] 0 = fresh sequence (zero state/conv window); nullptr: all 1
+  // full mode inputs
+  const __nv_bfloat16* qkv;  // [T, 3*H*D] pre-conv q | k | v
+  int64_t ld_qkv;
+  const __nv_bfloat16* g_raw;  // [T, H*D] decay gate input
+  int64_t ld_g;
+  const __nv_bfloat16* beta_raw;  // [T, H] pre-sigmoid
+  int64_t ld_beta;
+  const __nv_bfloat16* g2;  // [T, H*D] output gate (pre-sigmoid), nullable
+  int64_t ld_g2;
+  __nv_bfloat16* conv_state;     // [slots, 3*H*D, 3]
+  const __nv_bfloat16* conv_w;   // [3*H*D, 4] (nullable: no conv)
+  const __nv_bfloat16* conv_b;   // [3*H*D] nullable
+  const float* a_log;            // [H]
+  const float* g_bias;           // [H*D] nullable
+  float lower_bound;
+  const __nv_bfloat16* norm_w;   // [D] nullable: no gated norm
+  float eps, l2_eps, q_scale;
+  int l2norm;
+  // core mode inputs (fp32, [T, H, D] / [T, H])
+  const float *q_f32, *k_f32, *v_f32, *g_f32, *beta_f32;
+  // state and outputs
+  float* state;  // [slots, H, D(v), D(k)]
+  __nv_bfloat16* out;  // [T, H*D] (ld_out)
+  int64_t ld_out;
+  float* out_f32;  // core mode [T, H, D]
+};
+cudaError_t kda_recurrent(const KdaArgs& a, cudaStream_t stream);
 
 }  // namespace b200

@@ -10,6 +10,25 @@ void gemm_bf16_out(const at::Tensor& x, const at::Tensor& w, const c10::optional
 void rms_norm_out(at::Tensor& out, const at::Tensor& x, const at::Tensor& w, double eps);  // norm.cu
 void fused_add_rms_norm_(at::Tensor& x, at::Tensor& residual, const at::Tensor& w, double eps);  // norm.cu
 
+void moe_topk_op(const at::Tensor& logits, int64_t k, int64_t mode, const c10::optional<at::Tensor>& bias,
+                 double scale, bool renorm, at::Tensor& ids, at::Tensor& weights);  // router.cu
+void moe_build_assignments_op(const at::Tensor& ids, const at::Tensor& weights,
+                              const c10::optional<at::Tensor>& expert_map, int64_t E_local, int64_t tile_rows,
+                              at::Tensor& sorted_token, at::Tensor& sorted_weight, at::Tensor& slot_of,
+                              at::Tensor& items, at::Tensor& num_items, at::Tensor& expert_offsets);  // router.cu
+void exl3_input_rotate_op(const at::Tensor& x, int64_t in_features, const c10::optional<at::Tensor>& sorted_token,
+                          const c10::optional<at::Tensor>& expert_offsets, int64_t E_local, const at::Tensor& suh0,
+                          const c10::optional<at::Tensor>& suh1, at::Tensor& out0,
+                          const c10::optional<at::Tensor>& out1, int64_t rows);  // exl3.cu
+void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<at::Tensor>& trellis1,
+                  const at::Tensor& svh0, const c10::optional<at::Tensor>& svh1,
+                  const c10::optional<at::Tensor>& suh_next, int64_t bits_x2, int64_t codebook, const at::Tensor& b0,
+                  const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
+                  const at::Tensor& num_items, int64_t max_work, at::Tensor& out, int64_t out_mode,
+                  double swiglu_limit, const at::Tensor& status);  // exl3.cu
+void moe_combine_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
+                    const c10::optional<at::Tensor>& add, at::Tensor& out);  // exl3.cu
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -19,9 +38,25 @@ void register_host_bindings(pybind11::module_& m);
 #define B200_OP_SCHEMAS(X)                                                                               \
   X("gemm_bf16_out(Tensor x, Tensor w, Tensor? bias, Tensor(a!) out, Tensor(b!) status, int splits) -> ()") \
   X("rms_norm_out(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()")                                 \
-  X("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor w, float eps) -> ()")
+  X("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor w, float eps) -> ()")                 \
+  X("moe_topk(Tensor logits, int k, int mode, Tensor? bias, float scale, bool renorm, Tensor(a!) ids, "     \
+    "Tensor(b!) weights) -> ()")                                                                         \
+  X("moe_build_assignments(Tensor ids, Tensor weights, Tensor? expert_map, int E_local, int tile_rows, "   \
+    "Tensor(a!) sorted_token, Tensor(b!) sorted_weight, Tensor(c!) slot_of, Tensor(d!) items, "            \
+    "Tensor(e!) num_items, Tensor(f!) expert_offsets) -> ()")                                           \
+  X("exl3_input_rotate(Tensor x, int in_features, Tensor? sorted_token, Tensor? expert_offsets, "          \
+    "int E_local, Tensor suh0, Tensor? suh1, Tensor(a!) out0, Tensor(b!)? out1, int rows) -> ()")          \
+  X("exl3_gemm(int nmat, Tensor trellis0, Tensor? trellis1, Tensor svh0, Tensor? svh1, Tensor? suh_next, " \
+    "int bits_x2, int codebook, Tensor b0, Tensor? b1, int tile_rows, Tensor items, Tensor num_items, "     \
+    "int max_work, Tensor(a!) out, int out_mode, float swiglu_limit, Tensor(b!) status) -> ()")           \
+  X("moe_combine(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
   X("rms_norm_out", b200::rms_norm_out)    \
-  X("fused_add_rms_norm", b200::fused_add_rms_norm_)
+  X("fused_add_rms_norm", b200::fused_add_rms_norm_) \
+  X("moe_topk", b200::moe_topk_op)                    \
+  X("moe_build_assignments", b200::moe_build_assignments_op) \
+  X("exl3_input_rotate", b200::exl3_input_rotate_op)  \
+  X("exl3_gemm", b200::exl3_gemm_op)                  \
+  X("moe_combine", b200::moe_combine_op)

@@ -88,3 +88,141 @@ void fused_add_rms_norm_(at::Tensor& x, at::Tensor& residual, const at::Tensor& 
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+static inline const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+void moe_topk_op(const at::Tensor& logits, int64_t k, int64_t mode, const c10::optional<at::Tensor>& bias,
+                 double scale, bool renorm, at::Tensor& ids, at::Tensor& weights) {
+  B200_CHECK_CUDA(logits);
+  B200_CHECK_DTYPE(logits, at::kFloat);
+  TORCH_CHECK(logits.dim() == 2 && logits.is_contiguous(), "moe_topk: logits [T, E] contiguous fp32");
+  B200_CHECK_DTYPE(ids, at::kInt);
+  B200_CHECK_DTYPE(weights, at::kFloat);
+  const int T = logits.size(0), E = logits.size(1);
+  TORCH_CHECK(ids.numel() == (int64_t)T * k && weights.numel() == (int64_t)T * k, "moe_topk: output size");
+  if (bias.has_value()) {
+    B200_CHECK_DTYPE(*bias, at::kFloat);
+    TORCH_CHECK(bias->numel() == E, "moe_topk: bias size");
+  }
+  c10::cuda::CUDAGuard g(logits.device());
+  B200_LAUNCH(moe_topk(logits.data_ptr<float>(), T, E, (int)k, (int)mode,
+                       bias.has_value() ? bias->data_ptr<float>() : nullptr, (float)scale, renorm ? 1 : 0,
+                       ids.data_ptr<int>(), weights.data_ptr<float>(), cur_stream()));
+}
+
+void moe_build_assignments_op(const at::Tensor& ids, const at::Tensor& weights,
+                              const c10::optional<at::Tensor>& expert_map, int64_t E_local, int64_t tile_rows,
+                              at::Tensor& sorted_token, at::Tensor& sorted_weight, at::Tensor& slot_of,
+                              at::Tensor& items, at::Tensor& num_items, at::Tensor& expert_offsets) {
+  B200_CHECK_CUDA(ids);
+  B200_CHECK_DTYPE(ids, at::kInt);
+  B200_CHECK_DTYPE(weights, at::kFloat);
+  TORCH_CHECK(ids.dim() == 2 && ids.is_contiguous() && weights.sizes() == ids.sizes(), "build: ids [T, k]");
+  const int T = ids.size(0), k = ids.size(1);
+  TORCH_CHECK(sorted_token.numel() >= (int64_t)T * k && sorted_weight.numel() >= (int64_t)T * k &&
+                  slot_of.numel() >= (int64_t)T * k,
+              "build: assignment buffers too small");
+  TORCH_CHECK(items.scalar_type() == at::kInt && items.dim() == 2 && items.size(1) == 4, "build: items [n, 4] int32");
+  TORCH_CHECK(expert_offsets.numel() >= E_local + 1, "build: expert_offsets too small");
+  c10::cuda::CUDAGuard g(ids.device());
+  B200_LAUNCH(moe_build_assignments(
+      ids.data_ptr<int>(), weights.data_ptr<float>(), T, k,
+      expert_map.has_value() ? expert_map->data_ptr<int>() : nullptr, (int)E_local, (int)tile_rows,
+      sorted_token.data_ptr<int>(), sorted_weight.data_ptr<float>(), slot_of.data_ptr<int>(),
+      reinterpret_cast<int4*>(items.data_ptr<int>()), num_items.data_ptr<int>(), expert_offsets.data_ptr<int>(),
+      (int)items.size(0), cur_stream()));
+}
+
+void exl3_input_rotate_op(const at::Tensor& x, int64_t in_features, const c10::optional<at::Tensor>& sorted_token,
+                          const c10::optional<at::Tensor>& expert_offsets, int64_t E_local, const at::Tensor& suh0,
+                          const c10::optional<at::Tensor>& suh1, at::Tensor& out0,
+                          const c10::optional<at::Tensor>& out1, int64_t rows) {
+  B200_CHECK_CUDA(x);
+  B200_CHECK_DTYPE(x, at::kBFloat16);
+  B200_CHECK_DTYPE(suh0, at::kHalf);
+  B200_CHECK_DTYPE(out0, at::kHalf);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "rotate: x rows contiguous");
+  const int K = out0.size(-1);
+  TORCH_CHECK(suh0.size(-1) == K && out0.is_contiguous() && out0.size(0) >= rows, "rotate: geometry");
+  TORCH_CHECK(suh1.has_value() == out1.has_value(), "rotate: suh1/out1 go together");
+  c10::cuda::CUDAGuard g(x.device());
+  B200_LAUNCH(exl3_input_rotate(x.data_ptr(), x.stride(0), (int)in_features, K,
+                                sorted_token.has_value() ? sorted_token->data_ptr<int>() : nullptr,
+                                expert_offsets.has_value() ? expert_offsets->data_ptr<int>() : nullptr, (int)E_local,
+                                suh0.data_ptr(), opt_ptr(suh1), suh0.dim() == 2 ? suh0.stride(0) : 0, out0.data_ptr(),
+                                out1.has_value() ? out1->data_ptr() : nullptr, (int)rows, cur_stream()));
+}
+
+void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<at::Tensor>& trellis1,
+                  const at::Tensor& svh0, const c10::optional<at::Tensor>& svh1,
+                  const c10::optional<at::Tensor>& suh_next, int64_t bits_x2, int64_t codebook, const at::Tensor& b0,
+                  const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
+                  const at::Tensor& num_items, int64_t max_work, at::Tensor& out, int64_t out_mode,
+                  double swiglu_limit, const at::Tensor& status) {
+  B200_CHECK_CUDA(trellis0);
+  TORCH_CHECK(trellis0.scalar_type() == at::kShort && trellis0.dim() == 4 && trellis0.is_contiguous(),
+              "exl3_gemm: trellis [E, K/16, N/16, 8*bits_x2] int16");
+  TORCH_CHECK(trellis0.size(3) == 8 * bits_x2, "exl3_gemm: trellis stride vs bits_x2");
+  const int K = trellis0.size(1) * 16, N = trellis0.size(2) * 16;
+  TORCH_CHECK(nmat == 1 || nmat == 2, "exl3_gemm: nmat");
+  if (nmat == 2) {
+    TORCH_CHECK(trellis1.has_value() && svh1.has_value() && suh_next.has_value() && b1.has_value(),
+                "exl3_gemm: gate/up pass needs both matrices, suh_next and b1");
+    TORCH_CHECK(trellis1->sizes() == trellis0.sizes() && trellis1->is_contiguous(), "exl3_gemm: trellis1");
+    TORCH_CHECK(out.scalar_type() == at::kHalf, "exl3_gemm: gate/up output is fp16");
+  }
+  B200_CHECK_DTYPE(svh0, at::kHalf);
+  B200_CHECK_DTYPE(b0, at::kHalf);
+  TORCH_CHECK(svh0.size(-1) == N && b0.size(-1) == K && b0.is_contiguous(), "exl3_gemm: svh/b geometry");
+  TORCH_CHECK(out.stride(-1) == 1 && out.size(-1) >= N, "exl3_gemm: out");
+  TORCH_CHECK((out_mode == 0 && out.scalar_type() == at::kHalf) || (out_mode == 1 && out.scalar_type() == at::kFloat) ||
+                  (out_mode == 2 && out.scalar_type() == at::kBFloat16),
+              "exl3_gemm: out dtype vs out_mode");
+  c10::cuda::CUDAGuard g(b0.device());
+  Exl3GemmArgs a{};
+  a.nmat = (int)nmat;
+  a.trellis[0] = trellis0.data_ptr();
+  a.trellis[1] = nmat == 2 ? trellis1->data_ptr() : nullptr;
+  a.trellis_estride = trellis0.stride(0);
+  a.svh[0] = svh0.data_ptr();
+  a.svh[1] = nmat == 2 ? svh1->data_ptr() : nullptr;
+  a.svh_estride = svh0.dim() == 2 ? svh0.stride(0) : 0;
+  a.suh_next = opt_ptr(suh_next);
+  a.suh_next_estride = (suh_next.has_value() && suh_next->dim() == 2) ? suh_next->stride(0) : 0;
+  a.K = K;
+  a.N = N;
+  a.bits_x2 = (int)bits_x2;
+  a.codebook = (int)codebook;
+  a.b0 = b0.data_ptr();
+  a.b1 = opt_ptr(b1);
+  a.b_rows = b0.size(0);
+  a.tile_rows = (int)tile_rows;
+  a.items = items.data_ptr<int>();
+  a.num_items = num_items.data_ptr<int>();
+  a.max_work = (int)max_work;
+  a.out = out.data_ptr();
+  a.ld_out = out.stride(0);
+  a.out_mode = (int)out_mode;
+  a.swiglu_limit = (float)swiglu_limit;
+  a.status = status_ptr(status);
+  B200_LAUNCH(exl3_gemm(a, cur_stream()));
+}
+
+void moe_combine_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
+                    const c10::optional<at::Tensor>& add, at::Tensor& out) {
+  B200_CHECK_CUDA(y);
+  B200_CHECK_DTYPE(y, at::kFloat);
+  TORCH_CHECK(y.stride(-1) == 1 && out.stride(-1) == 1, "combine: layout");
+  const int T = out.size(0), H = out.size(1);
+  TORCH_CHECK(slot_of.numel() >= (int64_t)T * k, "combine: slot_of");
+  if (add.has_value()) TORCH_CHECK(add->sizes() == out.sizes() && add->stride(0) == out.stride(0), "combine: add");
+  c10::cuda::CUDAGuard g(y.device());
+  const bool f32 = out.scalar_type() == at::kFloat;
+  B200_LAUNCH(moe_combine(y.data_ptr<float>(), y.stride(0), slot_of.data_ptr<int>(), sorted_weight.data_ptr<float>(),
+                          T, (int)k, H, opt_ptr(add), f32 ? nullptr : out.data_ptr(), out.stride(0),
+                          f32 ? out.data_ptr<float>() : nullptr, cur_stream()));
+}
+
+}  // namespace b200

@@ -1,0 +1,159 @@
+"""MoE routing and EXL3 expert execution.
+
+GPU path (one call = 6 launches, all CUDA-graph capturable, no host sync):
+  moe_topk -> moe_build_assignments (deterministic expert-sorted rows + work
+  items) -> exl3_input_rotate (gate/up input rotations, fp16) -> exl3_gemm
+  gate/up pass (SwiGLU + down-input rotation fused in the epilogue) ->
+  exl3_gemm down pass -> moe_combine (weighted sum over top-k, fixed order).
+CPU path: the fp32 oracle of ``oracle.moe``.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+
+from .. import _ext
+from ..formats import exl3 as fx
+from ..oracle import moe as _ref
+
+
+@dataclasses.dataclass
+class Exl3Experts:
+    """Stacked EXL3 expert weights of one MoE layer on one rank.
+
+    gate/up: trellis [E, H/16, I/16, 8*b], suh [E, H], svh [E, I]
+    down:    trellis [E, I/16, H/16, 8*b], suh [E, I], svh [E, H]
+    ``expert_map`` (int32 [E_global], -1 = not on this rank) for expert parallel.
+    """
+
+    gate_trellis: torch.Tensor
+    up_trellis: torch.Tensor
+    down_trellis: torch.Tensor
+    gate_suh: torch.Tensor
+    up_suh: torch.Tensor
+    down_suh: torch.Tensor
+    gate_svh: torch.Tensor
+    up_svh: torch.Tensor
+    down_svh: torch.Tensor
+    bits_x2: int
+    codebook: int
+    hidden: int
+    intermediate: int
+    expert_map: torch.Tensor | None = None
+    swiglu_limit: float = 0.0
+
+    @property
+    def num_local(self) -> int:
+        return self.gate_trellis.shape[0]
+
+    @staticmethod
+    def from_matrices(gate: list, up: list, down: list, expert_map=None, swiglu_limit=0.0) -> "Exl3Experts":
+        g, u, d = fx.stack_experts(gate), fx.stack_experts(up), fx.stack_experts(down)
+        return Exl3Experts(g["trellis"], u["trellis"], d["trellis"], g["suh"], u["suh"], d["suh"], g["svh"],
+                           u["svh"], d["svh"], gate[0].bits_x2, gate[0].codebook, gate[0].in_features,
+                           gate[0].out_features, expert_map, swiglu_limit)
+
+    def matrices(self, which: str, e: int) -> fx.Exl3Matrix:
+        t = getattr(self, f"{which}_trellis")[e]
+        suh, svh = getattr(self, f"{which}_suh")[e], getattr(self, f"{which}_svh")[e]
+        fin, fout = (self.intermediate, self.hidden) if which == "down" else (self.hidden, self.intermediate)
+        return fx.Exl3Matrix(t, suh, svh, self.bits_x2, self.codebook, fin, fout)
+
+    def to(self, device) -> "Exl3Experts":
+        kw = {f.name: (getattr(self, f.name).to(device) if isinstance(getattr(self, f.name), torch.Tensor) else
+                       getattr(self, f.name)) for f in dataclasses.fields(self)}
+        return Exl3Experts(**kw)
+
+
+def topk(logits: torch.Tensor, k: int, mode: int = 0, bias: torch.Tensor | None = None, scale: float = 1.0,
+         renorm: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    if not logits.is_cuda:
+        return _ref.topk(logits, k, mode, bias, scale, renorm)
+    T = logits.shape[0]
+    ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    lf = logits.float().contiguous()
+    _ext.ops().moe_topk(lf, k, mode, None if bias is None else bias.float().contiguous(), scale, renorm, ids, w)
+    return ids, w
+
+
+def pick_tile_rows(T: int, k: int, E_local: int) -> int:
+    avg = max(1, T * k // max(1, E_local))
+    for t in (16, 32, 64):
+        if avg <= t // 2:
+            return t
+    return 128
+
+
+def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3Experts,
+             add: torch.Tensor | None = None, out_f32: bool = False) -> torch.Tensor:
+    """Routed EXL3 experts: out[t] = sum_j w[t,j] * expert_{ids[t,j]}(x[t]) (+ add[t])."""
+    T, H = x.shape
+    k = ids.shape[1]
+    if not x.is_cuda:
+        cache = getattr(ex, "_dense_cache", None)
+        if cache is None:
+            cache = {}
+            object.__setattr__(ex, "_dense_cache", cache)
+        d = {"gate": [ex.matrices("gate", e) for e in range(ex.num_local)],
+             "up": [ex.matrices("up", e) for e in range(ex.num_local)],
+             "down": [ex.matrices("down", e) for e in range(ex.num_local)],
+             "expert_map": ex.expert_map}
+        y = _ref.exl3_experts(x, ids, weights, d, ex.swiglu_limit or None, cache)
+        if add is not None:
+            y = y + add.float()
+        return y if out_f32 else y.to(x.dtype)
+    ops = _ext.ops()
+    dev = x.device
+    E = ex.num_local
+    Kh = ex.gate_trellis.shape[1] * 16  # padded hidden
+    I = ex.gate_trellis.shape[2] * 16  # padded intermediate
+    Hp = ex.down_trellis.shape[2] * 16  # padded hidden out
+    TK = T * k
+    tile = pick_tile_rows(T, k, E)
+    max_items = E + (TK + tile - 1) // tile
+    i32 = dict(dtype=torch.int32, device=dev)
+    sorted_token = torch.empty(TK, **i32)
+    sorted_weight = torch.empty(TK, dtype=torch.float32, device=dev)
+    slot_of = torch.empty(TK, **i32)
+    items = torch.empty(max_items, 4, **i32)
+    num_items = torch.empty(1, **i32)
+    offsets = torch.empty(E + 1, **i32)
+    ops.moe_build_assignments(ids.contiguous(), weights.float().contiguous(), ex.expert_map, E, tile, sorted_token,
+                              sorted_weight, slot_of, items, num_items, offsets)
+    xg = torch.empty(TK, Kh, dtype=torch.float16, device=dev)
+    xu = torch.empty(TK, Kh, dtype=torch.float16, device=dev)
+    ops.exl3_input_rotate(x, H, sorted_token, offsets, E, ex.gate_suh, ex.up_suh, xg, xu, TK)
+    h = torch.empty(TK, I, dtype=torch.float16, device=dev)
+    st = _ext.status_word(dev)
+    ops.exl3_gemm(2, ex.gate_trellis, ex.up_trellis, ex.gate_svh, ex.up_svh, ex.down_suh, ex.bits_x2, ex.codebook,
+                  xg, xu, tile, items, num_items, max_items * (I // 128), h, 0, float(ex.swiglu_limit or 0.0), st)
+    y = torch.empty(TK, Hp, dtype=torch.float32, device=dev)
+    ops.exl3_gemm(1, ex.down_trellis, None, ex.down_svh, None, None, ex.bits_x2, ex.codebook, h, None, tile, items,
+                  num_items, max_items * (Hp // 128), y, 1, 0.0, st)
+    out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16, device=dev)
+    ops.moe_combine(y, slot_of, sorted_weight, k, add, out)
+    return out
+
+
+def exl3_linear(x: torch.Tensor, m: fx.Exl3Matrix, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """Dense EXL3 linear (one matrix): the MoE kernels with a single expert."""
+    if not x.is_cuda:
+        return fx.linear(x, m).to(out_dtype)
+    ops = _ext.ops()
+    T = x.shape[0]
+    dev = x.device
+    K, N = m.padded_in, m.padded_out
+    tile = 128 if T > 64 else (64 if T > 32 else (32 if T > 16 else 16))
+    n_items = (T + tile - 1) // tile
+    items = torch.tensor([[0, i * tile, min(tile, T - i * tile), 0] for i in range(n_items)], dtype=torch.int32,
+                         device=dev) if T else torch.empty(0, 4, dtype=torch.int32, device=dev)
+    num = torch.tensor([n_items], dtype=torch.int32, device=dev)
+    xr = torch.empty(max(T, 1), K, dtype=torch.float16, device=dev)
+    ops.exl3_input_rotate(x, m.in_features, None, None, 1, m.suh, None, xr, None, T)
+    y = torch.empty(T, N, dtype=torch.float32 if out_dtype == torch.float32 else torch.bfloat16, device=dev)
+    ops.exl3_gemm(1, m.trellis.unsqueeze(0), None, m.svh, None, None, m.bits_x2, m.codebook, xr, None, tile, items,
+                  num, n_items * (N // 128), y, 1 if out_dtype == torch.float32 else 2, 0.0, _ext.status_word(dev))
+    return y[:, : m.out_features]
