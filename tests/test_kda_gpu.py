@@ -1,0 +1,98 @@
+"""KDA recurrent kernel vs the fp64/fp32 references."""
+
+import pytest
+import torch
+
+from vllm_cmp170hx_b200 import _ext
+from vllm_cmp170hx_b200.oracle import kda
+
+pytestmark = pytest.mark.gpu
+
+
+def test_config1_core_gpu():
+    """BASELINE config 1 shapes on the GPU kernel (core mode, fp32 I/O)."""
+    g = torch.Generator().manual_seed(0)
+    B, T, H, D = 4, 64, 8, 128
+    q = torch.randn(B, T, H, D, generator=g)
+    k = torch.randn(B, T, H, D, generator=g)
+    v = torch.randn(B, T, H, D, generator=g)
+    q, k = q / q.norm(dim=-1, keepdim=True), k / k.norm(dim=-1, keepdim=True)
+    gl = torch.nn.functional.logsigmoid(torch.randn(B, T, H, D, generator=g))
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=g))
+    o_ref, S_ref = kda.naive_recurrence(*(x.double() for x in (q, k, v, gl, beta)))
+    ops = _ext.ops()
+    state = torch.zeros(B, H, D, D, device="cuda")
+    has_init = torch.zeros(B, dtype=torch.int32, device="cuda")
+    # one decode step per call, state carried in the pool
+    outs = []
+    for t in range(T):
+        cu = torch.arange(0, B + 1, dtype=torch.int32, device="cuda")
+        o = torch.empty(B, H, D, device="cuda")
+        flat = lambda x: x[:, t].contiguous().cuda()  # noqa: E731
+        ops.kda_core(cu, None, has_init, flat(q), flat(k), flat(v), flat(gl), beta[:, t].contiguous().cuda(), state, o)
+        has_init.fill_(1)
+        outs.append(o.cpu())
+    o = torch.stack(outs, dim=1)
+    torch.cuda.synchronize()
+    assert (o.double() - o_ref).abs().max() < 1e-4
+    assert (state.cpu().double() - S_ref).abs().max() < 1e-4
+
+
+def test_core_prefill_varlen():
+    g = torch.Generator().manual_seed(1)
+    H, D = 4, 128
+    lens = [37, 1, 100]
+    T = sum(lens)
+    q = torch.randn(T, H, D, generator=g); q = q / q.norm(dim=-1, keepdim=True)
+    k = torch.randn(T, H, D, generator=g); k = k / k.norm(dim=-1, keepdim=True)
+    v = torch.randn(T, H, D, generator=g)
+    gl = torch.nn.functional.logsigmoid(torch.randn(T, H, D, generator=g))
+    beta = torch.sigmoid(torch.randn(T, H, generator=g))
+    S0 = torch.randn(3, H, D, D, generator=g) * 0.05
+    cu = torch.tensor([0, 37, 38, 138], dtype=torch.int32)
+    state = S0.clone().cuda()
+    o = torch.empty(T, H, D, device="cuda")
+    _ext.ops().kda_core(cu.cuda(), torch.tensor([2, 0, 1], dtype=torch.int32, device="cuda"), None, q.cuda(), k.cuda(),
+                        v.cuda(), gl.cuda(), beta.cuda(), state, o)
+    for s, slot in enumerate([2, 0, 1]):
+        a, b = int(cu[s]), int(cu[s + 1])
+        o_ref, S_ref = kda.naive_recurrence(*(x[a:b][None].double() for x in (q, k, v, gl, beta)),
+                                            S0[slot][None].double())
+        assert (o[a:b].cpu().double() - o_ref[0]).abs().max() < 1e-4
+        assert (state[slot].cpu().double() - S_ref[0]).abs().max() < 1e-4
+
+
+def test_full_layer_semantics():
+    """conv + gates + L2 norm + recurrence + gated RMSNorm vs the layer oracle."""
+    g = torch.Generator().manual_seed(2)
+    H, D = 2, 128
+    HD = H * D
+    lens = [5, 1, 20]
+    T = sum(lens)
+    cu = torch.tensor([0, 5, 6, 26], dtype=torch.int32)
+    qkv = torch.randn(T, 3 * HD, generator=g).to(torch.bfloat16)
+    g_raw = torch.randn(T, HD, generator=g).to(torch.bfloat16)
+    beta_raw = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    g2 = torch.randn(T, HD, generator=g).to(torch.bfloat16)
+    conv_w = (torch.randn(3 * HD, 4, generator=g) * 0.5).to(torch.bfloat16)
+    a_log = torch.randn(H, generator=g) * 0.5
+    g_bias = torch.randn(HD, generator=g) * 0.1
+    norm_w = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    state = torch.randn(4, H, D, D, generator=g) * 0.05
+    conv_state = torch.randn(4, 3 * HD, 3, generator=g).to(torch.bfloat16)
+    idx = torch.tensor([3, 1, 0], dtype=torch.int32)
+    has_init = torch.tensor([1, 0, 1], dtype=torch.int32)
+    st_r, cs_r = state.clone(), conv_state.clone()
+    ref = kda.kda_layer(qkv, g_raw, beta_raw, g2, cu, st_r, cs_r, idx, has_init, conv_w, None, a_log, g_bias, -5.0,
+                        norm_w)
+    st, cs = state.cuda(), conv_state.cuda()
+    out = torch.empty(T, HD, dtype=torch.bfloat16, device="cuda")
+    _ext.ops().kda_forward(cu.cuda(), idx.cuda(), has_init.cuda(), qkv.cuda(), g_raw.cuda(), beta_raw.cuda(), g2.cuda(),
+                           cs, conv_w.cuda(), None, a_log.cuda(), g_bias.cuda(), -5.0, norm_w.cuda(), 1e-5, 1e-6,
+                           D ** -0.5, True, st, out)
+    torch.cuda.synchronize()
+    rel = ((out.cpu().float() - ref).norm() / ref.norm()).item()
+    assert rel < 1e-2, rel
+    for slot in (3, 1, 0):
+        assert (st[slot].cpu() - st_r[slot]).abs().max() < 1e-3
+        assert torch.equal(cs[slot].cpu(), cs_r[slot])

@@ -29,6 +29,18 @@ void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<
 void moe_combine_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
                     const c10::optional<at::Tensor>& add, at::Tensor& out);  // exl3.cu
 
+void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
+                    const c10::optional<at::Tensor>& has_init, const at::Tensor& qkv, const at::Tensor& g_raw,
+                    const at::Tensor& beta_raw, const c10::optional<at::Tensor>& g2, at::Tensor& conv_state,
+                    const c10::optional<at::Tensor>& conv_w, const c10::optional<at::Tensor>& conv_b,
+                    const at::Tensor& a_log, const c10::optional<at::Tensor>& g_bias, double lower_bound,
+                    const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
+                    at::Tensor& state, at::Tensor& out);  // kda.cu
+void kda_core_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
+                 const c10::optional<at::Tensor>& has_init, const at::Tensor& q, const at::Tensor& k,
+                 const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta, at::Tensor& state,
+                 at::Tensor& out);  // kda.cu
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -49,7 +61,13 @@ void register_host_bindings(pybind11::module_& m);
   X("exl3_gemm(int nmat, Tensor trellis0, Tensor? trellis1, Tensor svh0, Tensor? svh1, Tensor? suh_next, " \
     "int bits_x2, int codebook, Tensor b0, Tensor? b1, int tile_rows, Tensor items, Tensor num_items, "     \
     "int max_work, Tensor(a!) out, int out_mode, float swiglu_limit, Tensor(b!) status) -> ()")           \
-  X("moe_combine(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out) -> ()")
+  X("moe_combine(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out) -> ()") \
+  X("kda_forward(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor qkv, Tensor g_raw, "        \
+    "Tensor beta_raw, Tensor? g2, Tensor(a!) conv_state, Tensor? conv_w, Tensor? conv_b, Tensor a_log, "   \
+    "Tensor? g_bias, float lower_bound, Tensor? norm_w, float eps, float l2_eps, float q_scale, "            \
+    "bool l2norm, Tensor(b!) state, Tensor(c!) out) -> ()")                                               \
+  X("kda_core(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor q, Tensor k, Tensor v, "      \
+    "Tensor g, Tensor beta, Tensor(a!) state, Tensor(b!) out) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -59,4 +77,6 @@ void register_host_bindings(pybind11::module_& m);
   X("moe_build_assignments", b200::moe_build_assignments_op) \
   X("exl3_input_rotate", b200::exl3_input_rotate_op)  \
   X("exl3_gemm", b200::exl3_gemm_op)                  \
-  X("moe_combine", b200::moe_combine_op)
+  X("moe_combine", b200::moe_combine_op)              \
+  X("kda_forward", b200::kda_forward_op)              \
+  X("kda_core", b200::kda_core_op)

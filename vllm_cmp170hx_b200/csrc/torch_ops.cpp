@@ -226,3 +226,91 @@ void moe_combine_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Te
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
+                    const c10::optional<at::Tensor>& has_init, const at::Tensor& qkv, const at::Tensor& g_raw,
+                    const at::Tensor& beta_raw, const c10::optional<at::Tensor>& g2, at::Tensor& conv_state,
+                    const c10::optional<at::Tensor>& conv_w, const c10::optional<at::Tensor>& conv_b,
+                    const at::Tensor& a_log, const c10::optional<at::Tensor>& g_bias, double lower_bound,
+                    const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
+                    at::Tensor& state, at::Tensor& out) {
+  B200_CHECK_CUDA(qkv);
+  B200_CHECK_DTYPE(qkv, at::kBFloat16);
+  B200_CHECK_DTYPE(state, at::kFloat);
+  B200_CHECK_DTYPE(a_log, at::kFloat);
+  TORCH_CHECK(state.dim() == 4 && state.size(2) == 128 && state.size(3) == 128 && state.is_contiguous(),
+              "kda: state [slots, H, 128, 128] fp32");
+  const int H = state.size(1);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) >= 3 * H * 128 && qkv.stride(1) == 1, "kda: qkv [T, 3*H*128]");
+  TORCH_CHECK(g_raw.stride(-1) == 1 && beta_raw.stride(-1) == 1 && out.stride(-1) == 1, "kda: inner strides");
+  TORCH_CHECK(conv_state.is_contiguous() && conv_state.size(1) == 3 * H * 128 && conv_state.size(2) == 3,
+              "kda: conv_state [slots, 3*H*128, 3]");
+  TORCH_CHECK(a_log.numel() == H, "kda: a_log [H]");
+  if (g_bias.has_value()) TORCH_CHECK(g_bias->scalar_type() == at::kFloat && g_bias->numel() == H * 128, "kda: g_bias");
+  c10::cuda::CUDAGuard g(qkv.device());
+  KdaArgs a{};
+  a.full = 1;
+  a.H = H;
+  a.D = 128;
+  a.num_seqs = cu_seqlens.numel() - 1;
+  a.cu_seqlens = cu_seqlens.data_ptr<int>();
+  a.state_idx = state_idx.has_value() ? state_idx->data_ptr<int>() : nullptr;
+  a.has_init = has_init.has_value() ? has_init->data_ptr<int>() : nullptr;
+  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  a.ld_qkv = qkv.stride(0);
+  a.g_raw = reinterpret_cast<const __nv_bfloat16*>(g_raw.data_ptr());
+  a.ld_g = g_raw.stride(0);
+  a.beta_raw = reinterpret_cast<const __nv_bfloat16*>(beta_raw.data_ptr());
+  a.ld_beta = beta_raw.stride(0);
+  a.g2 = g2.has_value() ? reinterpret_cast<const __nv_bfloat16*>(g2->data_ptr()) : nullptr;
+  a.ld_g2 = g2.has_value() ? g2->stride(0) : 0;
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.conv_w = conv_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(conv_w->data_ptr()) : nullptr;
+  a.conv_b = conv_b.has_value() ? reinterpret_cast<const __nv_bfloat16*>(conv_b->data_ptr()) : nullptr;
+  a.a_log = a_log.data_ptr<float>();
+  a.g_bias = g_bias.has_value() ? g_bias->data_ptr<float>() : nullptr;
+  a.lower_bound = (float)lower_bound;
+  a.norm_w = norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr()) : nullptr;
+  a.eps = (float)eps;
+  a.l2_eps = (float)l2_eps;
+  a.q_scale = (float)q_scale;
+  a.l2norm = l2norm ? 1 : 0;
+  a.state = state.data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ld_out = out.stride(0);
+  B200_LAUNCH(kda_recurrent(a, cur_stream()));
+}
+
+void kda_core_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
+                 const c10::optional<at::Tensor>& has_init, const at::Tensor& q, const at::Tensor& k,
+                 const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta, at::Tensor& state, at::Tensor& out) {
+  B200_CHECK_CUDA(q);
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &g, &out}) {
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 3 && t->size(2) == 128,
+                "kda_core: fp32 [T, H, 128] contiguous");
+  }
+  TORCH_CHECK(beta.scalar_type() == at::kFloat && beta.is_contiguous(), "kda_core: beta fp32 [T, H]");
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 4, "kda_core: state");
+  c10::cuda::CUDAGuard gd(q.device());
+  KdaArgs a{};
+  a.full = 0;
+  a.H = q.size(1);
+  a.D = 128;
+  a.num_seqs = cu_seqlens.numel() - 1;
+  a.cu_seqlens = cu_seqlens.data_ptr<int>();
+  a.state_idx = state_idx.has_value() ? state_idx->data_ptr<int>() : nullptr;
+  a.has_init = has_init.has_value() ? has_init->data_ptr<int>() : nullptr;
+  a.q_f32 = q.data_ptr<float>();
+  a.k_f32 = k.data_ptr<float>();
+  a.v_f32 = v.data_ptr<float>();
+  a.g_f32 = g.data_ptr<float>();
+  a.beta_f32 = beta.data_ptr<float>();
+  a.q_scale = 1.f;
+  a.state = state.data_ptr<float>();
+  a.out_f32 = out.data_ptr<float>();
+  B200_LAUNCH(kda_recurrent(a, cur_stream()));
+}
+
+}  // namespace b200
