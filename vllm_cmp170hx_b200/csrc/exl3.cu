@@ -244,7 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = it.x;
       bool ok = true;
       for (int kc = 0; kc < kchunks; ++kc) {
-        if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag)) {
+        const bool got = mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
@@ -276,7 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
-      if (!mbar_wait_or_abort(tfull, local & 1, p.status, abort_flag)) break;
+      const bool got = mbar_wait_or_abort(tfull, local & 1, p.status, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) break;  // TMEM loads are warp-collective
       tc_fence_after();
       const int rows = it.z;
       const int row0 = it.y;

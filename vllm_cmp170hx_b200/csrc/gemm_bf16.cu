@@ -205,7 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nt = mn / p.m_tiles;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait_or_abort(&tfull[acc], acc_phase, p.status, abort_flag)) {
+      // TMEM loads are warp-collective: leave together
+      const bool got = mbar_wait_or_abort(&tfull[acc], acc_phase, p.status, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
         *abort_flag = 1;
         break;
       }

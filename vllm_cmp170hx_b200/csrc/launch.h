@@ -114,4 +114,27 @@ struct KdaArgs {
 };
 cudaError_t kda_recurrent(const KdaArgs& a, cudaStream_t stream);
 
+// ---------------------------------------------------------------- mla_prep.cu / mla_attn.cu
+cudaError_t rope_apply(void* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
+                       const int* positions, const float* cos_sin, int interleaved, int T, cudaStream_t stream);
+cudaError_t mla_latent_cache_write(const void* kv, int64_t ld_kv, const void* norm_w, float eps, const int* positions,
+                                   const float* cos_sin, int interleaved, const int64_t* slots, void* cache, int T,
+                                   cudaStream_t stream);
+cudaError_t mla_index_k_write(const void* k, int64_t ld_k, const void* ln_w, const void* ln_b, float eps,
+                              const int* positions, const float* cos_sin, int rope_dim, int interleaved,
+                              const int64_t* slots, void* cache, float* cache_scale, int T, cudaStream_t stream);
+cudaError_t mla_index_q_prep(const void* q, int64_t ld_tok, int nheads, const int* positions, const float* cos_sin,
+                             int rope_dim, int interleaved, const void* w, int64_t ld_w, float wscale, void* q8,
+                             float* w_out, int T, cudaStream_t stream);
+cudaError_t mla_topk(const float* scores, int64_t ld_scores, const int* ctx_lens, int k, const int* token_seq,
+                     const int* block_table, int64_t ld_bt, int block_size, int* out_idx, int* out_count, int T,
+                     cudaStream_t stream);
+cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void* k_cache, int64_t num_slots,
+                               const float* k_scale, const int* ctx_lens, const int* token_seq, const int* block_table,
+                               int64_t ld_bt, float* scores, int64_t ld_scores, int max_ctx, uint32_t* status,
+                               cudaStream_t stream);
+cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache, const int* indices, const int* counts,
+                                 int topk, float sm_scale, int splits, void* out, float* part_o, float* part_ml,
+                                 float* lse, uint32_t* status, cudaStream_t stream);
+
 }  // namespace b200

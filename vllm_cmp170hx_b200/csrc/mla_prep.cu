@@ -1,0 +1,372 @@
+// Sparse-MLA glue kernels: RoPE, latent KV-cache write, indexer key/query
+// preparation and the canonical top-k selection.
+//
+// Reference behaviour: the DeepSeek-style sparse attention of
+// vllm_sm80/models/deepseek_v41/ops/sm80_attn_core.py (RMSNorm + RoPE of the
+// latent, indexer keys with LayerNorm + RoPE + Hadamard + fp8, top-k with
+// "lowest index wins ties, selection sorted ascending", lines 17-33) and the
+// GLM indexer glue (vllm_sm80/models/glm5next/ops/idx_glue.py: FWHT128 + fp8
+// quant with weight scale, latent-cache write merged into the index path).
+#include "common.cuh"
+#include "launch.h"
+
+namespace b200 {
+namespace mla {
+
+constexpr float kH128 = 0.08838834764831845f;
+constexpr float kFp8Max = 448.f;
+
+// rotary pair (x1, x2) -> (x1 c - x2 s, x2 c + x1 s)
+__device__ __forceinline__ void rot(float& a, float& b, float c, float s) {
+  const float x1 = a, x2 = b;
+  a = x1 * c - x2 * s;
+  b = x2 * c + x1 * s;
+}
+
+// In place RoPE on rot_dim dims at `offset` of every head of every token.
+// cos_sin: [max_pos, rot_dim] fp32 = [cos(rot_dim/2) | sin(rot_dim/2)].
+// interleaved: pairs (2i, 2i+1); else NeoX pairs (i, i + rot_dim/2).
+__global__ void rope_kernel(__nv_bfloat16* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
+                            const int* __restrict__ positions, const float* __restrict__ cos_sin, int interleaved,
+                            int T) {
+  const int half = rot_dim / 2;
+  const int64_t total = (int64_t)T * nheads * half;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int j = i % half;
+    const int h = (i / half) % nheads;
+    const int t = i / ((int64_t)half * nheads);
+    const float* cs = cos_sin + (int64_t)positions[t] * rot_dim;
+    const float c = cs[j], s = cs[half + j];
+    __nv_bfloat16* p = x + t * ld_tok + h * ld_head + offset;
+    const int i1 = interleaved ? 2 * j : j;
+    const int i2 = interleaved ? 2 * j + 1 : j + half;
+    float a = __bfloat162float(p[i1]), b = __bfloat162float(p[i2]);
+    rot(a, b, c, s);
+    p[i1] = __float2bfloat16(a);
+    p[i2] = __float2bfloat16(b);
+  }
+}
+
+// Latent cache row = [RMSNorm(kv[:512]) * w | RoPE(kv[512:576])] (one warp per token).
+__global__ void latent_cache_write_kernel(const __nv_bfloat16* __restrict__ kv, int64_t ld_kv,
+                                          const __nv_bfloat16* __restrict__ norm_w, float eps,
+                                          const int* __restrict__ positions, const float* __restrict__ cos_sin,
+                                          int interleaved, const int64_t* __restrict__ slots,
+                                          __nv_bfloat16* __restrict__ cache, int T) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  const int64_t slot = slots[t];
+  if (slot < 0) return;
+  const __nv_bfloat16* row = kv + (int64_t)t * ld_kv;
+  float c[16];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    c[i] = __bfloat162float(row[lane * 16 + i]);
+    ss += c[i] * c[i];
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / 512.f + eps);
+  __nv_bfloat16* dst = cache + slot * 576;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) dst[lane * 16 + i] = __float2bfloat16(c[i] * inv * __bfloat162float(norm_w[lane * 16 + i]));
+  // rope over the 64 rope dims: lane owns pair j = lane
+  const float* cs = cos_sin + (int64_t)positions[t] * 64;
+  const float cc = cs[lane], sn = cs[32 + lane];
+  const int i1 = interleaved ? 2 * lane : lane, i2 = interleaved ? 2 * lane + 1 : lane + 32;
+  float a = __bfloat162float(row[512 + i1]), b = __bfloat162float(row[512 + i2]);
+  rot(a, b, cc, sn);
+  dst[512 + i1] = __float2bfloat16(a);
+  dst[512 + i2] = __float2bfloat16(b);
+}
+
+// 128-dim vector held 4 per lane (dims 4*lane + i): H128 in place.
+__device__ __forceinline__ void h128_warp(float (&v)[4], int lane) {
+  float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+  v[0] = a0 + a2;
+  v[1] = a1 + a3;
+  v[2] = a0 - a2;
+  v[3] = a1 - a3;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+      v[i] = (lane & d) ? (o - v[i]) : (v[i] + o);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] *= kH128;
+}
+
+// RoPE (first rope_dim dims, pairs held within a lane for interleaved, or
+// across lanes for NeoX) on a 4-per-lane 128-vector.
+__device__ __forceinline__ void rope_warp(float (&v)[4], int lane, const float* cs, int rope_dim, int interleaved) {
+  const int half = rope_dim / 2;
+  if (interleaved) {
+    // pairs (4l, 4l+1), (4l+2, 4l+3) -> pair ids 2l, 2l+1
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      const int j = 2 * lane + pr;
+      if (4 * lane + 2 * pr + 1 < rope_dim) rot(v[2 * pr], v[2 * pr + 1], cs[j], cs[half + j]);
+    }
+  } else {
+    // pair (j, j + half): dims 4l+i for 4l+i < half pair with dims 4l+i+half
+    const int lanes_half = half / 4;  // partner lane offset
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float other = __shfl_sync(0xffffffffu, v[i], lane < lanes_half ? lane + lanes_half : lane - lanes_half);
+      const int d = 4 * lane + i;
+      if (d < half) {
+        v[i] = v[i] * cs[d] - other * cs[half + d];
+      } else if (d < rope_dim) {
+        const int j = d - half;
+        v[i] = v[i] * cs[j] + other * cs[half + j];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  __nv_fp8x4_e4m3 q(make_float4(a, b, c, d));
+  return *reinterpret_cast<uint32_t*>(&q);
+}
+
+// Indexer keys: LayerNorm(k) * w + b -> RoPE -> H128 -> e4m3 with a per-token scale.
+__global__ void index_k_write_kernel(const __nv_bfloat16* __restrict__ k, int64_t ld_k,
+                                     const __nv_bfloat16* __restrict__ ln_w, const __nv_bfloat16* __restrict__ ln_b,
+                                     float eps, const int* __restrict__ positions, const float* __restrict__ cos_sin,
+                                     int rope_dim, int interleaved, const int64_t* __restrict__ slots,
+                                     uint8_t* __restrict__ cache, float* __restrict__ cache_scale, int T) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  const int64_t slot = slots[t];
+  if (slot < 0) return;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(k[(int64_t)t * ld_k + lane * 4 + i]);
+  float mean = warp_sum(v[0] + v[1] + v[2] + v[3]) / 128.f;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) var += (v[i] - mean) * (v[i] - mean);
+  var = warp_sum(var) / 128.f;
+  const float inv = rsqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = lane * 4 + i;
+    v[i] = (v[i] - mean) * inv * (ln_w ? __bfloat162float(ln_w[d]) : 1.f) + (ln_b ? __bfloat162float(ln_b[d]) : 0.f);
+    v[i] = __bfloat162float(__float2bfloat16(v[i]));
+  }
+  rope_warp(v, lane, cos_sin + (int64_t)positions[t] * rope_dim, rope_dim, interleaved);
+  h128_warp(v, lane);
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = amax > 0.f ? amax / kFp8Max : 1.f;
+  const float rs = 1.f / scale;
+  reinterpret_cast<uint32_t*>(cache + slot * 128)[lane] = pack_e4m3x4(v[0] * rs, v[1] * rs, v[2] * rs, v[3] * rs);
+  if (lane == 0) cache_scale[slot] = scale;
+}
+
+// Indexer queries: per (token, head): RoPE -> H128 -> e4m3 with scale; the
+// head weight absorbs the scale: w_out = w * wscale * scale.
+__global__ void index_q_prep_kernel(const __nv_bfloat16* __restrict__ q, int64_t ld_tok, int nheads,
+                                    const int* __restrict__ positions, const float* __restrict__ cos_sin, int rope_dim,
+                                    int interleaved, const __nv_bfloat16* __restrict__ w, int64_t ld_w, float wscale,
+                                    uint8_t* __restrict__ q8, float* __restrict__ w_out, int T) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= T * nheads) return;
+  const int t = gw / nheads, h = gw % nheads;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(q[(int64_t)t * ld_tok + h * 128 + lane * 4 + i]);
+  rope_warp(v, lane, cos_sin + (int64_t)positions[t] * rope_dim, rope_dim, interleaved);
+  h128_warp(v, lane);
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = amax > 0.f ? amax / kFp8Max : 1.f;
+  const float rs = 1.f / scale;
+  reinterpret_cast<uint32_t*>(q8 + ((int64_t)t * nheads + h) * 128)[lane] =
+      pack_e4m3x4(v[0] * rs, v[1] * rs, v[2] * rs, v[3] * rs);
+  if (lane == 0) w_out[(int64_t)t * nheads + h] = __bfloat162float(w[(int64_t)t * ld_w + h]) * wscale * scale;
+}
+
+// ----------------------------------------------------------------------------- top-k
+// Order-preserving uint32 key of a float (larger float -> larger key).
+__device__ __forceinline__ uint32_t fkey(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kTopkThreads = 1024;
+
+// Block-wide exclusive scan of one int per thread; returns the prefix, *total = sum.
+__device__ int block_exclusive_scan(int v, int* tmp, int* total) {
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  int s = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, s, o);
+    if (lane >= o) s += t;
+  }
+  if (lane == 31) tmp[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < (int)(blockDim.x / 32) ? tmp[lane] : 0;
+    int ws = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, ws, o);
+      if (lane >= o) ws += t;
+    }
+    tmp[32 + lane] = ws - w;
+    if (lane == 31) tmp[64] = ws;
+  }
+  __syncthreads();
+  const int r = tmp[32 + warp] + s - v;
+  *total = tmp[64];
+  __syncthreads();
+  return r;
+}
+
+// Per token: the `k` largest scores among positions [0, ctx), ties to the
+// lowest position, output in ascending position order as cache slot ids
+// (block_table[seq][pos / bs] * bs + pos % bs); -1 pads when ctx < k.
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restrict__ scores, int64_t ld_scores,
+                                                            const int* __restrict__ ctx_lens, int k,
+                                                            const int* __restrict__ token_seq,
+                                                            const int* __restrict__ block_table, int64_t ld_bt,
+                                                            int block_size, int* __restrict__ out_idx,
+                                                            int* __restrict__ out_count) {
+  __shared__ int hist[256];
+  __shared__ int tmp[80];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_remaining;
+  const int t = blockIdx.x;
+  const int ctx = ctx_lens[t];
+  const int seq = token_seq ? token_seq[t] : t;
+  const float* row = scores + (int64_t)t * ld_scores;
+  const int* bt = block_table + (int64_t)seq * ld_bt;
+  int* out = out_idx + (int64_t)t * k;
+  const int tid = threadIdx.x;
+  if (ctx <= k) {
+    for (int p = tid; p < k; p += blockDim.x) out[p] = p < ctx ? bt[p / block_size] * block_size + p % block_size : -1;
+    if (tid == 0) out_count[t] = ctx;
+    return;
+  }
+  // radix select of the k-th largest key, 8 bits per pass
+  uint32_t prefix = 0, mask = 0;
+  int remaining = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int p = tid; p < ctx; p += blockDim.x) {
+      const uint32_t key = fkey(row[p]);
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (acc + hist[d] >= remaining) break;
+        acc += hist[d];
+      }
+      s_prefix = prefix | ((uint32_t)d << shift);
+      s_remaining = remaining - acc;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    remaining = s_remaining;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  // prefix == key of the k-th largest; `remaining` of the keys equal to it are taken
+  const int per = (ctx + blockDim.x - 1) / blockDim.x;
+  const int p0 = tid * per, p1 = min(ctx, p0 + per);
+  int n_eq = 0;
+  for (int p = p0; p < p1; ++p) n_eq += fkey(row[p]) == prefix;
+  int tot;
+  const int eq_before = block_exclusive_scan(n_eq, tmp, &tot);
+  int n_sel = 0;
+  {
+    int e = eq_before;
+    for (int p = p0; p < p1; ++p) {
+      const uint32_t key = fkey(row[p]);
+      if (key > prefix) ++n_sel;
+      else if (key == prefix) n_sel += (e++ < remaining);
+    }
+  }
+  const int sel_before = block_exclusive_scan(n_sel, tmp, &tot);
+  {
+    int e = eq_before, o = sel_before;
+    for (int p = p0; p < p1; ++p) {
+      const uint32_t key = fkey(row[p]);
+      bool take = key > prefix;
+      if (key == prefix) take = (e++ < remaining);
+      if (take) out[o++] = bt[p / block_size] * block_size + p % block_size;
+    }
+  }
+  for (int p = tot + tid; p < k; p += blockDim.x) out[p] = -1;
+  if (tid == 0) out_count[t] = tot;
+}
+
+}  // namespace mla
+
+cudaError_t rope_apply(void* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
+                       const int* positions, const float* cos_sin, int interleaved, int T, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int64_t total = (int64_t)T * nheads * (rot_dim / 2);
+  const int threads = 256;
+  const int blocks = (int)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+  mla::rope_kernel<<<blocks, threads, 0, stream>>>(reinterpret_cast<__nv_bfloat16*>(x), ld_tok, ld_head, nheads,
+                                                   offset, rot_dim, positions, cos_sin, interleaved, T);
+  return cudaGetLastError();
+}
+
+cudaError_t mla_latent_cache_write(const void* kv, int64_t ld_kv, const void* norm_w, float eps, const int* positions,
+                                   const float* cos_sin, int interleaved, const int64_t* slots, void* cache, int T,
+                                   cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  mla::latent_cache_write_kernel<<<(T * 32 + 255) / 256, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(kv), ld_kv, reinterpret_cast<const __nv_bfloat16*>(norm_w), eps,
+      positions, cos_sin, interleaved, slots, reinterpret_cast<__nv_bfloat16*>(cache), T);
+  return cudaGetLastError();
+}
+
+cudaError_t mla_index_k_write(const void* k, int64_t ld_k, const void* ln_w, const void* ln_b, float eps,
+                              const int* positions, const float* cos_sin, int rope_dim, int interleaved,
+                              const int64_t* slots, void* cache, float* cache_scale, int T, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  mla::index_k_write_kernel<<<(T * 32 + 255) / 256, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(k), ld_k, reinterpret_cast<const __nv_bfloat16*>(ln_w),
+      reinterpret_cast<const __nv_bfloat16*>(ln_b), eps, positions, cos_sin, rope_dim, interleaved, slots,
+      reinterpret_cast<uint8_t*>(cache), cache_scale, T);
+  return cudaGetLastError();
+}
+
+cudaError_t mla_index_q_prep(const void* q, int64_t ld_tok, int nheads, const int* positions, const float* cos_sin,
+                             int rope_dim, int interleaved, const void* w, int64_t ld_w, float wscale, void* q8,
+                             float* w_out, int T, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int warps = T * nheads;
+  mla::index_q_prep_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q), ld_tok, nheads, positions, cos_sin, rope_dim, interleaved,
+      reinterpret_cast<const __nv_bfloat16*>(w), ld_w, wscale, reinterpret_cast<uint8_t*>(q8), w_out, T);
+  return cudaGetLastError();
+}
+
+cudaError_t mla_topk(const float* scores, int64_t ld_scores, const int* ctx_lens, int k, const int* token_seq,
+                     const int* block_table, int64_t ld_bt, int block_size, int* out_idx, int* out_count, int T,
+                     cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  mla::topk_kernel<<<T, mla::kTopkThreads, 0, stream>>>(scores, ld_scores, ctx_lens, k, token_seq, block_table, ld_bt,
+                                                        block_size, out_idx, out_count);
+  return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -41,6 +41,28 @@ void kda_core_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& 
                  const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta, at::Tensor& state,
                  at::Tensor& out);  // kda.cu
 
+void rope_op(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin, int64_t offset, int64_t rot_dim,
+             bool interleaved);  // mla_prep.cu
+void mla_latent_cache_write_op(const at::Tensor& kv, const at::Tensor& norm_w, double eps, const at::Tensor& positions,
+                               const at::Tensor& cos_sin, bool interleaved, const at::Tensor& slots,
+                               at::Tensor& cache);  // mla_prep.cu
+void mla_index_k_write_op(const at::Tensor& k, const c10::optional<at::Tensor>& ln_w,
+                          const c10::optional<at::Tensor>& ln_b, double eps, const at::Tensor& positions,
+                          const at::Tensor& cos_sin, bool interleaved, const at::Tensor& slots, at::Tensor& cache,
+                          at::Tensor& cache_scale);  // mla_prep.cu
+void mla_index_q_prep_op(const at::Tensor& q, const at::Tensor& positions, const at::Tensor& cos_sin, bool interleaved,
+                         const at::Tensor& w, double wscale, at::Tensor& q8, at::Tensor& w_out);  // mla_prep.cu
+void mla_indexer_scores_op(const at::Tensor& q8, const at::Tensor& w, const at::Tensor& k_cache,
+                           const at::Tensor& k_scale, const at::Tensor& ctx_lens,
+                           const c10::optional<at::Tensor>& token_seq, const at::Tensor& block_table,
+                           int64_t max_ctx, at::Tensor& scores, const at::Tensor& status);  // mla_attn.cu
+void mla_topk_op(const at::Tensor& scores, const at::Tensor& ctx_lens, int64_t k,
+                 const c10::optional<at::Tensor>& token_seq, const at::Tensor& block_table, int64_t block_size,
+                 at::Tensor& out_idx, at::Tensor& out_count);  // mla_prep.cu
+void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& indices,
+                             const at::Tensor& counts, double sm_scale, int64_t splits, at::Tensor& out,
+                             const c10::optional<at::Tensor>& lse, const at::Tensor& status);  // mla_attn.cu
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -67,7 +89,20 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor? g_bias, float lower_bound, Tensor? norm_w, float eps, float l2_eps, float q_scale, "            \
     "bool l2norm, Tensor(b!) state, Tensor(c!) out) -> ()")                                               \
   X("kda_core(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor q, Tensor k, Tensor v, "      \
-    "Tensor g, Tensor beta, Tensor(a!) state, Tensor(b!) out) -> ()")
+    "Tensor g, Tensor beta, Tensor(a!) state, Tensor(b!) out) -> ()")                                     \
+  X("rope(Tensor(a!) x, Tensor positions, Tensor cos_sin, int offset, int rot_dim, bool interleaved) -> ()") \
+  X("mla_latent_cache_write(Tensor kv, Tensor norm_w, float eps, Tensor positions, Tensor cos_sin, "        \
+    "bool interleaved, Tensor slots, Tensor(a!) cache) -> ()")                                            \
+  X("mla_index_k_write(Tensor k, Tensor? ln_w, Tensor? ln_b, float eps, Tensor positions, Tensor cos_sin, " \
+    "bool interleaved, Tensor slots, Tensor(a!) cache, Tensor(b!) cache_scale) -> ()")                    \
+  X("mla_index_q_prep(Tensor q, Tensor positions, Tensor cos_sin, bool interleaved, Tensor w, float wscale, " \
+    "Tensor(a!) q8, Tensor(b!) w_out) -> ()")                                                             \
+  X("mla_indexer_scores(Tensor q8, Tensor w, Tensor k_cache, Tensor k_scale, Tensor ctx_lens, "           \
+    "Tensor? token_seq, Tensor block_table, int max_ctx, Tensor(a!) scores, Tensor(b!) status) -> ()")    \
+  X("mla_topk(Tensor scores, Tensor ctx_lens, int k, Tensor? token_seq, Tensor block_table, int block_size, " \
+    "Tensor(a!) out_idx, Tensor(b!) out_count) -> ()")                                                    \
+  X("mla_sparse_attention(Tensor q, Tensor cache, Tensor indices, Tensor counts, float sm_scale, int splits, " \
+    "Tensor(a!) out, Tensor(b!)? lse, Tensor(c!) status) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -79,4 +114,11 @@ void register_host_bindings(pybind11::module_& m);
   X("exl3_gemm", b200::exl3_gemm_op)                  \
   X("moe_combine", b200::moe_combine_op)              \
   X("kda_forward", b200::kda_forward_op)              \
-  X("kda_core", b200::kda_core_op)
+  X("kda_core", b200::kda_core_op)                    \
+  X("rope", b200::rope_op)                            \
+  X("mla_latent_cache_write", b200::mla_latent_cache_write_op) \
+  X("mla_index_k_write", b200::mla_index_k_write_op)  \
+  X("mla_index_q_prep", b200::mla_index_q_prep_op)    \
+  X("mla_indexer_scores", b200::mla_indexer_scores_op) \
+  X("mla_topk", b200::mla_topk_op)                    \
+  X("mla_sparse_attention", b200::mla_sparse_attention_op)

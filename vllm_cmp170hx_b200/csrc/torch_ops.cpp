@@ -314,3 +314,124 @@ void kda_core_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& 
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void rope_op(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin, int64_t offset, int64_t rot_dim,
+             bool interleaved) {
+  B200_CHECK_CUDA(x);
+  B200_CHECK_DTYPE(x, at::kBFloat16);
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "rope: x [T, heads, dim] with contiguous dim");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == rot_dim,
+              "rope: positions int32, cos_sin fp32 [max_pos, rot_dim]");
+  TORCH_CHECK(offset + rot_dim <= x.size(2) && rot_dim % 2 == 0, "rope: range");
+  c10::cuda::CUDAGuard g(x.device());
+  B200_LAUNCH(rope_apply(x.data_ptr(), x.stride(0), x.stride(1), x.size(1), (int)offset, (int)rot_dim,
+                         positions.data_ptr<int>(), cos_sin.data_ptr<float>(), interleaved ? 1 : 0, x.size(0),
+                         cur_stream()));
+}
+
+void mla_latent_cache_write_op(const at::Tensor& kv, const at::Tensor& norm_w, double eps, const at::Tensor& positions,
+                               const at::Tensor& cos_sin, bool interleaved, const at::Tensor& slots, at::Tensor& cache) {
+  B200_CHECK_CUDA(kv);
+  B200_CHECK_DTYPE(kv, at::kBFloat16);
+  B200_CHECK_DTYPE(cache, at::kBFloat16);
+  TORCH_CHECK(kv.dim() == 2 && kv.size(1) >= 576 && kv.stride(1) == 1, "latent write: kv [T, 576]");
+  TORCH_CHECK(cache.is_contiguous() && cache.size(-1) == 576, "latent write: cache [..., 576]");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && cos_sin.size(1) == 64, "latent write: slots int64, rope 64");
+  c10::cuda::CUDAGuard g(kv.device());
+  B200_LAUNCH(mla_latent_cache_write(kv.data_ptr(), kv.stride(0), norm_w.data_ptr(), (float)eps,
+                                     positions.data_ptr<int>(), cos_sin.data_ptr<float>(), interleaved ? 1 : 0,
+                                     slots.data_ptr<int64_t>(), cache.data_ptr(), kv.size(0), cur_stream()));
+}
+
+void mla_index_k_write_op(const at::Tensor& k, const c10::optional<at::Tensor>& ln_w,
+                          const c10::optional<at::Tensor>& ln_b, double eps, const at::Tensor& positions,
+                          const at::Tensor& cos_sin, bool interleaved, const at::Tensor& slots, at::Tensor& cache,
+                          at::Tensor& cache_scale) {
+  B200_CHECK_CUDA(k);
+  B200_CHECK_DTYPE(k, at::kBFloat16);
+  TORCH_CHECK(k.dim() == 2 && k.size(1) == 128 && k.stride(1) == 1, "index k: [T, 128]");
+  TORCH_CHECK(cache.is_contiguous() && cache.size(-1) == 128 && cache.element_size() == 1, "index k: cache uint8");
+  TORCH_CHECK(cache_scale.scalar_type() == at::kFloat, "index k: scale fp32");
+  c10::cuda::CUDAGuard g(k.device());
+  B200_LAUNCH(mla_index_k_write(k.data_ptr(), k.stride(0), opt_ptr(ln_w), opt_ptr(ln_b), (float)eps,
+                                positions.data_ptr<int>(), cos_sin.data_ptr<float>(), cos_sin.size(1),
+                                interleaved ? 1 : 0, slots.data_ptr<int64_t>(), cache.data_ptr(),
+                                cache_scale.data_ptr<float>(), k.size(0), cur_stream()));
+}
+
+void mla_index_q_prep_op(const at::Tensor& q, const at::Tensor& positions, const at::Tensor& cos_sin, bool interleaved,
+                         const at::Tensor& w, double wscale, at::Tensor& q8, at::Tensor& w_out) {
+  B200_CHECK_CUDA(q);
+  B200_CHECK_DTYPE(q, at::kBFloat16);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.stride(2) == 1 && q.stride(1) == 128, "index q: [T, H, 128]");
+  TORCH_CHECK(q8.is_contiguous() && q8.numel() == q.size(0) * q.size(1) * 128 && q8.element_size() == 1, "index q8");
+  TORCH_CHECK(w_out.scalar_type() == at::kFloat && w_out.numel() == q.size(0) * q.size(1), "index w_out");
+  B200_CHECK_DTYPE(w, at::kBFloat16);
+  c10::cuda::CUDAGuard g(q.device());
+  B200_LAUNCH(mla_index_q_prep(q.data_ptr(), q.stride(0), q.size(1), positions.data_ptr<int>(),
+                               cos_sin.data_ptr<float>(), cos_sin.size(1), interleaved ? 1 : 0, w.data_ptr(),
+                               w.stride(0), (float)wscale, q8.data_ptr(), w_out.data_ptr<float>(), q.size(0),
+                               cur_stream()));
+}
+
+void mla_indexer_scores_op(const at::Tensor& q8, const at::Tensor& w, const at::Tensor& k_cache,
+                           const at::Tensor& k_scale, const at::Tensor& ctx_lens, const c10::optional<at::Tensor>& token_seq,
+                           const at::Tensor& block_table, int64_t max_ctx, at::Tensor& scores, const at::Tensor& status) {
+  B200_CHECK_CUDA(q8);
+  TORCH_CHECK(q8.element_size() == 1 && q8.is_contiguous() && q8.size(-1) == 128 && q8.size(-2) == 64,
+              "indexer: q8 [T, 64, 128] fp8");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "indexer: w fp32 [T, 64]");
+  TORCH_CHECK(k_cache.element_size() == 1 && k_cache.is_contiguous() && k_cache.size(-1) == 128, "indexer: cache");
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.stride(1) == 1 && scores.size(1) >= max_ctx,
+              "indexer: scores [T, >= max_ctx] fp32");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2, "indexer: block_table int32 [S, n]");
+  c10::cuda::CUDAGuard g(q8.device());
+  const int T = q8.size(0);
+  B200_LAUNCH(mla_indexer_scores(q8.data_ptr(), w.data_ptr<float>(), T, k_cache.data_ptr(), k_cache.numel() / 128,
+                                 k_scale.data_ptr<float>(), ctx_lens.data_ptr<int>(),
+                                 token_seq.has_value() ? token_seq->data_ptr<int>() : nullptr,
+                                 block_table.data_ptr<int>(), block_table.stride(0), scores.data_ptr<float>(),
+                                 scores.stride(0), (int)max_ctx, status_ptr(status), cur_stream()));
+}
+
+void mla_topk_op(const at::Tensor& scores, const at::Tensor& ctx_lens, int64_t k,
+                 const c10::optional<at::Tensor>& token_seq, const at::Tensor& block_table, int64_t block_size,
+                 at::Tensor& out_idx, at::Tensor& out_count) {
+  B200_CHECK_CUDA(scores);
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.stride(1) == 1, "topk: scores fp32");
+  TORCH_CHECK(out_idx.scalar_type() == at::kInt && out_idx.is_contiguous() && out_idx.size(1) == k, "topk: out");
+  c10::cuda::CUDAGuard g(scores.device());
+  B200_LAUNCH(mla_topk(scores.data_ptr<float>(), scores.stride(0), ctx_lens.data_ptr<int>(), (int)k,
+                       token_seq.has_value() ? token_seq->data_ptr<int>() : nullptr, block_table.data_ptr<int>(),
+                       block_table.stride(0), (int)block_size, out_idx.data_ptr<int>(), out_count.data_ptr<int>(),
+                       scores.size(0), cur_stream()));
+}
+
+void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& indices,
+                             const at::Tensor& counts, double sm_scale, int64_t splits, at::Tensor& out,
+                             const c10::optional<at::Tensor>& lse, const at::Tensor& status) {
+  B200_CHECK_CUDA(q);
+  B200_CHECK_DTYPE(q, at::kBFloat16);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576 && q.is_contiguous(), "sparse attn: q [T, nh, 576] contiguous");
+  TORCH_CHECK(cache.scalar_type() == at::kBFloat16 && cache.is_contiguous() && cache.size(-1) == 576, "sparse attn: cache");
+  TORCH_CHECK(indices.scalar_type() == at::kInt && indices.is_contiguous() && indices.size(0) == q.size(0),
+              "sparse attn: indices [T, topk] int32");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(-1) == 512, "sparse attn: out");
+  c10::cuda::CUDAGuard g(q.device());
+  const int T = q.size(0), nh = q.size(1);
+  at::Tensor part_o, part_ml;
+  if (splits > 1) {
+    part_o = at::empty({splits, T, nh, 512}, q.options().dtype(at::kFloat));
+    part_ml = at::empty({splits, T, nh, 2}, q.options().dtype(at::kFloat));
+  }
+  B200_LAUNCH(mla_sparse_attention(q.data_ptr(), T, nh, cache.data_ptr(), indices.data_ptr<int>(),
+                                   counts.data_ptr<int>(), indices.size(1), (float)sm_scale, (int)splits,
+                                   out.data_ptr(), splits > 1 ? part_o.data_ptr<float>() : nullptr,
+                                   splits > 1 ? part_ml.data_ptr<float>() : nullptr,
+                                   lse.has_value() ? lse->data_ptr<float>() : nullptr, status_ptr(status),
+                                   cur_stream()));
+}
+
+}  // namespace b200
