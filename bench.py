@@ -1,0 +1,230 @@
+"""Headline benchmark: decode output tokens/s and p50 TPOT of the hybrid
+KDA/sparse-MLA MoE model (48 layers, hidden 2304, 32 heads,
+256 experts top-8 + 1 shared, EXL3 4-bit experts) serving 128 concurrent
+requests of 2048-token prompts, tensor parallel over N GPUs of one node.
+
+    python bench.py --gpus N --steps K --warmup W            # this framework
+    python bench.py --impl reference ...                      # the reference arm
+    torchrun --nproc-per-node N bench.py --gpus N ...         # N > 1
+
+Protocol: random-init weights and random token ids (no checkpoints, no
+datasets); all 128 prompts are prefilled through the engine (untimed), then
+W decode steps warm up (CUDA graphs captured) and K decode steps are timed.
+Each decode step reads every expert weight (~43.5 GB at TP1), far more than
+the 126 MB L2, so no flush is needed between steps.
+
+* value       = 128 * K / (sum of per-step device time) -- CUDA events around
+                each step's graph replay on the launching stream, max over ranks;
+* e2e.value   = 128 * K / (wall time of K `LLMEngine.step()` calls): includes
+                scheduling, the pinned host->device copy of the step inputs and
+                the device->host read of the sampled tokens, barrier + sync on
+                both sides, max over ranks;
+* p50_tpot_ms = median per-step e2e time (every running request gets one
+                token per step).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode output tok/s (box, max over ranks) at 1/2/4/8 B200; p50 TPOT"
+
+
+def reference_unavailable(args, reason: str) -> None:
+    print(json.dumps({"impl": "reference", "unavailable": reason, "metric": METRIC, "n_gpus": args.gpus}))
+
+
+def sample_clocks_start(index: int):
+    try:
+        return subprocess.Popen(
+            ["nvidia-smi", f"--id={index}",
+             "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+        return None
+
+
+def sample_clocks_stop(proc) -> dict:
+    if proc is None:
+        return {}
+    proc.terminate()
+    try:
+        out, _ = proc.communicate(timeout=5)
+    except subprocess.TimeoutExpired:
+        proc.kill()
+        out, _ = proc.communicate()
+    sm, mx, reasons = [], 0.0, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in out.strip().splitlines():
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 7:
+            continue
+        try:
+            sm.append(float(f[0]))
+            mx = max(mx, float(f[1]))
+        except ValueError:
+            continue
+        for n, v in zip(names, f[3:7]):
+            if v.lower() == "active":
+                reasons.add(n)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
+            "samples": len(sm)}
+
+
+def count_own_kernels(engine, steps: int) -> int:
+    """Kernels of this package's extension (namespace b200) launched by one
+    eager decode step, times the timed steps (graph replays run the same set)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    r = engine.runner
+    saved = r.cfg.enforce_eager
+    r.cfg.enforce_eager = True
+    try:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            engine.step()
+            torch.cuda.synchronize()
+    finally:
+        r.cfg.enforce_eager = saved
+    n = sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "b200" in e.name)
+    return n * steps
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--output", type=int, default=512)
+    ap.add_argument("--prefill-chunk", type=int, default=16384)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
+    args = ap.parse_args()
+
+    if args.impl == "reference":
+        ref = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref, "vllm_sm80")):
+            reference_unavailable(args, "reference not installed under baseline/_ref")
+            return
+        reference_unavailable(args, "the reference is a vLLM plugin whose model classes subclass upstream vLLM packages "
+                                    "(vllm/models/glm5next, deepseek_v41, qwen4_exp, model-runner V2) that the image's "
+                                    "vLLM 0.22 does not ship, and its native kernels build for sm_80 only")
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from vllm_cmp170hx_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, config3)
+    from vllm_cmp170hx_b200.engine.llm_engine import LLMEngine
+    from vllm_cmp170hx_b200.engine.request import SamplingParams
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    st = pstate.init(tp_size=args.gpus, pp_size=1, timeout_s=600)
+    dev = st.device
+    model_cfg = config3()
+    total_len = args.prompt + args.output + 64
+    cfg = EngineConfig(model=model_cfg,
+                       parallel=ParallelConfig(tensor_parallel_size=args.gpus, fused_comm=not args.nccl_baseline),
+                       scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
+                                                 max_model_len=total_len, max_num_partial_prefills=args.batch),
+                       cache=CacheConfig(num_blocks=args.batch * ((total_len + 63) // 64) + 1),
+                       seed=args.seed, device="cuda",
+                       cuda_graph_batch_sizes=[args.batch])
+    t0 = time.time()
+    engine = LLMEngine(cfg)
+    fused = False
+    if args.gpus > 1 and not args.nccl_baseline:
+        try:
+            from vllm_cmp170hx_b200.parallel import symm
+            fused = symm.enable_for_engine(engine)
+        except ImportError:
+            fused = False
+    torch.cuda.synchronize()
+    t_load = time.time() - t0
+    g = torch.Generator().manual_seed(args.seed)
+    V = model_cfg.vocab_size
+    for i in range(args.batch):
+        prompt = torch.randint(0, V, (args.prompt,), generator=g).tolist()
+        engine.add_request(prompt, SamplingParams(max_tokens=args.output, ignore_eos=True), f"bench-{i}")
+    # prefill (untimed): until every request has its first token
+    t1 = time.time()
+    while any(r.num_computed_tokens < r.num_prompt_tokens for r in engine.scheduler.running) or engine.scheduler.waiting:
+        engine.step()
+    torch.cuda.synchronize()
+    t_prefill = time.time() - t1
+    for _ in range(args.warmup):
+        engine.step()
+    launches = count_own_kernels(engine, args.steps)
+    engine.runner.time_device = True
+    clk = sample_clocks_start(dev.index or 0) if st.rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    dev_ms, e2e_ms = [], []
+    h2d = d2h = 0
+    t_start = time.perf_counter()
+    for _ in range(args.steps):
+        a = time.perf_counter()
+        engine.step()
+        torch.cuda.synchronize()
+        e2e_ms.append((time.perf_counter() - a) * 1e3)
+        s = engine.runner.last_stats
+        dev_ms.append(s.device_ms)
+        h2d, d2h = s.h2d_bytes, s.d2h_bytes
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    wall = time.perf_counter() - t_start
+    clocks = sample_clocks_stop(clk)
+    tot = torch.tensor([sum(dev_ms), wall * 1e3], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    dev_total_ms, wall_ms = tot.tolist()
+    toks = args.batch * args.steps
+    value = toks / (dev_total_ms / 1e3)
+    e2e_value = toks / (wall_ms / 1e3)
+    if st.rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_total_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "impl": "ours",
+            "data": "synthetic: random token ids, random-init weights of the config-3 architecture",
+            "config": {"model": "hybrid KDA/sparse-MLA MoE, 48 layers (36 KDA : 12 MLA), hidden 2304, 32 heads, "
+                                "256 experts top-8 + 1 shared, expert intermediate 1024, EXL3 4-bit experts, "
+                                "vocab 163840",
+                       "global_batch": args.batch, "seq_len": args.prompt, "output_len": args.output,
+                       "parallelism": f"tp{args.gpus}",
+                       "collectives": "fused symmetric-memory kernels" if fused else ("none" if args.gpus == 1 else "nccl"),
+                       "l2": "no flush: each step streams all expert weights (~43.5 GB / tp) >> 126 MB L2"},
+            "p50_tpot_ms": round(statistics.median(e2e_ms), 3),
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "LLMEngine.step()"},
+            "gpu_launches": launches,
+            "timing": {"load_s": round(t_load, 1), "prefill_s": round(t_prefill, 1)},
+        }), flush=True)
+    engine.runner.release_graphs()
+    if world > 1:
+        dist.barrier()
+        pstate.destroy()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,229 @@
+"""Model and engine configuration.
+
+Model configs describe the two model families of the reference's served
+models (README.md:32-37 of the reference: GLM-5.3-Flash hybrid KDA/sparse-MLA
+MoE, DeepSeek-V4.1-Flash sparse-MLA MoE) in the shapes BASELINE.json names:
+
+* :func:`config3` -- hybrid KDA/MLA MoE: 48 layers at 3:1 KDA:sparse-MLA,
+  hidden 2304, 32 heads, 256 routed experts top-8 + 1 shared, expert
+  intermediate 1024, EXL3 4-bit (bits_x2 = 8) experts, bf16 dense weights,
+  vocab 163840.
+* :func:`config4` -- DeepSeek-style sparse-MLA MoE: 43 layers, hidden 4096,
+  first 3 layers dense FFN 12288, 256 routed experts top-8 + 1 shared, expert
+  intermediate 1536, Marlin int4 group-128 experts, fp8 128x128 block-scaled
+  attention weights, 128 heads.
+* :func:`config2_layer` -- one sparse-MLA decode layer: 128 heads, kv_lora
+  512, qk_nope 128, qk_rope 64, v_head 128, indexer 64 x 128 top-2048.
+
+Engine config mirrors the knobs of the reference's engine settings
+(vllm_sm80/config.py:26 `additional_config["sm80"]`, engine_args.py:63
+`--prefill-chunk-with-decodes`, `--max-num-partial-prefills`).
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import json
+from dataclasses import dataclass, field
+
+
+@dataclass
+class KDAConfig:
+    num_heads: int = 32
+    head_dim: int = 128
+    conv_kernel: int = 4
+    lower_bound: float = -5.0
+
+
+@dataclass
+class MLAConfig:
+    num_heads: int = 32
+    q_lora_rank: int = 768
+    kv_lora_rank: int = 512
+    qk_nope_head_dim: int = 128
+    qk_rope_head_dim: int = 64
+    v_head_dim: int = 128
+    index_n_heads: int = 64
+    index_head_dim: int = 128
+    index_topk: int = 2048
+    rope_theta: float = 10000.0
+    rope_interleave: bool = False
+    attn_weight_format: str = "bf16"  # or "fp8_block" (128x128 block-scaled e4m3)
+
+    @property
+    def qk_head_dim(self) -> int:
+        return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+
+@dataclass
+class MoEConfig:
+    num_experts: int = 256
+    top_k: int = 8
+    intermediate: int = 1024
+    num_shared: int = 1
+    shared_intermediate: int = 1024
+    router: str = "softmax"  # softmax | sigmoid | sqrt_softplus
+    routed_scaling: float = 1.0
+    renormalize: bool = True
+    expert_format: str = "exl3"  # exl3 | marlin | bf16
+    exl3_bits_x2: int = 8
+    exl3_codebook: int = 2
+    swiglu_limit: float = 0.0
+
+    @property
+    def router_mode(self) -> int:
+        return {"softmax": 0, "sigmoid": 1, "sqrt_softplus": 2}[self.router]
+
+
+@dataclass
+class ModelConfig:
+    name: str = "hybrid-kda-mla-moe"
+    vocab_size: int = 163840
+    hidden_size: int = 2304
+    num_layers: int = 48
+    layer_types: list[str] = field(default_factory=list)  # "kda" | "mla" per layer
+    mlp_types: list[str] = field(default_factory=list)  # "dense" | "moe" per layer
+    dense_intermediate: int = 12288
+    kda: KDAConfig = field(default_factory=KDAConfig)
+    mla: MLAConfig = field(default_factory=MLAConfig)
+    moe: MoEConfig = field(default_factory=MoEConfig)
+    rms_eps: float = 1e-5
+    max_position: int = 1 << 20
+    tie_embeddings: bool = False
+    num_mtp_layers: int = 0
+    dtype: str = "bfloat16"
+
+    def __post_init__(self):
+        if not self.layer_types:
+            self.layer_types = ["mla" if i % 4 == 3 else "kda" for i in range(self.num_layers)]
+        if not self.mlp_types:
+            self.mlp_types = ["moe"] * self.num_layers
+        assert len(self.layer_types) == self.num_layers and len(self.mlp_types) == self.num_layers
+
+    @property
+    def num_kda_layers(self) -> int:
+        return sum(t == "kda" for t in self.layer_types)
+
+    @property
+    def num_mla_layers(self) -> int:
+        return sum(t == "mla" for t in self.layer_types)
+
+    def to_json(self) -> str:
+        return json.dumps(dataclasses.asdict(self), indent=2)
+
+    @staticmethod
+    def from_dict(d: dict) -> "ModelConfig":
+        d = dict(d)
+        kda = KDAConfig(**d.pop("kda", {}))
+        mla = MLAConfig(**d.pop("mla", {}))
+        moe = MoEConfig(**d.pop("moe", {}))
+        return ModelConfig(kda=kda, mla=mla, moe=moe, **d)
+
+
+def config3() -> ModelConfig:
+    """hybrid KDA/MLA MoE (EXL3 4-bit experts)."""
+    return ModelConfig(
+        name="hybrid-kda-mla-moe-48L-2304",
+        vocab_size=163840,
+        hidden_size=2304,
+        num_layers=48,
+        kda=KDAConfig(num_heads=32, head_dim=128),
+        mla=MLAConfig(num_heads=32, q_lora_rank=768),
+        moe=MoEConfig(num_experts=256, top_k=8, intermediate=1024, num_shared=1, shared_intermediate=1024,
+                      router="softmax", expert_format="exl3", exl3_bits_x2=8, exl3_codebook=2),
+    )
+
+
+def config4() -> ModelConfig:
+    """DeepSeek-style sparse-MLA MoE (Marlin int4 experts, fp8 attention)."""
+    L = 43
+    return ModelConfig(
+        name="deepseek-sparse-mla-moe-43L-4096",
+        vocab_size=129280,
+        hidden_size=4096,
+        num_layers=L,
+        layer_types=["mla"] * L,
+        mlp_types=["dense"] * 3 + ["moe"] * (L - 3),
+        dense_intermediate=12288,
+        mla=MLAConfig(num_heads=128, q_lora_rank=1536, attn_weight_format="fp8_block"),
+        moe=MoEConfig(num_experts=256, top_k=8, intermediate=1536, num_shared=1, shared_intermediate=1536,
+                      router="sigmoid", routed_scaling=2.5, expert_format="marlin"),
+        num_mtp_layers=1,
+    )
+
+
+def config2_layer() -> ModelConfig:
+    """a single sparse-MLA decode layer (128 heads)."""
+    return ModelConfig(
+        name="sparse-mla-decode-layer",
+        vocab_size=32000,
+        hidden_size=7168,
+        num_layers=1,
+        layer_types=["mla"],
+        mlp_types=["none"],
+        mla=MLAConfig(num_heads=128, q_lora_rank=1536),
+    )
+
+
+def tiny(layers: int = 4, experts: int = 8, hidden: int = 256, vocab: int = 512, expert_format: str = "exl3",
+         layer_types: list[str] | None = None) -> ModelConfig:
+    """Small model of the hybrid family for tests (CPU oracle path and GPU smoke)."""
+    return ModelConfig(
+        name="tiny-hybrid",
+        vocab_size=vocab,
+        hidden_size=hidden,
+        num_layers=layers,
+        layer_types=layer_types or [],
+        kda=KDAConfig(num_heads=2, head_dim=128),
+        mla=MLAConfig(num_heads=2, q_lora_rank=128, index_n_heads=64, index_topk=64),
+        moe=MoEConfig(num_experts=experts, top_k=2, intermediate=128, num_shared=1, shared_intermediate=128,
+                      expert_format=expert_format),
+        max_position=4096,
+    )
+
+
+PRESETS = {"config3": config3, "config4": config4, "config2_layer": config2_layer, "tiny": tiny}
+
+
+@dataclass
+class ParallelConfig:
+    tensor_parallel_size: int = 1
+    pipeline_parallel_size: int = 1
+    expert_parallel: bool = False  # experts split whole across ranks (else TP-split experts)
+    fused_comm: bool = True  # product path: fused GEMM+collective kernels; False = NCCL baseline
+
+    @property
+    def world_size(self) -> int:
+        return self.tensor_parallel_size * self.pipeline_parallel_size
+
+
+@dataclass
+class SchedulerConfig:
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 8192
+    max_model_len: int = 8192
+    prefill_chunk_with_decodes: bool = True  # fair chunked prefill: decodes ride along prefill chunks
+    max_num_partial_prefills: int = 1
+    long_prefill_token_threshold: int = 0
+    num_speculative_tokens: int = 0
+    adaptive_k: bool = False
+
+
+@dataclass
+class CacheConfig:
+    block_size: int = 64
+    num_blocks: int = 0  # 0: derive from memory
+    gpu_memory_utilization: float = 0.90
+    enable_prefix_caching: bool = False
+
+
+@dataclass
+class EngineConfig:
+    model: ModelConfig = field(default_factory=config3)
+    parallel: ParallelConfig = field(default_factory=ParallelConfig)
+    scheduler: SchedulerConfig = field(default_factory=SchedulerConfig)
+    cache: CacheConfig = field(default_factory=CacheConfig)
+    seed: int = 0
+    device: str = "cuda"
+    enforce_eager: bool = False
+    cuda_graph_batch_sizes: list[int] = field(default_factory=lambda: [1, 2, 4, 8, 16, 32, 64, 128, 256])

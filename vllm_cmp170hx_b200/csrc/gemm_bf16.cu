@@ -51,6 +51,7 @@ struct Params {
   int k_blocks_per_split;
   int m_tiles, n_tiles;
   __nv_bfloat16* C;
+  float* Cf;        // fp32 output instead of C (router logits)
   float* partial;  // [splits, M, N] (in the output's orientation) when splits > 1
   const __nv_bfloat16* bias;  // optional [N] (out features), added in the epilogue when splits == 1
   uint32_t* status;
@@ -232,6 +233,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 dst[off] = __uint_as_float(r[j]);
               }
             }
+          } else if (p.Cf != nullptr) {
+            const float bias = p.bias ? __bfloat162float(p.bias[p.transpose_out ? row : 0]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int col = col0 + j;
+              if (col < p.N) {
+                const float b = p.bias ? (p.transpose_out ? bias : __bfloat162float(p.bias[col])) : 0.f;
+                const size_t off = p.transpose_out ? (size_t)col * p.ldc + row : (size_t)row * p.ldc + col;
+                p.Cf[off] = __uint_as_float(r[j]) + b;
+              }
+            }
           } else if (p.transpose_out) {
             const float bias = p.bias ? __bfloat162float(p.bias[row]) : 0.f;
 #pragma unroll
@@ -280,16 +292,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Sum of split-K partials in split order, plus optional bias, to bf16.
-__global__ void splitk_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ C, int rows,
-                                     int cols, int ldc, int splits, const __nv_bfloat16* __restrict__ bias,
-                                     int bias_on_rows) {
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ C,
+                                     float* __restrict__ Cf, int rows, int cols, int ldc, int splits,
+                                     const __nv_bfloat16* __restrict__ bias, int bias_on_rows) {
   const size_t n = (size_t)rows * cols;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     float s = 0.f;
     for (int k = 0; k < splits; ++k) s += partial[(size_t)k * n + i];
     const int r = i / cols, c = i % cols;
     if (bias) s += __bfloat162float(bias[bias_on_rows ? r : c]);
-    C[(size_t)r * ldc + c] = __float2bfloat16(s);
+    if (Cf)
+      Cf[(size_t)r * ldc + c] = s;
+    else
+      C[(size_t)r * ldc + c] = __float2bfloat16(s);
   }
 }
 
@@ -370,7 +385,8 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   const int splits = gemm_bf16_splits(a.M, a.N, a.K, a.splits);
   p.k_blocks_per_split = (kb_total + splits - 1) / splits;
   p.splits = splits;
-  p.C = reinterpret_cast<__nv_bfloat16*>(a.c);
+  p.C = a.out_f32 ? nullptr : reinterpret_cast<__nv_bfloat16*>(a.c);
+  p.Cf = a.out_f32 ? reinterpret_cast<float*>(a.c) : nullptr;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   p.status = a.status;
   if (splits > 1) {
@@ -392,7 +408,7 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   // partial is [splits, M, N] in output orientation.
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>(((int64_t)a.M * a.N + threads - 1) / threads, (int64_t)sms * 8);
-  splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(p.partial, p.C, a.M, a.N, (int)a.ldc, splits,
+  splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(p.partial, p.C, p.Cf, a.M, a.N, (int)a.ldc, splits,
                                                        reinterpret_cast<const __nv_bfloat16*>(a.bias), 0);
   return cudaGetLastError();
 }

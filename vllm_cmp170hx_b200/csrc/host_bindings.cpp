@@ -5,8 +5,11 @@
 
 namespace b200 {
 
+void register_block_pool(pybind11::module_& m);  // block_pool.cpp
+
 void register_host_bindings(pybind11::module_& m) {
   m.attr("ARCH") = "sm_100a";
+  register_block_pool(m);
 }
 
 }  // namespace b200

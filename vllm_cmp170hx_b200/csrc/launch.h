@@ -25,6 +25,7 @@ struct GemmArgs {
   const void* bias;
   void* c;
   int64_t ldc;
+  int out_f32;  // 1: c is fp32
   int M, N, K;
   int splits;
   float* partial;
@@ -39,6 +40,9 @@ cudaError_t rms_norm(void* out, int64_t ld_out, const void* x, int64_t ld_x, con
                      cudaStream_t stream);
 cudaError_t fused_add_rms_norm(void* x, int64_t ld_x, void* residual, int64_t ld_res, const void* w, int T, int H,
                                float eps, cudaStream_t stream);
+// out[t, i] = silu(min(x[t, i], L)) * clamp(x[t, I + i], -L, L)  (L <= 0: no clamp), bf16
+cudaError_t silu_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int T, int I, float limit,
+                     cudaStream_t stream);
 
 // ---------------------------------------------------------------- router.cu
 // mode 0 softmax+renorm, 1 sigmoid(+bias select), 2 sqrt(softplus)(+bias select)
@@ -136,5 +140,11 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
 cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache, const int* indices, const int* counts,
                                  int topk, float sm_scale, int splits, void* out, float* part_o, float* part_ml,
                                  float* lse, uint32_t* status, cudaStream_t stream);
+
+// ---------------------------------------------------------------- sampling.cu
+cudaError_t sample_rows(const void* logits, int dtype, int64_t ld, int rows, int V, const float* temperature,
+                        uint64_t seed, const int64_t* step, int vocab_offset, float* out_val, int* out_idx,
+                        cudaStream_t stream);
+cudaError_t sample_combine(const float* vals, const int* idx, int R, int rows, int64_t* out, cudaStream_t stream);
 
 }  // namespace b200

@@ -6,6 +6,8 @@
 // registers between the reduction and the scaled store, fp32 accumulation.
 // Rows may be strided (e.g. the first 512 columns of a [T, 576] latent).
 #include "common.cuh"
+#include <algorithm>
+
 #include "launch.h"
 
 namespace b200 {
@@ -83,7 +85,38 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* o
   }
 }
 
+__global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, int64_t ld_out, const __nv_bfloat16* __restrict__ x,
+                                int64_t ld_x, int T, int I, float limit) {
+  const int64_t total = (int64_t)T * (I / 2);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = i / (I / 2);
+    const int c = (i % (I / 2)) * 2;
+    const __nv_bfloat162 g2 = *reinterpret_cast<const __nv_bfloat162*>(x + t * ld_x + c);
+    const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(x + t * ld_x + I + c);
+    float g0 = __bfloat162float(g2.x), g1 = __bfloat162float(g2.y);
+    float u0 = __bfloat162float(u2.x), u1 = __bfloat162float(u2.y);
+    if (limit > 0.f) {
+      g0 = fminf(g0, limit);
+      g1 = fminf(g1, limit);
+      u0 = fminf(fmaxf(u0, -limit), limit);
+      u1 = fminf(fmaxf(u1, -limit), limit);
+    }
+    *reinterpret_cast<__nv_bfloat162*>(out + t * ld_out + c) = __floats2bfloat162_rn(siluf_(g0) * u0, siluf_(g1) * u1);
+  }
+}
+
 }  // namespace
+
+cudaError_t silu_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int T, int I, float limit,
+                     cudaStream_t stream) {
+  if (I % 2 || ld_x % 2 || ld_out % 2) return cudaErrorInvalidValue;
+  if (T == 0) return cudaSuccess;
+  const int64_t total = (int64_t)T * (I / 2);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+  silu_mul_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<__nv_bfloat16*>(out), ld_out,
+                                              reinterpret_cast<const __nv_bfloat16*>(x), ld_x, T, I, limit);
+  return cudaGetLastError();
+}
 
 cudaError_t rms_norm(void* out, int64_t ld_out, const void* x, int64_t ld_x, const void* w, int T, int H, float eps,
                      cudaStream_t stream) {

@@ -9,6 +9,7 @@ void gemm_bf16_out(const at::Tensor& x, const at::Tensor& w, const c10::optional
                    const at::Tensor& status, int64_t splits);                       // gemm_bf16.cu
 void rms_norm_out(at::Tensor& out, const at::Tensor& x, const at::Tensor& w, double eps);  // norm.cu
 void fused_add_rms_norm_(at::Tensor& x, at::Tensor& residual, const at::Tensor& w, double eps);  // norm.cu
+void silu_mul_op(at::Tensor& out, const at::Tensor& x, double limit);  // norm.cu
 
 void moe_topk_op(const at::Tensor& logits, int64_t k, int64_t mode, const c10::optional<at::Tensor>& bias,
                  double scale, bool renorm, at::Tensor& ids, at::Tensor& weights);  // router.cu
@@ -63,6 +64,11 @@ void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const
                              const at::Tensor& counts, double sm_scale, int64_t splits, at::Tensor& out,
                              const c10::optional<at::Tensor>& lse, const at::Tensor& status);  // mla_attn.cu
 
+void sample_rows_op(const at::Tensor& logits, const c10::optional<at::Tensor>& temperature, int64_t seed,
+                    const c10::optional<at::Tensor>& step, int64_t vocab_offset, at::Tensor& out_val,
+                    at::Tensor& out_idx);  // sampling.cu
+void sample_combine_op(const at::Tensor& vals, const at::Tensor& idx, at::Tensor& out);  // sampling.cu
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -73,6 +79,7 @@ void register_host_bindings(pybind11::module_& m);
   X("gemm_bf16_out(Tensor x, Tensor w, Tensor? bias, Tensor(a!) out, Tensor(b!) status, int splits) -> ()") \
   X("rms_norm_out(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()")                                 \
   X("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor w, float eps) -> ()")                 \
+  X("silu_mul(Tensor(a!) out, Tensor x, float limit) -> ()")                                           \
   X("moe_topk(Tensor logits, int k, int mode, Tensor? bias, float scale, bool renorm, Tensor(a!) ids, "     \
     "Tensor(b!) weights) -> ()")                                                                         \
   X("moe_build_assignments(Tensor ids, Tensor weights, Tensor? expert_map, int E_local, int tile_rows, "   \
@@ -102,12 +109,16 @@ void register_host_bindings(pybind11::module_& m);
   X("mla_topk(Tensor scores, Tensor ctx_lens, int k, Tensor? token_seq, Tensor block_table, int block_size, " \
     "Tensor(a!) out_idx, Tensor(b!) out_count) -> ()")                                                    \
   X("mla_sparse_attention(Tensor q, Tensor cache, Tensor indices, Tensor counts, float sm_scale, int splits, " \
-    "Tensor(a!) out, Tensor(b!)? lse, Tensor(c!) status) -> ()")
+    "Tensor(a!) out, Tensor(b!)? lse, Tensor(c!) status) -> ()")                                         \
+  X("sample_rows(Tensor logits, Tensor? temperature, int seed, Tensor? step, int vocab_offset, "          \
+    "Tensor(a!) out_val, Tensor(b!) out_idx) -> ()")                                                     \
+  X("sample_combine(Tensor vals, Tensor idx, Tensor(a!) out) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
   X("rms_norm_out", b200::rms_norm_out)    \
   X("fused_add_rms_norm", b200::fused_add_rms_norm_) \
+  X("silu_mul", b200::silu_mul_op)                    \
   X("moe_topk", b200::moe_topk_op)                    \
   X("moe_build_assignments", b200::moe_build_assignments_op) \
   X("exl3_input_rotate", b200::exl3_input_rotate_op)  \
@@ -121,4 +132,6 @@ void register_host_bindings(pybind11::module_& m);
   X("mla_index_q_prep", b200::mla_index_q_prep_op)    \
   X("mla_indexer_scores", b200::mla_indexer_scores_op) \
   X("mla_topk", b200::mla_topk_op)                    \
-  X("mla_sparse_attention", b200::mla_sparse_attention_op)
+  X("mla_sparse_attention", b200::mla_sparse_attention_op) \
+  X("sample_rows", b200::sample_rows_op)              \
+  X("sample_combine", b200::sample_combine_op)

@@ -31,10 +31,10 @@ void gemm_bf16_out(const at::Tensor& x, const at::Tensor& w, const c10::optional
   B200_CHECK_CUDA(w);
   B200_CHECK_DTYPE(x, at::kBFloat16);
   B200_CHECK_DTYPE(w, at::kBFloat16);
-  B200_CHECK_DTYPE(out, at::kBFloat16);
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm_bf16: shape mismatch");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "gemm_bf16: inner dims must be contiguous");
   TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == w.size(0), "gemm_bf16: bad out shape");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat, "gemm_bf16: out bf16 or fp32");
   if (bias.has_value()) {
     B200_CHECK_DTYPE(*bias, at::kBFloat16);
     TORCH_CHECK(bias->numel() == w.size(0) && bias->is_contiguous(), "gemm_bf16: bad bias");
@@ -48,6 +48,7 @@ void gemm_bf16_out(const at::Tensor& x, const at::Tensor& w, const c10::optional
   a.bias = bias.has_value() ? bias->data_ptr() : nullptr;
   a.c = out.data_ptr();
   a.ldc = out.stride(0);
+  a.out_f32 = out.scalar_type() == at::kFloat ? 1 : 0;
   a.M = x.size(0);
   a.N = w.size(0);
   a.K = x.size(1);
@@ -72,6 +73,18 @@ void rms_norm_out(at::Tensor& out, const at::Tensor& x, const at::Tensor& w, dou
   c10::cuda::CUDAGuard g(x.device());
   B200_LAUNCH(rms_norm(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(), x.size(0), x.size(1),
                        (float)eps, cur_stream()));
+}
+
+void silu_mul_op(at::Tensor& out, const at::Tensor& x, double limit) {
+  B200_CHECK_CUDA(x);
+  B200_CHECK_DTYPE(x, at::kBFloat16);
+  B200_CHECK_DTYPE(out, at::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && out.dim() == 2 && x.size(1) == 2 * out.size(1) && x.size(0) == out.size(0) &&
+                  x.stride(1) == 1 && out.stride(1) == 1,
+              "silu_mul: x [T, 2I], out [T, I]");
+  c10::cuda::CUDAGuard g(x.device());
+  B200_LAUNCH(silu_mul(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0), x.size(0), out.size(1), (float)limit,
+                       cur_stream()));
 }
 
 void fused_add_rms_norm_(at::Tensor& x, at::Tensor& residual, const at::Tensor& w, double eps) {
@@ -432,6 +445,35 @@ void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const
                                    splits > 1 ? part_ml.data_ptr<float>() : nullptr,
                                    lse.has_value() ? lse->data_ptr<float>() : nullptr, status_ptr(status),
                                    cur_stream()));
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+void sample_rows_op(const at::Tensor& logits, const c10::optional<at::Tensor>& temperature, int64_t seed,
+                    const c10::optional<at::Tensor>& step, int64_t vocab_offset, at::Tensor& out_val,
+                    at::Tensor& out_idx) {
+  B200_CHECK_CUDA(logits);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: logits [rows, V]");
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 || logits.scalar_type() == at::kFloat, "sample: bf16/fp32");
+  TORCH_CHECK(out_val.scalar_type() == at::kFloat && out_idx.scalar_type() == at::kInt, "sample: outputs");
+  if (temperature.has_value()) TORCH_CHECK(temperature->scalar_type() == at::kFloat, "sample: temperature fp32");
+  if (step.has_value()) TORCH_CHECK(step->scalar_type() == at::kLong, "sample: step int64");
+  c10::cuda::CUDAGuard g(logits.device());
+  B200_LAUNCH(sample_rows(logits.data_ptr(), logits.scalar_type() == at::kFloat ? 1 : 0, logits.stride(0),
+                          logits.size(0), logits.size(1),
+                          temperature.has_value() ? temperature->data_ptr<float>() : nullptr, (uint64_t)seed,
+                          step.has_value() ? step->data_ptr<int64_t>() : nullptr, (int)vocab_offset,
+                          out_val.data_ptr<float>(), out_idx.data_ptr<int>(), cur_stream()));
+}
+
+void sample_combine_op(const at::Tensor& vals, const at::Tensor& idx, at::Tensor& out) {
+  B200_CHECK_CUDA(vals);
+  TORCH_CHECK(vals.dim() == 2 && idx.sizes() == vals.sizes() && out.scalar_type() == at::kLong, "combine: shapes");
+  c10::cuda::CUDAGuard g(vals.device());
+  B200_LAUNCH(sample_combine(vals.data_ptr<float>(), idx.data_ptr<int>(), vals.size(0), vals.size(1),
+                             out.data_ptr<int64_t>(), cur_stream()));
 }
 
 }  // namespace b200

@@ -1,0 +1,103 @@
+"""Public engine API.
+
+    engine = LLMEngine(EngineConfig(...))
+    engine.add_request(prompt_token_ids, SamplingParams(max_tokens=...))
+    while engine.has_unfinished():
+        for out in engine.step(): ...
+
+    LLM(cfg).generate(list_of_prompts, params) -> list[RequestOutput]
+
+Multi-GPU (tensor parallel) runs SPMD: one process per GPU, every rank runs
+the same scheduler on the same request stream (the API server broadcasts new
+requests from rank 0 over the gloo group), so all ranks build identical
+batches without a per-step metadata exchange; rank 0 returns outputs.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+
+import torch
+
+from ..config import EngineConfig
+from ..parallel import state as pstate
+from .request import Request, SamplingParams, Status
+from .runner import ModelRunner
+from .scheduler import Scheduler
+
+
+@dataclass
+class RequestOutput:
+    request_id: str
+    prompt_token_ids: list[int]
+    output_token_ids: list[int]
+    finished: bool
+    finish_reason: str | None = None
+    new_token_ids: list[int] | None = None
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig, model=None):
+        self.cfg = cfg
+        st = pstate.get()
+        if st.tp_size != cfg.parallel.tensor_parallel_size:
+            st = pstate.init(cfg.parallel.tensor_parallel_size, cfg.parallel.pipeline_parallel_size)
+        self.runner = ModelRunner(cfg, model)
+        self.scheduler = Scheduler(cfg.scheduler, cfg.cache, self.runner.block_pool, self.runner.slot_pool)
+        self.requests: dict[str, Request] = {}
+        self.num_steps = 0
+        self.eos_token_id: int | None = None
+
+    def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
+                    request_id: str | None = None) -> str:
+        req = Request(list(prompt_token_ids), params or SamplingParams(), request_id or "",
+                      eos_token_id=self.eos_token_id)
+        self.scheduler.add(req)
+        self.requests[req.request_id] = req
+        return req.request_id
+
+    def abort_request(self, request_id: str) -> None:
+        self.scheduler.abort(request_id)
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    def step(self) -> list[RequestOutput]:
+        out = self.scheduler.schedule()
+        if not out.reqs:
+            return []
+        before = {s.req.request_id: len(s.req.output_token_ids) for s in out.reqs}
+        sampled = self.runner.execute(out)
+        self.scheduler.update(out, sampled)
+        self.num_steps += 1
+        res = []
+        for s in out.reqs:
+            r = s.req
+            new = r.output_token_ids[before[r.request_id]:]
+            if new or r.status.finished:
+                res.append(RequestOutput(r.request_id, r.prompt_token_ids, list(r.output_token_ids),
+                                         r.status.finished,
+                                         r.status.value.replace("finished_", "") if r.status.finished else None, new))
+            if r.status.finished:
+                self.requests.pop(r.request_id, None)
+        return res
+
+
+class LLM:
+    """Offline batch generation over :class:`LLMEngine`."""
+
+    def __init__(self, cfg: EngineConfig, model=None):
+        self.engine = LLMEngine(cfg, model)
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
+                 ) -> list[RequestOutput]:
+        if not isinstance(params, list):
+            params = [params or SamplingParams()] * len(prompts)
+        ids = [self.engine.add_request(p, sp) for p, sp in zip(prompts, params)]
+        done: dict[str, RequestOutput] = {}
+        while self.engine.has_unfinished():
+            for o in self.engine.step():
+                if o.finished:
+                    done[o.request_id] = o
+        return [done[i] for i in ids]

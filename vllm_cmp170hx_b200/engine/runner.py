@@ -1,0 +1,303 @@
+"""Model runner: cache pools, batch preparation, eager and CUDA-graph execution,
+sampling.
+
+Per step the runner turns a :class:`SchedulerOutput` into the device tensors
+of a :class:`StepContext` (one host->device copy per tensor from pinned
+buffers), runs the model and the sampler, and copies the sampled token ids
+back.  Decode-only batches replay a CUDA graph captured per padded batch size
+(the reference's FULL decode graphs, vllm_sm80/worker/graph_mem_worker.py:64):
+padding rows point at the reserved KV block 0 and state slot 0 and write
+nothing (slot mapping -1).
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .. import _ext
+from ..config import EngineConfig
+from ..models.hybrid import HybridForCausalLM, StepContext
+from ..ops import sampling as sampling_ops
+from ..parallel import comm
+from ..parallel import state as pstate
+from .block_pool import SlotPool, make_block_pool
+from .scheduler import SchedulerOutput
+
+
+@dataclass
+class StepStats:
+    num_tokens: int = 0
+    graph: bool = False
+    h2d_bytes: int = 0
+    d2h_bytes: int = 0
+    device_ms: float = 0.0
+
+
+class ModelRunner:
+    def __init__(self, cfg: EngineConfig, model: HybridForCausalLM | None = None):
+        self.cfg = cfg
+        self.st = pstate.get()
+        self.device = torch.device(cfg.device if cfg.device != "cuda" else f"cuda:{self.st.local_rank}") \
+            if torch.cuda.is_available() and cfg.device.startswith("cuda") else torch.device("cpu")
+        self.model = model or HybridForCausalLM(cfg.model, self.device, cfg.seed)
+        self.mcfg = cfg.model
+        self.block_size = cfg.cache.block_size
+        assert self.block_size == 64, "the sparse-MLA kernels use 64-token blocks"
+        self.max_blocks_per_seq = math.ceil(cfg.scheduler.max_model_len / self.block_size)
+        self._alloc_caches()
+        self.step_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.graphs: dict[int, tuple] = {}
+        self.graph_pool = None
+        self.last_stats = StepStats()
+        self.time_device = False  # record CUDA events around each step's device work
+
+    # ------------------------------------------------------------------ caches
+    def _alloc_caches(self):
+        cfg = self.cfg
+        m = self.model
+        kda_ids, mla_ids = m.kda_layer_ids(), m.mla_layer_ids()
+        self.num_slots = cfg.scheduler.max_num_seqs + 1
+        rec_shape, conv_shape = m.kda_state_shapes()
+        nb = cfg.cache.num_blocks
+        if nb <= 0:
+            if self.device.type == "cuda":
+                torch.cuda.synchronize()
+                free, _total = torch.cuda.mem_get_info(self.device)
+                kda_bytes = len(kda_ids) * self.num_slots * (math.prod(rec_shape) * 4 + math.prod(conv_shape) * 2)
+                per_block = max(1, len(mla_ids)) * 64 * (576 * 2 + 128 + 4)
+                scratch = 6 << 30
+                avail = free * cfg.cache.gpu_memory_utilization - kda_bytes - scratch
+                nb = int(max(avail, 0) // per_block)
+                want = cfg.scheduler.max_num_seqs * self.max_blocks_per_seq + 1
+                nb = max(2, min(nb, want))
+            else:
+                nb = cfg.scheduler.max_num_seqs * self.max_blocks_per_seq + 1
+        self.num_blocks = nb
+        rows = nb * 64
+        self.mla_caches = {}
+        for i in mla_ids:
+            self.mla_caches[i] = (torch.zeros(rows, 576, dtype=torch.bfloat16, device=self.device),
+                                  torch.zeros(rows, 128, dtype=torch.uint8, device=self.device),
+                                  torch.ones(rows, dtype=torch.float32, device=self.device))
+        self.kda_states = {}
+        for i in kda_ids:
+            self.kda_states[i] = (torch.zeros(self.num_slots, *rec_shape, dtype=torch.float32, device=self.device),
+                                  torch.zeros(self.num_slots, *conv_shape, dtype=torch.bfloat16, device=self.device))
+        self.block_pool = make_block_pool(nb, 1)
+        self.slot_pool = SlotPool(self.num_slots, 1) if kda_ids else None
+
+    # ------------------------------------------------------------------ inputs
+    def _host_inputs(self, out: SchedulerOutput, pad_to: int | None = None):
+        reqs = out.reqs
+        S = len(reqs)
+        T = out.num_tokens
+        Sp = pad_to or S
+        Tp = T + (Sp - S)  # decode padding: one token per padded sequence
+        ids = np.zeros(Tp, dtype=np.int64)
+        pos = np.zeros(Tp, dtype=np.int32)
+        slots = np.full(Tp, -1, dtype=np.int64)
+        tseq = np.zeros(Tp, dtype=np.int32)
+        ctx = np.ones(Tp, dtype=np.int32)
+        cu = np.zeros(Sp + 1, dtype=np.int32)
+        kslot = np.zeros(Sp, dtype=np.int32)
+        hinit = np.zeros(Sp, dtype=np.int32)
+        bt = np.zeros((Sp, self.max_blocks_per_seq), dtype=np.int32)
+        temps = np.zeros(Sp, dtype=np.float32)
+        sample_rows = []
+        t = 0
+        max_ctx = 1
+        for i, s in enumerate(reqs):
+            r = s.req
+            toks = r.all_token_ids
+            n = s.num_new
+            a = s.start
+            seq_tokens = toks[a:a + n - s.num_draft] + list(r.draft_token_ids[: s.num_draft])
+            ids[t:t + n] = seq_tokens
+            p = np.arange(a, a + n, dtype=np.int32)
+            pos[t:t + n] = p
+            b = np.asarray(r.block_ids, dtype=np.int64)
+            slots[t:t + n] = b[p // 64] * 64 + p % 64
+            tseq[t:t + n] = i
+            ctx[t:t + n] = p + 1
+            max_ctx = max(max_ctx, a + n)
+            cu[i + 1] = cu[i] + n
+            kslot[i] = max(r.kda_slot, 0)
+            hinit[i] = 1 if a > 0 else 0
+            bt[i, : len(r.block_ids)] = r.block_ids
+            temps[i] = r.params.temperature
+            if s.sample:
+                if s.num_draft:
+                    sample_rows.extend(range(t, t + n))
+                else:
+                    sample_rows.append(t + n - 1)
+            t += n
+        for i in range(S, Sp):  # decode padding rows
+            cu[i + 1] = cu[i] + 1
+        return dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
+                    temps=temps, sample_rows=np.asarray(sample_rows, dtype=np.int64), max_ctx=max_ctx, T=Tp, S=Sp)
+
+    def _to_dev(self, a: np.ndarray, out: torch.Tensor | None = None) -> torch.Tensor:
+        t = torch.from_numpy(a)
+        if self.device.type == "cuda":
+            t = t.pin_memory()
+            if out is not None:
+                out.copy_(t, non_blocking=True)
+                return out
+            return t.to(self.device, non_blocking=True)
+        if out is not None:
+            out.copy_(t)
+            return out
+        return t
+
+    def _context(self, h: dict, bufs: dict | None = None, max_ctx: int | None = None) -> tuple:
+        b = bufs or {}
+        dev = {k: self._to_dev(h[k], b.get(k)) for k in ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit",
+                                                          "bt", "temps")}
+        ctx = StepContext(positions=dev["pos"], num_tokens=h["T"], slot_mapping=dev["slots"], token_seq=dev["tseq"],
+                          ctx_lens=dev["ctx"], block_table=dev["bt"], max_ctx=max_ctx or h["max_ctx"],
+                          cu_seqlens=dev["cu"], kda_slots=dev["kslot"], has_init=dev["hinit"],
+                          mla_caches=self.mla_caches, kda_states=self.kda_states,
+                          scores_buf=b.get("scores"))
+        nbytes = sum(h[k].nbytes for k in ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps"))
+        return dev, ctx, nbytes
+
+    # ------------------------------------------------------------------ forward + sample
+    def _forward_sample(self, ids, ctx, sample_rows, temps, seed):
+        hidden = self.model(ids, ctx)
+        hs = hidden if sample_rows is None else hidden.index_select(0, sample_rows)
+        logits = self.model.compute_logits(hs)
+        val, idx = sampling_ops.sample_local(logits, temps, seed, self.step_counter, self.model.vocab_offset)
+        if self.st.tp_size > 1:
+            vals = comm.tp_all_gather(val[None], dim=0)
+            idxs = comm.tp_all_gather(idx[None], dim=0)
+            return sampling_ops.combine(vals, idxs)
+        return idx.long()
+
+    @torch.inference_mode()
+    def execute(self, out: SchedulerOutput) -> dict[str, list[int]]:
+        if not out.reqs:
+            return {}
+        use_graph = (not self.cfg.enforce_eager and self.device.type == "cuda" and out.decode_only
+                     and all(s.num_draft == 0 for s in out.reqs)
+                     and len(out.reqs) <= max(self.cfg.cuda_graph_batch_sizes))
+        stats = StepStats(num_tokens=out.num_tokens, graph=use_graph)
+        if use_graph:
+            B = next(b for b in sorted(self.cfg.cuda_graph_batch_sizes) if b >= len(out.reqs))
+            if B not in self.graphs:
+                self._capture(B)
+            g, bufs, ids_out = self.graphs[B]
+            h = self._host_inputs(out, pad_to=B)
+            _, _, nbytes = self._context(h, bufs, self.cfg.scheduler.max_model_len)
+            ev = self._ev_start()
+            g.replay()
+            self._ev_end(ev)
+            tokens = ids_out[: len(out.reqs)]
+        else:
+            h = self._host_inputs(out)
+            dev, ctx, nbytes = self._context(h)
+            rows = self._to_dev(h["sample_rows"])
+            temps_rows = self._sample_temps(out, h)
+            ev = self._ev_start()
+            tokens = self._forward_sample(dev["ids"], ctx, rows, temps_rows, self.cfg.seed)
+            self._ev_end(ev)
+        self.step_counter += 1
+        host = tokens.to("cpu", non_blocking=False).tolist()
+        if self._events is not None:
+            stats.device_ms = self._events[0].elapsed_time(self._events[1])
+            self._events = None
+        stats.h2d_bytes = nbytes
+        stats.d2h_bytes = tokens.numel() * tokens.element_size()
+        self.last_stats = stats
+        if self.device.type == "cuda":
+            _ext.check_status(self.device)
+        return self._split_tokens(out, host)
+
+    _events = None
+
+    def _ev_start(self):
+        if not (self.time_device and self.device.type == "cuda"):
+            return None
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        return (a, b)
+
+    def _ev_end(self, ev):
+        if ev is not None:
+            ev[1].record()
+            self._events = ev
+
+    def _sample_temps(self, out, h):
+        temps = []
+        for s in out.reqs:
+            if s.sample:
+                temps.extend([s.req.params.temperature] * (s.num_new if s.num_draft else 1))
+        if not temps or all(t <= 0 for t in temps):
+            return None
+        return self._to_dev(np.asarray(temps, dtype=np.float32))
+
+    @staticmethod
+    def _split_tokens(out: SchedulerOutput, host: list[int]) -> dict[str, list[int]]:
+        res = {}
+        k = 0
+        for s in out.reqs:
+            if not s.sample:
+                continue
+            if s.num_draft:
+                # verify: accept drafts while they match the target's choice, then the bonus token
+                cand = host[k:k + s.num_new]
+                k += s.num_new
+                drafts = s.req.draft_token_ids[: s.num_draft]
+                acc = []
+                for j, d in enumerate(drafts):
+                    acc.append(cand[j])
+                    if cand[j] != d:
+                        break
+                else:
+                    acc.append(cand[s.num_draft])
+                res[s.req.request_id] = acc
+            else:
+                res[s.req.request_id] = [host[k]]
+                k += 1
+        return res
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def _capture(self, B: int):
+        dev = self.device
+        mml = self.cfg.scheduler.max_model_len
+        bufs = dict(ids=torch.zeros(B, dtype=torch.int64, device=dev), pos=torch.zeros(B, dtype=torch.int32, device=dev),
+                    slots=torch.full((B,), -1, dtype=torch.int64, device=dev),
+                    tseq=torch.arange(B, dtype=torch.int32, device=dev),
+                    ctx=torch.ones(B, dtype=torch.int32, device=dev),
+                    cu=torch.arange(B + 1, dtype=torch.int32, device=dev),
+                    kslot=torch.zeros(B, dtype=torch.int32, device=dev),
+                    hinit=torch.zeros(B, dtype=torch.int32, device=dev),
+                    bt=torch.zeros(B, self.max_blocks_per_seq, dtype=torch.int32, device=dev),
+                    temps=torch.zeros(B, dtype=torch.float32, device=dev),
+                    scores=torch.empty(B, mml, dtype=torch.float32, device=dev))
+        ctx = StepContext(positions=bufs["pos"], num_tokens=B, slot_mapping=bufs["slots"], token_seq=bufs["tseq"],
+                          ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
+                          kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
+                          kda_states=self.kda_states, scores_buf=bufs["scores"])
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        if self.graph_pool is None:
+            self.graph_pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g, pool=self.graph_pool):
+            ids_out = self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed)
+        torch.cuda.synchronize(dev)
+        self.graphs[B] = (g, bufs, ids_out)
+
+    def release_graphs(self):
+        self.graphs.clear()
+        self.graph_pool = None

@@ -1,0 +1,212 @@
+"""Continuous-batching scheduler with chunked prefill.
+
+Each step gets a token budget (`max_num_batched_tokens`).  Running requests
+are served first: a decoding request takes 1 token (plus its draft tokens
+under speculative decoding), a request still in prefill takes the next chunk
+of its prompt.  Waiting requests are admitted while budget, sequence slots,
+KV blocks and recurrent-state slots last.  A request that cannot grow its KV
+is handled by preempting the most recently admitted running request
+(recompute: its blocks and state slot are freed and it re-enters the queue
+head with `num_computed_tokens = 0`).
+
+Fair chunked prefill (the reference's `--prefill-chunk-with-decodes`,
+`--max-num-partial-prefills`, vllm_sm80/sched/step.py:36 Sm80Step): at most
+`max_num_partial_prefills` requests are in a partial prefill at once and a
+request's chunk is capped at `long_prefill_token_threshold` when set, so
+decodes keep flowing while long prompts are chunked.
+"""
+
+from __future__ import annotations
+
+import collections
+import time
+from dataclasses import dataclass, field
+
+from ..config import CacheConfig, SchedulerConfig
+from .request import Request, Status
+
+
+@dataclass
+class ScheduledReq:
+    req: Request
+    num_new: int  # tokens computed this step
+    start: int  # first position computed this step
+    sample: bool  # the step ends at the request's last known token -> sample
+    num_draft: int = 0
+
+
+@dataclass
+class SchedulerOutput:
+    reqs: list[ScheduledReq] = field(default_factory=list)
+    preempted: list[Request] = field(default_factory=list)
+
+    @property
+    def num_tokens(self) -> int:
+        return sum(s.num_new for s in self.reqs)
+
+    @property
+    def decode_only(self) -> bool:
+        return bool(self.reqs) and all(s.num_new == 1 + s.num_draft and s.start > 0 for s in self.reqs)
+
+
+class Scheduler:
+    def __init__(self, sched: SchedulerConfig, cache: CacheConfig, block_pool, slot_pool=None):
+        self.cfg = sched
+        self.block_size = cache.block_size
+        self.blocks = block_pool
+        self.slots = slot_pool
+        self.waiting: collections.deque[Request] = collections.deque()
+        self.running: list[Request] = []
+        self.finished: list[Request] = []
+
+    # ------------------------------------------------------------------ API
+    def add(self, req: Request) -> None:
+        if req.num_prompt_tokens + req.params.max_tokens > self.cfg.max_model_len:
+            req.params.max_tokens = max(1, self.cfg.max_model_len - req.num_prompt_tokens)
+        if req.num_prompt_tokens >= self.cfg.max_model_len:
+            raise ValueError(f"prompt of {req.num_prompt_tokens} tokens exceeds max_model_len {self.cfg.max_model_len}")
+        req.arrival = req.arrival or time.monotonic()
+        self.waiting.append(req)
+
+    def abort(self, request_id: str) -> bool:
+        for q in (self.running, self.waiting):
+            for r in list(q):
+                if r.request_id == request_id:
+                    q.remove(r)
+                    r.status = Status.FINISHED_ABORTED
+                    self._release(r)
+                    return True
+        return False
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    # ------------------------------------------------------------------ helpers
+    def _blocks_needed(self, req: Request, upto: int) -> int:
+        need = (upto + self.block_size - 1) // self.block_size
+        return max(0, need - len(req.block_ids))
+
+    def _grow(self, req: Request, upto: int) -> bool:
+        n = self._blocks_needed(req, upto)
+        if n == 0:
+            return True
+        if self.blocks.num_free() < n:
+            return False
+        req.block_ids.extend(int(b) for b in self.blocks.allocate(n))
+        return True
+
+    def _release(self, req: Request) -> None:
+        if req.block_ids:
+            self.blocks.free(req.block_ids)
+            req.block_ids = []
+        if self.slots is not None and req.kda_slot > 0:
+            self.slots.free(req.kda_slot)
+        req.kda_slot = -1
+
+    def _preempt(self, victim: Request, out: SchedulerOutput) -> None:
+        self.running.remove(victim)
+        self._release(victim)
+        victim.num_computed_tokens = 0
+        victim.num_preemptions += 1
+        victim.status = Status.PREEMPTED
+        victim.draft_token_ids = []
+        self.waiting.appendleft(victim)
+        out.preempted.append(victim)
+
+    # ------------------------------------------------------------------ schedule
+    def schedule(self) -> SchedulerOutput:
+        out = SchedulerOutput()
+        budget = self.cfg.max_num_batched_tokens
+        partial = 0
+        cap = self.cfg.long_prefill_token_threshold or budget
+        scheduled_ids = set()
+        i = 0
+        while i < len(self.running):
+            req = self.running[i]
+            remaining = req.num_tokens - req.num_computed_tokens
+            if remaining > 1 or (req.num_computed_tokens == 0):
+                # still in prefill (the last prompt token is computed together with sampling)
+                if partial >= self.cfg.max_num_partial_prefills:
+                    i += 1
+                    continue
+                n = min(remaining, budget, cap)
+                drafts = 0
+            else:
+                drafts = len(req.draft_token_ids)
+                n = 1 + drafts
+            if n <= 0 or n > budget:
+                i += 1
+                continue
+            upto = req.num_computed_tokens + n
+            while not self._grow(req, upto):
+                victim = self.running[-1]
+                if victim is req:
+                    break
+                self._preempt(victim, out)
+            if self._blocks_needed(req, upto) > 0:
+                # could not make room even alone: preempt this one
+                self._preempt(req, out)
+                continue
+            sample = upto >= req.num_tokens
+            if not sample:
+                partial += 1
+            out.reqs.append(ScheduledReq(req, n, req.num_computed_tokens, sample, drafts))
+            scheduled_ids.add(req.request_id)
+            budget -= n
+            i += 1
+        # admit waiting requests
+        while self.waiting and budget > 0 and len(self.running) < self.cfg.max_num_seqs:
+            req = self.waiting[0]
+            if partial >= self.cfg.max_num_partial_prefills and req.num_tokens > budget:
+                break
+            n = min(req.num_tokens - req.num_computed_tokens, budget, cap)
+            if self._blocks_needed(req, req.num_computed_tokens + n) > self.blocks.num_free():
+                break
+            if self.slots is not None and req.kda_slot <= 0 and self.slots.num_free() == 0:
+                break
+            self.waiting.popleft()
+            if self.slots is not None and req.kda_slot <= 0:
+                req.kda_slot = self.slots.allocate()
+            self._grow(req, req.num_computed_tokens + n)
+            req.status = Status.RUNNING
+            self.running.append(req)
+            sample = req.num_computed_tokens + n >= req.num_tokens
+            if not sample:
+                partial += 1
+            out.reqs.append(ScheduledReq(req, n, req.num_computed_tokens, sample, 0))
+            budget -= n
+        return out
+
+    # ------------------------------------------------------------------ update
+    def update(self, out: SchedulerOutput, sampled: dict[str, list[int]]) -> list[Request]:
+        """Advance computed counts, append sampled tokens (accepted drafts + the
+        bonus token under speculative decoding) and retire finished requests."""
+        now = time.monotonic()
+        done = []
+        for s in out.reqs:
+            req = s.req
+            if req.status.finished:
+                continue
+            toks = sampled.get(req.request_id, [])
+            if s.num_draft:
+                # verify step: positions of rejected drafts are recomputed later
+                accepted = max(0, len(toks) - 1)
+                req.num_computed_tokens = s.start + 1 + accepted
+            else:
+                req.num_computed_tokens = s.start + s.num_new
+            req.draft_token_ids = []
+            for t in toks:
+                req.output_token_ids.append(int(t))
+                if req.first_token_time is None:
+                    req.first_token_time = now
+                req.token_times.append(now)
+                if req.check_stop():
+                    break
+            if req.status.finished:
+                done.append(req)
+        for req in done:
+            if req in self.running:
+                self.running.remove(req)
+            self._release(req)
+            self.finished.append(req)
+        return done

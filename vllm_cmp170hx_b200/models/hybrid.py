@@ -1,0 +1,378 @@
+"""Hybrid KDA / sparse-MLA MoE causal LM (the GLM-5.3-Flash family of the
+reference, vllm_sm80/models/glm5next/sm80_model.py:112-434, in the shapes of
+BASELINE config 3), and the DeepSeek-style all-MLA variant (config 4) through
+the same classes.
+
+Per layer: RMSNorm -> attention (KDA or sparse MLA) -> row-parallel
+projection + TP all-reduce -> fused residual-add RMSNorm -> MoE (router,
+routed experts, shared expert) or dense MLP -> TP all-reduce.
+
+Tensor parallel: attention heads and expert intermediates are split across
+the TP group (whole H128 blocks for EXL3 experts, as the reference's
+`aligned_shard`, vllm_sm80/kernels/exl3/utils.py:146); the indexer, router
+and embedding are replicated; the LM head is vocab-parallel and sampling
+combines per-rank winners without gathering logits.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+
+from .. import ops
+from ..config import ModelConfig
+from ..formats import exl3 as fx
+from ..ops import kda as kda_ops
+from ..ops import mla as mla_ops
+from ..ops import moe as moe_ops
+from ..oracle import mla as mla_ref
+from ..parallel import comm
+from ..parallel import state as pstate
+from .layers import Linear, RMSNorm, WeightInit, default_std
+
+
+@dataclass
+class StepContext:
+    """Device tensors describing one forward batch (built by the runner)."""
+
+    positions: torch.Tensor  # [T] int32
+    num_tokens: int
+    # sparse-MLA (paged latent cache, block 64)
+    slot_mapping: torch.Tensor | None = None  # [T] int64 cache rows of the new tokens
+    token_seq: torch.Tensor | None = None  # [T] int32 sequence index of each token
+    ctx_lens: torch.Tensor | None = None  # [T] int32 visible positions (pos + 1)
+    block_table: torch.Tensor | None = None  # [S, max_blocks] int32
+    max_ctx: int = 0  # host bound of ctx_lens (indexer score width)
+    # KDA (per-sequence recurrent state slots)
+    cu_seqlens: torch.Tensor | None = None  # [S + 1] int32
+    kda_slots: torch.Tensor | None = None  # [S] int32
+    has_init: torch.Tensor | None = None  # [S] int32
+    # caches, by layer index
+    mla_caches: dict = field(default_factory=dict)  # i -> (latent [rows, 576], idx_k [rows, 128] u8, idx_s [rows])
+    kda_states: dict = field(default_factory=dict)  # i -> (rec [slots, H, 128, 128] f32, conv [slots, 3HD, 3])
+    scores_buf: torch.Tensor | None = None
+
+
+# ============================================================================ attention
+class KDAAttention(nn.Module):
+    """Kimi-delta attention layer (GLM `linear_attention`): fused input GEMM
+    [q | k | v | f_a | g_a | beta], low-rank gate up-projections f_b / g_b, the
+    fused conv + gates + recurrence + gated-norm kernel, row-parallel o_proj."""
+
+    def __init__(self, cfg: ModelConfig, wi: WeightInit, tp: int, tp_rank: int):
+        super().__init__()
+        k = cfg.kda
+        H, D = k.num_heads, k.head_dim
+        assert H % tp == 0 and D == 128
+        self.H = H // tp
+        self.D = D
+        self.lower_bound = k.lower_bound
+        hid = cfg.hidden_size
+        HD = self.H * D
+        sd = default_std(hid)
+        # fused input projection: q, k, v (this rank's heads) | f_a | g_a (replicated rank-D) | beta
+        wq = wi.normal((H * D, hid), sd, (0, tp_rank, tp))
+        wk = wi.normal((H * D, hid), sd, (0, tp_rank, tp))
+        wv = wi.normal((H * D, hid), sd, (0, tp_rank, tp))
+        wfa = wi.normal((D, hid), sd)
+        wga = wi.normal((D, hid), sd)
+        wb = wi.normal((H, hid), sd, (0, tp_rank, tp))
+        rows = 3 * HD + 2 * D + self.H
+        pad = (-rows) % 8  # keep the fused output's row stride 16-byte aligned (TMA)
+        wpad = torch.zeros(pad, hid, dtype=wq.dtype, device=wq.device)
+        self.in_proj = Linear(torch.cat([wq, wk, wv, wfa, wga, wb, wpad], dim=0).contiguous())
+        self.f_b = Linear(wi.normal((H * D, D), default_std(D), (0, tp_rank, tp)))
+        self.g_b = Linear(wi.normal((H * D, D), default_std(D), (0, tp_rank, tp)))
+        self.conv_w = nn.Parameter(wi.normal((3 * H * D, 4), 0.5, None).view(3, H, D, 4)[:, tp_rank * self.H:
+                                   (tp_rank + 1) * self.H].reshape(3 * HD, 4).contiguous(), requires_grad=False)
+        self.a_log = nn.Parameter(wi.uniform((H,), -1.0, 1.0)[tp_rank * self.H:(tp_rank + 1) * self.H].contiguous(),
+                                  requires_grad=False)
+        self.g_bias = nn.Parameter(wi.uniform((H * D,), -0.1, 0.1)[tp_rank * HD:(tp_rank + 1) * HD].contiguous(),
+                                   requires_grad=False)
+        self.norm_w = nn.Parameter(wi.ones_plus(D, 0.05), requires_grad=False)
+        self.o_proj = Linear(wi.normal((hid, H * D), default_std(H * D), (1, tp_rank, tp)))
+
+    def forward(self, x: torch.Tensor, ctx: StepContext, layer_idx: int) -> torch.Tensor:
+        rec, conv = ctx.kda_states[layer_idx]
+        proj = self.in_proj(x)
+        HD = self.H * self.D
+        qkv = proj[:, : 3 * HD]
+        fa = proj[:, 3 * HD: 3 * HD + self.D]
+        ga = proj[:, 3 * HD + self.D: 3 * HD + 2 * self.D]
+        beta = proj[:, 3 * HD + 2 * self.D: 3 * HD + 2 * self.D + self.H]
+        g_raw = self.f_b(fa)
+        g2 = self.g_b(ga)
+        o = kda_ops.kda_forward(qkv, g_raw, beta, g2, ctx.cu_seqlens, ctx.kda_slots, ctx.has_init, conv, self.conv_w,
+                                None, self.a_log, self.g_bias, self.lower_bound, self.norm_w, rec)
+        return self.o_proj(o)
+
+
+class MLAAttention(nn.Module):
+    """DeepSeek-V3.2-style sparse MLA with the lightning indexer
+    (vllm_sm80/models/glm5next/sm80_mla.py, sm80_indexer.py): absorbed
+    q_nope, paged latent cache (block 64), fp8 indexer top-k, latent
+    attention over the selected rows, per-head V up-projection, o_proj."""
+
+    def __init__(self, cfg: ModelConfig, wi: WeightInit, tp: int, tp_rank: int):
+        super().__init__()
+        m = cfg.mla
+        self.m = m
+        hid = cfg.hidden_size
+        assert m.num_heads % tp == 0
+        self.H = m.num_heads // tp
+        self.eps = cfg.rms_eps
+        sd = default_std(hid)
+        ql, kvl = m.q_lora_rank, m.kv_lora_rank
+        self.ql, self.kvl = ql, kvl
+        dn, dr, dv = m.qk_nope_head_dim, m.qk_rope_head_dim, m.v_head_dim
+        self.dn, self.dr, self.dv = dn, dr, dv
+        assert kvl == 512 and dr == 64 and m.index_head_dim == 128
+        # fused first projection: q_a | kv_a (512 + 64) | indexer k (128) | indexer head weights
+        self.in_splits = [ql, kvl + dr, m.index_head_dim, m.index_n_heads]
+        self.in_proj = Linear(torch.cat([wi.normal((ql, hid), sd), wi.normal((kvl + dr, hid), sd),
+                                         wi.normal((m.index_head_dim, hid), sd),
+                                         wi.normal((m.index_n_heads, hid), sd)], dim=0).contiguous())
+        self.q_a_norm = RMSNorm(wi.ones_plus(ql, 0.05), cfg.rms_eps)
+        self.kv_a_norm_w = nn.Parameter(wi.ones_plus(kvl, 0.05), requires_grad=False)
+        self.q_b = Linear(wi.normal((m.num_heads * (dn + dr), ql), default_std(ql), (0, tp_rank, tp)))
+        # kv_b: [H*(dn + dv), kvl] -> absorbed per-head W_UK [H, dn, kvl], W_UV [H, kvl, dv]
+        kvb = wi.normal((m.num_heads, dn + dv, kvl), default_std(kvl), (0, tp_rank, tp))
+        self.w_uk = nn.Parameter(kvb[:, :dn, :].contiguous(), requires_grad=False)  # [H, dn, kvl]
+        self.w_uv_t = nn.Parameter(kvb[:, dn:, :].contiguous(), requires_grad=False)  # [H, dv, kvl]
+        self.o_proj = Linear(wi.normal((hid, m.num_heads * dv), default_std(m.num_heads * dv), (1, tp_rank, tp)))
+        # indexer
+        self.idx_q = Linear(wi.normal((m.index_n_heads * m.index_head_dim, ql), default_std(ql)))
+        self.idx_k_ln_w = nn.Parameter(wi.ones_plus(m.index_head_dim, 0.05), requires_grad=False)
+        self.idx_k_ln_b = nn.Parameter(torch.zeros(m.index_head_dim, dtype=torch.bfloat16, device=wi.device),
+                                       requires_grad=False)
+        self.sm_scale = 1.0 / math.sqrt(dn + dr)
+        self.idx_wscale = m.index_n_heads ** -0.5 * m.index_head_dim ** -0.5
+        self.register_buffer("cos_sin", mla_ref.rope_cos_sin(min(cfg.max_position, 1 << 17), dr, m.rope_theta,
+                                                             wi.device), persistent=False)
+
+    def forward(self, x: torch.Tensor, ctx: StepContext, layer_idx: int) -> torch.Tensor:
+        latent, idx_k, idx_s = ctx.mla_caches[layer_idx]
+        T = x.shape[0]
+        m = self.m
+        proj = self.in_proj(x)
+        ql, kvl, dr = self.ql, self.kvl, self.dr
+        q_lat = self.q_a_norm(proj[:, :ql].contiguous())
+        kv = proj[:, ql: ql + kvl + dr]
+        k_idx = proj[:, ql + kvl + dr: ql + kvl + dr + m.index_head_dim]
+        w_idx = proj[:, ql + kvl + dr + m.index_head_dim:]
+        pos = ctx.positions
+        # caches for the new tokens
+        mla_ops.latent_cache_write(kv, self.kv_a_norm_w, self.eps, pos, self.cos_sin, m.rope_interleave,
+                                   ctx.slot_mapping, latent)
+        mla_ops.index_k_write(k_idx, self.idx_k_ln_w, self.idx_k_ln_b, 1e-6, pos, self.cos_sin, m.rope_interleave,
+                              ctx.slot_mapping, idx_k, idx_s)
+        # indexer top-k
+        iq = self.idx_q(q_lat).view(T, m.index_n_heads, m.index_head_dim)
+        q8, wq = mla_ops.index_q_prep(iq, pos, self.cos_sin, m.rope_interleave, w_idx, self.idx_wscale)
+        indices, counts = mla_ops.indexer_topk(q8, wq, idx_k, idx_s, ctx.ctx_lens, ctx.token_seq, ctx.block_table, 64,
+                                               m.index_topk, ctx.max_ctx, ctx.scores_buf)
+        # queries: rope part, absorbed nope part
+        q = self.q_b(q_lat).view(T, self.H, self.dn + dr)
+        mla_ops.rope_(q, pos, self.cos_sin, self.dn, dr, m.rope_interleave)
+        qf = torch.empty(T, self.H, kvl + dr, dtype=torch.bfloat16, device=x.device)
+        torch.bmm(q[:, :, : self.dn].transpose(0, 1), self.w_uk, out=qf[:, :, :kvl].transpose(0, 1))
+        qf[:, :, kvl:] = q[:, :, self.dn:]
+        o_lat = mla_ops.sparse_attention(qf, latent, indices, counts, self.sm_scale)
+        o = torch.bmm(o_lat.transpose(0, 1), self.w_uv_t.transpose(1, 2))  # [H, T, dv]
+        return self.o_proj(o.transpose(0, 1).reshape(T, self.H * self.dv))
+
+
+# ============================================================================ MLPs
+class DenseMLP(nn.Module):
+    def __init__(self, hid: int, inter: int, wi: WeightInit, tp: int, tp_rank: int, limit: float = 0.0):
+        super().__init__()
+        g = wi.normal((inter, hid), default_std(hid), (0, tp_rank, tp))
+        u = wi.normal((inter, hid), default_std(hid), (0, tp_rank, tp))
+        self.gate_up = Linear(torch.cat([g, u], dim=0).contiguous())
+        self.down = Linear(wi.normal((hid, inter), default_std(inter), (1, tp_rank, tp)))
+        self.limit = limit
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down(ops.silu_mul(self.gate_up(x), self.limit))
+
+
+def random_exl3_experts(E: int, hid: int, inter_local: int, bits_x2: int, codebook: int, wi: WeightInit,
+                        tp: int, tp_rank: int, limit: float) -> moe_ops.Exl3Experts:
+    """Random-init EXL3 experts (every 16-bit state is a valid code; suh = +-1,
+    svh = +-1/sqrt(K))."""
+    dev = wi.device
+    S = 8 * bits_x2
+    if wi.mode == "sliced":
+        inter = inter_local * tp
+        mats = {w: [] for w in ("gate", "up", "down")}
+        g = torch.Generator().manual_seed(wi.seed * 31 + 17)
+        for _ in range(E):
+            mats["gate"].append(fx.random_matrix(hid, inter, bits_x2, codebook, generator=g))
+            mats["up"].append(fx.random_matrix(hid, inter, bits_x2, codebook, generator=g))
+            mats["down"].append(fx.random_matrix(inter, hid, bits_x2, codebook, generator=g))
+        sl = slice(tp_rank * inter_local, (tp_rank + 1) * inter_local)
+        tsl = slice(tp_rank * inter_local // 16, (tp_rank + 1) * inter_local // 16)
+
+        def cut(m, which):
+            if which == "down":
+                return fx.Exl3Matrix(m.trellis[tsl].contiguous(), m.suh[sl].contiguous(), m.svh, bits_x2, codebook,
+                                     inter_local, hid)
+            return fx.Exl3Matrix(m.trellis[:, tsl].contiguous(), m.suh, m.svh[sl].contiguous(), bits_x2, codebook, hid,
+                                 inter_local)
+
+        ex = moe_ops.Exl3Experts.from_matrices([cut(m, "gate") for m in mats["gate"]],
+                                               [cut(m, "up") for m in mats["up"]],
+                                               [cut(m, "down") for m in mats["down"]], swiglu_limit=limit)
+        return ex.to(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(wi.seed * 7 + 1000 * pstate.get().rank + 3)
+
+    def trellis(k, n):
+        return torch.randint(-32768, 32768, (E, k // 16, n // 16, S), dtype=torch.int16, device=dev, generator=gen)
+
+    def signs(n, scale):
+        return ((torch.randint(0, 2, (E, n), device=dev, generator=gen) * 2 - 1) * scale).to(torch.float16)
+
+    return moe_ops.Exl3Experts(
+        gate_trellis=trellis(hid, inter_local), up_trellis=trellis(hid, inter_local),
+        down_trellis=trellis(inter_local, hid), gate_suh=signs(hid, 1.0), up_suh=signs(hid, 1.0),
+        down_suh=signs(inter_local, 1.0), gate_svh=signs(inter_local, hid ** -0.5),
+        up_svh=signs(inter_local, hid ** -0.5), down_svh=signs(hid, (inter_local * tp) ** -0.5), bits_x2=bits_x2,
+        codebook=codebook, hidden=hid, intermediate=inter_local, swiglu_limit=limit)
+
+
+class BF16Experts(nn.Module):
+    """Unquantised experts (tests / small models): per-expert loop on the GPU GEMM."""
+
+    def __init__(self, E: int, hid: int, inter_local: int, wi: WeightInit, tp: int, tp_rank: int, limit: float):
+        super().__init__()
+        self.gate_up = nn.Parameter(torch.stack([torch.cat([
+            wi.normal((inter_local * tp, hid), default_std(hid), (0, tp_rank, tp)),
+            wi.normal((inter_local * tp, hid), default_std(hid), (0, tp_rank, tp))]) for _ in range(E)]),
+            requires_grad=False)
+        self.down = nn.Parameter(torch.stack([wi.normal((hid, inter_local * tp), default_std(inter_local * tp),
+                                                        (1, tp_rank, tp)) for _ in range(E)]), requires_grad=False)
+        self.limit = limit
+
+    def forward(self, x, ids, w, add=None):
+        out = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32, device=x.device)
+        for e in range(self.gate_up.shape[0]):
+            mask = ids == e
+            rows = mask.any(-1).nonzero()[:, 0]
+            if rows.numel() == 0:
+                continue
+            h = ops.silu_mul(ops.gemm(x[rows], self.gate_up[e]), self.limit)
+            y = ops.gemm(h, self.down[e]).float()
+            out[rows] += (w * mask).sum(-1)[rows, None] * y
+        if add is not None:
+            out += add.float()
+        return out.to(x.dtype)
+
+
+class MoE(nn.Module):
+    def __init__(self, cfg: ModelConfig, wi: WeightInit, tp: int, tp_rank: int):
+        super().__init__()
+        mc = cfg.moe
+        self.mc = mc
+        hid = cfg.hidden_size
+        assert mc.intermediate % tp == 0
+        inter_local = mc.intermediate // tp
+        self.gate = Linear(wi.normal((mc.num_experts, hid), default_std(hid)))
+        self.e_bias = None
+        if mc.router != "softmax":
+            self.e_bias = nn.Parameter(wi.uniform((mc.num_experts,), -0.05, 0.05), requires_grad=False)
+        if mc.expert_format == "exl3":
+            assert inter_local % 128 == 0, "EXL3 TP cuts must keep whole H128 blocks"
+            self.experts = random_exl3_experts(mc.num_experts, hid, inter_local, mc.exl3_bits_x2, mc.exl3_codebook,
+                                               wi, tp, tp_rank, mc.swiglu_limit)
+        elif mc.expert_format == "bf16":
+            self.experts = BF16Experts(mc.num_experts, hid, inter_local, wi, tp, tp_rank, mc.swiglu_limit)
+        else:
+            from . import marlin_experts
+            self.experts = marlin_experts.random_marlin_experts(mc.num_experts, hid, inter_local, wi, tp, tp_rank)
+        self.shared = None
+        if mc.num_shared:
+            self.shared = DenseMLP(hid, mc.shared_intermediate * mc.num_shared, wi, tp, tp_rank, mc.swiglu_limit)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        logits = self.gate(x, out_dtype=torch.float32)
+        ids, w = moe_ops.topk(logits, self.mc.top_k, self.mc.router_mode, self.e_bias, self.mc.routed_scaling,
+                              self.mc.renormalize)
+        shared = self.shared(x) if self.shared is not None else None
+        if isinstance(self.experts, moe_ops.Exl3Experts):
+            return moe_ops.exl3_moe(x, ids, w, self.experts, add=shared)
+        return self.experts(x, ids, w, add=shared)
+
+
+# ============================================================================ model
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: ModelConfig, idx: int, wi: WeightInit, tp: int, tp_rank: int):
+        super().__init__()
+        self.idx = idx
+        self.kind = cfg.layer_types[idx]
+        self.input_norm = RMSNorm(wi.ones_plus(cfg.hidden_size, 0.05), cfg.rms_eps)
+        self.post_norm = RMSNorm(wi.ones_plus(cfg.hidden_size, 0.05), cfg.rms_eps)
+        self.attn = (KDAAttention if self.kind == "kda" else MLAAttention)(cfg, wi, tp, tp_rank)
+        mt = cfg.mlp_types[idx]
+        if mt == "moe":
+            self.mlp = MoE(cfg, wi, tp, tp_rank)
+        elif mt == "dense":
+            self.mlp = DenseMLP(cfg.hidden_size, cfg.dense_intermediate, wi, tp, tp_rank)
+        else:
+            self.mlp = None
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None, ctx: StepContext):
+        if residual is None:
+            residual = x
+            h = self.input_norm(x)
+        else:
+            h = self.input_norm(x, residual)
+        a = comm.tp_all_reduce(self.attn(h, ctx, self.idx))
+        if self.mlp is None:
+            residual = residual + a
+            return a, residual
+        h = self.post_norm(a, residual)
+        return comm.tp_all_reduce(self.mlp(h)), residual
+
+
+class HybridForCausalLM(nn.Module):
+    def __init__(self, cfg: ModelConfig, device="cuda", seed: int = 0, init_mode: str = "local"):
+        super().__init__()
+        st = pstate.get()
+        tp, tp_rank = st.tp_size, st.tp_rank
+        self.cfg = cfg
+        wi = WeightInit(seed, device, init_mode)
+        self.embed = nn.Parameter(wi.normal((cfg.vocab_size, cfg.hidden_size), 1.0), requires_grad=False)
+        self.layers = nn.ModuleList([DecoderLayer(cfg, i, wi, tp, tp_rank) for i in range(cfg.num_layers)])
+        self.norm = RMSNorm(wi.ones_plus(cfg.hidden_size, 0.05), cfg.rms_eps)
+        assert cfg.vocab_size % tp == 0
+        self.vocab_local = cfg.vocab_size // tp
+        self.vocab_offset = tp_rank * self.vocab_local
+        self.lm_head = Linear(wi.normal((cfg.vocab_size, cfg.hidden_size), default_std(cfg.hidden_size),
+                                        (0, tp_rank, tp)))
+
+    def forward(self, input_ids: torch.Tensor, ctx: StepContext) -> torch.Tensor:
+        x = self.embed[input_ids]
+        residual = None
+        for layer in self.layers:
+            x, residual = layer(x, residual, ctx)
+        return self.norm(x, residual)
+
+    def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """This rank's vocab shard of the logits [rows, V / tp] (bf16)."""
+        return self.lm_head(hidden)
+
+    # ------------------------------------------------------------------ cache geometry
+    def kda_state_shapes(self):
+        st = pstate.get()
+        H = self.cfg.kda.num_heads // st.tp_size
+        return (H, 128, 128), (3 * H * 128, 3)
+
+    def kda_layer_ids(self):
+        return [i for i, t in enumerate(self.cfg.layer_types) if t == "kda"]
+
+    def mla_layer_ids(self):
+        return [i for i, t in enumerate(self.cfg.layer_types) if t == "mla"]

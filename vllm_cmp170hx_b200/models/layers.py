@@ -1,0 +1,97 @@
+"""Model building blocks over the package's ops (tcgen05 kernels on GPU,
+oracles on CPU) and the TP collectives.
+
+Weights are created by a :class:`WeightInit` that either draws the full
+logical tensor from a seeded CPU generator and keeps this rank's shard
+(`mode="sliced"`: the same model at every TP size, used by tests) or draws
+only the local shard on the device (`mode="local"`: fast random init of the
+BASELINE-sized models for benchmarks).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import nn
+
+from .. import ops
+from ..parallel import comm
+from ..parallel import state as pstate
+
+
+class WeightInit:
+    def __init__(self, seed: int, device, mode: str = "local", dtype=torch.bfloat16):
+        self.seed = seed
+        self.device = torch.device(device)
+        self.mode = mode
+        self.dtype = dtype
+        self._n = 0
+
+    def _gen(self, device) -> torch.Generator:
+        self._n += 1
+        g = torch.Generator(device=device)
+        st = pstate.get()
+        salt = 0 if self.mode == "sliced" else 7919 * st.rank
+        g.manual_seed(self.seed * 1000003 + self._n * 9973 + salt)
+        return g
+
+    def normal(self, shape, std: float, shard: tuple[int, int, int] | None = None, dtype=None) -> torch.Tensor:
+        """shard = (dim, rank, size): keep this rank's contiguous part along dim."""
+        dtype = dtype or self.dtype
+        if self.mode == "sliced" or self.device.type == "cpu":
+            t = torch.randn(*shape, generator=self._gen("cpu")) * std
+            if shard is not None:
+                d, r, n = shard
+                t = t.chunk(n, dim=d)[r]
+            return t.to(dtype).contiguous().to(self.device)
+        local = list(shape)
+        if shard is not None:
+            d, _, n = shard
+            local[d] //= n
+        return (torch.randn(*local, generator=self._gen(self.device), device=self.device) * std).to(dtype)
+
+    def ones_plus(self, n: int, scale: float = 0.0, dtype=None) -> torch.Tensor:
+        t = torch.ones(n) + scale * torch.randn(n, generator=self._gen("cpu"))
+        return t.to(dtype or self.dtype).to(self.device)
+
+    def uniform(self, shape, lo: float, hi: float, dtype=torch.float32) -> torch.Tensor:
+        t = torch.rand(*shape, generator=self._gen("cpu")) * (hi - lo) + lo
+        return t.to(dtype).to(self.device)
+
+
+class Linear(nn.Module):
+    """y = x W^T; weight [out, in] bf16 (this rank's shard)."""
+
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None = None):
+        super().__init__()
+        self.weight = nn.Parameter(weight, requires_grad=False)
+        self.bias = None if bias is None else nn.Parameter(bias, requires_grad=False)
+
+    @property
+    def out_features(self) -> int:
+        return self.weight.shape[0]
+
+    def forward(self, x: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+        return ops.gemm(x, self.weight, self.bias, out_dtype=out_dtype)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, weight: torch.Tensor, eps: float):
+        super().__init__()
+        self.weight = nn.Parameter(weight, requires_grad=False)
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None):
+        if residual is None:
+            return ops.rms_norm(x, self.weight, self.eps)
+        ops.fused_add_rms_norm(x, residual, self.weight, self.eps)
+        return x
+
+
+def row_parallel_reduce(y: torch.Tensor) -> torch.Tensor:
+    return comm.tp_all_reduce(y)
+
+
+def default_std(fan_in: int) -> float:
+    return 1.0 / math.sqrt(fan_in)

@@ -20,20 +20,20 @@ def _native(t: torch.Tensor) -> bool:
 
 
 def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
-         splits: int = 0) -> torch.Tensor:
-    """y = x @ w^T (+ bias), bf16 in/out, fp32 accumulate (tcgen05 on GPU)."""
+         splits: int = 0, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """y = x @ w^T (+ bias), bf16 inputs, fp32 accumulate, bf16 or fp32 output (tcgen05 on GPU)."""
     lead = x.shape[:-1]
     x2 = x.reshape(-1, x.shape[-1])
     if not _native(x2):
-        y = _ref.linear(x2, w, bias)
+        y = (x2.float() @ w.float().t() + (bias.float() if bias is not None else 0)).to(out_dtype)
         if out is not None:
             out.view(-1, w.shape[0]).copy_(y)
             return out
         return y.view(*lead, w.shape[0])
-    if x2.stride(-1) != 1:
-        x2 = x2.contiguous()
+    if x2.stride(-1) != 1 or (x2.stride(0) % 8 and x2.shape[0] > 1):
+        x2 = x2.contiguous()  # TMA needs 16-byte row strides
     if out is None:
-        out = torch.empty(*lead, w.shape[0], dtype=torch.bfloat16, device=x.device)
+        out = torch.empty(*lead, w.shape[0], dtype=out_dtype, device=x.device)
     o2 = out.view(-1, w.shape[0])
     _ext.ops().gemm_bf16_out(x2, w, bias, o2, _ext.status_word(x.device), splits)
     return out
@@ -60,3 +60,18 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
         _ref.fused_add_rms_norm(x, residual, w, eps)
         return
     _ext.ops().fused_add_rms_norm(x, residual, w, eps)
+
+
+def silu_mul(x: torch.Tensor, limit: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU of [gate | up] halves of the last dim (optional clamp)."""
+    I = x.shape[-1] // 2
+    if not _native(x):
+        y = _ref.silu_and_mul(x, limit or None)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(*x.shape[:-1], I, dtype=x.dtype, device=x.device)
+    _ext.ops().silu_mul(out.view(-1, I), x.view(-1, 2 * I), float(limit))
+    return out

@@ -1,0 +1,42 @@
+"""Greedy / temperature sampling over (vocab-sharded) logits."""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _ext
+
+
+def sample_local(logits: torch.Tensor, temperature: torch.Tensor | None, seed: int, step: torch.Tensor | None,
+                 vocab_offset: int = 0):
+    """Per-row winner of this vocab shard: (value [rows] fp32, global index [rows] int32).
+    Greedy rows (temperature <= 0) take the argmax; others the Gumbel-max sample."""
+    rows = logits.shape[0]
+    if not logits.is_cuda:
+        x = logits.float()
+        if temperature is not None:
+            g = torch.Generator().manual_seed(int(seed) + int(step.item() if step is not None else 0))
+            u = torch.rand(x.shape, generator=g).clamp_(1e-12, 1 - 1e-7)
+            t = temperature.float()[:, None]
+            noisy = x / t.clamp_min(1e-6) - torch.log(-torch.log(u))
+            x = torch.where(t > 0, noisy, x)
+        v, i = x.max(dim=-1)  # torch.max returns the first maximal index
+        return v, (i + vocab_offset).int()
+    val = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    idx = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    _ext.ops().sample_rows(logits, temperature, int(seed), step, vocab_offset, val, idx)
+    return val, idx
+
+
+def combine(vals: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """vals/idx [R, rows] per-shard winners -> token ids [rows] int64."""
+    if not vals.is_cuda:
+        best = vals.max(dim=0).values
+        out = torch.empty(vals.shape[1], dtype=torch.int64)
+        for r in range(vals.shape[1]):
+            cand = idx[:, r][vals[:, r] == best[r]]
+            out[r] = int(cand.min())
+        return out
+    out = torch.empty(vals.shape[1], dtype=torch.int64, device=vals.device)
+    _ext.ops().sample_combine(vals.contiguous(), idx.contiguous(), out)
+    return out
