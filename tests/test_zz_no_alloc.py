@@ -1,0 +1,69 @@
+"""The allocation-free GEMM entry point, called through its exported C symbol.
+
+`b200_gemm_bf16_noalloc` serves callers that cannot allocate device memory:
+its split-K scratch is a fixed area compiled into the library instead of
+memory taken from PyTorch's allocator.  This test loads the extension as a
+plain shared library, calls the symbol twice in a row with fresh inputs and
+checks each result against the ordinary op (torch.ops.b200.gemm_bf16_out)
+with the same tolerance as the other GEMM tests.  It also checks that a shape
+needing more scratch than the fixed maximum is refused with the documented
+code.  (This file is named so pytest collects it last.)
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOO_LARGE = -1
+
+
+def _entry():
+    from vllm_cmp170hx_b200 import _C
+
+    lib = ctypes.CDLL(_C.__file__)
+    f = lib.b200_gemm_bf16_noalloc
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                  ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    return f
+
+
+def _call(f, x, w, y, splits=0):
+    M, K = x.shape
+    N = w.shape[0]
+    stream = torch.cuda.current_stream().cuda_stream
+    return f(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(), y.stride(0), M, N, K, splits, stream)
+
+
+def _rel_err(y, r):
+    return ((y.float() - r.float()).norm() / r.float().norm().clamp_min(1e-12)).item()
+
+
+def test_noalloc_matches_existing_entry_point_twice():
+    from vllm_cmp170hx_b200 import ops
+
+    f = _entry()
+    torch.manual_seed(0)
+    # small M, long K: the split-K path, whose partials live in the fixed scratch
+    M, N, K = 8, 1024, 4096
+    for call in range(2):
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / K ** 0.5
+        expected = ops.gemm(x, w)
+        y = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+        rc = _call(f, x, w, y)
+        torch.cuda.synchronize()
+        assert rc == 0, (call, rc)
+        assert _rel_err(y, expected) < 1e-2, (call, _rel_err(y, expected))
+
+
+def test_noalloc_refuses_more_scratch_than_its_maximum():
+    f = _entry()
+    M, N, K = 64, 8192, 8192
+    x = torch.zeros(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.zeros(N, K, device="cuda", dtype=torch.bfloat16)
+    y = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
+    assert _call(f, x, w, y, splits=16) == TOO_LARGE

@@ -414,3 +414,92 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace b200
+
+// ============================================================================
+// Allocation-free entry point (declared and documented in noalloc.h; it has
+// no counterpart in the reference).  The split-K scratch and the status word
+// are file-scope device arrays; their device addresses are looked up once
+// per device and passed to the same kernel the ordinary op launches.
+// ============================================================================
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace b200 {
+namespace noalloc {
+
+static __device__ __align__(256) float g_scratch[B200_NOALLOC_SCRATCH_FLOATS];
+static __device__ __align__(256) uint32_t g_status[64];
+
+struct DeviceScratch {
+  float* partial = nullptr;
+  uint32_t* status = nullptr;
+};
+constexpr int kMaxDevices = 64;
+static DeviceScratch g_dev[kMaxDevices];
+static std::mutex g_mu;
+
+// Device addresses of this device's copy of the scratch arrays (looked up on
+// the first call made with that device current).
+static cudaError_t scratch_for_current_device(DeviceScratch* out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_dev[dev].partial == nullptr) {
+    void* p = nullptr;
+    void* s = nullptr;
+    e = cudaGetSymbolAddress(&p, g_scratch);
+    if (e != cudaSuccess) return e;
+    e = cudaGetSymbolAddress(&s, g_status);
+    if (e != cudaSuccess) return e;
+    g_dev[dev].partial = static_cast<float*>(p);
+    g_dev[dev].status = static_cast<uint32_t*>(s);
+  }
+  *out = g_dev[dev];
+  return cudaSuccess;
+}
+
+}  // namespace noalloc
+}  // namespace b200
+
+extern "C" int b200_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc,
+                                      int M, int N, int K, int splits, cudaStream_t stream) {
+  using namespace b200;
+  if (x == nullptr || w == nullptr || c == nullptr || M <= 0 || N <= 0 || K <= 0 || K % 8 != 0 || splits < 0 ||
+      ldx < K || ldw < K || ldc < N)
+    return B200_NOALLOC_BAD_ARGS;
+  noalloc::DeviceScratch s;
+  cudaError_t e = noalloc::scratch_for_current_device(&s);
+  if (e != cudaSuccess) return (int)e;
+  const int used = gemm_bf16_splits(M, N, K, splits);
+  if (used > 1 && (uint64_t)used * (uint64_t)M * (uint64_t)N > (uint64_t)B200_NOALLOC_SCRATCH_FLOATS)
+    return B200_NOALLOC_TOO_LARGE;
+  // The status word must start at zero for this call; the partial sums need
+  // no clearing (every split writes its whole [M, N] slice).
+  e = cudaMemsetAsync(s.status, 0, sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return (int)e;
+  GemmArgs a{};
+  a.x = x;
+  a.ldx = ldx;
+  a.w = w;
+  a.ldw = ldw;
+  a.bias = nullptr;
+  a.c = c;
+  a.ldc = ldc;
+  a.out_f32 = 0;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.splits = used;
+  a.partial = s.partial;
+  a.partial_cap = B200_NOALLOC_SCRATCH_FLOATS;
+  a.status = s.status;
+  try {
+    e = gemm_bf16(a, stream);
+  } catch (...) {  // tensor-map encoding rejected the operands (alignment)
+    return B200_NOALLOC_BAD_ARGS;
+  }
+  return (int)e;
+}
