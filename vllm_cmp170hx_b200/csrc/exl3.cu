@@ -6,12 +6,12 @@
 // register fragments (dense_mma.cu:249, moe_v2.cu:443); on sm_100 the MMA
 // reads its operands from shared memory, so here:
 //
-//   * 8 decoder warps read trellis words straight from global memory (one
-//     coalesced 128-byte row per 16x16 tile at 4 bits), decode 8 states per
-//     lane and store fp16 pairs into the UMMA "no swizzle" K-major layout
-//     (8x16-byte core matrices; bank-conflict-free: lane L writes word L);
-//   * a TMA warp stages the (Hadamard-rotated, fp16) activation rows of the
-//     work item with 128-byte swizzle;
+//   * a TMA warp streams the trellis words of each 4 x 8-tile chunk into a
+//     shared-memory ring; 16 decoder warps decode 8 states per lane and store
+//     fp16 pairs into the 128-byte-swizzled K-major operand layout
+//     (bank-conflict-free: the swizzle spreads a warp's 8 rows over all banks);
+//   * a second TMA warp stages the (Hadamard-rotated, fp16) activation rows of
+//     the work item in their own ring (128-byte swizzle);
 //   * one thread issues tcgen05.mma (M = 128 output features, N = rows of the
 //     item rounded to 16, K = 64 per stage) into TMEM;
 //   * the decoder warps then run the epilogue from TMEM: the output H128 is a
@@ -25,13 +25,16 @@
 // kernel with one "expert" whose rows are all tokens.
 #include "common.cuh"
 #include "launch.h"
+#include <stdexcept>
+#include <string>
+
 #include "tma_host.h"
 
 namespace b200 {
 namespace exl3 {
 
-constexpr int kDecodeWarps = 8;
-constexpr int kThreads = (kDecodeWarps + 2) * 32;  // + TMA warp + MMA warp
+constexpr int kDecodeWarps = 16;
+
 constexpr int BK = 64;                              // K per pipeline stage (4 tile rows)
 constexpr int A_BYTES = 128 * BK * 2;               // one 128 x 64 fp16 operand tile
 constexpr int A_LBO = 2048;                         // bytes between K-adjacent core matrices
@@ -60,37 +63,54 @@ struct GemmParams {
 };
 
 // ----------------------------------------------------------------------------- codebooks
+// Two states -> two fp16 weights packed as half2 (inline PTX keeps the
+// format constants as immediates).
 template <int CB>
 __device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
+  uint32_t r;
   if constexpr (CB == 2) {
-    const uint32_t p0 = s0 * 0x83DCD12Du, p1 = s1 * 0x83DCD12Du;
-    const uint32_t t0 = __dp4a(p0, 0x01010101u, 0x6400u);
-    const uint32_t t1 = __dp4a(p1, 0x01010101u, 0x6400u);
-    const uint32_t h = __byte_perm(t0, t1, 0x5410);
-    const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x1eee), __ushort_as_half(0x1eee)),
-                              __halves2half2(__ushort_as_half(0xc931), __ushort_as_half(0xc931)));
-    return *reinterpret_cast<const uint32_t*>(&r);
+    // t = 0x6400 + bytesum(s * 0x83DCD12D); w = fma16(half(t), 0x1eee, 0xc931)
+    asm("{\n\t.reg .b32 p0, p1, t0, t1, h;\n\t"
+        "mul.lo.u32 p0, %1, 0x83DCD12D;\n\t"
+        "mul.lo.u32 p1, %2, 0x83DCD12D;\n\t"
+        "dp4a.u32.u32 t0, p0, 0x01010101, 0x6400;\n\t"
+        "dp4a.u32.u32 t1, p1, 0x01010101, 0x6400;\n\t"
+        "prmt.b32 h, t0, t1, 0x5410;\n\t"
+        "fma.rn.f16x2 %0, h, %3, %4;\n\t}"
+        : "=r"(r)
+        : "r"(s0), "r"(s1), "r"(0x1eee1eeeu), "r"(0xc931c931u));
   } else {
-    const uint32_t p0 = ((s0 * 0xCBAC1FEDu) & 0x8fff8fffu) ^ 0x3b603b60u;
-    const uint32_t p1 = ((s1 * 0xCBAC1FEDu) & 0x8fff8fffu) ^ 0x3b603b60u;
-    const uint32_t lo = __byte_perm(p0, p1, 0x5410);
-    const uint32_t hi = __byte_perm(p0, p1, 0x7632);
-    const __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
-    return *reinterpret_cast<const uint32_t*>(&r);
+    // p = (s * 0xCBAC1FED) & 0x8fff8fff ^ 0x3b603b60; w = half(p.lo) + half(p.hi)
+    asm("{\n\t.reg .b32 p0, p1, lo, hi;\n\t"
+        "mul.lo.u32 p0, %1, 0xCBAC1FED;\n\t"
+        "mul.lo.u32 p1, %2, 0xCBAC1FED;\n\t"
+        "lop3.b32 p0, p0, 0x8fff8fff, 0x3b603b60, 0x6a;\n\t"
+        "lop3.b32 p1, p1, 0x8fff8fff, 0x3b603b60, 0x6a;\n\t"
+        "prmt.b32 lo, p0, p1, 0x5410;\n\t"
+        "prmt.b32 hi, p0, p1, 0x7632;\n\t"
+        "add.rn.f16x2 %0, lo, hi;\n\t}"
+        : "=r"(r)
+        : "r"(s0), "r"(s1));
   }
+  return r;
 }
 
 // 8 states of lane L in a 16x16 tile at 4 bits per weight (bits_x2 = 8):
 // the lane's window is word L-1 (low bits) and word L of the 32-word ring.
+// State j is the 64-bit window (w_prev:w_self) shifted right by 28 - 4j and
+// masked to 16 bits.  Shifts that are multiples of 8 are byte selections of
+// w_self; shifts of 4 mod 8 are byte selections of the window shifted by 4.
 __device__ __forceinline__ void states_b8(uint32_t w_prev, uint32_t w_self, uint32_t (&s)[8]) {
+  const uint32_t lo4 = __funnelshift_r(w_self, w_prev, 4);  // low word of (window >> 4)
   s[0] = __funnelshift_r(w_self, w_prev, 28) & 0xffffu;
   s[1] = __funnelshift_r(w_self, w_prev, 24) & 0xffffu;
-  s[2] = __funnelshift_r(w_self, w_prev, 20) & 0xffffu;
-  s[3] = w_self >> 16;
-  s[4] = (w_self >> 12) & 0xffffu;
+  // __byte_perm(x, 0, sel): result byte i = byte sel_i of x (selector 4 = zero)
+  s[2] = __byte_perm(lo4, 0, 0x4432);
+  s[3] = __byte_perm(w_self, 0, 0x4432);
+  s[4] = __byte_perm(lo4, 0, 0x4421);
   s[5] = __byte_perm(w_self, 0, 0x4421);
-  s[6] = (w_self >> 4) & 0xffffu;
-  s[7] = w_self & 0xffffu;
+  s[6] = __byte_perm(lo4, 0, 0x4410);
+  s[7] = __byte_perm(w_self, 0, 0x4410);
 }
 
 // Generic bitrate: lane L's state j starts at ring bit (L*4*b + c_j) mod (128 b)
@@ -107,7 +127,7 @@ __device__ __forceinline__ void states_generic(const uint32_t* __restrict__ word
     pos = pos >= ring ? pos - ring : pos;
     const int lo = pos >> 5;
     const int hi = lo + 1 == nwords ? 0 : lo + 1;
-    const uint32_t w0 = __ldg(words + lo), w1 = __ldg(words + hi);
+    const uint32_t w0 = words[lo], w1 = words[hi];
     s[j] = __funnelshift_l(w1, w0, pos & 31) >> 16;
   }
 }
@@ -129,11 +149,42 @@ __device__ __forceinline__ void decode_tile_store(const uint32_t* __restrict__ t
   const uint32_t v23 = cb_pair<CB>(s[2], s[3]);  // rows 2a+8, 2a+9 col b
   const uint32_t v45 = cb_pair<CB>(s[4], s[5]);  // rows 2a, 2a+1   col b+8
   const uint32_t v67 = cb_pair<CB>(s[6], s[7]);  // rows 2a+8, 2a+9 col b+8
-  const uint32_t base = (uint32_t)(tr * 2) * A_LBO + (uint32_t)(tc * 2) * A_SBO + lane * 4;
-  *reinterpret_cast<uint32_t*>(a_stage + base) = v01;
-  *reinterpret_cast<uint32_t*>(a_stage + base + A_LBO) = v23;
-  *reinterpret_cast<uint32_t*>(a_stage + base + A_SBO) = v45;
-  *reinterpret_cast<uint32_t*>(a_stage + base + A_LBO + A_SBO) = v67;
+  // 128-byte-swizzled K-major tile (128 rows x 64 fp16): element (m, k) at
+  // (m / 8) * 1024 + (m % 8) * 128 + ((k / 8) ^ (m % 8)) * 16 + (k % 8) * 2.
+  // Lane (a = lane & 3, b = lane >> 2) holds rows m = 16 tc + b (+8) and
+  // columns k = 16 tr + 2a (+8); the XOR spreads the 8 rows b over all banks.
+  const uint32_t la = lane & 3, lb = lane >> 2;
+  const uint32_t row = (uint32_t)tc * 2048 + lb * 128 + la * 4;
+  const uint32_t c0 = (((uint32_t)tr * 2) ^ lb) << 4, c1 = (((uint32_t)tr * 2 + 1) ^ lb) << 4;
+  *reinterpret_cast<uint32_t*>(a_stage + row + c0) = v01;
+  *reinterpret_cast<uint32_t*>(a_stage + row + c1) = v23;
+  *reinterpret_cast<uint32_t*>(a_stage + row + 1024 + c0) = v45;
+  *reinterpret_cast<uint32_t*>(a_stage + row + 1024 + c1) = v67;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// 4-bit fast path: decode the lane's 8 weights of one tile whose words start
+// at shared address `tw` (word `lane` at tw + 4 lane) and store them at the
+// four precomputed operand addresses o0..o3 (see decode_tile_store).
+template <int CB>
+__device__ __forceinline__ void decode_tile_b8(uint32_t tw_lane, int lane, uint32_t o0, uint32_t o1, uint32_t o2,
+                                               uint32_t o3) {
+  const uint32_t w_self = lds32(tw_lane);
+  const uint32_t w_prev = __shfl_sync(0xffffffffu, w_self, (lane + 31) & 31);
+  uint32_t st[8];
+  states_b8(w_prev, w_self, st);
+  sts32(o0, cb_pair<CB>(st[0], st[1]));
+  sts32(o1, cb_pair<CB>(st[2], st[3]));
+  sts32(o2, cb_pair<CB>(st[4], st[5]));
+  sts32(o3, cb_pair<CB>(st[6], st[7]));
 }
 
 // In-register butterfly over the 128 features held one per thread of a
@@ -165,36 +216,80 @@ __device__ __forceinline__ void h128_group(float (&v)[NV], int lane, int q, floa
   for (int i = 0; i < NV; ++i) v[i] *= kH128;
 }
 
-template <int NMAT>
-struct Smem {
-  // per stage: NMAT A tiles then NMAT B tiles
-  static int stage_bytes(int tile_rows) { return NMAT * (A_BYTES + tile_rows * 128); }
-  static int stages(int tile_rows) {
-    int s = (200 * 1024 - 16 * 1024) / stage_bytes(tile_rows);
-    return s > 6 ? 6 : s;
-  }
-  static int total(int tile_rows) {
-    return 1024 + stages(tile_rows) * stage_bytes(tile_rows) + 2 * 16 * 128 * 4 /*xbuf*/ + 256 /*barriers*/;
-  }
+// Shared-memory plan: `ab` stages of [NMAT decoded A tiles | NMAT B tiles]
+// and `raw` stages of NMAT raw trellis chunks (32 tiles each), sized on the
+// host so both rings fit next to the epilogue exchange buffers.
+struct Plan {
+  int a_stages, b_stages, raw_stages;  // decoded-A ring, activation ring, raw trellis ring
+  int a_bytes, b_bytes, raw_bytes;     // bytes per stage of each ring
+  int smem;
 };
 
+constexpr int kGroups = kDecodeWarps / 4;  // epilogue warp groups (4 warps = 128 TMEM lanes)
+constexpr int kXbufBytes = 16 * 128 * 4;   // per-group H128 exchange buffer
+
+// Shared-memory plan: three independent rings so that neither the trellis
+// nor the activation loads wait for the decoded-operand ring to drain.
+inline Plan make_plan(int nmat, int tile_rows, int bits_x2) {
+  Plan pl{};
+  pl.a_bytes = nmat * A_BYTES;
+  pl.b_bytes = nmat * tile_rows * 128;
+  pl.raw_bytes = nmat * 32 * 16 * bits_x2;
+  const int budget = 210 * 1024 - kGroups * kXbufBytes;
+  pl.a_stages = 3;
+  pl.raw_stages = 6;
+  pl.b_stages = (budget - pl.a_stages * pl.a_bytes - pl.raw_stages * pl.raw_bytes) / pl.b_bytes;
+  if (pl.b_stages > 8) pl.b_stages = 8;
+  while (pl.b_stages < 2 && pl.a_stages > 2) {
+    --pl.a_stages;
+    pl.b_stages = (budget - pl.a_stages * pl.a_bytes - pl.raw_stages * pl.raw_bytes) / pl.b_bytes;
+  }
+  while (pl.b_stages < 2 && pl.raw_stages > 3) {
+    --pl.raw_stages;
+    pl.b_stages = (budget - pl.a_stages * pl.a_bytes - pl.raw_stages * pl.raw_bytes) / pl.b_bytes;
+  }
+  if (pl.b_stages > 8) pl.b_stages = 8;
+  const int left = budget - pl.a_stages * pl.a_bytes - pl.b_stages * pl.b_bytes;
+  pl.raw_stages = left / pl.raw_bytes > 8 ? 8 : left / pl.raw_bytes;
+  pl.smem = 1024 + pl.a_stages * pl.a_bytes + pl.b_stages * pl.b_bytes + pl.raw_stages * pl.raw_bytes +
+            kGroups * kXbufBytes + 512;
+  return pl;
+}
+
+constexpr int kRawWarp = kDecodeWarps;      // trellis producer (TMA)
+constexpr int kBWarp = kDecodeWarps + 1;    // activation producer (TMA)
+constexpr int kMmaWarp = kDecodeWarps + 2;  // TMEM owner + MMA issuer
+constexpr int kThreadsStaged = (kDecodeWarps + 3) * 32;
+
 // NMAT = 2: gate/up pass (writes the rotated SwiGLU intermediate), 1: down / dense.
+// Trellis chunks (4 tile rows x 8 tile columns per matrix) arrive by TMA in
+// a ring `raw_stages` deep, so the decoder warps never wait on global memory.
 template <int NMAT, int CB, bool FAST>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsStaged, 1)
     exl3_gemm_kernel(const __grid_constant__ CUtensorMap tma_b0, const __grid_constant__ CUtensorMap tma_b1,
-                     GemmParams p, int stages) {
+                     const __grid_constant__ CUtensorMap tma_t0, const __grid_constant__ CUtensorMap tma_t1,
+                     GemmParams p, Plan pl) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int tile_rows = p.tile_rows;
-  const int b_bytes = tile_rows * 128;
-  const int stage_bytes = NMAT * (A_BYTES + b_bytes);
-  float* xbuf = reinterpret_cast<float*>(smem + stages * stage_bytes);  // [2 groups][16][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xbuf + 2 * 16 * 128);
-  uint64_t* full = bars;            // [stages] 8 decoder warps + 1 TMA arrival + tx
-  uint64_t* empty = bars + 6;       // [stages] MMA commit
-  uint64_t* tfull = bars + 12;      // accumulator ready
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  const int b_bytes = tile_rows * 128;  // one matrix's activation tile
+  const int stages = pl.a_stages;
+  const int bstages = pl.b_stages;
+  const int rstages = pl.raw_stages;
+  uint8_t* sa = smem;
+  uint8_t* sbb = sa + stages * pl.a_bytes;
+  uint8_t* raw = sbb + bstages * pl.b_bytes;
+  float* xbuf = reinterpret_cast<float*>(raw + rstages * pl.raw_bytes);  // [kGroups][16][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xbuf + kGroups * 16 * 128);
+  uint64_t* full = bars;             // [4]  decoder warps: decoded A stage ready
+  uint64_t* empty = bars + 4;        // [4]  MMA commit: A stage free
+  uint64_t* raw_full = bars + 8;     // [8]  trellis TMA tx
+  uint64_t* raw_empty = bars + 16;   // [8]  decoder warps
+  uint64_t* b_full = bars + 24;      // [8]  activation TMA tx
+  uint64_t* b_empty = bars + 32;     // [8]  MMA commit
+  uint64_t* tfull = bars + 40;       // accumulator ready
+  uint64_t* drain = bars + 41;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 42);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -202,18 +297,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tmem_cols_needed = NMAT * tile_rows;
   const uint32_t tmem_cols = tmem_cols_needed <= 32 ? 32 : tmem_cols_needed <= 64 ? 64 : tmem_cols_needed <= 128 ? 128
                              : tmem_cols_needed <= 256 ? 256 : 512;
+  const int tile_bytes = FAST ? 128 : 16 * p.bits_x2;  // one 16x16 trellis tile
+  const int mat_raw = 32 * tile_bytes;     // one matrix's chunk (4 x 8 tiles)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) {
-      mbar_init(&full[i], kDecodeWarps + 1);
+      mbar_init(&full[i], kDecodeWarps);
       mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < bstages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < rstages; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], kDecodeWarps);
     }
     mbar_init(tfull, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kDecodeWarps + 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
@@ -226,53 +331,87 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_items = *p.num_items;
   const int total = n_items * n_tiles;
   const int kchunks = p.K / BK;
-  const int kt_per_row = p.N / 16;  // trellis tiles per tile row
+  const int kt_rows = p.K / 16;  // trellis tile rows per expert
 
-  auto a_tile = [&](int stage, int m) { return smem + stage * stage_bytes + m * A_BYTES; };
-  auto b_tile = [&](int stage, int m) { return smem + stage * stage_bytes + NMAT * A_BYTES + m * b_bytes; };
+  auto a_tile = [&](int stage, int m) { return sa + stage * pl.a_bytes + m * A_BYTES; };
+  auto b_tile = [&](int stage, int m) { return sbb + stage * pl.b_bytes + m * b_bytes; };
 
   if (warp < kDecodeWarps) {
     // =================================================================== decoders + epilogue
-    int stage = 0;
-    uint32_t phase = 0;
+    int stage = 0, rs = 0;
+    uint32_t phase = 0, rphase = 0;
     int local = 0;
     const int g = warp / 4;  // epilogue warp group
     const int q = warp % 4;  // TMEM lane quarter
+    const int tc = warp & 7;                          // decoded tile column (16 output features)
+    const int tr0 = (warp >> 3) * (4 / (kDecodeWarps / 8));  // first tile row of this warp
+    constexpr int kRowsPerWarp = 4 / (kDecodeWarps / 8);
+    // per-warp constant addressing of the 4-bit path: this lane's word of tile
+    // (tr0 + r, tc) in a raw stage, and its four operand store offsets
+    const uint32_t raw_lane_off = (uint32_t)((tr0 * 8 + tc) * 128 + lane * 4);
+    uint32_t st_off[kRowsPerWarp][4];
+    {
+      const uint32_t la = lane & 3, lb = lane >> 2;
+      const uint32_t row = (uint32_t)tc * 2048 + lb * 128 + la * 4;
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
+        const uint32_t tr = tr0 + r;
+        const uint32_t c0 = ((tr * 2) ^ lb) << 4, c1 = ((tr * 2 + 1) ^ lb) << 4;
+        st_off[r][0] = row + c0;
+        st_off[r][1] = row + c1;
+        st_off[r][2] = row + 1024 + c0;
+        st_off[r][3] = row + 1024 + c1;
+      }
+    }
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
       const int4 it = p.items[u / n_tiles];
       const int tile = u % n_tiles;
       const int e = it.x;
       bool ok = true;
       for (int kc = 0; kc < kchunks; ++kc) {
-        const bool got = mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag);
+        bool got = mbar_wait_or_abort(&raw_full[rs], rphase, p.status, abort_flag);
+        got = got && mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
+        const uint8_t* rbase = raw + rs * pl.raw_bytes;
+        if constexpr (FAST) {
+          const uint32_t rb = smem_u32(rbase) + raw_lane_off;
+          const uint32_t ab = smem_u32(a_tile(stage, 0));
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-          const uint32_t* tw_base =
-              reinterpret_cast<const uint32_t*>(p.trellis[m] + (int64_t)e * p.trellis_estride[m]);
-          const int words_per_tile = 4 * p.bits_x2;
-          uint32_t w[4];
-          const uint32_t* tws[4];
+          for (int m = 0; m < NMAT; ++m) {
 #pragma unroll
-          for (int tr = 0; tr < 4; ++tr) {
-            const int kt = kc * 4 + tr;
-            const int nt = tile * 8 + warp;
-            tws[tr] = tw_base + (int64_t)(kt * kt_per_row + nt) * words_per_tile;
-            if constexpr (FAST) w[tr] = __ldg(tws[tr] + lane);
+            for (int r = 0; r < kRowsPerWarp; ++r) {
+              const uint32_t mo = m * A_BYTES;
+              decode_tile_b8<CB>(rb + m * 32 * 128 + r * 8 * 128, lane, ab + mo + st_off[r][0],
+                                 ab + mo + st_off[r][1], ab + mo + st_off[r][2], ab + mo + st_off[r][3]);
+            }
           }
+        } else {
 #pragma unroll
-          for (int tr = 0; tr < 4; ++tr)
-            decode_tile_store<CB, FAST>(tws[tr], FAST ? w[tr] : 0u, p.bits_x2, lane, a_tile(stage, m), warp, tr);
+          for (int m = 0; m < NMAT; ++m) {
+#pragma unroll
+            for (int r = 0; r < kRowsPerWarp; ++r) {
+              const int tr = tr0 + r;
+              const uint32_t* tw =
+                  reinterpret_cast<const uint32_t*>(rbase + m * mat_raw + (tr * 8 + tc) * tile_bytes);
+              decode_tile_store<CB, FAST>(tw, 0u, p.bits_x2, lane, a_tile(stage, m), tc, tr);
+            }
+          }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[stage]);
         if (++stage == stages) {
           stage = 0;
           phase ^= 1;
+        }
+        if (++rs == rstages) {
+          rs = 0;
+          rphase ^= 1;
         }
       }
       if (!ok) break;
@@ -286,10 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int feat = tile * 128 + f;
       float* xb = xbuf + g * 16 * 128;
       const int nchunks = (rows + 15) / 16;
-      // column chunks alternate between the two warp groups; each group's
+      // column chunks are dealt round-robin to the warp groups; each group's
       // named barrier spans its own 4 warps only
-      for (int c = g; c < nchunks; c += 2) {
-        const bool active = true;
+      for (int c = g; c < nchunks; c += kGroups) {
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c * 16;
         if constexpr (NMAT == 2) {
           uint32_t rg[16], ru[16];
@@ -318,13 +456,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             gv[i] = siluf_(gg) * uu * sn;
           }
           h128_group<16>(gv, lane, q, xb, 1 + g);
-          if (active) {
-            __half* out = reinterpret_cast<__half*>(p.out);
+          __half* out = reinterpret_cast<__half*>(p.out);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int r = c * 16 + i;
-              if (r < rows) out[(int64_t)(row0 + r) * p.ld_out + feat] = __float2half_rn(gv[i]);
-            }
+          for (int i = 0; i < 16; ++i) {
+            const int r = c * 16 + i;
+            if (r < rows) out[(int64_t)(row0 + r) * p.ld_out + feat] = __float2half_rn(gv[i]);
           }
         } else {
           uint32_t ra[16];
@@ -335,24 +471,59 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
           h128_group<16>(v, lane, q, xb, 1 + g);
           const float s = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
-          if (active) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int r = c * 16 + i;
-              if (r >= rows) continue;
-              const int64_t o = (int64_t)(row0 + r) * p.ld_out + feat;
-              if (p.out_mode == 1)
-                reinterpret_cast<float*>(p.out)[o] = v[i] * s;
-              else
-                reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(v[i] * s);
-            }
+          for (int i = 0; i < 16; ++i) {
+            const int r = c * 16 + i;
+            if (r >= rows) continue;
+            const int64_t o = (int64_t)(row0 + r) * p.ld_out + feat;
+            if (p.out_mode == 1)
+              reinterpret_cast<float*>(p.out)[o] = v[i] * s;
+            else
+              reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(v[i] * s);
           }
         }
       }
       tc_fence_before();
     }
-  } else if (warp == kDecodeWarps) {
-    // =================================================================== TMA producer
+  } else if (warp == kRawWarp) {
+    // =================================================================== trellis producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tma_t0);
+      if (NMAT == 2) tma_prefetch_desc(&tma_t1);
+      int rs = 0;
+      uint32_t rphase = 0, issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int4 it = p.items[u / n_tiles];
+        const int tile = u % n_tiles;
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!mbar_wait_or_abort(&raw_empty[rs], rphase ^ 1, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&raw_full[rs], NMAT * mat_raw);
+          uint8_t* dst = raw + rs * pl.raw_bytes;
+          const int z = it.x * kt_rows + kc * 4;
+          tma_load_3d(dst, &tma_t0, &raw_full[rs], 0, tile * 8, z);
+          if (NMAT == 2) tma_load_3d(dst + mat_raw, &tma_t1, &raw_full[rs], 0, tile * 8, z);
+          ++issued;
+          if (++rs == rstages) {
+            rs = 0;
+            rphase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        const uint32_t n = issued < (uint32_t)rstages ? issued : (uint32_t)rstages;
+        for (uint32_t i = 0; i < n; ++i) {
+          const uint32_t k = issued - 1 - i;
+          mbar_wait(&raw_full[k % rstages], (k / rstages) & 1, nullptr);
+        }
+      }
+    }
+  } else if (warp == kBWarp) {
+    // =================================================================== activation producer
     if (elect_one()) {
       tma_prefetch_desc(&tma_b0);
       if (NMAT == 2) tma_prefetch_desc(&tma_b1);
@@ -363,15 +534,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const int4 it = p.items[u / n_tiles];
         for (int kc = 0; kc < kchunks; ++kc) {
-          if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag)) {
+          if (!mbar_wait_or_abort(&b_empty[stage], phase ^ 1, p.status, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], NMAT * b_bytes);
-          tma_load_2d(b_tile(stage, 0), &tma_b0, &full[stage], kc * BK, it.y);
-          if (NMAT == 2) tma_load_2d(b_tile(stage, 1), &tma_b1, &full[stage], kc * BK, it.y);
+          mbar_arrive_expect_tx(&b_full[stage], NMAT * b_bytes);
+          tma_load_2d(b_tile(stage, 0), &tma_b0, &b_full[stage], kc * BK, it.y);
+          if (NMAT == 2) tma_load_2d(b_tile(stage, 1), &tma_b1, &b_full[stage], kc * BK, it.y);
           ++issued;
-          if (++stage == stages) {
+          if (++stage == bstages) {
             stage = 0;
             phase ^= 1;
           }
@@ -379,25 +550,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) {
         *abort_flag = 1;
-        const uint32_t n = issued < (uint32_t)stages ? issued : (uint32_t)stages;
+        const uint32_t n = issued < (uint32_t)bstages ? issued : (uint32_t)bstages;
         for (uint32_t i = 0; i < n; ++i) {
           const uint32_t k = issued - 1 - i;
-          mbar_wait(&full[k % stages], (k / stages) & 1, nullptr);
+          mbar_wait(&b_full[k % bstages], (k / bstages) & 1, nullptr);
         }
       }
     }
   } else {
     // =================================================================== MMA issuer
     if (elect_one()) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int stage = 0, bs = 0;
+      uint32_t phase = 0, bphase = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const int4 it = p.items[u / n_tiles];
         const int n_pad = (it.z + 15) / 16 * 16;
         const uint32_t idesc = make_idesc_f16(128, n_pad, 0 /*f16*/);
         for (int kc = 0; kc < kchunks; ++kc) {
-          if (!mbar_wait_or_abort(&full[stage], phase, p.status, abort_flag)) {
+          const bool ga = mbar_wait_or_abort(&b_full[bs], bphase, p.status, abort_flag) &&
+                          mbar_wait_or_abort(&full[stage], phase, p.status, abort_flag);
+          if (!ga) {
             ok = false;
             break;
           }
@@ -407,16 +580,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t d = tmem_base + m * tile_rows;
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t da = make_smem_desc(smem_u32(a_tile(stage, m)) + k * 2 * A_LBO, A_LBO, A_SBO,
-                                                 kSwizzleNone);
-              const uint64_t db = desc_kmajor_sw128(b_tile(stage, m)) + 2 * k;
+              const uint64_t da = desc_kmajor_sw128(a_tile(stage, m)) + 2 * k;
+              const uint64_t db = desc_kmajor_sw128(b_tile(bs, m)) + 2 * k;
               umma_f16(d, da, db, idesc, (kc > 0 || k > 0) ? 1u : 0u);
             }
           }
           umma_commit(&empty[stage]);
+          umma_commit(&b_empty[bs]);
           if (++stage == stages) {
             stage = 0;
             phase ^= 1;
+          }
+          if (++bs == bstages) {
+            bs = 0;
+            bphase ^= 1;
           }
         }
         if (!ok) break;
@@ -429,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kDecodeWarps + 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
   }
@@ -498,52 +675,89 @@ __global__ void input_rotate_kernel(const __nv_bfloat16* __restrict__ x, int64_t
 }
 
 // out[t, :] = sum_j w[t, j] * y[slot[t, j], :]  (+ add[t, :]), fp32 math, fixed j order.
+// grid (T, column blocks of 4 * blockDim); 4 consecutive columns per thread.
 __global__ void combine_kernel(const float* __restrict__ y, int64_t ld_y, const int* __restrict__ slot_of,
                                const float* __restrict__ sorted_weight, int k, int H,
                                const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out,
                                int64_t ld_out, float* __restrict__ out_f32) {
   const int t = blockIdx.x;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const int s = slot_of[(int64_t)t * k + j];
-      if (s >= 0) acc += sorted_weight[s] * y[(int64_t)s * ld_y + c];
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+  if (c >= H) return;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool vec = (c + 4 <= H) && (ld_y % 4 == 0);
+  for (int j = 0; j < k; ++j) {
+    const int s = slot_of[(int64_t)t * k + j];
+    if (s < 0) continue;
+    const float w = sorted_weight[s];
+    const float* row = y + (int64_t)s * ld_y + c;
+    if (vec) {
+      const float4 v = *reinterpret_cast<const float4*>(row);
+      acc[0] += w * v.x;
+      acc[1] += w * v.y;
+      acc[2] += w * v.z;
+      acc[3] += w * v.w;
+    } else {
+      for (int i = 0; i < 4 && c + i < H; ++i) acc[i] += w * row[i];
     }
-    if (add) acc += __bfloat162float(add[(int64_t)t * ld_out + c]);
+  }
+  for (int i = 0; i < 4 && c + i < H; ++i) {
+    float a = acc[i];
+    if (add) a += __bfloat162float(add[(int64_t)t * ld_out + c + i]);
     if (out_f32)
-      out_f32[(int64_t)t * H + c] = acc;
+      out_f32[(int64_t)t * H + c + i] = a;
     else
-      out[(int64_t)t * ld_out + c] = __float2bfloat16(acc);
+      out[(int64_t)t * ld_out + c + i] = __float2bfloat16(a);
   }
 }
 
+// 3-D view of a trellis [E, K/16, N/16, 8*bits_x2] int16 as uint32 tile words:
+// (words of a tile, tile column, tile row over all experts); box = 4 tile rows
+// x 8 tile columns = one pipeline chunk of one 128-wide output tile.
+inline CUtensorMap make_trellis_map(const void* base, int E, int K, int N, int bits_x2) {
+  const uint64_t words = 4ull * bits_x2;
+  CUtensorMap map;
+  cuuint64_t gdim[3] = {words, (cuuint64_t)(N / 16), (cuuint64_t)E * (K / 16)};
+  cuuint64_t gstride[2] = {words * 4, (cuuint64_t)(N / 16) * words * 4};
+  cuuint32_t box[3] = {(cuuint32_t)words, 8, 4};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), gdim, gstride,
+                                    box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("trellis tensor map: " + std::to_string((int)r));
+  return map;
+}
+
 template <int NMAT, int CB, bool FAST>
-cudaError_t launch_gemm(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, cudaStream_t stream,
-                        int grid) {
-  const int stages = Smem<NMAT>::stages(p.tile_rows);
-  if (stages < 1) return cudaErrorInvalidValue;
-  const int smem = Smem<NMAT>::total(p.tile_rows);
+cudaError_t launch_gemm(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, int E,
+                        cudaStream_t stream, int grid) {
+  const Plan pl = make_plan(NMAT, p.tile_rows, p.bits_x2);
+  if (pl.a_stages < 2 || pl.b_stages < 2 || pl.raw_stages < 2 || pl.a_stages > 4 || pl.b_stages > 8 ||
+      pl.raw_stages > 8 || pl.smem > 227 * 1024)
+    return cudaErrorInvalidValue;
   CUtensorMap m0 = make_tma_2d(b0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b_rows, p.K, p.K, p.tile_rows, BK,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap m1 = NMAT == 2 ? make_tma_2d(b1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b_rows, p.K, p.K, p.tile_rows,
                                            BK, CU_TENSOR_MAP_SWIZZLE_128B)
                              : m0;
+  CUtensorMap t0 = make_trellis_map(p.trellis[0], E, p.K, p.N, p.bits_x2);
+  CUtensorMap t1 = NMAT == 2 ? make_trellis_map(p.trellis[1], E, p.K, p.N, p.bits_x2) : t0;
   auto kern = exl3_gemm_kernel<NMAT, CB, FAST>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, smem, stream>>>(m0, m1, p, stages);
+  kern<<<grid, kThreadsStaged, pl.smem, stream>>>(m0, m1, t0, t1, p, pl);
   return cudaGetLastError();
 }
 
 template <int NMAT>
-cudaError_t dispatch(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, cudaStream_t s, int grid) {
+cudaError_t dispatch(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, int E, cudaStream_t s,
+                     int grid) {
   const bool fast = p.bits_x2 == 8;
   if (p.codebook == 1) {
-    return fast ? launch_gemm<NMAT, 1, true>(p, b0, b1, b_rows, s, grid)
-                : launch_gemm<NMAT, 1, false>(p, b0, b1, b_rows, s, grid);
+    return fast ? launch_gemm<NMAT, 1, true>(p, b0, b1, b_rows, E, s, grid)
+                : launch_gemm<NMAT, 1, false>(p, b0, b1, b_rows, E, s, grid);
   }
-  return fast ? launch_gemm<NMAT, 2, true>(p, b0, b1, b_rows, s, grid)
-              : launch_gemm<NMAT, 2, false>(p, b0, b1, b_rows, s, grid);
+  return fast ? launch_gemm<NMAT, 2, true>(p, b0, b1, b_rows, E, s, grid)
+              : launch_gemm<NMAT, 2, false>(p, b0, b1, b_rows, E, s, grid);
 }
 
 }  // namespace exl3
@@ -589,14 +803,15 @@ cudaError_t exl3_gemm(const Exl3GemmArgs& a, cudaStream_t stream) {
   p.swiglu_limit = a.swiglu_limit;
   p.status = a.status;
   const int grid = std::max(1, std::min(a.max_work, device_sm_count()));
-  if (a.nmat == 2) return dispatch<2>(p, a.b0, a.b1, a.b_rows, stream, grid);
-  return dispatch<1>(p, a.b0, nullptr, a.b_rows, stream, grid);
+  if (a.nmat == 2) return dispatch<2>(p, a.b0, a.b1, a.b_rows, a.num_experts, stream, grid);
+  return dispatch<1>(p, a.b0, nullptr, a.b_rows, a.num_experts, stream, grid);
 }
 
 cudaError_t moe_combine(const float* y, int64_t ld_y, const int* slot_of, const float* sorted_weight, int T, int k,
                         int H, const void* add, void* out, int64_t ld_out, float* out_f32, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  exl3::combine_kernel<<<T, 256, 0, stream>>>(y, ld_y, slot_of, sorted_weight, k, H,
+  dim3 grid(T, (H + 4 * 128 - 1) / (4 * 128));
+  exl3::combine_kernel<<<grid, 128, 0, stream>>>(y, ld_y, slot_of, sorted_weight, k, H,
                                               reinterpret_cast<const __nv_bfloat16*>(add),
                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_f32);
   return cudaGetLastError();

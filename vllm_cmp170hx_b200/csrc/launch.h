@@ -57,7 +57,8 @@ cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, i
 struct Exl3GemmArgs {
   int nmat;                 // 2: gate/up pass, 1: down / dense
   const void* trellis[2];   // int16 [E, K/16, N/16, 8*bits_x2]
-  int64_t trellis_estride;  // elements between experts
+  int64_t trellis_estride;  // elements between experts (contiguous [E, K/16, N/16, 8*bits_x2])
+  int num_experts;
   const void* svh[2];       // fp16 [E, N]
   int64_t svh_estride;
   const void* suh_next;     // fp16 [E, N] (gate/up pass only): suh of the down matrix

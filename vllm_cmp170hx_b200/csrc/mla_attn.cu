@@ -221,7 +221,7 @@ constexpr int PT = 64;                  // positions per tile
 constexpr int DIM = 576;                // latent 512 + rope 64
 constexpr int KV_BYTES = PT * DIM * 2;  // 73728
 constexpr int Q_BYTES = 128 * 64 * 2;   // one 64-dim chunk of 128 head rows
-constexpr int QST = 2;
+constexpr int QST = 3;
 constexpr int P_BYTES = 128 * PT * 2;   // 16384
 constexpr int SMEM = 1024 + 2 * KV_BYTES + QST * Q_BYTES + 2 * P_BYTES + 256;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -235,6 +235,7 @@ struct Params {
   const __nv_bfloat16* cache;  // [slots, 576]
   float sm_scale_log2;
   int splits;
+  int q_box_rows;      // rows of Q loaded per chunk (real heads of the group, <= 128)
   __nv_bfloat16* out;  // [T, nh, 512] (splits == 1)
   float* part_o;       // [splits, T, nh, 512] (splits > 1)
   float* part_ml;      // [splits, T, nh, 2] (max, sum) log2 domain
@@ -256,14 +257,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * P_BYTES);
   uint64_t* kv_full = bars;        // 2, count 4 (gather warps)
   uint64_t* kv_empty = bars + 2;   // 2, MMA commit
-  uint64_t* q_full = bars + 4;     // QST
-  uint64_t* q_empty = bars + 6;    // QST
-  uint64_t* s_full = bars + 8;     // 2
-  uint64_t* p_full = bars + 10;    // 2, count 128
-  uint64_t* p_empty = bars + 12;   // 2
-  uint64_t* o_full = bars + 14;
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_full = bars + 4;     // QST (<= 4)
+  uint64_t* q_empty = bars + 8;    // QST
+  uint64_t* s_full = bars + 12;    // 2
+  uint64_t* p_full = bars + 14;    // 2, count 128
+  uint64_t* p_empty = bars + 16;   // 2
+  uint64_t* o_full = bars + 18;
+  uint64_t* drain = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int t = blockIdx.x;
@@ -279,11 +280,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nt = max(0, tile1 - tile0);
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < QST; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 4);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&p_empty[i], 1);
@@ -311,13 +314,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t qph = 0, issued = 0;
       bool ok = true;
       const int row0 = t * p.nh + hg * 128;
+      // only this group's real head rows are loaded; the MMA's other rows
+      // read stale shared memory and their TMEM rows are never used
+      const uint32_t q_bytes = (uint32_t)p.q_box_rows * 128;
       for (int i = 0; i < nt && ok; ++i) {
         for (int c = 0; c < DIM / 64; ++c) {
           if (!mbar_wait_or_abort(&q_empty[qs], qph ^ 1, p.status, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&q_full[qs], Q_BYTES);
+          mbar_arrive_expect_tx(&q_full[qs], q_bytes);
           tma_load_2d(sq + qs * Q_BYTES, &tma_q, &q_full[qs], c * 64, row0);
           ++issued;
           if (++qs == QST) {
@@ -344,18 +350,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_or_abort(&kv_empty[b], ((i >> 1) & 1) ^ 1, p.status, abort_flag)) break;
       uint8_t* dst = skv + b * KV_BYTES;
       const int pbase = (tile0 + i) * PT;
-      // warp iteration: 8 rows x 4 chunks; 8 row groups x 18 chunk groups = 144 iterations / 4 warps
-#pragma unroll 4
+      // warp iteration: 8 rows x 4 chunks; 8 row groups x 18 chunk groups =
+      // 144 iterations over 4 warps.  Every copy is issued before any wait
+      // (cp.async, 16 B, zero-filled for positions without a row).
       for (int it = gw; it < 144; it += 4) {
         const int rg = it / 18, cgp = it % 18;
         const int pos = rg * 8 + (lane & 7);
         const int chunk = cgp * 4 + (lane >> 3);
         const int gp = pbase + pos;
         const int slot = gp < count ? idx[gp] : -1;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (slot >= 0) v = __ldg(reinterpret_cast<const uint4*>(p.cache + (int64_t)slot * DIM) + chunk);
-        *reinterpret_cast<uint4*>(dst + kv_off(pos, chunk)) = v;
+        const void* src = slot >= 0 ? reinterpret_cast<const void*>(reinterpret_cast<const uint4*>(p.cache +
+                                                                     (int64_t)slot * DIM) + chunk)
+                                    : reinterpret_cast<const void*>(p.cache);
+        const uint32_t sz = slot >= 0 ? 16u : 0u;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + kv_off(pos, chunk))),
+                     "l"(src), "r"(sz)
+                     : "memory");
       }
+      asm volatile("cp.async.wait_all;" ::: "memory");
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&kv_full[b]);
@@ -624,9 +636,11 @@ cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache
                                  float* lse, uint32_t* status, cudaStream_t stream) {
   using namespace mla::attn;
   if (T == 0) return cudaSuccess;
-  CUtensorMap tq = make_tma_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)T * nh, DIM, DIM, 128, 64,
+  const int box_rows = nh >= 128 ? 128 : (nh + 7) / 8 * 8;
+  CUtensorMap tq = make_tma_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)T * nh, DIM, DIM, box_rows, 64,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   Params p{};
+  p.q_box_rows = box_rows;
   p.indices = indices;
   p.counts = counts;
   p.topk = topk;

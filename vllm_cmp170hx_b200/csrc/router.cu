@@ -195,16 +195,34 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     }
     __syncthreads();
   }
-  // work items (single thread: E_local is small)
-  if (tid == 0) {
-    int n = 0;
-    for (int e = 0; e < E_local; ++e) {
-      const int r0 = expert_offsets[e], r1 = expert_offsets[e + 1];
-      for (int r = r0; r < r1 && n < max_items; r += tile_rows) {
-        items[n++] = make_int4(e, r, min(tile_rows, r1 - r), 0);
+  // work items: expert e contributes ceil(count_e / tile_rows) items, placed
+  // at the exclusive prefix of those counts (one block-wide scan)
+  __syncthreads();
+  int* nitems = warp_counts;  // reuse: [E_local] item counts, then prefix
+  for (int e = tid; e < E_local; e += blockDim.x)
+    nitems[e] = (expert_offsets[e + 1] - expert_offsets[e] + tile_rows - 1) / tile_rows;
+  __syncthreads();
+  if (warp == 0) {
+    int carry = 0;
+    for (int c0 = 0; c0 < E_local; c0 += 32) {
+      const int e = c0 + lane;
+      const int v = e < E_local ? nitems[e] : 0;
+      int s = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += t;
       }
+      if (e < E_local) base[e] = carry + s - v;  // reuse base[] as the item prefix
+      carry += __shfl_sync(0xffffffffu, s, 31);
     }
-    num_items[0] = n;
+    if (lane == 0) num_items[0] = carry < max_items ? carry : max_items;
+  }
+  __syncthreads();
+  for (int e = tid; e < E_local; e += blockDim.x) {
+    const int r0 = expert_offsets[e], r1 = expert_offsets[e + 1];
+    int n = base[e];
+    for (int r = r0; r < r1 && n < max_items; r += tile_rows) items[n++] = make_int4(e, r, min(tile_rows, r1 - r), 0);
   }
 }
 

@@ -199,6 +199,7 @@ void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<
   a.trellis[0] = trellis0.data_ptr();
   a.trellis[1] = nmat == 2 ? trellis1->data_ptr() : nullptr;
   a.trellis_estride = trellis0.stride(0);
+  a.num_experts = trellis0.size(0);
   a.svh[0] = svh0.data_ptr();
   a.svh[1] = nmat == 2 ? svh1->data_ptr() : nullptr;
   a.svh_estride = svh0.dim() == 2 ? svh0.stride(0) : 0;
