@@ -1,0 +1,64 @@
+"""Tensor parallel on CPU ranks (gloo): the tiny hybrid model at TP=2 with
+sliced weights generates the same greedy tokens as at TP=1 (heads, expert
+intermediates and the vocab shard split across ranks; per-rank sampling
+winners combined)."""
+
+import json
+import os
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny
+
+PROMPTS = [[(5 * i + 3 * j) % 500 for j in range(9 + 13 * i)] for i in range(3)]
+
+
+def _cfg(tp, fmt):
+    m = tiny(layers=4, experts=4, hidden=256, expert_format=fmt)
+    m.moe.intermediate = 256  # two H128 blocks: one per rank at TP=2
+    m.moe.shared_intermediate = 256
+    return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256),
+                        cache=CacheConfig(num_blocks=32), device="cpu", enforce_eager=True)
+
+
+def _generate(tp, fmt):
+    from vllm_cmp170hx_b200.engine.llm_engine import LLM
+    from vllm_cmp170hx_b200.engine.request import SamplingParams
+    from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+
+    cfg = _cfg(tp, fmt)
+    model = HybridForCausalLM(cfg.model, "cpu", seed=5, init_mode="sliced")
+    outs = LLM(cfg, model).generate(PROMPTS, SamplingParams(max_tokens=3))
+    return [o.output_token_ids for o in outs]
+
+
+def _worker(rank, world, port, fmt, path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.init(tp_size=world, device="cpu", timeout_s=120)
+    toks = _generate(world, fmt)
+    if rank == 0:
+        with open(path, "w") as f:
+            json.dump(toks, f)
+    pstate.destroy()
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "exl3"])
+def test_tp2_matches_tp1(fmt):
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    ref = _generate(1, fmt)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.json")
+        port = 29500 + os.getpid() % 1000
+        mp.start_processes(_worker, args=(2, port, fmt, path), nprocs=2, join=True, start_method="spawn")
+        with open(path) as f:
+            got = json.load(f)
+    assert got == ref

@@ -148,4 +148,9 @@ cudaError_t sample_rows(const void* logits, int dtype, int64_t ld, int rows, int
                         cudaStream_t stream);
 cudaError_t sample_combine(const float* vals, const int* idx, int R, int rows, int64_t* out, cudaStream_t stream);
 
+// ---------------------------------------------------------------- comm.cu
+cudaError_t symm_all_reduce(const void* in, void* out, int64_t n, const uint64_t* peers, int rank, int world,
+                            int64_t data_off, int64_t half_bytes, uint32_t* epochs, int blocks, uint32_t* status,
+                            uint64_t timeout_ns, cudaStream_t stream);
+
 }  // namespace b200

@@ -69,6 +69,10 @@ void sample_rows_op(const at::Tensor& logits, const c10::optional<at::Tensor>& t
                     at::Tensor& out_idx);  // sampling.cu
 void sample_combine_op(const at::Tensor& vals, const at::Tensor& idx, at::Tensor& out);  // sampling.cu
 
+void symm_all_reduce_op(const at::Tensor& in, at::Tensor& out, const at::Tensor& peers, int64_t rank, int64_t world,
+                        int64_t data_off, int64_t half_bytes, at::Tensor& epochs, const at::Tensor& status,
+                        double timeout_s);  // comm.cu
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -112,7 +116,9 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor(a!) out, Tensor(b!)? lse, Tensor(c!) status) -> ()")                                         \
   X("sample_rows(Tensor logits, Tensor? temperature, int seed, Tensor? step, int vocab_offset, "          \
     "Tensor(a!) out_val, Tensor(b!) out_idx) -> ()")                                                     \
-  X("sample_combine(Tensor vals, Tensor idx, Tensor(a!) out) -> ()")
+  X("sample_combine(Tensor vals, Tensor idx, Tensor(a!) out) -> ()")                                     \
+  X("symm_all_reduce(Tensor input, Tensor(a!) out, Tensor peers, int rank, int world, int data_off, "     \
+    "int half_bytes, Tensor(b!) epochs, Tensor(c!) status, float timeout_s) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -134,4 +140,5 @@ void register_host_bindings(pybind11::module_& m);
   X("mla_topk", b200::mla_topk_op)                    \
   X("mla_sparse_attention", b200::mla_sparse_attention_op) \
   X("sample_rows", b200::sample_rows_op)              \
-  X("sample_combine", b200::sample_combine_op)
+  X("sample_combine", b200::sample_combine_op)        \
+  X("symm_all_reduce", b200::symm_all_reduce_op)

@@ -478,3 +478,23 @@ void sample_combine_op(const at::Tensor& vals, const at::Tensor& idx, at::Tensor
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void symm_all_reduce_op(const at::Tensor& in, at::Tensor& out, const at::Tensor& peers, int64_t rank, int64_t world,
+                        int64_t data_off, int64_t half_bytes, at::Tensor& epochs, const at::Tensor& status,
+                        double timeout_s) {
+  B200_CHECK_CUDA(in);
+  B200_CHECK_DTYPE(in, at::kBFloat16);
+  TORCH_CHECK(in.is_contiguous() && out.is_contiguous() && out.sizes() == in.sizes(), "symm_all_reduce: layout");
+  TORCH_CHECK(in.numel() % 8 == 0, "symm_all_reduce: element count must be a multiple of 8");
+  TORCH_CHECK(peers.scalar_type() == at::kLong && peers.numel() == world && peers.is_cuda(), "symm_all_reduce: peers");
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.is_cuda(), "symm_all_reduce: epochs int32");
+  c10::cuda::CUDAGuard g(in.device());
+  B200_LAUNCH(symm_all_reduce(in.data_ptr(), out.data_ptr(), in.numel(),
+                              reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), (int)rank, (int)world,
+                              data_off, half_bytes, reinterpret_cast<uint32_t*>(epochs.data_ptr<int>()),
+                              (int)epochs.numel(), status_ptr(status), (uint64_t)(timeout_s * 1e9), cur_stream()));
+}
+
+}  // namespace b200
