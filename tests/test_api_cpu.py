@@ -1,0 +1,76 @@
+"""HTTP API over the engine on CPU (tiny model): completions, chat with
+reasoning + tool-call parsing, streaming, Anthropic messages, metrics; and
+the parsers' recovery rules."""
+
+import json
+
+import pytest
+
+from vllm_cmp170hx_b200.api import parsers
+
+
+def test_parsers_reasoning_and_tools():
+    r, c = parsers.split_reasoning("<think>plan</think>answer")
+    assert (r, c) == ("plan", "answer")
+    calls, content = parsers.parse_tool_calls('hi <tool_call>{"name": "f", "arguments": {"a": 1}}</tool_call>')
+    assert content == "hi" and calls[0].name == "f" and calls[0].arguments == {"a": 1}
+    # recovery: single quotes and trailing comma
+    calls, _ = parsers.parse_tool_calls("<tool_call>{'name': 'g', 'arguments': {'x': 2,},}</tool_call>")
+    assert calls and calls[0].name == "g" and calls[0].arguments == {"x": 2}
+    # GLM argument tags
+    calls, _ = parsers.parse_tool_calls("<tool_call>get<arg_key>city</arg_key><arg_value>\"Oslo\"</arg_value></tool_call>")
+    assert calls[0].name == "get" and calls[0].arguments == {"city": "Oslo"}
+    # unrecoverable call stays text
+    calls, content = parsers.parse_tool_calls("<tool_call>{{{</tool_call>")
+    assert not calls and "<tool_call>" in content
+
+
+def test_streaming_parser_holds_back_partial_tags():
+    sp = parsers.StreamingParser()
+    out = [sp.feed(x) for x in ["<th", "ink>ab", "c</th", "ink>hello <tool", '_call>{"name":"f","arguments":{}}',
+                                "</tool_call> bye"]]
+    r = "".join(o[0] for o in out)
+    c = "".join(o[1] for o in out) + sp.finish()[1]
+    assert r == "abc" and c == "hello  bye" and sp.calls[0].name == "f"
+
+
+@pytest.fixture(scope="module")
+def client():
+    from fastapi.testclient import TestClient
+
+    from vllm_cmp170hx_b200.api.server import AsyncEngine, build_app
+    from vllm_cmp170hx_b200.api.tokenizer import ByteTokenizer
+    from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, SchedulerConfig, tiny
+    from vllm_cmp170hx_b200.engine.llm_engine import LLMEngine
+    from vllm_cmp170hx_b200.engine.spmd import SPMDEngine
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    cfg = EngineConfig(model=tiny(layers=2, experts=4, expert_format="bf16"),
+                       scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=256, max_model_len=512),
+                       cache=CacheConfig(num_blocks=32), device="cpu", enforce_eager=True)
+    eng = LLMEngine(cfg)
+    ae = AsyncEngine(SPMDEngine(eng))
+    with TestClient(build_app(ae, ByteTokenizer(512), "tiny")) as c:
+        yield c
+    ae.shutdown()
+
+
+def test_http_endpoints(client):
+    assert client.get("/health").json()["status"] == "ok"
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    r = client.post("/v1/completions", json={"prompt": "hello", "max_tokens": 3}).json()
+    assert r["usage"]["completion_tokens"] == 3 and len(r["choices"][0]["token_ids"]) == 3
+    r = client.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 2}).json()
+    assert r["usage"]["prompt_tokens"] == 3
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                   "max_tokens": 4}).json()
+    assert r["choices"][0]["message"]["role"] == "assistant"
+    with client.stream("POST", "/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                             "max_tokens": 3, "stream": True}) as s:
+        lines = [l for l in s.iter_lines() if l.startswith("data: ")]
+    assert lines[-1] == "data: [DONE]" and json.loads(lines[-2][6:])["choices"][0]["finish_reason"] == "length"
+    r = client.post("/v1/messages", json={"system": "be brief", "messages": [{"role": "user", "content": "hi"}],
+                                          "max_tokens": 2}).json()
+    assert r["type"] == "message" and r["usage"]["output_tokens"] == 2
+    assert "b200_requests_total" in client.get("/metrics").text

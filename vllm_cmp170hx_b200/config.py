@@ -227,3 +227,52 @@ class EngineConfig:
     device: str = "cuda"
     enforce_eager: bool = False
     cuda_graph_batch_sizes: list[int] = field(default_factory=lambda: [1, 2, 4, 8, 16, 32, 64, 128, 256])
+
+
+def from_hf_config(hf: dict) -> ModelConfig:
+    """ModelConfig from a Hugging Face style config.json of the supported
+    families: GLM-5.x hybrid (`glm5_next[_text]`: linear_attn_config, layer_types
+    'linear_attention' / 'deepseek_sparse_attention', the fixture shape of
+    tests/models/fixtures/native_checkpoint_configs/glm53_flash/config.json in the
+    reference) and DeepSeek-V3.x-style sparse MLA MoE (`deepseek_v3[2]`)."""
+    c = hf.get("text_config", hf)
+    n = int(c["num_hidden_layers"])
+    lt = c.get("layer_types")
+    if lt:
+        layer_types = ["kda" if t == "linear_attention" else "mla" for t in lt]
+    else:
+        layer_types = ["mla"] * n
+    fkd = int(c.get("first_k_dense_replace", 0))
+    mlp_types = c.get("mlp_layer_types")
+    if mlp_types:
+        mlp_types = ["moe" if t == "sparse" else "dense" for t in mlp_types]
+    else:
+        mlp_types = ["dense" if i < fkd else "moe" for i in range(n)]
+    la = c.get("linear_attn_config", {})
+    kda = KDAConfig(num_heads=int(la.get("num_heads", c.get("linear_num_heads", 32))),
+                    head_dim=int(la.get("head_dim", c.get("linear_head_dim", 128))),
+                    conv_kernel=int(la.get("short_conv_kernel_size", c.get("linear_conv_kernel_dim", 4))),
+                    lower_bound=float(la.get("gate_lower_bound", c.get("linear_lower_bound", -5.0))))
+    rope = int(c.get("qk_rope_head_dim", 64) or 64)
+    mla = MLAConfig(num_heads=int(c["num_attention_heads"]), q_lora_rank=int(c.get("q_lora_rank") or 1536),
+                    kv_lora_rank=int(c.get("kv_lora_rank", 512)),
+                    qk_nope_head_dim=int(c.get("qk_nope_head_dim", 128)) if rope else 128,
+                    qk_rope_head_dim=64, v_head_dim=min(int(c.get("v_head_dim", 128)), 512),
+                    index_n_heads=int(c.get("index_n_heads", 64)), index_head_dim=int(c.get("index_head_dim", 128)),
+                    index_topk=int(c.get("index_topk", 2048)), rope_theta=float(c.get("rope_theta", 10000.0)),
+                    rope_interleave=bool(c.get("indexer_rope_interleave", False)))
+    scoring = c.get("scoring_func", "softmax")
+    moe = MoEConfig(num_experts=int(c.get("n_routed_experts", 0) or 1), top_k=int(c.get("num_experts_per_tok", 1)),
+                    intermediate=int(c.get("moe_intermediate_size", c.get("intermediate_size", 1024))),
+                    num_shared=int(c.get("n_shared_experts", 0) or 0),
+                    shared_intermediate=int(c.get("moe_intermediate_size", 1024)),
+                    router={"sigmoid": "sigmoid", "sqrtsoftplus": "sqrt_softplus"}.get(scoring, "softmax"),
+                    routed_scaling=float(c.get("routed_scaling_factor", 1.0)),
+                    renormalize=bool(c.get("norm_topk_prob", True)), swiglu_limit=float(c.get("swiglu_limit", 0.0)))
+    return ModelConfig(name=str(c.get("model_type", "hf")), vocab_size=int(c["vocab_size"]),
+                       hidden_size=int(c["hidden_size"]), num_layers=n, layer_types=layer_types, mlp_types=mlp_types,
+                       dense_intermediate=int(c.get("intermediate_size", 12288)), kda=kda, mla=mla, moe=moe,
+                       rms_eps=float(c.get("rms_norm_eps", 1e-5)),
+                       max_position=int(c.get("max_position_embeddings", 1 << 20)),
+                       tie_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                       num_mtp_layers=int(c.get("num_nextn_predict_layers", 0)))
