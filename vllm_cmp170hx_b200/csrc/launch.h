@@ -153,4 +153,28 @@ cudaError_t symm_all_reduce(const void* in, void* out, int64_t n, const uint64_t
                             int64_t data_off, int64_t half_bytes, uint32_t* epochs, int blocks, uint32_t* status,
                             uint64_t timeout_ns, cudaStream_t stream);
 
+// ---------------------------------------------------------------- dequant_gemm.cu
+struct DequantGemmArgs {
+  int format;            // 0 Marlin int4 g128, 1 fp8 e4m3 128x128 block
+  int nmat;              // 2: gate/up pass (SwiGLU), 1: down / dense
+  const void* w[2];      // Marlin int32 [E, K/16, 2N]; fp8 uint8 [E, N, K]
+  const void* scale[2];  // Marlin bf16 [E, K/128, N] (stored order); fp8 fp32 [E, N/128, K/128]
+  int E, K, N;
+  const void* b0;        // activations [b_rows, K] (bf16 Marlin, fp16 fp8)
+  const void* b1;
+  int64_t b_rows;
+  int tile_rows;
+  const int* items;
+  const int* num_items;
+  int max_work;
+  void* out;
+  int64_t ld_out;
+  int out_mode;          // 0 operand type, 1 fp32, 2 bf16
+  float swiglu_limit;
+  uint32_t* status;
+};
+cudaError_t dequant_gemm(const DequantGemmArgs& a, cudaStream_t stream);
+cudaError_t gather_rows(const void* x, int64_t ld_x, int K, const int* src, void* out, int to_f16, int rows,
+                        cudaStream_t stream);
+
 }  // namespace b200

@@ -73,6 +73,14 @@ void symm_all_reduce_op(const at::Tensor& in, at::Tensor& out, const at::Tensor&
                         int64_t data_off, int64_t half_bytes, at::Tensor& epochs, const at::Tensor& status,
                         double timeout_s);  // comm.cu
 
+void dequant_gemm_op(int64_t format, int64_t nmat, const at::Tensor& w0, const c10::optional<at::Tensor>& w1,
+                     const at::Tensor& s0, const c10::optional<at::Tensor>& s1, const at::Tensor& b0,
+                     const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
+                     const at::Tensor& num_items, int64_t max_work, at::Tensor& out, int64_t out_mode,
+                     double swiglu_limit, const at::Tensor& status);  // dequant_gemm.cu
+void gather_rows_op(const at::Tensor& x, const c10::optional<at::Tensor>& src, at::Tensor& out,
+                    int64_t rows);  // dequant_gemm.cu
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -118,7 +126,11 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor(a!) out_val, Tensor(b!) out_idx) -> ()")                                                     \
   X("sample_combine(Tensor vals, Tensor idx, Tensor(a!) out) -> ()")                                     \
   X("symm_all_reduce(Tensor input, Tensor(a!) out, Tensor peers, int rank, int world, int data_off, "     \
-    "int half_bytes, Tensor(b!) epochs, Tensor(c!) status, float timeout_s) -> ()")
+    "int half_bytes, Tensor(b!) epochs, Tensor(c!) status, float timeout_s) -> ()")                       \
+  X("dequant_gemm(int format, int nmat, Tensor w0, Tensor? w1, Tensor s0, Tensor? s1, Tensor b0, Tensor? b1, " \
+    "int tile_rows, Tensor items, Tensor num_items, int max_work, Tensor(a!) out, int out_mode, "             \
+    "float swiglu_limit, Tensor(b!) status) -> ()")                                                       \
+  X("gather_rows(Tensor x, Tensor? src, Tensor(a!) out, int rows) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -141,4 +153,6 @@ void register_host_bindings(pybind11::module_& m);
   X("mla_sparse_attention", b200::mla_sparse_attention_op) \
   X("sample_rows", b200::sample_rows_op)              \
   X("sample_combine", b200::sample_combine_op)        \
-  X("symm_all_reduce", b200::symm_all_reduce_op)
+  X("symm_all_reduce", b200::symm_all_reduce_op)      \
+  X("dequant_gemm", b200::dequant_gemm_op)            \
+  X("gather_rows", b200::gather_rows_op)

@@ -498,3 +498,66 @@ void symm_all_reduce_op(const at::Tensor& in, at::Tensor& out, const at::Tensor&
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void dequant_gemm_op(int64_t format, int64_t nmat, const at::Tensor& w0, const c10::optional<at::Tensor>& w1,
+                     const at::Tensor& s0, const c10::optional<at::Tensor>& s1, const at::Tensor& b0,
+                     const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
+                     const at::Tensor& num_items, int64_t max_work, at::Tensor& out, int64_t out_mode,
+                     double swiglu_limit, const at::Tensor& status) {
+  B200_CHECK_CUDA(w0);
+  TORCH_CHECK(w0.dim() == 3 && w0.is_contiguous(), "dequant_gemm: weights [E, ...] contiguous");
+  DequantGemmArgs a{};
+  a.format = (int)format;
+  a.nmat = (int)nmat;
+  a.E = w0.size(0);
+  if (format == 0) {
+    TORCH_CHECK(w0.scalar_type() == at::kInt, "marlin: packed int32 [E, K/16, 2N]");
+    a.K = w0.size(1) * 16;
+    a.N = w0.size(2) / 2;
+    TORCH_CHECK(s0.scalar_type() == at::kBFloat16 && s0.size(1) == a.K / 128 && s0.size(2) == a.N, "marlin scales");
+  } else {
+    TORCH_CHECK(w0.element_size() == 1, "fp8: weights [E, N, K] one byte each");
+    a.N = w0.size(1);
+    a.K = w0.size(2);
+    TORCH_CHECK(s0.scalar_type() == at::kFloat && s0.size(1) == a.N / 128 && s0.size(2) == a.K / 128, "fp8 scales");
+  }
+  TORCH_CHECK(s0.is_contiguous(), "dequant_gemm: scales contiguous");
+  if (nmat == 2) {
+    TORCH_CHECK(w1.has_value() && s1.has_value() && b1.has_value(), "dequant_gemm: gate/up needs w1, s1, b1");
+    TORCH_CHECK(w1->sizes() == w0.sizes() && w1->is_contiguous(), "dequant_gemm: w1 shape");
+  }
+  TORCH_CHECK(b0.is_contiguous() && b0.size(-1) == a.K, "dequant_gemm: activations [rows, K]");
+  TORCH_CHECK(b0.scalar_type() == (format == 0 ? at::kBFloat16 : at::kHalf), "dequant_gemm: activation dtype");
+  c10::cuda::CUDAGuard g(b0.device());
+  a.w[0] = w0.data_ptr();
+  a.w[1] = nmat == 2 ? w1->data_ptr() : nullptr;
+  a.scale[0] = s0.data_ptr();
+  a.scale[1] = nmat == 2 ? s1->data_ptr() : nullptr;
+  a.b0 = b0.data_ptr();
+  a.b1 = opt_ptr(b1);
+  a.b_rows = b0.size(0);
+  a.tile_rows = (int)tile_rows;
+  a.items = items.data_ptr<int>();
+  a.num_items = num_items.data_ptr<int>();
+  a.max_work = (int)max_work;
+  a.out = out.data_ptr();
+  a.ld_out = out.stride(0);
+  a.out_mode = (int)out_mode;
+  a.swiglu_limit = (float)swiglu_limit;
+  a.status = status_ptr(status);
+  B200_LAUNCH(dequant_gemm(a, cur_stream()));
+}
+
+void gather_rows_op(const at::Tensor& x, const c10::optional<at::Tensor>& src, at::Tensor& out, int64_t rows) {
+  B200_CHECK_CUDA(x);
+  B200_CHECK_DTYPE(x, at::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.is_contiguous() && out.size(-1) == x.size(1), "gather_rows");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kHalf, "gather_rows: out bf16/fp16");
+  c10::cuda::CUDAGuard g(x.device());
+  B200_LAUNCH(gather_rows(x.data_ptr(), x.stride(0), x.size(1), src.has_value() ? src->data_ptr<int>() : nullptr,
+                          out.data_ptr(), out.scalar_type() == at::kHalf ? 1 : 0, (int)rows, cur_stream()));
+}
+
+}  // namespace b200
