@@ -182,7 +182,26 @@ def tiny(layers: int = 4, experts: int = 8, hidden: int = 256, vocab: int = 512,
     )
 
 
-PRESETS = {"config3": config3, "config4": config4, "config2_layer": config2_layer, "tiny": tiny}
+def tiny_deepseek(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: int = 512) -> ModelConfig:
+    """Small model of the DeepSeek family (all sparse-MLA, Marlin experts, fp8 attention, dense first layer)."""
+    return ModelConfig(
+        name="tiny-deepseek",
+        vocab_size=vocab,
+        hidden_size=hidden,
+        num_layers=layers,
+        layer_types=["mla"] * layers,
+        mlp_types=["dense"] + ["moe"] * (layers - 1),
+        dense_intermediate=256,
+        mla=MLAConfig(num_heads=2, q_lora_rank=128, index_n_heads=64, index_topk=64, attn_weight_format="fp8_block"),
+        moe=MoEConfig(num_experts=experts, top_k=2, intermediate=256, num_shared=1, shared_intermediate=128,
+                      router="sigmoid", routed_scaling=2.5, expert_format="marlin"),
+        max_position=4096,
+        num_mtp_layers=1,
+    )
+
+
+PRESETS = {"config3": config3, "config4": config4, "config2_layer": config2_layer, "tiny": tiny,
+           "tiny_deepseek": tiny_deepseek}
 
 
 @dataclass

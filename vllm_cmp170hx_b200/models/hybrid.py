@@ -56,6 +56,12 @@ class StepContext:
     scores_buf: torch.Tensor | None = None
 
 
+def _fp8_proj(w: torch.Tensor):
+    from .marlin_experts import Fp8Proj
+
+    return Fp8Proj(w)
+
+
 # ============================================================================ attention
 class KDAAttention(nn.Module):
     """Kimi-delta attention layer (GLM `linear_attention`): fused input GEMM
@@ -132,17 +138,19 @@ class MLAAttention(nn.Module):
         assert kvl == 512 and dr == 64 and m.index_head_dim == 128
         # fused first projection: q_a | kv_a (512 + 64) | indexer k (128) | indexer head weights
         self.in_splits = [ql, kvl + dr, m.index_head_dim, m.index_n_heads]
-        self.in_proj = Linear(torch.cat([wi.normal((ql, hid), sd), wi.normal((kvl + dr, hid), sd),
-                                         wi.normal((m.index_head_dim, hid), sd),
-                                         wi.normal((m.index_n_heads, hid), sd)], dim=0).contiguous())
+        fp8 = m.attn_weight_format == "fp8_block"
+        Proj = _fp8_proj if fp8 else Linear
+        self.in_proj = Proj(torch.cat([wi.normal((ql, hid), sd), wi.normal((kvl + dr, hid), sd),
+                                       wi.normal((m.index_head_dim, hid), sd),
+                                       wi.normal((m.index_n_heads, hid), sd)], dim=0).contiguous())
         self.q_a_norm = RMSNorm(wi.ones_plus(ql, 0.05), cfg.rms_eps)
         self.kv_a_norm_w = nn.Parameter(wi.ones_plus(kvl, 0.05), requires_grad=False)
-        self.q_b = Linear(wi.normal((m.num_heads * (dn + dr), ql), default_std(ql), (0, tp_rank, tp)))
+        self.q_b = Proj(wi.normal((m.num_heads * (dn + dr), ql), default_std(ql), (0, tp_rank, tp)))
         # kv_b: [H*(dn + dv), kvl] -> absorbed per-head W_UK [H, dn, kvl], W_UV [H, kvl, dv]
         kvb = wi.normal((m.num_heads, dn + dv, kvl), default_std(kvl), (0, tp_rank, tp))
         self.w_uk = nn.Parameter(kvb[:, :dn, :].contiguous(), requires_grad=False)  # [H, dn, kvl]
         self.w_uv_t = nn.Parameter(kvb[:, dn:, :].contiguous(), requires_grad=False)  # [H, dv, kvl]
-        self.o_proj = Linear(wi.normal((hid, m.num_heads * dv), default_std(m.num_heads * dv), (1, tp_rank, tp)))
+        self.o_proj = Proj(wi.normal((hid, m.num_heads * dv), default_std(m.num_heads * dv), (1, tp_rank, tp)))
         # indexer
         self.idx_q = Linear(wi.normal((m.index_n_heads * m.index_head_dim, ql), default_std(ql)))
         self.idx_k_ln_w = nn.Parameter(wi.ones_plus(m.index_head_dim, 0.05), requires_grad=False)
@@ -304,6 +312,10 @@ class MoE(nn.Module):
         shared = self.shared(x) if self.shared is not None else None
         if isinstance(self.experts, moe_ops.Exl3Experts):
             return moe_ops.exl3_moe(x, ids, w, self.experts, add=shared)
+        from ..ops.dequant import MarlinExperts, marlin_moe
+
+        if isinstance(self.experts, MarlinExperts):
+            return marlin_moe(x, ids, w, self.experts, add=shared)
         return self.experts(x, ids, w, add=shared)
 
 
