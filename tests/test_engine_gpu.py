@@ -27,7 +27,7 @@ def test_gpu_forward_matches_cpu_oracle(fmt):
     prompts = [list(range(3, 3 + 90)), [5, 9, 11]]
     hs = {}
     for dev in ("cpu", "cuda"):
-        model = HybridForCausalLM(_cfg(dev).model, dev, seed=3, init_mode="sliced")
+        model = HybridForCausalLM(_cfg(dev, fmt=fmt).model, dev, seed=3, init_mode="sliced")
         eng = LLMEngine(_cfg(dev, fmt=fmt), model)
         for p in prompts:
             eng.add_request(p, SamplingParams(max_tokens=1))

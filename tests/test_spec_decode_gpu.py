@@ -1,0 +1,90 @@
+"""DeepSeek-family model and MTP speculative decoding on the GPU: the tiny
+DeepSeek model (fp8 block-scaled attention projections, Marlin int4 experts)
+against the CPU oracle, and greedy speculative decoding against plain greedy
+decoding (CUDA-graph decode)."""
+
+import pytest
+import torch
+
+from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, SchedulerConfig, tiny_deepseek
+from vllm_cmp170hx_b200.engine import spec_decode
+from vllm_cmp170hx_b200.engine.llm_engine import LLM, LLMEngine
+from vllm_cmp170hx_b200.engine.request import SamplingParams
+from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+from vllm_cmp170hx_b200.parallel import state as pstate
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg(device, k=0, eager=False):
+    return EngineConfig(model=tiny_deepseek(layers=3, experts=8, hidden=256, vocab=512),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=256, max_model_len=512,
+                                                  num_speculative_tokens=k),
+                        cache=CacheConfig(num_blocks=40), device=device, enforce_eager=eager,
+                        cuda_graph_batch_sizes=[1, 2, 4])
+
+
+PROMPTS = [list(range(3, 3 + n)) for n in (12, 70, 131)]
+MAX_TOKENS = [10, 8, 7]
+
+
+@pytest.fixture(scope="module")
+def model():
+    pstate.set_state(pstate.ParallelState())
+    return HybridForCausalLM(_cfg("cuda").model, "cuda", seed=9)
+
+
+def test_deepseek_forward_matches_cpu_oracle():
+    pstate.set_state(pstate.ParallelState())
+    logits = {}
+    for dev in ("cpu", "cuda"):
+        m = HybridForCausalLM(_cfg(dev).model, dev, seed=3, init_mode="sliced")
+        eng = LLMEngine(_cfg(dev, eager=True), m)
+        for p in PROMPTS[:2]:
+            eng.add_request(p, SamplingParams(max_tokens=1))
+        out = eng.scheduler.schedule()
+        h = eng.runner._host_inputs(out)
+        d, ctx, _ = eng.runner._context(h)
+        with torch.inference_mode():
+            logits[dev] = m.compute_logits(m(d["ids"], ctx)).float().cpu()
+    rel = ((logits["cuda"] - logits["cpu"]).norm() / logits["cpu"].norm()).item()
+    assert rel < 5e-2, rel
+
+
+def _plain(model):
+    params = [SamplingParams(max_tokens=m) for m in MAX_TOKENS]
+    return [o.output_token_ids for o in LLM(_cfg("cuda"), model).generate(PROMPTS, params)]
+
+
+def test_greedy_spec_matches_plain(model):
+    ref = _plain(model)
+    llm = LLM(_cfg("cuda", k=3), model)
+    got = [o.output_token_ids for o in llm.generate(PROMPTS, [SamplingParams(max_tokens=m) for m in MAX_TOKENS])]
+    assert got == ref
+    assert llm.engine.runner.spec.stats["proposed"] > 0
+
+
+def test_planted_drafts_all_accepted(model, monkeypatch):
+    ref = _plain(model)
+    by_prompt = {tuple(p): r for p, r in zip(PROMPTS, ref)}
+
+    def oracle(self, out, hidden, accepted):
+        for s in out.reqs:
+            req = s.req
+            if req.status.finished or req.num_computed_tokens != req.num_tokens - 1:
+                continue
+            n = len(req.output_token_ids)
+            req.draft_token_ids = by_prompt[tuple(req.prompt_token_ids)][n:n + min(self.k, req.params.max_tokens - n - 1)]
+
+    monkeypatch.setattr(spec_decode.SpecDecoder, "propose", oracle)
+    llm = LLM(_cfg("cuda", k=3), model)
+    got = [o.output_token_ids for o in llm.generate(PROMPTS, [SamplingParams(max_tokens=m) for m in MAX_TOKENS])]
+    assert got == ref
+    st = llm.engine.runner.spec.stats
+    assert st["accepted"] == st["proposed"] > 0
+
+
+def test_sampled_spec(model):
+    llm = LLM(_cfg("cuda", k=3), model)
+    got = llm.generate(PROMPTS, [SamplingParams(max_tokens=m, temperature=0.7) for m in MAX_TOKENS])
+    assert [len(o.output_token_ids) for o in got] == MAX_TOKENS

@@ -11,17 +11,25 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny
+from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny, tiny_deepseek
 
 PROMPTS = [[(5 * i + 3 * j) % 500 for j in range(9 + 13 * i)] for i in range(3)]
 
 
 def _cfg(tp, fmt):
-    m = tiny(layers=4, experts=4, hidden=256, expert_format=fmt)
-    m.moe.intermediate = 256  # two H128 blocks: one per rank at TP=2
-    m.moe.shared_intermediate = 256
+    k = 0
+    if fmt == "deepseek_mtp":  # Marlin experts, fp8 attention projections, MTP speculative decoding
+        m = tiny_deepseek(layers=2, experts=4, hidden=256, vocab=512)
+        m.moe.intermediate = 256
+        m.mla.num_heads = 4  # two heads per rank: q_b shards of 384 rows hold whole fp8 scale blocks
+        k = 2
+    else:
+        m = tiny(layers=4, experts=4, hidden=256, expert_format=fmt)
+        m.moe.intermediate = 256  # two H128 blocks: one per rank at TP=2
+        m.moe.shared_intermediate = 256
     return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp),
-                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256,
+                                                  num_speculative_tokens=k),
                         cache=CacheConfig(num_blocks=32), device="cpu", enforce_eager=True)
 
 
@@ -32,7 +40,7 @@ def _generate(tp, fmt):
 
     cfg = _cfg(tp, fmt)
     model = HybridForCausalLM(cfg.model, "cpu", seed=5, init_mode="sliced")
-    outs = LLM(cfg, model).generate(PROMPTS, SamplingParams(max_tokens=3))
+    outs = LLM(cfg, model).generate(PROMPTS, SamplingParams(max_tokens=6 if cfg.scheduler.num_speculative_tokens else 3))
     return [o.output_token_ids for o in outs]
 
 
@@ -49,7 +57,7 @@ def _worker(rank, world, port, fmt, path):
     pstate.destroy()
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "exl3"])
+@pytest.mark.parametrize("fmt", ["bf16", "exl3", "deepseek_mtp"])
 def test_tp2_matches_tp1(fmt):
     from vllm_cmp170hx_b200.parallel import state as pstate
 

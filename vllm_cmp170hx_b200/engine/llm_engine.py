@@ -70,6 +70,7 @@ class LLMEngine:
         before = {s.req.request_id: len(s.req.output_token_ids) for s in out.reqs}
         sampled = self.runner.execute(out)
         self.scheduler.update(out, sampled)
+        self.runner.propose()
         self.num_steps += 1
         res = []
         for s in out.reqs:

@@ -55,6 +55,12 @@ class ModelRunner:
         self.graph_pool = None
         self.last_stats = StepStats()
         self.time_device = False  # record CUDA events around each step's device work
+        self.spec = None
+        self._pending = None
+        if cfg.scheduler.num_speculative_tokens > 0:
+            from .spec_decode import SpecDecoder
+
+            self.spec = SpecDecoder(self, cfg.scheduler.num_speculative_tokens)
 
     # ------------------------------------------------------------------ caches
     def _alloc_caches(self):
@@ -69,7 +75,8 @@ class ModelRunner:
                 torch.cuda.synchronize()
                 free, _total = torch.cuda.mem_get_info(self.device)
                 kda_bytes = len(kda_ids) * self.num_slots * (math.prod(rec_shape) * 4 + math.prod(conv_shape) * 2)
-                per_block = max(1, len(mla_ids)) * 64 * (576 * 2 + 128 + 4)
+                n_mla = len(mla_ids) + (1 if cfg.scheduler.num_speculative_tokens > 0 else 0)  # + MTP layer
+                per_block = max(1, n_mla) * 64 * (576 * 2 + 128 + 4)
                 scratch = 6 << 30
                 avail = free * cfg.cache.gpu_memory_utilization - kda_bytes - scratch
                 nb = int(max(avail, 0) // per_block)
@@ -182,6 +189,8 @@ class ModelRunner:
     def execute(self, out: SchedulerOutput) -> dict[str, list[int]]:
         if not out.reqs:
             return {}
+        if self.spec is not None:
+            return self._execute_spec(out)
         use_graph = (not self.cfg.enforce_eager and self.device.type == "cuda" and out.decode_only
                      and all(s.num_draft == 0 for s in out.reqs)
                      and len(out.reqs) <= max(self.cfg.cuda_graph_batch_sizes))
@@ -218,6 +227,47 @@ class ModelRunner:
         return self._split_tokens(out, host)
 
     _events = None
+
+    def _execute_spec(self, out: SchedulerOutput) -> dict[str, list[int]]:
+        """Eager target step with draft verification; the hidden states are kept for :meth:`propose`."""
+        h = self._host_inputs(out)
+        dev, ctx, nbytes = self._context(h)
+        ev = self._ev_start()
+        hidden = self.model(dev["ids"], ctx)
+        rows_of = {}
+        k = 0
+        t = 0
+        for s in out.reqs:
+            if s.sample:
+                n = s.num_new if s.num_draft else 1
+                rows_of[s.req.request_id] = list(range(k, k + n))
+                k += n
+            t += s.num_new
+        res = {}
+        if k:
+            logits = self.model.compute_logits(hidden.index_select(0, self._to_dev(h["sample_rows"])))
+            res = self.spec.verify(out, logits, rows_of)
+        self._ev_end(ev)
+        self.step_counter += 1
+        stats = StepStats(num_tokens=out.num_tokens, graph=False, h2d_bytes=nbytes,
+                          d2h_bytes=8 * sum(len(v) for v in res.values()))
+        if self._events is not None:
+            stats.device_ms = self._events[0].elapsed_time(self._events[1])
+            self._events = None
+        self.last_stats = stats
+        self._pending = (out, hidden, res)
+        if self.device.type == "cuda":
+            _ext.check_status(self.device)
+        return res
+
+    @torch.inference_mode()
+    def propose(self) -> None:
+        """Draft tokens for the next step (speculative decoding; after the scheduler update)."""
+        if self.spec is None or self._pending is None:
+            return
+        out, hidden, res = self._pending
+        self._pending = None
+        self.spec.propose(out, hidden, res)
 
     def _ev_start(self):
         if not (self.time_device and self.device.type == "cuda"):

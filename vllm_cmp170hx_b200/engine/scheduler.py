@@ -58,6 +58,8 @@ class Scheduler:
         self.waiting: collections.deque[Request] = collections.deque()
         self.running: list[Request] = []
         self.finished: list[Request] = []
+        # speculative decoding: KV blocks reserved past a sampling step for the drafter's own cache writes
+        self.lookahead = max(0, sched.num_speculative_tokens - 1)
 
     # ------------------------------------------------------------------ API
     def add(self, req: Request) -> None:
@@ -132,12 +134,15 @@ class Scheduler:
                 n = min(remaining, budget, cap)
                 drafts = 0
             else:
-                drafts = len(req.draft_token_ids)
+                drafts = min(len(req.draft_token_ids), max(0, budget - 1))
                 n = 1 + drafts
             if n <= 0 or n > budget:
                 i += 1
                 continue
             upto = req.num_computed_tokens + n
+            if upto >= req.num_tokens:
+                # the drafter writes its cache up to k-1 positions past this step
+                upto = min(upto + self.lookahead, self.cfg.max_model_len)
             while not self._grow(req, upto):
                 victim = self.running[-1]
                 if victim is req:
@@ -147,7 +152,7 @@ class Scheduler:
                 # could not make room even alone: preempt this one
                 self._preempt(req, out)
                 continue
-            sample = upto >= req.num_tokens
+            sample = req.num_computed_tokens + n >= req.num_tokens
             if not sample:
                 partial += 1
             out.reqs.append(ScheduledReq(req, n, req.num_computed_tokens, sample, drafts))
@@ -160,14 +165,17 @@ class Scheduler:
             if partial >= self.cfg.max_num_partial_prefills and req.num_tokens > budget:
                 break
             n = min(req.num_tokens - req.num_computed_tokens, budget, cap)
-            if self._blocks_needed(req, req.num_computed_tokens + n) > self.blocks.num_free():
+            upto = req.num_computed_tokens + n
+            if upto >= req.num_tokens:
+                upto = min(upto + self.lookahead, self.cfg.max_model_len)
+            if self._blocks_needed(req, upto) > self.blocks.num_free():
                 break
             if self.slots is not None and req.kda_slot <= 0 and self.slots.num_free() == 0:
                 break
             self.waiting.popleft()
             if self.slots is not None and req.kda_slot <= 0:
                 req.kda_slot = self.slots.allocate()
-            self._grow(req, req.num_computed_tokens + n)
+            self._grow(req, upto)
             req.status = Status.RUNNING
             self.running.append(req)
             sample = req.num_computed_tokens + n >= req.num_tokens

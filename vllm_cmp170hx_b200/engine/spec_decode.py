@@ -1,0 +1,276 @@
+"""Speculative decoding with an MTP draft head: verification, rejection
+sampling and proposal over vocab-sharded logits.
+
+A request verified with k drafts d_1..d_k computes positions p..p+k holding
+[last, d_1..d_k]; the target's logits row j scores the token after position
+p+j.  Greedy requests accept drafts while they equal the target's argmax and
+take the target's token at the first mismatch (the bonus token after k
+accepts).  Sampled requests use speculative rejection sampling: accept d_j
+with probability min(1, p_j(d_j) / q_j(d_j)); at the first rejection sample
+from normalize(max(0, p_j - q_j)); after k accepts sample the bonus from
+p_k, where p is the target's tempered softmax and q the draft's.  The
+resulting tokens are distributed exactly as the target's own samples.
+
+Everything is batched over the step's rows and stays on the device until a
+single host copy: with tensor parallel the vocab is sharded, maxima and sums
+are all-reduced, the draft token's probability comes from its owning shard,
+and residual/bonus draws are Gumbel-max per shard (the sampling kernel, whose
+noise is indexed by global vocab id) combined across ranks, so logits are
+never gathered (the reference shards its argmax the same way,
+vllm_sm80/spec_decode/shard_argmax.py).  Acceptance uniforms come from a
+host generator seeded by (seed, step), identical on every rank.
+
+Proposal (the DeepSeek MTP drafter of the reference's config 5): after the
+target step the MTP head catches up over the positions the target just
+computed -- position i takes token i+1 and the target's final hidden h_i --
+and then chains k-1 single-token steps on its own hidden state.  The drafts
+of all requests are produced together and copied to the host once.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ..models.hybrid import StepContext
+from ..ops import sampling as sampling_ops
+from ..parallel import comm
+from ..parallel import state as pstate
+
+_SEED_VERIFY = 0x5BD1E995
+_SEED_DRAFT = 0x27D4EB2F
+
+
+def _all_reduce(x: torch.Tensor, op=dist.ReduceOp.SUM) -> torch.Tensor:
+    st = pstate.get()
+    if st.tp_size > 1:
+        dist.all_reduce(x, op=op, group=st.tp_group)
+    return x
+
+
+def _sample(logits: torch.Tensor, temps: torch.Tensor | None, seed: int, step: torch.Tensor | None, off: int):
+    """Token ids [rows] (device int64) of greedy/Gumbel sampling over the sharded vocab."""
+    val, idx = sampling_ops.sample_local(logits, temps, seed, step, off)
+    if pstate.get().tp_size > 1:
+        return sampling_ops.combine(comm.tp_all_gather(val[None], 0), comm.tp_all_gather(idx[None], 0))
+    return idx.long()
+
+
+def tempered_probs(logits: torch.Tensor, temps: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(unnormalised exp(l/T - max) of this shard [rows, V_local], global sums [rows])."""
+    z = logits.float() / temps[:, None]
+    m = _all_reduce(z.max(dim=-1).values.contiguous(), dist.ReduceOp.MAX)
+    e = torch.exp(z - m[:, None])
+    return e, e.sum(-1)
+
+
+class SpecDecoder:
+    """MTP drafter + verifier bound to a :class:`ModelRunner`."""
+
+    def __init__(self, runner, k: int):
+        from ..models.mtp import MTPHead
+
+        self.runner = runner
+        self.k = k
+        cfg = runner.cfg
+        if runner.model.kda_layer_ids():
+            raise NotImplementedError("speculative decoding of KDA layers needs per-token recurrent-state "
+                                      "recovery, which this engine does not implement; use an all-MLA model")
+        self.mtp = MTPHead(cfg.model, runner.model, runner.device, cfg.seed,
+                           getattr(runner.model, "init_mode", "local"))
+        rows = runner.num_blocks * 64
+        runner.mla_caches[self.mtp.layer_id] = (
+            torch.zeros(rows, 576, dtype=torch.bfloat16, device=runner.device),
+            torch.zeros(rows, 128, dtype=torch.uint8, device=runner.device),
+            torch.ones(rows, dtype=torch.float32, device=runner.device))
+        self.step_no = 0
+        # draft distributions of sampled requests: rid -> (tensor [k, A, V_local], row a)
+        self.q_store: dict[str, tuple[torch.Tensor, int]] = {}
+        self.stats = {"proposed": 0, "accepted": 0, "steps": 0}
+
+    # ------------------------------------------------------------------ verification
+    def verify(self, out, logits: torch.Tensor, rows_of: dict[str, list[int]]) -> dict[str, list[int]]:
+        """logits: this rank's shard [R, V_local] of the sampled rows; rows_of: request -> its rows, in order."""
+        r = self.runner
+        off = r.model.vocab_offset
+        dev = logits.device
+        self.step_no += 1
+        greedy = _sample(logits, None, 0, None, off)
+        # sampled requests: probabilities of the drafts and the residual / bonus draws
+        trows, ttemps, tdraft, tq = [], [], [], []
+        for s in out.reqs:
+            req = s.req
+            if not s.sample or req.params.temperature <= 0:
+                continue
+            rows = rows_of[req.request_id]
+            qs = self.q_store.get(req.request_id)
+            for j, row in enumerate(rows):
+                trows.append(row)
+                ttemps.append(req.params.temperature)
+                d = req.draft_token_ids[j] if j < s.num_draft else -1
+                tdraft.append(d)
+                tq.append((qs, j) if (d >= 0 and qs is not None) else None)
+        host_stats = None
+        final = None
+        if trows:
+            sel = torch.tensor(trows, device=dev)
+            temps = torch.tensor(ttemps, dtype=torch.float32, device=dev)
+            e, ssum = tempered_probs(logits.index_select(0, sel), temps)
+            Vl = e.shape[1]
+            q = torch.zeros_like(e)
+            for i, t in enumerate(tq):
+                if t is not None:
+                    qs, j = t
+                    q[i] = qs[0][j, qs[1]]
+            d = torch.tensor(tdraft, dtype=torch.int64, device=dev) - off
+            own = (d >= 0) & (d < Vl)
+            dl = d.clamp(0, Vl - 1)[:, None]
+            pd = torch.where(own, e.gather(1, dl)[:, 0], 0.0)
+            qd = torch.where(own, q.gather(1, dl)[:, 0], 0.0)
+            st = _all_reduce(torch.stack([ssum, pd, qd], dim=1).contiguous())
+            p = e / st[:, :1]
+            resid = torch.clamp(p - q, min=0.0)  # bonus rows: q = 0 -> p
+            ones = torch.ones(len(trows), dtype=torch.float32, device=dev)
+            final = _sample(torch.log(resid), ones, r.cfg.seed ^ _SEED_VERIFY, r.step_counter, off)
+            host_stats = st
+        g_host = greedy.cpu().tolist()
+        f_host = final.cpu().tolist() if final is not None else []
+        if host_stats is not None:
+            hs = host_stats.cpu().numpy()
+            pd_h = hs[:, 1] / np.maximum(hs[:, 0], 1e-30)
+            qd_h = hs[:, 2]
+            gen = torch.Generator().manual_seed((r.cfg.seed * 1000003 + self.step_no) & 0x7FFFFFFFFFFF)
+            u = torch.rand(len(trows), generator=gen, dtype=torch.float64).numpy()
+        res = {}
+        ti = 0
+        for s in out.reqs:
+            if not s.sample:
+                continue
+            req = s.req
+            rows = rows_of[req.request_id]
+            drafts = req.draft_token_ids[: s.num_draft]
+            acc = []
+            if req.params.temperature <= 0:
+                for j, dtok in enumerate(drafts):
+                    acc.append(g_host[rows[j]])
+                    if acc[-1] != dtok:
+                        break
+                else:
+                    acc.append(g_host[rows[len(drafts)]])
+            else:
+                base = ti
+                ti += len(rows)
+                for j, dtok in enumerate(drafts):
+                    qd = qd_h[base + j] if tq[base + j] is not None else 1.0
+                    if qd > 0 and u[base + j] < min(1.0, pd_h[base + j] / qd):
+                        acc.append(dtok)
+                        continue
+                    acc.append(f_host[base + j])
+                    break
+                else:
+                    acc.append(f_host[base + len(drafts)])
+            self.stats["proposed"] += len(drafts)
+            self.stats["accepted"] += sum(1 for a, b in zip(acc, drafts) if a == b)
+            res[req.request_id] = acc
+        self.stats["steps"] += 1
+        return res
+
+    # ------------------------------------------------------------------ proposal
+    def propose(self, out, hidden: torch.Tensor, accepted: dict[str, list[int]]) -> None:
+        """Set ``draft_token_ids`` of the step's unfinished requests (call after the scheduler update)."""
+        r = self.runner
+        dev = r.device
+        for s in out.reqs:
+            self.q_store.pop(s.req.request_id, None)
+        ids, pos, hrows, tseq, reqs = [], [], [], [], []
+        last = []
+        t = 0
+        for s in out.reqs:
+            req = s.req
+            n_rows = s.num_new
+            base = t
+            t += n_rows
+            if s.num_draft:
+                toks = accepted.get(req.request_id, [])
+            else:
+                known = req.all_token_ids
+                toks = known[s.start + 1: s.start + s.num_new + 1]
+            m = min(len(toks), n_rows)
+            if m == 0:
+                continue
+            reqs.append(req)
+            for j in range(m):
+                ids.append(toks[j])
+                pos.append(s.start + j)
+                hrows.append(base + j)
+                tseq.append(len(reqs) - 1)
+            last.append(len(ids) - 1)
+        if not ids:
+            return
+        ctx = self._ctx(pos, tseq, reqs)
+        hs = hidden.index_select(0, torch.tensor(hrows, device=dev))
+        x = self.mtp(torch.tensor(ids, device=dev), hs, ctx)
+        # chain over the requests that keep decoding
+        act = [i for i, req in enumerate(reqs)
+               if not req.status.finished and req.num_computed_tokens == req.num_tokens - 1]
+        if not act:
+            return
+        areqs = [reqs[i] for i in act]
+        cur = x.index_select(0, torch.tensor([last[i] for i in act], device=dev))
+        cur_pos = [pos[last[i]] for i in act]
+        A = len(areqs)
+        temps_l = [q.params.temperature for q in areqs]
+        temps = torch.tensor(temps_l, dtype=torch.float32, device=dev) if any(v > 0 for v in temps_l) else None
+        samp = [i for i, v in enumerate(temps_l) if v > 0]
+        qbuf = torch.empty(self.k, len(samp), r.model.vocab_local, dtype=torch.float32, device=dev) if samp else None
+        drafts = []
+        for j in range(self.k):
+            logits = self.mtp.compute_logits(cur)
+            tok = _sample(logits, temps, r.cfg.seed ^ (_SEED_DRAFT + j), r.step_counter, r.model.vocab_offset)
+            if samp:
+                sel = torch.tensor(samp, device=dev)
+                e, ssum = tempered_probs(logits.index_select(0, sel), temps.index_select(0, sel))
+                qbuf[j] = e / ssum[:, None]
+            drafts.append(tok)
+            if j + 1 == self.k:
+                break
+            cur_pos = [p + 1 for p in cur_pos]
+            ctx = self._ctx(cur_pos, list(range(A)), areqs)
+            cur = self.mtp(tok, cur, ctx)
+        dh = torch.stack(drafts, dim=1).cpu().tolist()
+        for a, req in enumerate(areqs):
+            limit = max(0, min(self.k, req.params.max_tokens - len(req.output_token_ids) - 1))
+            req.draft_token_ids = [int(v) for v in dh[a][:limit]]
+        for qi, a in enumerate(samp):
+            self.q_store[areqs[a].request_id] = (qbuf, qi)
+
+    def _ctx(self, pos, tseq, reqs) -> StepContext:
+        r = self.runner
+        p = np.asarray(pos, dtype=np.int64)
+        ts = np.asarray(tseq, dtype=np.int64)
+        S = len(reqs)
+        cap = r.max_blocks_per_seq * 64
+        bt = np.zeros((S, r.max_blocks_per_seq), dtype=np.int32)
+        slots = np.full(len(pos), -1, dtype=np.int64)
+        for i, req in enumerate(reqs):
+            bt[i, : len(req.block_ids)] = req.block_ids
+        for i in range(len(pos)):
+            b = reqs[ts[i]].block_ids
+            if p[i] // 64 < len(b):  # draft positions past the allocated blocks write nothing
+                slots[i] = b[p[i] // 64] * 64 + p[i] % 64
+        cu = np.zeros(S + 1, dtype=np.int32)
+        np.add.at(cu, ts + 1, 1)
+        cu = np.cumsum(cu).astype(np.int32)
+
+        def t(a, dt):
+            return r._to_dev(np.ascontiguousarray(a, dtype=dt))
+
+        return StepContext(positions=t(p, np.int32), num_tokens=len(pos), slot_mapping=t(slots, np.int64),
+                           token_seq=t(ts, np.int32), ctx_lens=t(np.minimum(p + 1, cap), np.int32),
+                           block_table=t(bt, np.int32), max_ctx=int(min(p.max() + 1, cap)),
+                           cu_seqlens=t(cu, np.int32), kda_slots=t(np.zeros(S), np.int32),
+                           has_init=t(np.ones(S), np.int32), mla_caches=r.mla_caches, kda_states=r.kda_states)
+
+    def acceptance_rate(self) -> float:
+        return self.stats["accepted"] / max(1, self.stats["proposed"])

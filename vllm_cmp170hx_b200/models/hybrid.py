@@ -140,6 +140,9 @@ class MLAAttention(nn.Module):
         self.in_splits = [ql, kvl + dr, m.index_head_dim, m.index_n_heads]
         fp8 = m.attn_weight_format == "fp8_block"
         Proj = _fp8_proj if fp8 else Linear
+        if fp8 and tp > 1:
+            # a rank's shard of a block-scaled weight must hold whole 128x128 scale blocks
+            assert self.H * (dn + dr) % 128 == 0 and self.H * dv % 128 == 0, "fp8 shard not 128-aligned"
         self.in_proj = Proj(torch.cat([wi.normal((ql, hid), sd), wi.normal((kvl + dr, hid), sd),
                                        wi.normal((m.index_head_dim, hid), sd),
                                        wi.normal((m.index_n_heads, hid), sd)], dim=0).contiguous())
@@ -357,6 +360,7 @@ class HybridForCausalLM(nn.Module):
         tp, tp_rank = st.tp_size, st.tp_rank
         self.cfg = cfg
         wi = WeightInit(seed, device, init_mode)
+        self.init_mode = init_mode
         self.embed = nn.Parameter(wi.normal((cfg.vocab_size, cfg.hidden_size), 1.0), requires_grad=False)
         self.layers = nn.ModuleList([DecoderLayer(cfg, i, wi, tp, tp_rank) for i in range(cfg.num_layers)])
         self.norm = RMSNorm(wi.ones_plus(cfg.hidden_size, 0.05), cfg.rms_eps)
