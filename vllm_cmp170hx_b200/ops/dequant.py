@@ -11,7 +11,7 @@ import torch
 from .. import _ext
 from ..formats import fp8 as f8
 from ..formats import marlin as fm
-from .moe import pick_tile_rows
+from .moe import dense_items, pick_tile_rows
 
 
 @dataclasses.dataclass
@@ -128,9 +128,7 @@ def fp8_linear(x: torch.Tensor, lin: Fp8Linear) -> torch.Tensor:
     dev = x.device
     tile = 128 if T > 64 else (64 if T > 32 else (32 if T > 16 else 16))
     n_items = (T + tile - 1) // tile
-    items = torch.tensor([[0, i * tile, min(tile, T - i * tile), 0] for i in range(n_items)], dtype=torch.int32,
-                         device=dev)
-    num = torch.tensor([n_items], dtype=torch.int32, device=dev)
+    items, num = dense_items(T, tile, dev)
     xh = torch.empty(T, K, dtype=torch.float16, device=dev)
     ops.gather_rows(x2 if x2.stride(-1) == 1 else x2.contiguous(), None, xh, T)
     out = torch.empty(T, N, dtype=torch.bfloat16, device=dev)

@@ -138,6 +138,27 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
     return out
 
 
+_DENSE_ITEMS: dict = {}
+
+
+def dense_items(T: int, tile: int, dev) -> tuple[torch.Tensor, torch.Tensor]:
+    """Work items {expert 0, row0, rows, 0} [n, 4] int32 and their count [1] covering T rows of a dense
+    (one-matrix) GEMM.  Built with device ops so CUDA-graph capture can record them; cached per shape
+    outside capture (a tensor made during capture holds its values only after a replay)."""
+    key = (T, tile, str(dev))
+    hit = _DENSE_ITEMS.get(key)
+    if hit is not None:
+        return hit
+    n = (T + tile - 1) // tile
+    r = torch.arange(n, dtype=torch.int32, device=dev) * tile
+    z = torch.zeros_like(r)
+    items = torch.stack([z, r, (T - r).clamp(max=tile), z], dim=1).contiguous()
+    num = torch.full((1,), n, dtype=torch.int32, device=dev)
+    if not (torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()):
+        _DENSE_ITEMS[key] = (items, num)
+    return items, num
+
+
 def exl3_linear(x: torch.Tensor, m: fx.Exl3Matrix, out_dtype=torch.bfloat16) -> torch.Tensor:
     """Dense EXL3 linear (one matrix): the MoE kernels with a single expert."""
     if not x.is_cuda:
@@ -148,9 +169,7 @@ def exl3_linear(x: torch.Tensor, m: fx.Exl3Matrix, out_dtype=torch.bfloat16) -> 
     K, N = m.padded_in, m.padded_out
     tile = 128 if T > 64 else (64 if T > 32 else (32 if T > 16 else 16))
     n_items = (T + tile - 1) // tile
-    items = torch.tensor([[0, i * tile, min(tile, T - i * tile), 0] for i in range(n_items)], dtype=torch.int32,
-                         device=dev) if T else torch.empty(0, 4, dtype=torch.int32, device=dev)
-    num = torch.tensor([n_items], dtype=torch.int32, device=dev)
+    items, num = dense_items(T, tile, dev)
     xr = torch.empty(max(T, 1), K, dtype=torch.float16, device=dev)
     ops.exl3_input_rotate(x, m.in_features, None, None, 1, m.suh, None, xr, None, T)
     y = torch.empty(T, N, dtype=torch.float32 if out_dtype == torch.float32 else torch.bfloat16, device=dev)
