@@ -1,0 +1,210 @@
+"""Kernel micro-benchmarks at the shapes of the BASELINE configs.
+
+    python -m vllm_cmp170hx_b200.bench.kernels <op> [--tokens T] [--iters N] ...
+
+ops:
+  gemm        bf16 GEMM y = x W^T (ours vs cuBLAS), --m --n --k
+  exl3_moe    config-3 routed experts (256 x [2304 -> 1024 -> 2304], top-8, EXL3 4-bit), --tokens
+  marlin_moe  config-4 routed experts (256 x [4096 -> 1536 -> 4096], top-8, Marlin int4 g128), --tokens
+  fp8_linear  fp8 128x128 block-scaled linear, --m --n --k
+  mla_decode  config-2 sparse-MLA decode layer (128 heads, top-2048 of --ctx positions), --tokens = batch
+  kda_decode  config-3 KDA layer decode step (32 heads x 128), --tokens = sequences
+
+Each op prints one JSON line: mean device time per call over --iters calls
+timed with CUDA events after warm-up (inputs larger than L2 where the op
+streams weights), the algorithmic bytes / FLOPs and their fraction of the
+measured machine peaks (HBM copy bandwidth and cuBLAS bf16 throughput read
+from MEASURED_PEAKS.json at the repository root when present).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from .. import _ext, ops
+from ..config import config2_layer, config3, config4
+from ..models.hybrid import KDAAttention, MLAAttention, StepContext
+from ..models.layers import WeightInit
+from ..parallel import state as pstate
+
+_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def _peaks() -> dict:
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d.get("hbm_gbs", _PEAKS["hbm_gbs"]), "bf16_tflops": d.get("bf16_tflops", _PEAKS["bf16_tflops"]),
+                "source": "measured"}
+    return dict(_PEAKS, source="fallback")
+
+
+def time_us(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / iters
+
+
+def _report(op: str, us: float, nbytes: float = 0.0, flops: float = 0.0, **extra) -> dict:
+    pk = _peaks()
+    out = {"op": op, "us": round(us, 2)}
+    if nbytes:
+        gbs = nbytes / us / 1e3
+        out.update(bytes=int(nbytes), gbs=round(gbs, 1), frac_hbm=round(gbs / pk["hbm_gbs"], 3))
+    if flops:
+        tf = flops / us / 1e6
+        out.update(flops=int(flops), tflops=round(tf, 1), frac_bf16=round(tf / pk["bf16_tflops"], 3))
+    out["peaks"] = pk["source"]
+    out.update(extra)
+    print(json.dumps(out), flush=True)
+    return out
+
+
+def bench_gemm(a):
+    x = torch.randn(a.m, a.k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(a.n, a.k, device="cuda", dtype=torch.bfloat16)
+    nbytes = 2 * (a.m * a.k + a.n * a.k + a.m * a.n)
+    ours = time_us(lambda: ops.gemm(x, w), a.iters)
+    ref = time_us(lambda: torch.nn.functional.linear(x, w), a.iters)
+    return _report("gemm", ours, nbytes, 2.0 * a.m * a.n * a.k, m=a.m, n=a.n, k=a.k, cublas_us=round(ref, 2))
+
+
+def _route(T, E, k, dev):
+    from ..ops import moe as moe_ops
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    return moe_ops.topk(torch.randn(T, E, device=dev, generator=g), k, 0)
+
+
+def bench_exl3_moe(a):
+    from ..models.hybrid import random_exl3_experts
+    from ..ops import moe as moe_ops
+
+    c = config3()
+    E, H, I, k = c.moe.num_experts, c.hidden_size, c.moe.intermediate, c.moe.top_k
+    ex = random_exl3_experts(E, H, I, c.moe.exl3_bits_x2, c.moe.exl3_codebook, WeightInit(0, "cuda", "local"), 1, 0,
+                             0.0)
+    x = torch.randn(a.tokens, H, device="cuda", dtype=torch.bfloat16)
+    ids, w = _route(a.tokens, E, k, "cuda")
+    used = int(torch.unique(ids).numel())
+    nbytes = used * 3 * H * I * c.moe.exl3_bits_x2 / 16  # trellis bits of the touched experts
+    us = time_us(lambda: moe_ops.exl3_moe(x, ids, w, ex), a.iters)
+    return _report("exl3_moe", us, nbytes, 2.0 * a.tokens * k * 3 * H * I, tokens=a.tokens, experts_touched=used)
+
+
+def bench_marlin_moe(a):
+    from ..models.marlin_experts import random_marlin_experts
+    from ..ops.dequant import marlin_moe
+
+    c = config4()
+    E, H, I, k = c.moe.num_experts, c.hidden_size, c.moe.intermediate, c.moe.top_k
+    ex = random_marlin_experts(E, H, I, WeightInit(0, "cuda", "local"), 1, 0)
+    x = torch.randn(a.tokens, H, device="cuda", dtype=torch.bfloat16)
+    ids, w = _route(a.tokens, E, k, "cuda")
+    used = int(torch.unique(ids).numel())
+    nbytes = used * 3 * H * I * (0.5 + 2 / 128)  # int4 codes + bf16 group scales
+    us = time_us(lambda: marlin_moe(x, ids, w, ex), a.iters)
+    return _report("marlin_moe", us, nbytes, 2.0 * a.tokens * k * 3 * H * I, tokens=a.tokens, experts_touched=used)
+
+
+def bench_fp8_linear(a):
+    from ..formats import fp8 as f8
+    from ..ops.dequant import Fp8Linear, fp8_linear
+
+    w = torch.randn(a.n, a.k) * a.k ** -0.5
+    q, s = f8.quantize(w)
+    lin = Fp8Linear(q.cuda(), s.cuda())
+    x = torch.randn(a.m, a.k, device="cuda", dtype=torch.bfloat16)
+    us = time_us(lambda: fp8_linear(x, lin), a.iters)
+    return _report("fp8_linear", us, a.n * a.k + 2 * (a.m * a.k + a.m * a.n), 2.0 * a.m * a.n * a.k, m=a.m, n=a.n,
+                   k=a.k)
+
+
+def _paged_ctx(B, ctx, dev, mla_layer=None, kda_layer=None, kda_shapes=None):
+    nb = (ctx + 63) // 64
+    bt = torch.arange(B * nb, dtype=torch.int32, device=dev).view(B, nb) + 1
+    pos = torch.full((B,), ctx - 1, dtype=torch.int32, device=dev)
+    slots = (bt[:, -1].long() * 64 + (ctx - 1) % 64)
+    caches, states = {}, {}
+    rows = (B * nb + 1) * 64
+    if mla_layer is not None:
+        g = torch.Generator(device=dev).manual_seed(1)
+        lat = torch.randn(rows, 576, device=dev, dtype=torch.bfloat16, generator=g)
+        idx_k = torch.randint(0, 120, (rows, 128), dtype=torch.uint8, device=dev, generator=g)  # finite e4m3 codes
+        idx_s = torch.rand(rows, device=dev, generator=g) * 0.1 + 0.01
+        caches[0] = (lat, idx_k, idx_s)
+    if kda_shapes is not None:
+        rec_shape, conv_shape = kda_shapes
+        states[0] = (torch.zeros(B + 1, *rec_shape, device=dev), torch.zeros(B + 1, *conv_shape, device=dev,
+                                                                              dtype=torch.bfloat16))
+    return StepContext(positions=pos, num_tokens=B, slot_mapping=slots, token_seq=torch.arange(B, dtype=torch.int32,
+                                                                                                 device=dev),
+                       ctx_lens=pos + 1, block_table=bt, max_ctx=ctx,
+                       cu_seqlens=torch.arange(B + 1, dtype=torch.int32, device=dev),
+                       kda_slots=torch.arange(1, B + 1, dtype=torch.int32, device=dev),
+                       has_init=torch.ones(B, dtype=torch.int32, device=dev), mla_caches=caches, kda_states=states,
+                       scores_buf=torch.empty(B, ctx, device=dev))
+
+
+def bench_mla_decode(a):
+    c = config2_layer()
+    layer = MLAAttention(c, WeightInit(0, "cuda", "local"), 1, 0)
+    ctx = _paged_ctx(a.tokens, a.ctx, "cuda", mla_layer=layer)
+    x = torch.randn(a.tokens, c.hidden_size, device="cuda", dtype=torch.bfloat16)
+    topk = c.mla.index_topk
+    # bytes: selected latent rows + indexer keys over the context + the layer's weights
+    wbytes = sum(p.numel() * p.element_size() for p in layer.parameters())
+    nbytes = a.tokens * (min(topk, a.ctx) * 576 * 2 + a.ctx * (128 + 4)) + wbytes
+    with torch.inference_mode():
+        us = time_us(lambda: layer(x, ctx, 0), a.iters)
+    return _report("mla_decode", us, nbytes, tokens=a.tokens, ctx=a.ctx, topk=topk, heads=c.mla.num_heads)
+
+
+def bench_kda_decode(a):
+    c = config3()
+    layer = KDAAttention(c, WeightInit(0, "cuda", "local"), 1, 0)
+    H, D = c.kda.num_heads, c.kda.head_dim
+    shapes = ((H, D, D), (3 * H * D, 3))
+    ctx = _paged_ctx(a.tokens, 64, "cuda", kda_shapes=shapes)
+    x = torch.randn(a.tokens, c.hidden_size, device="cuda", dtype=torch.bfloat16)
+    wbytes = sum(p.numel() * p.element_size() for p in layer.parameters())
+    nbytes = a.tokens * H * D * D * 4 * 2 + wbytes  # fp32 state read + written, weights
+    with torch.inference_mode():
+        us = time_us(lambda: layer(x, ctx, 0), a.iters)
+    return _report("kda_decode", us, nbytes, seqs=a.tokens, heads=H)
+
+
+OPS = {"gemm": bench_gemm, "exl3_moe": bench_exl3_moe, "marlin_moe": bench_marlin_moe, "fp8_linear": bench_fp8_linear,
+       "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("op", choices=sorted(OPS))
+    ap.add_argument("--tokens", type=int, default=128)
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--m", type=int, default=128)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args(argv)
+    pstate.set_state(pstate.ParallelState())
+    OPS[a.op](a)
+    _ext.check_status(torch.device("cuda"))
+
+
+if __name__ == "__main__":
+    main()
