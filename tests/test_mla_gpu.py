@@ -106,12 +106,16 @@ def test_indexer_and_topk():
         assert (out[t, len(p):] == -1).all()
 
 
-@pytest.mark.parametrize("nh,count,splits", [(128, 2048, 1), (32, 2048, 1), (16, 100, 1), (64, 1000, 3), (128, 64, 2)])
-def test_sparse_attention(nh, count, splits):
+@pytest.mark.parametrize("nh,count,splits,qscale", [(128, 2048, 1, 0.3), (32, 2048, 1, 0.3), (16, 100, 1, 0.3),
+                                                    (64, 1000, 3, 0.3), (128, 64, 2, 0.3), (8, 257, 1, 0.3),
+                                                    (128, 2048, 8, 0.3), (32, 1500, 1, 3.0), (160, 700, 2, 0.3)])
+def test_sparse_attention(nh, count, splits, qscale):
+    """qscale 3.0 gives logit ranges that force rescaling across the 256-position blocks;
+    nh 160 spans two head groups; count 257 ends one position into a second block."""
     torch.manual_seed(nh + count)
     T, topk, nslots = 3, 2048, 5000
     cache = torch.randn(nslots, 576, dtype=torch.bfloat16, device="cuda")
-    q = (torch.randn(T, nh, 576, device="cuda") * 0.3).to(torch.bfloat16)
+    q = (torch.randn(T, nh, 576, device="cuda") * qscale).to(torch.bfloat16)
     idx = torch.full((T, topk), -1, dtype=torch.int32, device="cuda")
     counts = torch.tensor([count, max(1, count // 2), count], dtype=torch.int32, device="cuda")
     for t in range(T):

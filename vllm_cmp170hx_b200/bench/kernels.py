@@ -45,9 +45,20 @@ def _peaks() -> dict:
     return dict(_PEAKS, source="fallback")
 
 
+_PROFILE = False
+
+
 def time_us(fn, iters: int, warmup: int = 3) -> float:
     for _ in range(warmup):
         fn()
+    if _PROFILE:  # per-kernel breakdown of one call (guidance only; times under the profiler are not reported)
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=25, max_name_column_width=70))
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
@@ -200,7 +211,10 @@ def main(argv=None):
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--profile", action="store_true", help="print a per-kernel table of one call (torch profiler)")
     a = ap.parse_args(argv)
+    global _PROFILE
+    _PROFILE = a.profile
     pstate.set_state(pstate.ParallelState())
     OPS[a.op](a)
     _ext.check_status(torch.device("cuda"))

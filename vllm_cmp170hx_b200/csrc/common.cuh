@@ -192,6 +192,18 @@ B200_DEVICE void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A is read from tensor
+// memory, row m in lane m, K-major with two 16-bit elements per 32-bit column
+// (a K = 16 step spans 8 columns).
+B200_DEVICE void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
 // kind::f8f6f4 (e4m3 / e5m2 operands, fp32 accumulate), K = 32 per instruction.
 B200_DEVICE void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
   asm volatile(

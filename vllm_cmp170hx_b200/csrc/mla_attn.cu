@@ -15,19 +15,8 @@
 // into one of two TMEM buffers; the epilogue thread of each position reduces
 // its TMEM row: sum_h w_h relu(d_h) * k_scale.
 //
-// Attention (one CTA per (token, head group of 128, latent half, split)):
-//   * Q (heads x 576) streams in 64-dim chunks through TMA (128-byte swizzle);
-//   * 4 gather warps copy the 64 selected latent rows of a tile
-//     (64 x 1152 B) into shared memory as 8x16-byte core matrices, a layout
-//     that is at once the K-major B operand of S = Q K^T (N = positions) and
-//     the MN-major B operand of O += P V (N = latent dims);
-//   * S (heads x 64 positions, fp32) double-buffers in TMEM; the softmax warps
-//     (one head row per thread, no cross-thread reductions) keep a running
-//     max with lazy rescaling of the TMEM accumulator, write P (bf16) into
-//     shared memory as the A operand of P V;
-//   * O (heads x 256 latent dims of this CTA's half) accumulates in TMEM.
-//   The 576-dim QK^T is recomputed by the two latent halves: TMEM (512 fp32
-//   columns per lane) cannot hold the full 128 x 512 O next to S.
+// Attention: see the block-form kernel below (blocks of 128 positions, K chunks
+// retained as V, P in tensor memory); splits are merged by merge_kernel.
 #include "common.cuh"
 #include "launch.h"
 #include "tma_host.h"
@@ -214,375 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 }  // namespace idx
 
-// ============================================================================= sparse attention
+// ============================================================================= split merge
 namespace attn {
-constexpr int kThreads = 320;           // 10 warps
-constexpr int PT = 64;                  // positions per tile
-constexpr int DIM = 576;                // latent 512 + rope 64
-constexpr int KV_BYTES = PT * DIM * 2;  // 73728
-constexpr int Q_BYTES = 128 * 64 * 2;   // one 64-dim chunk of 128 head rows
-constexpr int QST = 3;
-constexpr int P_BYTES = 128 * PT * 2;   // 16384
-constexpr int SMEM = 1024 + 2 * KV_BYTES + QST * Q_BYTES + 2 * P_BYTES + 256;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleThreshold = 8.f;  // log2 units
-
-struct Params {
-  const int* indices;  // [T, topk] cache rows (-1 = none)
-  const int* counts;   // [T]
-  int topk;
-  int nh;              // heads of the token
-  const __nv_bfloat16* cache;  // [slots, 576]
-  float sm_scale_log2;
-  int splits;
-  int q_box_rows;      // rows of Q loaded per chunk (real heads of the group, <= 128)
-  __nv_bfloat16* out;  // [T, nh, 512] (splits == 1)
-  float* part_o;       // [splits, T, nh, 512] (splits > 1)
-  float* part_ml;      // [splits, T, nh, 2] (max, sum) log2 domain
-  float* lse;          // [T, nh] natural log (splits == 1, optional)
-  int T;
-  uint32_t* status;
-};
-
-// core-matrix layout of a KV tile: (dim group di, pos group pi) at (di*8 + pi)*128, row r at +16r
-B200_DEVICE uint32_t kv_off(int pos, int chunk) { return (uint32_t)((chunk * 8 + (pos >> 3)) * 128 + (pos & 7) * 16); }
-
-__global__ void __launch_bounds__(kThreads, 1)
-    sparse_attn_kernel(const __grid_constant__ CUtensorMap tma_q, Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* skv = smem;                          // [2][KV_BYTES]
-  uint8_t* sq = smem + 2 * KV_BYTES;            // [QST][Q_BYTES]
-  uint8_t* sp = sq + QST * Q_BYTES;             // [2][P_BYTES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * P_BYTES);
-  uint64_t* kv_full = bars;        // 2, count 4 (gather warps)
-  uint64_t* kv_empty = bars + 2;   // 2, MMA commit
-  uint64_t* q_full = bars + 4;     // QST (<= 4)
-  uint64_t* q_empty = bars + 8;    // QST
-  uint64_t* s_full = bars + 12;    // 2
-  uint64_t* p_full = bars + 14;    // 2, count 128
-  uint64_t* p_empty = bars + 16;   // 2
-  uint64_t* o_full = bars + 18;
-  uint64_t* drain = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int t = blockIdx.x;
-  const int hg = blockIdx.y;        // head group of 128
-  const int half = blockIdx.z % 2;  // latent half
-  const int split = blockIdx.z / 2;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int count = p.counts[t];
-  const int ntiles_all = (count + PT - 1) / PT;
-  const int per = (ntiles_all + p.splits - 1) / p.splits;
-  const int tile0 = split * per;
-  const int tile1 = min(ntiles_all, tile0 + per);
-  const int nt = max(0, tile1 - tile0);
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < QST; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 4);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&p_empty[i], 1);
-    }
-    mbar_init(o_full, 1);
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tS = tmem_base;        // 2 x 64 columns
-  const uint32_t tO = tmem_base + 256;  // 256 columns
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ Q chunk producer
-    if (elect_one()) {
-      int qs = 0;
-      uint32_t qph = 0, issued = 0;
-      bool ok = true;
-      const int row0 = t * p.nh + hg * 128;
-      // only this group's real head rows are loaded; the MMA's other rows
-      // read stale shared memory and their TMEM rows are never used
-      const uint32_t q_bytes = (uint32_t)p.q_box_rows * 128;
-      for (int i = 0; i < nt && ok; ++i) {
-        for (int c = 0; c < DIM / 64; ++c) {
-          if (!mbar_wait_or_abort(&q_empty[qs], qph ^ 1, p.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&q_full[qs], q_bytes);
-          tma_load_2d(sq + qs * Q_BYTES, &tma_q, &q_full[qs], c * 64, row0);
-          ++issued;
-          if (++qs == QST) {
-            qs = 0;
-            qph ^= 1;
-          }
-        }
-      }
-      if (!ok) {
-        *abort_flag = 1;
-        const uint32_t n = issued < (uint32_t)QST ? issued : (uint32_t)QST;
-        for (uint32_t j = 0; j < n; ++j) {
-          const uint32_t k = issued - 1 - j;
-          mbar_wait(&q_full[k % QST], (k / QST) & 1, nullptr);
-        }
-      }
-    }
-  } else if (warp >= 1 && warp <= 4) {
-    // ------------------------------------------------------------------ KV gather (128 threads)
-    const int gw = warp - 1;
-    const int* idx = p.indices + (int64_t)t * p.topk;
-    for (int i = 0; i < nt; ++i) {
-      const int b = i & 1;
-      if (!mbar_wait_or_abort(&kv_empty[b], ((i >> 1) & 1) ^ 1, p.status, abort_flag)) break;
-      uint8_t* dst = skv + b * KV_BYTES;
-      const int pbase = (tile0 + i) * PT;
-      // warp iteration: 8 rows x 4 chunks; 8 row groups x 18 chunk groups =
-      // 144 iterations over 4 warps.  Every copy is issued before any wait
-      // (cp.async, 16 B, zero-filled for positions without a row).
-      for (int it = gw; it < 144; it += 4) {
-        const int rg = it / 18, cgp = it % 18;
-        const int pos = rg * 8 + (lane & 7);
-        const int chunk = cgp * 4 + (lane >> 3);
-        const int gp = pbase + pos;
-        const int slot = gp < count ? idx[gp] : -1;
-        const void* src = slot >= 0 ? reinterpret_cast<const void*>(reinterpret_cast<const uint4*>(p.cache +
-                                                                     (int64_t)slot * DIM) + chunk)
-                                    : reinterpret_cast<const void*>(p.cache);
-        const uint32_t sz = slot >= 0 ? 16u : 0u;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + kv_off(pos, chunk))),
-                     "l"(src), "r"(sz)
-                     : "memory");
-      }
-      asm volatile("cp.async.wait_all;" ::: "memory");
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&kv_full[b]);
-    }
-  } else if (warp == 5) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      constexpr uint32_t idesc_qk = make_idesc_f16(128, PT, 1);
-      constexpr uint32_t idesc_pv = make_idesc_f16(128, 256, 1, false, true);
-      int qs = 0;
-      uint32_t qph = 0;
-      bool ok = true;
-      auto issue_qk = [&](int i) -> bool {
-        const int b = i & 1;
-        if (!mbar_wait_or_abort(&kv_full[b], (i >> 1) & 1, p.status, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t kv_base = smem_u32(skv + b * KV_BYTES);
-        for (int c = 0; c < DIM / 64; ++c) {
-          if (!mbar_wait_or_abort(&q_full[qs], qph, p.status, abort_flag)) return false;
-          tc_fence_after();
-          const uint64_t dq = desc_kmajor_sw128(sq + qs * Q_BYTES);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int di0 = c * 8 + 2 * k;  // 16 dims = 2 dim groups
-            const uint64_t dk = make_smem_desc(kv_base + di0 * 8 * 128, 8 * 128 /*LBO: next dim group*/,
-                                               128 /*SBO: next pos group*/, kSwizzleNone);
-            umma_f16(tS + b * 64, dq + 2 * k, dk, idesc_qk, (c > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&q_empty[qs]);
-          if (++qs == QST) {
-            qs = 0;
-            qph ^= 1;
-          }
-        }
-        umma_commit(&s_full[b]);
-        return true;
-      };
-      if (nt > 0) ok = issue_qk(0);
-      for (int i = 0; i < nt && ok; ++i) {
-        const int b = i & 1;
-        if (i + 1 < nt) {
-          ok = issue_qk(i + 1);
-          if (!ok) break;
-        }
-        if (!mbar_wait_or_abort(&p_full[b], (i >> 1) & 1, p.status, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t p_base = smem_u32(sp + b * P_BYTES);
-        const uint32_t kv_base = smem_u32(skv + b * KV_BYTES);
-#pragma unroll
-        for (int k = 0; k < PT / 16; ++k) {
-          const uint64_t dp = make_smem_desc(p_base + 2 * k * 2048, 2048, 128, kSwizzleNone);
-          // V (MN-major): latent dims of this half = dim groups [32*half, 32*half + 32); K = positions 16k..
-          const uint64_t dv = make_smem_desc(kv_base + ((half * 32) * 8 + 2 * k) * 128, 128 /*LBO: next pos group*/,
-                                             8 * 128 /*SBO: next dim group*/, kSwizzleNone);
-          umma_f16(tO, dp, dv, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(&kv_empty[b]);
-        umma_commit(&p_empty[b]);
-      }
-      if (ok) umma_commit(o_full);
-      if (!ok) *abort_flag = 1;
-      umma_commit(drain);
-      mbar_wait(drain, 0, nullptr);
-    }
-  } else {
-    // ------------------------------------------------------------------ softmax + epilogue (warps 6..9)
-    const int q = warp & 3;  // TMEM lane quarter: head row = 32q + lane
-    const int h = q * 32 + lane;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int i = 0; i < nt; ++i) {
-      const int b = i & 1;
-      if (!mbar_wait_or_abort(&s_full[b], (i >> 1) & 1, p.status, abort_flag)) ok = false;
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float s[PT];
-      const uint32_t ta = tS + ((uint32_t)(q * 32) << 16) + b * 64;
-#pragma unroll
-      for (int c = 0; c < PT; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(ta + c, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) s[c + j] = __uint_as_float(r[j]) * p.sm_scale_log2;
-      }
-      const int pbase = (tile0 + i) * PT;
-      float mt = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < PT; ++j) {
-        if (pbase + j >= count) s[j] = -INFINITY;
-        mt = fmaxf(mt, s[j]);
-      }
-      // Lazy rescale: a row moves its reference max only when the tile's max
-      // exceeds it by more than 2^8.  TMEM loads/stores are warp-collective,
-      // so the warp rescales together when any of its rows needs it (factor 1
-      // for the others).
-      const bool need = (mt > m_run + kRescaleThreshold) || (m_run == -INFINITY);
-      const float m_new = need ? fmaxf(mt, m_run) : m_run;
-      const bool need_o = need && i > 0 && m_run != -INFINITY;
-      if (__any_sync(0xffffffffu, need_o)) {
-        // O must hold every earlier PV before it is rescaled
-        const int pb = (i - 1) & 1;
-        if (!mbar_wait_or_abort(&p_empty[pb], ((i - 1) >> 1) & 1, p.status, abort_flag)) ok = false;
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float f = need_o ? exp2f(m_run - m_new) : 1.f;
-        const uint32_t to = tO + ((uint32_t)(q * 32) << 16);
-        for (int c = 0; c < 256; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(to + c, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
-          tmem_st16(to + c, r);
-        }
-        tmem_wait_st();
-        l_run *= f;
-      }
-      m_run = m_new;
-      // P buffer b is free once PV(i - 2) completed
-      if (i >= 2 && !mbar_wait_or_abort(&p_empty[b], ((i - 2) >> 1) & 1, p.status, abort_flag)) {
-        ok = false;
-        break;
-      }
-      uint8_t* pb = sp + b * P_BYTES;
-#pragma unroll
-      for (int kg = 0; kg < PT / 8; ++kg) {
-        float e[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          e[j] = m_run == -INFINITY ? 0.f : exp2f(s[kg * 8 + j] - m_run);
-          l_run += e[j];
-        }
-        uint4 v;
-        v.x = pack_bf16x2(e[0], e[1]);
-        v.y = pack_bf16x2(e[2], e[3]);
-        v.z = pack_bf16x2(e[4], e[5]);
-        v.w = pack_bf16x2(e[6], e[7]);
-        // A operand (heads x positions, K-major core matrices): (kg, head group) at kg*2048 + (h/8)*128 + (h%8)*16
-        *reinterpret_cast<uint4*>(pb + kg * 2048 + (h >> 3) * 128 + (h & 7) * 16) = v;
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[b]);
-    }
-    // ---------------------------------------------------------------- epilogue
-    const int head = hg * 128 + h;
-    bool o_ok = ok && nt > 0;
-    if (o_ok) o_ok = mbar_wait_or_abort(o_full, 0, p.status, abort_flag);
-    if (__all_sync(0xffffffffu, o_ok)) {
-      tc_fence_after();
-      const uint32_t to = tO + ((uint32_t)(q * 32) << 16);
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      for (int c = 0; c < 256; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(to + c, r);
-        tmem_wait_ld();
-        if (head < p.nh) {
-          const int64_t base = ((int64_t)t * p.nh + head) * 512 + half * 256 + c;
-          if (p.splits == 1) {
-            uint4 v0, v1;
-            v0.x = pack_bf16x2(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
-            v0.y = pack_bf16x2(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
-            v0.z = pack_bf16x2(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
-            v0.w = pack_bf16x2(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
-            v1.x = pack_bf16x2(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
-            v1.y = pack_bf16x2(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
-            v1.z = pack_bf16x2(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
-            v1.w = pack_bf16x2(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
-            reinterpret_cast<uint4*>(p.out + base)[0] = v0;
-            reinterpret_cast<uint4*>(p.out + base)[1] = v1;
-          } else {
-            float* dst = p.part_o + (int64_t)split * p.T * p.nh * 512 + base;
-#pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-          }
-        }
-      }
-    } else if (head < p.nh && nt == 0) {
-      // no positions in this split
-      if (p.splits == 1) {
-        for (int c = 0; c < 256; ++c) p.out[((int64_t)t * p.nh + head) * 512 + half * 256 + c] = __float2bfloat16(0.f);
-      } else {
-        float* dst = p.part_o + (int64_t)split * p.T * p.nh * 512 + ((int64_t)t * p.nh + head) * 512 + half * 256;
-        for (int c = 0; c < 256; ++c) dst[c] = 0.f;
-      }
-    }
-    if (head < p.nh && half == 0) {
-      if (p.splits > 1) {
-        float* ml = p.part_ml + (((int64_t)split * p.T + t) * p.nh + head) * 2;
-        ml[0] = m_run;
-        ml[1] = l_run;
-      } else if (p.lse) {
-        p.lse[(int64_t)t * p.nh + head] = l_run > 0.f ? (m_run + log2f(l_run)) / kLog2e : -INFINITY;
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 5) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
-  }
-}
 
 // merge split partials: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s
 __global__ void merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits, int T,
@@ -607,6 +230,430 @@ __global__ void merge_kernel(const float* __restrict__ part_o, const float* __re
   if (threadIdx.x == 0 && lse) lse[th] = L > 0.f ? (M + log2f(L)) / kLog2e : -INFINITY;
 }
 }  // namespace attn
+
+
+// ============================================================================= sparse attention, block form
+// One CTA per (token, head group of 128, latent half, split); the split's
+// positions are processed in blocks of 128.
+//   QK   S[128 heads x 128 pos] = sum over the 9 dim chunks of Q_c K_c^T.
+//        A K chunk (128 gathered rows x 64 dims) is copied with cp.async
+//        into the 128-byte-swizzled layout: the 8 lanes of a row write one
+//        128-byte line (coalesced, bank-conflict free).  That layout is at
+//        once the K-major B operand of Q K^T (rows = positions) and the
+//        MN-major B operand of P V (64-dim atoms, 8 positions per 1024-byte
+//        row group), so the 4 chunks holding this CTA's latent half are
+//        RETAINED (double-buffered across blocks) and serve as V: no second
+//        gather.  The other 5 chunks stream through a 3-stage ring.  Copies
+//        complete on mbarriers (cp.async.mbarrier.arrive), so up to 11
+//        chunks are in flight per SM.
+//   softmax  one head row per thread: exact max / exp over the block, a lazy
+//        rescale of the O accumulator across blocks; P is converted to bf16
+//        in place in TMEM (over its S columns).
+//   PV   O[128 x 256 latent dims of this half] += P V, A = P from TMEM.
+// The MMA thread interleaves Q K^T of block b with P V of block b - 1, so the
+// softmax of one block overlaps the next block's Q K^T.
+// TMEM columns: S/P 0 [0, 128), S/P 1 [128, 256), O [256, 512).
+namespace attn4 {
+constexpr int kThreads = 320;  // w0 Q TMA, w1-4 gather, w5 MMA, w6-9 softmax + epilogue
+constexpr int BP = 128;        // positions per block
+constexpr int DIM = 576;
+constexpr int NCH = DIM / 64;           // 9 dim chunks
+constexpr int NSTREAM = 5;              // chunks outside this half's latent dims (incl. RoPE)
+constexpr int NRET = NCH - NSTREAM;     // 4 retained chunks = V
+constexpr int CH_BYTES = BP * 128;      // 16 KiB: 128 positions x 64 dims
+constexpr int Q_BYTES = 128 * 128;      // 16 KiB: 128 head rows x 64 dims
+constexpr int NQ = 3, NKS = 3;          // Q ring, streamed-K ring
+constexpr int R_BYTES = NRET * CH_BYTES;  // 64 KiB per retained buffer (x2)
+constexpr int OFF_Q = 0;
+constexpr int OFF_KS = OFF_Q + NQ * Q_BYTES;
+constexpr int OFF_R = OFF_KS + NKS * CH_BYTES;
+constexpr int OFF_BAR = OFF_R + 2 * R_BYTES;
+constexpr int SMEM = 1024 + OFF_BAR + 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.f;
+
+struct Params {
+  const int* indices;
+  const int* counts;
+  int topk;
+  int nh;
+  const __nv_bfloat16* cache;
+  float sm_scale_log2;
+  int splits;
+  int q_box_rows;
+  __nv_bfloat16* out;
+  float* part_o;
+  float* part_ml;
+  float* lse;
+  int T;
+  uint32_t* status;
+};
+
+// byte offset of (row r, 16-byte chunk c) in a 128-byte-swizzled tile of 128-byte rows
+B200_DEVICE uint32_t sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
+
+// dim chunk processed i-th in a block: first the 5 chunks outside this half's latent dims, then
+// this half's 4 (retained as V)
+B200_DEVICE int chunk_at(int i, int half) {
+  if (i >= NSTREAM) return half * 4 + (i - NSTREAM);
+  return half == 0 ? 4 + i : (i < 4 ? i : 8);
+}
+
+B200_DEVICE void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+// arrive on `bar` once all of this thread's earlier cp.async copies have landed (the barrier's
+// expected count includes this arrival)
+B200_DEVICE void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    sparse_attn_block_kernel(const __grid_constant__ CUtensorMap tma_q, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sq = smem + OFF_Q;
+  uint8_t* sks = smem + OFF_KS;
+  uint8_t* sr = smem + OFF_R;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars;         // NQ, TMA
+  uint64_t* q_empty = bars + 3;    // NQ, MMA commit
+  uint64_t* ks_full = bars + 6;    // NKS, 128 gather threads
+  uint64_t* ks_empty = bars + 9;   // NKS, MMA commit
+  uint64_t* r_full = bars + 12;    // [2][NRET], 128 gather threads, one phase per use
+  uint64_t* r_empty = bars + 20;   // 2, MMA commit after P V
+  uint64_t* s_full = bars + 22;    // 2, MMA commit after Q K^T
+  uint64_t* p_full = bars + 24;    // 2, 128 softmax threads
+  uint64_t* pv_done = bars + 26;   // 2, MMA commit after P V
+  uint64_t* o_full = bars + 28;
+  uint64_t* drain = bars + 29;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int t = blockIdx.x;
+  const int hg = blockIdx.y;
+  const int half = blockIdx.z & 1;
+  const int split = blockIdx.z >> 1;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int count = min(p.counts[t], p.topk);
+  const int nblk_all = (count + BP - 1) / BP;
+  const int per = (nblk_all + p.splits - 1) / p.splits;
+  const int blk0 = split * per;
+  const int nb = max(0, min(nblk_all, blk0 + per) - blk0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NQ; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < NKS; ++i) {
+      mbar_init(&ks_full[i], 128);
+      mbar_init(&ks_empty[i], 1);
+    }
+    for (int i = 0; i < 2 * NRET; ++i) mbar_init(&r_full[i], 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&r_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  // Q rows past the group's real heads are never loaded: keep them zero
+  for (int i = threadIdx.x; i < NQ * Q_BYTES / 16; i += kThreads) reinterpret_cast<uint4*>(sq)[i] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tO = tmem_base + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ Q chunks (TMA), in MMA order
+    if (elect_one()) {
+      const int row0 = t * p.nh + hg * 128;
+      const uint32_t q_bytes = (uint32_t)p.q_box_rows * 128;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int b = 0; b < nb && ok; ++b) {
+        for (int i = 0; i < NCH; ++i) {
+          const uint32_t st = issued % NQ, ph = (issued / NQ) & 1;
+          if (!mbar_wait_or_abort(&q_empty[st], ph ^ 1, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&q_full[st], q_bytes);
+          tma_load_2d(sq + st * Q_BYTES, &tma_q, &q_full[st], chunk_at(i, half) * 64, row0);
+          ++issued;
+        }
+      }
+      if (!ok) {  // let the loads in flight land before the CTA exits
+        const uint32_t n = issued < (uint32_t)NQ ? issued : (uint32_t)NQ;
+        for (uint32_t j = 0; j < n; ++j) {
+          const uint32_t k = issued - 1 - j;
+          mbar_wait(&q_full[k % NQ], (k / NQ) & 1, nullptr);
+        }
+      }
+    }
+  } else if (warp >= 1 && warp <= 4) {
+    // ------------------------------------------------------------------ row gathers (128 threads)
+    // A warp instruction copies 4 rows x 128 bytes; warp gw copies the rows r with r % 4 == gw,
+    // and lane l holds the cache row index of block row 4 l + gw.
+    const int gw = warp - 1;
+    const int sub = lane >> 3, ch = lane & 7;
+    const int* idx_g = p.indices + (int64_t)t * p.topk;
+    auto fetch_idx = [&](int b) -> int {
+      const int pos = (blk0 + b) * BP + lane * 4 + gw;
+      return pos < count ? idx_g[pos] : -1;
+    };
+    int cur = nb > 0 ? fetch_idx(0) : -1;
+    uint32_t ns = 0;
+    bool ok = true;
+    for (int b = 0; b < nb && ok; ++b) {
+      const int nxt = b + 1 < nb ? fetch_idx(b + 1) : -1;  // in flight while this block's copies issue
+      const int rb = b & 1;
+      for (int i = 0; i < NCH; ++i) {
+        const int c = chunk_at(i, half);
+        uint32_t dst;
+        uint64_t* bar;
+        if (i < NSTREAM) {
+          const uint32_t st = ns % NKS, ph = (ns / NKS) & 1;
+          // warp-uniform outcome: the copy loop below shuffles across all lanes
+          if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&ks_empty[st], ph ^ 1, p.status, abort_flag))) {
+            ok = false;
+            break;
+          }
+          dst = smem_u32(sks + st * CH_BYTES);
+          bar = &ks_full[st];
+          ++ns;
+        } else {
+          // retained buffer rb was V of block b - 2: wait until its P V has run
+          if (i == NSTREAM && b >= 2 &&
+              !__all_sync(0xffffffffu, mbar_wait_or_abort(&r_empty[rb], ((b >> 1) - 1) & 1, p.status, abort_flag))) {
+            ok = false;
+            break;
+          }
+          dst = smem_u32(sr + rb * R_BYTES + (i - NSTREAM) * CH_BYTES);
+          bar = &r_full[rb * NRET + (i - NSTREAM)];
+        }
+#pragma unroll
+        for (int it = 0; it < BP / 16; ++it) {
+          const int r = it * 16 + sub * 4 + gw;
+          const int slot = __shfl_sync(0xffffffffu, cur, it * 4 + sub);
+          const void* src = slot >= 0 ? reinterpret_cast<const void*>(p.cache + (int64_t)slot * DIM + c * 64 + ch * 8)
+                                      : reinterpret_cast<const void*>(p.cache);
+          cp_async16(dst + sw128(r, ch), src, slot >= 0 ? 16u : 0u);
+        }
+        cp_async_arrive(bar);
+      }
+      cur = nxt;
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = make_idesc_f16(128, BP, 1);
+      constexpr uint32_t idesc_pv = make_idesc_f16(128, 256, 1, false, true);
+      uint32_t nq = 0, nk = 0;
+      bool ok = true;
+      auto qk_block = [&](int b) -> bool {
+        const int sb = b & 1;
+        // S/P buffer sb last held P of block b - 2: its P V must have read it
+        if (b >= 2 && !mbar_wait_or_abort(&pv_done[sb], ((b >> 1) - 1) & 1, p.status, abort_flag)) return false;
+        const uint32_t ts = tmem_base + (uint32_t)sb * BP;
+        for (int i = 0; i < NCH; ++i) {
+          const uint32_t qs = nq % NQ, qph = (nq / NQ) & 1;
+          if (!mbar_wait_or_abort(&q_full[qs], qph, p.status, abort_flag)) return false;
+          uint32_t kbase;
+          uint32_t kst = 0;
+          if (i < NSTREAM) {
+            kst = nk % NKS;
+            if (!mbar_wait_or_abort(&ks_full[kst], (nk / NKS) & 1, p.status, abort_flag)) return false;
+            kbase = smem_u32(sks + kst * CH_BYTES);
+          } else {
+            if (!mbar_wait_or_abort(&r_full[sb * NRET + (i - NSTREAM)], (b >> 1) & 1, p.status, abort_flag))
+              return false;
+            kbase = smem_u32(sr + sb * R_BYTES + (i - NSTREAM) * CH_BYTES);
+          }
+          fence_proxy_async_smem();  // the rows were written by cp.async (generic proxy)
+          tc_fence_after();
+          const uint64_t dq = desc_kmajor_sw128(sq + qs * Q_BYTES);
+          const uint64_t dk = make_smem_desc(kbase, 16, 1024, kSwizzle128B);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_f16(ts, dq + 2 * k, dk + 2 * k, idesc_qk, (i > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&q_empty[qs]);
+          ++nq;
+          if (i < NSTREAM) {
+            umma_commit(&ks_empty[kst]);
+            ++nk;
+          }
+        }
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      auto pv_block = [&](int b) -> bool {
+        const int sb = b & 1;
+        if (!mbar_wait_or_abort(&p_full[sb], (b >> 1) & 1, p.status, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t pa = tmem_base + (uint32_t)sb * BP;  // P: 128 positions = 64 columns of bf16 pairs
+        const uint32_t rbase = smem_u32(sr + sb * R_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BP / 16; ++kk) {
+          // V: 16 positions = two 1024-byte row groups; the next 64 latent dims = the next retained chunk
+          const uint64_t dv = make_smem_desc(rbase + kk * 2048, CH_BYTES /*LBO*/, 1024 /*SBO*/, kSwizzle128B);
+          umma_f16_ts(tO, pa + kk * 8, dv, idesc_pv, (b > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&r_empty[sb]);
+        umma_commit(&pv_done[sb]);
+        return true;
+      };
+      for (int b = 0; b <= nb && ok; ++b) {
+        if (b < nb) ok = qk_block(b);
+        if (ok && b >= 1) ok = pv_block(b - 1);
+      }
+      if (ok && nb > 0) umma_commit(o_full);
+      if (!ok) *abort_flag = 1;
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue (warps 6..9)
+    const int q = warp & 3;
+    const int h = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int b = 0; b < nb; ++b) {
+      const int sb = b & 1;
+      if (!mbar_wait_or_abort(&s_full[sb], (b >> 1) & 1, p.status, abort_flag)) ok = false;
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ts = tmem_base + lane_off + (uint32_t)sb * BP;
+      const int valid = min(BP, count - (blk0 + b) * BP);
+      float mt = -INFINITY;
+      for (int c = 0; c < BP; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(ts + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c + j < valid) mt = fmaxf(mt, __uint_as_float(r[j]) * p.sm_scale_log2);
+      }
+      const bool need = (mt > m_run + kRescaleThreshold) || (m_run == -INFINITY);
+      const float m_new = need ? fmaxf(mt, m_run) : m_run;
+      const bool need_o = need && b > 0 && m_run != -INFINITY;
+      if (__any_sync(0xffffffffu, need_o)) {
+        // O holds every earlier P V only once block b - 1's has completed
+        if (!mbar_wait_or_abort(&pv_done[(b - 1) & 1], ((b - 1) >> 1) & 1, p.status, abort_flag)) ok = false;
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = need_o ? exp2f(m_run - m_new) : 1.f;
+        for (int c = 0; c < 256; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tO + lane_off + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
+          tmem_st16(tO + lane_off + c, r);
+        }
+        tmem_wait_st();
+        l_run *= f;
+      }
+      m_run = m_new;
+      // P in place: positions c..c+15 (S columns c..c+15, already read) -> bf16 pair columns c/2..c/2+7
+      for (int c = 0; c < BP; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(ts + c, r);
+        tmem_wait_ld();
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float e0 = (c + 2 * j < valid) ? exp2f(__uint_as_float(r[2 * j]) * p.sm_scale_log2 - m_run) : 0.f;
+          const float e1 = (c + 2 * j + 1 < valid) ? exp2f(__uint_as_float(r[2 * j + 1]) * p.sm_scale_log2 - m_run)
+                                                   : 0.f;
+          l_run += e0 + e1;
+          pk[j] = pack_bf16x2(e0, e1);
+        }
+        tmem_st8(ts + c / 2, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[sb]);
+    }
+    // ---------------------------------------------------------------- epilogue
+    const int head = hg * 128 + h;
+    bool o_ok = ok && nb > 0;
+    if (o_ok) o_ok = mbar_wait_or_abort(o_full, 0, p.status, abort_flag);
+    if (__all_sync(0xffffffffu, o_ok)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      for (int c = 0; c < 256; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(tO + lane_off + c, r);
+        tmem_wait_ld();
+        if (head < p.nh) {
+          const int64_t base = ((int64_t)t * p.nh + head) * 512 + half * 256 + c;
+          if (p.splits == 1) {
+            uint4 v0, v1;
+            v0.x = pack_bf16x2(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
+            v0.y = pack_bf16x2(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
+            v0.z = pack_bf16x2(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
+            v0.w = pack_bf16x2(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
+            v1.x = pack_bf16x2(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
+            v1.y = pack_bf16x2(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
+            v1.z = pack_bf16x2(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
+            v1.w = pack_bf16x2(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
+            reinterpret_cast<uint4*>(p.out + base)[0] = v0;
+            reinterpret_cast<uint4*>(p.out + base)[1] = v1;
+          } else {
+            float* dst = p.part_o + (int64_t)split * p.T * p.nh * 512 + base;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          }
+        }
+      }
+    } else if (head < p.nh && nb == 0) {
+      if (p.splits == 1) {
+        for (int c = 0; c < 256; ++c) p.out[((int64_t)t * p.nh + head) * 512 + half * 256 + c] = __float2bfloat16(0.f);
+      } else {
+        float* dst = p.part_o + (int64_t)split * p.T * p.nh * 512 + ((int64_t)t * p.nh + head) * 512 + half * 256;
+        for (int c = 0; c < 256; ++c) dst[c] = 0.f;
+      }
+    }
+    if (head < p.nh && half == 0) {
+      if (p.splits > 1) {
+        float* ml = p.part_ml + (((int64_t)split * p.T + t) * p.nh + head) * 2;
+        ml[0] = nb > 0 ? m_run : -INFINITY;
+        ml[1] = nb > 0 ? l_run : 0.f;
+      } else if (p.lse) {
+        p.lse[(int64_t)t * p.nh + head] = l_run > 0.f ? (m_run + log2f(l_run)) / kLog2e : -INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+}  // namespace attn4
 
 }  // namespace mla
 
@@ -634,7 +681,7 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
 cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache, const int* indices, const int* counts,
                                  int topk, float sm_scale, int splits, void* out, float* part_o, float* part_ml,
                                  float* lse, uint32_t* status, cudaStream_t stream) {
-  using namespace mla::attn;
+  using namespace mla::attn4;
   if (T == 0) return cudaSuccess;
   const int box_rows = nh >= 128 ? 128 : (nh + 7) / 8 * 8;
   CUtensorMap tq = make_tma_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)T * nh, DIM, DIM, box_rows, 64,
@@ -654,13 +701,14 @@ cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache
   p.lse = lse;
   p.T = T;
   p.status = status;
-  cudaError_t e = cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  cudaError_t e = cudaFuncSetAttribute(sparse_attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(T, (nh + 127) / 128, 2 * splits);
-  sparse_attn_kernel<<<grid, kThreads, SMEM, stream>>>(tq, p);
+  sparse_attn_block_kernel<<<grid, kThreads, SMEM, stream>>>(tq, p);
   e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
-  merge_kernel<<<T * nh, 128, 0, stream>>>(part_o, part_ml, splits, T, nh, reinterpret_cast<__nv_bfloat16*>(out), lse);
+  mla::attn::merge_kernel<<<T * nh, 128, 0, stream>>>(part_o, part_ml, splits, T, nh,
+                                                      reinterpret_cast<__nv_bfloat16*>(out), lse);
   return cudaGetLastError();
 }
 

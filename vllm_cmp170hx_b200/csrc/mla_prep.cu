@@ -236,83 +236,194 @@ __device__ int block_exclusive_scan(int v, int* tmp, int* total) {
 // Per token: the `k` largest scores among positions [0, ctx), ties to the
 // lowest position, output in ascending position order as cache slot ids
 // (block_table[seq][pos / bs] * bs + pos % bs); -1 pads when ctx < k.
+//
+// One CTA per token.  The row's order-preserving keys are cached in shared
+// memory when they fit (otherwise re-read from global memory each pass).
+// Range-adaptive radix select: the k-th key is known to lie in [lo, hi];
+// each pass histograms (key - lo) >> shift over 2048 bins, with shift chosen
+// so the range fills the bins (scores crowd a narrow band of float
+// exponents, so fixed top-bit digits would pile onto a few bins); a warp
+// whose lanes all hit one bin adds once.  A parallel suffix scan finds the
+// bin holding the k-th key, which becomes the next [lo, hi]; two or three
+// passes reach a single key.  The output pass walks the row in
+// 1024-position chunks, one position per thread, and places a taken
+// position at (#greater before it) + min(#equal before it, remaining) from
+// warp ballots: ascending order, lowest positions win ties, coalesced.
+template <bool CACHED>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restrict__ scores, int64_t ld_scores,
                                                             const int* __restrict__ ctx_lens, int k,
                                                             const int* __restrict__ token_seq,
                                                             const int* __restrict__ block_table, int64_t ld_bt,
                                                             int block_size, int* __restrict__ out_idx,
                                                             int* __restrict__ out_count) {
-  __shared__ int hist[256];
+  extern __shared__ uint32_t skeys[];
+  constexpr int NBIN = 2048;
+  __shared__ int hist[NBIN];
   __shared__ int tmp[80];
-  __shared__ uint32_t s_prefix;
+  __shared__ int wcnt[2][32];
+  __shared__ uint32_t s_lo, s_hi, s_red[2][32];
   __shared__ int s_remaining;
+  __shared__ int s_run[2];
   const int t = blockIdx.x;
   const int ctx = ctx_lens[t];
   const int seq = token_seq ? token_seq[t] : t;
   const float* row = scores + (int64_t)t * ld_scores;
   const int* bt = block_table + (int64_t)seq * ld_bt;
   int* out = out_idx + (int64_t)t * k;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (ctx <= k) {
     for (int p = tid; p < k; p += blockDim.x) out[p] = p < ctx ? bt[p / block_size] * block_size + p % block_size : -1;
     if (tid == 0) out_count[t] = ctx;
     return;
   }
-  // radix select of the k-th largest key, 8 bits per pass
-  uint32_t prefix = 0, mask = 0;
-  int remaining = k;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-    for (int p = tid; p < ctx; p += blockDim.x) {
-      const uint32_t key = fkey(row[p]);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+  auto key_at = [&](int p) -> uint32_t { return CACHED ? skeys[p] : fkey(row[p]); };
+  // keys (cached) and their range
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+  for (int base = 0; base < ctx; base += 8 * kTopkThreads) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {  // eight independent loads in flight per thread
+      const int p = base + j * kTopkThreads + tid;
+      v[j] = p < ctx ? row[p] : 0.f;
     }
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0;
-      int d = 255;
-      for (; d > 0; --d) {
-        if (acc + hist[d] >= remaining) break;
-        acc += hist[d];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int p = base + j * kTopkThreads + tid;
+      if (p < ctx) {
+        const uint32_t key = fkey(v[j]);
+        if (CACHED) skeys[p] = key;
+        kmin = min(kmin, key);
+        kmax = max(kmax, key);
       }
-      s_prefix = prefix | ((uint32_t)d << shift);
-      s_remaining = remaining - acc;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+  }
+  if (lane == 0) {
+    s_red[0][warp] = kmin;
+    s_red[1][warp] = kmax;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    kmin = s_red[0][lane];
+    kmax = s_red[1][lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+      kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) {
+      s_lo = kmin;
+      s_hi = kmax;
+      s_remaining = k;
+    }
+  }
+  __syncthreads();
+  uint32_t lo = s_lo, hi = s_hi;
+  int remaining = s_remaining;
+#pragma unroll 1
+  while (lo < hi) {
+    const uint32_t span = hi - lo;  // >= 1
+    const int bits = 32 - __clz(span);
+    const int shift = bits > 11 ? bits - 11 : 0;
+    for (int i = tid; i < NBIN; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int base = 0; base < ctx; base += blockDim.x) {
+      const int p = base + tid;
+      const uint32_t key = p < ctx ? key_at(p) : 0u;
+      const bool sel = p < ctx && key >= lo && key <= hi;
+      const int bin = sel ? (int)((key - lo) >> shift) : -1;
+      const int bin0 = __shfl_sync(0xffffffffu, bin, 0);
+      if (__all_sync(0xffffffffu, bin == bin0)) {
+        if (lane == 0 && bin0 >= 0) atomicAdd(&hist[bin0], 32);
+      } else if (sel) {
+        atomicAdd(&hist[bin], 1);
+      }
     }
     __syncthreads();
-    prefix = s_prefix;
+    // suffix scan: thread j owns bins NBIN-1-2j and NBIN-2-2j (counted from the top)
+    const int top = NBIN - 1 - 2 * tid;
+    const int c0 = top >= 0 ? hist[top] : 0, c1 = top - 1 >= 0 ? hist[top - 1] : 0;
+    int tot;
+    const int above = block_exclusive_scan(c0 + c1, tmp, &tot);
+    if (top >= 0) {
+      int bsel = -1, before = 0;
+      if (above < remaining && above + c0 >= remaining) {
+        bsel = top;
+        before = above;
+      } else if (top - 1 >= 0 && above + c0 < remaining && above + c0 + c1 >= remaining) {
+        bsel = top - 1;
+        before = above + c0;
+      }
+      if (bsel >= 0) {
+        const uint32_t nlo = lo + ((uint32_t)bsel << shift);
+        const uint32_t w = shift >= 32 ? 0xffffffffu : ((1u << shift) - 1u);
+        s_lo = nlo;
+        s_hi = (hi - nlo > w) ? nlo + w : hi;
+        s_remaining = remaining - before;
+      }
+    }
+    __syncthreads();
+    lo = s_lo;
+    hi = s_hi;
     remaining = s_remaining;
-    mask |= 255u << shift;
-    __syncthreads();
   }
-  // prefix == key of the k-th largest; `remaining` of the keys equal to it are taken
-  const int per = (ctx + blockDim.x - 1) / blockDim.x;
-  const int p0 = tid * per, p1 = min(ctx, p0 + per);
-  int n_eq = 0;
-  for (int p = p0; p < p1; ++p) n_eq += fkey(row[p]) == prefix;
-  int tot;
-  const int eq_before = block_exclusive_scan(n_eq, tmp, &tot);
-  int n_sel = 0;
-  {
-    int e = eq_before;
-    for (int p = p0; p < p1; ++p) {
-      const uint32_t key = fkey(row[p]);
-      if (key > prefix) ++n_sel;
-      else if (key == prefix) n_sel += (e++ < remaining);
+  const uint32_t kth = lo;  // key of the k-th largest; the first `remaining` positions holding it are taken
+  // Output: warp w walks positions [w * span, (w + 1) * span) in 32-position steps.  Sweep 1
+  // counts its keys above / equal to kth, a block scan gives each warp its offsets, sweep 2
+  // places the taken positions.
+  const int span = ((ctx + 31) / 32 + 31) / 32 * 32;
+  const int w0 = warp * span, w1 = min(ctx, w0 + span);
+  int g_cnt = 0, e_cnt = 0;
+  for (int base = w0; base < w1; base += 32) {
+    const int p = base + lane;
+    const uint32_t key = p < w1 ? key_at(p) : 0u;
+    g_cnt += __popc(__ballot_sync(0xffffffffu, p < w1 && key > kth));
+    e_cnt += __popc(__ballot_sync(0xffffffffu, p < w1 && key == kth));
+  }
+  if (lane == 0) {
+    wcnt[0][warp] = g_cnt;
+    wcnt[1][warp] = e_cnt;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int g = wcnt[0][lane], e = wcnt[1][lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int g2 = __shfl_up_sync(0xffffffffu, g, o), e2 = __shfl_up_sync(0xffffffffu, e, o);
+      if (lane >= o) {
+        g += g2;
+        e += e2;
+      }
+    }
+    wcnt[0][lane] = g - wcnt[0][lane];  // exclusive
+    wcnt[1][lane] = e - wcnt[1][lane];
+    if (lane == 31) {
+      s_run[0] = g;
+      s_run[1] = e;
     }
   }
-  const int sel_before = block_exclusive_scan(n_sel, tmp, &tot);
-  {
-    int e = eq_before, o = sel_before;
-    for (int p = p0; p < p1; ++p) {
-      const uint32_t key = fkey(row[p]);
-      bool take = key > prefix;
-      if (key == prefix) take = (e++ < remaining);
-      if (take) out[o++] = bt[p / block_size] * block_size + p % block_size;
-    }
+  __syncthreads();
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  int g_run = wcnt[0][warp], e_run = wcnt[1][warp];
+  for (int base = w0; base < w1; base += 32) {
+    const int p = base + lane;
+    const uint32_t key = p < w1 ? key_at(p) : 0u;
+    const bool gt = p < w1 && key > kth;
+    const bool eq = p < w1 && key == kth;
+    const uint32_t bg = __ballot_sync(0xffffffffu, gt), be = __ballot_sync(0xffffffffu, eq);
+    const int e_before = e_run + __popc(be & lt_mask);
+    if (gt || (eq && e_before < remaining)) out[g_run + __popc(bg & lt_mask) + min(e_before, remaining)] =
+        bt[p / block_size] * block_size + p % block_size;
+    g_run += __popc(bg);
+    e_run += __popc(be);
   }
-  for (int p = tot + tid; p < k; p += blockDim.x) out[p] = -1;
-  if (tid == 0) out_count[t] = tot;
+  const int total = s_run[0] + min(s_run[1], remaining);
+  for (int p = total + tid; p < k; p += blockDim.x) out[p] = -1;
+  if (tid == 0) out_count[t] = total;
 }
 
 }  // namespace mla
@@ -364,8 +475,18 @@ cudaError_t mla_topk(const float* scores, int64_t ld_scores, const int* ctx_lens
                      const int* block_table, int64_t ld_bt, int block_size, int* out_idx, int* out_count, int T,
                      cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  mla::topk_kernel<<<T, mla::kTopkThreads, 0, stream>>>(scores, ld_scores, ctx_lens, k, token_seq, block_table, ld_bt,
-                                                        block_size, out_idx, out_count);
+  // keys of a whole row cached in shared memory when they fit (the row width bounds every ctx)
+  const int64_t cache_bytes = ld_scores * 4;
+  if (cache_bytes <= 192 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(mla::topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)cache_bytes);
+    if (e != cudaSuccess) return e;
+    mla::topk_kernel<true><<<T, mla::kTopkThreads, cache_bytes, stream>>>(
+        scores, ld_scores, ctx_lens, k, token_seq, block_table, ld_bt, block_size, out_idx, out_count);
+  } else {
+    mla::topk_kernel<false><<<T, mla::kTopkThreads, 0, stream>>>(scores, ld_scores, ctx_lens, k, token_seq,
+                                                                 block_table, ld_bt, block_size, out_idx, out_count);
+  }
   return cudaGetLastError();
 }
 

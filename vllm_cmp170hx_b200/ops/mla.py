@@ -83,9 +83,23 @@ def indexer_topk(q8, w, k_cache, k_scale, ctx_lens, token_seq, block_table, bloc
     return idx, cnt
 
 
-def pick_splits(T: int, nh: int, num_sms: int = 148) -> int:
-    ctas = T * ((nh + 127) // 128) * 2
-    return max(1, min(8, (2 * num_sms) // max(1, ctas)))
+def pick_splits(T: int, nh: int, topk: int = 2048, num_sms: int = 148, max_partial_bytes: int = 512 << 20,
+                block_us: float = 2.0, merge_bytes_per_us: float = 5e6) -> int:
+    """Position splits of the block attention kernel (blocks of 128 positions): the count with the
+    least estimated time = waves x blocks per CTA x the time of one block on one SM, plus the merge
+    pass over the fp32 partial outputs (written and read once) when split."""
+    base = T * ((nh + 127) // 128) * 2  # CTAs per split: tokens x head groups x latent halves
+    nblk = max(1, (topk + 127) // 128)
+    best, best_cost = 1, None
+    for s in range(1, nblk + 1):
+        part = s * T * nh * 512 * 4
+        if s > 1 and part > max_partial_bytes:
+            break
+        waves = -(-base * s // num_sms)
+        cost = waves * -(-nblk // s) * block_us + ((2 * part) / merge_bytes_per_us if s > 1 else 0.0)
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = s, cost
+    return best
 
 
 def sparse_attention(q: torch.Tensor, cache: torch.Tensor, indices: torch.Tensor, counts: torch.Tensor,
@@ -106,7 +120,7 @@ def sparse_attention(q: torch.Tensor, cache: torch.Tensor, indices: torch.Tensor
         return (out, lse) if want_lse else out
     out = torch.empty(T, nh, 512, dtype=torch.bfloat16, device=q.device)
     lse = torch.empty(T, nh, dtype=torch.float32, device=q.device) if want_lse else None
-    s = splits if splits is not None else pick_splits(T, nh)
+    s = splits if splits is not None else pick_splits(T, nh, indices.shape[1])
     _ext.ops().mla_sparse_attention(q.contiguous(), cache, indices, counts, sm_scale, s, out, lse,
                                     _ext.status_word(q.device))
     return (out, lse) if want_lse else out
