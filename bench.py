@@ -83,9 +83,11 @@ def sample_clocks_stop(proc) -> dict:
             "samples": len(sm)}
 
 
-def count_own_kernels(engine, steps: int) -> int:
+def count_own_kernels(engine, steps: int, table: bool = False) -> int:
     """Kernels of this package's extension (namespace b200) launched by one
-    eager decode step, times the timed steps (graph replays run the same set)."""
+    eager decode step, times the timed steps (graph replays run the same set).
+    With `table`, print that step's per-kernel device times to stderr (a
+    profiler view for guidance, never a reported number)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
 
@@ -99,6 +101,9 @@ def count_own_kernels(engine, steps: int) -> int:
     finally:
         r.cfg.enforce_eager = saved
     n = sum(1 for e in prof.events() if e.device_type.name == "CUDA" and "b200" in e.name)
+    if table:
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=90),
+              file=sys.stderr, flush=True)
     return n * steps
 
 
@@ -114,6 +119,7 @@ def main():
     ap.add_argument("--prefill-chunk", type=int, default=16384)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
+    ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -171,7 +177,7 @@ def main():
     t_prefill = time.time() - t1
     for _ in range(args.warmup):
         engine.step()
-    launches = count_own_kernels(engine, args.steps)
+    launches = count_own_kernels(engine, args.steps, table=args.profile and st.rank == 0)
     engine.runner.time_device = True
     clk = sample_clocks_start(dev.index or 0) if st.rank == 0 else None
     if world > 1:

@@ -55,7 +55,32 @@ struct Params {
   float* partial;  // [splits, M, N] (in the output's orientation) when splits > 1
   const __nv_bfloat16* bias;  // optional [N] (out features), added in the epilogue when splits == 1
   uint32_t* status;
+  // Fused all-reduce over the tensor-parallel group (ar = 1; one tile per CTA, splits == 1).
+  // Symmetric buffer of every rank: flags[cta][quarter][src] (uint32 epochs) at flag_off, tile slots
+  // [cta][epoch parity][src][128][BN] bf16 at data_off.  Each CTA pushes its bf16 tile into slot
+  // `rank` of every rank, publishes a flag per TMEM lane quarter, then sums its tile over the
+  // ranks' slots (pushed to it) in rank order and writes C.
+  int ar;
+  const uint64_t* peers;
+  int rank, world;
+  int64_t flag_off, data_off, tile_bytes;
+  uint32_t* epochs;  // [gridDim.x] per-CTA call counters (this rank)
+  uint64_t timeout_ns;
 };
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_cg_u4(const void* ptr) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(ptr));
+  return v;
+}
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -75,11 +100,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = bars + 2 * S + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* s_epoch = tmem_slot + 2;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
+    if (p.ar) *s_epoch = p.epochs[blockIdx.x] + 1;
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
@@ -221,6 +248,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(taddr + c, r);
         tmem_wait_ld();
         const int col0 = nt * BN + c;
+        if (p.ar) {
+          // bf16 tile row (this lane), columns c..c+15, into slot `rank` of every rank
+          uint4 v0, v1;
+          v0.x = pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1]));
+          v0.y = pack_bf16x2(__uint_as_float(r[2]), __uint_as_float(r[3]));
+          v0.z = pack_bf16x2(__uint_as_float(r[4]), __uint_as_float(r[5]));
+          v0.w = pack_bf16x2(__uint_as_float(r[6]), __uint_as_float(r[7]));
+          v1.x = pack_bf16x2(__uint_as_float(r[8]), __uint_as_float(r[9]));
+          v1.y = pack_bf16x2(__uint_as_float(r[10]), __uint_as_float(r[11]));
+          v1.z = pack_bf16x2(__uint_as_float(r[12]), __uint_as_float(r[13]));
+          v1.w = pack_bf16x2(__uint_as_float(r[14]), __uint_as_float(r[15]));
+          const uint32_t e = *s_epoch;
+          const int64_t slot = ((int64_t)(blockIdx.x * 2 + (e & 1)) * p.world + p.rank) * p.tile_bytes +
+                               ((int64_t)(q * 32 + lane) * BN + c) * 2;
+          for (int dst = 0; dst < p.world; ++dst) {
+            uint4* d = reinterpret_cast<uint4*>(p.peers[dst] + p.data_off + slot);
+            d[0] = v0;
+            d[1] = v1;
+          }
+          continue;
+        }
         if (row < p.M) {
           if (p.splits > 1) {
             // fp32 partials in output orientation
@@ -280,11 +328,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if (p.ar) {
+        // this quarter's rows reached every rank: publish (stores before the flag, system scope)
+        __threadfence_system();
+        __syncwarp();
+        if (lane < p.world) {
+          uint32_t* f = reinterpret_cast<uint32_t*>(p.peers[lane] + p.flag_off) +
+                        ((int64_t)blockIdx.x * 4 + q) * p.world + p.rank;
+          st_release_sys_u32(f, *s_epoch);
+        }
+      }
+    }
+    if (p.ar && local == 1 && !*abort_flag) {
+      // ---------------------------------------------------------- all-reduce of this CTA's tile
+      const uint32_t e = *s_epoch;
+      const int mt = blockIdx.x % p.m_tiles, nt = blockIdx.x / p.m_tiles;
+      bool ok = true;
+      if (lane < p.world) {
+        const uint32_t* f = reinterpret_cast<const uint32_t*>(p.peers[p.rank] + p.flag_off) +
+                            ((int64_t)blockIdx.x * 4 + q) * p.world + lane;
+        const uint64_t t0 = globaltimer();
+        while ((int32_t)(ld_acquire_sys_u32(f) - e) < 0) {
+          if (globaltimer() - t0 > p.timeout_ns) {
+            record_error(p.status, kErrPeerTimeout);
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (__all_sync(0xffffffffu, ok)) {
+        const int row = mt * BM + q * 32 + lane;  // A row of this lane
+        const uint8_t* base = reinterpret_cast<const uint8_t*>(p.peers[p.rank] + p.data_off) +
+                              (int64_t)(blockIdx.x * 2 + (e & 1)) * p.world * p.tile_bytes +
+                              (int64_t)(q * 32 + lane) * BN * 2;
+        const float bias = (p.bias && p.transpose_out && row < p.M) ? __bfloat162float(p.bias[row]) : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 8) {
+          float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int src = 0; src < p.world; ++src) {
+            const uint4 v = ld_cg_u4(base + (int64_t)src * p.tile_bytes + c * 2);
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc8[i] += __bfloat162float(h[i]);
+          }
+          if (row >= p.M) continue;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int col = nt * BN + c + i;
+            if (col >= p.N) break;
+            if (p.transpose_out) {
+              p.C[(size_t)col * p.ldc + row] = __float2bfloat16(acc8[i] + bias);
+            } else {
+              const float b = p.bias ? __bfloat162float(p.bias[col]) : 0.f;
+              p.C[(size_t)row * p.ldc + col] = __float2bfloat16(acc8[i] + b);
+            }
+          }
+        }
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (p.ar && threadIdx.x == 0) p.epochs[blockIdx.x] = *s_epoch;
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C_::TMEM_COLS);
@@ -411,6 +517,65 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(p.partial, p.C, p.Cf, a.M, a.N, (int)a.ldc, splits,
                                                        reinterpret_cast<const __nv_bfloat16*>(a.bias), 0);
   return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16_allreduce(const GemmArArgs& a, cudaStream_t stream) {
+  using namespace gemm;
+  if (a.M == 0 || a.N == 0) return cudaSuccess;
+  if (a.K % 8 != 0 || a.world < 1 || a.world > 8) return cudaErrorInvalidValue;
+  const int sms = device_sm_count();
+  const bool swap = a.M <= 128;
+  const void* A = swap ? a.w : a.x;
+  const void* B = swap ? a.x : a.w;
+  const int64_t lda = swap ? a.ldw : a.ldx;
+  const int64_t ldb = swap ? a.ldx : a.ldw;
+  const int Ma = swap ? a.N : a.M;
+  const int Nb = swap ? a.M : a.N;
+  const int bn = swap ? (Nb <= 16 ? 16 : Nb <= 32 ? 32 : Nb <= 64 ? 64 : 128) : 256;
+  Params p{};
+  p.M = Ma;
+  p.N = Nb;
+  p.K = a.K;
+  p.ldc = (int)a.ldc;
+  p.transpose_out = swap ? 1 : 0;
+  p.m_tiles = (Ma + BM - 1) / BM;
+  p.n_tiles = (Nb + bn - 1) / bn;
+  const int kb_total = (a.K + BK - 1) / BK;
+  p.k_blocks_per_split = kb_total;
+  p.splits = 1;
+  p.C = reinterpret_cast<__nv_bfloat16*>(a.c);
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  p.status = a.status;
+  p.ar = 1;
+  p.peers = a.peers;
+  p.rank = a.rank;
+  p.world = a.world;
+  p.flag_off = a.flag_off;
+  p.data_off = a.data_off;
+  p.tile_bytes = (int64_t)BM * bn * 2;
+  p.epochs = a.epochs;
+  p.timeout_ns = a.timeout_ns;
+  const int tiles = p.m_tiles * p.n_tiles;
+  // one tile per CTA, every CTA resident: the fused reduction waits on peers
+  if (tiles > sms || tiles > a.max_ctas || p.tile_bytes > a.tile_bytes_cap) return cudaErrorInvalidValue;
+  switch (bn) {
+    case 16: return launch<16>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, tiles);
+    case 32: return launch<32>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, tiles);
+    case 64: return launch<64>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, tiles);
+    case 128: return launch<128>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, tiles);
+    default: return launch<256>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, tiles);
+  }
+}
+
+// Whether gemm_bf16_allreduce takes this shape (one output tile per CTA within the CTA and slot caps).
+int gemm_bf16_allreduce_fits(int M, int N, int max_ctas, int64_t tile_bytes_cap) {
+  using namespace gemm;
+  const bool swap = M <= 128;
+  const int Ma = swap ? N : M;
+  const int Nb = swap ? M : N;
+  const int bn = swap ? (Nb <= 16 ? 16 : Nb <= 32 ? 32 : Nb <= 64 ? 64 : 128) : 256;
+  const int tiles = ((Ma + BM - 1) / BM) * ((Nb + bn - 1) / bn);
+  return tiles <= device_sm_count() && tiles <= max_ctas && (int64_t)BM * bn * 2 <= tile_bytes_cap;
 }
 
 }  // namespace b200

@@ -35,6 +35,47 @@ struct GemmArgs {
 int gemm_bf16_splits(int M, int N, int K, int splits_req);
 cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 
+// GEMM fused with the tensor-parallel all-reduce over symmetric peer buffers (gemm_bf16.cu).
+struct GemmArArgs {
+  const void* x;
+  int64_t ldx;
+  const void* w;
+  int64_t ldw;
+  const void* bias;
+  void* c;  // bf16 [M, N] (ldc), the all-reduced result
+  int64_t ldc;
+  int M, N, K;
+  const uint64_t* peers;  // [world] symmetric buffer base of each rank
+  int rank, world;
+  int64_t flag_off, data_off;
+  int64_t tile_bytes_cap;  // bytes reserved per (cta, parity, src) slot
+  int max_ctas;            // CTAs the flag / slot areas are sized for
+  uint32_t* epochs;        // [max_ctas] per-CTA call counters
+  uint32_t* status;
+  uint64_t timeout_ns;
+};
+cudaError_t gemm_bf16_allreduce(const GemmArArgs& a, cudaStream_t stream);
+
+// MoE combine fused with the tensor-parallel all-reduce (fused_comm.cu).
+struct CombineArArgs {
+  const float* y;  // [assignments, ld_y] fp32 expert outputs
+  int64_t ld_y;
+  const int* slot_of;         // [T, k] assignment row of (token, j), -1 none
+  const float* sorted_weight;  // [assignments] router weight
+  int k;
+  const __nv_bfloat16* add;  // [T, H] shared-expert output or null
+  __nv_bfloat16* out;        // [T, H]
+  int T, H;
+  const uint64_t* peers;
+  int rank, world;
+  int64_t flag_off, data_off, slot_bytes;
+  uint32_t* epochs;  // [blocks]
+  uint32_t* status;
+  uint64_t timeout_ns;
+};
+cudaError_t combine_allreduce(const CombineArArgs& a, int blocks, cudaStream_t stream);
+int gemm_bf16_allreduce_fits(int M, int N, int max_ctas, int64_t tile_bytes_cap);
+
 // ---------------------------------------------------------------- norm.cu
 cudaError_t rms_norm(void* out, int64_t ld_out, const void* x, int64_t ld_x, const void* w, int T, int H, float eps,
                      cudaStream_t stream);

@@ -73,6 +73,15 @@ void symm_all_reduce_op(const at::Tensor& in, at::Tensor& out, const at::Tensor&
                         int64_t data_off, int64_t half_bytes, at::Tensor& epochs, const at::Tensor& status,
                         double timeout_s);  // comm.cu
 
+void gemm_allreduce_op(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+                       const at::Tensor& peers, int64_t rank, int64_t world, int64_t flag_off, int64_t data_off,
+                       int64_t tile_bytes_cap, int64_t max_ctas, at::Tensor& epochs, const at::Tensor& status,
+                       double timeout_s);  // gemm_bf16.cu
+void combine_allreduce_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
+                          const c10::optional<at::Tensor>& add, at::Tensor& out, const at::Tensor& peers,
+                          int64_t rank, int64_t world, int64_t flag_off, int64_t data_off, int64_t slot_bytes,
+                          at::Tensor& epochs, const at::Tensor& status, double timeout_s);  // fused_comm.cu
+
 void dequant_gemm_op(int64_t format, int64_t nmat, const at::Tensor& w0, const c10::optional<at::Tensor>& w1,
                      const at::Tensor& s0, const c10::optional<at::Tensor>& s1, const at::Tensor& b0,
                      const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
@@ -130,7 +139,13 @@ void register_host_bindings(pybind11::module_& m);
   X("dequant_gemm(int format, int nmat, Tensor w0, Tensor? w1, Tensor s0, Tensor? s1, Tensor b0, Tensor? b1, " \
     "int tile_rows, Tensor items, Tensor num_items, int max_work, Tensor(a!) out, int out_mode, "             \
     "float swiglu_limit, Tensor(b!) status) -> ()")                                                       \
-  X("gather_rows(Tensor x, Tensor? src, Tensor(a!) out, int rows) -> ()")
+  X("gather_rows(Tensor x, Tensor? src, Tensor(a!) out, int rows) -> ()")                               \
+  X("gemm_allreduce(Tensor x, Tensor w, Tensor? bias, Tensor(a!) out, Tensor peers, int rank, int world, "  \
+    "int flag_off, int data_off, int tile_bytes_cap, int max_ctas, Tensor(b!) epochs, Tensor(c!) status, " \
+    "float timeout_s) -> ()")                                                                            \
+  X("combine_allreduce(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out, " \
+    "Tensor peers, int rank, int world, int flag_off, int data_off, int slot_bytes, Tensor(b!) epochs, "    \
+    "Tensor(c!) status, float timeout_s) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -155,4 +170,6 @@ void register_host_bindings(pybind11::module_& m);
   X("sample_combine", b200::sample_combine_op)        \
   X("symm_all_reduce", b200::symm_all_reduce_op)      \
   X("dequant_gemm", b200::dequant_gemm_op)            \
-  X("gather_rows", b200::gather_rows_op)
+  X("gather_rows", b200::gather_rows_op)              \
+  X("gemm_allreduce", b200::gemm_allreduce_op)        \
+  X("combine_allreduce", b200::combine_allreduce_op)

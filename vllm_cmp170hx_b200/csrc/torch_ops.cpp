@@ -561,3 +561,86 @@ void gather_rows_op(const at::Tensor& x, const c10::optional<at::Tensor>& src, a
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void gemm_allreduce_op(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+                       const at::Tensor& peers, int64_t rank, int64_t world, int64_t flag_off, int64_t data_off,
+                       int64_t tile_bytes_cap, int64_t max_ctas, at::Tensor& epochs, const at::Tensor& status,
+                       double timeout_s) {
+  B200_CHECK_CUDA(x);
+  B200_CHECK_DTYPE(x, at::kBFloat16);
+  B200_CHECK_DTYPE(w, at::kBFloat16);
+  B200_CHECK_DTYPE(out, at::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm_allreduce: shape mismatch");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "gemm_allreduce: inner dims contiguous");
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == w.size(0), "gemm_allreduce: bad out shape");
+  TORCH_CHECK(peers.scalar_type() == at::kLong && peers.numel() == world && peers.is_cuda(), "gemm_allreduce: peers");
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= max_ctas, "gemm_allreduce: epochs");
+  if (bias.has_value()) {
+    B200_CHECK_DTYPE(*bias, at::kBFloat16);
+    TORCH_CHECK(bias->numel() == w.size(0) && bias->is_contiguous(), "gemm_allreduce: bad bias");
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  GemmArArgs a{};
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.w = w.data_ptr();
+  a.ldw = w.stride(0);
+  a.bias = bias.has_value() ? bias->data_ptr() : nullptr;
+  a.c = out.data_ptr();
+  a.ldc = out.stride(0);
+  a.M = x.size(0);
+  a.N = w.size(0);
+  a.K = x.size(1);
+  a.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.flag_off = flag_off;
+  a.data_off = data_off;
+  a.tile_bytes_cap = tile_bytes_cap;
+  a.max_ctas = (int)max_ctas;
+  a.epochs = reinterpret_cast<uint32_t*>(epochs.data_ptr<int>());
+  a.status = status_ptr(status);
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  B200_LAUNCH(gemm_bf16_allreduce(a, cur_stream()));
+}
+
+void combine_allreduce_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
+                          const c10::optional<at::Tensor>& add, at::Tensor& out, const at::Tensor& peers,
+                          int64_t rank, int64_t world, int64_t flag_off, int64_t data_off, int64_t slot_bytes,
+                          at::Tensor& epochs, const at::Tensor& status, double timeout_s) {
+  B200_CHECK_CUDA(y);
+  B200_CHECK_DTYPE(y, at::kFloat);
+  B200_CHECK_DTYPE(out, at::kBFloat16);
+  TORCH_CHECK(y.stride(1) == 1 && out.is_contiguous() && out.dim() == 2, "combine_allreduce: layout");
+  TORCH_CHECK(slot_of.scalar_type() == at::kInt && slot_of.is_contiguous(), "combine_allreduce: slot_of int32");
+  TORCH_CHECK(sorted_weight.scalar_type() == at::kFloat, "combine_allreduce: weights fp32");
+  if (add.has_value()) {
+    B200_CHECK_DTYPE(*add, at::kBFloat16);
+    TORCH_CHECK(add->is_contiguous() && add->sizes() == out.sizes(), "combine_allreduce: add");
+  }
+  c10::cuda::CUDAGuard g(y.device());
+  CombineArArgs a{};
+  a.y = y.data_ptr<float>();
+  a.ld_y = y.stride(0);
+  a.slot_of = slot_of.data_ptr<int>();
+  a.sorted_weight = sorted_weight.data_ptr<float>();
+  a.k = (int)k;
+  a.add = add.has_value() ? reinterpret_cast<const __nv_bfloat16*>(add->data_ptr()) : nullptr;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.T = out.size(0);
+  a.H = out.size(1);
+  a.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.flag_off = flag_off;
+  a.data_off = data_off;
+  a.slot_bytes = slot_bytes;
+  a.epochs = reinterpret_cast<uint32_t*>(epochs.data_ptr<int>());
+  a.status = status_ptr(status);
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  B200_LAUNCH(combine_allreduce(a, (int)epochs.numel(), cur_stream()));
+}
+
+}  // namespace b200

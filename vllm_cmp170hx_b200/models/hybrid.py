@@ -113,7 +113,7 @@ class KDAAttention(nn.Module):
         g2 = self.g_b(ga)
         o = kda_ops.kda_forward(qkv, g_raw, beta, g2, ctx.cu_seqlens, ctx.kda_slots, ctx.has_init, conv, self.conv_w,
                                 None, self.a_log, self.g_bias, self.lower_bound, self.norm_w, rec)
-        return self.o_proj(o)
+        return self.o_proj.forward_reduced(o)
 
 
 class MLAAttention(nn.Module):
@@ -193,7 +193,7 @@ class MLAAttention(nn.Module):
         qf[:, :, kvl:] = q[:, :, self.dn:]
         o_lat = mla_ops.sparse_attention(qf, latent, indices, counts, self.sm_scale)
         o = torch.bmm(o_lat.transpose(0, 1), self.w_uv_t.transpose(1, 2))  # [H, T, dv]
-        return self.o_proj(o.transpose(0, 1).reshape(T, self.H * self.dv))
+        return self.o_proj.forward_reduced(o.transpose(0, 1).reshape(T, self.H * self.dv))
 
 
 # ============================================================================ MLPs
@@ -206,8 +206,9 @@ class DenseMLP(nn.Module):
         self.down = Linear(wi.normal((hid, inter), default_std(inter), (1, tp_rank, tp)))
         self.limit = limit
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down(ops.silu_mul(self.gate_up(x), self.limit))
+    def forward(self, x: torch.Tensor, reduce: bool = False) -> torch.Tensor:
+        h = ops.silu_mul(self.gate_up(x), self.limit)
+        return self.down.forward_reduced(h) if reduce else self.down(h)
 
 
 def random_exl3_experts(E: int, hid: int, inter_local: int, bits_x2: int, codebook: int, wi: WeightInit,
@@ -268,7 +269,7 @@ class BF16Experts(nn.Module):
                                                         (1, tp_rank, tp)) for _ in range(E)]), requires_grad=False)
         self.limit = limit
 
-    def forward(self, x, ids, w, add=None):
+    def forward(self, x, ids, w, add=None, reduce: bool = False):
         out = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32, device=x.device)
         for e in range(self.gate_up.shape[0]):
             mask = ids == e
@@ -280,7 +281,8 @@ class BF16Experts(nn.Module):
             out[rows] += (w * mask).sum(-1)[rows, None] * y
         if add is not None:
             out += add.float()
-        return out.to(x.dtype)
+        out = out.to(x.dtype)
+        return comm.tp_all_reduce(out) if reduce else out
 
 
 class MoE(nn.Module):
@@ -308,18 +310,19 @@ class MoE(nn.Module):
         if mc.num_shared:
             self.shared = DenseMLP(hid, mc.shared_intermediate * mc.num_shared, wi, tp, tp_rank, mc.swiglu_limit)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, reduce: bool = False) -> torch.Tensor:
+        """reduce: return the output summed over the tensor-parallel group."""
         logits = self.gate(x, out_dtype=torch.float32)
         ids, w = moe_ops.topk(logits, self.mc.top_k, self.mc.router_mode, self.e_bias, self.mc.routed_scaling,
                               self.mc.renormalize)
         shared = self.shared(x) if self.shared is not None else None
         if isinstance(self.experts, moe_ops.Exl3Experts):
-            return moe_ops.exl3_moe(x, ids, w, self.experts, add=shared)
+            return moe_ops.exl3_moe(x, ids, w, self.experts, add=shared, reduce=reduce)
         from ..ops.dequant import MarlinExperts, marlin_moe
 
         if isinstance(self.experts, MarlinExperts):
-            return marlin_moe(x, ids, w, self.experts, add=shared)
-        return self.experts(x, ids, w, add=shared)
+            return marlin_moe(x, ids, w, self.experts, add=shared, reduce=reduce)
+        return self.experts(x, ids, w, add=shared, reduce=reduce)
 
 
 # ============================================================================ model
@@ -345,12 +348,12 @@ class DecoderLayer(nn.Module):
             h = self.input_norm(x)
         else:
             h = self.input_norm(x, residual)
-        a = comm.tp_all_reduce(self.attn(h, ctx, self.idx))
+        a = self.attn(h, ctx, self.idx)  # row-parallel o_proj: already summed over the TP group
         if self.mlp is None:
             residual = residual + a
             return a, residual
         h = self.post_norm(a, residual)
-        return comm.tp_all_reduce(self.mlp(h)), residual
+        return self.mlp(h, reduce=True), residual
 
 
 class HybridForCausalLM(nn.Module):

@@ -75,6 +75,10 @@ class Linear(nn.Module):
     def forward(self, x: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
         return ops.gemm(x, self.weight, self.bias, out_dtype=out_dtype)
 
+    def forward_reduced(self, x: torch.Tensor) -> torch.Tensor:
+        """Row-parallel use: the output summed over the tensor-parallel group."""
+        return comm.gemm_all_reduce(x, self.weight, self.bias)
+
 
 class RMSNorm(nn.Module):
     def __init__(self, weight: torch.Tensor, eps: float):

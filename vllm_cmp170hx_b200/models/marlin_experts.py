@@ -92,3 +92,8 @@ class Fp8Proj(torch.nn.Module):
     def forward(self, x: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
         y = self.lin(x)
         return y if out_dtype == torch.bfloat16 else y.to(out_dtype)
+
+    def forward_reduced(self, x: torch.Tensor) -> torch.Tensor:
+        from ..parallel import comm
+
+        return comm.tp_all_reduce(self.lin(x))

@@ -66,13 +66,17 @@ def _moe_cpu(x, ids, w, ex: MarlinExperts) -> torch.Tensor:
 
 
 def marlin_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: MarlinExperts,
-               add: torch.Tensor | None = None, out_f32: bool = False) -> torch.Tensor:
+               add: torch.Tensor | None = None, out_f32: bool = False, reduce: bool = False) -> torch.Tensor:
     T, H = x.shape
     k = ids.shape[1]
     if not x.is_cuda:
         y = _moe_cpu(x, ids, weights, ex)
         if add is not None:
             y = y + add.float()
+        if reduce:
+            from ..parallel import comm
+
+            return comm.tp_all_reduce(y.to(x.dtype))
         return y if out_f32 else y.to(x.dtype)
     ops = _ext.ops()
     dev = x.device
@@ -99,6 +103,10 @@ def marlin_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Ma
     y = torch.empty(TK, H, dtype=torch.float32, device=dev)
     ops.dequant_gemm(0, 1, ex.down, None, ex.down_s, None, h, None, tile, items, num_items, max_items * (H // 128), y,
                      1, 0.0, st)
+    if reduce:
+        from ..parallel import comm
+
+        return comm.combine_all_reduce(y, slot_of, sorted_weight, k, add, T, H)
     out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16, device=dev)
     ops.moe_combine(y, slot_of, sorted_weight, k, add, out)
     return out

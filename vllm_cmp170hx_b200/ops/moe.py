@@ -88,8 +88,9 @@ def pick_tile_rows(T: int, k: int, E_local: int) -> int:
 
 
 def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3Experts,
-             add: torch.Tensor | None = None, out_f32: bool = False) -> torch.Tensor:
-    """Routed EXL3 experts: out[t] = sum_j w[t,j] * expert_{ids[t,j]}(x[t]) (+ add[t])."""
+             add: torch.Tensor | None = None, out_f32: bool = False, reduce: bool = False) -> torch.Tensor:
+    """Routed EXL3 experts: out[t] = sum_j w[t,j] * expert_{ids[t,j]}(x[t]) (+ add[t]); with `reduce`,
+    summed over the tensor-parallel group (bf16; the combine fused with the all-reduce)."""
     T, H = x.shape
     k = ids.shape[1]
     if not x.is_cuda:
@@ -104,6 +105,10 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
         y = _ref.exl3_experts(x, ids, weights, d, ex.swiglu_limit or None, cache)
         if add is not None:
             y = y + add.float()
+        if reduce:
+            from ..parallel import comm
+
+            return comm.tp_all_reduce(y.to(x.dtype))
         return y if out_f32 else y.to(x.dtype)
     ops = _ext.ops()
     dev = x.device
@@ -133,6 +138,10 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
     y = torch.empty(TK, Hp, dtype=torch.float32, device=dev)
     ops.exl3_gemm(1, ex.down_trellis, None, ex.down_svh, None, None, ex.bits_x2, ex.codebook, h, None, tile, items,
                   num_items, max_items * (Hp // 128), y, 1, 0.0, st)
+    if reduce:
+        from ..parallel import comm
+
+        return comm.combine_all_reduce(y, slot_of, sorted_weight, k, add, T, H)
     out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16, device=dev)
     ops.moe_combine(y, slot_of, sorted_weight, k, add, out)
     return out

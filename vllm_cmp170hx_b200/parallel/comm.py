@@ -21,13 +21,15 @@ import torch.distributed as dist
 
 from . import state as _state
 
-_FUSED = {"enabled": False, "symm": None}
+_FUSED = {"enabled": False, "symm": None, "fused": None}
 
 
-def enable_fused(symm) -> None:
-    """Route TP all-reduces through the symmetric-memory kernels of `symm`."""
+def enable_fused(symm, fused=None) -> None:
+    """Route TP all-reduces through the symmetric-memory kernels of `symm`, and the row-parallel
+    projections / MoE combines through the compute-fused kernels of `fused`."""
     _FUSED["enabled"] = symm is not None
     _FUSED["symm"] = symm
+    _FUSED["fused"] = fused
 
 
 def fused_enabled() -> bool:
@@ -72,3 +74,38 @@ def tp_reduce_scatter(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty(x.shape[0] // st.tp_size, *x.shape[1:], dtype=x.dtype, device=x.device)
     dist.reduce_scatter_tensor(out, x.contiguous(), group=st.tp_group)
     return out
+
+
+def gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Row-parallel projection: sum over the TP group of x @ w^T (+ bias once).  Product path: one
+    kernel computes the GEMM tile, pushes it to every rank and sums the pushed tiles (gemm_bf16.cu);
+    baseline: GEMM, then the all-reduce."""
+    from .. import ops
+
+    st = _state.get()
+    if st.tp_size == 1:
+        return ops.gemm(x, w, bias)
+    fc = _FUSED["fused"]
+    if fc is not None and x.is_cuda:
+        y = fc.gemm_all_reduce(x, w, bias)
+        if y is not None:
+            return y
+    y = tp_all_reduce(ops.gemm(x, w))
+    return y if bias is None else y + bias
+
+
+def combine_all_reduce(y: torch.Tensor, slot_of: torch.Tensor, sorted_weight: torch.Tensor, k: int,
+                       add: torch.Tensor | None, T: int, H: int) -> torch.Tensor:
+    """MoE output: out[t] = sum_j w * y[slot] (+ add[t]), summed over the TP group (bf16 [T, H]).
+    Product path: the combine and the all-reduce in one kernel (fused_comm.cu)."""
+    from .. import _ext
+
+    st = _state.get()
+    fc = _FUSED["fused"]
+    if st.tp_size > 1 and fc is not None and y.is_cuda:
+        out = fc.combine_all_reduce(y, slot_of, sorted_weight, k, add, T, H)
+        if out is not None:
+            return out
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=y.device)
+    _ext.ops().moe_combine(y, slot_of, sorted_weight, k, add, out)
+    return tp_all_reduce(out)

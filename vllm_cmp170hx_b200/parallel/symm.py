@@ -60,6 +60,83 @@ class SymmComm:
         return out
 
 
+class FusedComm:
+    """Symmetric buffer of the compute-fused all-reduce kernels.
+
+    Layout per rank: [GEMM flags: cta x 4 lane quarters x src][combine flags: block x src]
+    [GEMM tile slots: cta x 2 parities x src x tile][combine slots: 2 parities x src x message].
+    Each kernel keeps per-CTA (per-block) call counters as its flag epochs."""
+
+    def __init__(self, group, cpu_group, device: torch.device, max_ctas: int = 160, tile_cap: int = 64 << 10,
+                 combine_bytes: int = 4 << 20, combine_blocks: int = 148, timeout_s: float = 10.0):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_ctas, self.tile_cap = max_ctas, tile_cap
+        self.combine_bytes, self.combine_blocks = combine_bytes, combine_blocks
+        self.timeout_s = timeout_s
+        w = self.world
+
+        def up(n):
+            return (n + 4095) // 4096 * 4096
+
+        self.gemm_flag_off = 0
+        self.comb_flag_off = up(max_ctas * 4 * w * 4)
+        flags_end = self.comb_flag_off + up(combine_blocks * w * 4)
+        self.gemm_data_off = flags_end
+        self.comb_data_off = self.gemm_data_off + max_ctas * 2 * w * tile_cap
+        total = self.comb_data_off + 2 * w * combine_bytes
+        self.buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
+        self.buf[:flags_end].zero_()
+        torch.cuda.synchronize(device)
+        self.hdl = symm_mem.rendezvous(self.buf, group)
+        self.peers = torch.tensor(list(self.hdl.buffer_ptrs), dtype=torch.int64, device=device)
+        self.gemm_epochs = torch.zeros(max_ctas, dtype=torch.int32, device=device)
+        self.comb_epochs = torch.zeros(combine_blocks, dtype=torch.int32, device=device)
+        self._fits: dict = {}
+        torch.cuda.synchronize(device)
+        dist.barrier(group=cpu_group)
+
+    def gemm_all_reduce(self, x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor | None:
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        M, N = x2.shape[0], w.shape[0]
+        key = (M, N)
+        fits = self._fits.get(key)
+        if fits is None:
+            fits = self._gemm_fits(M, N, x.device)
+            self._fits[key] = fits
+        if not fits or x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+            return None
+        if x2.stride(-1) != 1 or (x2.stride(0) % 8 and M > 1):
+            x2 = x2.contiguous()
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+        _ext.ops().gemm_allreduce(x2, w, bias, out, self.peers, self.rank, self.world, self.gemm_flag_off,
+                                  self.gemm_data_off, self.tile_cap, self.max_ctas, self.gemm_epochs,
+                                  _ext.status_word(x.device), self.timeout_s)
+        return out.view(*lead, N)
+
+    def _gemm_fits(self, M: int, N: int, device) -> bool:
+        """Same rule as gemm_bf16_allreduce_fits (gemm_bf16.cu): one 128-row output tile per CTA, every
+        CTA resident, the tile within a slot."""
+        swap = M <= 128
+        ma, nb = (N, M) if swap else (M, N)
+        bn = (16 if nb <= 16 else 32 if nb <= 32 else 64 if nb <= 64 else 128) if swap else 256
+        tiles = -(-ma // 128) * -(-nb // bn)
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        return tiles <= sms and tiles <= self.max_ctas and 128 * bn * 2 <= self.tile_cap
+
+    def combine_all_reduce(self, y, slot_of, sorted_weight, k: int, add, T: int, H: int) -> torch.Tensor | None:
+        if T * H * 2 > self.combine_bytes or H % 8 or y.stride(0) % 4:
+            return None
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=y.device)
+        _ext.ops().combine_allreduce(y, slot_of, sorted_weight, k, add, out, self.peers, self.rank, self.world,
+                                     self.comb_flag_off, self.comb_data_off, self.combine_bytes, self.comb_epochs,
+                                     _ext.status_word(y.device), self.timeout_s)
+        return out
+
+
 def _agree(ok: bool, cpu_group) -> bool:
     t = torch.tensor([1 if ok else 0], dtype=torch.int32)
     dist.all_reduce(t, op=dist.ReduceOp.MIN, group=cpu_group)
@@ -72,7 +149,7 @@ def enable_for_engine(engine) -> bool:
     st = pstate.get()
     if st.tp_size == 1 or st.device.type != "cuda":
         return False
-    symm = None
+    symm = fused = None
     try:
         symm = SymmComm(st.tp_group, st.tp_cpu_group, st.device)
         ok = True
@@ -80,7 +157,15 @@ def enable_for_engine(engine) -> bool:
         log.warning("symmetric-memory all-reduce unavailable on rank %d: %s", st.rank, e)
         ok = False
     ok = _agree(ok, st.tp_cpu_group)
-    comm.enable_fused(symm if ok else None)
+    fused_ok = False
+    if ok and engine.cfg.parallel.fused_comm:
+        try:
+            fused = FusedComm(st.tp_group, st.tp_cpu_group, st.device)
+            fused_ok = True
+        except Exception as e:  # noqa: BLE001
+            log.warning("fused compute + all-reduce kernels unavailable on rank %d: %s", st.rank, e)
+        fused_ok = _agree(fused_ok, st.tp_cpu_group)
+    comm.enable_fused(symm if ok else None, fused if fused_ok else None)
     if st.rank == 0:
         log.info("TP all-reduce: %s", "symmetric-memory one-shot kernel" if ok else "NCCL")
     return ok
