@@ -216,6 +216,76 @@ __device__ __forceinline__ void h128_group(float (&v)[NV], int lane, int q, floa
   for (int i = 0; i < NV; ++i) v[i] *= kH128;
 }
 
+template <int NV>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[NV]) {
+  if constexpr (NV == 16) {
+    tmem_ld16(taddr, r);
+  } else {
+    static_assert(NV == 4, "4 or 16 columns");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+  }
+}
+
+// Epilogue of NV accumulator columns (= rows c0 .. c0+NV-1 of the item) for this thread's output
+// feature: H128 across the 128 TMEM lanes, svh, and for the gate/up pass SwiGLU plus the down
+// projection's input rotation (suh, H128), written in the form the down pass reads.
+template <int NMAT, int NV>
+__device__ __forceinline__ void epilogue_block(const GemmParams& p, uint32_t tlane, int tile_rows, int c0, int rows,
+                                               int row0, int feat, float sg, float su, float sn, int lane, int q,
+                                               float* xb, int bar_id) {
+  if constexpr (NMAT == 2) {
+    uint32_t rg[NV], ru[NV];
+    tmem_ld_cols<NV>(tlane + c0, rg);
+    tmem_ld_cols<NV>(tlane + tile_rows + c0, ru);
+    tmem_wait_ld();
+    float gv[NV], uv[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      gv[i] = __uint_as_float(rg[i]);
+      uv[i] = __uint_as_float(ru[i]);
+    }
+    h128_group<NV>(gv, lane, q, xb, bar_id);
+    h128_group<NV>(uv, lane, q, xb, bar_id);
+    const float L = p.swiglu_limit;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float gg = gv[i] * sg, uu = uv[i] * su;
+      if (L > 0.f) {
+        gg = fminf(gg, L);
+        uu = fminf(fmaxf(uu, -L), L);
+      }
+      gv[i] = siluf_(gg) * uu * sn;
+    }
+    h128_group<NV>(gv, lane, q, xb, bar_id);
+    __half* out = reinterpret_cast<__half*>(p.out);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int r = c0 + i;
+      if (r < rows) out[(int64_t)(row0 + r) * p.ld_out + feat] = __float2half_rn(gv[i]);
+    }
+  } else {
+    uint32_t ra[NV];
+    tmem_ld_cols<NV>(tlane + c0, ra);
+    tmem_wait_ld();
+    float v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = __uint_as_float(ra[i]);
+    h128_group<NV>(v, lane, q, xb, bar_id);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int r = c0 + i;
+      if (r >= rows) continue;
+      const int64_t o = (int64_t)(row0 + r) * p.ld_out + feat;
+      if (p.out_mode == 1)
+        reinterpret_cast<float*>(p.out)[o] = v[i] * sg;
+      else
+        reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(v[i] * sg);
+    }
+  }
+}
+
 // Shared-memory plan: `ab` stages of [NMAT decoded A tiles | NMAT B tiles]
 // and `raw` stages of NMAT raw trellis chunks (32 tiles each), sized on the
 // host so both rings fit next to the epilogue exchange buffers.
@@ -435,63 +505,19 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
       const int feat = tile * 128 + f;
       float* xb = xbuf + g * 16 * 128;
       const int nchunks = (rows + 15) / 16;
-      // column chunks are dealt round-robin to the warp groups; each group's
-      // named barrier spans its own 4 warps only
-      for (int c = g; c < nchunks; c += kGroups) {
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c * 16;
-        if constexpr (NMAT == 2) {
-          uint32_t rg[16], ru[16];
-          tmem_ld16(taddr, rg);
-          tmem_ld16(taddr + tile_rows, ru);
-          tmem_wait_ld();
-          float gv[16], uv[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            gv[i] = __uint_as_float(rg[i]);
-            uv[i] = __uint_as_float(ru[i]);
-          }
-          h128_group<16>(gv, lane, q, xb, 1 + g);
-          h128_group<16>(uv, lane, q, xb, 1 + g);
-          const float sg = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
-          const float su = __half2float(p.svh[1][(int64_t)e * p.svh_estride[1] + feat]);
-          const float sn = __half2float(p.suh_next[(int64_t)e * p.suh_next_estride + feat]);
-          const float L = p.swiglu_limit;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float gg = gv[i] * sg, uu = uv[i] * su;
-            if (L > 0.f) {
-              gg = fminf(gg, L);
-              uu = fminf(fmaxf(uu, -L), L);
-            }
-            gv[i] = siluf_(gg) * uu * sn;
-          }
-          h128_group<16>(gv, lane, q, xb, 1 + g);
-          __half* out = reinterpret_cast<__half*>(p.out);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int r = c * 16 + i;
-            if (r < rows) out[(int64_t)(row0 + r) * p.ld_out + feat] = __float2half_rn(gv[i]);
-          }
-        } else {
-          uint32_t ra[16];
-          tmem_ld16(taddr, ra);
-          tmem_wait_ld();
-          float v[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
-          h128_group<16>(v, lane, q, xb, 1 + g);
-          const float s = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int r = c * 16 + i;
-            if (r >= rows) continue;
-            const int64_t o = (int64_t)(row0 + r) * p.ld_out + feat;
-            if (p.out_mode == 1)
-              reinterpret_cast<float*>(p.out)[o] = v[i] * s;
-            else
-              reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(v[i] * s);
-          }
-        }
+      // Column blocks are dealt round-robin to the warp groups (each group's named barrier spans
+      // its own 4 warps).  Items of at most 16 rows (decode) are split into 4-column blocks, so
+      // all four groups share the epilogue instead of one group holding the next item's decode.
+      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16);
+      const float sg = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
+      const float su = NMAT == 2 ? __half2float(p.svh[1][(int64_t)e * p.svh_estride[1] + feat]) : 0.f;
+      const float sn = NMAT == 2 ? __half2float(p.suh_next[(int64_t)e * p.suh_next_estride + feat]) : 0.f;
+      if (nchunks >= kGroups) {
+        for (int c = g; c < nchunks; c += kGroups)
+          epilogue_block<NMAT, 16>(p, tlane, tile_rows, c * 16, rows, row0, feat, sg, su, sn, lane, q, xb, 1 + g);
+      } else {
+        for (int c = g; c < (rows + 3) / 4; c += kGroups)
+          epilogue_block<NMAT, 4>(p, tlane, tile_rows, c * 4, rows, row0, feat, sg, su, sn, lane, q, xb, 1 + g);
       }
       tc_fence_before();
     }
