@@ -37,6 +37,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode output tok/s (box, max over ranks) at 1/2/4/8 B200; p50 TPOT"
+MODEL_DESC = {
+    3: "hybrid KDA/sparse-MLA MoE, 48 layers (36 KDA : 12 MLA), hidden 2304, 32 heads, 256 experts top-8 + 1 shared, "
+       "expert intermediate 1024, EXL3 4-bit experts, vocab 163840",
+    4: "DeepSeek-style sparse-MLA MoE, 43 layers (3 dense FFN 12288), hidden 4096, 128 heads, 256 experts top-8 + 1 "
+       "shared, expert intermediate 1536, Marlin int4 g128 experts, fp8 128x128 block-scaled attention, vocab 129280",
+}
 
 
 def reference_unavailable(args, reason: str) -> None:
@@ -120,6 +126,9 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
     ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
+    ap.add_argument("--config", type=int, default=3, choices=[3, 4],
+                    help="BASELINE config: 3 = hybrid KDA/MLA EXL3 MoE at TP=N (headline); "
+                         "4 = DeepSeek-style Marlin MoE, experts EP=N, attention TP=N")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -135,7 +144,8 @@ def main():
     import torch
     import torch.distributed as dist
 
-    from vllm_cmp170hx_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, config3)
+    from vllm_cmp170hx_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, config3,
+                                           config4)
     from vllm_cmp170hx_b200.engine.llm_engine import LLMEngine
     from vllm_cmp170hx_b200.engine.request import SamplingParams
     from vllm_cmp170hx_b200.parallel import state as pstate
@@ -144,10 +154,11 @@ def main():
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
     st = pstate.init(tp_size=args.gpus, pp_size=1, timeout_s=600)
     dev = st.device
-    model_cfg = config3()
+    model_cfg = config3() if args.config == 3 else config4()
     total_len = args.prompt + args.output + 64
     cfg = EngineConfig(model=model_cfg,
-                       parallel=ParallelConfig(tensor_parallel_size=args.gpus, fused_comm=not args.nccl_baseline),
+                       parallel=ParallelConfig(tensor_parallel_size=args.gpus, fused_comm=not args.nccl_baseline,
+                                               expert_parallel=args.config == 4),
                        scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
                                                  max_model_len=total_len, max_num_partial_prefills=args.batch),
                        cache=CacheConfig(num_blocks=args.batch * ((total_len + 63) // 64) + 1),
@@ -211,14 +222,12 @@ def main():
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_total_ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "impl": "ours",
-            "data": "synthetic: random token ids, random-init weights of the config-3 architecture",
-            "config": {"model": "hybrid KDA/sparse-MLA MoE, 48 layers (36 KDA : 12 MLA), hidden 2304, 32 heads, "
-                                "256 experts top-8 + 1 shared, expert intermediate 1024, EXL3 4-bit experts, "
-                                "vocab 163840",
+            "data": f"synthetic: random token ids, random-init weights of the config-{args.config} architecture",
+            "config": {"model": MODEL_DESC[args.config],
                        "global_batch": args.batch, "seq_len": args.prompt, "output_len": args.output,
-                       "parallelism": f"tp{args.gpus}",
+                       "parallelism": f"tp{args.gpus}" if args.config == 3 else f"ep{args.gpus}+attn-tp{args.gpus}",
                        "collectives": "fused symmetric-memory kernels" if fused else ("none" if args.gpus == 1 else "nccl"),
-                       "l2": "no flush: each step streams all expert weights (~43.5 GB / tp) >> 126 MB L2"},
+                       "l2": "no flush: each step streams the expert weights (GBs per GPU) >> 126 MB L2"},
             "p50_tpot_ms": round(statistics.median(e2e_ms), 3),
             "clocks": clocks,
             "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,

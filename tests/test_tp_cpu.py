@@ -18,6 +18,8 @@ PROMPTS = [[(5 * i + 3 * j) % 500 for j in range(9 + 13 * i)] for i in range(3)]
 
 def _cfg(tp, fmt):
     k = 0
+    ep = fmt.endswith("_ep")
+    fmt = fmt[:-3] if ep else fmt
     if fmt == "deepseek_mtp":  # Marlin experts, fp8 attention projections, MTP speculative decoding
         m = tiny_deepseek(layers=2, experts=4, hidden=256, vocab=512)
         m.moe.intermediate = 256
@@ -27,7 +29,7 @@ def _cfg(tp, fmt):
         m = tiny(layers=4, experts=4, hidden=256, expert_format=fmt)
         m.moe.intermediate = 256  # two H128 blocks: one per rank at TP=2
         m.moe.shared_intermediate = 256
-    return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp),
+    return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp, expert_parallel=ep),
                         scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256,
                                                   num_speculative_tokens=k),
                         cache=CacheConfig(num_blocks=32), device="cpu", enforce_eager=True)
@@ -38,7 +40,10 @@ def _generate(tp, fmt):
     from vllm_cmp170hx_b200.engine.request import SamplingParams
     from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
 
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
     cfg = _cfg(tp, fmt)
+    pstate.get().expert_parallel = cfg.parallel.expert_parallel
     model = HybridForCausalLM(cfg.model, "cpu", seed=5, init_mode="sliced")
     outs = LLM(cfg, model).generate(PROMPTS, SamplingParams(max_tokens=6 if cfg.scheduler.num_speculative_tokens else 3))
     return [o.output_token_ids for o in outs]
@@ -57,7 +62,7 @@ def _worker(rank, world, port, fmt, path):
     pstate.destroy()
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "exl3", "deepseek_mtp"])
+@pytest.mark.parametrize("fmt", ["bf16", "exl3", "deepseek_mtp", "exl3_ep", "deepseek_mtp_ep"])
 def test_tp2_matches_tp1(fmt):
     from vllm_cmp170hx_b200.parallel import state as pstate
 

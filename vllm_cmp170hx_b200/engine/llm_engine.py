@@ -43,6 +43,7 @@ class LLMEngine:
         st = pstate.get()
         if st.tp_size != cfg.parallel.tensor_parallel_size:
             st = pstate.init(cfg.parallel.tensor_parallel_size, cfg.parallel.pipeline_parallel_size)
+        st.expert_parallel = bool(cfg.parallel.expert_parallel)
         self.runner = ModelRunner(cfg, model)
         self.scheduler = Scheduler(cfg.scheduler, cfg.cache, self.runner.block_pool, self.runner.slot_pool)
         self.requests: dict[str, Request] = {}

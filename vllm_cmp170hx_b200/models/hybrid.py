@@ -269,10 +269,13 @@ class BF16Experts(nn.Module):
                                                         (1, tp_rank, tp)) for _ in range(E)]), requires_grad=False)
         self.limit = limit
 
+    expert_map = None  # global expert -> local index (-1: not on this rank), expert parallel only
+
     def forward(self, x, ids, w, add=None, reduce: bool = False):
         out = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32, device=x.device)
         for e in range(self.gate_up.shape[0]):
-            mask = ids == e
+            ge = e if self.expert_map is None else int((self.expert_map == e).nonzero()[0, 0])
+            mask = ids == ge
             rows = mask.any(-1).nonzero()[:, 0]
             if rows.numel() == 0:
                 continue
@@ -286,29 +289,66 @@ class BF16Experts(nn.Module):
 
 
 class MoE(nn.Module):
+    """Router, routed experts and shared expert.  Routed experts are split across the TP group
+    either by intermediate columns (every rank holds a slice of every expert; whole H128 blocks for
+    EXL3, vllm_sm80/kernels/exl3/quant.py:869) or, with expert parallelism, whole (rank r holds
+    experts [r E/tp, (r+1) E/tp)).  Tokens are replicated over the group (tensor-parallel
+    attention), so the expert-parallel dispatch is the local selection of the assignments whose
+    expert this rank holds (``expert_map``), and the combine of every rank's partial output is the
+    fused combine + all-reduce -- the reference's EP layout, which dispatches by all-gather and
+    combines by reduce-scatter (vllm_sm80/kernels/exl3/quant.py:1913-1934)."""
+
     def __init__(self, cfg: ModelConfig, wi: WeightInit, tp: int, tp_rank: int):
         super().__init__()
         mc = cfg.moe
         self.mc = mc
         hid = cfg.hidden_size
-        assert mc.intermediate % tp == 0
-        inter_local = mc.intermediate // tp
+        ep = pstate.get().expert_parallel and tp > 1
         self.gate = Linear(wi.normal((mc.num_experts, hid), default_std(hid)))
         self.e_bias = None
         if mc.router != "softmax":
             self.e_bias = nn.Parameter(wi.uniform((mc.num_experts,), -0.05, 0.05), requires_grad=False)
-        if mc.expert_format == "exl3":
-            assert inter_local % 128 == 0, "EXL3 TP cuts must keep whole H128 blocks"
-            self.experts = random_exl3_experts(mc.num_experts, hid, inter_local, mc.exl3_bits_x2, mc.exl3_codebook,
-                                               wi, tp, tp_rank, mc.swiglu_limit)
-        elif mc.expert_format == "bf16":
-            self.experts = BF16Experts(mc.num_experts, hid, inter_local, wi, tp, tp_rank, mc.swiglu_limit)
+        if ep:
+            assert mc.num_experts % tp == 0, "expert parallel needs the experts to divide over the group"
+            e_local = mc.num_experts // tp
+            first = tp_rank * e_local
+            emap = torch.full((mc.num_experts,), -1, dtype=torch.int32)
+            emap[first:first + e_local] = torch.arange(e_local, dtype=torch.int32)
+            self.experts = self._experts(mc, hid, mc.intermediate, wi, 1, 0, first, e_local)
+            self.experts.expert_map = emap.to(wi.device)
         else:
-            from . import marlin_experts
-            self.experts = marlin_experts.random_marlin_experts(mc.num_experts, hid, inter_local, wi, tp, tp_rank)
+            assert mc.intermediate % tp == 0
+            self.experts = self._experts(mc, hid, mc.intermediate // tp, wi, tp, tp_rank, 0, mc.num_experts)
         self.shared = None
         if mc.num_shared:
             self.shared = DenseMLP(hid, mc.shared_intermediate * mc.num_shared, wi, tp, tp_rank, mc.swiglu_limit)
+
+    @staticmethod
+    def _experts(mc, hid, inter_local, wi, tp, tp_rank, first: int, count: int):
+        """`count` experts starting at global expert `first` (`sliced` init draws every expert and
+        keeps these, so a model is the same under any split)."""
+        E = mc.num_experts
+        subset = not (first == 0 and count == E)
+        n_draw = E if (subset and wi.mode == "sliced") else count
+        if mc.expert_format == "exl3":
+            assert inter_local % 128 == 0, "EXL3 TP cuts must keep whole H128 blocks"
+            ex = random_exl3_experts(n_draw, hid, inter_local, mc.exl3_bits_x2, mc.exl3_codebook, wi, tp, tp_rank,
+                                     mc.swiglu_limit)
+            if n_draw != count:
+                ex = ex.select(first, count)
+            return ex
+        if mc.expert_format == "bf16":
+            ex = BF16Experts(n_draw, hid, inter_local, wi, tp, tp_rank, mc.swiglu_limit)
+            if n_draw != count:
+                ex.gate_up = nn.Parameter(ex.gate_up[first:first + count].contiguous(), requires_grad=False)
+                ex.down = nn.Parameter(ex.down[first:first + count].contiguous(), requires_grad=False)
+            return ex
+        from . import marlin_experts
+
+        ex = marlin_experts.random_marlin_experts(n_draw, hid, inter_local, wi, tp, tp_rank)
+        if n_draw != count:
+            ex = ex.select(first, count)
+        return ex
 
     def forward(self, x: torch.Tensor, reduce: bool = False) -> torch.Tensor:
         """reduce: return the output summed over the tensor-parallel group."""

@@ -34,6 +34,12 @@ class MarlinExperts:
     def num_local(self) -> int:
         return self.gate.shape[0]
 
+    def select(self, first: int, count: int) -> "MarlinExperts":
+        """Experts [first, first + count) (expert-parallel share of a fully drawn layer)."""
+        sl = slice(first, first + count)
+        return dataclasses.replace(self, **{n: getattr(self, n)[sl].contiguous()
+                                            for n in ("gate", "gate_s", "up", "up_s", "down", "down_s")})
+
     def dense(self, which: str, e: int) -> torch.Tensor:
         """Dequantized [K, N] weight of one expert (oracle path)."""
         return fm.unpack(getattr(self, which)[e].cpu(), getattr(self, which + "_s")[e].cpu())

@@ -55,6 +55,14 @@ class Exl3Experts:
                            u["svh"], d["svh"], gate[0].bits_x2, gate[0].codebook, gate[0].in_features,
                            gate[0].out_features, expert_map, swiglu_limit)
 
+    def select(self, first: int, count: int) -> "Exl3Experts":
+        """Experts [first, first + count) (expert-parallel share of a fully drawn layer)."""
+        import dataclasses
+
+        sl = slice(first, first + count)
+        return dataclasses.replace(self, **{f"{w}_{t}": getattr(self, f"{w}_{t}")[sl].contiguous()
+                                            for w in ("gate", "up", "down") for t in ("trellis", "suh", "svh")})
+
     def matrices(self, which: str, e: int) -> fx.Exl3Matrix:
         t = getattr(self, f"{which}_trellis")[e]
         suh, svh = getattr(self, f"{which}_suh")[e], getattr(self, f"{which}_svh")[e]

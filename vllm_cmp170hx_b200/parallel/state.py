@@ -33,6 +33,8 @@ class ParallelState:
     world_cpu_group: object = None
     device: torch.device = field(default_factory=lambda: torch.device("cpu"))
     backend: str = "none"
+    # routed experts split whole across the TP group (expert parallel) instead of by intermediate columns
+    expert_parallel: bool = False
 
     @property
     def is_first_pp(self) -> bool:
