@@ -16,7 +16,7 @@ from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, ParallelConfig,
 PROMPTS = [[(5 * i + 3 * j) % 500 for j in range(9 + 13 * i)] for i in range(3)]
 
 
-def _cfg(tp, fmt):
+def _cfg(tp, fmt, pp=1):
     k = 0
     ep = fmt.endswith("_ep")
     fmt = fmt[:-3] if ep else fmt
@@ -29,20 +29,21 @@ def _cfg(tp, fmt):
         m = tiny(layers=4, experts=4, hidden=256, expert_format=fmt)
         m.moe.intermediate = 256  # two H128 blocks: one per rank at TP=2
         m.moe.shared_intermediate = 256
-    return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp, expert_parallel=ep),
+    return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp, expert_parallel=ep,
+                                                         pipeline_parallel_size=pp),
                         scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256,
                                                   num_speculative_tokens=k),
                         cache=CacheConfig(num_blocks=32), device="cpu", enforce_eager=True)
 
 
-def _generate(tp, fmt):
+def _generate(tp, fmt, pp=1):
     from vllm_cmp170hx_b200.engine.llm_engine import LLM
     from vllm_cmp170hx_b200.engine.request import SamplingParams
     from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
 
     from vllm_cmp170hx_b200.parallel import state as pstate
 
-    cfg = _cfg(tp, fmt)
+    cfg = _cfg(tp, fmt, pp)
     pstate.get().expert_parallel = cfg.parallel.expert_parallel
     model = HybridForCausalLM(cfg.model, "cpu", seed=5, init_mode="sliced")
     outs = LLM(cfg, model).generate(PROMPTS, SamplingParams(max_tokens=6 if cfg.scheduler.num_speculative_tokens else 3))
@@ -72,6 +73,37 @@ def test_tp2_matches_tp1(fmt):
         path = os.path.join(d, "out.json")
         port = 29500 + os.getpid() % 1000
         mp.start_processes(_worker, args=(2, port, fmt, path), nprocs=2, join=True, start_method="spawn")
+        with open(path) as f:
+            got = json.load(f)
+    assert got == ref
+
+
+def _pp_worker(rank, world, port, fmt, tp, path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.init(tp_size=tp, pp_size=world // tp, device="cpu", timeout_s=120)
+    toks = _generate(tp, fmt, world // tp)
+    if rank == 0:
+        with open(path, "w") as f:
+            json.dump(toks, f)
+    pstate.destroy()
+
+
+@pytest.mark.parametrize("fmt,tp", [("exl3", 1), ("deepseek_mtp", 1), ("deepseek_mtp", 2)])
+def test_pp2_matches_pp1(fmt, tp):
+    """Two pipeline stages (packed p2p hops, micro-batches, token / draft broadcast from the last
+    stage) generate the same tokens as one stage; deepseek_mtp adds MTP speculative decoding."""
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    ref = _generate(1, fmt)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.json")
+        port = 28700 + os.getpid() % 1000
+        mp.start_processes(_pp_worker, args=(2 * tp, port, fmt, tp, path), nprocs=2 * tp, join=True,
+                           start_method="spawn")
         with open(path) as f:
             got = json.load(f)
     assert got == ref

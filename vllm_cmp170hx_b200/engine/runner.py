@@ -57,7 +57,8 @@ class ModelRunner:
         self.time_device = False  # record CUDA events around each step's device work
         self.spec = None
         self._pending = None
-        if cfg.scheduler.num_speculative_tokens > 0:
+        self._pp_hidden: list = []
+        if cfg.scheduler.num_speculative_tokens > 0 and self.st.is_last_pp:
             from .spec_decode import SpecDecoder
 
             self.spec = SpecDecoder(self, cfg.scheduler.num_speculative_tokens)
@@ -175,7 +176,9 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ forward + sample
     def _forward_sample(self, ids, ctx, sample_rows, temps, seed):
-        hidden = self.model(ids, ctx)
+        return self._sample_hidden(self.model(ids, ctx), sample_rows, temps, seed)
+
+    def _sample_hidden(self, hidden, sample_rows, temps, seed):
         hs = hidden if sample_rows is None else hidden.index_select(0, sample_rows)
         logits = self.model.compute_logits(hs)
         val, idx = sampling_ops.sample_local(logits, temps, seed, self.step_counter, self.model.vocab_offset)
@@ -189,6 +192,8 @@ class ModelRunner:
     def execute(self, out: SchedulerOutput) -> dict[str, list[int]]:
         if not out.reqs:
             return {}
+        if self.st.pp_size > 1:
+            return self._execute_pp(out)
         if self.spec is not None:
             return self._execute_spec(out)
         use_graph = (not self.cfg.enforce_eager and self.device.type == "cuda" and out.decode_only
@@ -228,6 +233,95 @@ class ModelRunner:
 
     _events = None
 
+    # ------------------------------------------------------------------ pipeline parallel
+    def _micro_batches(self, out: SchedulerOutput) -> list[SchedulerOutput]:
+        """Split the step into up to pp_size micro-batches of consecutive requests with about equal
+        token counts, so stage s works on micro-batch i + 1 while stage s + 1 works on i."""
+        n = min(self.st.pp_size, len(out.reqs))
+        total = out.num_tokens
+        mbs, cur, acc = [], [], 0
+        for s in out.reqs:
+            cur.append(s)
+            acc += s.num_new
+            if len(mbs) < n - 1 and acc >= total * (len(mbs) + 1) / n:
+                mbs.append(SchedulerOutput(reqs=cur))
+                cur = []
+        if cur:
+            mbs.append(SchedulerOutput(reqs=cur))
+        return mbs
+
+    def _execute_pp(self, out: SchedulerOutput) -> dict[str, list[int]]:
+        """One step of this rank's pipeline stage (eager).  The boundary tensors of a micro-batch
+        (hidden and residual) travel as one packed [2, T, H] buffer over NCCL p2p in the stage's TP
+        column (the reference's packed hop, vllm_sm80/worker/pp_hop.py:52); sends are asynchronous so
+        a stage computes its next micro-batch while the previous one is in flight.  Every rank runs
+        the same scheduler, so shapes need no metadata message.  The last stage samples and
+        broadcasts the tokens over the column."""
+        import torch.distributed as dist
+
+        st = self.st
+        m = self.model
+        H = self.mcfg.hidden_size
+        grp = st.pp_group
+        sends, toks, nbytes = [], [], 0
+        verify = {}
+        for mb in self._micro_batches(out):
+            h = self._host_inputs(mb)
+            dev, ctx, nb = self._context(h)
+            nbytes += nb
+            if m.first:
+                res = m(dev["ids"], ctx)
+            else:
+                buf = torch.empty(2, h["T"], H, dtype=torch.bfloat16, device=self.device)
+                dist.recv(buf, src=st.pp_peer(st.pp_rank - 1), group=grp)
+                res = m(None, ctx, (buf[0], buf[1]))
+            if not m.last:
+                x, r = res
+                packed = torch.stack([x, r])
+                sends.append((dist.isend(packed, dst=st.pp_peer(st.pp_rank + 1), group=grp), packed))
+            elif self.spec is not None:
+                rows = self._to_dev(h["sample_rows"])
+                verify.update(self._verify_mb(mb, res, rows))
+                self._pp_hidden.append((mb, res))  # the MTP head catches up over every position
+            else:
+                rows = self._to_dev(h["sample_rows"])
+                toks.append(self._sample_hidden(res, rows, self._sample_temps(mb, h), self.cfg.seed))
+        for w, _ in sends:
+            w.wait()
+        self.step_counter += 1
+        last = st.pp_peer(st.pp_size - 1)
+        if self._spec_enabled_elsewhere():
+            obj = [verify if m.last else None]
+            dist.broadcast_object_list(obj, src=last, group=st.pp_cpu_group)
+            res = obj[0]
+            self._pp_last_out, self._pp_last_res = out, res
+        else:
+            n = sum(1 for s in out.reqs if s.sample)
+            tokens = torch.cat(toks) if m.last and toks else torch.empty(n, dtype=torch.int64, device=self.device)
+            if n:
+                dist.broadcast(tokens, src=last, group=grp)
+            res = self._split_tokens(out, tokens.cpu().tolist())
+        self.last_stats = StepStats(num_tokens=out.num_tokens, graph=False, h2d_bytes=nbytes,
+                                    d2h_bytes=8 * sum(len(v) for v in res.values()))
+        if self.device.type == "cuda":
+            _ext.check_status(self.device)
+        return res
+
+    def _spec_enabled_elsewhere(self) -> bool:
+        return self.cfg.scheduler.num_speculative_tokens > 0
+
+    def _verify_mb(self, mb: SchedulerOutput, hidden, rows) -> dict[str, list[int]]:
+        rows_of, k = {}, 0
+        for s in mb.reqs:
+            if s.sample:
+                n = s.num_new if s.num_draft else 1
+                rows_of[s.req.request_id] = list(range(k, k + n))
+                k += n
+        if not k:
+            return {}
+        logits = self.model.compute_logits(hidden.index_select(0, rows))
+        return self.spec.verify(mb, logits, rows_of)
+
     def _execute_spec(self, out: SchedulerOutput) -> dict[str, list[int]]:
         """Eager target step with draft verification; the hidden states are kept for :meth:`propose`."""
         h = self._host_inputs(out)
@@ -262,12 +356,39 @@ class ModelRunner:
 
     @torch.inference_mode()
     def propose(self) -> None:
-        """Draft tokens for the next step (speculative decoding; after the scheduler update)."""
+        """Draft tokens for the next step (speculative decoding; after the scheduler update).  With
+        pipeline parallelism the last stage drafts and broadcasts the drafts to the other stages."""
+        if self.cfg.scheduler.num_speculative_tokens <= 0:
+            return
+        if self.st.pp_size > 1:
+            import torch.distributed as dist
+
+            drafts = None
+            if self.spec is not None:
+                for mb, hidden in self._pp_hidden:
+                    self.spec.propose(mb, hidden, self._pp_accepted(mb))
+                drafts = {s.req.request_id: list(s.req.draft_token_ids) for mb, _ in self._pp_hidden
+                          for s in mb.reqs}
+            self._pp_hidden = []
+            obj = [drafts]
+            dist.broadcast_object_list(obj, src=self.st.pp_peer(self.st.pp_size - 1), group=self.st.pp_cpu_group)
+            if self.spec is None and self._pp_last_out is not None:
+                for s in self._pp_last_out.reqs:
+                    d = obj[0].get(s.req.request_id)
+                    if d is not None and not s.req.status.finished:
+                        s.req.draft_token_ids = list(d)
+            return
         if self.spec is None or self._pending is None:
             return
         out, hidden, res = self._pending
         self._pending = None
         self.spec.propose(out, hidden, res)
+
+    _pp_last_out = None
+    _pp_last_res: dict = {}
+
+    def _pp_accepted(self, mb) -> dict:
+        return {s.req.request_id: self._pp_last_res.get(s.req.request_id, []) for s in mb.reqs}
 
     def _ev_start(self):
         if not (self.time_device and self.device.type == "cuda"):

@@ -396,7 +396,21 @@ class DecoderLayer(nn.Module):
         return self.mlp(h, reduce=True), residual
 
 
+def stage_layers(num_layers: int, pp_size: int, pp_rank: int) -> tuple[int, int]:
+    """Layers [start, end) of pipeline stage `pp_rank` (contiguous, sizes differ by at most one)."""
+    base, extra = divmod(num_layers, pp_size)
+    start = pp_rank * base + min(pp_rank, extra)
+    return start, start + base + (1 if pp_rank < extra else 0)
+
+
 class HybridForCausalLM(nn.Module):
+    """The decoder stack of one pipeline stage (all of it without pipeline parallelism).
+
+    Stage 0 embeds the tokens; a later stage takes the previous stage's (hidden, residual) pair;
+    the last stage applies the final norm and holds the vocab-parallel LM head.  The last stage
+    also keeps the embedding (the MTP head reads it).  With `sliced` init every layer is drawn
+    and the stage keeps its own, so a model is the same under any split."""
+
     def __init__(self, cfg: ModelConfig, device="cuda", seed: int = 0, init_mode: str = "local"):
         super().__init__()
         st = pstate.get()
@@ -404,21 +418,41 @@ class HybridForCausalLM(nn.Module):
         self.cfg = cfg
         wi = WeightInit(seed, device, init_mode)
         self.init_mode = init_mode
-        self.embed = nn.Parameter(wi.normal((cfg.vocab_size, cfg.hidden_size), 1.0), requires_grad=False)
-        self.layers = nn.ModuleList([DecoderLayer(cfg, i, wi, tp, tp_rank) for i in range(cfg.num_layers)])
-        self.norm = RMSNorm(wi.ones_plus(cfg.hidden_size, 0.05), cfg.rms_eps)
+        self.first, self.last = st.is_first_pp, st.is_last_pp
+        self.layer_start, self.layer_end = stage_layers(cfg.num_layers, st.pp_size, st.pp_rank)
+        embed = wi.normal((cfg.vocab_size, cfg.hidden_size), 1.0) if (self.first or self.last or
+                                                                      init_mode == "sliced") else None
+        self.embed = nn.Parameter(embed, requires_grad=False) if (self.first or self.last) else None
+        layers = []
+        for i in range(cfg.num_layers):
+            local = self.layer_start <= i < self.layer_end
+            if local or init_mode == "sliced":
+                layer = DecoderLayer(cfg, i, wi, tp, tp_rank)
+                if local:
+                    layers.append(layer)
+        self.layers = nn.ModuleList(layers)
+        norm_w = wi.ones_plus(cfg.hidden_size, 0.05)
         assert cfg.vocab_size % tp == 0
         self.vocab_local = cfg.vocab_size // tp
         self.vocab_offset = tp_rank * self.vocab_local
-        self.lm_head = Linear(wi.normal((cfg.vocab_size, cfg.hidden_size), default_std(cfg.hidden_size),
-                                        (0, tp_rank, tp)))
+        head = wi.normal((cfg.vocab_size, cfg.hidden_size), default_std(cfg.hidden_size), (0, tp_rank, tp)) \
+            if (self.last or init_mode == "sliced") else None
+        self.norm = RMSNorm(norm_w, cfg.rms_eps) if self.last else None
+        self.lm_head = Linear(head) if self.last else None
 
-    def forward(self, input_ids: torch.Tensor, ctx: StepContext) -> torch.Tensor:
-        x = self.embed[input_ids]
-        residual = None
+    def forward(self, input_ids: torch.Tensor, ctx: StepContext,
+                hidden_in: tuple[torch.Tensor, torch.Tensor] | None = None):
+        """First stage: token ids; later stages: `hidden_in` = the previous stage's (hidden, residual).
+        Returns the normed final hidden on the last stage, else this stage's (hidden, residual)."""
+        if self.first:
+            x, residual = self.embed[input_ids], None
+        else:
+            x, residual = hidden_in
         for layer in self.layers:
             x, residual = layer(x, residual, ctx)
-        return self.norm(x, residual)
+        if self.last:
+            return self.norm(x, residual)
+        return x, residual
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """This rank's vocab shard of the logits [rows, V / tp] (bf16)."""
@@ -431,7 +465,9 @@ class HybridForCausalLM(nn.Module):
         return (H, 128, 128), (3 * H * 128, 3)
 
     def kda_layer_ids(self):
-        return [i for i, t in enumerate(self.cfg.layer_types) if t == "kda"]
+        """KDA layers of this stage (global indices)."""
+        return [i for i, t in enumerate(self.cfg.layer_types) if t == "kda" and self.layer_start <= i < self.layer_end]
 
     def mla_layer_ids(self):
-        return [i for i, t in enumerate(self.cfg.layer_types) if t == "mla"]
+        """Sparse-MLA layers of this stage (global indices)."""
+        return [i for i, t in enumerate(self.cfg.layer_types) if t == "mla" and self.layer_start <= i < self.layer_end]

@@ -28,11 +28,13 @@ class WeightInit:
         self.dtype = dtype
         self._n = 0
 
-    def _gen(self, device) -> torch.Generator:
+    def _gen(self, device, sharded: bool = False) -> torch.Generator:
+        """Generator of the next draw.  In `local` mode a rank's shard of a split tensor gets its own
+        stream (rank salt); replicated tensors get the same stream on every rank."""
         self._n += 1
         g = torch.Generator(device=device)
         st = pstate.get()
-        salt = 0 if self.mode == "sliced" else 7919 * st.rank
+        salt = 7919 * (st.tp_rank + 1) if (self.mode != "sliced" and sharded) else 0
         g.manual_seed(self.seed * 1000003 + self._n * 9973 + salt)
         return g
 
@@ -49,7 +51,8 @@ class WeightInit:
         if shard is not None:
             d, _, n = shard
             local[d] //= n
-        return (torch.randn(*local, generator=self._gen(self.device), device=self.device) * std).to(dtype)
+        return (torch.randn(*local, generator=self._gen(self.device, shard is not None), device=self.device)
+                * std).to(dtype)
 
     def ones_plus(self, n: int, scale: float = 0.0, dtype=None) -> torch.Tensor:
         t = torch.ones(n) + scale * torch.randn(n, generator=self._gen("cpu"))

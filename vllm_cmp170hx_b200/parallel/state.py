@@ -30,6 +30,7 @@ class ParallelState:
     tp_group: object = None  # device group (NCCL) or None
     tp_cpu_group: object = None  # gloo
     pp_group: object = None
+    pp_cpu_group: object = None  # gloo group of the same ranks as pp_group
     world_cpu_group: object = None
     device: torch.device = field(default_factory=lambda: torch.device("cpu"))
     backend: str = "none"
@@ -43,6 +44,10 @@ class ParallelState:
     @property
     def is_last_pp(self) -> bool:
         return self.pp_rank == self.pp_size - 1
+
+    def pp_peer(self, stage: int) -> int:
+        """Global rank of pipeline stage `stage` in this rank's TP column."""
+        return stage * self.tp_size + self.tp_rank
 
     def tp_ranks(self) -> list[int]:
         base = self.pp_rank * self.tp_size
@@ -98,8 +103,9 @@ def init(tp_size: int = 1, pp_size: int = 1, backend: str | None = None, timeout
     for t in range(tp_size):
         ranks = [p * tp_size + t for p in range(pp_size)]
         g = dist.new_group(ranks, backend=be, timeout=to)
+        gc = dist.new_group(ranks, backend="gloo", timeout=to)
         if t == st.tp_rank:
-            st.pp_group = g
+            st.pp_group, st.pp_cpu_group = g, gc
     set_state(st)
     return st
 
