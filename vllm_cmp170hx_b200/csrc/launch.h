@@ -74,6 +74,11 @@ struct CombineArArgs {
   uint64_t timeout_ns;
 };
 cudaError_t combine_allreduce(const CombineArArgs& a, int blocks, cudaStream_t stream);
+
+// ---------------------------------------------------------------- timing.cu
+cudaError_t timing_stamp(int64_t* ring, const int* cursor, int width, int col, cudaStream_t stream);
+cudaError_t timing_open_row(int64_t* ring, int* cursor, int rows, int width, int64_t* step_counter,
+                            cudaStream_t stream);
 int gemm_bf16_allreduce_fits(int M, int N, int max_ctas, int64_t tile_bytes_cap);
 
 // ---------------------------------------------------------------- norm.cu

@@ -82,6 +82,9 @@ void combine_allreduce_op(const at::Tensor& y, const at::Tensor& slot_of, const 
                           int64_t rank, int64_t world, int64_t flag_off, int64_t data_off, int64_t slot_bytes,
                           at::Tensor& epochs, const at::Tensor& status, double timeout_s);  // fused_comm.cu
 
+void timing_stamp_op(at::Tensor& ring, const at::Tensor& cursor, int64_t col);             // timing.cu
+void timing_open_row_op(at::Tensor& ring, at::Tensor& cursor, at::Tensor& step_counter);  // timing.cu
+
 void dequant_gemm_op(int64_t format, int64_t nmat, const at::Tensor& w0, const c10::optional<at::Tensor>& w1,
                      const at::Tensor& s0, const c10::optional<at::Tensor>& s1, const at::Tensor& b0,
                      const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
@@ -143,6 +146,8 @@ void register_host_bindings(pybind11::module_& m);
   X("gemm_allreduce(Tensor x, Tensor w, Tensor? bias, Tensor(a!) out, Tensor peers, int rank, int world, "  \
     "int flag_off, int data_off, int tile_bytes_cap, int max_ctas, Tensor(b!) epochs, Tensor(c!) status, " \
     "float timeout_s) -> ()")                                                                            \
+  X("timing_stamp(Tensor(a!) ring, Tensor cursor, int col) -> ()")                                      \
+  X("timing_open_row(Tensor(a!) ring, Tensor(b!) cursor, Tensor(c!) step_counter) -> ()")               \
   X("combine_allreduce(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out, " \
     "Tensor peers, int rank, int world, int flag_off, int data_off, int slot_bytes, Tensor(b!) epochs, "    \
     "Tensor(c!) status, float timeout_s) -> ()")
@@ -172,4 +177,6 @@ void register_host_bindings(pybind11::module_& m);
   X("dequant_gemm", b200::dequant_gemm_op)            \
   X("gather_rows", b200::gather_rows_op)              \
   X("gemm_allreduce", b200::gemm_allreduce_op)        \
-  X("combine_allreduce", b200::combine_allreduce_op)
+  X("combine_allreduce", b200::combine_allreduce_op) \
+  X("timing_stamp", b200::timing_stamp_op)            \
+  X("timing_open_row", b200::timing_open_row_op)

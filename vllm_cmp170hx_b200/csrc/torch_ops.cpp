@@ -644,3 +644,25 @@ void combine_allreduce_op(const at::Tensor& y, const at::Tensor& slot_of, const 
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void timing_stamp_op(at::Tensor& ring, const at::Tensor& cursor, int64_t col) {
+  B200_CHECK_CUDA(ring);
+  TORCH_CHECK(ring.scalar_type() == at::kLong && ring.dim() == 2 && ring.is_contiguous(), "timing ring int64 [rows, w]");
+  TORCH_CHECK(cursor.scalar_type() == at::kInt && cursor.is_cuda(), "timing cursor int32");
+  c10::cuda::CUDAGuard g(ring.device());
+  B200_LAUNCH(timing_stamp(ring.data_ptr<int64_t>(), cursor.data_ptr<int>(), (int)ring.size(1), (int)col,
+                           cur_stream()));
+}
+
+void timing_open_row_op(at::Tensor& ring, at::Tensor& cursor, at::Tensor& step_counter) {
+  B200_CHECK_CUDA(ring);
+  TORCH_CHECK(ring.scalar_type() == at::kLong && ring.dim() == 2 && ring.is_contiguous(), "timing ring int64 [rows, w]");
+  TORCH_CHECK(step_counter.scalar_type() == at::kLong && step_counter.is_cuda(), "timing step counter int64");
+  c10::cuda::CUDAGuard g(ring.device());
+  B200_LAUNCH(timing_open_row(ring.data_ptr<int64_t>(), cursor.data_ptr<int>(), (int)ring.size(0), (int)ring.size(1),
+                              step_counter.data_ptr<int64_t>(), cur_stream()));
+}
+
+}  // namespace b200

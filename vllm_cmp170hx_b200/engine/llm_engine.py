@@ -46,9 +46,56 @@ class LLMEngine:
         st.expert_parallel = bool(cfg.parallel.expert_parallel)
         self.runner = ModelRunner(cfg, model)
         self.scheduler = Scheduler(cfg.scheduler, cfg.cache, self.runner.block_pool, self.runner.slot_pool)
+        self._diagnostics(st)
         self.requests: dict[str, Request] = {}
         self.num_steps = 0
         self.eos_token_id: int | None = None
+
+    def _diagnostics(self, st) -> None:
+        from .. import envs
+        from ..utils import memory
+        from ..utils.capture import KernelCapture
+
+        envs.check_environment()
+        if envs.get("VLLM_B200_MEM_ATTRIBUTION"):
+            memory.log_attribution(self.runner.model, st.rank)
+        if envs.get("VLLM_B200_KV_PLAN_LOG"):
+            memory.log_kv_plan(self.runner, st.rank)
+        self.capture = KernelCapture.from_env(st.rank)
+        if self.capture is not None:
+            self.capture.install()
+        envs.log_gate("kernel-call capture", self.capture is not None)
+
+    def profile(self, steps: int, out_dir: str) -> str:
+        """Run `steps` engine steps under the torch profiler and write this rank's chrome trace
+        (plus an execution trace with VLLM_B200_EXECUTION_TRACE; ranks export one after another with
+        VLLM_B200_SERIAL_TRACE_EXPORT).  Returns the trace path."""
+        import contextlib
+        import os
+
+        from torch.profiler import ProfilerActivity, profile as tprofile
+
+        from .. import envs
+        from ..utils import trace
+
+        st = pstate.get()
+        os.makedirs(out_dir, exist_ok=True)
+        stem = os.path.join(out_dir, f"rank{st.rank}")
+        acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if torch.cuda.is_available() else [])
+        et = trace.execution_trace(stem) if envs.get("VLLM_B200_EXECUTION_TRACE") else contextlib.nullcontext()
+        with et, tprofile(activities=acts) as prof:
+            for _ in range(steps):
+                if not self.has_unfinished():
+                    break
+                self.step()
+            if torch.cuda.is_available():
+                torch.cuda.synchronize()
+        path = stem + ".trace.json"
+        if envs.get("VLLM_B200_SERIAL_TRACE_EXPORT") and st.world_size > 1:
+            trace.serial_export(prof, path, st.rank, st.world_size, out_dir)
+        else:
+            prof.export_chrome_trace(path)
+        return path
 
     def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
                     request_id: str | None = None) -> str:

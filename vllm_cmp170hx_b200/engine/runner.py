@@ -55,6 +55,15 @@ class ModelRunner:
         self.graph_pool = None
         self.last_stats = StepStats()
         self.time_device = False  # record CUDA events around each step's device work
+        from .. import envs
+        from ..utils.light_timing import LightTimer
+
+        self.timer = LightTimer.from_env(self.device)
+        if self.timer is not None:
+            self.timer.attach(self.model)
+        envs.log_gate("light timing", self.timer is not None)
+        self._check_indices = bool(envs.get("VLLM_B200_STATE_INDEX_CHECK"))
+        envs.log_gate("state index check", self._check_indices)
         self.spec = None
         self._pending = None
         self._pp_hidden: list = []
@@ -146,8 +155,14 @@ class ModelRunner:
             t += n
         for i in range(S, Sp):  # decode padding rows
             cu[i + 1] = cu[i] + 1
-        return dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
-                    temps=temps, sample_rows=np.asarray(sample_rows, dtype=np.int64), max_ctx=max_ctx, T=Tp, S=Sp)
+        h = dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
+                 temps=temps, sample_rows=np.asarray(sample_rows, dtype=np.int64), max_ctx=max_ctx, T=Tp, S=Sp)
+        if self._check_indices:
+            from ..utils.state_check import check_step
+
+            check_step(h, out, self.num_blocks, self.block_size, self.num_slots if self.slot_pool else 0,
+                       self.cfg.scheduler.max_model_len)
+        return h
 
     def _to_dev(self, a: np.ndarray, out: torch.Tensor | None = None) -> torch.Tensor:
         t = torch.from_numpy(a)
@@ -176,6 +191,8 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ forward + sample
     def _forward_sample(self, ids, ctx, sample_rows, temps, seed):
+        if self.timer is not None:
+            self.timer.open_row()
         return self._sample_hidden(self.model(ids, ctx), sample_rows, temps, seed)
 
     def _sample_hidden(self, hidden, sample_rows, temps, seed):
