@@ -52,3 +52,26 @@ def test_engine_step_outputs(model):
         outs += eng.step()
     fin = [o for o in outs if o.finished]
     assert len(fin) == 1 and fin[0].request_id == rid and fin[0].finish_reason == "length"
+
+
+def test_failed_input_isolation():
+    """A request whose prompt contains a token with a NaN embedding finishes with an error; the
+    other requests in the batch finish normally with the tokens they produce alone."""
+    pstate.set_state(pstate.ParallelState())
+    m = HybridForCausalLM(_cfg().model, "cpu", seed=2, init_mode="sliced")
+    good = [[(5 * j + 1) % 400 for j in range(20)], [(7 * j + 3) % 400 for j in range(33)]]
+    alone = [o.output_token_ids for o in LLM(_cfg(), m).generate(good, SamplingParams(max_tokens=4))]
+    m.embed.data[450] = float("nan")
+    bad = [11, 12, 450, 13]
+    outs = LLM(_cfg(), m).generate([good[0], bad, good[1]], SamplingParams(max_tokens=4))
+    assert outs[1].finish_reason == "error" and outs[1].output_token_ids == []
+    assert [outs[0].output_token_ids, outs[2].output_token_ids] == alone
+
+
+def test_warmup_leaves_pools_free(model):
+    eng = LLMEngine(_cfg(), model)
+    free = eng.runner.block_pool.num_free()
+    eng.warmup()
+    assert eng.runner.block_pool.num_free() == free
+    out = eng.step()  # nothing scheduled
+    assert out == [] and not eng.has_unfinished()

@@ -246,21 +246,37 @@ def main(argv=None):
     ap.add_argument("--prefill-chunk-with-decodes", action="store_true", default=True)
     ap.add_argument("--max-num-partial-prefills", type=int, default=1)
     ap.add_argument("--device", default="cuda")
+    ap.add_argument("--pp", type=int, default=1, help="pipeline-parallel stages")
+    ap.add_argument("--enable-expert-parallel", action="store_true", help="routed experts split whole over TP")
+    ap.add_argument("--num-speculative-tokens", type=int, default=0, help="MTP draft tokens per step")
+    ap.add_argument("--enforce-eager", action="store_true", help="no CUDA graphs")
+    ap.add_argument("--nccl-collectives", action="store_true", help="TP collectives on NCCL (baseline path)")
+    ap.add_argument("--no-warmup", action="store_true")
     args = ap.parse_args(argv)
 
     from ..parallel import state as pstate
     from ..registry import resolve
 
-    st = pstate.init(tp_size=args.tp, device=args.device)
+    st = pstate.init(tp_size=args.tp, pp_size=args.pp, device=args.device)
     mcfg, _ckpt = resolve(args.model)
-    cfg = EngineConfig(model=mcfg, parallel=ParallelConfig(tensor_parallel_size=args.tp),
+    cfg = EngineConfig(model=mcfg,
+                       parallel=ParallelConfig(tensor_parallel_size=args.tp, pipeline_parallel_size=args.pp,
+                                               expert_parallel=args.enable_expert_parallel,
+                                               fused_comm=not args.nccl_collectives),
                        scheduler=SchedulerConfig(max_num_seqs=args.max_num_seqs,
                                                  max_num_batched_tokens=args.max_num_batched_tokens,
                                                  max_model_len=args.max_model_len,
                                                  prefill_chunk_with_decodes=args.prefill_chunk_with_decodes,
-                                                 max_num_partial_prefills=args.max_num_partial_prefills),
-                       cache=CacheConfig(), device=args.device)
+                                                 max_num_partial_prefills=args.max_num_partial_prefills,
+                                                 num_speculative_tokens=args.num_speculative_tokens),
+                       cache=CacheConfig(), device=args.device, enforce_eager=args.enforce_eager)
     engine = LLMEngine(cfg)
+    if st.tp_size > 1 and not args.nccl_collectives:
+        from ..parallel import symm
+
+        symm.enable_for_engine(engine)
+    if not args.no_warmup:
+        engine.warmup()
     tok = get_tokenizer(args.tokenizer, mcfg.vocab_size)
     engine.eos_token_id = getattr(tok, "eos_token_id", None)
     spmd = SPMDEngine(engine)

@@ -66,6 +66,18 @@ class LLMEngine:
             self.capture.install()
         envs.log_gate("kernel-call capture", self.capture is not None)
 
+    def warmup(self, capture_graphs: bool = True) -> dict[int, int]:
+        """Kernel warm-up (one throwaway prefill + decode) and, on the GPU, capture of every decode
+        graph; returns the bytes each graph capture kept (logged).  Every rank calls it at start-up."""
+        import logging
+
+        self.runner.warmup()
+        kept = self.runner.capture_graphs() if capture_graphs else {}
+        if kept:
+            logging.getLogger("vllm_cmp170hx_b200").info(
+                "CUDA graphs captured: %s", ", ".join(f"batch {b}: {v / 2**20:.1f} MiB" for b, v in kept.items()))
+        return kept
+
     def profile(self, steps: int, out_dir: str) -> str:
         """Run `steps` engine steps under the torch profiler and write this rank's chrome trace
         (plus an execution trace with VLLM_B200_EXECUTION_TRACE; ranks export one after another with

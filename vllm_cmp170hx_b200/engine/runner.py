@@ -26,6 +26,7 @@ from ..ops import sampling as sampling_ops
 from ..parallel import comm
 from ..parallel import state as pstate
 from .block_pool import SlotPool, make_block_pool
+from .failed_inputs import sanitize, sanitize_dict
 from .scheduler import SchedulerOutput
 
 
@@ -246,7 +247,7 @@ class ModelRunner:
         self.last_stats = stats
         if self.device.type == "cuda":
             _ext.check_status(self.device)
-        return self._split_tokens(out, host)
+        return self._split_tokens(out, sanitize(host, self.mcfg.vocab_size))
 
     _events = None
 
@@ -317,7 +318,7 @@ class ModelRunner:
             tokens = torch.cat(toks) if m.last and toks else torch.empty(n, dtype=torch.int64, device=self.device)
             if n:
                 dist.broadcast(tokens, src=last, group=grp)
-            res = self._split_tokens(out, tokens.cpu().tolist())
+            res = self._split_tokens(out, sanitize(tokens.cpu().tolist(), self.mcfg.vocab_size))
         self.last_stats = StepStats(num_tokens=out.num_tokens, graph=False, h2d_bytes=nbytes,
                                     d2h_bytes=8 * sum(len(v) for v in res.values()))
         if self.device.type == "cuda":
@@ -337,7 +338,7 @@ class ModelRunner:
         if not k:
             return {}
         logits = self.model.compute_logits(hidden.index_select(0, rows))
-        return self.spec.verify(mb, logits, rows_of)
+        return sanitize_dict(self.spec.verify(mb, logits, rows_of), self.mcfg.vocab_size)
 
     def _execute_spec(self, out: SchedulerOutput) -> dict[str, list[int]]:
         """Eager target step with draft verification; the hidden states are kept for :meth:`propose`."""
@@ -357,7 +358,7 @@ class ModelRunner:
         res = {}
         if k:
             logits = self.model.compute_logits(hidden.index_select(0, self._to_dev(h["sample_rows"])))
-            res = self.spec.verify(out, logits, rows_of)
+            res = sanitize_dict(self.spec.verify(out, logits, rows_of), self.mcfg.vocab_size)
         self._ev_end(ev)
         self.step_counter += 1
         stats = StepStats(num_tokens=out.num_tokens, graph=False, h2d_bytes=nbytes,
@@ -485,6 +486,62 @@ class ModelRunner:
             ids_out = self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed)
         torch.cuda.synchronize(dev)
         self.graphs[B] = (g, bufs, ids_out)
+
+    def capture_graphs(self) -> dict[int, int]:
+        """Capture the decode graph of every configured batch size up front and return the device
+        bytes each capture kept (growth of the allocator's reserved memory across the capture; the
+        graphs share one pool, so later sizes reuse what earlier ones reserved).  The reference
+        measures the same quantity to split its graph-memory budget
+        (vllm_sm80/worker/cudagraph_mem.py:202-284)."""
+        kept = {}
+        if self.device.type != "cuda" or self.cfg.enforce_eager or self.st.pp_size > 1:
+            return kept
+        for B in sorted(self.cfg.cuda_graph_batch_sizes):
+            if B in self.graphs or B > self.cfg.scheduler.max_num_seqs:
+                continue
+            torch.cuda.synchronize(self.device)
+            before = torch.cuda.memory_reserved(self.device)
+            self._capture(B)
+            torch.cuda.synchronize(self.device)
+            kept[B] = torch.cuda.memory_reserved(self.device) - before
+        return kept
+
+    @torch.inference_mode()
+    def warmup(self) -> None:
+        """Run one prefill and one decode step of a throwaway request through every kernel family
+        the model uses, before any graph is captured or request served: per-kernel attributes, the
+        status word and cached work items are set up outside capture (the reference's kernel
+        warm-up driver, vllm_sm80/kernels/warmup.py:38)."""
+        from .request import Request, SamplingParams
+        from .scheduler import ScheduledReq
+
+        n = max(2, min(64, self.cfg.scheduler.max_model_len // 2))
+        req = Request(list(range(1, n + 1)), SamplingParams(max_tokens=2), request_id="__warmup__")
+        need = (n + 2 + self.block_size - 1) // self.block_size
+        if self.block_pool.num_free() < need:
+            return
+        req.block_ids = [int(b) for b in self.block_pool.allocate(need)]
+        if self.slot_pool is not None:
+            req.kda_slot = self.slot_pool.allocate()
+        try:
+            saved = self.cfg.enforce_eager
+            self.cfg.enforce_eager = True
+            try:
+                self.execute(SchedulerOutput(reqs=[ScheduledReq(req, n, 0, True)]))
+                req.output_token_ids.append(1)
+                req.num_computed_tokens = n
+                self.execute(SchedulerOutput(reqs=[ScheduledReq(req, 1, n, True)]))
+            finally:
+                self.cfg.enforce_eager = saved
+        finally:
+            self.block_pool.free(req.block_ids)
+            if self.slot_pool is not None and req.kda_slot > 0:
+                self.slot_pool.free(req.kda_slot)
+            self._pending = None
+            if self.spec is not None:
+                self.spec.q_store.clear()
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
 
     def release_graphs(self):
         self.graphs.clear()

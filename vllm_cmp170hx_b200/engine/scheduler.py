@@ -23,6 +23,7 @@ import time
 from dataclasses import dataclass, field
 
 from ..config import CacheConfig, SchedulerConfig
+from .failed_inputs import FAILED_TOKEN
 from .request import Request, Status
 
 
@@ -196,6 +197,12 @@ class Scheduler:
             if req.status.finished:
                 continue
             toks = sampled.get(req.request_id, [])
+            if FAILED_TOKEN in toks:
+                # no valid token from this step (poisoned inputs): finish with an error, drop the step
+                req.status = Status.FINISHED_ERROR
+                req.draft_token_ids = []
+                done.append(req)
+                continue
             if s.num_draft:
                 # verify step: positions of rejected drafts are recomputed later
                 accepted = max(0, len(toks) - 1)

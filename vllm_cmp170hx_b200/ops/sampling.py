@@ -13,7 +13,8 @@ def sample_local(logits: torch.Tensor, temperature: torch.Tensor | None, seed: i
     Greedy rows (temperature <= 0) take the argmax; others the Gumbel-max sample."""
     rows = logits.shape[0]
     if not logits.is_cuda:
-        x = logits.float()
+        # as the kernel: NaN never wins; a row without any finite winner reports index 2^31 - 1
+        x = torch.nan_to_num(logits.float(), nan=float("-inf"))
         if temperature is not None:
             g = torch.Generator().manual_seed(int(seed) + int(step.item() if step is not None else 0))
             u = torch.rand(x.shape, generator=g).clamp_(1e-12, 1 - 1e-7)
@@ -21,6 +22,7 @@ def sample_local(logits: torch.Tensor, temperature: torch.Tensor | None, seed: i
             noisy = x / t.clamp_min(1e-6) - torch.log(-torch.log(u))
             x = torch.where(t > 0, noisy, x)
         v, i = x.max(dim=-1)  # torch.max returns the first maximal index
+        i = torch.where(torch.isneginf(v), torch.full_like(i, 2**31 - 1 - vocab_offset), i)
         return v, (i + vocab_offset).int()
     val = torch.empty(rows, dtype=torch.float32, device=logits.device)
     idx = torch.empty(rows, dtype=torch.int32, device=logits.device)
