@@ -122,3 +122,27 @@ def test_rejection_sampling_preserves_target_distribution():
         counts[res["r"][0]] += 1
     emp = counts / N
     assert np.abs(emp - p.numpy()).max() < 0.025, (emp, p.numpy())
+
+
+def test_adaptive_k_policies():
+    from vllm_cmp170hx_b200.engine.adaptive_k import AdaptiveKPolicy, expected_tokens
+
+    p = AdaptiveKPolicy(3)
+    assert [p.choose(n) for n in (1, 8, 20, 100, 1000)] == [3, 3, 2, 1, 1]
+    assert abs(expected_tokens(3, 0.5) - 1.875) < 1e-9 and expected_tokens(2, 1.0) == 3
+    a = AdaptiveKPolicy(3, mode="accept")
+    a.accept_rate = 0.9
+    assert a.choose(1) == 3  # cheap drafts, high acceptance: full depth
+    a.accept_rate = 0.05
+    for _ in range(3):
+        k = a.choose(400)  # compute-bound batch, drafts rarely accepted: no drafts
+    assert k == 0
+
+
+def test_greedy_spec_with_adaptive_k_matches_plain(model):
+    ref = _plain(model)
+    cfg = _cfg(k=3)
+    cfg.scheduler.adaptive_k = "by_load"
+    llm = LLM(cfg, model)
+    got = [o.output_token_ids for o in llm.generate(PROMPTS, [SamplingParams(max_tokens=m) for m in MAX_TOKENS])]
+    assert got == ref and llm.engine.scheduler.draft_cap == 3

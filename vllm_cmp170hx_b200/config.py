@@ -225,7 +225,7 @@ class SchedulerConfig:
     max_num_partial_prefills: int = 1
     long_prefill_token_threshold: int = 0
     num_speculative_tokens: int = 0
-    adaptive_k: bool = False
+    adaptive_k: str = ""  # '' off, 'by_load', 'accept' (load-adaptive draft count)
 
 
 @dataclass

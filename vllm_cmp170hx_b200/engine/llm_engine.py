@@ -47,6 +47,18 @@ class LLMEngine:
         self.runner = ModelRunner(cfg, model)
         self.scheduler = Scheduler(cfg.scheduler, cfg.cache, self.runner.block_pool, self.runner.slot_pool)
         self._diagnostics(st)
+        self.adaptive_k = None
+        self._k_seen = (0, 0)
+        mode = cfg.scheduler.adaptive_k or ""
+        if not mode:
+            from .. import envs
+
+            mode = envs.get("VLLM_B200_ADAPTIVE_K")
+        if mode and cfg.scheduler.num_speculative_tokens > 0:
+            from .adaptive_k import AdaptiveKPolicy
+
+            self.adaptive_k = AdaptiveKPolicy(cfg.scheduler.num_speculative_tokens,
+                                              mode if mode in ("by_load", "accept") else "by_load")
         self.requests: dict[str, Request] = {}
         self.num_steps = 0
         self.eos_token_id: int | None = None
@@ -124,6 +136,13 @@ class LLMEngine:
         return self.scheduler.has_work()
 
     def step(self) -> list[RequestOutput]:
+        if self.adaptive_k is not None:
+            spec = self.runner.spec
+            if spec is not None:
+                st = spec.stats
+                self.adaptive_k.observe(st["proposed"] - self._k_seen[0], st["accepted"] - self._k_seen[1])
+                self._k_seen = (st["proposed"], st["accepted"])
+            self.scheduler.draft_cap = self.adaptive_k.choose(len(self.scheduler.running))
         out = self.scheduler.schedule()
         if not out.reqs:
             return []

@@ -61,6 +61,7 @@ class Scheduler:
         self.finished: list[Request] = []
         # speculative decoding: KV blocks reserved past a sampling step for the drafter's own cache writes
         self.lookahead = max(0, sched.num_speculative_tokens - 1)
+        self.draft_cap = sched.num_speculative_tokens  # drafts verified per request this step (adaptive k)
 
     # ------------------------------------------------------------------ API
     def add(self, req: Request) -> None:
@@ -135,7 +136,7 @@ class Scheduler:
                 n = min(remaining, budget, cap)
                 drafts = 0
             else:
-                drafts = min(len(req.draft_token_ids), max(0, budget - 1))
+                drafts = min(len(req.draft_token_ids), max(0, budget - 1), self.draft_cap)
                 n = 1 + drafts
             if n <= 0 or n > budget:
                 i += 1
