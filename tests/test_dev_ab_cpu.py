@@ -1,0 +1,35 @@
+"""Dev A/B switches and hot swaps flip implementations between steps; greedy outputs agree."""
+
+import pytest
+
+from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, SchedulerConfig, tiny
+from vllm_cmp170hx_b200.dev.ab import DevAB, HotSwap
+from vllm_cmp170hx_b200.engine.llm_engine import LLM
+from vllm_cmp170hx_b200.engine.request import SamplingParams
+from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+from vllm_cmp170hx_b200.parallel import state as pstate
+
+
+def _cfg():
+    return EngineConfig(model=tiny(layers=2, experts=4, expert_format="bf16"),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=256),
+                        cache=CacheConfig(num_blocks=24), device="cpu", enforce_eager=True)
+
+
+def test_switch_flip_and_hot_swap():
+    pstate.set_state(pstate.ParallelState())
+    m = HybridForCausalLM(_cfg().model, "cpu", seed=4)
+    prompts = [list(range(3, 30)), list(range(40, 52))]
+    ref = [o.output_token_ids for o in LLM(_cfg(), m).generate(prompts, SamplingParams(max_tokens=4))]
+    llm = LLM(_cfg(), m)
+    ab = DevAB(llm.engine, "attention_splits")
+    assert ab.flip() == "b" and ab.flip() == "a"
+    with pytest.raises(KeyError):
+        DevAB(llm.engine, "nope")
+    hs = HotSwap(["gemm:torch"])
+    hs.swap_in()
+    try:
+        got = [o.output_token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=4))]
+    finally:
+        hs.swap_out()
+    assert got == ref

@@ -77,6 +77,14 @@ class LLMEngine:
         if self.capture is not None:
             self.capture.install()
         envs.log_gate("kernel-call capture", self.capture is not None)
+        from ..dev.ab import DevAB, HotSwap
+
+        self.dev_ab = DevAB.from_env(self)
+        self.hot_swap = HotSwap.from_env()
+        if self.hot_swap is not None:
+            self.hot_swap.swap_in()
+        envs.log_gate("dev A/B switch", self.dev_ab is not None)
+        envs.log_gate("hot swap", self.hot_swap is not None)
 
     def warmup(self, capture_graphs: bool = True) -> dict[int, int]:
         """Kernel warm-up (one throwaway prefill + decode) and, on the GPU, capture of every decode

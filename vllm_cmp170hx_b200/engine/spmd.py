@@ -21,6 +21,7 @@ class Control:
     new: list[tuple[str, list[int], SamplingParams]] = field(default_factory=list)
     aborts: list[str] = field(default_factory=list)
     stop: bool = False
+    ab_flip: bool = False  # flip the dev A/B switch before this step (every rank at the same step)
 
 
 class SPMDEngine:
@@ -42,6 +43,8 @@ class SPMDEngine:
             self.engine.add_request(prompt, params, rid)
         for rid in ctl.aborts:
             self.engine.abort_request(rid)
+        if ctl.ab_flip and self.engine.dev_ab is not None:
+            self.engine.dev_ab.flip()
         if ctl.stop:
             return []
         return self.engine.step() if self.engine.has_unfinished() else []
@@ -53,6 +56,8 @@ class SPMDEngine:
                 self.engine.add_request(prompt, params, rid)
             for rid in ctl.aborts:
                 self.engine.abort_request(rid)
+            if ctl.ab_flip and self.engine.dev_ab is not None:
+                self.engine.dev_ab.flip()
             if ctl.stop:
                 return
             if self.engine.has_unfinished():
