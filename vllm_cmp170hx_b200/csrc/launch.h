@@ -75,6 +75,10 @@ struct CombineArArgs {
 };
 cudaError_t combine_allreduce(const CombineArArgs& a, int blocks, cudaStream_t stream);
 
+// ---------------------------------------------------------------- rows.cu
+cudaError_t dequant_rows_e4m3(const void* rows, int64_t row_bytes, int D, const uint8_t* failed, void* out, int n,
+                              cudaStream_t stream);
+
 // ---------------------------------------------------------------- timing.cu
 cudaError_t timing_stamp(int64_t* ring, const int* cursor, int width, int col, cudaStream_t stream);
 cudaError_t timing_open_row(int64_t* ring, int* cursor, int rows, int width, int64_t* step_counter,

@@ -82,6 +82,8 @@ void combine_allreduce_op(const at::Tensor& y, const at::Tensor& slot_of, const 
                           int64_t rank, int64_t world, int64_t flag_off, int64_t data_off, int64_t slot_bytes,
                           at::Tensor& epochs, const at::Tensor& status, double timeout_s);  // fused_comm.cu
 
+void dequant_rows_op(const at::Tensor& rows, int64_t D, const c10::optional<at::Tensor>& failed,
+                     at::Tensor& out);  // rows.cu
 void timing_stamp_op(at::Tensor& ring, const at::Tensor& cursor, int64_t col);             // timing.cu
 void timing_open_row_op(at::Tensor& ring, at::Tensor& cursor, at::Tensor& step_counter);  // timing.cu
 
@@ -146,6 +148,7 @@ void register_host_bindings(pybind11::module_& m);
   X("gemm_allreduce(Tensor x, Tensor w, Tensor? bias, Tensor(a!) out, Tensor peers, int rank, int world, "  \
     "int flag_off, int data_off, int tile_bytes_cap, int max_ctas, Tensor(b!) epochs, Tensor(c!) status, " \
     "float timeout_s) -> ()")                                                                            \
+  X("dequant_rows(Tensor rows, int D, Tensor? failed, Tensor(a!) out) -> ()")                           \
   X("timing_stamp(Tensor(a!) ring, Tensor cursor, int col) -> ()")                                      \
   X("timing_open_row(Tensor(a!) ring, Tensor(b!) cursor, Tensor(c!) step_counter) -> ()")               \
   X("combine_allreduce(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out, " \
@@ -179,4 +182,5 @@ void register_host_bindings(pybind11::module_& m);
   X("gemm_allreduce", b200::gemm_allreduce_op)        \
   X("combine_allreduce", b200::combine_allreduce_op) \
   X("timing_stamp", b200::timing_stamp_op)            \
+  X("dequant_rows", b200::dequant_rows_op)            \
   X("timing_open_row", b200::timing_open_row_op)

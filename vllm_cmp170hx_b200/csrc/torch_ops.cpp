@@ -666,3 +666,22 @@ void timing_open_row_op(at::Tensor& ring, at::Tensor& cursor, at::Tensor& step_c
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void dequant_rows_op(const at::Tensor& rows, int64_t D, const c10::optional<at::Tensor>& failed, at::Tensor& out) {
+  B200_CHECK_CUDA(rows);
+  TORCH_CHECK(rows.scalar_type() == at::kByte && rows.dim() == 2 && rows.is_contiguous(), "rows: uint8 [n, row_bytes]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(0) == rows.size(0) &&
+                  out.size(1) == D,
+              "out: bf16 [n, D]");
+  if (failed.has_value())
+    TORCH_CHECK(failed->scalar_type() == at::kByte && failed->is_cuda() && failed->numel() == rows.size(0),
+                "failed: device uint8 [n]");
+  c10::cuda::CUDAGuard g(rows.device());
+  B200_LAUNCH(dequant_rows_e4m3(rows.data_ptr(), rows.size(1), (int)D,
+                                failed.has_value() ? failed->data_ptr<uint8_t>() : nullptr, out.data_ptr(),
+                                (int)rows.size(0), cur_stream()));
+}
+
+}  // namespace b200
