@@ -96,3 +96,38 @@ def test_full_layer_semantics():
     for slot in (3, 1, 0):
         assert (st[slot].cpu() - st_r[slot]).abs().max() < 1e-3
         assert torch.equal(cs[slot].cpu(), cs_r[slot])
+
+
+def test_verify_records_and_recover_match_prefix():
+    """A verify call over k+1 tokens leaves the state untouched; recovering n tokens gives bitwise the
+    state (and conv window) of running only those n tokens."""
+    from vllm_cmp170hx_b200.ops import kda as kda_ops
+
+    torch.manual_seed(3)
+    H, T = 2, 4
+    dev = "cuda"
+    qkv = (torch.randn(T, 3 * H * 128, device=dev) * 0.5).to(torch.bfloat16)
+    g_raw = torch.randn(T, H * 128, device=dev).to(torch.bfloat16)
+    beta = torch.randn(T, H, device=dev).to(torch.bfloat16)
+    g2 = torch.randn(T, H * 128, device=dev).to(torch.bfloat16)
+    conv_w = (torch.randn(3 * H * 128, 4, device=dev) * 0.5).to(torch.bfloat16)
+    a_log = torch.randn(H, device=dev)
+    norm_w = torch.ones(128, device=dev, dtype=torch.bfloat16)
+    st0 = torch.randn(2, H, 128, 128, device=dev) * 0.1
+    cv0 = torch.randn(2, 3 * H * 128, 3, device=dev).to(torch.bfloat16)
+    cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    sidx = torch.tensor([1], dtype=torch.int32, device=dev)
+    init = torch.ones(1, dtype=torch.int32, device=dev)
+    for n in (1, 2, 4):
+        st, cv = st0.clone(), cv0.clone()
+        recs = kda_ops.KdaRecords()
+        kda_ops.kda_forward(qkv, g_raw, beta, g2, cu, sidx, init, cv, conv_w, None, a_log, None, -5.0, norm_w, st,
+                            verify=torch.ones(1, dtype=torch.int32, device=dev), records=recs)
+        assert torch.equal(st, st0) and torch.equal(cv, cv0)
+        kda_ops.kda_recover(recs, torch.tensor([n], dtype=torch.int32), st, cv)
+        st_ref, cv_ref = st0.clone(), cv0.clone()
+        cu_n = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        kda_ops.kda_forward(qkv[:n], g_raw[:n], beta[:n], g2[:n], cu_n, sidx, init, cv_ref, conv_w, None, a_log, None,
+                            -5.0, norm_w, st_ref)
+        assert torch.equal(st, st_ref), n
+        assert torch.equal(cv, cv_ref), n

@@ -146,3 +146,44 @@ def test_greedy_spec_with_adaptive_k_matches_plain(model):
     llm = LLM(cfg, model)
     got = [o.output_token_ids for o in llm.generate(PROMPTS, [SamplingParams(max_tokens=m) for m in MAX_TOKENS])]
     assert got == ref and llm.engine.scheduler.draft_cap == 3
+
+
+def _hybrid_cfg(k=0):
+    from vllm_cmp170hx_b200.config import tiny
+
+    m = tiny(layers=4, experts=4, expert_format="bf16", layer_types=["kda", "mla", "kda", "kda"])
+    return EngineConfig(model=m, scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=256,
+                                                           num_speculative_tokens=k),
+                        cache=CacheConfig(num_blocks=48), device="cpu", enforce_eager=True)
+
+
+@pytest.mark.parametrize("mode", ["mtp", "oracle", "half"])
+def test_hybrid_kda_spec_matches_plain(mode, monkeypatch):
+    """Speculative decoding through KDA layers: the verify step records the recurrence updates and
+    the recovery applies only the accepted prefix, so greedy output equals plain decoding."""
+    pstate.set_state(pstate.ParallelState())
+    m = HybridForCausalLM(_hybrid_cfg().model, "cpu", seed=6)
+    params = [SamplingParams(max_tokens=n) for n in MAX_TOKENS]
+    ref = [o.output_token_ids for o in LLM(_hybrid_cfg(), m).generate(PROMPTS, params)]
+    if mode != "mtp":
+        by_prompt = {tuple(p): r for p, r in zip(PROMPTS, ref)}
+
+        def planted(self, out, hidden, accepted):
+            for s in out.reqs:
+                req = s.req
+                if req.status.finished or req.num_computed_tokens != req.num_tokens - 1:
+                    continue
+                n = len(req.output_token_ids)
+                d = list(by_prompt[tuple(req.prompt_token_ids)][n:n + self.k])
+                if mode == "half":
+                    d = [t if i % 2 == 0 else (t + 1) % 500 for i, t in enumerate(d)]
+                req.draft_token_ids = d[:max(0, min(self.k, req.params.max_tokens - n - 1))]
+
+        monkeypatch.setattr(spec_decode.SpecDecoder, "propose", planted)
+    llm = LLM(_hybrid_cfg(k=3), m)
+    got = [o.output_token_ids for o in llm.generate(PROMPTS, params)]
+    assert got == ref
+    st = llm.engine.runner.spec.stats
+    assert st["proposed"] > 0
+    if mode == "oracle":
+        assert st["accepted"] == st["proposed"]

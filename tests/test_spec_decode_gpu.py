@@ -93,3 +93,40 @@ def test_sampled_spec(model):
     llm = LLM(_cfg("cuda", k=3), model)
     got = llm.generate(PROMPTS, [SamplingParams(max_tokens=m, temperature=0.7) for m in MAX_TOKENS])
     assert [len(o.output_token_ids) for o in got] == MAX_TOKENS
+
+
+def _hybrid_cfg(k=0, eager=False):
+    from vllm_cmp170hx_b200.config import tiny
+
+    m = tiny(layers=4, experts=8, layer_types=["kda", "mla", "kda", "kda"])
+    return EngineConfig(model=m, scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=256,
+                                                           max_model_len=512, num_speculative_tokens=k),
+                        cache=CacheConfig(num_blocks=40), device="cuda", enforce_eager=eager,
+                        cuda_graph_batch_sizes=[1, 2, 4])
+
+
+@pytest.mark.parametrize("planted", [False, True])
+def test_hybrid_kda_spec_matches_plain(planted, monkeypatch):
+    """Verify steps through the KDA kernel record (u, k, decay) per token; the recover kernel applies
+    the accepted prefix: greedy speculative output equals plain decoding on the GPU."""
+    pstate.set_state(pstate.ParallelState())
+    m = HybridForCausalLM(_hybrid_cfg().model, "cuda", seed=12)
+    params = [SamplingParams(max_tokens=n) for n in MAX_TOKENS]
+    ref = [o.output_token_ids for o in LLM(_hybrid_cfg(), m).generate(PROMPTS, params)]
+    if planted:
+        by_prompt = {tuple(p): r for p, r in zip(PROMPTS, ref)}
+
+        def oracle(self, out, hidden, accepted):
+            for s in out.reqs:
+                req = s.req
+                if req.status.finished or req.num_computed_tokens != req.num_tokens - 1:
+                    continue
+                n = len(req.output_token_ids)
+                d = list(by_prompt[tuple(req.prompt_token_ids)][n:n + self.k])
+                d = [t if i != 1 else (t + 1) % 500 for i, t in enumerate(d)]  # reject the second draft
+                req.draft_token_ids = d[:max(0, min(self.k, req.params.max_tokens - n - 1))]
+
+        monkeypatch.setattr(spec_decode.SpecDecoder, "propose", oracle)
+    llm = LLM(_hybrid_cfg(k=3), m)
+    got = [o.output_token_ids for o in llm.generate(PROMPTS, params)]
+    assert got == ref

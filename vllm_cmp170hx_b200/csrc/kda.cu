@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(kThreads) kda_recurrent_kernel(KdaArgs p) {
   const int t0 = p.cu_seqlens[seq], t1 = p.cu_seqlens[seq + 1];
   const int slot = p.state_idx ? p.state_idx[seq] : seq;
   const bool has_init = p.has_init ? (p.has_init[seq] != 0) : true;
+  const bool verify = p.verify != nullptr && p.verify[seq] != 0 && p.rec != nullptr;
   const int HD = p.H * D;
 
   __shared__ __align__(16) float raw_s[3][D];  // q, k, v of the current token (post conv+silu)
@@ -130,6 +131,11 @@ __global__ void __launch_bounds__(kThreads) kda_recurrent_kernel(KdaArgs p) {
       kn = rsqrtf(sk + p.l2_eps);
     }
     const float beta = beta_s;
+    if (verify && tid < D) {  // the token's normalised key and decay (what the recurrence applies)
+      float* r = p.rec + ((int64_t)t * p.H + h) * 3 * D;
+      r[D + tid] = raw_s[1][tid] * kn;
+      r[2 * D + tid] = e_s[tid];
+    }
     float kk[4][4], qq[4][4], ee[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -155,6 +161,7 @@ __global__ void __launch_bounds__(kThreads) kda_recurrent_kernel(KdaArgs p) {
       kv += __shfl_xor_sync(0xffffffffu, kv, 2);
       kv += __shfl_xor_sync(0xffffffffu, kv, 4);
       const float u = (raw_s[2][row] - kv) * beta;
+      if (verify && cg == 0) p.rec[(((int64_t)t * p.H + h) * 3 + 0) * D + row] = u;
       float o = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j)
@@ -192,6 +199,7 @@ __global__ void __launch_bounds__(kThreads) kda_recurrent_kernel(KdaArgs p) {
   }
 
   // ------------------------------------------------------------------ write back
+  if (verify) return;  // kda_recover applies the accepted prefix later
 #pragma unroll
   for (int gi = 0; gi < 2; ++gi) {
     const int row = warp * 8 + gi * 4 + rs;
@@ -208,7 +216,84 @@ __global__ void __launch_bounds__(kThreads) kda_recurrent_kernel(KdaArgs p) {
   }
 }
 
+// S <- S * e_t + u_t k_t^T for the first keep[s] recorded tokens (the same per-element operations,
+// in the same order, as the recurrence itself, so the result equals having run only those tokens),
+// then the conv window advanced past them.
+__global__ void __launch_bounds__(kThreads) kda_recover_kernel(KdaRecoverArgs p) {
+  const int seq = blockIdx.x / p.H;
+  const int h = blockIdx.x % p.H;
+  const int n = p.keep[seq];
+  if (n <= 0) return;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int rs = lane >> 3, cg = lane & 7;
+  const int t0 = p.cu_seqlens[seq];
+  const int slot = p.state_idx ? p.state_idx[seq] : seq;
+  float* S = p.state + ((int64_t)slot * p.H + h) * D * D;
+  float st[2][4][4];
+#pragma unroll
+  for (int gi = 0; gi < 2; ++gi) {
+    const int row = warp * 8 + gi * 4 + rs;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(S + row * D + j * 32 + cg * 4);
+      st[gi][j][0] = v.x;
+      st[gi][j][1] = v.y;
+      st[gi][j][2] = v.z;
+      st[gi][j][3] = v.w;
+    }
+  }
+  for (int t = t0; t < t0 + n; ++t) {
+    const float* r = p.rec + ((int64_t)t * p.H + h) * 3 * D;
+    float kk[4][4], ee[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 k4 = *reinterpret_cast<const float4*>(r + D + j * 32 + cg * 4);
+      const float4 e4 = *reinterpret_cast<const float4*>(r + 2 * D + j * 32 + cg * 4);
+      kk[j][0] = k4.x; kk[j][1] = k4.y; kk[j][2] = k4.z; kk[j][3] = k4.w;
+      ee[j][0] = e4.x; ee[j][1] = e4.y; ee[j][2] = e4.z; ee[j][3] = e4.w;
+    }
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+      const int row = warp * 8 + gi * 4 + rs;
+      const float u = r[row];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) st[gi][j][i] = fmaf(u, kk[j][i], st[gi][j][i] * ee[j][i]);
+    }
+  }
+#pragma unroll
+  for (int gi = 0; gi < 2; ++gi) {
+    const int row = warp * 8 + gi * 4 + rs;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4*>(S + row * D + j * 32 + cg * 4) =
+          make_float4(st[gi][j][0], st[gi][j][1], st[gi][j][2], st[gi][j][3]);
+  }
+  if (p.conv_state && tid < 3 * D) {
+    // window after the kept tokens: the last three pre-conv inputs, older ones from the old window
+    const int HD = p.H * D;
+    const int which = tid / D, c = tid % D;
+    const int64_t gc = (int64_t)which * HD + h * D + c;
+    __nv_bfloat16* cs = p.conv_state + ((int64_t)slot * 3 * HD + gc) * 3;
+    float w[3] = {__bfloat162float(cs[0]), __bfloat162float(cs[1]), __bfloat162float(cs[2])};
+    for (int t = t0; t < t0 + n; ++t) {
+      w[0] = w[1];
+      w[1] = w[2];
+      w[2] = __bfloat162float(p.qkv[(int64_t)t * p.ld_qkv + gc]);
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) cs[i] = __float2bfloat16(w[i]);
+  }
+}
+
 }  // namespace kda
+
+cudaError_t kda_recover(const KdaRecoverArgs& a, cudaStream_t stream) {
+  if (a.num_seqs == 0) return cudaSuccess;
+  kda::kda_recover_kernel<<<a.num_seqs * a.H, kda::kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
 
 cudaError_t kda_recurrent(const KdaArgs& a, cudaStream_t stream) {
   if (a.num_seqs == 0) return cudaSuccess;

@@ -166,8 +166,28 @@ struct KdaArgs {
   __nv_bfloat16* out;  // [T, H*D] (ld_out)
   int64_t ld_out;
   float* out_f32;  // core mode [T, H, D]
+  // speculative verify: for sequences with verify[s] != 0 the state and conv window are left as they
+  // were and every token's update is recorded instead, rec [T, H, 3, D] = (u, k, decay); kda_recover
+  // then applies the accepted prefix
+  const int* verify;  // [num_seqs] nullable
+  float* rec;
 };
 cudaError_t kda_recurrent(const KdaArgs& a, cudaStream_t stream);
+
+// Applies the first keep[s] recorded tokens of each verified sequence to its state, and moves its conv
+// window past them (the window is rebuilt from the step's pre-conv inputs).
+struct KdaRecoverArgs {
+  int H, num_seqs;
+  const int* cu_seqlens;
+  const int* state_idx;
+  const int* keep;  // [num_seqs] tokens to apply (0: sequence untouched)
+  const float* rec;  // [T, H, 3, 128]
+  float* state;      // [slots, H, 128, 128]
+  const __nv_bfloat16* qkv;  // [T, 3*H*128] pre-conv inputs of the step
+  int64_t ld_qkv;
+  __nv_bfloat16* conv_state;  // [slots, 3*H*128, 3] (nullable)
+};
+cudaError_t kda_recover(const KdaRecoverArgs& a, cudaStream_t stream);
 
 // ---------------------------------------------------------------- mla_prep.cu / mla_attn.cu
 cudaError_t rope_apply(void* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,

@@ -36,7 +36,11 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                     const c10::optional<at::Tensor>& conv_w, const c10::optional<at::Tensor>& conv_b,
                     const at::Tensor& a_log, const c10::optional<at::Tensor>& g_bias, double lower_bound,
                     const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
-                    at::Tensor& state, at::Tensor& out);  // kda.cu
+                    at::Tensor& state, at::Tensor& out, const c10::optional<at::Tensor>& verify,
+                    const c10::optional<at::Tensor>& rec);
+void kda_recover_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx, const at::Tensor& keep,
+                    const at::Tensor& rec, at::Tensor& state, const at::Tensor& qkv,
+                    const c10::optional<at::Tensor>& conv_state);  // kda.cu
 void kda_core_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
                  const c10::optional<at::Tensor>& has_init, const at::Tensor& q, const at::Tensor& k,
                  const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta, at::Tensor& state,
@@ -120,7 +124,9 @@ void register_host_bindings(pybind11::module_& m);
   X("kda_forward(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor qkv, Tensor g_raw, "        \
     "Tensor beta_raw, Tensor? g2, Tensor(a!) conv_state, Tensor? conv_w, Tensor? conv_b, Tensor a_log, "   \
     "Tensor? g_bias, float lower_bound, Tensor? norm_w, float eps, float l2_eps, float q_scale, "            \
-    "bool l2norm, Tensor(b!) state, Tensor(c!) out) -> ()")                                               \
+    "bool l2norm, Tensor(b!) state, Tensor(c!) out, Tensor? verify=None, Tensor(d!)? rec=None) -> ()")       \
+  X("kda_recover(Tensor cu_seqlens, Tensor? state_idx, Tensor keep, Tensor rec, Tensor(a!) state, "         \
+    "Tensor qkv, Tensor(b!)? conv_state) -> ()")                                                          \
   X("kda_core(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor q, Tensor k, Tensor v, "      \
     "Tensor g, Tensor beta, Tensor(a!) state, Tensor(b!) out) -> ()")                                     \
   X("rope(Tensor(a!) x, Tensor positions, Tensor cos_sin, int offset, int rot_dim, bool interleaved) -> ()") \
@@ -167,6 +173,7 @@ void register_host_bindings(pybind11::module_& m);
   X("moe_combine", b200::moe_combine_op)              \
   X("kda_forward", b200::kda_forward_op)              \
   X("kda_core", b200::kda_core_op)                    \
+  X("kda_recover", b200::kda_recover_op)              \
   X("rope", b200::rope_op)                            \
   X("mla_latent_cache_write", b200::mla_latent_cache_write_op) \
   X("mla_index_k_write", b200::mla_index_k_write_op)  \

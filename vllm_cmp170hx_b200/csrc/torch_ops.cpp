@@ -249,7 +249,8 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                     const c10::optional<at::Tensor>& conv_w, const c10::optional<at::Tensor>& conv_b,
                     const at::Tensor& a_log, const c10::optional<at::Tensor>& g_bias, double lower_bound,
                     const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
-                    at::Tensor& state, at::Tensor& out) {
+                    at::Tensor& state, at::Tensor& out, const c10::optional<at::Tensor>& verify,
+                    const c10::optional<at::Tensor>& rec) {
   B200_CHECK_CUDA(qkv);
   B200_CHECK_DTYPE(qkv, at::kBFloat16);
   B200_CHECK_DTYPE(state, at::kFloat);
@@ -294,6 +295,13 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
   a.state = state.data_ptr<float>();
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.ld_out = out.stride(0);
+  if (verify.has_value()) {
+    TORCH_CHECK(rec.has_value() && rec->scalar_type() == at::kFloat && rec->is_contiguous() &&
+                    rec->numel() >= qkv.size(0) * H * 3 * 128 && verify->scalar_type() == at::kInt,
+                "kda verify: int32 flags [num_seqs] and fp32 records [T, H, 3, 128]");
+    a.verify = verify->data_ptr<int>();
+    a.rec = rec->data_ptr<float>();
+  }
   B200_LAUNCH(kda_recurrent(a, cur_stream()));
 }
 
@@ -682,6 +690,31 @@ void dequant_rows_op(const at::Tensor& rows, int64_t D, const c10::optional<at::
   B200_LAUNCH(dequant_rows_e4m3(rows.data_ptr(), rows.size(1), (int)D,
                                 failed.has_value() ? failed->data_ptr<uint8_t>() : nullptr, out.data_ptr(),
                                 (int)rows.size(0), cur_stream()));
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+void kda_recover_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx, const at::Tensor& keep,
+                    const at::Tensor& rec, at::Tensor& state, const at::Tensor& qkv,
+                    const c10::optional<at::Tensor>& conv_state) {
+  B200_CHECK_CUDA(rec);
+  TORCH_CHECK(rec.scalar_type() == at::kFloat && state.scalar_type() == at::kFloat && keep.scalar_type() == at::kInt,
+              "kda_recover: fp32 records/state, int32 keep");
+  c10::cuda::CUDAGuard g(rec.device());
+  KdaRecoverArgs a{};
+  a.H = state.size(1);
+  a.num_seqs = cu_seqlens.numel() - 1;
+  a.cu_seqlens = cu_seqlens.data_ptr<int>();
+  a.state_idx = state_idx.has_value() ? state_idx->data_ptr<int>() : nullptr;
+  a.keep = keep.data_ptr<int>();
+  a.rec = rec.data_ptr<float>();
+  a.state = state.data_ptr<float>();
+  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  a.ld_qkv = qkv.stride(0);
+  a.conv_state = conv_state.has_value() ? reinterpret_cast<__nv_bfloat16*>(conv_state->data_ptr()) : nullptr;
+  B200_LAUNCH(kda_recover(a, cur_stream()));
 }
 
 }  // namespace b200

@@ -283,9 +283,13 @@ class ModelRunner:
         grp = st.pp_group
         sends, toks, nbytes = [], [], 0
         verify = {}
+        mb_ctx = []
         for mb in self._micro_batches(out):
             h = self._host_inputs(mb)
             dev, ctx, nb = self._context(h)
+            if self._spec_enabled_elsewhere():
+                self._kda_verify_flags(mb, ctx)
+                mb_ctx.append((mb, ctx))
             nbytes += nb
             if m.first:
                 res = m(dev["ids"], ctx)
@@ -313,6 +317,8 @@ class ModelRunner:
             dist.broadcast_object_list(obj, src=last, group=st.pp_cpu_group)
             res = obj[0]
             self._pp_last_out, self._pp_last_res = out, res
+            for mb, ctx in mb_ctx:
+                self._kda_recover(mb, ctx, res)
         else:
             n = sum(1 for s in out.reqs if s.sample)
             tokens = torch.cat(toks) if m.last and toks else torch.empty(n, dtype=torch.int64, device=self.device)
@@ -324,6 +330,22 @@ class ModelRunner:
         if self.device.type == "cuda":
             _ext.check_status(self.device)
         return res
+
+    def _kda_verify_flags(self, out: SchedulerOutput, ctx) -> None:
+        """Sequences verifying drafts through KDA layers record their updates instead of committing
+        them (the state must end at the last accepted token)."""
+        if not self.model.kda_layer_ids() or not any(s.num_draft for s in out.reqs):
+            return
+        flags = np.asarray([1 if s.num_draft else 0 for s in out.reqs], dtype=np.int32)
+        ctx.kda_verify = self._to_dev(flags)
+
+    def _kda_recover(self, out: SchedulerOutput, ctx, res: dict) -> None:
+        if ctx.kda_verify is None:
+            return
+        keep = np.asarray([len(res.get(s.req.request_id, [])) if s.num_draft else 0 for s in out.reqs],
+                          dtype=np.int32)
+        keep = np.maximum(keep, np.asarray([1 if s.num_draft else 0 for s in out.reqs], dtype=np.int32))
+        self.model.kda_recover(ctx, torch.from_numpy(keep))
 
     def _spec_enabled_elsewhere(self) -> bool:
         return self.cfg.scheduler.num_speculative_tokens > 0
@@ -344,6 +366,7 @@ class ModelRunner:
         """Eager target step with draft verification; the hidden states are kept for :meth:`propose`."""
         h = self._host_inputs(out)
         dev, ctx, nbytes = self._context(h)
+        self._kda_verify_flags(out, ctx)
         ev = self._ev_start()
         hidden = self.model(dev["ids"], ctx)
         rows_of = {}
@@ -359,6 +382,7 @@ class ModelRunner:
         if k:
             logits = self.model.compute_logits(hidden.index_select(0, self._to_dev(h["sample_rows"])))
             res = sanitize_dict(self.spec.verify(out, logits, rows_of), self.mcfg.vocab_size)
+        self._kda_recover(out, ctx, res)
         self._ev_end(ev)
         self.step_counter += 1
         stats = StepStats(num_tokens=out.num_tokens, graph=False, h2d_bytes=nbytes,

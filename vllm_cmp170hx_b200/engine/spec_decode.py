@@ -74,9 +74,6 @@ class SpecDecoder:
         self.runner = runner
         self.k = k
         cfg = runner.cfg
-        if runner.model.kda_layer_ids():
-            raise NotImplementedError("speculative decoding of KDA layers needs per-token recurrent-state "
-                                      "recovery, which this engine does not implement; use an all-MLA model")
         self.mtp = MTPHead(cfg.model, runner.model, runner.device, cfg.seed,
                            getattr(runner.model, "init_mode", "local"))
         rows = runner.num_blocks * 64

@@ -54,6 +54,10 @@ class StepContext:
     mla_caches: dict = field(default_factory=dict)  # i -> (latent [rows, 576], idx_k [rows, 128] u8, idx_s [rows])
     kda_states: dict = field(default_factory=dict)  # i -> (rec [slots, H, 128, 128] f32, conv [slots, 3HD, 3])
     scores_buf: torch.Tensor | None = None
+    # speculative verify of models with KDA layers: int32 [S] (1 = the sequence's state is only
+    # recorded, see HybridForCausalLM.kda_recover) and the per-layer records of the step
+    kda_verify: torch.Tensor | None = None
+    kda_records: dict = field(default_factory=dict)
 
 
 def _fp8_proj(w: torch.Tensor):
@@ -111,8 +115,12 @@ class KDAAttention(nn.Module):
         beta = proj[:, 3 * HD + 2 * self.D: 3 * HD + 2 * self.D + self.H]
         g_raw = self.f_b(fa)
         g2 = self.g_b(ga)
+        records = None
+        if ctx.kda_verify is not None:
+            records = ctx.kda_records.setdefault(layer_idx, kda_ops.KdaRecords())
         o = kda_ops.kda_forward(qkv, g_raw, beta, g2, ctx.cu_seqlens, ctx.kda_slots, ctx.has_init, conv, self.conv_w,
-                                None, self.a_log, self.g_bias, self.lower_bound, self.norm_w, rec)
+                                None, self.a_log, self.g_bias, self.lower_bound, self.norm_w, rec,
+                                verify=ctx.kda_verify, records=records)
         return self.o_proj.forward_reduced(o)
 
 
@@ -453,6 +461,13 @@ class HybridForCausalLM(nn.Module):
         if self.last:
             return self.norm(x, residual)
         return x, residual
+
+    def kda_recover(self, ctx: StepContext, keep: torch.Tensor) -> None:
+        """After a speculative verify step: advance every verified sequence's KDA state and conv
+        window over its first keep[s] tokens (the last committed token plus the accepted drafts)."""
+        for layer_idx, records in ctx.kda_records.items():
+            rec_state, conv = ctx.kda_states[layer_idx]
+            kda_ops.kda_recover(records, keep, rec_state, conv)
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """This rank's vocab shard of the logits [rows, V / tp] (bf16)."""
