@@ -126,6 +126,11 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
     ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
+    ap.add_argument("--ep", action="store_true", help="config 3: routed experts split whole over the ranks (EP=N) "
+                                                      "instead of by intermediate columns")
+    ap.add_argument("--emulate-tp", type=int, default=0,
+                    help="1 GPU standing in for rank 0 of a TP group of this size (collectives return local data): "
+                         "prints the per-rank step time of the compute kernels only, never a bench line")
     ap.add_argument("--config", type=int, default=3, choices=[3, 4],
                     help="BASELINE config: 3 = hybrid KDA/MLA EXL3 MoE at TP=N (headline); "
                          "4 = DeepSeek-style Marlin MoE, experts EP=N, attention TP=N")
@@ -152,13 +157,19 @@ def main():
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
-    st = pstate.init(tp_size=args.gpus, pp_size=1, timeout_s=600)
+    if args.emulate_tp:
+        assert world == 1, "--emulate-tp runs in one process"
+        st = pstate.emulate(args.emulate_tp)
+        args.gpus = args.emulate_tp
+        args.nccl_baseline = True  # no symmetric-memory kernels without peers
+    else:
+        st = pstate.init(tp_size=args.gpus, pp_size=1, timeout_s=600)
     dev = st.device
     model_cfg = config3() if args.config == 3 else config4()
     total_len = args.prompt + args.output + 64
     cfg = EngineConfig(model=model_cfg,
                        parallel=ParallelConfig(tensor_parallel_size=args.gpus, fused_comm=not args.nccl_baseline,
-                                               expert_parallel=args.config == 4),
+                                               expert_parallel=args.config == 4 or args.ep),
                        scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
                                                  max_model_len=total_len, max_num_partial_prefills=args.batch),
                        cache=CacheConfig(num_blocks=args.batch * ((total_len + 63) // 64) + 1),
@@ -167,7 +178,7 @@ def main():
     t0 = time.time()
     engine = LLMEngine(cfg)
     fused = False
-    if args.gpus > 1 and not args.nccl_baseline:
+    if args.gpus > 1 and not args.nccl_baseline and not args.emulate_tp:
         try:
             from vllm_cmp170hx_b200.parallel import symm
             fused = symm.enable_for_engine(engine)
@@ -217,6 +228,12 @@ def main():
     toks = args.batch * args.steps
     value = toks / (dev_total_ms / 1e3)
     e2e_value = toks / (wall_ms / 1e3)
+    if args.emulate_tp:
+        print(json.dumps({"emulated_tp": args.emulate_tp, "config": args.config, "batch": args.batch,
+                          "per_rank_compute_ms_per_step": round(dev_total_ms / args.steps, 3),
+                          "p50_step_ms": round(statistics.median(e2e_ms), 3), "clocks": clocks}), flush=True)
+        engine.runner.release_graphs()
+        return
     if st.rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -225,7 +242,8 @@ def main():
             "data": f"synthetic: random token ids, random-init weights of the config-{args.config} architecture",
             "config": {"model": MODEL_DESC[args.config],
                        "global_batch": args.batch, "seq_len": args.prompt, "output_len": args.output,
-                       "parallelism": f"tp{args.gpus}" if args.config == 3 else f"ep{args.gpus}+attn-tp{args.gpus}",
+                       "parallelism": (f"ep{args.gpus}+attn-tp{args.gpus}" if args.config == 4 or args.ep
+                                       else f"tp{args.gpus}"),
                        "collectives": "fused symmetric-memory kernels" if fused else ("none" if args.gpus == 1 else "nccl"),
                        "l2": "no flush: each step streams the expert weights (GBs per GPU) >> 126 MB L2"},
             "p50_tpot_ms": round(statistics.median(e2e_ms), 3),

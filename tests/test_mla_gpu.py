@@ -108,7 +108,8 @@ def test_indexer_and_topk():
 
 @pytest.mark.parametrize("nh,count,splits,qscale", [(128, 2048, 1, 0.3), (32, 2048, 1, 0.3), (16, 100, 1, 0.3),
                                                     (64, 1000, 3, 0.3), (128, 64, 2, 0.3), (8, 257, 1, 0.3),
-                                                    (128, 2048, 8, 0.3), (32, 1500, 1, 3.0), (160, 700, 2, 0.3)])
+                                                    (128, 2048, 8, 0.3), (32, 1500, 1, 3.0), (160, 700, 2, 0.3),
+                                                    (4, 300, 1, 0.3), (4, 2048, 2, 0.3)])
 def test_sparse_attention(nh, count, splits, qscale):
     """qscale 3.0 gives logit ranges that force rescaling across the 256-position blocks;
     nh 160 spans two head groups; count 257 ends one position into a second block."""

@@ -107,3 +107,18 @@ def test_pp2_matches_pp1(fmt, tp):
         with open(path) as f:
             got = json.load(f)
     assert got == ref
+
+
+@pytest.mark.parametrize("fmt", ["exl3", "deepseek_mtp"])
+def test_emulated_tp_runs_per_rank_shapes(fmt):
+    """One process standing in for rank 0 of a TP=2 group: the engine builds the per-rank shards and
+    steps through them with collectives returning local data (per-rank kernel profiling)."""
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    st = pstate.emulate(2, device="cpu")
+    try:
+        toks = _generate(2, fmt)
+        assert [len(t) for t in toks] == [6 if fmt == "deepseek_mtp" else 3] * len(PROMPTS)
+        assert st.emulated and pstate.get().tp_size == 2
+    finally:
+        pstate.set_state(pstate.ParallelState())

@@ -44,7 +44,7 @@ _SEED_DRAFT = 0x27D4EB2F
 
 def _all_reduce(x: torch.Tensor, op=dist.ReduceOp.SUM) -> torch.Tensor:
     st = pstate.get()
-    if st.tp_size > 1:
+    if st.tp_size > 1 and not st.emulated:
         dist.all_reduce(x, op=op, group=st.tp_group)
     return x
 

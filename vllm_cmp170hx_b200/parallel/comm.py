@@ -38,7 +38,7 @@ def fused_enabled() -> bool:
 
 def tp_all_reduce(x: torch.Tensor) -> torch.Tensor:
     st = _state.get()
-    if st.tp_size == 1:
+    if st.tp_size == 1 or st.emulated:
         return x
     symm = _FUSED["symm"]
     if _FUSED["enabled"] and symm is not None and symm.can_all_reduce(x):
@@ -51,6 +51,8 @@ def tp_all_gather(x: torch.Tensor, dim: int = 0) -> torch.Tensor:
     st = _state.get()
     if st.tp_size == 1:
         return x
+    if st.emulated:
+        return torch.cat([x] * st.tp_size, dim=dim)
     parts = [torch.empty_like(x) for _ in range(st.tp_size)]
     dist.all_gather(parts, x.contiguous(), group=st.tp_group)
     return torch.cat(parts, dim=dim)
@@ -59,8 +61,8 @@ def tp_all_gather(x: torch.Tensor, dim: int = 0) -> torch.Tensor:
 def tp_all_gather_into(out: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """out [tp * n, ...] <- concatenation of every rank's x [n, ...] (rank order)."""
     st = _state.get()
-    if st.tp_size == 1:
-        out.copy_(x)
+    if st.tp_size == 1 or st.emulated:
+        out.copy_(x.repeat(out.shape[0] // x.shape[0], *([1] * (x.dim() - 1))))
         return out
     dist.all_gather_into_tensor(out, x.contiguous(), group=st.tp_group)
     return out
@@ -71,6 +73,8 @@ def tp_reduce_scatter(x: torch.Tensor) -> torch.Tensor:
     st = _state.get()
     if st.tp_size == 1:
         return x
+    if st.emulated:
+        return x[: x.shape[0] // st.tp_size]
     out = torch.empty(x.shape[0] // st.tp_size, *x.shape[1:], dtype=x.dtype, device=x.device)
     dist.reduce_scatter_tensor(out, x.contiguous(), group=st.tp_group)
     return out

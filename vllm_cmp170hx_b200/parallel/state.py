@@ -36,6 +36,9 @@ class ParallelState:
     backend: str = "none"
     # routed experts split whole across the TP group (expert parallel) instead of by intermediate columns
     expert_parallel: bool = False
+    # one process standing in for rank 0 of a tp_size group (per-rank kernel profiling): every
+    # collective returns local data, so the numbers are wrong but each kernel gets its per-rank shape
+    emulated: bool = False
 
     @property
     def is_first_pp(self) -> bool:
@@ -106,6 +109,15 @@ def init(tp_size: int = 1, pp_size: int = 1, backend: str | None = None, timeout
         gc = dist.new_group(ranks, backend="gloo", timeout=to)
         if t == st.tp_rank:
             st.pp_group, st.pp_cpu_group = g, gc
+    set_state(st)
+    return st
+
+
+def emulate(tp_size: int, device: str = "cuda") -> ParallelState:
+    """Single-process stand-in for rank 0 of a `tp_size` TP group (no process group).  Only for
+    measuring per-rank kernel costs of a layout whose GPUs are not at hand."""
+    dev = torch.device(device, 0) if device.startswith("cuda") else torch.device("cpu")
+    st = ParallelState(tp_size=tp_size, tp_rank=0, device=dev, backend="emulated", emulated=True)
     set_state(st)
     return st
 
