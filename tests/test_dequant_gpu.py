@@ -45,3 +45,27 @@ def test_fp8_block_linear(T, N, K):
     torch.cuda.synchronize()
     _ext.check_status(torch.device("cuda"))
     assert _rel(y.cpu(), ref) < 1e-2, _rel(y.cpu(), ref)
+
+
+@pytest.mark.parametrize("first,count", [(0, 4), (12, 4)])
+def test_marlin_moe_expert_subset(first, count):
+    """Expert parallel: experts [first, first + count) of 16 on this rank, the rest dropped."""
+    T, E, k = 80, 16, 4
+    g = torch.Generator().manual_seed(first + 7)
+    H, I = 256, 256
+    gp, gs = fm.random_experts(E, H, I, generator=g)
+    up, us = fm.random_experts(E, H, I, generator=g)
+    dp, ds = fm.random_experts(E, I, H, generator=g)
+    ex = dequant.MarlinExperts(gp, gs, up, us, dp, ds, H, I).select(first, count)
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    emap[first:first + count] = torch.arange(count, dtype=torch.int32)
+    ex.expert_map = emap
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    ids, w = moe_ref.topk(torch.randn(T, E, generator=g), k, 0)
+    ref = dequant.marlin_moe(x, ids, w, ex, out_f32=True)
+    exg = dequant.MarlinExperts(*(getattr(ex, f).cuda() for f in ("gate", "gate_s", "up", "up_s", "down", "down_s")),
+                                H, I, expert_map=emap.cuda())
+    y = dequant.marlin_moe(x.cuda(), ids.cuda(), w.cuda(), exg, out_f32=True)
+    torch.cuda.synchronize()
+    _ext.check_status(torch.device("cuda"))
+    assert _rel(y.cpu(), ref) < 1e-2, _rel(y.cpu(), ref)

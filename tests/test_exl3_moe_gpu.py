@@ -58,3 +58,28 @@ def test_exl3_moe(T, E, k):
     # deterministic run to run
     y2 = moe_ops.exl3_moe(x.cuda(), ids.cuda(), w.cuda(), ex.to("cuda"), out_f32=True)
     assert torch.equal(y, y2)
+
+
+@pytest.mark.parametrize("first,count", [(0, 4), (12, 4), (5, 9)])
+def test_exl3_moe_expert_subset(first, count):
+    """Expert parallel: this rank holds experts [first, first + count); assignments to the others are
+    dropped (the rows past the local ones stay unused), and the output is the local experts' share."""
+    T, E, k = 96, 16, 8
+    g = torch.Generator().manual_seed(first * 31 + count)
+    H, I = 256, 256
+    gate = [fx.random_matrix(H, I, 8, 2, generator=g) for _ in range(E)]
+    up = [fx.random_matrix(H, I, 8, 2, generator=g) for _ in range(E)]
+    down = [fx.random_matrix(I, H, 8, 2, generator=g) for _ in range(E)]
+    sl = slice(first, first + count)
+    ex = moe_ops.Exl3Experts.from_matrices(gate[sl], up[sl], down[sl])
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    emap[sl] = torch.arange(count, dtype=torch.int32)
+    ex.expert_map = emap
+    x = (torch.randn(T, H, generator=g) * 0.5).to(torch.bfloat16)
+    ids, w = moe_ref.topk(torch.randn(T, E, generator=g), k, 0)
+    ref = moe_ref.exl3_experts(x.float(), ids, w, {"gate": gate[sl], "up": up[sl], "down": down[sl],
+                                                   "expert_map": emap}, None, {})
+    y = moe_ops.exl3_moe(x.cuda(), ids.cuda(), w.cuda(), ex.to("cuda"), out_f32=True)
+    torch.cuda.synchronize()
+    _ext.check_status(torch.device("cuda"))
+    assert _rel(y.cpu(), ref) < 5e-3, _rel(y.cpu(), ref)

@@ -9,6 +9,7 @@ ops:
   fp8_linear  fp8 128x128 block-scaled linear, --m --n --k
   mla_decode  config-2 sparse-MLA decode layer (128 heads, top-2048 of --ctx positions), --tokens = batch
   kda_decode  config-3 KDA layer decode step (32 heads x 128), --tokens = sequences
+  attn        the sparse-attention kernel alone, --tokens --heads --topk --ctx --splits
 
 Each op prints one JSON line: mean device time per call over --iters calls
 timed with CUDA events after warm-up (inputs larger than L2 where the op
@@ -184,6 +185,24 @@ def bench_mla_decode(a):
     return _report("mla_decode", us, nbytes, tokens=a.tokens, ctx=a.ctx, topk=topk, heads=c.mla.num_heads)
 
 
+def bench_attn(a):
+    """The sparse-attention kernel alone: --tokens queries of --heads heads, each attending to --topk
+    gathered latent rows of a --ctx-row cache (random rows, so every gather is a separate line)."""
+    from ..ops import mla as mla_ops
+
+    T, nh, cnt = a.tokens, a.heads, min(a.topk, a.ctx)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = (torch.randn(T, nh, 576, device="cuda", generator=g) * 0.3).to(torch.bfloat16)
+    cache = torch.randn(a.ctx, 576, device="cuda", generator=g).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(a.ctx, device="cuda", generator=g)[:a.topk] for _ in range(T)]).int()
+    counts = torch.full((T,), cnt, dtype=torch.int32, device="cuda")
+    splits = a.splits or mla_ops.pick_splits(T, nh, a.topk)
+    us = time_us(lambda: mla_ops.sparse_attention(q, cache, idx, counts, 576 ** -0.5, splits), a.iters)
+    nbytes = T * cnt * 576 * 2 + T * nh * (576 + 512) * 2
+    flops = 2.0 * T * nh * cnt * (576 + 512)
+    return _report("attn", us, nbytes, flops, tokens=T, heads=nh, count=cnt, splits=splits)
+
+
 def bench_kda_decode(a):
     c = config3()
     layer = KDAAttention(c, WeightInit(0, "cuda", "local"), 1, 0)
@@ -199,7 +218,7 @@ def bench_kda_decode(a):
 
 
 OPS = {"gemm": bench_gemm, "exl3_moe": bench_exl3_moe, "marlin_moe": bench_marlin_moe, "fp8_linear": bench_fp8_linear,
-       "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode}
+       "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode, "attn": bench_attn}
 
 
 def main(argv=None):
@@ -211,6 +230,9 @@ def main(argv=None):
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--heads", type=int, default=128, help="attn: query heads")
+    ap.add_argument("--topk", type=int, default=2048, help="attn: gathered rows per query")
+    ap.add_argument("--splits", type=int, default=0, help="attn: position splits (0: the launcher's choice)")
     ap.add_argument("--profile", action="store_true", help="print a per-kernel table of one call (torch profiler)")
     a = ap.parse_args(argv)
     global _PROFILE

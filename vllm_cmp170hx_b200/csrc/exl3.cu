@@ -662,6 +662,8 @@ __global__ void input_rotate_kernel(const __nv_bfloat16* __restrict__ x, int64_t
   const int nblk = K / 128;
   if (gw >= rows * nblk) return;
   const int r = gw / nblk, blk = gw % nblk;
+  // rows past the assigned ones (expert parallel: assignments to other ranks' experts) are unused
+  if (expert_offsets && r >= expert_offsets[E_local]) return;
   int e = 0;
   if (expert_offsets) {  // expert of row r: binary search in offsets
     int lo = 0, hi = E_local;

@@ -195,6 +195,15 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     }
     __syncthreads();
   }
+  // rows past the assigned ones (assignments to experts of other ranks): token 0, weight 0, so a
+  // consumer that walks all T*k rows reads valid memory
+  {
+    const int total = expert_offsets[E_local];
+    for (int r = total + tid; r < TK; r += blockDim.x) {
+      sorted_token[r] = 0;
+      sorted_weight[r] = 0.f;
+    }
+  }
   // work items: expert e contributes ceil(count_e / tile_rows) items, placed
   // at the exclusive prefix of those counts (one block-wide scan)
   __syncthreads();
