@@ -47,6 +47,7 @@ def _peaks() -> dict:
 
 
 _PROFILE = False
+_GRAPH = False
 
 
 def time_us(fn, iters: int, warmup: int = 3) -> float:
@@ -62,6 +63,23 @@ def time_us(fn, iters: int, warmup: int = 3) -> float:
         print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=25, max_name_column_width=70))
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if _GRAPH:  # the calls replayed from one CUDA graph: device time without host launch gaps
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / iters
     a.record()
     for _ in range(iters):
         fn()
@@ -107,14 +125,22 @@ def bench_exl3_moe(a):
 
     c = config3()
     E, H, I, k = c.moe.num_experts, c.hidden_size, c.moe.intermediate, c.moe.top_k
-    ex = random_exl3_experts(E, H, I, c.moe.exl3_bits_x2, c.moe.exl3_codebook, WeightInit(0, "cuda", "local"), 1, 0,
-                             0.0)
+    # one rank's share: --tp splits every expert's intermediate, --ep keeps E / tp whole experts
+    E_loc, I_loc = (E // a.tp, I) if a.ep else (E, I // a.tp)
+    ex = random_exl3_experts(E_loc, H, I_loc, c.moe.exl3_bits_x2, c.moe.exl3_codebook,
+                             WeightInit(0, "cuda", "local"), 1, 0, 0.0)
+    if a.ep and a.tp > 1:
+        emap = torch.full((E,), -1, dtype=torch.int32)
+        emap[:E_loc] = torch.arange(E_loc, dtype=torch.int32)
+        ex.expert_map = emap.cuda()
     x = torch.randn(a.tokens, H, device="cuda", dtype=torch.bfloat16)
     ids, w = _route(a.tokens, E, k, "cuda")
-    used = int(torch.unique(ids).numel())
-    nbytes = used * 3 * H * I * c.moe.exl3_bits_x2 / 16  # trellis bits of the touched experts
+    used = int(torch.unique(ids[ids < E_loc] if a.ep else ids).numel())
+    nbytes = used * 3 * H * I_loc * c.moe.exl3_bits_x2 / 16  # trellis bits of the touched experts
+    pairs = int((ids < E_loc).sum()) if a.ep else a.tokens * k
     us = time_us(lambda: moe_ops.exl3_moe(x, ids, w, ex), a.iters)
-    return _report("exl3_moe", us, nbytes, 2.0 * a.tokens * k * 3 * H * I, tokens=a.tokens, experts_touched=used)
+    return _report("exl3_moe", us, nbytes, 2.0 * pairs * 3 * H * I_loc, tokens=a.tokens, experts_touched=used,
+                   tp=a.tp, ep=a.ep)
 
 
 def bench_marlin_moe(a):
@@ -231,12 +257,16 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--heads", type=int, default=128, help="attn: query heads")
+    ap.add_argument("--tp", type=int, default=1, help="exl3_moe: the share of one rank of a group this size")
+    ap.add_argument("--ep", action="store_true", help="exl3_moe: experts split whole (expert parallel)")
     ap.add_argument("--topk", type=int, default=2048, help="attn: gathered rows per query")
     ap.add_argument("--splits", type=int, default=0, help="attn: position splits (0: the launcher's choice)")
     ap.add_argument("--profile", action="store_true", help="print a per-kernel table of one call (torch profiler)")
+    ap.add_argument("--graph", action="store_true", help="time --iters calls replayed from one CUDA graph")
     a = ap.parse_args(argv)
-    global _PROFILE
+    global _PROFILE, _GRAPH
     _PROFILE = a.profile
+    _GRAPH = a.graph
     pstate.set_state(pstate.ParallelState())
     OPS[a.op](a)
     _ext.check_status(torch.device("cuda"))

@@ -87,6 +87,50 @@ B200_DEVICE void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Thread-block clusters: rank, distributed shared memory, cluster-scope barriers
+// ---------------------------------------------------------------------------
+B200_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The address of `local` (a shared-memory address of this CTA) in CTA `cta` of the cluster.
+B200_DEVICE uint32_t cluster_map(uint32_t local, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(cta));
+  return r;
+}
+
+// All threads of every CTA of the cluster (aligned: every thread of each warp executes it).  Used
+// once, right after the mbarrier initialisation, when every CTA reaches it unconditionally.
+B200_DEVICE void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive (release, cluster scope) on the mbarrier at the same offset as `bar` in CTA `cta`.
+B200_DEVICE void mbar_arrive_remote(uint64_t* bar, uint32_t cta) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_map(smem_u32(bar), cta))
+               : "memory");
+}
+
+// Bulk copy of `bytes` (16-B multiple, both ends 16-B aligned) from this CTA's shared memory to the
+// same-offset-independent address `dst_local` in CTA `cta` of the cluster; completion is signalled on
+// that CTA's mbarrier `bar_local` (its offset), as transaction bytes.  Not a multicast: one
+// destination, inside this GPU.
+B200_DEVICE void bulk_copy_to_cta(uint32_t dst_local, const void* src, uint32_t bytes, uint64_t* bar_local, uint32_t cta) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          cluster_map(dst_local, cta)),
+      "r"(smem_u32(src)), "r"(bytes), "r"(cluster_map(smem_u32(bar_local), cta))
+      : "memory");
+}
+
+B200_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the source side of every committed bulk copy has been read (its shared memory may be reused)
+B200_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 B200_DEVICE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
@@ -102,6 +146,28 @@ B200_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+B200_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for a phase completed by arrivals of other CTAs of the cluster (acquire at cluster
+// scope, so their writes before the arrive are visible).
+B200_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+  }
+  record_error(status, kErrMbarTimeout);
+  return false;
 }
 
 // Bounded wait for the phase with the given parity.  Returns false (and

@@ -449,24 +449,26 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
         if constexpr (FAST) {
           // all of this warp's tiles of the chunk at once: loads first, then the independent
           // decode chains (plain shared accesses, so the compiler interleaves them)
+          // explicit shared-space loads and stores (32-bit shared addresses, no generic-address
+          // resolution); the codebook arithmetic between them schedules freely
           constexpr int NT = NMAT * kRowsPerWarp;
-          const uint32_t* rw = reinterpret_cast<const uint32_t*>(rbase + raw_lane_off);
+          const uint32_t rw = smem_u32(rbase) + raw_lane_off;
           uint32_t w_self[NT], w_prev[NT];
 #pragma unroll
-          for (int i = 0; i < NT; ++i) w_self[i] = rw[((i / kRowsPerWarp) * 32 * 128 + (i % kRowsPerWarp) * 8 * 128) / 4];
+          for (int i = 0; i < NT; ++i) w_self[i] = lds32(rw + (i / kRowsPerWarp) * 32 * 128 + (i % kRowsPerWarp) * 8 * 128);
 #pragma unroll
           for (int i = 0; i < NT; ++i) w_prev[i] = __shfl_sync(0xffffffffu, w_self[i], (lane + 31) & 31);
-          uint8_t* ab = a_tile(stage, 0);
+          const uint32_t ab = smem_u32(a_tile(stage, 0));
 #pragma unroll
           for (int i = 0; i < NT; ++i) {
             const int m = i / kRowsPerWarp, r = i % kRowsPerWarp;
             uint32_t st[8];
             states_b8(w_prev[i], w_self[i], st);
-            uint8_t* mo = ab + m * A_BYTES;
-            *reinterpret_cast<uint32_t*>(mo + st_off[r][0]) = cb_pair<CB>(st[0], st[1]);
-            *reinterpret_cast<uint32_t*>(mo + st_off[r][1]) = cb_pair<CB>(st[2], st[3]);
-            *reinterpret_cast<uint32_t*>(mo + st_off[r][2]) = cb_pair<CB>(st[4], st[5]);
-            *reinterpret_cast<uint32_t*>(mo + st_off[r][3]) = cb_pair<CB>(st[6], st[7]);
+            const uint32_t mo = ab + m * A_BYTES;
+            sts32(mo + st_off[r][0], cb_pair<CB>(st[0], st[1]));
+            sts32(mo + st_off[r][1], cb_pair<CB>(st[2], st[3]));
+            sts32(mo + st_off[r][2], cb_pair<CB>(st[4], st[5]));
+            sts32(mo + st_off[r][3], cb_pair<CB>(st[6], st[7]));
           }
         } else {
 #pragma unroll

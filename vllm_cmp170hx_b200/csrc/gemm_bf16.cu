@@ -38,9 +38,12 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  // transposed (swap-mode) output tile staged in shared memory: BN token rows x 128 features, bf16
+  static constexpr int OUT_BYTES = BN <= 128 ? BN * BM * 2 : 0;
+  static constexpr int STAGE_BUDGET = 224 * 1024 - OUT_BYTES - 1024 - 256;
+  static constexpr int STAGES = STAGE_BUDGET / STAGE_BYTES > 8 ? 8 : STAGE_BUDGET / STAGE_BYTES;
   static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;  // power of two for BN in {16..256}
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 };
 
 struct Params {
@@ -92,13 +95,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + S * C_::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C_::STAGE_BYTES);
+  uint8_t* smem_out = smem + S * C_::STAGE_BYTES;  // OUT_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_out + C_::OUT_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
   uint64_t* tempty = bars + 2 * S + 2;
   uint64_t* drain = bars + 2 * S + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* staged = bars + 2 * S + 5;   // 128 epilogue threads: the output tile is in smem_out
+  uint64_t* written = bars + 2 * S + 6;  // 128 epilogue threads: smem_out may be refilled
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* s_epoch = tmem_slot + 2;
 
@@ -116,6 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(staged, 128);
+    mbar_init(written, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -131,6 +139,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // bf16 output, transposed: staged in smem, written as 16-byte runs of features (a token's row)
+  const bool staged_out = C_::OUT_BYTES > 0 && p.transpose_out && !p.ar && p.splits == 1 && p.Cf == nullptr &&
+                          (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 && (p.ldc & 7) == 0;
 
   const int tiles_mn = p.m_tiles * p.n_tiles;
   const int total = tiles_mn * p.splits;
@@ -242,6 +253,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;  // A row == TMEM lane
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      if (staged_out) {
+        // this thread's feature row of the tile -> column (q * 32 + lane) of the [token][feature]
+        // staging tile (a warp's 32 lanes fill 64 contiguous bytes per token: no bank conflicts)
+        const float bias = (p.bias && row < p.M) ? __bfloat162float(p.bias[row]) : 0.f;
+        const uint32_t so = smem_u32(smem_out) + (uint32_t)(q * 32 + lane) * 2;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const __nv_bfloat16 h = __float2bfloat16(__uint_as_float(r[j]) + bias);
+            asm volatile("st.shared.b16 [%0], %1;" ::"r"(so + (uint32_t)(c + j) * (BM * 2)),
+                         "h"(*reinterpret_cast<const unsigned short*>(&h))
+                         : "memory");
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);  // the accumulator is free once read
+        mbar_arrive(staged);
+        const bool st_ok = mbar_wait_or_abort(staged, local & 1, p.status, abort_flag);
+        if (st_ok) {
+          // 16-byte runs: token row n of the tile, features 8 g .. 8 g + 7
+          const int et = (warp - 2) * 32 + lane;
+          for (int i = et; i < BN * (BM / 8); i += 128) {
+            const int n = i / (BM / 8), g = i % (BM / 8);
+            const int col = nt * BN + n, f0 = mt * BM + g * 8;
+            if (col >= p.N || f0 >= p.M) continue;
+            const uint8_t* src = smem_out + n * (BM * 2) + g * 16;
+            __nv_bfloat16* dst = p.C + (size_t)col * p.ldc + f0;
+            if (f0 + 8 <= p.M) {
+              *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+            } else {
+              for (int k = 0; k < p.M - f0; ++k) dst[k] = reinterpret_cast<const __nv_bfloat16*>(src)[k];
+            }
+          }
+        }
+        mbar_arrive(written);
+        if (!mbar_wait_or_abort(written, local & 1, p.status, abort_flag) || !st_ok) break;
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         uint32_t r[16];
@@ -397,6 +450,217 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- cluster split-K
+// Decode-shaped GEMMs (few output tiles, long K).  The K range of one 128 x BN output tile is split
+// over the `splits` CTAs of a thread-block cluster (splits <= 8).  Each CTA accumulates its share in
+// TMEM and parks the fp32 partial in its own shared memory, grouped by the CTA that will reduce
+// each row range; one thread then bulk-copies every group into its reducer's receive slot
+// (cp.async.bulk shared::cta -> shared::cluster, completion as transaction bytes on the reducer's
+// mbarrier).  CTA r sums the `splits` slots of rows [r R, (r + 1) R) in split order (deterministic),
+// adds the bias and writes C in 16-byte runs.  No fp32 partials go through global memory, there is
+// no second kernel, and the only cluster-wide barrier is the one after the mbarrier initialisation.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_csk_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                         Params p) {
+  using C_ = Cfg<BN>;
+  constexpr int S = C_::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + S * C_::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C_::STAGE_BYTES + C_::OUT_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* parked = bars + 2 * S + 1;  // 128 epilogue threads: the partial groups are in smem
+  uint64_t* recv = bars + 2 * S + 2;    // every CTA's group for this CTA's rows has landed
+  uint64_t* drain = bars + 2 * S + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int splits = p.splits;
+  const uint32_t rank = cluster_ctarank();
+  const int mn = blockIdx.x / splits;
+  const int mt = mn % p.m_tiles, nt = mn / p.m_tiles;
+  const int kb_total = (p.K + BK - 1) / BK;
+  const int kb0 = (int)rank * p.k_blocks_per_split;
+  const int kb1 = min(kb_total, kb0 + p.k_blocks_per_split);
+  // rows of the tile reduced by CTA j: [j R, j R + R), R a multiple of 4 (16-byte groups)
+  const int R = ((BM + splits - 1) / splits + 3) / 4 * 4;
+  const int GROUP = BN * R;  // floats of one group: [BN columns][R rows]
+  // parked groups [splits][BN][R] then the receive slots [splits][BN][R] (over the drained stages)
+  float* park = reinterpret_cast<float*>(smem);
+  float* slots = park + splits * GROUP;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(parked, 128);
+    mbar_init(recv, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C_::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  // peers copy into this CTA's slots and signal its barrier: all initialised first
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0, issued = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+        tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
+        tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        const uint32_t n = issued < (uint32_t)S ? issued : (uint32_t)S;
+        for (uint32_t i = 0; i < n; ++i) {
+          const uint32_t k = issued - 1 - i;
+          mbar_wait(&full[k % S], (k / S) & 1, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, 1 /*bf16*/);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_or_abort(&full[stage], phase, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t da = desc_kmajor_sw128(smem_a + stage * C_::A_BYTES);
+        const uint64_t db = desc_kmajor_sw128(smem_b + stage * C_::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) umma_f16(tmem_base, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok) umma_commit(tfull);
+      if (!ok) *abort_flag = 1;
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue: park, exchange, reduce
+    const int q = warp & 3;
+    const int et = threadIdx.x - 64;  // 0..127
+    const int row = q * 32 + lane;    // tile row == TMEM lane
+    const int dst = row / R, rl = row % R;
+    if (et == 0) mbar_arrive_expect_tx(recv, (uint32_t)(splits * GROUP * 4));
+    bool ok = mbar_wait_or_abort(tfull, 0, p.status, abort_flag);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
+      float* pg = park + dst * GROUP + rl;  // column c at pg[c * R]
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pg[(c + j) * R] = __uint_as_float(r[j]);
+      }
+    } else {
+      ok = false;
+    }
+    fence_proxy_async_smem();  // the parked groups are read by the bulk-copy engine
+    mbar_arrive(parked);
+    if (et == 0) {
+      // every group is written (or abandoned: its reducer still gets bytes and does not wait out)
+      if (!mbar_wait(parked, 0, p.status)) *abort_flag = 1;
+      for (int j = 0; j < splits; ++j)
+        bulk_copy_to_cta(smem_u32(slots + rank * GROUP), park + j * GROUP, (uint32_t)(GROUP * 4), recv, (uint32_t)j);
+      bulk_commit_group();
+    }
+    ok = mbar_wait_or_abort(recv, 0, p.status, abort_flag) && ok;
+    const int r0 = (int)rank * R, r1 = min(BM, r0 + R);
+    if (ok && r1 > r0) {
+      // runs of 4 rows of one column: thread et takes (column n, rows r0 + 4 g ..)
+      const int ng = (r1 - r0 + 3) / 4;
+      for (int i = et; i < BN * ng; i += 128) {
+        const int n = i / ng, g = i % ng;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int j = 0; j < splits; ++j) {
+          const float4 v = *reinterpret_cast<const float4*>(slots + j * GROUP + n * R + g * 4);
+          acc[0] += v.x;
+          acc[1] += v.y;
+          acc[2] += v.z;
+          acc[3] += v.w;
+        }
+        const int col = nt * BN + n;
+        const int grow0 = mt * BM + r0 + g * 4;
+        if (col >= p.N || grow0 >= p.M) continue;
+        const int nrow = min(4, min(r1 - (r0 + g * 4), p.M - grow0));
+        if (p.bias)
+          for (int k = 0; k < nrow; ++k) acc[k] += __bfloat162float(p.transpose_out ? p.bias[grow0 + k] : p.bias[col]);
+        if (p.transpose_out && p.Cf == nullptr && nrow == 4 && ((reinterpret_cast<uintptr_t>(p.C) & 7) == 0) &&
+            (p.ldc & 3) == 0) {
+          uint2 v;
+          v.x = pack_bf16x2(acc[0], acc[1]);
+          v.y = pack_bf16x2(acc[2], acc[3]);
+          *reinterpret_cast<uint2*>(p.C + (size_t)col * p.ldc + grow0) = v;
+        } else {
+          for (int k = 0; k < nrow; ++k) {
+            const size_t off = p.transpose_out ? (size_t)col * p.ldc + grow0 + k : (size_t)(grow0 + k) * p.ldc + col;
+            if (p.Cf != nullptr)
+              p.Cf[off] = acc[k];
+            else
+              p.C[off] = __float2bfloat16(acc[k]);
+          }
+        }
+      }
+    }
+    // this CTA's parked groups must be read out before its shared memory goes away
+    if (et == 0) bulk_wait_read_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+}
+
 // Sum of split-K partials in split order, plus optional bias, to bf16.
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ C,
                                      float* __restrict__ Cf, int rows, int cols, int ldc, int splits,
@@ -429,6 +693,37 @@ cudaError_t launch(const void* A, int64_t lda, int rows_a, const void* B, int64_
   return cudaGetLastError();
 }
 
+template <int BN>
+cudaError_t launch_csk(const void* A, int64_t lda, int rows_a, const void* B, int64_t ldb, int rows_b, int K,
+                       const Params& p, cudaStream_t stream) {
+  using C_ = Cfg<BN>;
+  CUtensorMap ta = make_tma_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_a, K, lda, BM, BK,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_b, K, ldb, BN, BK,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  // parked groups + receive slots: 2 x splits x R rows x BN fp32 over the operand stages
+  const int R = ((BM + p.splits - 1) / p.splits + 3) / 4 * 4;
+  if ((int64_t)2 * p.splits * R * BN * 4 > (int64_t)C_::STAGES * C_::STAGE_BYTES) return cudaErrorInvalidValue;
+  auto kern = gemm_bf16_csk_kernel<BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.m_tiles * p.n_tiles * p.splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C_::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 }  // namespace gemm
 
 int device_sm_count() {
@@ -444,6 +739,12 @@ int device_sm_count() {
   return cached[dev];
 }
 
+// Splits up to this many run as one thread-block cluster per tile, reduced in distributed shared
+// memory (gemm_bf16_csk_kernel); more go through fp32 partials and a reduce kernel.
+constexpr int kMaxClusterSplits = 8;
+
+bool gemm_bf16_uses_partial(int M, int splits) { return splits > kMaxClusterSplits || (splits > 1 && M > 128); }
+
 // Number of K splits the launcher uses for this shape (splits_req > 0 forces it).
 int gemm_bf16_splits(int M, int N, int K, int splits_req) {
   using namespace gemm;
@@ -458,7 +759,8 @@ int gemm_bf16_splits(int M, int N, int K, int splits_req) {
   if (splits_req > 0) {
     splits = splits_req;
   } else if (tiles < sms) {
-    splits = std::max(1, std::min(sms / tiles, kb_total / 4));
+    // K split over a cluster of at most 8 CTAs per tile, at least 2 K blocks each
+    splits = std::max(1, std::min(std::min(kMaxClusterSplits, sms / tiles), kb_total / 2));
   }
   splits = std::max(1, std::min(splits, kb_total));
   const int per = (kb_total + splits - 1) / splits;
@@ -495,6 +797,14 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.Cf = a.out_f32 ? reinterpret_cast<float*>(a.c) : nullptr;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   p.status = a.status;
+  if (splits > 1 && splits <= kMaxClusterSplits && bn <= 128) {
+    switch (bn) {
+      case 16: return launch_csk<16>(A, lda, Ma, B, ldb, Nb, a.K, p, stream);
+      case 32: return launch_csk<32>(A, lda, Ma, B, ldb, Nb, a.K, p, stream);
+      case 64: return launch_csk<64>(A, lda, Ma, B, ldb, Nb, a.K, p, stream);
+      default: return launch_csk<128>(A, lda, Ma, B, ldb, Nb, a.K, p, stream);
+    }
+  }
   if (splits > 1) {
     if (a.partial == nullptr || a.partial_cap < (int64_t)splits * a.M * a.N) return cudaErrorInvalidValue;
     p.partial = a.partial;
@@ -639,7 +949,7 @@ extern "C" int b200_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w,
   cudaError_t e = noalloc::scratch_for_current_device(&s);
   if (e != cudaSuccess) return (int)e;
   const int used = gemm_bf16_splits(M, N, K, splits);
-  if (used > 1 && (uint64_t)used * (uint64_t)M * (uint64_t)N > (uint64_t)B200_NOALLOC_SCRATCH_FLOATS)
+  if (gemm_bf16_uses_partial(M, used) && (uint64_t)used * (uint64_t)M * (uint64_t)N > (uint64_t)B200_NOALLOC_SCRATCH_FLOATS)
     return B200_NOALLOC_TOO_LARGE;
   // The status word must start at zero for this call; the partial sums need
   // no clearing (every split writes its whole [M, N] slice).

@@ -33,6 +33,8 @@ struct GemmArgs {
   uint32_t* status;
 };
 int gemm_bf16_splits(int M, int N, int K, int splits_req);
+// Whether a launch with this many splits needs the fp32 partial scratch (cluster-reduced splits do not).
+bool gemm_bf16_uses_partial(int M, int splits);
 cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 
 // GEMM fused with the tensor-parallel all-reduce over symmetric peer buffers (gemm_bf16.cu).

@@ -55,7 +55,7 @@ void gemm_bf16_out(const at::Tensor& x, const at::Tensor& w, const c10::optional
   a.status = status_ptr(status);
   a.splits = gemm_bf16_splits(a.M, a.N, a.K, (int)splits);
   at::Tensor partial;
-  if (a.splits > 1) {
+  if (gemm_bf16_uses_partial(a.M, a.splits)) {
     partial = at::empty({(int64_t)a.splits * a.M * a.N}, x.options().dtype(at::kFloat));
     a.partial = partial.data_ptr<float>();
     a.partial_cap = partial.numel();
