@@ -126,6 +126,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
     ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
+    ap.add_argument("--eager", action="store_true", help="no CUDA graphs (debugging)")
     ap.add_argument("--ep", action="store_true", help="config 3: routed experts split whole over the ranks (EP=N) "
                                                       "instead of by intermediate columns")
     ap.add_argument("--emulate-tp", type=int, default=0,
@@ -173,7 +174,7 @@ def main():
                        scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
                                                  max_model_len=total_len, max_num_partial_prefills=args.batch),
                        cache=CacheConfig(num_blocks=args.batch * ((total_len + 63) // 64) + 1),
-                       seed=args.seed, device="cuda",
+                       seed=args.seed, device="cuda", enforce_eager=args.eager,
                        cuda_graph_batch_sizes=[args.batch])
     t0 = time.time()
     engine = LLMEngine(cfg)
@@ -207,6 +208,8 @@ def main():
     torch.cuda.synchronize()
     dev_ms, e2e_ms = [], []
     h2d = d2h = 0
+    reqs = list(engine.requests.values())
+    emitted0 = sum(len(r.output_token_ids) for r in reqs)
     t_start = time.perf_counter()
     for _ in range(args.steps):
         a = time.perf_counter()
@@ -225,11 +228,16 @@ def main():
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
     dev_total_ms, wall_ms = tot.tolist()
-    toks = args.batch * args.steps
+    # tokens actually emitted in the timed steps (a request that finished early, e.g. on a failed
+    # input row, emits none, and the number says so)
+    emitted = sum(len(r.output_token_ids) for r in reqs) - emitted0
+    failed = sum(1 for r in reqs if r.status.name == "FINISHED_ERROR")
+    toks = emitted
     value = toks / (dev_total_ms / 1e3)
     e2e_value = toks / (wall_ms / 1e3)
     if args.emulate_tp:
         print(json.dumps({"emulated_tp": args.emulate_tp, "config": args.config, "batch": args.batch,
+                          "tokens_emitted": emitted, "requests_failed": failed,
                           "per_rank_compute_ms_per_step": round(dev_total_ms / args.steps, 3),
                           "p50_step_ms": round(statistics.median(e2e_ms), 3), "clocks": clocks}), flush=True)
         engine.runner.release_graphs()
@@ -251,6 +259,7 @@ def main():
             "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "LLMEngine.step()"},
             "gpu_launches": launches,
+            "tokens_emitted": emitted, "requests_failed": failed,
             "timing": {"load_s": round(t_load, 1), "prefill_s": round(t_prefill, 1)},
         }), flush=True)
     engine.runner.release_graphs()

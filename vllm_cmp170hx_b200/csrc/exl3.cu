@@ -14,11 +14,12 @@
 //     the work item in their own ring (128-byte swizzle);
 //   * one thread issues tcgen05.mma (M = 128 output features, N = rows of the
 //     item rounded to 16, K = 64 per stage) into TMEM;
-//   * the decoder warps then run the epilogue from TMEM: the output H128 is a
+//   * four epilogue warps read the result from TMEM: the output H128 is a
 //     butterfly across the 128 TMEM lanes (shuffles + one shared exchange),
 //     svh scaling, and for the gate/up pass SwiGLU plus the down projection's
 //     input rotation, so the intermediate is written once, already in the
-//     form the down pass consumes.
+//     form the down pass consumes.  Two accumulators alternate between work
+//     units, so the decoders start unit u + 1 while unit u is read out.
 //
 // A work item is (local expert, first row, rows <= tile_rows) of the
 // expert-sorted assignment list (router.cu); a dense EXL3 linear is the same
@@ -295,7 +296,8 @@ struct Plan {
   int smem;
 };
 
-constexpr int kGroups = kDecodeWarps / 4;  // epilogue warp groups (4 warps = 128 TMEM lanes)
+constexpr int kEpiWarps = 4;               // dedicated epilogue warps (one group: 128 TMEM lanes)
+constexpr int kGroups = 1;                 // epilogue warp groups (named barrier 1, xbuf slice 0)
 constexpr int kXbufBytes = 16 * 128 * 4;   // per-group H128 exchange buffer
 
 // Shared-memory plan: three independent rings so that neither the trellis
@@ -326,10 +328,11 @@ inline Plan make_plan(int nmat, int tile_rows, int bits_x2) {
   return pl;
 }
 
-constexpr int kRawWarp = kDecodeWarps;      // trellis producer (TMA)
-constexpr int kBWarp = kDecodeWarps + 1;    // activation producer (TMA)
-constexpr int kMmaWarp = kDecodeWarps + 2;  // TMEM owner + MMA issuer
-constexpr int kThreadsStaged = (kDecodeWarps + 3) * 32;
+constexpr int kEpiWarp0 = kDecodeWarps;                // epilogue warps [kEpiWarp0, kEpiWarp0 + 4)
+constexpr int kRawWarp = kDecodeWarps + kEpiWarps;      // trellis producer (TMA)
+constexpr int kBWarp = kRawWarp + 1;                    // activation producer (TMA)
+constexpr int kMmaWarp = kRawWarp + 2;                  // TMEM owner + MMA issuer
+constexpr int kThreadsStaged = (kMmaWarp + 1) * 32;
 
 // NMAT = 2: gate/up pass (writes the rotated SwiGLU intermediate), 1: down / dense.
 // Trellis chunks (4 tile rows x 8 tile columns per matrix) arrive by TMA in
@@ -357,14 +360,16 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
   uint64_t* raw_empty = bars + 16;   // [8]  decoder warps
   uint64_t* b_full = bars + 24;      // [8]  activation TMA tx
   uint64_t* b_empty = bars + 32;     // [8]  MMA commit
-  uint64_t* tfull = bars + 40;       // accumulator ready
-  uint64_t* drain = bars + 41;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 42);
+  uint64_t* tfull = bars + 40;       // [2] MMA commit: accumulator ready
+  uint64_t* tempty = bars + 42;      // [2] epilogue warps: accumulator read out
+  uint64_t* drain = bars + 44;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 45);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int tmem_cols_needed = NMAT * tile_rows;
+  const int acc_cols = NMAT * tile_rows;  // one accumulator; two alternate between units
+  const int tmem_cols_needed = 2 * acc_cols;
   const uint32_t tmem_cols = tmem_cols_needed <= 32 ? 32 : tmem_cols_needed <= 64 ? 64 : tmem_cols_needed <= 128 ? 128
                              : tmem_cols_needed <= 256 ? 256 : 512;
   const int tile_bytes = FAST ? 128 : 16 * p.bits_x2;  // one 16x16 trellis tile
@@ -383,7 +388,10 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kDecodeWarps);
     }
-    mbar_init(tfull, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], kEpiWarps * 32);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -407,12 +415,9 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
   auto b_tile = [&](int stage, int m) { return sbb + stage * pl.b_bytes + m * b_bytes; };
 
   if (warp < kDecodeWarps) {
-    // =================================================================== decoders + epilogue
+    // =================================================================== decoders
     int stage = 0, rs = 0;
     uint32_t phase = 0, rphase = 0;
-    int local = 0;
-    const int g = warp / 4;  // epilogue warp group
-    const int q = warp % 4;  // TMEM lane quarter
     const int tc = warp & 7;                          // decoded tile column (16 output features)
     const int tr0 = (warp >> 3) * (4 / (kDecodeWarps / 8));  // first tile row of this warp
     constexpr int kRowsPerWarp = 4 / (kDecodeWarps / 8);
@@ -433,10 +438,7 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
         st_off[r][3] = row + 1024 + c1;
       }
     }
-    for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
-      const int4 it = p.items[u / n_tiles];
-      const int tile = u % n_tiles;
-      const int e = it.x;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
       bool ok = true;
       for (int kc = 0; kc < kchunks; ++kc) {
         bool got = mbar_wait_or_abort(&raw_full[rs], rphase, p.status, abort_flag);
@@ -497,31 +499,38 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
         }
       }
       if (!ok) break;
-      // ---------------------------------------------------------------- epilogue
-      const bool got = mbar_wait_or_abort(tfull, local & 1, p.status, abort_flag);
+    }
+  } else if (warp < kEpiWarp0 + kEpiWarps) {
+    // =================================================================== epilogue warps
+    // Read accumulator (local & 1) of every unit this CTA runs while the decoders and the MMA
+    // already fill the other one: the decode of unit u + 1 never waits for the epilogue of u.
+    const int q = warp % 4;  // TMEM lane quarter
+    const int f = q * 32 + lane;
+    int local = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
+      const int4 it = p.items[u / n_tiles];
+      const int tile = u % n_tiles;
+      const int e = it.x;
+      const int acc = local & 1;
+      const bool got = mbar_wait_or_abort(&tfull[acc], (local >> 1) & 1, p.status, abort_flag);
       if (!__all_sync(0xffffffffu, got)) break;  // TMEM loads are warp-collective
       tc_fence_after();
       const int rows = it.z;
       const int row0 = it.y;
-      const int f = q * 32 + lane;
       const int feat = tile * 128 + f;
-      float* xb = xbuf + g * 16 * 128;
       const int nchunks = (rows + 15) / 16;
-      // Column blocks are dealt round-robin to the warp groups (each group's named barrier spans
-      // its own 4 warps).  Items of at most 16 rows (decode) are split into 4-column blocks, so
-      // all four groups share the epilogue instead of one group holding the next item's decode.
-      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16);
+      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * acc_cols);
       const float sg = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
       const float su = NMAT == 2 ? __half2float(p.svh[1][(int64_t)e * p.svh_estride[1] + feat]) : 0.f;
       const float sn = NMAT == 2 ? __half2float(p.suh_next[(int64_t)e * p.suh_next_estride + feat]) : 0.f;
-      if (nchunks >= kGroups) {
-        for (int c = g; c < nchunks; c += kGroups)
-          epilogue_block<NMAT, 16>(p, tlane, tile_rows, c * 16, rows, row0, feat, sg, su, sn, lane, q, xb, 1 + g);
+      if (rows > 4) {
+        for (int c = 0; c < nchunks; ++c)
+          epilogue_block<NMAT, 16>(p, tlane, tile_rows, c * 16, rows, row0, feat, sg, su, sn, lane, q, xbuf, 1);
       } else {
-        for (int c = g; c < (rows + 3) / 4; c += kGroups)
-          epilogue_block<NMAT, 4>(p, tlane, tile_rows, c * 4, rows, row0, feat, sg, su, sn, lane, q, xb, 1 + g);
+        epilogue_block<NMAT, 4>(p, tlane, tile_rows, 0, rows, row0, feat, sg, su, sn, lane, q, xbuf, 1);
       }
       tc_fence_before();
+      mbar_arrive(&tempty[acc]);
     }
   } else if (warp == kRawWarp) {
     // =================================================================== trellis producer
@@ -601,10 +610,18 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
       int stage = 0, bs = 0;
       uint32_t phase = 0, bphase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      int local = 0;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++local) {
         const int4 it = p.items[u / n_tiles];
         const int n_pad = (it.z + 15) / 16 * 16;
         const uint32_t idesc = make_idesc_f16(128, n_pad, 0 /*f16*/);
+        const int acc = local & 1;
+        // the epilogue warps have read this accumulator's previous unit
+        if (!mbar_wait_or_abort(&tempty[acc], ((local >> 1) & 1) ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         for (int kc = 0; kc < kchunks; ++kc) {
           const bool ga = mbar_wait_or_abort(&b_full[bs], bphase, p.status, abort_flag) &&
                           mbar_wait_or_abort(&full[stage], phase, p.status, abort_flag);
@@ -615,7 +632,7 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
           tc_fence_after();
 #pragma unroll
           for (int m = 0; m < NMAT; ++m) {
-            const uint32_t d = tmem_base + m * tile_rows;
+            const uint32_t d = tmem_base + acc * acc_cols + m * tile_rows;
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
               const uint64_t da = desc_kmajor_sw128(a_tile(stage, m)) + 2 * k;
@@ -635,7 +652,7 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
           }
         }
         if (!ok) break;
-        umma_commit(tfull);
+        umma_commit(&tfull[acc]);
       }
       if (!ok) *abort_flag = 1;
       umma_commit(drain);

@@ -459,17 +459,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 // mbarrier).  CTA r sums the `splits` slots of rows [r R, (r + 1) R) in split order (deterministic),
 // adds the bias and writes C in 16-byte runs.  No fp32 partials go through global memory, there is
 // no second kernel, and the only cluster-wide barrier is the one after the mbarrier initialisation.
+// Shared memory of the cluster kernel: the operand stages (at most 4: a CTA holds a few K blocks),
+// over which the parked groups are written once its own MMAs are done, then the receive slots in a
+// region of their own (peers copy into them while this CTA may still be streaming its operands),
+// then the barriers.
+template <int BN>
+struct CskPlan {
+  static constexpr int S = Cfg<BN>::STAGES < 4 ? Cfg<BN>::STAGES : 4;
+  static constexpr int MAX_ROWS = 144;  // max of splits x R over splits = 2..8 (R = ceil(128 / splits), to 4)
+  static constexpr int GROUPS_BYTES = MAX_ROWS * BN * 4;
+  static constexpr int STAGE_REGION = S * Cfg<BN>::STAGE_BYTES > GROUPS_BYTES ? S * Cfg<BN>::STAGE_BYTES : GROUPS_BYTES;
+  static constexpr int SLOTS_OFF = STAGE_REGION;
+  static constexpr int BARS_OFF = SLOTS_OFF + GROUPS_BYTES;
+  static constexpr int SMEM_BYTES = BARS_OFF + 256 + 1024;
+};
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_csk_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                          Params p) {
   using C_ = Cfg<BN>;
-  constexpr int S = C_::STAGES;
+  using P_ = CskPlan<BN>;
+  constexpr int S = P_::S;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + S * C_::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C_::STAGE_BYTES + C_::OUT_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_::BARS_OFF);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
@@ -491,9 +507,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // rows of the tile reduced by CTA j: [j R, j R + R), R a multiple of 4 (16-byte groups)
   const int R = ((BM + splits - 1) / splits + 3) / 4 * 4;
   const int GROUP = BN * R;  // floats of one group: [BN columns][R rows]
-  // parked groups [splits][BN][R] then the receive slots [splits][BN][R] (over the drained stages)
+  // parked groups [splits][BN][R] over the drained stages; receive slots [splits][BN][R] apart
   float* park = reinterpret_cast<float*>(smem);
-  float* slots = park + splits * GROUP;
+  float* slots = reinterpret_cast<float*>(smem + P_::SLOTS_OFF);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -701,16 +717,16 @@ cudaError_t launch_csk(const void* A, int64_t lda, int rows_a, const void* B, in
                                CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tb = make_tma_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_b, K, ldb, BN, BK,
                                CU_TENSOR_MAP_SWIZZLE_128B);
-  // parked groups + receive slots: 2 x splits x R rows x BN fp32 over the operand stages
+  using P_ = CskPlan<BN>;
   const int R = ((BM + p.splits - 1) / p.splits + 3) / 4 * 4;
-  if ((int64_t)2 * p.splits * R * BN * 4 > (int64_t)C_::STAGES * C_::STAGE_BYTES) return cudaErrorInvalidValue;
+  if (p.splits * R > P_::MAX_ROWS) return cudaErrorInvalidValue;
   auto kern = gemm_bf16_csk_kernel<BN>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.m_tiles * p.n_tiles * p.splits);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C_::SMEM_BYTES;
+  cfg.dynamicSmemBytes = P_::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

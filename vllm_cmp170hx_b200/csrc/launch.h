@@ -101,7 +101,7 @@ cudaError_t silu_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int
 cudaError_t moe_topk(const float* logits, int T, int E, int k, int mode, const float* bias, float scale, int renorm,
                      int* ids, float* weights, cudaStream_t stream);
 cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, int k, const int* expert_map,
-                                  int E_local, int tile_rows, int* sorted_token, float* sorted_weight, int* slot_of,
+                                  int E_map, int E_local, int tile_rows, int* sorted_token, float* sorted_weight, int* slot_of,
                                   int4* items, int* num_items, int* expert_offsets, int max_items,
                                   cudaStream_t stream);
 

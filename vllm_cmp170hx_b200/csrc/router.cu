@@ -11,6 +11,8 @@
 // The assignment list is built deterministically (counting sort in
 // (token, slot) order, no atomics on the data path) by one CTA, and chunked
 // into work items of at most `tile_rows` rows for the grouped GEMMs.
+#include <cfloat>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -67,6 +69,9 @@ __global__ void topk_kernel(const float* __restrict__ logits, int T, int E, int 
       score[i] = sqrtf(sp);
       key[i] = score[i] + (bias ? bias[e] : 0.f);
     }
+    // a NaN key (a failed row) ranks below every real score but stays selectable, so every row
+    // gets k distinct valid expert ids (its weights carry the NaN on to the output row)
+    if (key[i] != key[i]) key[i] = -FLT_MAX;
   }
   float picked_sum = 0.f;
   float my_w = 0.f;
@@ -113,8 +118,9 @@ __global__ void topk_kernel(const float* __restrict__ logits, int T, int E, int 
   }
 }
 
-// One CTA.  Inputs: ids [T*k] (global expert ids), expert_map [E_global] ->
-// local index or -1 (nullptr: identity).  Outputs:
+// One CTA.  Inputs: ids [T*k] (global expert ids), expert_map [E_map] ->
+// local index or -1 (nullptr: identity over E_map = E_local experts); an id
+// outside [0, E_map) counts as another rank's.  Outputs:
 //   sorted_token[a], sorted_weight[a]  for assignment rows a in expert order,
 //   slot_of[t*k + j] = a (or -1 when the expert is not local),
 //   items[i] = {local_expert, row0, rows, 0}, num_items[0] = count,
@@ -123,7 +129,7 @@ constexpr int kBuildThreads = 1024;
 
 __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     const int* __restrict__ ids, const float* __restrict__ weights, int TK, int k, const int* __restrict__ expert_map,
-    int E_local, int tile_rows, int* __restrict__ sorted_token, float* __restrict__ sorted_weight,
+    int E_map, int E_local, int tile_rows, int* __restrict__ sorted_token, float* __restrict__ sorted_weight,
     int* __restrict__ slot_of, int4* __restrict__ items, int* __restrict__ num_items, int* __restrict__ expert_offsets,
     int max_items) {
   extern __shared__ int sm[];
@@ -136,7 +142,7 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
   // pass 1: counts
   for (int a = tid; a < TK; a += blockDim.x) {
     int e = ids[a];
-    if (expert_map) e = expert_map[e];
+    e = (e >= 0 && e < E_map) ? (expert_map ? expert_map[e] : e) : -1;
     if (e >= 0 && e < E_local) atomicAdd(&counts[e], 1);
   }
   __syncthreads();
@@ -167,7 +173,7 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     int e = -1;
     if (a < TK) {
       e = ids[a];
-      if (expert_map) e = expert_map[e];
+      e = (e >= 0 && e < E_map) ? (expert_map ? expert_map[e] : e) : -1;
       if (e >= E_local) e = -1;
     }
     for (int i = tid; i < 32 * E_local; i += blockDim.x) warp_counts[i] = 0;
@@ -248,7 +254,7 @@ cudaError_t moe_topk(const float* logits, int T, int E, int k, int mode, const f
 }
 
 cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, int k, const int* expert_map,
-                                  int E_local, int tile_rows, int* sorted_token, float* sorted_weight, int* slot_of,
+                                  int E_map, int E_local, int tile_rows, int* sorted_token, float* sorted_weight, int* slot_of,
                                   int4* items, int* num_items, int* expert_offsets, int max_items,
                                   cudaStream_t stream) {
   const size_t smem = sizeof(int) * (2 * E_local + 32 * E_local);
@@ -256,7 +262,8 @@ cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, i
   cudaError_t e = cudaFuncSetAttribute(build_assignments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
-  build_assignments_kernel<<<1, kBuildThreads, smem, stream>>>(ids, weights, T * k, k, expert_map, E_local,
+  build_assignments_kernel<<<1, kBuildThreads, smem, stream>>>(ids, weights, T * k, k, expert_map,
+                                                               expert_map ? E_map : E_local, E_local,
                                                                tile_rows, sorted_token, sorted_weight, slot_of, items,
                                                                num_items, expert_offsets, max_items);
   return cudaGetLastError();

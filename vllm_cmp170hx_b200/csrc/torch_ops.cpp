@@ -142,7 +142,8 @@ void moe_build_assignments_op(const at::Tensor& ids, const at::Tensor& weights,
   c10::cuda::CUDAGuard g(ids.device());
   B200_LAUNCH(moe_build_assignments(
       ids.data_ptr<int>(), weights.data_ptr<float>(), T, k,
-      expert_map.has_value() ? expert_map->data_ptr<int>() : nullptr, (int)E_local, (int)tile_rows,
+      expert_map.has_value() ? expert_map->data_ptr<int>() : nullptr,
+      expert_map.has_value() ? (int)expert_map->numel() : (int)E_local, (int)E_local, (int)tile_rows,
       sorted_token.data_ptr<int>(), sorted_weight.data_ptr<float>(), slot_of.data_ptr<int>(),
       reinterpret_cast<int4*>(items.data_ptr<int>()), num_items.data_ptr<int>(), expert_offsets.data_ptr<int>(),
       (int)items.size(0), cur_stream()));
