@@ -127,8 +127,10 @@ def main():
     ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
     ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
     ap.add_argument("--eager", action="store_true", help="no CUDA graphs (debugging)")
-    ap.add_argument("--ep", action="store_true", help="config 3: routed experts split whole over the ranks (EP=N) "
-                                                      "instead of by intermediate columns")
+    ap.add_argument("--ep", action="store_true", help="(default for N > 1) routed experts split whole over the "
+                                                      "ranks (EP=N)")
+    ap.add_argument("--moe-tp", action="store_true", help="config 3 at N > 1: split every routed expert by "
+                                                          "intermediate columns instead (tensor-parallel MoE)")
     ap.add_argument("--emulate-tp", type=int, default=0,
                     help="1 GPU standing in for rank 0 of a TP group of this size (collectives return local data): "
                          "prints the per-rank step time of the compute kernels only, never a bench line")
@@ -165,12 +167,14 @@ def main():
         args.nccl_baseline = True  # no symmetric-memory kernels without peers
     else:
         st = pstate.init(tp_size=args.gpus, pp_size=1, timeout_s=600)
+    # routed experts: whole experts per rank (EP) unless asked otherwise; attention stays tensor parallel
+    args.ep = args.config == 4 or args.ep or (args.gpus > 1 and not args.moe_tp)
     dev = st.device
     model_cfg = config3() if args.config == 3 else config4()
     total_len = args.prompt + args.output + 64
     cfg = EngineConfig(model=model_cfg,
                        parallel=ParallelConfig(tensor_parallel_size=args.gpus, fused_comm=not args.nccl_baseline,
-                                               expert_parallel=args.config == 4 or args.ep),
+                                               expert_parallel=args.ep),
                        scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
                                                  max_model_len=total_len, max_num_partial_prefills=args.batch),
                        cache=CacheConfig(num_blocks=args.batch * ((total_len + 63) // 64) + 1),
@@ -250,7 +254,7 @@ def main():
             "data": f"synthetic: random token ids, random-init weights of the config-{args.config} architecture",
             "config": {"model": MODEL_DESC[args.config],
                        "global_batch": args.batch, "seq_len": args.prompt, "output_len": args.output,
-                       "parallelism": (f"ep{args.gpus}+attn-tp{args.gpus}" if args.config == 4 or args.ep
+                       "parallelism": (f"ep{args.gpus}+attn-tp{args.gpus}" if args.ep and args.gpus > 1
                                        else f"tp{args.gpus}"),
                        "collectives": "fused symmetric-memory kernels" if fused else ("none" if args.gpus == 1 else "nccl"),
                        "l2": "no flush: each step streams the expert weights (GBs per GPU) >> 126 MB L2"},
