@@ -18,6 +18,8 @@ PROMPTS = [[(5 * i + 3 * j) % 500 for j in range(9 + 13 * i)] for i in range(3)]
 
 def _cfg(tp, fmt, pp=1):
     k = 0
+    hc = fmt.endswith("_hc")
+    fmt = fmt[:-3] if hc else fmt
     ep = fmt.endswith("_ep")
     fmt = fmt[:-3] if ep else fmt
     if fmt == "deepseek_mtp":  # Marlin experts, fp8 attention projections, MTP speculative decoding
@@ -29,6 +31,7 @@ def _cfg(tp, fmt, pp=1):
         m = tiny(layers=4, experts=4, hidden=256, expert_format=fmt)
         m.moe.intermediate = 256  # two H128 blocks: one per rank at TP=2
         m.moe.shared_intermediate = 256
+        m.hc_mult = 4 if hc else 0
     return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp, expert_parallel=ep,
                                                          pipeline_parallel_size=pp),
                         scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256,
@@ -63,7 +66,7 @@ def _worker(rank, world, port, fmt, path):
     pstate.destroy()
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "exl3", "deepseek_mtp", "exl3_ep", "deepseek_mtp_ep"])
+@pytest.mark.parametrize("fmt", ["bf16", "exl3", "deepseek_mtp", "exl3_ep", "deepseek_mtp_ep", "exl3_hc"])
 def test_tp2_matches_tp1(fmt):
     from vllm_cmp170hx_b200.parallel import state as pstate
 

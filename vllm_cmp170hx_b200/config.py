@@ -92,6 +92,13 @@ class ModelConfig:
     tie_embeddings: bool = False
     num_mtp_layers: int = 0
     dtype: str = "bfloat16"
+    # manifold-constrained hyper-connections: hc_mult residual streams (0: the plain residual);
+    # hc_delayed collapses each sublayer input with the previous boundary's pre (DeepSeek-V4.1 form)
+    hc_mult: int = 0
+    hc_sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
+    hc_post_mult: float = 2.0
+    hc_delayed: bool = False
 
     def __post_init__(self):
         if not self.layer_types:

@@ -191,6 +191,30 @@ struct KdaRecoverArgs {
 };
 cudaError_t kda_recover(const KdaRecoverArgs& a, cudaStream_t stream);
 
+// ---------------------------------------------------------------- mhc.cu
+// One mHC sublayer boundary per token: post of x into the streams (x nullable), coefficients of the
+// new streams (pre / post / Sinkhorn comb), and the next sublayer input RMSNorm(collapse).
+// mode 0: collapse with the fresh pre; 1: with pre_mix (carried); 2: stream 0.
+struct MhcArgs {
+  const __nv_bfloat16* x;      // [T, d] or nullptr
+  const __nv_bfloat16* H;      // [T, hc, d]
+  const float* post;           // [T, hc] (with x)
+  const float* comb;           // [T, hc, hc] (with x)
+  const float* fn;             // [2 hc + hc^2, hc d]
+  const float* scale;          // [3]
+  const float* base;           // [2 hc + hc^2]
+  const __nv_bfloat16* norm_w; // [d]
+  const float* pre_mix;        // [T, hc] (mode 1)
+  float rms_eps, eps, post_mult, norm_eps;
+  int iters, mode, T, hc, d;
+  __nv_bfloat16* H_out;  // may equal H
+  __nv_bfloat16* y;      // [T, d]
+  float* post_out;       // [T, hc]
+  float* comb_out;       // [T, hc, hc]
+  float* pre_out;        // [T, hc]
+};
+cudaError_t mhc_post_pre(const MhcArgs& a, cudaStream_t stream);
+
 // ---------------------------------------------------------------- mla_prep.cu / mla_attn.cu
 cudaError_t rope_apply(void* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
                        const int* positions, const float* cos_sin, int interleaved, int T, cudaStream_t stream);

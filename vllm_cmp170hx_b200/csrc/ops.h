@@ -38,6 +38,11 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                     const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
                     at::Tensor& state, at::Tensor& out, const c10::optional<at::Tensor>& verify,
                     const c10::optional<at::Tensor>& rec);
+void mhc_post_pre_op(const c10::optional<at::Tensor>& x, const at::Tensor& H, const c10::optional<at::Tensor>& post,
+                     const c10::optional<at::Tensor>& comb, const at::Tensor& fn, const at::Tensor& scale,
+                     const at::Tensor& base, const at::Tensor& norm_w, const c10::optional<at::Tensor>& pre_mix,
+                     double rms_eps, double eps, double post_mult, int64_t iters, double norm_eps, int64_t mode,
+                     at::Tensor& H_out, at::Tensor& y, at::Tensor& post_out, at::Tensor& comb_out, at::Tensor& pre_out);
 void kda_recover_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx, const at::Tensor& keep,
                     const at::Tensor& rec, at::Tensor& state, const at::Tensor& qkv,
                     const c10::optional<at::Tensor>& conv_state);  // kda.cu
@@ -125,6 +130,9 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor beta_raw, Tensor? g2, Tensor(a!) conv_state, Tensor? conv_w, Tensor? conv_b, Tensor a_log, "   \
     "Tensor? g_bias, float lower_bound, Tensor? norm_w, float eps, float l2_eps, float q_scale, "            \
     "bool l2norm, Tensor(b!) state, Tensor(c!) out, Tensor? verify=None, Tensor(d!)? rec=None) -> ()")       \
+  X("mhc_post_pre(Tensor? x, Tensor H, Tensor? post, Tensor? comb, Tensor fn, Tensor scale, Tensor base, "   \
+    "Tensor norm_w, Tensor? pre_mix, float rms_eps, float eps, float post_mult, int iters, float norm_eps, "  \
+    "int mode, Tensor(a!) H_out, Tensor(b!) y, Tensor(c!) post_out, Tensor(d!) comb_out, Tensor(e!) pre_out) -> ()") \
   X("kda_recover(Tensor cu_seqlens, Tensor? state_idx, Tensor keep, Tensor rec, Tensor(a!) state, "         \
     "Tensor qkv, Tensor(b!)? conv_state) -> ()")                                                          \
   X("kda_core(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor q, Tensor k, Tensor v, "      \
@@ -174,6 +182,7 @@ void register_host_bindings(pybind11::module_& m);
   X("kda_forward", b200::kda_forward_op)              \
   X("kda_core", b200::kda_core_op)                    \
   X("kda_recover", b200::kda_recover_op)              \
+  X("mhc_post_pre", b200::mhc_post_pre_op)            \
   X("rope", b200::rope_op)                            \
   X("mla_latent_cache_write", b200::mla_latent_cache_write_op) \
   X("mla_index_k_write", b200::mla_index_k_write_op)  \

@@ -718,4 +718,57 @@ void kda_recover_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
   B200_LAUNCH(kda_recover(a, cur_stream()));
 }
 
+void mhc_post_pre_op(const c10::optional<at::Tensor>& x, const at::Tensor& H, const c10::optional<at::Tensor>& post,
+                     const c10::optional<at::Tensor>& comb, const at::Tensor& fn, const at::Tensor& scale,
+                     const at::Tensor& base, const at::Tensor& norm_w, const c10::optional<at::Tensor>& pre_mix,
+                     double rms_eps, double eps, double post_mult, int64_t iters, double norm_eps, int64_t mode,
+                     at::Tensor& H_out, at::Tensor& y, at::Tensor& post_out, at::Tensor& comb_out, at::Tensor& pre_out) {
+  B200_CHECK_CUDA(H);
+  TORCH_CHECK(H.dim() == 3 && H.is_contiguous() && H.scalar_type() == at::kBFloat16, "mhc: H [T, hc, d] bf16");
+  const int64_t T = H.size(0), hc = H.size(1), d = H.size(2);
+  const int64_t N = 2 * hc + hc * hc;
+  TORCH_CHECK(fn.scalar_type() == at::kFloat && fn.is_contiguous() && fn.size(0) == N && fn.size(1) == hc * d,
+              "mhc: fn [2 hc + hc^2, hc d] fp32");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.numel() >= 3 && base.scalar_type() == at::kFloat &&
+                  base.numel() == N && norm_w.scalar_type() == at::kBFloat16 && norm_w.numel() == d,
+              "mhc: scale [3] / base [N] fp32, norm_w [d] bf16");
+  TORCH_CHECK(H_out.is_contiguous() && H_out.sizes() == H.sizes() && y.is_contiguous() && y.size(0) == T &&
+                  y.size(1) == d && post_out.is_contiguous() && comb_out.is_contiguous() && pre_out.is_contiguous(),
+              "mhc: output shapes");
+  if (x.has_value()) {
+    TORCH_CHECK(x->is_contiguous() && x->scalar_type() == at::kBFloat16 && x->size(0) == T && x->size(1) == d &&
+                    post.has_value() && comb.has_value() && post->is_contiguous() && comb->is_contiguous() &&
+                    post->scalar_type() == at::kFloat && comb->scalar_type() == at::kFloat,
+                "mhc: x [T, d] bf16 with post [T, hc] / comb [T, hc, hc] fp32");
+  }
+  TORCH_CHECK(mode != 1 || (pre_mix.has_value() && pre_mix->is_contiguous() && pre_mix->scalar_type() == at::kFloat),
+              "mhc: mode 1 needs pre_mix [T, hc] fp32");
+  c10::cuda::CUDAGuard g(H.device());
+  MhcArgs a{};
+  a.x = x.has_value() ? reinterpret_cast<const __nv_bfloat16*>(x->data_ptr()) : nullptr;
+  a.H = reinterpret_cast<const __nv_bfloat16*>(H.data_ptr());
+  a.post = post.has_value() ? post->data_ptr<float>() : nullptr;
+  a.comb = comb.has_value() ? comb->data_ptr<float>() : nullptr;
+  a.fn = fn.data_ptr<float>();
+  a.scale = scale.data_ptr<float>();
+  a.base = base.data_ptr<float>();
+  a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr());
+  a.pre_mix = pre_mix.has_value() ? pre_mix->data_ptr<float>() : nullptr;
+  a.rms_eps = (float)rms_eps;
+  a.eps = (float)eps;
+  a.post_mult = (float)post_mult;
+  a.norm_eps = (float)norm_eps;
+  a.iters = (int)iters;
+  a.mode = (int)mode;
+  a.T = (int)T;
+  a.hc = (int)hc;
+  a.d = (int)d;
+  a.H_out = reinterpret_cast<__nv_bfloat16*>(H_out.data_ptr());
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.post_out = post_out.data_ptr<float>();
+  a.comb_out = comb_out.data_ptr<float>();
+  a.pre_out = pre_out.data_ptr<float>();
+  B200_LAUNCH(mhc_post_pre(a, cur_stream()));
+}
+
 }  // namespace b200

@@ -26,6 +26,7 @@ from .. import ops
 from ..config import ModelConfig
 from ..formats import exl3 as fx
 from ..ops import kda as kda_ops
+from ..ops import mhc as mhc_ops
 from ..ops import mla as mla_ops
 from ..ops import moe as moe_ops
 from ..oracle import mla as mla_ref
@@ -374,6 +375,37 @@ class MoE(nn.Module):
 
 
 # ============================================================================ model
+class HyperConnection(nn.Module):
+    """Coefficient parameters of one mHC boundary: fn [2n + n^2, n d], scale [3], base [2n + n^2]
+    (fp32, replicated over tensor-parallel ranks)."""
+
+    def __init__(self, cfg: ModelConfig, wi: WeightInit):
+        super().__init__()
+        n, d = cfg.hc_mult, cfg.hidden_size
+        N = 2 * n + n * n
+        self.fn = nn.Parameter(wi.normal((N, n * d), (n * d) ** -0.5, dtype=torch.float32), requires_grad=False)
+        self.scale = nn.Parameter(wi.uniform((3,), 0.5, 1.5).float(), requires_grad=False)
+        self.base = nn.Parameter(wi.uniform((N,), -0.5, 0.5).float(), requires_grad=False)
+
+    def __call__(self, state: "HCState", norm: RMSNorm, cfg: ModelConfig) -> tuple["HCState", torch.Tensor]:
+        H, inp, post, comb, pre = mhc_ops.post_pre(
+            state.x, state.H, state.post, state.comb, self.fn, self.scale, self.base, norm.weight,
+            rms_eps=cfg.rms_eps, eps=cfg.hc_eps, post_mult=cfg.hc_post_mult, iters=cfg.hc_sinkhorn_iters,
+            norm_eps=norm.eps, delayed=cfg.hc_delayed, pre_mix=state.pre_mix)
+        return HCState(None, H, post, comb, pre if cfg.hc_delayed else None), inp
+
+
+@dataclass
+class HCState:
+    """The mHC residual between sublayers: streams H [T, n, d], the pending sublayer output x with
+    the post / comb it is applied with at the next boundary, and (delayed form) the carried pre."""
+    x: torch.Tensor | None
+    H: torch.Tensor
+    post: torch.Tensor | None = None
+    comb: torch.Tensor | None = None
+    pre_mix: torch.Tensor | None = None
+
+
 class DecoderLayer(nn.Module):
     def __init__(self, cfg: ModelConfig, idx: int, wi: WeightInit, tp: int, tp_rank: int):
         super().__init__()
@@ -389,6 +421,21 @@ class DecoderLayer(nn.Module):
             self.mlp = DenseMLP(cfg.hidden_size, cfg.dense_intermediate, wi, tp, tp_rank)
         else:
             self.mlp = None
+        self.cfg = cfg
+        if cfg.hc_mult:
+            self.hc_attn = HyperConnection(cfg, wi)
+            self.hc_mlp = HyperConnection(cfg, wi) if self.mlp is not None else None
+
+    def forward_hc(self, state: HCState, ctx: StepContext) -> HCState:
+        """mHC form: each sublayer reads the collapsed, normalised streams at its boundary and
+        leaves its output pending for the next boundary's post."""
+        state, h = self.hc_attn(state, self.input_norm, self.cfg)
+        state.x = self.attn(h, ctx, self.idx)
+        if self.mlp is not None:
+            # the attention output's post, then the MLP input, in one boundary op
+            state, h = self.hc_mlp(state, self.post_norm, self.cfg)
+            state.x = self.mlp(h, reduce=True)
+        return state
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None, ctx: StepContext):
         if residual is None:
@@ -447,11 +494,22 @@ class HybridForCausalLM(nn.Module):
             if (self.last or init_mode == "sliced") else None
         self.norm = RMSNorm(norm_w, cfg.rms_eps) if self.last else None
         self.lm_head = Linear(head) if self.last else None
+        if cfg.hc_mult:
+            if st.pp_size > 1:
+                raise NotImplementedError("hyper-connection streams across pipeline stages are not supported")
+            # the final boundary: the last sublayer's post, then the head collapse + final norm
+            self.hc_head = HyperConnection(cfg, wi)
 
     def forward(self, input_ids: torch.Tensor, ctx: StepContext,
                 hidden_in: tuple[torch.Tensor, torch.Tensor] | None = None):
         """First stage: token ids; later stages: `hidden_in` = the previous stage's (hidden, residual).
         Returns the normed final hidden on the last stage, else this stage's (hidden, residual)."""
+        if self.cfg.hc_mult:
+            e = self.embed[input_ids]
+            state = HCState(None, e.unsqueeze(1).repeat(1, self.cfg.hc_mult, 1).contiguous())
+            for layer in self.layers:
+                state = layer.forward_hc(state, ctx)
+            return self.hc_head(state, self.norm, self.cfg)[1]
         if self.first:
             x, residual = self.embed[input_ids], None
         else:

@@ -28,7 +28,9 @@ class MTPHead(nn.Module):
         H = cfg.hidden_size
         self.layer_id = cfg.num_layers  # cache key of the MTP layer
         # the MTP layer is an MLA layer with the model's MLP type of the last layer
-        mcfg = ModelConfig.from_dict({**_cfg_dict(cfg), "num_layers": cfg.num_layers + 1,
+        # (a plain residual inside the MTP layer even when the target widens its residual into
+        # hyper-connection streams: the head consumes the target's final, collapsed hidden state)
+        mcfg = ModelConfig.from_dict({**_cfg_dict(cfg), "num_layers": cfg.num_layers + 1, "hc_mult": 0,
                                       "layer_types": cfg.layer_types + ["mla"],
                                       "mlp_types": cfg.mlp_types + [cfg.mlp_types[-1]]})
         self.enorm = RMSNorm(wi.ones_plus(H, 0.05), cfg.rms_eps)
