@@ -83,6 +83,40 @@ class Linear(nn.Module):
         return comm.gemm_all_reduce(x, self.weight, self.bias)
 
 
+class GroupedLinear(nn.Module):
+    """Block-diagonal projection: x [T, G, in] -> [T, G * out], output group g = x[:, g] W_g^T.
+
+    bf16 groups run as one GEMM per group straight off the strided input view and into their
+    column slice of the output (no copies); fp8 block-scaled groups (`fmt="fp8_block"`, the
+    DeepSeek-V4.1 `wo_a` form) go through the fp8 dequant GEMM per group.  The reference runs a
+    block-diagonal layer of any linear method group by group the same way
+    (vllm_sm80/layers/grouped_linear.py:35-94)."""
+
+    def __init__(self, weights: torch.Tensor, fmt: str = "bf16"):
+        super().__init__()
+        G, out_g, _ = weights.shape
+        self.groups, self.out_g, self.fmt = G, out_g, fmt
+        if fmt == "bf16":
+            self.weight = nn.Parameter(weights.contiguous(), requires_grad=False)
+        elif fmt == "fp8_block":
+            from .marlin_experts import Fp8Proj
+
+            self.parts = nn.ModuleList([Fp8Proj(weights[g]) for g in range(G)])
+        else:
+            raise ValueError(f"unknown grouped linear format {fmt!r}")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dim() != 3 or x.shape[1] != self.groups:
+            raise ValueError(f"grouped input must be [tokens, {self.groups}, in]")
+        if self.fmt != "bf16":
+            return torch.cat([p(x[:, g]) for g, p in enumerate(self.parts)], dim=-1)
+        T = x.shape[0]
+        out = torch.empty(T, self.groups * self.out_g, dtype=torch.bfloat16, device=x.device)
+        for g in range(self.groups):
+            ops.gemm(x[:, g], self.weight[g], out=out[:, g * self.out_g:(g + 1) * self.out_g])
+        return out
+
+
 class RMSNorm(nn.Module):
     def __init__(self, weight: torch.Tensor, eps: float):
         super().__init__()
