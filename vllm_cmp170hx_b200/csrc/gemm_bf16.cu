@@ -761,6 +761,45 @@ constexpr int kMaxClusterSplits = 8;
 
 bool gemm_bf16_uses_partial(int M, int splits) { return splits > kMaxClusterSplits || (splits > 1 && M > 128); }
 
+// How many clusters of `s` CTAs of the cluster kernel can be resident at once (one wave), cached.
+static int csk_max_active(int bn, int s) {
+  using namespace gemm;
+  static int cache[5][kMaxClusterSplits + 1] = {};
+  const int bi = bn <= 16 ? 0 : bn <= 32 ? 1 : bn <= 64 ? 2 : 3;
+  int& c = cache[bi][s];
+  if (c == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = s;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(s * 64);
+    cfg.blockDim = dim3(kThreads);
+    int n = 0;
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (bi) {
+#define B200_CSK_OCC(BN_)                                                                                       \
+  {                                                                                                            \
+    cfg.dynamicSmemBytes = CskPlan<BN_>::SMEM_BYTES;                                                            \
+    cudaFuncSetAttribute(gemm_bf16_csk_kernel<BN_>, cudaFuncAttributeMaxDynamicSharedMemorySize,               \
+                         CskPlan<BN_>::SMEM_BYTES);                                                             \
+    e = cudaOccupancyMaxActiveClusters(&n, gemm_bf16_csk_kernel<BN_>, &cfg);                                   \
+    break;                                                                                                     \
+  }
+      case 0: B200_CSK_OCC(16)
+      case 1: B200_CSK_OCC(32)
+      case 2: B200_CSK_OCC(64)
+      default: B200_CSK_OCC(128)
+#undef B200_CSK_OCC
+    }
+    c = (e == cudaSuccess && n > 0) ? n : std::max(1, device_sm_count() / s);
+  }
+  return c;
+}
+
 // Number of K splits the launcher uses for this shape (splits_req > 0 forces it).
 int gemm_bf16_splits(int M, int N, int K, int splits_req) {
   using namespace gemm;
@@ -775,8 +814,11 @@ int gemm_bf16_splits(int M, int N, int K, int splits_req) {
   if (splits_req > 0) {
     splits = splits_req;
   } else if (tiles < sms) {
-    // K split over a cluster of at most 8 CTAs per tile, at least 2 K blocks each
+    // K split over a cluster of at most 8 CTAs per tile, at least 2 K blocks each, and no more
+    // splits than leave every tile's cluster resident in one wave
     splits = std::max(1, std::min(std::min(kMaxClusterSplits, sms / tiles), kb_total / 2));
+    if (M <= 128 && bn <= 128)
+      while (splits > 1 && csk_max_active(bn, splits) < tiles) --splits;
   }
   splits = std::max(1, std::min(splits, kb_total));
   const int per = (kb_total + splits - 1) / splits;
