@@ -59,6 +59,7 @@ __device__ __forceinline__ uint32_t* flag_ptr(uint64_t base, int block, int src,
 }
 
 __global__ void __launch_bounds__(kThreads) oneshot_all_reduce_kernel(ArParams p) {
+  pdl_prologue();
   __shared__ uint32_t s_epoch;
   __shared__ int s_fail;
   const int b = blockIdx.x;
@@ -126,7 +127,7 @@ cudaError_t symm_all_reduce(const void* in, void* out, int64_t n, const uint64_t
   if (n == 0) return cudaSuccess;
   comm::ArParams p{reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), n, peers, rank,
                    world, data_off, half_bytes, epochs, status, timeout_ns};
-  comm::oneshot_all_reduce_kernel<<<blocks, comm::kThreads, 0, stream>>>(p);
+  launch_pdl(comm::oneshot_all_reduce_kernel, dim3(blocks), dim3(comm::kThreads), 0, stream, p);
   return cudaGetLastError();
 }
 

@@ -8,6 +8,7 @@
 // that runs out records an error code in a device word the host reads, and
 // the caller unwinds (it never traps).
 #pragma once
+#include <utility>
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -85,6 +86,35 @@ B200_DEVICE void fence_proxy_async_smem() {
 
 B200_DEVICE void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of this package is launched with
+// programmatic stream serialisation (`launch_pdl`) and starts with `pdl_prologue()`:
+// it waits for the previous kernel in the stream to complete (and its memory to
+// be visible) before touching anything, then lets the next kernel launch.  So a
+// kernel's CTAs are scheduled, and reach that wait, while its predecessor
+// drains, instead of after it (the per-launch gap of CUDA-graph decode steps).
+// ---------------------------------------------------------------------------
+B200_DEVICE void pdl_prologue() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

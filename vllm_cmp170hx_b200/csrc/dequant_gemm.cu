@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tma_w0, const __grid_constant__ CUtensorMap tma_w1,
                         const __grid_constant__ CUtensorMap tma_s0, const __grid_constant__ CUtensorMap tma_s1,
                         Params p, Plan pl) {
+  pdl_prologue();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int tile_rows = p.tile_rows;
@@ -433,6 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // out[r, :] = x[src(r), :] converted to the operand type (bf16 copy or fp16).
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, int K,
                                    const int* __restrict__ src, void* out, int to_f16, int rows) {
+  pdl_prologue();
   const int r = blockIdx.x;
   if (r >= rows) return;
   const int s = src ? src[r] : r;
@@ -486,7 +488,7 @@ cudaError_t launch(const DequantGemmArgs& a, const Params& p, cudaStream_t strea
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
   const int grid = std::max(1, std::min(a.max_work, device_sm_count()));
-  kern<<<grid, kThreads, pl.smem, stream>>>(b0, b1, w0, w1, s0, s1, p, pl);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), pl.smem, stream, b0, b1, w0, w1, s0, s1, p, pl);
   return cudaGetLastError();
 }
 
@@ -523,7 +525,7 @@ cudaError_t gather_rows(const void* x, int64_t ld_x, int K, const int* src, void
                         cudaStream_t stream) {
   if (K % 8 || ld_x % 8) return cudaErrorInvalidValue;
   if (rows == 0) return cudaSuccess;
-  dq::gather_rows_kernel<<<rows, 128, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), ld_x, K, src, out, to_f16,
+  launch_pdl(dq::gather_rows_kernel, dim3(rows), dim3(128), 0, stream, reinterpret_cast<const __nv_bfloat16*>(x), ld_x, K, src, out, to_f16,
                                                    rows);
   return cudaGetLastError();
 }

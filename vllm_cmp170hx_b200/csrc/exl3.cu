@@ -402,6 +402,7 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
   }
   tc_fence_before();
   __syncthreads();
+  pdl_prologue();  // setup above overlaps the previous kernel's tail
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -676,6 +677,7 @@ __global__ void input_rotate_kernel(const __nv_bfloat16* __restrict__ x, int64_t
                                     int E_local, const __half* __restrict__ suh0, const __half* __restrict__ suh1,
                                     int64_t suh_estride, __half* __restrict__ out0, __half* __restrict__ out1,
                                     int rows) {
+  pdl_prologue();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   const int nblk = K / 128;
@@ -737,6 +739,7 @@ __global__ void combine_kernel(const float* __restrict__ y, int64_t ld_y, const 
                                const float* __restrict__ sorted_weight, int k, int H,
                                const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out,
                                int64_t ld_out, float* __restrict__ out_f32) {
+  pdl_prologue();
   const int t = blockIdx.x;
   const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (c >= H) return;
@@ -801,7 +804,7 @@ cudaError_t launch_gemm(const GemmParams& p, const void* b0, const void* b1, int
   auto kern = exl3_gemm_kernel<NMAT, CB, FAST>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreadsStaged, pl.smem, stream>>>(m0, m1, t0, t1, p, pl);
+  launch_pdl(kern, dim3(grid), dim3(kThreadsStaged), pl.smem, stream, m0, m1, t0, t1, p, pl);
   return cudaGetLastError();
 }
 
@@ -826,7 +829,7 @@ cudaError_t exl3_input_rotate(const void* x, int64_t ld_x, int in_features, int 
   if (rows == 0) return cudaSuccess;
   const int warps = rows * (K / 128);
   const int threads = 256;
-  exl3::input_rotate_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, stream>>>(
+  launch_pdl(exl3::input_rotate_kernel, dim3((warps * 32 + threads - 1) / threads), dim3(threads), 0, stream, 
       reinterpret_cast<const __nv_bfloat16*>(x), ld_x, in_features, K, sorted_token, expert_offsets, E_local,
       reinterpret_cast<const __half*>(suh0), reinterpret_cast<const __half*>(suh1), suh_estride,
       reinterpret_cast<__half*>(out0), reinterpret_cast<__half*>(out1), rows);
@@ -868,7 +871,7 @@ cudaError_t moe_combine(const float* y, int64_t ld_y, const int* slot_of, const 
                         int H, const void* add, void* out, int64_t ld_out, float* out_f32, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   dim3 grid(T, (H + 4 * 128 - 1) / (4 * 128));
-  exl3::combine_kernel<<<grid, 128, 0, stream>>>(y, ld_y, slot_of, sorted_weight, k, H,
+  launch_pdl(exl3::combine_kernel, dim3(grid), dim3(128), 0, stream, y, ld_y, slot_of, sorted_weight, k, H,
                                               reinterpret_cast<const __nv_bfloat16*>(add),
                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_f32);
   return cudaGetLastError();

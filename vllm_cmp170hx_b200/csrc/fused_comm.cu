@@ -42,6 +42,7 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
 }
 
 __global__ void __launch_bounds__(kThreads) combine_allreduce_kernel(CombineArArgs p) {
+  pdl_prologue();
   __shared__ uint32_t s_epoch;
   __shared__ int s_fail;
   const int b = blockIdx.x;
@@ -134,7 +135,7 @@ cudaError_t combine_allreduce(const CombineArArgs& a, int blocks, cudaStream_t s
   if (a.H % 8 || a.world < 1 || a.world > 32 || blocks < 1 || (a.ld_y % 4)) return cudaErrorInvalidValue;
   if ((int64_t)a.T * a.H * 2 > a.slot_bytes) return cudaErrorInvalidValue;
   if (a.T == 0) return cudaSuccess;
-  fused::combine_allreduce_kernel<<<blocks, fused::kThreads, 0, stream>>>(a);
+  launch_pdl(fused::combine_allreduce_kernel, dim3(blocks), dim3(fused::kThreads), 0, stream, a);
   return cudaGetLastError();
 }
 

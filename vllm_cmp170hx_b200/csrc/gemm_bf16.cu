@@ -112,7 +112,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    if (p.ar) *s_epoch = p.epochs[blockIdx.x] + 1;
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
@@ -137,6 +136,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  pdl_prologue();  // setup above overlaps the previous kernel's tail
+  if (p.ar) {  // this CTA's call counter (written by the previous call of this kernel)
+    if (threadIdx.x == 0) *s_epoch = p.epochs[blockIdx.x] + 1;
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // bf16 output, transposed: staged in smem, written as 16-byte runs of features (a token's row)
@@ -535,6 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   // peers copy into this CTA's slots and signal its barrier: all initialised first
   cluster_sync_all();
+  pdl_prologue();  // setup above overlaps the previous kernel's tail
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -681,6 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ C,
                                      float* __restrict__ Cf, int rows, int cols, int ldc, int splits,
                                      const __nv_bfloat16* __restrict__ bias, int bias_on_rows) {
+  pdl_prologue();
   const size_t n = (size_t)rows * cols;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     float s = 0.f;
@@ -705,7 +711,7 @@ cudaError_t launch(const void* A, int64_t lda, int rows_a, const void* B, int64_
   auto kern = gemm_bf16_tn_kernel<BN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, C_::SMEM_BYTES, stream>>>(ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), C_::SMEM_BYTES, stream, ta, tb, p);
   return cudaGetLastError();
 }
 
@@ -728,13 +734,15 @@ cudaError_t launch_csk(const void* A, int64_t lda, int rows_a, const void* B, in
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = P_::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = p.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
@@ -882,7 +890,7 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   // partial is [splits, M, N] in output orientation.
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>(((int64_t)a.M * a.N + threads - 1) / threads, (int64_t)sms * 8);
-  splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(p.partial, p.C, p.Cf, a.M, a.N, (int)a.ldc, splits,
+  launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(threads), 0, stream, p.partial, p.C, p.Cf, a.M, a.N, (int)a.ldc, splits,
                                                        reinterpret_cast<const __nv_bfloat16*>(a.bias), 0);
   return cudaGetLastError();
 }

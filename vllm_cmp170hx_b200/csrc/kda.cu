@@ -40,6 +40,7 @@ struct ItemIn {
 
 template <bool FULL>
 __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
+  pdl_prologue();
   // Persistent: CTA c runs the (sequence, head) items c, c + grid, ...  The next item's 64 KiB
   // state is bulk-copied into the other half of a shared double buffer while this item computes,
   // and each item's final state is written straight from registers, so state reads and writes
@@ -325,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
 // in the same order, as the recurrence itself, so the result equals having run only those tokens),
 // then the conv window advanced past them.
 __global__ void __launch_bounds__(kThreads) kda_recover_kernel(KdaRecoverArgs p) {
+  pdl_prologue();
   const int seq = blockIdx.x / p.H;
   const int h = blockIdx.x % p.H;
   const int n = p.keep[seq];
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kThreads) kda_recover_kernel(KdaRecoverArgs p)
 
 cudaError_t kda_recover(const KdaRecoverArgs& a, cudaStream_t stream) {
   if (a.num_seqs == 0) return cudaSuccess;
-  kda::kda_recover_kernel<<<a.num_seqs * a.H, kda::kThreads, 0, stream>>>(a);
+  launch_pdl(kda::kda_recover_kernel, dim3(a.num_seqs * a.H), dim3(kda::kThreads), 0, stream, a);
   return cudaGetLastError();
 }
 
@@ -409,7 +411,7 @@ cudaError_t kda_recurrent(const KdaArgs& a, cudaStream_t stream) {
   auto kern = a.full ? kda::kda_recurrent_kernel<true> : kda::kda_recurrent_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kda::kThreads, smem, stream>>>(a);
+  launch_pdl(kern, dim3(grid), dim3(kda::kThreads), smem, stream, a);
   return cudaGetLastError();
 }
 

@@ -25,6 +25,7 @@ constexpr int kWarps = kThreads / 32;
 
 template <int HC>
 __global__ void __launch_bounds__(kThreads) post_pre_kernel(MhcArgs a) {
+  pdl_prologue();
   constexpr int N = 2 * HC + HC * HC;
   extern __shared__ uint8_t smem_raw[];
   const int d = a.d;
@@ -198,7 +199,7 @@ cudaError_t mhc_post_pre(const MhcArgs& a, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(post_pre_kernel<HC>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                          (int)smem);                                                        \
     if (e != cudaSuccess) return e;                                                                          \
-    post_pre_kernel<HC><<<a.T, kThreads, smem, stream>>>(a);                                                 \
+    launch_pdl(post_pre_kernel<HC>, dim3(a.T), dim3(kThreads), smem, stream, a);                                                 \
     break;                                                                                                    \
   }
     B200_MHC_CASE(2)

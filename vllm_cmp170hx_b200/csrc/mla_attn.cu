@@ -55,6 +55,7 @@ struct Params {
 
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constant__ CUtensorMap tma_q, Params p) {
+  pdl_prologue();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sa = smem;
@@ -210,6 +211,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 // merge split partials: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s
 __global__ void merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits, int T,
                              int nh, __nv_bfloat16* __restrict__ out, float* __restrict__ lse) {
+  pdl_prologue();
   const int th = blockIdx.x;  // t * nh + h
   float M = -INFINITY;
   for (int s = 0; s < splits; ++s) M = fmaxf(M, part_ml[((int64_t)s * T * nh + th) * 2]);
@@ -311,6 +313,7 @@ B200_DEVICE void cp_async_arrive(uint64_t* bar) {
 
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_attn_block_kernel(const __grid_constant__ CUtensorMap tma_q, Params p) {
+  pdl_prologue();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sq = smem + OFF_Q;
@@ -674,7 +677,7 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
   const int sms = device_sm_count();
   int ysplit = std::max(1, std::min(tiles, (2 * sms + T - 1) / T));
   dim3 grid(T, ysplit);
-  indexer_kernel<<<grid, kThreads, SMEM, stream>>>(tk, tq, p);
+  launch_pdl(indexer_kernel, dim3(grid), dim3(kThreads), SMEM, stream, tk, tq, p);
   return cudaGetLastError();
 }
 
@@ -704,10 +707,10 @@ cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache
   cudaError_t e = cudaFuncSetAttribute(sparse_attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(T, (nh + 127) / 128, 2 * splits);
-  sparse_attn_block_kernel<<<grid, kThreads, SMEM, stream>>>(tq, p);
+  launch_pdl(sparse_attn_block_kernel, dim3(grid), dim3(kThreads), SMEM, stream, tq, p);
   e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
-  mla::attn::merge_kernel<<<T * nh, 128, 0, stream>>>(part_o, part_ml, splits, T, nh,
+  launch_pdl(mla::attn::merge_kernel, dim3(T * nh), dim3(128), 0, stream, part_o, part_ml, splits, T, nh,
                                                       reinterpret_cast<__nv_bfloat16*>(out), lse);
   return cudaGetLastError();
 }

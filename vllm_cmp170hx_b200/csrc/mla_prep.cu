@@ -29,6 +29,7 @@ __device__ __forceinline__ void rot(float& a, float& b, float c, float s) {
 __global__ void rope_kernel(__nv_bfloat16* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
                             const int* __restrict__ positions, const float* __restrict__ cos_sin, int interleaved,
                             int T) {
+  pdl_prologue();
   const int half = rot_dim / 2;
   const int64_t total = (int64_t)T * nheads * half;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -53,6 +54,7 @@ __global__ void latent_cache_write_kernel(const __nv_bfloat16* __restrict__ kv, 
                                           const int* __restrict__ positions, const float* __restrict__ cos_sin,
                                           int interleaved, const int64_t* __restrict__ slots,
                                           __nv_bfloat16* __restrict__ cache, int T) {
+  pdl_prologue();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
@@ -139,6 +141,7 @@ __global__ void index_k_write_kernel(const __nv_bfloat16* __restrict__ k, int64_
                                      float eps, const int* __restrict__ positions, const float* __restrict__ cos_sin,
                                      int rope_dim, int interleaved, const int64_t* __restrict__ slots,
                                      uint8_t* __restrict__ cache, float* __restrict__ cache_scale, int T) {
+  pdl_prologue();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
@@ -176,6 +179,7 @@ __global__ void index_q_prep_kernel(const __nv_bfloat16* __restrict__ q, int64_t
                                     const int* __restrict__ positions, const float* __restrict__ cos_sin, int rope_dim,
                                     int interleaved, const __nv_bfloat16* __restrict__ w, int64_t ld_w, float wscale,
                                     uint8_t* __restrict__ q8, float* __restrict__ w_out, int T) {
+  pdl_prologue();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (gw >= T * nheads) return;
@@ -256,6 +260,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restr
                                                             const int* __restrict__ block_table, int64_t ld_bt,
                                                             int block_size, int* __restrict__ out_idx,
                                                             int* __restrict__ out_count) {
+  pdl_prologue();
   extern __shared__ uint32_t skeys[];
   constexpr int NBIN = 2048;
   __shared__ int hist[NBIN];
@@ -434,7 +439,7 @@ cudaError_t rope_apply(void* x, int64_t ld_tok, int64_t ld_head, int nheads, int
   const int64_t total = (int64_t)T * nheads * (rot_dim / 2);
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
-  mla::rope_kernel<<<blocks, threads, 0, stream>>>(reinterpret_cast<__nv_bfloat16*>(x), ld_tok, ld_head, nheads,
+  launch_pdl(mla::rope_kernel, dim3(blocks), dim3(threads), 0, stream, reinterpret_cast<__nv_bfloat16*>(x), ld_tok, ld_head, nheads,
                                                    offset, rot_dim, positions, cos_sin, interleaved, T);
   return cudaGetLastError();
 }
@@ -443,7 +448,7 @@ cudaError_t mla_latent_cache_write(const void* kv, int64_t ld_kv, const void* no
                                    const float* cos_sin, int interleaved, const int64_t* slots, void* cache, int T,
                                    cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  mla::latent_cache_write_kernel<<<(T * 32 + 255) / 256, 256, 0, stream>>>(
+  launch_pdl(mla::latent_cache_write_kernel, dim3((T * 32 + 255) / 256), dim3(256), 0, stream, 
       reinterpret_cast<const __nv_bfloat16*>(kv), ld_kv, reinterpret_cast<const __nv_bfloat16*>(norm_w), eps,
       positions, cos_sin, interleaved, slots, reinterpret_cast<__nv_bfloat16*>(cache), T);
   return cudaGetLastError();
@@ -453,7 +458,7 @@ cudaError_t mla_index_k_write(const void* k, int64_t ld_k, const void* ln_w, con
                               const int* positions, const float* cos_sin, int rope_dim, int interleaved,
                               const int64_t* slots, void* cache, float* cache_scale, int T, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  mla::index_k_write_kernel<<<(T * 32 + 255) / 256, 256, 0, stream>>>(
+  launch_pdl(mla::index_k_write_kernel, dim3((T * 32 + 255) / 256), dim3(256), 0, stream, 
       reinterpret_cast<const __nv_bfloat16*>(k), ld_k, reinterpret_cast<const __nv_bfloat16*>(ln_w),
       reinterpret_cast<const __nv_bfloat16*>(ln_b), eps, positions, cos_sin, rope_dim, interleaved, slots,
       reinterpret_cast<uint8_t*>(cache), cache_scale, T);
@@ -465,7 +470,7 @@ cudaError_t mla_index_q_prep(const void* q, int64_t ld_tok, int nheads, const in
                              float* w_out, int T, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   const int warps = T * nheads;
-  mla::index_q_prep_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(
+  launch_pdl(mla::index_q_prep_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, stream, 
       reinterpret_cast<const __nv_bfloat16*>(q), ld_tok, nheads, positions, cos_sin, rope_dim, interleaved,
       reinterpret_cast<const __nv_bfloat16*>(w), ld_w, wscale, reinterpret_cast<uint8_t*>(q8), w_out, T);
   return cudaGetLastError();
@@ -481,10 +486,10 @@ cudaError_t mla_topk(const float* scores, int64_t ld_scores, const int* ctx_lens
     cudaError_t e = cudaFuncSetAttribute(mla::topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)cache_bytes);
     if (e != cudaSuccess) return e;
-    mla::topk_kernel<true><<<T, mla::kTopkThreads, cache_bytes, stream>>>(
+    launch_pdl(mla::topk_kernel<true>, dim3(T), dim3(mla::kTopkThreads), cache_bytes, stream, 
         scores, ld_scores, ctx_lens, k, token_seq, block_table, ld_bt, block_size, out_idx, out_count);
   } else {
-    mla::topk_kernel<false><<<T, mla::kTopkThreads, 0, stream>>>(scores, ld_scores, ctx_lens, k, token_seq,
+    launch_pdl(mla::topk_kernel<false>, dim3(T), dim3(mla::kTopkThreads), 0, stream, scores, ld_scores, ctx_lens, k, token_seq,
                                                                  block_table, ld_bt, block_size, out_idx, out_count);
   }
   return cudaGetLastError();

@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* o
                                                                 __nv_bfloat16* __restrict__ residual, int ld_res,
                                                                 const __nv_bfloat16* __restrict__ w, int H,
                                                                 float eps) {
+  pdl_prologue();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nvec = H / 8;
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* o
 
 __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, int64_t ld_out, const __nv_bfloat16* __restrict__ x,
                                 int64_t ld_x, int T, int I, float limit) {
+  pdl_prologue();
   const int64_t total = (int64_t)T * (I / 2);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int t = i / (I / 2);
@@ -113,7 +115,7 @@ cudaError_t silu_mul(void* out, int64_t ld_out, const void* x, int64_t ld_x, int
   if (T == 0) return cudaSuccess;
   const int64_t total = (int64_t)T * (I / 2);
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
-  silu_mul_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<__nv_bfloat16*>(out), ld_out,
+  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, stream, reinterpret_cast<__nv_bfloat16*>(out), ld_out,
                                               reinterpret_cast<const __nv_bfloat16*>(x), ld_x, T, I, limit);
   return cudaGetLastError();
 }
@@ -122,7 +124,7 @@ cudaError_t rms_norm(void* out, int64_t ld_out, const void* x, int64_t ld_x, con
                      cudaStream_t stream) {
   if (H % 8 != 0 || H > kNormThreads * kMaxVec * 8 || ld_x % 8 != 0 || ld_out % 8 != 0) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  rms_norm_kernel<0><<<T, kNormThreads, 0, stream>>>(
+  launch_pdl(rms_norm_kernel<0>, dim3(T), dim3(kNormThreads), 0, stream, 
       reinterpret_cast<__nv_bfloat16*>(out), (int)ld_out, reinterpret_cast<const __nv_bfloat16*>(x), (int)ld_x,
       nullptr, 0, reinterpret_cast<const __nv_bfloat16*>(w), H, eps);
   return cudaGetLastError();
@@ -132,7 +134,7 @@ cudaError_t fused_add_rms_norm(void* x, int64_t ld_x, void* residual, int64_t ld
                                float eps, cudaStream_t stream) {
   if (H % 8 != 0 || H > kNormThreads * kMaxVec * 8 || ld_x % 8 != 0 || ld_res % 8 != 0) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  rms_norm_kernel<1><<<T, kNormThreads, 0, stream>>>(
+  launch_pdl(rms_norm_kernel<1>, dim3(T), dim3(kNormThreads), 0, stream, 
       reinterpret_cast<__nv_bfloat16*>(x), (int)ld_x, reinterpret_cast<const __nv_bfloat16*>(x), (int)ld_x,
       reinterpret_cast<__nv_bfloat16*>(residual), (int)ld_res, reinterpret_cast<const __nv_bfloat16*>(w), H, eps);
   return cudaGetLastError();

@@ -24,6 +24,7 @@ constexpr int kMaxExpertsPerLane = 16;  // E <= 512
 __global__ void topk_kernel(const float* __restrict__ logits, int T, int E, int k, int mode,
                             const float* __restrict__ bias, float scale, int renorm, int* __restrict__ ids,
                             float* __restrict__ weights) {
+  pdl_prologue();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= T) return;
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     int E_map, int E_local, int tile_rows, int* __restrict__ sorted_token, float* __restrict__ sorted_weight,
     int* __restrict__ slot_of, int4* __restrict__ items, int* __restrict__ num_items, int* __restrict__ expert_offsets,
     int max_items) {
+  pdl_prologue();
   extern __shared__ int sm[];
   int* counts = sm;                         // [E_local]
   int* base = sm + E_local;                 // [E_local]  running base during placement
@@ -249,7 +251,7 @@ cudaError_t moe_topk(const float* logits, int T, int E, int k, int mode, const f
   if (T == 0) return cudaSuccess;
   const int threads = 256;
   const int blocks = (T * 32 + threads - 1) / threads;
-  topk_kernel<<<blocks, threads, 0, stream>>>(logits, T, E, k, mode, bias, scale, renorm, ids, weights);
+  launch_pdl(topk_kernel, dim3(blocks), dim3(threads), 0, stream, logits, T, E, k, mode, bias, scale, renorm, ids, weights);
   return cudaGetLastError();
 }
 
@@ -262,7 +264,7 @@ cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, i
   cudaError_t e = cudaFuncSetAttribute(build_assignments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
-  build_assignments_kernel<<<1, kBuildThreads, smem, stream>>>(ids, weights, T * k, k, expert_map,
+  launch_pdl(build_assignments_kernel, dim3(1), dim3(kBuildThreads), smem, stream, ids, weights, T * k, k, expert_map,
                                                                expert_map ? E_map : E_local, E_local,
                                                                tile_rows, sorted_token, sorted_weight, slot_of, items,
                                                                num_items, expert_offsets, max_items);

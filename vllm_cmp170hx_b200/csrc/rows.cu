@@ -25,6 +25,7 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
 
 __global__ void dequant_rows_kernel(const uint8_t* __restrict__ rows, int64_t row_bytes, int D,
                                     const uint8_t* __restrict__ failed, __nv_bfloat16* __restrict__ out, int n) {
+  pdl_prologue();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= n) return;
   const uint8_t* row = rows + (int64_t)warp * row_bytes;
@@ -62,7 +63,7 @@ cudaError_t dequant_rows_e4m3(const void* rows, int64_t row_bytes, int D, const 
   if (D % 256 != 0 || row_bytes < D + D / 32 || row_bytes % 8 != 0) return cudaErrorInvalidValue;
   if (n == 0) return cudaSuccess;
   const int threads = 256, warps = threads / 32;
-  dequant_rows_kernel<<<(n + warps - 1) / warps, threads, 0, stream>>>(
+  launch_pdl(dequant_rows_kernel, dim3((n + warps - 1) / warps), dim3(threads), 0, stream, 
       reinterpret_cast<const uint8_t*>(rows), row_bytes, D, failed, reinterpret_cast<__nv_bfloat16*>(out), n);
   return cudaGetLastError();
 }

@@ -38,6 +38,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const T* __restrict__ 
                                                           const float* __restrict__ temperature, uint64_t seed,
                                                           const int64_t* __restrict__ step, int vocab_offset,
                                                           float* __restrict__ out_val, int* __restrict__ out_idx) {
+  pdl_prologue();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int row = blockIdx.x;
@@ -88,6 +89,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const T* __restrict__ 
 // Combine per-rank winners [R, rows] -> token ids [rows] (first max, lowest index).
 __global__ void combine_kernel(const float* __restrict__ vals, const int* __restrict__ idx, int R, int rows,
                                int64_t* __restrict__ out) {
+  pdl_prologue();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   float b = -INFINITY;
@@ -103,18 +105,18 @@ cudaError_t sample_rows(const void* logits, int dtype /*0 bf16, 1 fp32*/, int64_
                         int* out_idx, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
   if (dtype == 0)
-    sample_kernel<__nv_bfloat16><<<rows, kThreads, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ld, V,
+    launch_pdl(sample_kernel<__nv_bfloat16>, dim3(rows), dim3(kThreads), 0, stream, reinterpret_cast<const __nv_bfloat16*>(logits), ld, V,
                                                                 temperature, seed, step, vocab_offset, out_val,
                                                                 out_idx);
   else
-    sample_kernel<float><<<rows, kThreads, 0, stream>>>(reinterpret_cast<const float*>(logits), ld, V, temperature,
+    launch_pdl(sample_kernel<float>, dim3(rows), dim3(kThreads), 0, stream, reinterpret_cast<const float*>(logits), ld, V, temperature,
                                                         seed, step, vocab_offset, out_val, out_idx);
   return cudaGetLastError();
 }
 
 cudaError_t sample_combine(const float* vals, const int* idx, int R, int rows, int64_t* out, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
-  combine_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(vals, idx, R, rows, out);
+  launch_pdl(combine_kernel, dim3((rows + 127) / 128), dim3(128), 0, stream, vals, idx, R, rows, out);
   return cudaGetLastError();
 }
 

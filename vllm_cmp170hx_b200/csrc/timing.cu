@@ -14,11 +14,13 @@ namespace b200 {
 namespace {
 
 __global__ void stamp_kernel(int64_t* ring, const int* cursor, int width, int col) {
+  pdl_prologue();
   const int row = *cursor;
   ring[(int64_t)row * width + col] = (int64_t)globaltimer();
 }
 
 __global__ void open_row_kernel(int64_t* ring, int* cursor, int rows, int width, int64_t* step_counter) {
+  pdl_prologue();
   __shared__ int s_row;
   if (threadIdx.x == 0) {
     const int r = (*cursor + 1) % rows;
@@ -34,13 +36,13 @@ __global__ void open_row_kernel(int64_t* ring, int* cursor, int rows, int width,
 
 cudaError_t timing_stamp(int64_t* ring, const int* cursor, int width, int col, cudaStream_t stream) {
   if (col < 1 || col >= width) return cudaErrorInvalidValue;  // column 0 holds the row's step number
-  stamp_kernel<<<1, 1, 0, stream>>>(ring, cursor, width, col);
+  launch_pdl(stamp_kernel, dim3(1), dim3(1), 0, stream, ring, cursor, width, col);
   return cudaGetLastError();
 }
 
 cudaError_t timing_open_row(int64_t* ring, int* cursor, int rows, int width, int64_t* step_counter,
                             cudaStream_t stream) {
-  open_row_kernel<<<1, 128, 0, stream>>>(ring, cursor, rows, width, step_counter);
+  launch_pdl(open_row_kernel, dim3(1), dim3(128), 0, stream, ring, cursor, rows, width, step_counter);
   return cudaGetLastError();
 }
 
