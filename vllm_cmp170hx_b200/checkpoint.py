@@ -111,7 +111,12 @@ def load(model: torch.nn.Module, in_dir: str, strict: bool = True) -> None:
                                      f"{dst.dtype}")
         with torch.no_grad():
             dst.copy_(src.to(dst.device))
-    for _, obj in _containers(model):  # decoded-weight caches of the CPU reference path are now stale
+    drop_decoded_caches(model)
+
+
+def drop_decoded_caches(model: torch.nn.Module) -> None:
+    """Forget the decoded-weight caches of the CPU reference path (stale once weights change)."""
+    for _, obj in _containers(model):
         for attr in ("_dense_cache", "_dense"):
             if attr in vars(obj):
                 object.__delattr__(obj, attr)

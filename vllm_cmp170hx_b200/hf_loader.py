@@ -1,0 +1,333 @@
+"""Load checkpoints by upstream (Hugging Face) tensor names, cut for this rank.
+
+Names follow the upstream model families the engine serves:
+
+* Kimi-delta attention layers (Kimi-Linear / GLM `linear_attention` naming), prefix
+  ``model.layers.{i}.self_attn.``: ``q_proj k_proj v_proj`` ``[H*D, hid]``, ``f_a_proj g_a_proj``
+  ``[D, hid]``, ``f_b_proj g_b_proj`` ``[H*D, D]``, ``b_proj`` ``[H, hid]``,
+  ``{q,k,v}_conv1d.weight`` ``[H*D, 1, 4]``, ``A_log`` ``[H]``, ``dt_bias`` ``[H*D]``,
+  ``o_norm.weight`` ``[D]``, ``o_proj`` ``[hid, H*D]``;
+* sparse-MLA layers (DeepSeek-V3.2 naming): ``q_a_proj q_a_layernorm q_b_proj kv_a_proj_with_mqa
+  kv_a_layernorm kv_b_proj o_proj`` and the indexer ``indexer.{wq_b, wk, k_norm, weights_proj}``;
+  fp8 projections as ``weight`` (e4m3) + ``weight_scale_inv`` (one fp32 scale per 128 x 128 block);
+* MLPs: ``mlp.{gate,up,down}_proj`` (dense), ``mlp.gate.weight`` (+ ``e_score_correction_bias``),
+  ``mlp.experts.{e}.{gate,up,down}_proj.weight`` (bf16) or ``.{trellis,suh,svh}`` (EXL3),
+  ``mlp.shared_experts.{gate,up,down}_proj``;
+* ``model.embed_tokens.weight``, ``model.norm.weight``, ``lm_head.weight``,
+  ``model.layers.{i}.{input,post_attention}_layernorm.weight``.
+
+Tensor-parallel cuts match the model's own (heads of q/k/v/b/conv/A_log/dt_bias, rows of q_b and
+the per-head kv_b, columns of o_proj, intermediate columns of the experts in whole 128-column
+blocks for EXL3, the vocab rows of lm_head); expert parallel keeps this rank's whole experts.  The
+reference loads the same upstream names through vLLM's weight loaders
+(vllm_sm80/models/glm5next/sm80_model.py:112, models/deepseek_v41/sm80_model.py:449).
+Marlin-packed experts load from this package's own checkpoints (checkpoint.py), not from GPTQ files.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+from collections.abc import Mapping
+
+import torch
+
+from .formats import exl3 as fx
+from .formats import fp8 as f8
+from .parallel import state as pstate
+
+
+class MissingTensor(KeyError):
+    pass
+
+
+def open_dir(path: str) -> Mapping[str, torch.Tensor]:
+    """All tensors of the ``*.safetensors`` files of a directory, read lazily by name."""
+    from safetensors import safe_open
+
+    handles = {}
+    index = {}
+    for f in sorted(glob.glob(os.path.join(path, "*.safetensors"))):
+        h = safe_open(f, framework="pt")
+        handles[f] = h
+        for k in h.keys():
+            index[k] = f
+
+    class _Lazy(Mapping):
+        def __getitem__(self, k):
+            if k not in index:
+                raise MissingTensor(k)
+            return handles[index[k]].get_tensor(k)
+
+        def __iter__(self):
+            return iter(index)
+
+        def __len__(self):
+            return len(index)
+
+    return _Lazy()
+
+
+def _get(t: Mapping, name: str) -> torch.Tensor:
+    if name not in t:
+        raise MissingTensor(name)
+    return t[name]
+
+
+def _dense(t: Mapping, name: str) -> torch.Tensor:
+    """A projection's weight as float: bf16 as stored, fp8 dequantised with its block scales."""
+    w = _get(t, name + ".weight")
+    if w.dtype == torch.float8_e4m3fn:
+        return f8.dequantize(w, _get(t, name + ".weight_scale_inv").float())
+    return w.float()
+
+
+def _rows(x: torch.Tensor, tp: int, r: int) -> torch.Tensor:
+    n = x.shape[0] // tp
+    return x[r * n:(r + 1) * n]
+
+
+def _cols(x: torch.Tensor, tp: int, r: int) -> torch.Tensor:
+    n = x.shape[1] // tp
+    return x[:, r * n:(r + 1) * n]
+
+
+def _set(dst: torch.Tensor, src: torch.Tensor) -> None:
+    if tuple(dst.shape) != tuple(src.shape):
+        raise ValueError(f"shape {tuple(src.shape)} does not fit {tuple(dst.shape)}")
+    with torch.no_grad():
+        dst.copy_(src.to(dst.dtype))
+
+
+def _set_linear(lin, w: torch.Tensor) -> None:
+    """A bf16 Linear or an fp8 block-scaled projection (re-quantised from the dense weight)."""
+    if hasattr(lin, "lin"):  # Fp8Proj
+        q, s = f8.quantize(w.float().cpu())
+        _set(lin.lin.weight, q.view(lin.lin.weight.dtype) if q.dtype != lin.lin.weight.dtype else q)
+        _set(lin.lin.scale, s)
+    else:
+        _set(lin.weight, w)
+
+
+def _load_kda(a, t, p, tp, r):
+    H, D = a.H * tp, a.D
+    q, k, v = (_rows(_dense(t, p + n), tp, r) for n in ("q_proj", "k_proj", "v_proj"))
+    fa, ga = _dense(t, p + "f_a_proj"), _dense(t, p + "g_a_proj")
+    b = _rows(_dense(t, p + "b_proj"), tp, r)
+    w = torch.cat([q, k, v, fa, ga, b], 0)
+    pad = a.in_proj.weight.shape[0] - w.shape[0]
+    _set_linear(a.in_proj, torch.cat([w, w.new_zeros(pad, w.shape[1])], 0))
+    _set_linear(a.f_b, _rows(_dense(t, p + "f_b_proj"), tp, r))
+    _set_linear(a.g_b, _rows(_dense(t, p + "g_b_proj"), tp, r))
+    conv = torch.stack([_get(t, p + f"{n}_conv1d.weight").float().reshape(H, D, 4) for n in ("q", "k", "v")])
+    _set(a.conv_w, conv[:, r * a.H:(r + 1) * a.H].reshape(-1, 4))
+    _set(a.a_log, _rows(_get(t, p + "A_log").float().reshape(H), tp, r))
+    _set(a.g_bias, _rows(_get(t, p + "dt_bias").float().reshape(H * D), tp, r))
+    _set(a.norm_w, _get(t, p + "o_norm.weight"))
+    _set_linear(a.o_proj, _cols(_dense(t, p + "o_proj"), tp, r))
+
+
+def _load_mla(a, t, p, tp, r):
+    m = a.m
+    w = torch.cat([_dense(t, p + "q_a_proj"), _dense(t, p + "kv_a_proj_with_mqa"), _dense(t, p + "indexer.wk"),
+                   _dense(t, p + "indexer.weights_proj")], 0)
+    _set_linear(a.in_proj, w)
+    _set(a.q_a_norm.weight, _get(t, p + "q_a_layernorm.weight"))
+    _set(a.kv_a_norm_w, _get(t, p + "kv_a_layernorm.weight"))
+    _set_linear(a.q_b, _rows(_dense(t, p + "q_b_proj"), tp, r))
+    kvb = _rows(_dense(t, p + "kv_b_proj").view(m.num_heads, a.dn + a.dv, a.kvl), tp, r)
+    _set(a.w_uk, kvb[:, :a.dn])
+    _set(a.w_uv_t, kvb[:, a.dn:])
+    _set_linear(a.o_proj, _cols(_dense(t, p + "o_proj"), tp, r))
+    _set_linear(a.idx_q, _dense(t, p + "indexer.wq_b"))
+    _set(a.idx_k_ln_w, _get(t, p + "indexer.k_norm.weight"))
+    if p + "indexer.k_norm.bias" in t:
+        _set(a.idx_k_ln_b, _get(t, p + "indexer.k_norm.bias"))
+
+
+def _load_dense_mlp(mlp, t, p, tp, r):
+    g, u = (_rows(_dense(t, p + n), tp, r) for n in ("gate_proj", "up_proj"))
+    _set_linear(mlp.gate_up, torch.cat([g, u], 0))
+    _set_linear(mlp.down, _cols(_dense(t, p + "down_proj"), tp, r))
+
+
+def _expert_range(moe, E):
+    emap = getattr(moe.experts, "expert_map", None)
+    if emap is None:
+        return list(range(E))
+    emap = emap.cpu()
+    return [int(e) for e in (emap >= 0).nonzero().flatten()]
+
+
+def _load_moe(moe, t, p, tp, r):
+    from .models.hybrid import BF16Experts
+    from .ops.moe import Exl3Experts
+
+    mc = moe.mc
+    _set_linear(moe.gate, _dense(t, p + "gate"))
+    if moe.e_bias is not None:
+        _set(moe.e_bias, _get(t, p + "gate.e_score_correction_bias"))
+    ep = getattr(moe.experts, "expert_map", None) is not None
+    ttp, tr = (1, 0) if ep else (tp, r)
+    experts = _expert_range(moe, mc.num_experts)
+    ex = moe.experts
+    if isinstance(ex, BF16Experts):
+        for j, e in enumerate(experts):
+            q = p + f"experts.{e}."
+            g, u = (_rows(_dense(t, q + n), ttp, tr) for n in ("gate_proj", "up_proj"))
+            _set(ex.gate_up[j], torch.cat([g, u], 0))
+            _set(ex.down[j], _cols(_dense(t, q + "down_proj"), ttp, tr))
+    elif isinstance(ex, Exl3Experts):
+        mats = {w: [] for w in ("gate", "up", "down")}
+        for e in experts:
+            for w in mats:
+                q = p + f"experts.{e}.{w}_proj."
+                tr_, suh, svh = _get(t, q + "trellis"), _get(t, q + "suh"), _get(t, q + "svh")
+                fin, fout = tr_.shape[0] * 16, tr_.shape[1] * 16
+                mats[w].append(_cut_exl3(fx.Exl3Matrix(tr_, suh, svh, ex.bits_x2, ex.codebook, fin, fout), w,
+                                         ttp, tr))
+        new = Exl3Experts.from_matrices(mats["gate"], mats["up"], mats["down"], ex.expert_map, ex.swiglu_limit)
+        for name in ("gate", "up", "down"):
+            for part in ("trellis", "suh", "svh"):
+                _set(getattr(ex, f"{name}_{part}"), getattr(new, f"{name}_{part}"))
+    else:
+        raise NotImplementedError("Marlin-packed experts load from this package's own checkpoints")
+    if moe.shared is not None:
+        _load_dense_mlp(moe.shared, t, p + "shared_experts.", tp, r)
+
+
+def _cut_exl3(m: "fx.Exl3Matrix", which: str, tp: int, r: int) -> "fx.Exl3Matrix":
+    """This rank's whole-H128 share of an expert matrix: intermediate columns of gate/up, rows of down."""
+    if tp == 1:
+        return m
+    if which == "down":
+        n = m.in_features // tp
+        return fx.Exl3Matrix(m.trellis[r * n // 16:(r + 1) * n // 16].contiguous(), m.suh[r * n:(r + 1) * n].contiguous(),
+                             m.svh, m.bits_x2, m.codebook, n, m.out_features)
+    n = m.out_features // tp
+    return fx.Exl3Matrix(m.trellis[:, r * n // 16:(r + 1) * n // 16].contiguous(), m.suh,
+                         m.svh[r * n:(r + 1) * n].contiguous(), m.bits_x2, m.codebook, m.in_features, n)
+
+
+def load_hf(model, tensors: Mapping[str, torch.Tensor] | str) -> None:
+    """Fill a built HybridForCausalLM (this rank's stage and shards) from upstream-named tensors (a
+    mapping, or a directory of safetensors files)."""
+    t = open_dir(tensors) if isinstance(tensors, str) else tensors
+    st = pstate.get()
+    tp, r = st.tp_size, st.tp_rank
+    if model.embed is not None:
+        _set(model.embed, _get(t, "model.embed_tokens.weight"))
+    if model.norm is not None:
+        _set(model.norm.weight, _get(t, "model.norm.weight"))
+    if model.lm_head is not None:
+        _set_linear(model.lm_head, _rows(_dense(t, "lm_head"), tp, r))
+    for layer in model.layers:
+        p = f"model.layers.{layer.idx}."
+        _set(layer.input_norm.weight, _get(t, p + "input_layernorm.weight"))
+        _set(layer.post_norm.weight, _get(t, p + "post_attention_layernorm.weight"))
+        (_load_kda if layer.kind == "kda" else _load_mla)(layer.attn, t, p + "self_attn.", tp, r)
+        if layer.mlp is None:
+            continue
+        if hasattr(layer.mlp, "gate_up"):
+            _load_dense_mlp(layer.mlp, t, p + "mlp.", tp, r)
+        else:
+            _load_moe(layer.mlp, t, p + "mlp.", tp, r)
+    from .checkpoint import drop_decoded_caches
+
+    drop_decoded_caches(model)
+
+
+def export_hf(model) -> dict[str, torch.Tensor]:
+    """The upstream-named tensors of a single-rank model (the inverse of `load_hf` at TP = 1)."""
+    from .models.hybrid import BF16Experts
+    from .ops.moe import Exl3Experts
+
+    st = pstate.get()
+    if st.tp_size != 1 or st.pp_size != 1:
+        raise ValueError("export_hf writes a whole model: run it at TP = PP = 1")
+    out: dict[str, torch.Tensor] = {}
+
+    def dense(lin):
+        if hasattr(lin, "lin"):
+            return f8.dequantize(lin.lin.weight, lin.lin.scale.float()).to(torch.bfloat16)
+        return lin.weight.detach()
+
+    def put(name: str, lin) -> None:
+        """A projection under `name`: fp8 stays fp8 (+ its block scales), bf16 as is."""
+        if hasattr(lin, "lin"):
+            out[name + ".weight"] = lin.lin.weight.detach()
+            out[name + ".weight_scale_inv"] = lin.lin.scale.detach()
+        else:
+            out[name + ".weight"] = lin.weight.detach()
+
+    out["model.embed_tokens.weight"] = model.embed.detach()
+    out["model.norm.weight"] = model.norm.weight.detach()
+    out["lm_head.weight"] = dense(model.lm_head)
+    for layer in model.layers:
+        p = f"model.layers.{layer.idx}."
+        out[p + "input_layernorm.weight"] = layer.input_norm.weight.detach()
+        out[p + "post_attention_layernorm.weight"] = layer.post_norm.weight.detach()
+        a = layer.attn
+        q = p + "self_attn."
+        if layer.kind == "kda":
+            H, D = a.H, a.D
+            w = dense(a.in_proj)
+            s = [H * D, H * D, H * D, D, D, H]
+            parts = torch.split(w[:sum(s)], s, 0)
+            for n, x in zip(("q_proj", "k_proj", "v_proj", "f_a_proj", "g_a_proj", "b_proj"), parts):
+                out[q + n + ".weight"] = x.contiguous()
+            out[q + "f_b_proj.weight"] = dense(a.f_b)
+            out[q + "g_b_proj.weight"] = dense(a.g_b)
+            conv = a.conv_w.detach().view(3, H * D, 1, 4)
+            for i, n in enumerate("qkv"):
+                out[q + f"{n}_conv1d.weight"] = conv[i].contiguous()
+            out[q + "A_log"] = a.a_log.detach()
+            out[q + "dt_bias"] = a.g_bias.detach()
+            out[q + "o_norm.weight"] = a.norm_w.detach()
+            out[q + "o_proj.weight"] = dense(a.o_proj)
+        else:
+            m = a.m
+            w = dense(a.in_proj)
+            s = [a.ql, a.kvl + a.dr, m.index_head_dim, m.index_n_heads]
+            for n, x in zip(("q_a_proj", "kv_a_proj_with_mqa", "indexer.wk", "indexer.weights_proj"), torch.split(w, s, 0)):
+                out[q + n + ".weight"] = x.contiguous()
+            out[q + "q_a_layernorm.weight"] = a.q_a_norm.weight.detach()
+            out[q + "kv_a_layernorm.weight"] = a.kv_a_norm_w.detach()
+            put(q + "q_b_proj", a.q_b)
+            out[q + "kv_b_proj.weight"] = torch.cat([a.w_uk.detach(), a.w_uv_t.detach()], 1).reshape(-1, a.kvl)
+            put(q + "o_proj", a.o_proj)
+            put(q + "indexer.wq_b", a.idx_q)
+            out[q + "indexer.k_norm.weight"] = a.idx_k_ln_w.detach()
+            out[q + "indexer.k_norm.bias"] = a.idx_k_ln_b.detach()
+        mlp = layer.mlp
+        if mlp is None:
+            continue
+        q = p + "mlp."
+        if hasattr(mlp, "gate_up"):
+            g, u = dense(mlp.gate_up).chunk(2, 0)
+            out[q + "gate_proj.weight"], out[q + "up_proj.weight"] = g.contiguous(), u.contiguous()
+            out[q + "down_proj.weight"] = dense(mlp.down)
+            continue
+        out[q + "gate.weight"] = dense(mlp.gate)
+        if mlp.e_bias is not None:
+            out[q + "gate.e_score_correction_bias"] = mlp.e_bias.detach()
+        ex = mlp.experts
+        if isinstance(ex, BF16Experts):
+            for e in range(ex.gate_up.shape[0]):
+                g, u = ex.gate_up[e].detach().chunk(2, 0)
+                out[q + f"experts.{e}.gate_proj.weight"] = g.contiguous()
+                out[q + f"experts.{e}.up_proj.weight"] = u.contiguous()
+                out[q + f"experts.{e}.down_proj.weight"] = ex.down[e].detach()
+        elif isinstance(ex, Exl3Experts):
+            for e in range(ex.num_local):
+                for w in ("gate", "up", "down"):
+                    for part in ("trellis", "suh", "svh"):
+                        out[q + f"experts.{e}.{w}_proj.{part}"] = getattr(ex, f"{w}_{part}")[e].detach()
+        else:
+            raise NotImplementedError("Marlin-packed experts are exported by checkpoint.py")
+        if mlp.shared is not None:
+            g, u = dense(mlp.shared.gate_up).chunk(2, 0)
+            out[q + "shared_experts.gate_proj.weight"] = g.contiguous()
+            out[q + "shared_experts.up_proj.weight"] = u.contiguous()
+            out[q + "shared_experts.down_proj.weight"] = dense(mlp.shared.down)
+    return out
