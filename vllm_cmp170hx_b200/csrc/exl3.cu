@@ -60,8 +60,18 @@ struct GemmParams {
   int64_t ld_out;
   int out_mode;        // 0: fp16 (gate/up intermediate), 1: fp32, 2: bf16
   float swiglu_limit;  // <= 0: none
+  // Codebook 2 keeps the per-weight fp16 affine step out of the decode: the A operand holds
+  // half(0x6400 + bytesum) = 1024 + bytesum exactly, and the epilogue forms
+  // a * acc + b * sum_k x_k (a, b the codebook's constants) from the activation row sums:
+  const float* sx[2];  // per matrix: [rows][sx_parts] partial sums of the activation rows (summed in order)
+  int sx_parts;
+  float* hsum;         // gate/up pass: [rows][N / 128] partial sums of the intermediate it writes
   uint32_t* status;
 };
+
+// Codebook 2's affine constants (fp16 0x1eee and 0xc931 as floats).
+__device__ __forceinline__ float cb2_a() { return __half2float(__ushort_as_half((unsigned short)0x1eee)); }
+__device__ __forceinline__ float cb2_b() { return __half2float(__ushort_as_half((unsigned short)0xc931)); }
 
 // ----------------------------------------------------------------------------- codebooks
 // Two states -> two fp16 weights packed as half2 (inline PTX keeps the
@@ -70,16 +80,16 @@ template <int CB>
 __device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
   uint32_t r;
   if constexpr (CB == 2) {
-    // t = 0x6400 + bytesum(s * 0x83DCD12D); w = fma16(half(t), 0x1eee, 0xc931)
-    asm("{\n\t.reg .b32 p0, p1, t0, t1, h;\n\t"
+    // t = 0x6400 + bytesum(s * 0x83DCD12D) as fp16 (= 1024 + bytesum, exact); the codebook's
+    // w = 0x1eee * t + 0xc931 is applied to the accumulator in the epilogue (kCbA, kCbB)
+    asm("{\n\t.reg .b32 p0, p1, t0, t1;\n\t"
         "mul.lo.u32 p0, %1, 0x83DCD12D;\n\t"
         "mul.lo.u32 p1, %2, 0x83DCD12D;\n\t"
         "dp4a.u32.u32 t0, p0, 0x01010101, 0x6400;\n\t"
         "dp4a.u32.u32 t1, p1, 0x01010101, 0x6400;\n\t"
-        "prmt.b32 h, t0, t1, 0x5410;\n\t"
-        "fma.rn.f16x2 %0, h, %3, %4;\n\t}"
+        "prmt.b32 %0, t0, t1, 0x5410;\n\t}"
         : "=r"(r)
-        : "r"(s0), "r"(s1), "r"(0x1eee1eeeu), "r"(0xc931c931u));
+        : "r"(s0), "r"(s1));
   } else {
     // p = (s * 0xCBAC1FED) & 0x8fff8fff ^ 0x3b603b60; w = half(p.lo) + half(p.hi)
     asm("{\n\t.reg .b32 p0, p1, lo, hi;\n\t"
@@ -217,6 +227,32 @@ __device__ __forceinline__ void h128_group(float (&v)[NV], int lane, int q, floa
   for (int i = 0; i < NV; ++i) v[i] *= kH128;
 }
 
+// Sum over the 128 threads of a 4-warp group of each of NV values (fixed order: deterministic).
+template <int NV>
+__device__ __forceinline__ void group_sum(float (&v)[NV], int lane, int q, float* xbuf, int bar_id) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) xbuf[q * NV + i] = v[i];
+  }
+  asm volatile("bar.sync %0, 128;" ::"r"(bar_id));
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = (xbuf[i] + xbuf[NV + i]) + (xbuf[2 * NV + i] + xbuf[3 * NV + i]);
+  asm volatile("bar.sync %0, 128;" ::"r"(bar_id));
+}
+
+// The activation row sum of row `row` for matrix m (0 outside the item's rows).
+__device__ __forceinline__ float row_sum(const GemmParams& p, int m, int row, bool valid) {
+  if (!valid || p.sx[m] == nullptr) return 0.f;
+  float s = 0.f;
+  for (int i = 0; i < p.sx_parts; ++i) s += p.sx[m][(int64_t)row * p.sx_parts + i];
+  return s;
+}
+
 template <int NV>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[NV]) {
   if constexpr (NV == 16) {
@@ -234,8 +270,11 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[NV]) 
 // projection's input rotation (suh, H128), written in the form the down pass reads.
 template <int NMAT, int NV>
 __device__ __forceinline__ void epilogue_block(const GemmParams& p, uint32_t tlane, int tile_rows, int c0, int rows,
-                                               int row0, int feat, float sg, float su, float sn, int lane, int q,
-                                               float* xb, int bar_id) {
+                                               int row0, int feat, int tile, float sg, float su, float sn, int lane,
+                                               int q, float* xb, int bar_id, const float* pre0 = nullptr,
+                                               const float* pre1 = nullptr) {
+  const bool fold = p.codebook == 2;
+  const float ca = cb2_a(), cbb = cb2_b();
   if constexpr (NMAT == 2) {
     uint32_t rg[NV], ru[NV];
     tmem_ld_cols<NV>(tlane + c0, rg);
@@ -246,6 +285,11 @@ __device__ __forceinline__ void epilogue_block(const GemmParams& p, uint32_t tla
     for (int i = 0; i < NV; ++i) {
       gv[i] = __uint_as_float(rg[i]);
       uv[i] = __uint_as_float(ru[i]);
+      if (fold) {
+        const bool ok = c0 + i < rows;
+        gv[i] = ca * gv[i] + cbb * (pre0 ? pre0[i] : row_sum(p, 0, row0 + c0 + i, ok));
+        uv[i] = ca * uv[i] + cbb * (pre1 ? pre1[i] : row_sum(p, 1, row0 + c0 + i, ok));
+      }
     }
     h128_group<NV>(gv, lane, q, xb, bar_id);
     h128_group<NV>(uv, lane, q, xb, bar_id);
@@ -261,10 +305,22 @@ __device__ __forceinline__ void epilogue_block(const GemmParams& p, uint32_t tla
     }
     h128_group<NV>(gv, lane, q, xb, bar_id);
     __half* out = reinterpret_cast<__half*>(p.out);
+    float hs[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int r = c0 + i;
-      if (r < rows) out[(int64_t)(row0 + r) * p.ld_out + feat] = __float2half_rn(gv[i]);
+      const __half hv = __float2half_rn(gv[i]);
+      hs[i] = r < rows ? __half2float(hv) : 0.f;
+      if (r < rows) out[(int64_t)(row0 + r) * p.ld_out + feat] = hv;
+    }
+    if (p.hsum != nullptr) {  // the down pass's activation row sums, one partial per feature tile
+      group_sum<NV>(hs, lane, q, xb, bar_id);
+      if (q == 0 && lane == 0) {
+        const int parts = p.N / 128;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+          if (c0 + i < rows) p.hsum[(int64_t)(row0 + c0 + i) * parts + tile] = hs[i];
+      }
     }
   } else {
     uint32_t ra[NV];
@@ -272,7 +328,10 @@ __device__ __forceinline__ void epilogue_block(const GemmParams& p, uint32_t tla
     tmem_wait_ld();
     float v[NV];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) v[i] = __uint_as_float(ra[i]);
+    for (int i = 0; i < NV; ++i) {
+      v[i] = __uint_as_float(ra[i]);
+      if (fold) v[i] = ca * v[i] + cbb * (pre0 ? pre0[i] : row_sum(p, 0, row0 + c0 + i, c0 + i < rows));
+    }
     h128_group<NV>(v, lane, q, xb, bar_id);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
@@ -513,22 +572,32 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
       const int tile = u % n_tiles;
       const int e = it.x;
       const int acc = local & 1;
-      const bool got = mbar_wait_or_abort(&tfull[acc], (local >> 1) & 1, p.status, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) break;  // TMEM loads are warp-collective
-      tc_fence_after();
       const int rows = it.z;
       const int row0 = it.y;
       const int feat = tile * 128 + f;
-      const int nchunks = (rows + 15) / 16;
-      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * acc_cols);
+      // the unit's scales and (short items) activation row sums: loaded while its MMAs still run
       const float sg = __half2float(p.svh[0][(int64_t)e * p.svh_estride[0] + feat]);
       const float su = NMAT == 2 ? __half2float(p.svh[1][(int64_t)e * p.svh_estride[1] + feat]) : 0.f;
       const float sn = NMAT == 2 ? __half2float(p.suh_next[(int64_t)e * p.suh_next_estride + feat]) : 0.f;
+      float pre0[4] = {0.f, 0.f, 0.f, 0.f}, pre1[4] = {0.f, 0.f, 0.f, 0.f};
+      if (rows <= 4 && p.codebook == 2) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          pre0[i] = row_sum(p, 0, row0 + i, i < rows);
+          if (NMAT == 2) pre1[i] = row_sum(p, 1, row0 + i, i < rows);
+        }
+      }
+      const bool got = mbar_wait_or_abort(&tfull[acc], (local >> 1) & 1, p.status, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) break;  // TMEM loads are warp-collective
+      tc_fence_after();
+      const int nchunks = (rows + 15) / 16;
+      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * acc_cols);
       if (rows > 4) {
         for (int c = 0; c < nchunks; ++c)
-          epilogue_block<NMAT, 16>(p, tlane, tile_rows, c * 16, rows, row0, feat, sg, su, sn, lane, q, xbuf, 1);
+          epilogue_block<NMAT, 16>(p, tlane, tile_rows, c * 16, rows, row0, feat, tile, sg, su, sn, lane, q, xbuf, 1);
       } else {
-        epilogue_block<NMAT, 4>(p, tlane, tile_rows, 0, rows, row0, feat, sg, su, sn, lane, q, xbuf, 1);
+        epilogue_block<NMAT, 4>(p, tlane, tile_rows, 0, rows, row0, feat, tile, sg, su, sn, lane, q, xbuf, 1, pre0,
+                                pre1);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -669,22 +738,25 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
 }
 
 // ----------------------------------------------------------------------------- input rotation
-// out[r, :] = fp16( H128( x[src_row(r), :] * suh ) ) for each of NMAT suh
-// vectors (per expert).  One warp per (row, 128-block): 4 values per lane,
-// 2 in-register butterfly stages + 5 shuffle stages.
+// out[r, :] = fp16( H128( x[src_row(r), :] * suh ) ) for each of NMAT suh vectors (per expert), and
+// sum[r] = the sum of the row's fp16 outputs (what the MMA reads): the codebook's affine step is
+// applied to the accumulator in the epilogue as a * acc + b * sum.  One CTA per row, one warp per
+// 128-block (4 values per lane, 2 in-register butterfly stages + 5 shuffle stages); the row sum is
+// reduced over the warps in block order (deterministic).
+constexpr int kRotMaxWarps = 32;
 __global__ void input_rotate_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, int in_features, int K,
                                     const int* __restrict__ sorted_token, const int* __restrict__ expert_offsets,
                                     int E_local, const __half* __restrict__ suh0, const __half* __restrict__ suh1,
                                     int64_t suh_estride, __half* __restrict__ out0, __half* __restrict__ out1,
-                                    int rows) {
+                                    float* __restrict__ sum0, float* __restrict__ sum1, int rows) {
   pdl_prologue();
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-  const int lane = threadIdx.x % 32;
+  __shared__ float part[2][kRotMaxWarps];
+  const int r = blockIdx.x;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nwarps = blockDim.x / 32;
   const int nblk = K / 128;
-  if (gw >= rows * nblk) return;
-  const int r = gw / nblk, blk = gw % nblk;
   // rows past the assigned ones (expert parallel: assignments to other ranks' experts) are unused
-  if (expert_offsets && r >= expert_offsets[E_local]) return;
+  if (r >= rows || (expert_offsets && r >= expert_offsets[E_local])) return;
   int e = 0;
   if (expert_offsets) {  // expert of row r: binary search in offsets
     int lo = 0, hi = E_local;
@@ -695,41 +767,63 @@ __global__ void input_rotate_kernel(const __nv_bfloat16* __restrict__ x, int64_t
     e = lo;
   }
   const int tok = sorted_token ? sorted_token[r] : r;
-  const int c0 = blk * 128 + lane * 4;
-  float xv[4];
+  float acc[2] = {0.f, 0.f};
+  for (int blk = warp; blk < nblk; blk += nwarps) {
+    const int c0 = blk * 128 + lane * 4;
+    float xv[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = c0 + i;
-    xv[i] = c < in_features ? __bfloat162float(x[(int64_t)tok * ld_x + c]) : 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const int c = c0 + i;
+      xv[i] = c < in_features ? __bfloat162float(x[(int64_t)tok * ld_x + c]) : 0.f;
+    }
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const __half* suh = m == 0 ? suh0 : suh1;
+      __half* out = m == 0 ? out0 : out1;
+      if (suh == nullptr) break;
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = xv[i] * __half2float(suh[(int64_t)e * suh_estride + c0 + i]);
+      // in-register: features 4*lane + {0,1,2,3}: distances 1, 2
+      float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+      v[0] = a0 + a2;
+      v[1] = a1 + a3;
+      v[2] = a0 - a2;
+      v[3] = a1 - a3;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+          v[i] = (lane & d) ? (o - v[i]) : (v[i] + o);
+        }
+      }
+      __half2 h01 = __floats2half2_rn(v[0] * kH128, v[1] * kH128);
+      __half2 h23 = __floats2half2_rn(v[2] * kH128, v[3] * kH128);
+      const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+      acc[m] += (f01.x + f01.y) + (f23.x + f23.y);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&h01);
+      pk.y = *reinterpret_cast<uint32_t*>(&h23);
+      *reinterpret_cast<uint2*>(out + (int64_t)r * K + c0) = pk;
+    }
   }
+  if (sum0 == nullptr && sum1 == nullptr) return;
 #pragma unroll
   for (int m = 0; m < 2; ++m) {
-    const __half* suh = m == 0 ? suh0 : suh1;
-    __half* out = m == 0 ? out0 : out1;
-    if (suh == nullptr) break;
-    float v[4];
+    float v = acc[m];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = xv[i] * __half2float(suh[(int64_t)e * suh_estride + c0 + i]);
-    // in-register: features 4*lane + {0,1,2,3}: distances 1, 2
-    float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
-    v[0] = a0 + a2;
-    v[1] = a1 + a3;
-    v[2] = a0 - a2;
-    v[3] = a1 - a3;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
-        v[i] = (lane & d) ? (o - v[i]) : (v[i] + o);
-      }
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) part[m][warp] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 2) {
+    float* sum = threadIdx.x == 0 ? sum0 : sum1;
+    if (sum != nullptr) {
+      float v = 0.f;
+      for (int w = 0; w < nwarps; ++w) v += part[threadIdx.x][w];
+      sum[r] = v;
     }
-    __half2 h01 = __floats2half2_rn(v[0] * kH128, v[1] * kH128);
-    __half2 h23 = __floats2half2_rn(v[2] * kH128, v[3] * kH128);
-    uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&h01);
-    pk.y = *reinterpret_cast<uint32_t*>(&h23);
-    *reinterpret_cast<uint2*>(out + (int64_t)r * K + c0) = pk;
   }
 }
 
@@ -824,15 +918,15 @@ cudaError_t dispatch(const GemmParams& p, const void* b0, const void* b1, int64_
 
 cudaError_t exl3_input_rotate(const void* x, int64_t ld_x, int in_features, int K, const int* sorted_token,
                               const int* expert_offsets, int E_local, const void* suh0, const void* suh1,
-                              int64_t suh_estride, void* out0, void* out1, int rows, cudaStream_t stream) {
+                              int64_t suh_estride, void* out0, void* out1, float* sum0, float* sum1, int rows,
+                              cudaStream_t stream) {
   if (K % 128) return cudaErrorInvalidValue;
   if (rows == 0) return cudaSuccess;
-  const int warps = rows * (K / 128);
-  const int threads = 256;
-  launch_pdl(exl3::input_rotate_kernel, dim3((warps * 32 + threads - 1) / threads), dim3(threads), 0, stream, 
-      reinterpret_cast<const __nv_bfloat16*>(x), ld_x, in_features, K, sorted_token, expert_offsets, E_local,
-      reinterpret_cast<const __half*>(suh0), reinterpret_cast<const __half*>(suh1), suh_estride,
-      reinterpret_cast<__half*>(out0), reinterpret_cast<__half*>(out1), rows);
+  const int threads = 32 * std::min(K / 128, exl3::kRotMaxWarps);
+  launch_pdl(exl3::input_rotate_kernel, dim3(rows), dim3(threads), 0, stream,
+             reinterpret_cast<const __nv_bfloat16*>(x), ld_x, in_features, K, sorted_token, expert_offsets, E_local,
+             reinterpret_cast<const __half*>(suh0), reinterpret_cast<const __half*>(suh1), suh_estride,
+             reinterpret_cast<__half*>(out0), reinterpret_cast<__half*>(out1), sum0, sum1, rows);
   return cudaGetLastError();
 }
 
@@ -861,7 +955,14 @@ cudaError_t exl3_gemm(const Exl3GemmArgs& a, cudaStream_t stream) {
   p.ld_out = a.ld_out;
   p.out_mode = a.out_mode;
   p.swiglu_limit = a.swiglu_limit;
+  p.sx[0] = a.sx0;
+  p.sx[1] = a.sx1;
+  p.sx_parts = a.sx_parts;
+  p.hsum = a.hsum;
   p.status = a.status;
+  // codebook 2 folds its affine step into the epilogue: it needs the activation row sums
+  if (a.codebook == 2 && (a.sx0 == nullptr || (a.nmat == 2 && a.sx1 == nullptr) || a.sx_parts < 1))
+    return cudaErrorInvalidValue;
   const int grid = std::max(1, std::min(a.max_work, device_sm_count()));
   if (a.nmat == 2) return dispatch<2>(p, a.b0, a.b1, a.b_rows, a.num_experts, stream, grid);
   return dispatch<1>(p, a.b0, nullptr, a.b_rows, a.num_experts, stream, grid);

@@ -127,12 +127,20 @@ struct Exl3GemmArgs {
   int64_t ld_out;
   int out_mode;             // 0 fp16, 1 fp32, 2 bf16
   float swiglu_limit;
+  // codebook 2: per-row sums of the activation rows b0 / b1, [b_rows][sx_parts] partials each
+  // (the input rotation writes them with sx_parts = 1; the gate/up pass writes the down pass's)
+  const float* sx0;
+  const float* sx1;
+  int sx_parts;
+  float* hsum;              // gate/up pass: [b_rows][N / 128] partial row sums of the intermediate
   uint32_t* status;
 };
 cudaError_t exl3_gemm(const Exl3GemmArgs& a, cudaStream_t stream);
+// Also writes sum0 / sum1 [rows]: each output row's sum of its fp16 values (nullable).
 cudaError_t exl3_input_rotate(const void* x, int64_t ld_x, int in_features, int K, const int* sorted_token,
                               const int* expert_offsets, int E_local, const void* suh0, const void* suh1,
-                              int64_t suh_estride, void* out0, void* out1, int rows, cudaStream_t stream);
+                              int64_t suh_estride, void* out0, void* out1, float* sum0, float* sum1, int rows,
+                              cudaStream_t stream);
 cudaError_t moe_combine(const float* y, int64_t ld_y, const int* slot_of, const float* sorted_weight, int T, int k,
                         int H, const void* add, void* out, int64_t ld_out, float* out_f32, cudaStream_t stream);
 

@@ -20,13 +20,16 @@ void moe_build_assignments_op(const at::Tensor& ids, const at::Tensor& weights,
 void exl3_input_rotate_op(const at::Tensor& x, int64_t in_features, const c10::optional<at::Tensor>& sorted_token,
                           const c10::optional<at::Tensor>& expert_offsets, int64_t E_local, const at::Tensor& suh0,
                           const c10::optional<at::Tensor>& suh1, at::Tensor& out0,
-                          const c10::optional<at::Tensor>& out1, int64_t rows);  // exl3.cu
+                          const c10::optional<at::Tensor>& out1, int64_t rows,
+                          const c10::optional<at::Tensor>& sum0, const c10::optional<at::Tensor>& sum1);  // exl3.cu
 void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<at::Tensor>& trellis1,
                   const at::Tensor& svh0, const c10::optional<at::Tensor>& svh1,
                   const c10::optional<at::Tensor>& suh_next, int64_t bits_x2, int64_t codebook, const at::Tensor& b0,
                   const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
                   const at::Tensor& num_items, int64_t max_work, at::Tensor& out, int64_t out_mode,
-                  double swiglu_limit, const at::Tensor& status);  // exl3.cu
+                  double swiglu_limit, const at::Tensor& status, const c10::optional<at::Tensor>& sx0,
+                  const c10::optional<at::Tensor>& sx1, int64_t sx_parts,
+                  const c10::optional<at::Tensor>& hsum);  // exl3.cu
 void moe_combine_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
                     const c10::optional<at::Tensor>& add, at::Tensor& out);  // exl3.cu
 
@@ -121,10 +124,12 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor(a!) sorted_token, Tensor(b!) sorted_weight, Tensor(c!) slot_of, Tensor(d!) items, "            \
     "Tensor(e!) num_items, Tensor(f!) expert_offsets) -> ()")                                           \
   X("exl3_input_rotate(Tensor x, int in_features, Tensor? sorted_token, Tensor? expert_offsets, "          \
-    "int E_local, Tensor suh0, Tensor? suh1, Tensor(a!) out0, Tensor(b!)? out1, int rows) -> ()")          \
+    "int E_local, Tensor suh0, Tensor? suh1, Tensor(a!) out0, Tensor(b!)? out1, int rows, "                \
+    "Tensor(c!)? sum0=None, Tensor(d!)? sum1=None) -> ()")                                                 \
   X("exl3_gemm(int nmat, Tensor trellis0, Tensor? trellis1, Tensor svh0, Tensor? svh1, Tensor? suh_next, " \
     "int bits_x2, int codebook, Tensor b0, Tensor? b1, int tile_rows, Tensor items, Tensor num_items, "     \
-    "int max_work, Tensor(a!) out, int out_mode, float swiglu_limit, Tensor(b!) status) -> ()")           \
+    "int max_work, Tensor(a!) out, int out_mode, float swiglu_limit, Tensor(b!) status, "                 \
+    "Tensor? sx0=None, Tensor? sx1=None, int sx_parts=1, Tensor(c!)? hsum=None) -> ()")                    \
   X("moe_combine(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out) -> ()") \
   X("kda_forward(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor qkv, Tensor g_raw, "        \
     "Tensor beta_raw, Tensor? g2, Tensor(a!) conv_state, Tensor? conv_w, Tensor? conv_b, Tensor a_log, "   \

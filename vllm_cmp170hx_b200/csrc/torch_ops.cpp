@@ -152,8 +152,12 @@ void moe_build_assignments_op(const at::Tensor& ids, const at::Tensor& weights,
 void exl3_input_rotate_op(const at::Tensor& x, int64_t in_features, const c10::optional<at::Tensor>& sorted_token,
                           const c10::optional<at::Tensor>& expert_offsets, int64_t E_local, const at::Tensor& suh0,
                           const c10::optional<at::Tensor>& suh1, at::Tensor& out0,
-                          const c10::optional<at::Tensor>& out1, int64_t rows) {
+                          const c10::optional<at::Tensor>& out1, int64_t rows,
+                          const c10::optional<at::Tensor>& sum0, const c10::optional<at::Tensor>& sum1) {
   B200_CHECK_CUDA(x);
+  TORCH_CHECK((!sum0.has_value() || (sum0->scalar_type() == at::kFloat && sum0->numel() >= rows)) &&
+                  (!sum1.has_value() || (sum1->scalar_type() == at::kFloat && sum1->numel() >= rows)),
+              "rotate: row sums fp32 [rows]");
   B200_CHECK_DTYPE(x, at::kBFloat16);
   B200_CHECK_DTYPE(suh0, at::kHalf);
   B200_CHECK_DTYPE(out0, at::kHalf);
@@ -166,7 +170,9 @@ void exl3_input_rotate_op(const at::Tensor& x, int64_t in_features, const c10::o
                                 sorted_token.has_value() ? sorted_token->data_ptr<int>() : nullptr,
                                 expert_offsets.has_value() ? expert_offsets->data_ptr<int>() : nullptr, (int)E_local,
                                 suh0.data_ptr(), opt_ptr(suh1), suh0.dim() == 2 ? suh0.stride(0) : 0, out0.data_ptr(),
-                                out1.has_value() ? out1->data_ptr() : nullptr, (int)rows, cur_stream()));
+                                out1.has_value() ? out1->data_ptr() : nullptr,
+                                sum0.has_value() ? sum0->data_ptr<float>() : nullptr,
+                                sum1.has_value() ? sum1->data_ptr<float>() : nullptr, (int)rows, cur_stream()));
 }
 
 void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<at::Tensor>& trellis1,
@@ -174,8 +180,13 @@ void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<
                   const c10::optional<at::Tensor>& suh_next, int64_t bits_x2, int64_t codebook, const at::Tensor& b0,
                   const c10::optional<at::Tensor>& b1, int64_t tile_rows, const at::Tensor& items,
                   const at::Tensor& num_items, int64_t max_work, at::Tensor& out, int64_t out_mode,
-                  double swiglu_limit, const at::Tensor& status) {
+                  double swiglu_limit, const at::Tensor& status, const c10::optional<at::Tensor>& sx0,
+                  const c10::optional<at::Tensor>& sx1, int64_t sx_parts, const c10::optional<at::Tensor>& hsum) {
   B200_CHECK_CUDA(trellis0);
+  TORCH_CHECK((!sx0.has_value() || sx0->scalar_type() == at::kFloat) &&
+                  (!sx1.has_value() || sx1->scalar_type() == at::kFloat) &&
+                  (!hsum.has_value() || hsum->scalar_type() == at::kFloat),
+              "exl3_gemm: row sums fp32");
   TORCH_CHECK(trellis0.scalar_type() == at::kShort && trellis0.dim() == 4 && trellis0.is_contiguous(),
               "exl3_gemm: trellis [E, K/16, N/16, 8*bits_x2] int16");
   TORCH_CHECK(trellis0.size(3) == 8 * bits_x2, "exl3_gemm: trellis stride vs bits_x2");
@@ -221,6 +232,10 @@ void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<
   a.ld_out = out.stride(0);
   a.out_mode = (int)out_mode;
   a.swiglu_limit = (float)swiglu_limit;
+  a.sx0 = sx0.has_value() ? sx0->data_ptr<float>() : nullptr;
+  a.sx1 = sx1.has_value() ? sx1->data_ptr<float>() : nullptr;
+  a.sx_parts = (int)sx_parts;
+  a.hsum = hsum.has_value() ? hsum->data_ptr<float>() : nullptr;
   a.status = status_ptr(status);
   B200_LAUNCH(exl3_gemm(a, cur_stream()));
 }

@@ -138,14 +138,19 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
                               sorted_weight, slot_of, items, num_items, offsets)
     xg = torch.empty(TK, Kh, dtype=torch.float16, device=dev)
     xu = torch.empty(TK, Kh, dtype=torch.float16, device=dev)
-    ops.exl3_input_rotate(x, H, sorted_token, offsets, E, ex.gate_suh, ex.up_suh, xg, xu, TK)
+    # activation row sums (codebook 2 applies its affine step to the accumulator: a acc + b sum x)
+    sg = torch.empty(TK, dtype=torch.float32, device=dev)
+    su = torch.empty(TK, dtype=torch.float32, device=dev)
+    ops.exl3_input_rotate(x, H, sorted_token, offsets, E, ex.gate_suh, ex.up_suh, xg, xu, TK, sg, su)
     h = torch.empty(TK, I, dtype=torch.float16, device=dev)
+    hsum = torch.empty(TK, I // 128, dtype=torch.float32, device=dev)
     st = _ext.status_word(dev)
     ops.exl3_gemm(2, ex.gate_trellis, ex.up_trellis, ex.gate_svh, ex.up_svh, ex.down_suh, ex.bits_x2, ex.codebook,
-                  xg, xu, tile, items, num_items, max_items * (I // 128), h, 0, float(ex.swiglu_limit or 0.0), st)
+                  xg, xu, tile, items, num_items, max_items * (I // 128), h, 0, float(ex.swiglu_limit or 0.0), st,
+                  sg, su, 1, hsum)
     y = torch.empty(TK, Hp, dtype=torch.float32, device=dev)
     ops.exl3_gemm(1, ex.down_trellis, None, ex.down_svh, None, None, ex.bits_x2, ex.codebook, h, None, tile, items,
-                  num_items, max_items * (Hp // 128), y, 1, 0.0, st)
+                  num_items, max_items * (Hp // 128), y, 1, 0.0, st, hsum, None, I // 128, None)
     if reduce:
         from ..parallel import comm
 
@@ -188,8 +193,10 @@ def exl3_linear(x: torch.Tensor, m: fx.Exl3Matrix, out_dtype=torch.bfloat16) -> 
     n_items = (T + tile - 1) // tile
     items, num = dense_items(T, tile, dev)
     xr = torch.empty(max(T, 1), K, dtype=torch.float16, device=dev)
-    ops.exl3_input_rotate(x, m.in_features, None, None, 1, m.suh, None, xr, None, T)
+    sx = torch.empty(max(T, 1), dtype=torch.float32, device=dev)
+    ops.exl3_input_rotate(x, m.in_features, None, None, 1, m.suh, None, xr, None, T, sx, None)
     y = torch.empty(T, N, dtype=torch.float32 if out_dtype == torch.float32 else torch.bfloat16, device=dev)
     ops.exl3_gemm(1, m.trellis.unsqueeze(0), None, m.svh, None, None, m.bits_x2, m.codebook, xr, None, tile, items,
-                  num, n_items * (N // 128), y, 1 if out_dtype == torch.float32 else 2, 0.0, _ext.status_word(dev))
+                  num, n_items * (N // 128), y, 1 if out_dtype == torch.float32 else 2, 0.0, _ext.status_word(dev),
+                  sx, None, 1, None)
     return y[:, : m.out_features]
