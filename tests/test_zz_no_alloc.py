@@ -42,19 +42,24 @@ def _rel_err(y, r):
     return ((y.float() - r.float()).norm() / r.float().norm().clamp_min(1e-12)).item()
 
 
-def test_noalloc_matches_existing_entry_point_twice():
+# (M, N, K, splits): the first two split K through fp32 partials in the fixed scratch (more than
+# 8 splits, or more than 128 rows); the last lets the library choose, which for a small M reduces
+# the splits on chip and leaves the scratch alone.
+CASES = [(8, 1024, 4096, 16), (256, 1024, 4096, 2), (8, 1024, 4096, 0)]
+
+
+@pytest.mark.parametrize("M,N,K,splits", CASES)
+def test_noalloc_matches_existing_entry_point_twice(M, N, K, splits):
     from vllm_cmp170hx_b200 import ops
 
     f = _entry()
     torch.manual_seed(0)
-    # small M, long K: the split-K path, whose partials live in the fixed scratch
-    M, N, K = 8, 1024, 4096
     for call in range(2):
         x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
         w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / K ** 0.5
         expected = ops.gemm(x, w)
         y = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
-        rc = _call(f, x, w, y)
+        rc = _call(f, x, w, y, splits)
         torch.cuda.synchronize()
         assert rc == 0, (call, rc)
         assert _rel_err(y, expected) < 1e-2, (call, _rel_err(y, expected))

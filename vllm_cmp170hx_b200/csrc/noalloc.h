@@ -18,7 +18,9 @@
 //     partial sums and the kernel's status word live in file-scope
 //     `static __device__` arrays: B200_NOALLOC_SCRATCH_FLOATS fp32 values
 //     (4 MiB) plus one small status block.  Every GPU that loads the library
-//     holds this memory until the process exits.
+//     holds this memory until the process exits.  Shapes of at most 128 rows
+//     split at most 8 ways reduce their partial sums on chip (a thread-block
+//     cluster) and leave the scratch untouched.
 //   * The first call on a device looks up the device address of that scratch
 //     (cudaGetSymbolAddress, with that device current).  Make the first call
 //     on each device before any stream capture.
