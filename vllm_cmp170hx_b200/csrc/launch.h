@@ -80,6 +80,10 @@ cudaError_t combine_allreduce(const CombineArArgs& a, int blocks, cudaStream_t s
 // ---------------------------------------------------------------- rows.cu
 cudaError_t dequant_rows_e4m3(const void* rows, int64_t row_bytes, int D, const uint8_t* failed, void* out, int n,
                               cudaStream_t stream);
+cudaError_t ple_decode_rows(const void* rows, int64_t words, const int64_t* ids, const void* bias,
+                            const int64_t* head_off, const int64_t* head_vocab, int heads, int dim, int bits,
+                            int64_t owner_lo, int64_t owner_hi, const uint8_t* failed, void* out, int n,
+                            cudaStream_t stream);
 
 // ---------------------------------------------------------------- timing.cu
 cudaError_t timing_stamp(int64_t* ring, const int* cursor, int width, int col, cudaStream_t stream);

@@ -96,6 +96,9 @@ void combine_allreduce_op(const at::Tensor& y, const at::Tensor& slot_of, const 
 
 void dequant_rows_op(const at::Tensor& rows, int64_t D, const c10::optional<at::Tensor>& failed,
                      at::Tensor& out);  // rows.cu
+void ple_decode_op(const at::Tensor& rows, const at::Tensor& ids, const at::Tensor& head_bias,
+                   const at::Tensor& head_offsets, const at::Tensor& head_vocab, int64_t owner_lo, int64_t owner_hi,
+                   int64_t bits, const c10::optional<at::Tensor>& failed, at::Tensor& out);  // rows.cu
 void timing_stamp_op(at::Tensor& ring, const at::Tensor& cursor, int64_t col);             // timing.cu
 void timing_open_row_op(at::Tensor& ring, at::Tensor& cursor, at::Tensor& step_counter);  // timing.cu
 
@@ -168,6 +171,8 @@ void register_host_bindings(pybind11::module_& m);
     "int flag_off, int data_off, int tile_bytes_cap, int max_ctas, Tensor(b!) epochs, Tensor(c!) status, " \
     "float timeout_s) -> ()")                                                                            \
   X("dequant_rows(Tensor rows, int D, Tensor? failed, Tensor(a!) out) -> ()")                           \
+  X("ple_decode(Tensor rows, Tensor ids, Tensor head_bias, Tensor head_offsets, Tensor head_vocab, "     \
+    "int owner_lo, int owner_hi, int bits, Tensor? failed, Tensor(a!) out) -> ()")                      \
   X("timing_stamp(Tensor(a!) ring, Tensor cursor, int col) -> ()")                                      \
   X("timing_open_row(Tensor(a!) ring, Tensor(b!) cursor, Tensor(c!) step_counter) -> ()")               \
   X("combine_allreduce(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out, " \
@@ -204,4 +209,5 @@ void register_host_bindings(pybind11::module_& m);
   X("combine_allreduce", b200::combine_allreduce_op) \
   X("timing_stamp", b200::timing_stamp_op)            \
   X("dequant_rows", b200::dequant_rows_op)            \
+  X("ple_decode", b200::ple_decode_op)                \
   X("timing_open_row", b200::timing_open_row_op)

@@ -37,9 +37,12 @@ namespace b200 {
 
 class RowReader {
  public:
-  RowReader(const std::string& path, int64_t row_bytes, int64_t num_rows, int threads, int retries, bool o_direct)
-      : row_bytes_(row_bytes), num_rows_(num_rows), retries_(retries), o_direct_(o_direct) {
+  // Row r is the row_bytes bytes at byte base + r * row_bytes of the file.
+  RowReader(const std::string& path, int64_t row_bytes, int64_t num_rows, int threads, int retries, bool o_direct,
+            int64_t base = 0)
+      : row_bytes_(row_bytes), num_rows_(num_rows), base_(base), retries_(retries), o_direct_(o_direct) {
     if (row_bytes <= 0 || num_rows <= 0) throw std::invalid_argument("row_bytes and num_rows must be positive");
+    if (base < 0) throw std::invalid_argument("base must be non-negative");
     fd_ = ::open(path.c_str(), O_RDONLY | (o_direct ? O_DIRECT : 0));
     if (fd_ < 0) throw std::runtime_error("cannot open row table " + path);
     const int n = threads < 1 ? 1 : threads;
@@ -96,7 +99,7 @@ class RowReader {
       ++failures_;
       return false;
     }
-    const int64_t off = row * row_bytes_;
+    const int64_t off = base_ + row * row_bytes_;
     int delay_us = 1000;
     for (int attempt = 0; attempt <= retries_; ++attempt) {
       if (attempt > 0) {
@@ -155,7 +158,7 @@ class RowReader {
     }
   }
 
-  int64_t row_bytes_, num_rows_;
+  int64_t row_bytes_, num_rows_, base_;
   int retries_;
   bool o_direct_;
   int fd_ = -1;
@@ -180,7 +183,8 @@ class RowCache {
     data_.resize((size_t)slots * reader_->row_bytes());
   }
 
-  // Writes rows `ids` into out [n, row_bytes] (uint8, host); returns the failed-row mask.
+  // Writes rows `ids` into out [n, row_bytes] (uint8, host); returns the failed-row mask.  A negative
+  // id (a row the caller does not need, e.g. another rank's) is written as zeros and is not read.
   torch::Tensor fetch(const torch::Tensor& ids, torch::Tensor& out) {
     TORCH_CHECK(ids.scalar_type() == at::kLong && ids.dim() == 1 && !ids.is_cuda(), "ids: host int64 [n]");
     TORCH_CHECK(out.scalar_type() == at::kByte && !out.is_cuda() && out.is_contiguous() && out.size(0) == ids.size(0) &&
@@ -195,6 +199,10 @@ class RowCache {
     std::vector<int64_t> miss_idx;
     std::lock_guard<std::mutex> g(mu_);
     for (int64_t i = 0; i < n; ++i) {
+      if (id[i] < 0) {
+        std::memset(o + i * rb, 0, rb);
+        continue;
+      }
       const int64_t slot = lookup(id[i]);
       if (slot >= 0) {
         std::memcpy(o + i * rb, &data_[(size_t)slot * rb], rb);
@@ -260,8 +268,9 @@ class RowCache {
 void register_row_store(pybind11::module_& m) {
   namespace py = pybind11;
   py::class_<RowReader, std::shared_ptr<RowReader>>(m, "RowReader")
-      .def(py::init<const std::string&, int64_t, int64_t, int, int, bool>(), py::arg("path"), py::arg("row_bytes"),
-           py::arg("num_rows"), py::arg("threads") = 8, py::arg("retries") = 3, py::arg("o_direct") = false)
+      .def(py::init<const std::string&, int64_t, int64_t, int, int, bool, int64_t>(), py::arg("path"),
+           py::arg("row_bytes"), py::arg("num_rows"), py::arg("threads") = 8, py::arg("retries") = 3,
+           py::arg("o_direct") = false, py::arg("base") = 0)
       .def("read",
            [](RowReader& r, const torch::Tensor& ids, torch::Tensor& out) {
              TORCH_CHECK(ids.scalar_type() == at::kLong && !ids.is_cuda() && out.scalar_type() == at::kByte &&

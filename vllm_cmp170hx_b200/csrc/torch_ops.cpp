@@ -708,6 +708,38 @@ void dequant_rows_op(const at::Tensor& rows, int64_t D, const c10::optional<at::
                                 (int)rows.size(0), cur_stream()));
 }
 
+void ple_decode_op(const at::Tensor& rows, const at::Tensor& ids, const at::Tensor& head_bias,
+                   const at::Tensor& head_offsets, const at::Tensor& head_vocab, int64_t owner_lo, int64_t owner_hi,
+                   int64_t bits, const c10::optional<at::Tensor>& failed, at::Tensor& out) {
+  B200_CHECK_CUDA(rows);
+  TORCH_CHECK(rows.scalar_type() == at::kShort && rows.dim() == 2 && rows.is_contiguous(),
+              "ple_decode: rows int16 [n, 1 + dim*bits/16]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.is_contiguous() &&
+                  out.size(0) == rows.size(0),
+              "ple_decode: out bf16 [n, dim]");
+  const int64_t n = rows.size(0), dim = out.size(1), heads = head_bias.size(0);
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_cuda() && ids.is_contiguous() && ids.numel() == n,
+              "ple_decode: ids device int64 [n]");
+  TORCH_CHECK(head_bias.scalar_type() == at::kHalf && head_bias.is_cuda() && head_bias.is_contiguous() &&
+                  head_bias.dim() == 2 && head_bias.size(1) == dim && heads > 0,
+              "ple_decode: head_bias fp16 [heads, dim]");
+  for (const at::Tensor* t : {&head_offsets, &head_vocab})
+    TORCH_CHECK(t->scalar_type() == at::kLong && t->is_cuda() && t->is_contiguous() && t->numel() == heads,
+                "ple_decode: head offsets / vocab sizes device int64 [heads]");
+  TORCH_CHECK(bits >= 1 && bits <= 16 && (dim * bits) % 16 == 0 && rows.size(1) == 1 + dim * bits / 16,
+              "ple_decode: rows must be [n, 1 + dim*bits/16] with bits in [1, 16] and dim*bits a multiple of 16");
+  TORCH_CHECK(0 <= owner_lo && owner_lo <= owner_hi, "ple_decode: owner range");
+  if (failed.has_value())
+    TORCH_CHECK(failed->scalar_type() == at::kByte && failed->is_cuda() && failed->numel() == n,
+                "ple_decode: failed device uint8 [n]");
+  c10::cuda::CUDAGuard g(rows.device());
+  B200_LAUNCH(ple_decode_rows(rows.data_ptr(), rows.size(1), ids.data_ptr<int64_t>(), head_bias.data_ptr(),
+                              head_offsets.data_ptr<int64_t>(), head_vocab.data_ptr<int64_t>(), (int)heads, (int)dim,
+                              (int)bits, owner_lo, owner_hi,
+                              failed.has_value() ? failed->data_ptr<uint8_t>() : nullptr, out.data_ptr(), (int)n,
+                              cur_stream()));
+}
+
 }  // namespace b200
 
 namespace b200 {
