@@ -61,3 +61,24 @@ def test_hc_model_generates(delayed):
     assert outs == again and all(len(o) == 5 for o in outs)
     # the streams matter: the same weights without hyper-connections decode differently
     assert model.layers[0].hc_attn.fn.shape == (2 * 4 + 16, 4 * 256)
+
+
+@pytest.mark.parametrize("delayed", [False, True])
+def test_hc_state_hop_round_trip(delayed):
+    """The mHC state packed into one 16-byte-aligned uint8 message and back (pipeline hop)."""
+    from vllm_cmp170hx_b200.config import tiny
+    from vllm_cmp170hx_b200.models import hybrid
+
+    cfg = tiny(layers=2, experts=4, hidden=256)
+    cfg.hc_mult, cfg.hc_delayed = 4, delayed
+    T, n, d = 5, 4, 256
+    st = hybrid.HCState(torch.randn(T, d).bfloat16(), torch.randn(T, n, d).bfloat16(), torch.rand(T, n),
+                        torch.rand(T, n, n), torch.rand(T, n) if delayed else None)
+    buf = hybrid.hc_pack(st, cfg)
+    assert buf.dtype == torch.uint8 and buf.numel() == hybrid.hc_hop_bytes(cfg, T) and buf.numel() % 16 == 0
+    back = hybrid.hc_unpack(buf.clone(), cfg, T)
+    for name in ("x", "H", "post", "comb"):
+        assert torch.equal(getattr(back, name), getattr(st, name)), name
+    assert (back.pre_mix is None) == (not delayed)
+    if delayed:
+        assert torch.equal(back.pre_mix, st.pre_mix)

@@ -94,10 +94,11 @@ def _pp_worker(rank, world, port, fmt, tp, path):
     pstate.destroy()
 
 
-@pytest.mark.parametrize("fmt,tp", [("exl3", 1), ("deepseek_mtp", 1), ("deepseek_mtp", 2)])
+@pytest.mark.parametrize("fmt,tp", [("exl3", 1), ("deepseek_mtp", 1), ("deepseek_mtp", 2), ("exl3_hc", 1)])
 def test_pp2_matches_pp1(fmt, tp):
     """Two pipeline stages (packed p2p hops, micro-batches, token / draft broadcast from the last
-    stage) generate the same tokens as one stage; deepseek_mtp adds MTP speculative decoding."""
+    stage) generate the same tokens as one stage; deepseek_mtp adds MTP speculative decoding, exl3_hc
+    hyper-connection streams (the whole mHC state crosses the stage boundary)."""
     from vllm_cmp170hx_b200.parallel import state as pstate
 
     pstate.set_state(pstate.ParallelState())

@@ -21,6 +21,7 @@ import torch
 
 from .. import _ext
 from ..config import EngineConfig
+from ..models import hybrid
 from ..models.hybrid import HybridForCausalLM, StepContext
 from ..ops import sampling as sampling_ops
 from ..parallel import comm
@@ -280,6 +281,7 @@ class ModelRunner:
         st = self.st
         m = self.model
         H = self.mcfg.hidden_size
+        hc = bool(self.mcfg.hc_mult)
         grp = st.pp_group
         sends, toks, nbytes = [], [], 0
         verify = {}
@@ -293,13 +295,17 @@ class ModelRunner:
             nbytes += nb
             if m.first:
                 res = m(dev["ids"], ctx)
+            elif hc:
+                # hyper-connection streams: the whole mHC state as one packed uint8 message
+                buf = torch.empty(hybrid.hc_hop_bytes(self.mcfg, h["T"]), dtype=torch.uint8, device=self.device)
+                dist.recv(buf, src=st.pp_peer(st.pp_rank - 1), group=grp)
+                res = m(None, ctx, hybrid.hc_unpack(buf, self.mcfg, h["T"]))
             else:
                 buf = torch.empty(2, h["T"], H, dtype=torch.bfloat16, device=self.device)
                 dist.recv(buf, src=st.pp_peer(st.pp_rank - 1), group=grp)
                 res = m(None, ctx, (buf[0], buf[1]))
             if not m.last:
-                x, r = res
-                packed = torch.stack([x, r])
+                packed = hybrid.hc_pack(res, self.mcfg) if hc else torch.stack(list(res))
                 sends.append((dist.isend(packed, dst=st.pp_peer(st.pp_rank + 1), group=grp), packed))
             elif self.spec is not None:
                 rows = self._to_dev(h["sample_rows"])

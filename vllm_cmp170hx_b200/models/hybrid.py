@@ -395,6 +395,46 @@ class HyperConnection(nn.Module):
         return HCState(None, H, post, comb, pre if cfg.hc_delayed else None), inp
 
 
+def hc_hop_fields(cfg: ModelConfig, T: int) -> list[tuple[str, tuple[int, ...], torch.dtype]]:
+    """The mHC state crossing a pipeline-stage boundary after a layer: the pending sublayer output,
+    the streams, the post / comb it is applied with and (delayed form) the carried pre."""
+    n, d = cfg.hc_mult, cfg.hidden_size
+    f = [("x", (T, d), torch.bfloat16), ("H", (T, n, d), torch.bfloat16), ("post", (T, n), torch.float32),
+         ("comb", (T, n, n), torch.float32)]
+    if cfg.hc_delayed:
+        f.append(("pre_mix", (T, n), torch.float32))
+    return f
+
+
+def _hop_segments(cfg: ModelConfig, T: int):
+    off, segs = 0, []
+    for name, shape, dt in hc_hop_fields(cfg, T):
+        nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+        segs.append((name, shape, dt, off, nb))
+        off += (nb + 15) // 16 * 16  # every segment 16-byte aligned
+    return segs, off
+
+
+def hc_hop_bytes(cfg: ModelConfig, T: int) -> int:
+    return _hop_segments(cfg, T)[1]
+
+
+def hc_pack(state: "HCState", cfg: ModelConfig) -> torch.Tensor:
+    """The state as one flat uint8 buffer (one p2p message per hop; the layout follows from T)."""
+    T = state.H.shape[0]
+    segs, total = _hop_segments(cfg, T)
+    buf = torch.empty(total, dtype=torch.uint8, device=state.H.device)
+    for name, shape, dt, off, nb in segs:
+        buf[off:off + nb].view(dt).view(shape).copy_(getattr(state, name))
+    return buf
+
+
+def hc_unpack(buf: torch.Tensor, cfg: ModelConfig, T: int) -> "HCState":
+    segs, _ = _hop_segments(cfg, T)
+    vals = {name: buf[off:off + nb].view(dt).view(shape) for name, shape, dt, off, nb in segs}
+    return HCState(vals["x"], vals["H"], vals["post"], vals["comb"], vals.get("pre_mix"))
+
+
 @dataclass
 class HCState:
     """The mHC residual between sublayers: streams H [T, n, d], the pending sublayer output x with
@@ -494,21 +534,27 @@ class HybridForCausalLM(nn.Module):
             if (self.last or init_mode == "sliced") else None
         self.norm = RMSNorm(norm_w, cfg.rms_eps) if self.last else None
         self.lm_head = Linear(head) if self.last else None
-        if cfg.hc_mult:
-            if st.pp_size > 1:
-                raise NotImplementedError("hyper-connection streams across pipeline stages are not supported")
+        self.hc_head = None
+        if cfg.hc_mult and (self.last or init_mode == "sliced"):
             # the final boundary: the last sublayer's post, then the head collapse + final norm
-            self.hc_head = HyperConnection(cfg, wi)
+            hc_head = HyperConnection(cfg, wi)
+            self.hc_head = hc_head if self.last else None
 
     def forward(self, input_ids: torch.Tensor, ctx: StepContext,
-                hidden_in: tuple[torch.Tensor, torch.Tensor] | None = None):
-        """First stage: token ids; later stages: `hidden_in` = the previous stage's (hidden, residual).
-        Returns the normed final hidden on the last stage, else this stage's (hidden, residual)."""
+                hidden_in: "tuple[torch.Tensor, torch.Tensor] | HCState | None" = None):
+        """First stage: token ids; later stages: `hidden_in` = the previous stage's (hidden, residual),
+        or its `HCState` with hyper-connections.  Returns the normed final hidden on the last stage,
+        else what the next stage takes as `hidden_in`."""
         if self.cfg.hc_mult:
-            e = self.embed[input_ids]
-            state = HCState(None, e.unsqueeze(1).repeat(1, self.cfg.hc_mult, 1).contiguous())
+            if self.first:
+                e = self.embed[input_ids]
+                state = HCState(None, e.unsqueeze(1).repeat(1, self.cfg.hc_mult, 1).contiguous())
+            else:
+                state = hidden_in
             for layer in self.layers:
                 state = layer.forward_hc(state, ctx)
+            if not self.last:
+                return state
             return self.hc_head(state, self.norm, self.cfg)[1]
         if self.first:
             x, residual = self.embed[input_ids], None
