@@ -1,0 +1,154 @@
+"""DeepSeek-V4.1 attention core on the host: the quantize-dequantize grids, and the cached,
+chunked core (window ring, compressed groups at ratio 1 and 2, indexer top-k, candidate blocks,
+sinks) against a from-scratch per-token recomputation (reference: models/deepseek_v41/ops/
+sm80_attn_core.py, ops/sm80_act_quant.py)."""
+
+import pytest
+import torch
+
+from vllm_cmp170hx_b200.oracle import dsv4_attn as ref
+from vllm_cmp170hx_b200.ops.dsv4_attn import DSv4AttnCore, DSv4AttnSpec
+
+
+def test_qdq_grids():
+    x = torch.tensor([[0.0, 0.3, -1.1, 2.6, 5.0, -6.0, 100.0, 7e-3] * 4])
+    y = ref.qdq_fp4(x, 32, "e8m0")
+    s = 32.0  # the smallest power of two >= 100 / 6
+    grid = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6])
+    q = (y / s).abs().flatten()
+    assert all(bool((grid == v).any()) for v in q), q
+    y8 = ref.qdq_fp8(x, 32)
+    assert torch.equal(y8, ref.qdq_fp8(y8, 32))  # values on the grid stay put
+    assert ((y8 - x).abs() <= x.abs() * 2 ** -3 + 2 ** -9 * 2 ** -2).all()
+    # e4m3 block scales: s = e4m3(amax / 6)
+    z = ref.qdq_fp4(torch.full((1, 16), 0.75), 16, "e4m3")
+    assert torch.allclose(z, torch.full((1, 16), 0.75))
+
+
+def _weights(spec, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    d = spec.head_dim
+    freqs = 1.0 / (10000 ** (torch.arange(0, spec.rope_dim, 2).float() / spec.rope_dim))
+    return dict(freqs=freqs, sink=torch.randn(spec.heads, generator=g),
+                comp_norm=(1 + 0.1 * torch.randn(d, generator=g)).bfloat16(),
+                wk=(torch.randn(spec.index_dim, d, generator=g) * d ** -0.5).bfloat16(),
+                k_norm=(1 + 0.1 * torch.randn(spec.index_dim, generator=g)).bfloat16())
+
+
+def _inputs(spec, n, seed):
+    g = torch.Generator().manual_seed(seed)
+    d = spec.head_dim
+    return dict(q=torch.randn(n, spec.heads, d, generator=g).bfloat16(),
+                kv=torch.randn(n, d, generator=g).bfloat16(),
+                ks=torch.randn(n, 2 * d, generator=g),
+                iq=torch.randn(n, spec.index_heads, spec.index_dim, generator=g).bfloat16(),
+                iw=torch.randn(n, spec.index_heads, generator=g).bfloat16())
+
+
+def _scratch(spec, w, inp, p, cand=None):
+    """Query at position p of one sequence, recomputed from the raw inputs of positions 0..p."""
+    fr = w["freqs"]
+    pos = torch.tensor([p])
+    rows, valid = [], []
+    for b in range(spec.window):
+        j = p - b
+        ok = j >= 0
+        rows.append(ref.window_rows(inp["kv"][max(j, 0)][None], torch.tensor([max(j, 0)]), fr)[0])
+        valid.append(ok)
+    n_vis = (p + 1) // spec.ratio
+    sel = torch.full((spec.index_topk,), -1)
+    comp = []
+    if n_vis:
+        lat, gpos = [], []
+        for gi in range(n_vis):
+            if spec.ratio == 1:
+                lat.append(ref.rms_norm(inp["kv"][gi][None], w["comp_norm"], spec.eps)[0])
+            else:
+                lat.append(ref.pool_pair(inp["ks"][2 * gi][None], inp["ks"][2 * gi + 1][None], w["comp_norm"],
+                                         spec.eps)[0])
+            gpos.append(gi * spec.ratio)
+        lat, gpos = torch.stack(lat), torch.tensor(gpos)
+        comp = ref.compressed_rows(lat, gpos, fr)
+        keys = ref.index_key_rows((lat.float() @ w["wk"].float().t()).bfloat16(), w["k_norm"], fr, gpos, spec.eps)
+        qi = ref.index_query(inp["iq"][p][None], pos, fr)
+        wi = (inp["iw"][p][None].float() * (spec.index_dim ** -0.5 * spec.index_heads ** -0.5)).bfloat16()
+        sc = ref.index_scores(qi, wi, keys, torch.tensor([n_vis]), spec.index_heads_per_rank)
+        if cand is not None:
+            sc = ref.mask_to_candidates(sc, cand[None], spec.candidate_block)
+        sel = ref.topk_canonical(sc, torch.tensor([n_vis]), spec.index_topk)[0]
+        cb = ref.candidate_blocks(sc, torch.tensor([n_vis]), spec.candidate_blocks, spec.candidate_block)[0] \
+            if spec.candidate_blocks else None
+    else:
+        cb = torch.full((spec.candidate_blocks,), -1, dtype=torch.int32) if spec.candidate_blocks else None
+    for s in sel.tolist():
+        rows.append(comp[s] if s >= 0 else torch.zeros(spec.head_dim, dtype=torch.bfloat16))
+        valid.append(s >= 0)
+    qr = ref.rope(inp["q"][p][None], pos, fr)
+    o = ref.sparse_attention(qr, torch.stack(rows)[None], torch.tensor(valid)[None], w["sink"], spec.head_dim ** -0.5)
+    return ref.output_qdq(o, pos, fr, spec.out_groups)[0], cb
+
+
+def _run(spec, w, seqs, chunks, device="cpu", candidates=None):
+    """Two interleaved sequences stepped through the core in the given chunk sizes."""
+    core = DSv4AttnCore(spec, max_seqs=2, max_len=64, max_chunk=max(chunks), device=device, **w)
+    done = [0, 0]
+    outs = [[None] * len(s["kv"]) for s in seqs]
+    cands = [[None] * len(s["kv"]) for s in seqs]
+    for c in chunks:
+        seq, pos = [], []
+        for s in range(2):
+            n = min(c, len(seqs[s]["kv"]) - done[s])
+            seq += [s] * n
+            pos += list(range(done[s], done[s] + n))
+        if not seq:
+            break
+        seq_t, pos_t = torch.tensor(seq), torch.tensor(pos)
+
+        def pick(key):
+            return torch.stack([seqs[s][key][p] for s, p in zip(seq, pos)]).to(device)
+        cin = None
+        if candidates is not None:
+            cin = torch.stack([candidates[s][p] for s, p in zip(seq, pos)]).to(device)
+        cout = []
+        o = core.step(seq_t.to(device), pos_t.to(device), pick("q"), pick("kv"), pick("ks"), pick("iq"), pick("iw"),
+                      candidates_in=cin, candidates_out=cout if spec.candidate_blocks else None)
+        for i, (s, p) in enumerate(zip(seq, pos)):
+            outs[s][p] = o[i].cpu()
+            if cout:
+                cands[s][p] = cout[0][i].cpu()
+        for s in range(2):
+            done[s] += seq.count(s)
+    return outs, cands
+
+
+@pytest.mark.parametrize("ratio", [1, 2])
+def test_chunked_core_matches_from_scratch(ratio):
+    spec = DSv4AttnSpec(heads=4, window=8, ratio=ratio, index_heads=4, index_topk=5, index_heads_per_rank=2,
+                        out_groups=2)
+    w = _weights(spec)
+    seqs = [_inputs(spec, 23, 1), _inputs(spec, 17, 2)]
+    outs, _ = _run(spec, w, seqs, [6, 5, 1, 1, 4, 1, 1, 7, 1, 1])
+    for s in range(2):
+        for p in range(len(seqs[s]["kv"])):
+            exp, _ = _scratch(spec, w, seqs[s], p)
+            assert torch.equal(outs[s][p], exp), (ratio, s, p)
+
+
+def test_candidate_blocks_two_levels():
+    """A source layer picks candidate blocks; a user layer attends only inside them."""
+    src = DSv4AttnSpec(heads=2, window=4, ratio=1, index_heads=2, index_topk=6, index_heads_per_rank=2,
+                       candidate_blocks=2, candidate_block=4)
+    w = _weights(src, 3)
+    seqs = [_inputs(src, 30, 4), _inputs(src, 21, 5)]
+    _, cands = _run(src, w, seqs, [9, 1, 1, 12, 1, 1, 9])
+    for s in range(2):
+        for p in range(len(seqs[s]["kv"])):
+            _, cb = _scratch(src, w, seqs[s], p)
+            assert torch.equal(cands[s][p], cb), (s, p)
+    user = DSv4AttnSpec(heads=2, window=4, ratio=1, index_heads=2, index_topk=3, index_heads_per_rank=2,
+                        candidate_block=4)
+    outs, _ = _run(user, w, seqs, [9, 1, 1, 12, 1, 1, 9], candidates=cands)
+    for s in range(2):
+        for p in range(len(seqs[s]["kv"])):
+            exp, _ = _scratch(user, w, seqs[s], p, cand=cands[s][p])
+            assert torch.equal(outs[s][p], exp), (s, p)

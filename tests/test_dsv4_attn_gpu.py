@@ -1,0 +1,63 @@
+"""DeepSeek-V4.1 attention on the GPU: the 512-wide block-sparse attention kernel with per-head
+sinks (csrc/mla_attn.cu, D = 512) against the fp32 oracle, unsplit and split over positions (the
+sink then enters in the merge), and the cached core on CUDA against the same core on the host."""
+
+import pytest
+import torch
+
+from vllm_cmp170hx_b200.oracle import dsv4_attn as ref
+from vllm_cmp170hx_b200.ops.dsv4_attn import DSv4AttnCore, DSv4AttnSpec, attend
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("T,h,splits", [(5, 64, 1), (3, 64, 3), (9, 8, 1), (2, 128, 2), (4, 16, 4)])
+def test_sink_attention_matches_oracle(T, h, splits):
+    g = torch.Generator().manual_seed(T * 100 + h)
+    rows = 3000
+    pool = (torch.randn(rows, 512, generator=g) * 0.5).bfloat16()
+    q = (torch.randn(T, h, 512, generator=g) * 0.5).bfloat16()
+    idx = torch.randint(0, rows, (T, 128 + 512), generator=g)
+    idx[torch.rand(T, 640, generator=g) < 0.3] = -1
+    idx[0, :] = -1  # a query with no row gets zeros
+    idx[0, 5] = 17 if T > 1 else -1
+    idx[-1, 200:] = -1
+    sink = torch.randn(h, generator=g) * 2
+    scale = 512 ** -0.5
+    exp = ref.sparse_attention(q, pool[idx.clamp_min(0)], idx >= 0, sink, scale)
+    got = attend(q.cuda(), pool.cuda(), idx.cuda(), sink.cuda(), scale, splits=splits).cpu()
+    assert _rel(got, exp) < 1e-2, _rel(got, exp)
+    empty = (idx < 0).all(1)
+    assert (got[empty] == 0).all()
+
+
+@pytest.mark.parametrize("ratio", [1, 2])
+def test_core_on_cuda_matches_host(ratio):
+    spec = DSv4AttnSpec(heads=16, window=128, ratio=ratio, index_heads=8, index_topk=64, index_heads_per_rank=4,
+                        out_groups=2)
+    g = torch.Generator().manual_seed(ratio)
+    d = 512
+    w = dict(freqs=1.0 / (10000 ** (torch.arange(0, 64, 2).float() / 64)), sink=torch.randn(16, generator=g),
+             comp_norm=(1 + 0.1 * torch.randn(d, generator=g)).bfloat16(),
+             wk=(torch.randn(128, d, generator=g) * d ** -0.5).bfloat16(),
+             k_norm=(1 + 0.1 * torch.randn(128, generator=g)).bfloat16())
+    cores = {dev: DSv4AttnCore(spec, max_seqs=2, max_len=512, max_chunk=160, device=dev,
+                               **{k: v.to(dev) for k, v in w.items()}) for dev in ("cpu", "cuda")}
+    n = 300
+    inp = dict(q=torch.randn(2, n, 16, d, generator=g).bfloat16(), kv=torch.randn(2, n, d, generator=g).bfloat16(),
+               ks=torch.randn(2, n, 2 * d, generator=g), iq=torch.randn(2, n, 8, 128, generator=g).bfloat16(),
+               iw=torch.randn(2, n, 8, generator=g).bfloat16())
+    done = 0
+    for c in [150, 140, 1, 1, 1, 7]:
+        seq = torch.tensor([0] * c + [1] * c)
+        pos = torch.tensor(list(range(done, done + c)) * 2)
+        args = [inp[k][seq, pos] for k in ("q", "kv", "ks", "iq", "iw")]
+        out = {dev: cores[dev].step(seq.to(dev), pos.to(dev), *[a.to(dev) for a in args]).cpu()
+               for dev in ("cpu", "cuda")}
+        torch.cuda.synchronize()
+        assert _rel(out["cuda"], out["cpu"]) < 2e-2, (c, _rel(out["cuda"], out["cpu"]))
+        done += c

@@ -246,9 +246,12 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
                                const float* k_scale, const int* ctx_lens, const int* token_seq, const int* block_table,
                                int64_t ld_bt, float* scores, int64_t ld_scores, int max_ctx, uint32_t* status,
                                cudaStream_t stream);
-cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache, const int* indices, const int* counts,
-                                 int topk, float sm_scale, int splits, void* out, float* part_o, float* part_ml,
-                                 float* lse, uint32_t* status, cudaStream_t stream);
+// q [T, nh, dim] (dim 576: MLA latent + RoPE; 512: DeepSeek-V4.1 rows), cache rows of dim; V = the
+// first 512 dims.  sink: per-head logits added to the softmax denominator (null: none).
+cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const void* cache, const int* indices,
+                                 const int* counts, int topk, float sm_scale, int splits, void* out, float* part_o,
+                                 float* part_ml, float* lse, const float* sink, uint32_t* status,
+                                 cudaStream_t stream);
 
 // ---------------------------------------------------------------- sampling.cu
 cudaError_t sample_rows(const void* logits, int dtype, int64_t ld, int rows, int V, const float* temperature,

@@ -210,7 +210,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // merge split partials: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s
 __global__ void merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits, int T,
-                             int nh, __nv_bfloat16* __restrict__ out, float* __restrict__ lse) {
+                             int nh, __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
+                             const float* __restrict__ sink) {
   pdl_prologue();
   const int th = blockIdx.x;  // t * nh + h
   float M = -INFINITY;
@@ -220,6 +221,9 @@ __global__ void merge_kernel(const float* __restrict__ part_o, const float* __re
     const float m = part_ml[((int64_t)s * T * nh + th) * 2];
     if (m != -INFINITY) L += exp2f(m - M) * part_ml[((int64_t)s * T * nh + th) * 2 + 1];
   }
+  if (threadIdx.x == 0 && lse) lse[th] = L > 0.f ? (M + log2f(L)) / kLog2e : -INFINITY;
+  // a sink adds exp(sink) to the denominator only (not to the returned log-sum-exp)
+  if (sink != nullptr && M != -INFINITY) L += exp2f(sink[th % nh] * kLog2e - M);
   const float inv = L > 0.f ? 1.f / L : 0.f;
   for (int c = threadIdx.x; c < 512; c += blockDim.x) {
     float acc = 0.f;
@@ -229,7 +233,6 @@ __global__ void merge_kernel(const float* __restrict__ part_o, const float* __re
     }
     out[(int64_t)th * 512 + c] = __float2bfloat16(acc * inv);
   }
-  if (threadIdx.x == 0 && lse) lse[th] = L > 0.f ? (M + log2f(L)) / kLog2e : -INFINITY;
 }
 }  // namespace attn
 
@@ -258,10 +261,14 @@ __global__ void merge_kernel(const float* __restrict__ part_o, const float* __re
 namespace attn4 {
 constexpr int kThreads = 320;  // w0 Q TMA, w1-4 gather, w5 MMA, w6-9 softmax + epilogue
 constexpr int BP = 128;        // positions per block
-constexpr int DIM = 576;
-constexpr int NCH = DIM / 64;           // 9 dim chunks
-constexpr int NSTREAM = 5;              // chunks outside this half's latent dims (incl. RoPE)
-constexpr int NRET = NCH - NSTREAM;     // 4 retained chunks = V
+// Row width D (template): 576 = MLA latent 512 + RoPE 64 (V = the latent), or 512 = DeepSeek-V4.1
+// rows (RoPE tail inside; V = the whole row).  Either way V is 512 dims, 256 per latent half.
+constexpr int NRET = 4;                 // retained chunks = this half's 256 V dims
+template <int D>
+struct Geo {
+  static constexpr int NCH = D / 64;             // dim chunks: 9 or 8
+  static constexpr int NSTREAM = NCH - NRET;     // chunks outside this half's V dims: 5 or 4
+};
 constexpr int CH_BYTES = BP * 128;      // 16 KiB: 128 positions x 64 dims
 constexpr int Q_BYTES = 128 * 128;      // 16 KiB: 128 head rows x 64 dims
 constexpr int NQ = 3, NKS = 3;          // Q ring, streamed-K ring
@@ -287,6 +294,7 @@ struct Params {
   float* part_o;
   float* part_ml;
   float* lse;
+  const float* sink;  // per-head softmax sink logit (natural-log units, already scaled), or null
   int T;
   uint32_t* status;
 };
@@ -294,11 +302,12 @@ struct Params {
 // byte offset of (row r, 16-byte chunk c) in a 128-byte-swizzled tile of 128-byte rows
 B200_DEVICE uint32_t sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
 
-// dim chunk processed i-th in a block: first the 5 chunks outside this half's latent dims, then
-// this half's 4 (retained as V)
+// dim chunk processed i-th in a block: first the chunks outside this half's V dims (the other
+// half's, then the RoPE chunk 8 when D = 576), then this half's 4 (retained as V)
+template <int D>
 B200_DEVICE int chunk_at(int i, int half) {
-  if (i >= NSTREAM) return half * 4 + (i - NSTREAM);
-  return half == 0 ? 4 + i : (i < 4 ? i : 8);
+  if (i >= Geo<D>::NSTREAM) return half * 4 + (i - Geo<D>::NSTREAM);
+  return half == 0 ? 4 + i : (i < 4 ? i : i + 4);
 }
 
 B200_DEVICE void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
@@ -311,8 +320,10 @@ B200_DEVICE void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_attn_block_kernel(const __grid_constant__ CUtensorMap tma_q, Params p) {
+  constexpr int NCH = Geo<D>::NCH, NSTREAM = Geo<D>::NSTREAM;
   pdl_prologue();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -394,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&q_full[st], q_bytes);
-          tma_load_2d(sq + st * Q_BYTES, &tma_q, &q_full[st], chunk_at(i, half) * 64, row0);
+          tma_load_2d(sq + st * Q_BYTES, &tma_q, &q_full[st], chunk_at<D>(i, half) * 64, row0);
           ++issued;
         }
       }
@@ -424,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nxt = b + 1 < nb ? fetch_idx(b + 1) : -1;  // in flight while this block's copies issue
       const int rb = b & 1;
       for (int i = 0; i < NCH; ++i) {
-        const int c = chunk_at(i, half);
+        const int c = chunk_at<D>(i, half);
         uint32_t dst;
         uint64_t* bar;
         if (i < NSTREAM) {
@@ -451,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int it = 0; it < BP / 16; ++it) {
           const int r = it * 16 + sub * 4 + gw;
           const int slot = __shfl_sync(0xffffffffu, cur, it * 4 + sub);
-          const void* src = slot >= 0 ? reinterpret_cast<const void*>(p.cache + (int64_t)slot * DIM + c * 64 + ch * 8)
+          const void* src = slot >= 0 ? reinterpret_cast<const void*>(p.cache + (int64_t)slot * D + c * 64 + ch * 8)
                                       : reinterpret_cast<const void*>(p.cache);
           cp_async16(dst + sw128(r, ch), src, slot >= 0 ? 16u : 0u);
         }
@@ -603,7 +614,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (o_ok) o_ok = mbar_wait_or_abort(o_full, 0, p.status, abort_flag);
     if (__all_sync(0xffffffffu, o_ok)) {
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      float l_tot = l_run;
+      if (p.sink != nullptr && p.splits == 1 && head < p.nh) l_tot += exp2f(p.sink[head] * kLog2e - m_run);
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
       for (int c = 0; c < 256; c += 16) {
         uint32_t r[16];
         tmem_ld16(tO + lane_off + c, r);
@@ -681,11 +694,27 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
   return cudaGetLastError();
 }
 
-cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache, const int* indices, const int* counts,
-                                 int topk, float sm_scale, int splits, void* out, float* part_o, float* part_ml,
-                                 float* lse, uint32_t* status, cudaStream_t stream) {
+namespace {
+template <int D>
+cudaError_t launch_sparse_attention(const CUtensorMap& tq, const mla::attn4::Params& p, int T, int nh, int splits,
+                                    cudaStream_t stream) {
+  using namespace mla::attn4;
+  cudaError_t e = cudaFuncSetAttribute(sparse_attn_block_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid(T, (nh + 127) / 128, 2 * splits);
+  launch_pdl(sparse_attn_block_kernel<D>, dim3(grid), dim3(kThreads), SMEM, stream, tq, p);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const void* cache, const int* indices,
+                                 const int* counts, int topk, float sm_scale, int splits, void* out, float* part_o,
+                                 float* part_ml, float* lse, const float* sink, uint32_t* status,
+                                 cudaStream_t stream) {
   using namespace mla::attn4;
   if (T == 0) return cudaSuccess;
+  if (dim != 512 && dim != 576) return cudaErrorInvalidValue;
+  const int DIM = dim;
   const int box_rows = nh >= 128 ? 128 : (nh + 7) / 8 * 8;
   CUtensorMap tq = make_tma_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)T * nh, DIM, DIM, box_rows, 64,
                                CU_TENSOR_MAP_SWIZZLE_128B);
@@ -702,16 +731,14 @@ cudaError_t mla_sparse_attention(const void* q, int T, int nh, const void* cache
   p.part_o = part_o;
   p.part_ml = part_ml;
   p.lse = lse;
+  p.sink = sink;
   p.T = T;
   p.status = status;
-  cudaError_t e = cudaFuncSetAttribute(sparse_attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-  if (e != cudaSuccess) return e;
-  dim3 grid(T, (nh + 127) / 128, 2 * splits);
-  launch_pdl(sparse_attn_block_kernel, dim3(grid), dim3(kThreads), SMEM, stream, tq, p);
-  e = cudaGetLastError();
+  cudaError_t e = dim == 512 ? launch_sparse_attention<512>(tq, p, T, nh, splits, stream)
+                             : launch_sparse_attention<576>(tq, p, T, nh, splits, stream);
   if (e != cudaSuccess || splits == 1) return e;
   launch_pdl(mla::attn::merge_kernel, dim3(T * nh), dim3(128), 0, stream, part_o, part_ml, splits, T, nh,
-                                                      reinterpret_cast<__nv_bfloat16*>(out), lse);
+             reinterpret_cast<__nv_bfloat16*>(out), lse, sink);
   return cudaGetLastError();
 }
 

@@ -449,11 +449,19 @@ void mla_topk_op(const at::Tensor& scores, const at::Tensor& ctx_lens, int64_t k
 
 void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& indices,
                              const at::Tensor& counts, double sm_scale, int64_t splits, at::Tensor& out,
-                             const c10::optional<at::Tensor>& lse, const at::Tensor& status) {
+                             const c10::optional<at::Tensor>& lse, const at::Tensor& status,
+                             const c10::optional<at::Tensor>& sink) {
   B200_CHECK_CUDA(q);
   B200_CHECK_DTYPE(q, at::kBFloat16);
-  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576 && q.is_contiguous(), "sparse attn: q [T, nh, 576] contiguous");
-  TORCH_CHECK(cache.scalar_type() == at::kBFloat16 && cache.is_contiguous() && cache.size(-1) == 576, "sparse attn: cache");
+  TORCH_CHECK(q.dim() == 3 && (q.size(2) == 576 || q.size(2) == 512) && q.is_contiguous(),
+              "sparse attn: q [T, nh, 576 or 512] contiguous");
+  const int dim = (int)q.size(2);
+  TORCH_CHECK(cache.scalar_type() == at::kBFloat16 && cache.is_contiguous() && cache.size(-1) == dim,
+              "sparse attn: cache rows must match q's width");
+  if (sink.has_value())
+    TORCH_CHECK(sink->scalar_type() == at::kFloat && sink->is_cuda() && sink->is_contiguous() &&
+                    sink->numel() == q.size(1),
+                "sparse attn: sink fp32 [nh]");
   TORCH_CHECK(indices.scalar_type() == at::kInt && indices.is_contiguous() && indices.size(0) == q.size(0),
               "sparse attn: indices [T, topk] int32");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(-1) == 512, "sparse attn: out");
@@ -464,11 +472,12 @@ void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const
     part_o = at::empty({splits, T, nh, 512}, q.options().dtype(at::kFloat));
     part_ml = at::empty({splits, T, nh, 2}, q.options().dtype(at::kFloat));
   }
-  B200_LAUNCH(mla_sparse_attention(q.data_ptr(), T, nh, cache.data_ptr(), indices.data_ptr<int>(),
+  B200_LAUNCH(mla_sparse_attention(q.data_ptr(), T, nh, dim, cache.data_ptr(), indices.data_ptr<int>(),
                                    counts.data_ptr<int>(), indices.size(1), (float)sm_scale, (int)splits,
                                    out.data_ptr(), splits > 1 ? part_o.data_ptr<float>() : nullptr,
                                    splits > 1 ? part_ml.data_ptr<float>() : nullptr,
-                                   lse.has_value() ? lse->data_ptr<float>() : nullptr, status_ptr(status),
+                                   lse.has_value() ? lse->data_ptr<float>() : nullptr,
+                                   sink.has_value() ? sink->data_ptr<float>() : nullptr, status_ptr(status),
                                    cur_stream()));
 }
 
