@@ -233,6 +233,8 @@ class SchedulerConfig:
     long_prefill_token_threshold: int = 0
     num_speculative_tokens: int = 0
     adaptive_k: str = ""  # '' off, 'by_load', 'accept' (load-adaptive draft count)
+    spec_method: str = "mtp"  # drafter: 'mtp' (chained MTP head) or 'dflash' (block drafter)
+    dflash_layers: int = 1  # DFlash drafter depth
 
 
 @dataclass

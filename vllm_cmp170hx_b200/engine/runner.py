@@ -87,8 +87,12 @@ class ModelRunner:
                 torch.cuda.synchronize()
                 free, _total = torch.cuda.mem_get_info(self.device)
                 kda_bytes = len(kda_ids) * self.num_slots * (math.prod(rec_shape) * 4 + math.prod(conv_shape) * 2)
-                n_mla = len(mla_ids) + (1 if cfg.scheduler.num_speculative_tokens > 0 else 0)  # + MTP layer
+                spec = cfg.scheduler.num_speculative_tokens > 0
+                mtp = spec and cfg.scheduler.spec_method == "mtp"
+                n_mla = len(mla_ids) + (1 if mtp else 0)  # + MTP layer
                 per_block = max(1, n_mla) * 64 * (576 * 2 + 128 + 4)
+                if spec and not mtp:  # DFlash context keys / values (the drafter's default shape)
+                    per_block += cfg.scheduler.dflash_layers * 64 * 2 * 4 * 128 * 2
                 scratch = 6 << 30
                 avail = free * cfg.cache.gpu_memory_utilization - kda_bytes - scratch
                 nb = int(max(avail, 0) // per_block)

@@ -23,7 +23,10 @@ host generator seeded by (seed, step), identical on every rank.
 Proposal (the DeepSeek MTP drafter of the reference's config 5): after the
 target step the MTP head catches up over the positions the target just
 computed -- position i takes token i+1 and the target's final hidden h_i --
-and then chains k-1 single-token steps on its own hidden state.  The drafts
+and then chains k-1 single-token steps on its own hidden state.  With the
+DFlash block drafter (models/dflash.py) the step's verified positions are
+stored as context rows from the target's auxiliary hidden states and all k
+drafts come from one non-causal forward of [bonus, mask x k].  The drafts
 of all requests are produced together and copied to the host once.
 """
 
@@ -69,18 +72,32 @@ class SpecDecoder:
     """MTP drafter + verifier bound to a :class:`ModelRunner`."""
 
     def __init__(self, runner, k: int):
-        from ..models.mtp import MTPHead
-
         self.runner = runner
         self.k = k
         cfg = runner.cfg
-        self.mtp = MTPHead(cfg.model, runner.model, runner.device, cfg.seed,
-                           getattr(runner.model, "init_mode", "local"))
         rows = runner.num_blocks * 64
-        runner.mla_caches[self.mtp.layer_id] = (
-            torch.zeros(rows, 576, dtype=torch.bfloat16, device=runner.device),
-            torch.zeros(rows, 128, dtype=torch.uint8, device=runner.device),
-            torch.ones(rows, dtype=torch.float32, device=runner.device))
+        self.method = cfg.scheduler.spec_method
+        init_mode = getattr(runner.model, "init_mode", "local")
+        self.mtp = self.dflash = None
+        if self.method == "dflash":
+            from ..models.dflash import DFlashConfig, DFlashDrafter
+
+            if runner.st.pp_size > 1 or cfg.model.hc_mult:
+                raise NotImplementedError("the DFlash drafter runs without pipeline stages and hyper-connections")
+            dc = DFlashConfig(num_layers=cfg.scheduler.dflash_layers)
+            self.dflash = DFlashDrafter(cfg.model, dc, runner.model, runner.device, cfg.seed, init_mode)
+            runner.model.aux_layer_ids = tuple(self.dflash.dc.aux_layer_ids)
+            self.dcaches = self.dflash.alloc_caches(rows, runner.device)
+        elif self.method == "mtp":
+            from ..models.mtp import MTPHead
+
+            self.mtp = MTPHead(cfg.model, runner.model, runner.device, cfg.seed, init_mode)
+            runner.mla_caches[self.mtp.layer_id] = (
+                torch.zeros(rows, 576, dtype=torch.bfloat16, device=runner.device),
+                torch.zeros(rows, 128, dtype=torch.uint8, device=runner.device),
+                torch.ones(rows, dtype=torch.float32, device=runner.device))
+        else:
+            raise ValueError(f"unknown speculative method {self.method!r}")
         self.step_no = 0
         # draft distributions of sampled requests: rid -> (tensor [k, A, V_local], row a)
         self.q_store: dict[str, tuple[torch.Tensor, int]] = {}
@@ -180,6 +197,8 @@ class SpecDecoder:
         dev = r.device
         for s in out.reqs:
             self.q_store.pop(s.req.request_id, None)
+        if self.dflash is not None:
+            return self._propose_dflash(out, accepted)
         ids, pos, hrows, tseq, reqs = [], [], [], [], []
         last = []
         t = 0
@@ -235,6 +254,66 @@ class SpecDecoder:
             cur_pos = [p + 1 for p in cur_pos]
             ctx = self._ctx(cur_pos, list(range(A)), areqs)
             cur = self.mtp(tok, cur, ctx)
+        dh = torch.stack(drafts, dim=1).cpu().tolist()
+        for a, req in enumerate(areqs):
+            limit = max(0, min(self.k, req.params.max_tokens - len(req.output_token_ids) - 1))
+            req.draft_token_ids = [int(v) for v in dh[a][:limit]]
+        for qi, a in enumerate(samp):
+            self.q_store[areqs[a].request_id] = (qbuf, qi)
+
+    def _slot(self, req, p: int) -> int:
+        b = req.block_ids
+        return b[p // 64] * 64 + p % 64 if p // 64 < len(b) else -1
+
+    def _propose_dflash(self, out, accepted: dict[str, list[int]]) -> None:
+        """DFlash: store the context rows this step verified, then draft all k tokens of every
+        request that keeps decoding with one block forward."""
+        r = self.runner
+        dev = r.device
+        d = self.dflash
+        rows, pos, slots = [], [], []
+        t = 0
+        for s in out.reqs:
+            req, base = s.req, t
+            t += s.num_new
+            # a verify step keeps the last token and the accepted drafts (acc = accepted + 1 token)
+            m = min(len(accepted.get(req.request_id, [])), s.num_new) if s.num_draft else s.num_new
+            for j in range(m):
+                rows.append(base + j)
+                pos.append(s.start + j)
+                slots.append(self._slot(req, s.start + j))
+        aux = r.model.aux_hidden
+        if rows:
+            ri = torch.tensor(rows, device=dev)
+            states = d.context_states([a.index_select(0, ri) for a in aux])
+            d.store_context(states, torch.tensor(pos, device=dev), torch.tensor(slots, device=dev), self.dcaches)
+        areqs = [s.req for s in out.reqs
+                 if not s.req.status.finished and s.req.num_computed_tokens == s.req.num_tokens - 1]
+        if not areqs:
+            return
+        A = len(areqs)
+        last = [q.num_computed_tokens - 1 for q in areqs]
+        C = max(last) + 1
+        cs = np.full((A, C), -1, dtype=np.int64)
+        for a, q in enumerate(areqs):
+            b = np.asarray(q.block_ids, dtype=np.int64)
+            p = np.arange(last[a] + 1)
+            cs[a, : last[a] + 1] = b[p // 64] * 64 + p % 64
+        ctx_slots = r._to_dev(cs)
+        bonus = torch.tensor([q.all_token_ids[q.num_computed_tokens] for q in areqs], device=dev)
+        h = d(bonus, torch.tensor(last, device=dev), ctx_slots, ctx_slots >= 0, self.dcaches, self.k)
+        temps_l = [q.params.temperature for q in areqs]
+        temps = torch.tensor(temps_l, dtype=torch.float32, device=dev) if any(v > 0 for v in temps_l) else None
+        samp = [i for i, v in enumerate(temps_l) if v > 0]
+        qbuf = torch.empty(self.k, len(samp), r.model.vocab_local, dtype=torch.float32, device=dev) if samp else None
+        drafts = []
+        for j in range(self.k):
+            logits = r.model.compute_logits(h[:, j].contiguous())
+            drafts.append(_sample(logits, temps, r.cfg.seed ^ (_SEED_DRAFT + j), r.step_counter, r.model.vocab_offset))
+            if samp:
+                sel = torch.tensor(samp, device=dev)
+                e, ssum = tempered_probs(logits.index_select(0, sel), temps.index_select(0, sel))
+                qbuf[j] = e / ssum[:, None]
         dh = torch.stack(drafts, dim=1).cpu().tolist()
         for a, req in enumerate(areqs):
             limit = max(0, min(self.k, req.params.max_tokens - len(req.output_token_ids) - 1))

@@ -534,6 +534,9 @@ class HybridForCausalLM(nn.Module):
             if (self.last or init_mode == "sliced") else None
         self.norm = RMSNorm(norm_w, cfg.rms_eps) if self.last else None
         self.lm_head = Linear(head) if self.last else None
+        # layers whose output the forward keeps in `aux_hidden` (set by a DFlash drafter)
+        self.aux_layer_ids: tuple[int, ...] = ()
+        self.aux_hidden: list[torch.Tensor] = []
         self.hc_head = None
         if cfg.hc_mult and (self.last or init_mode == "sliced"):
             # the final boundary: the last sublayer's post, then the head collapse + final norm
@@ -560,8 +563,13 @@ class HybridForCausalLM(nn.Module):
             x, residual = self.embed[input_ids], None
         else:
             x, residual = hidden_in
+        aux = self.aux_layer_ids
+        if aux:
+            self.aux_hidden = []
         for layer in self.layers:
             x, residual = layer(x, residual, ctx)
+            if layer.idx in aux:  # the residual stream after this layer (a block drafter's input)
+                self.aux_hidden.append(x + residual)
         if self.last:
             return self.norm(x, residual)
         return x, residual
