@@ -1,0 +1,110 @@
+"""Per-request verify depth (the reference's DSpark adaptive depth, spec_decode/dspark_row_mask*.py):
+policy parsing, the E(k) / cost(k) and tau decision rules, the draft-logit statistics, and greedy
+speculative decoding under a policy emitting exactly the tokens of plain decoding."""
+
+import json
+import math
+
+import pytest
+import torch
+
+from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, SchedulerConfig, tiny_deepseek
+from vllm_cmp170hx_b200.engine.depth_policy import DepthPolicy, draft_features, logit_stats
+from vllm_cmp170hx_b200.engine.llm_engine import LLM
+from vllm_cmp170hx_b200.engine.request import SamplingParams
+from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+from vllm_cmp170hx_b200.parallel import state as pstate
+
+
+def _pol(**kw):
+    raw = {"schema": "dspark-depth-policy/1", "max_depth": 3, "features": ["bias"],
+           "weights": [[0.0], [0.0], [0.0]], "costs": {"1": {"0": 10, "1": 11, "2": 12, "3": 13},
+                                                        "4": {"0": 10, "1": 14, "2": 18, "3": 22}}}
+    raw.update(kw)
+    return DepthPolicy.from_dict(raw)
+
+
+def test_policy_validation():
+    with pytest.raises(ValueError):
+        _pol(schema="x")
+    with pytest.raises(ValueError):
+        _pol(features=["bias", "nope"], weights=[[0, 0]] * 3)
+    with pytest.raises(ValueError):
+        _pol(costs={"1": {"0": 1, "2": 2}})  # a gap in k
+    with pytest.raises(ValueError):
+        _pol(costs={"1": {"0": 3, "1": 2}})  # decreasing
+    assert _pol().max_depth == 3
+
+
+def _brute(p, T, b):
+    K = len(p)
+    best, arg = -1.0, 0
+    for k in range(K + 1):
+        E = 1 + sum(math.prod(p[:i + 1]) for i in range(k))
+        c = T[K] - (T[K] - T[k]) / b
+        if E / c >= best - 1e-15:
+            best, arg = E / c, k
+    return arg
+
+
+def test_cost_rule_and_interpolation():
+    pol = _pol()
+    for probs in ([0.9, 0.8, 0.7], [0.1, 0.9, 0.9], [0.5, 0.5, 0.5], [0.99, 0.01, 0.99]):
+        p = torch.tensor([probs])
+        for b in (1, 2, 4, 7):
+            T = pol.cost_row(b, 3)
+            assert pol.live(p, b) == [_brute(probs, T, b)], (probs, b)
+    # batch 2 lies between the listed 1 and 4: T_2(k) = T_1(k) * 2/3 + T_4(k) / 3
+    assert pol.cost_row(2, 3) == pytest.approx([10, 11 * 2 / 3 + 14 / 3, 12 * 2 / 3 + 18 / 3, 13 * 2 / 3 + 22 / 3])
+
+
+def test_tau_rule():
+    pol = _pol(tau={"2": 0.5, "8": 0.2})
+    p = torch.tensor([[0.9, 0.6, 0.9], [0.4, 0.9, 0.9]])
+    # cumulative products: row 0 .9, .54, .486; row 1 .4, .36, .324
+    assert pol.live(p, 2) == [2, 0]
+    assert pol.live(p, 8) == [3, 3]  # tau .2
+    assert pol.live(p, 5) == [3, 2]  # tau interpolated to .35
+    assert pol.live(p[:1], 1) == [_brute([0.9, 0.6, 0.9], pol.cost_row(1, 3), 1)]  # one request: the cost rule
+
+
+def test_logit_stats_and_features():
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(3, 1000, generator=g) * 3
+    st = logit_stats(x)
+    p = x.softmax(-1)
+    assert torch.allclose(st[:, 0], p.max(-1).values, rtol=1e-5)
+    assert torch.allclose(st[:, 1], -(p * p.log()).sum(-1), rtol=1e-4)
+    f = draft_features(3, 1, st[:, None], torch.full((3, 1), 0.75))
+    assert torch.allclose(f[..., 0], torch.ones(3, 1))
+    assert torch.allclose(f[..., 1], torch.full((3, 1), math.log(3.0)))
+
+
+def _cfg(k, policy=""):
+    return EngineConfig(model=tiny_deepseek(layers=3, experts=4, hidden=256, vocab=512),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=256,
+                                                  num_speculative_tokens=k, spec_method="dflash",
+                                                  depth_policy=policy),
+                        cache=CacheConfig(num_blocks=48), device="cpu", enforce_eager=True)
+
+
+@pytest.mark.parametrize("bias,cut", [(3.0, False), (-20.0, True)])
+def test_greedy_spec_under_depth_policy_matches_plain(tmp_path, bias, cut):
+    pstate.set_state(pstate.ParallelState())
+    path = tmp_path / "policy.json"
+    path.write_text(json.dumps({
+        "schema": "dspark-depth-policy/1", "max_depth": 3, "features": ["bias", "logit_conf", "logit_top1", "ent"],
+        "weights": [[bias, 0.1, 0.1, -0.01]] * 3,
+        "costs": {"1": {"0": 10, "1": 10.5, "2": 11, "3": 11.5}, "4": {"0": 10, "1": 11, "2": 12, "3": 13}}}))
+    prompts = [[(5 * i + 3 * j) % 500 for j in range(n)] for i, n in enumerate([9, 40, 71])]
+    model = HybridForCausalLM(_cfg(0).model, "cpu", seed=3)
+    plain = LLM(_cfg(0), model).generate(prompts, SamplingParams(max_tokens=8))
+    llm = LLM(_cfg(3, str(path)), model)
+    got = llm.generate(prompts, SamplingParams(max_tokens=8))
+    model.aux_layer_ids = ()
+    assert [o.output_token_ids for o in got] == [o.output_token_ids for o in plain]
+    st = llm.engine.runner.spec.stats
+    if cut:  # every draft judged not worth verifying: none scheduled
+        assert st["proposed"] == 0 and st["depth_cut"] > 0
+    else:
+        assert st["proposed"] > 0

@@ -235,6 +235,7 @@ class SchedulerConfig:
     adaptive_k: str = ""  # '' off, 'by_load', 'accept' (load-adaptive draft count)
     spec_method: str = "mtp"  # drafter: 'mtp' (chained MTP head) or 'dflash' (block drafter)
     dflash_layers: int = 1  # DFlash drafter depth
+    depth_policy: str = ""  # per-request verify depth policy file (dspark-depth-policy/1); "" off
 
 
 @dataclass

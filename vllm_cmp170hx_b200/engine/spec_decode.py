@@ -36,10 +36,12 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
+from .. import envs
 from ..models.hybrid import StepContext
 from ..ops import sampling as sampling_ops
 from ..parallel import comm
 from ..parallel import state as pstate
+from .depth_policy import logit_stats
 
 _SEED_VERIFY = 0x5BD1E995
 _SEED_DRAFT = 0x27D4EB2F
@@ -98,6 +100,14 @@ class SpecDecoder:
                 torch.ones(rows, dtype=torch.float32, device=runner.device))
         else:
             raise ValueError(f"unknown speculative method {self.method!r}")
+        self.depth = None
+        path = cfg.scheduler.depth_policy or envs.get("VLLM_B200_ADAPTIVE_DEPTH")
+        if path:
+            from .depth_policy import DepthPolicy
+
+            self.depth = DepthPolicy.load(path)
+            if self.depth.uses_conf and self.dflash is None:
+                raise ValueError("the depth policy reads a confidence head, which only the DFlash drafter has")
         self.step_no = 0
         # draft distributions of sampled requests: rid -> (tensor [k, A, V_local], row a)
         self.q_store: dict[str, tuple[torch.Tensor, int]] = {}
@@ -240,10 +250,12 @@ class SpecDecoder:
         temps = torch.tensor(temps_l, dtype=torch.float32, device=dev) if any(v > 0 for v in temps_l) else None
         samp = [i for i, v in enumerate(temps_l) if v > 0]
         qbuf = torch.empty(self.k, len(samp), r.model.vocab_local, dtype=torch.float32, device=dev) if samp else None
-        drafts = []
+        drafts, stats = [], []
         for j in range(self.k):
             logits = self.mtp.compute_logits(cur)
             tok = _sample(logits, temps, r.cfg.seed ^ (_SEED_DRAFT + j), r.step_counter, r.model.vocab_offset)
+            if self.depth is not None and self.depth.uses_stats:
+                stats.append(logit_stats(logits, _all_reduce))
             if samp:
                 sel = torch.tensor(samp, device=dev)
                 e, ssum = tempered_probs(logits.index_select(0, sel), temps.index_select(0, sel))
@@ -254,12 +266,26 @@ class SpecDecoder:
             cur_pos = [p + 1 for p in cur_pos]
             ctx = self._ctx(cur_pos, list(range(A)), areqs)
             cur = self.mtp(tok, cur, ctx)
+        live = self._live(A, stats, None)
         dh = torch.stack(drafts, dim=1).cpu().tolist()
         for a, req in enumerate(areqs):
-            limit = max(0, min(self.k, req.params.max_tokens - len(req.output_token_ids) - 1))
+            limit = max(0, min(self.k, live[a], req.params.max_tokens - len(req.output_token_ids) - 1))
             req.draft_token_ids = [int(v) for v in dh[a][:limit]]
         for qi, a in enumerate(samp):
             self.q_store[areqs[a].request_id] = (qbuf, qi)
+
+    def _live(self, A: int, stats: list, conf) -> list[int]:
+        """Drafts worth verifying per request (all k without a depth policy)."""
+        if self.depth is None:
+            return [self.k] * A
+        from .depth_policy import draft_features
+
+        K = min(self.k, self.depth.max_depth)
+        st = torch.stack(stats, 1)[:, :K] if stats else None
+        feats = draft_features(A, K, st, conf[:, :K] if conf is not None else None, self.runner.device)
+        live = self.depth.live(self.depth.accept_probs(feats), A)
+        self.stats["depth_cut"] = self.stats.get("depth_cut", 0) + sum(self.k - v for v in live)
+        return live
 
     def _slot(self, req, p: int) -> int:
         b = req.block_ids
@@ -306,17 +332,20 @@ class SpecDecoder:
         temps = torch.tensor(temps_l, dtype=torch.float32, device=dev) if any(v > 0 for v in temps_l) else None
         samp = [i for i, v in enumerate(temps_l) if v > 0]
         qbuf = torch.empty(self.k, len(samp), r.model.vocab_local, dtype=torch.float32, device=dev) if samp else None
-        drafts = []
+        drafts, stats = [], []
         for j in range(self.k):
             logits = r.model.compute_logits(h[:, j].contiguous())
             drafts.append(_sample(logits, temps, r.cfg.seed ^ (_SEED_DRAFT + j), r.step_counter, r.model.vocab_offset))
+            if self.depth is not None and self.depth.uses_stats:
+                stats.append(logit_stats(logits, _all_reduce))
             if samp:
                 sel = torch.tensor(samp, device=dev)
                 e, ssum = tempered_probs(logits.index_select(0, sel), temps.index_select(0, sel))
                 qbuf[j] = e / ssum[:, None]
+        live = self._live(A, stats, d.confidence(h) if (self.depth is not None and self.depth.uses_conf) else None)
         dh = torch.stack(drafts, dim=1).cpu().tolist()
         for a, req in enumerate(areqs):
-            limit = max(0, min(self.k, req.params.max_tokens - len(req.output_token_ids) - 1))
+            limit = max(0, min(self.k, live[a], req.params.max_tokens - len(req.output_token_ids) - 1))
             req.draft_token_ids = [int(v) for v in dh[a][:limit]]
         for qi, a in enumerate(samp):
             self.q_store[areqs[a].request_id] = (qbuf, qi)

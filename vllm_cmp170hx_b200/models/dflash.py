@@ -121,7 +121,14 @@ class DFlashDrafter(nn.Module):
         self.hidden_norm = RMSNorm(wi.ones_plus(H, 0.05), cfg.rms_eps)
         self.layers = nn.ModuleList(DFlashLayer(H, self.dc, cfg.rms_eps, wi) for _ in range(self.dc.num_layers))
         self.norm = RMSNorm(wi.ones_plus(H, 0.05), cfg.rms_eps)
+        # confidence head: the estimated acceptance of each draft position (a verify-depth feature)
+        self.conf_head = Linear(wi.normal((1, H), default_std(H)))
         self.target = [target]  # embedding and LM head are the target's (not submodules)
+
+    def confidence(self, h: torch.Tensor) -> torch.Tensor:
+        """sigmoid of the confidence head over the mask rows' hidden states [A, k, H] -> [A, k]."""
+        A, k, H = h.shape
+        return torch.sigmoid(ops.gemm(h.reshape(A * k, H), self.conf_head.weight, out_dtype=torch.float32)).view(A, k)
 
     def context_states(self, aux: list[torch.Tensor]) -> torch.Tensor:
         """The target's auxiliary hidden states [n, H] each -> context states [n, H]."""
