@@ -90,7 +90,9 @@ def _scratch(spec, w, inp, p, cand=None):
 
 def _run(spec, w, seqs, chunks, device="cpu", candidates=None):
     """Two interleaved sequences stepped through the core in the given chunk sizes."""
-    core = DSv4AttnCore(spec, max_seqs=2, max_len=64, max_chunk=max(chunks), device=device, **w)
+    core = DSv4AttnCore(spec, num_slots=3, group_rows=4 * 64, max_step_tokens=2 * max(chunks), device=device, **w)
+    bt = torch.tensor([[3], [1]], device=device)  # one 64-row block per sequence, not in order
+    slot = torch.tensor([2, 0], device=device)
     done = [0, 0]
     outs = [[None] * len(s["kv"]) for s in seqs]
     cands = [[None] * len(s["kv"]) for s in seqs]
@@ -110,7 +112,8 @@ def _run(spec, w, seqs, chunks, device="cpu", candidates=None):
         if candidates is not None:
             cin = torch.stack([candidates[s][p] for s, p in zip(seq, pos)]).to(device)
         cout = []
-        o = core.step(seq_t.to(device), pos_t.to(device), pick("q"), pick("kv"), pick("ks"), pick("iq"), pick("iw"),
+        o = core.step(seq_t.to(device), pos_t.to(device), slot, bt, pick("q"), pick("kv"), pick("ks"), pick("iq"),
+                      pick("iw"),
                       candidates_in=cin, candidates_out=cout if spec.candidate_blocks else None)
         for i, (s, p) in enumerate(zip(seq, pos)):
             outs[s][p] = o[i].cpu()

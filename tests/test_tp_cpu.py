@@ -11,7 +11,8 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny, tiny_deepseek
+from vllm_cmp170hx_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny, tiny_deepseek,
+                                       tiny_dsv4)
 
 PROMPTS = [[(5 * i + 3 * j) % 500 for j in range(9 + 13 * i)] for i in range(3)]
 
@@ -22,7 +23,9 @@ def _cfg(tp, fmt, pp=1):
     fmt = fmt[:-3] if hc else fmt
     ep = fmt.endswith("_ep")
     fmt = fmt[:-3] if ep else fmt
-    if fmt == "deepseek_mtp":  # Marlin experts, fp8 attention projections, MTP speculative decoding
+    if fmt == "dsv4":  # DeepSeek-V4.1 attention (window + compressed groups + sinks), delayed mHC, EXL3
+        m = tiny_dsv4(layers=3, experts=4, hidden=256, vocab=512)
+    elif fmt == "deepseek_mtp":  # Marlin experts, fp8 attention projections, MTP speculative decoding
         m = tiny_deepseek(layers=2, experts=4, hidden=256, vocab=512)
         m.moe.intermediate = 256
         m.mla.num_heads = 4  # two heads per rank: q_b shards of 384 rows hold whole fp8 scale blocks
@@ -66,7 +69,7 @@ def _worker(rank, world, port, fmt, path):
     pstate.destroy()
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "exl3", "deepseek_mtp", "exl3_ep", "deepseek_mtp_ep", "exl3_hc"])
+@pytest.mark.parametrize("fmt", ["bf16", "exl3", "deepseek_mtp", "exl3_ep", "deepseek_mtp_ep", "exl3_hc", "dsv4"])
 def test_tp2_matches_tp1(fmt):
     from vllm_cmp170hx_b200.parallel import state as pstate
 

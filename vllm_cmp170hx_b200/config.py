@@ -56,6 +56,26 @@ class MLAConfig:
 
 
 @dataclass
+class DSAConfig:
+    """DeepSeek-V4.1 attention (layer type "dsa"): MQA over 512-wide rows (K = V, RoPE on the last
+    64) from a sliding window plus compressed groups chosen by an indexer; per-head sinks; the
+    output goes through grouped wo_a then row-parallel wo_b."""
+    num_heads: int = 64
+    head_dim: int = 512
+    rope_dim: int = 64
+    q_lora_rank: int = 1536
+    window: int = 128
+    compress_ratios: list[int] = field(default_factory=list)  # per dsa layer: 0 (window only), 1 or 2
+    index_n_heads: int = 32
+    index_head_dim: int = 128
+    index_topk: int = 512
+    index_rank_groups: int = 1  # score rounding groups of the indexer heads (the reference's TP)
+    o_groups: int = 8
+    o_lora_rank: int = 1024
+    rope_theta: float = 10000.0
+
+
+@dataclass
 class MoEConfig:
     num_experts: int = 256
     top_k: int = 8
@@ -81,12 +101,13 @@ class ModelConfig:
     vocab_size: int = 163840
     hidden_size: int = 2304
     num_layers: int = 48
-    layer_types: list[str] = field(default_factory=list)  # "kda" | "mla" per layer
+    layer_types: list[str] = field(default_factory=list)  # "kda" | "mla" | "dsa" per layer
     mlp_types: list[str] = field(default_factory=list)  # "dense" | "moe" per layer
     dense_intermediate: int = 12288
     kda: KDAConfig = field(default_factory=KDAConfig)
     mla: MLAConfig = field(default_factory=MLAConfig)
     moe: MoEConfig = field(default_factory=MoEConfig)
+    dsa: DSAConfig = field(default_factory=DSAConfig)
     rms_eps: float = 1e-5
     max_position: int = 1 << 20
     tie_embeddings: bool = False
@@ -124,7 +145,8 @@ class ModelConfig:
         kda = KDAConfig(**d.pop("kda", {}))
         mla = MLAConfig(**d.pop("mla", {}))
         moe = MoEConfig(**d.pop("moe", {}))
-        return ModelConfig(kda=kda, mla=mla, moe=moe, **d)
+        dsa = DSAConfig(**d.pop("dsa", {}))
+        return ModelConfig(kda=kda, mla=mla, moe=moe, dsa=dsa, **d)
 
 
 def config3() -> ModelConfig:
@@ -207,8 +229,30 @@ def tiny_deepseek(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: i
     )
 
 
+def tiny_dsv4(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: int = 512) -> ModelConfig:
+    """Small DeepSeek-V4.1-style model: compressed sparse attention layers (window + ratio 1 / 2 /
+    window-only), sqrt-softplus routing, EXL3 experts, delayed hyper-connections."""
+    ratios = [(1, 2, 0)[i % 3] for i in range(layers)]
+    return ModelConfig(
+        name="tiny-dsv4",
+        vocab_size=vocab,
+        hidden_size=hidden,
+        num_layers=layers,
+        layer_types=["dsa"] * layers,
+        mlp_types=["dense"] + ["moe"] * (layers - 1),
+        dense_intermediate=256,
+        dsa=DSAConfig(num_heads=4, q_lora_rank=128, window=16, compress_ratios=ratios, index_n_heads=4,
+                      index_topk=8, index_rank_groups=2, o_groups=2, o_lora_rank=128),
+        moe=MoEConfig(num_experts=experts, top_k=2, intermediate=256, num_shared=1, shared_intermediate=128,
+                      router="sqrt_softplus", routed_scaling=1.5, expert_format="exl3"),
+        max_position=4096,
+        hc_mult=4,
+        hc_delayed=True,
+    )
+
+
 PRESETS = {"config3": config3, "config4": config4, "config2_layer": config2_layer, "tiny": tiny,
-           "tiny_deepseek": tiny_deepseek}
+           "tiny_deepseek": tiny_deepseek, "tiny_dsv4": tiny_dsv4}
 
 
 @dataclass

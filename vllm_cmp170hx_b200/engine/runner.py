@@ -93,6 +93,14 @@ class ModelRunner:
                 per_block = max(1, n_mla) * 64 * (576 * 2 + 128 + 4)
                 if spec and not mtp:  # DFlash context keys / values (the drafter's default shape)
                     per_block += cfg.scheduler.dflash_layers * 64 * 2 * 4 * 128 * 2
+                n_dsa = len(m.dsa_layer_ids())
+                if n_dsa:  # DeepSeek-V4.1 group rows + index keys, and the per-slot rings / step scratch
+                    a = self.mcfg.dsa
+                    per_block += n_dsa * 64 * (a.head_dim * 2 + a.index_head_dim * 2)
+                    sc = cfg.scheduler
+                    k = sc.num_speculative_tokens
+                    kda_bytes += n_dsa * (self.num_slots * ((a.window + k) * a.head_dim * 2 + (k + 2) * a.head_dim * 8)
+                                          + max(sc.max_num_batched_tokens, sc.max_num_seqs) * a.head_dim * 2)
                 scratch = 6 << 30
                 avail = free * cfg.cache.gpu_memory_utilization - kda_bytes - scratch
                 nb = int(max(avail, 0) // per_block)
@@ -111,8 +119,19 @@ class ModelRunner:
         for i in kda_ids:
             self.kda_states[i] = (torch.zeros(self.num_slots, *rec_shape, dtype=torch.float32, device=self.device),
                                   torch.zeros(self.num_slots, *conv_shape, dtype=torch.bfloat16, device=self.device))
+        # DeepSeek-V4.1 attention: compressed groups paged on the token blocks, a window ring per
+        # state slot, one step's window rows of scratch
+        self.dsa_cores = {}
+        dsa_ids = m.dsa_layer_ids()
+        sc = cfg.scheduler
+        max_step = max(sc.max_num_batched_tokens, sc.max_num_seqs) * (1 + sc.num_speculative_tokens)
+        for i in dsa_ids:
+            self.dsa_cores[i] = m.layer(i).attn.make_core(self.num_slots, rows, max_step,
+                                                           sc.num_speculative_tokens, self.device)
         self.block_pool = make_block_pool(nb, 1)
-        self.slot_pool = SlotPool(self.num_slots, 1) if kda_ids else None
+        self.slot_pool = SlotPool(self.num_slots, 1) if (kda_ids or dsa_ids) else None
+        # layers that read host values inside the forward cannot be captured in decode graphs
+        self.graphs_ok = not dsa_ids
 
     # ------------------------------------------------------------------ inputs
     def _host_inputs(self, out: SchedulerOutput, pad_to: int | None = None):
@@ -190,6 +209,7 @@ class ModelRunner:
         ctx = StepContext(positions=dev["pos"], num_tokens=h["T"], slot_mapping=dev["slots"], token_seq=dev["tseq"],
                           ctx_lens=dev["ctx"], block_table=dev["bt"], max_ctx=max_ctx or h["max_ctx"],
                           cu_seqlens=dev["cu"], kda_slots=dev["kslot"], has_init=dev["hinit"],
+                          dsa_cores=self.dsa_cores,
                           mla_caches=self.mla_caches, kda_states=self.kda_states,
                           scores_buf=b.get("scores"))
         nbytes = sum(h[k].nbytes for k in ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps"))
@@ -219,7 +239,7 @@ class ModelRunner:
             return self._execute_pp(out)
         if self.spec is not None:
             return self._execute_spec(out)
-        use_graph = (not self.cfg.enforce_eager and self.device.type == "cuda" and out.decode_only
+        use_graph = (not self.cfg.enforce_eager and self.graphs_ok and self.device.type == "cuda" and out.decode_only
                      and all(s.num_draft == 0 for s in out.reqs)
                      and len(out.reqs) <= max(self.cfg.cuda_graph_batch_sizes))
         stats = StepStats(num_tokens=out.num_tokens, graph=use_graph)
@@ -528,7 +548,7 @@ class ModelRunner:
         measures the same quantity to split its graph-memory budget
         (vllm_sm80/worker/cudagraph_mem.py:202-284)."""
         kept = {}
-        if self.device.type != "cuda" or self.cfg.enforce_eager or self.st.pp_size > 1:
+        if self.device.type != "cuda" or self.cfg.enforce_eager or self.st.pp_size > 1 or not self.graphs_ok:
             return kept
         for B in sorted(self.cfg.cuda_graph_batch_sizes):
             if B in self.graphs or B > self.cfg.scheduler.max_num_seqs:

@@ -59,6 +59,8 @@ class StepContext:
     # recorded, see HybridForCausalLM.kda_recover) and the per-layer records of the step
     kda_verify: torch.Tensor | None = None
     kda_records: dict = field(default_factory=dict)
+    # DeepSeek-V4.1 attention layers: i -> DSv4AttnCore (caches; rings indexed by kda_slots)
+    dsa_cores: dict = field(default_factory=dict)
 
 
 def _fp8_proj(w: torch.Tensor):
@@ -453,7 +455,12 @@ class DecoderLayer(nn.Module):
         self.kind = cfg.layer_types[idx]
         self.input_norm = RMSNorm(wi.ones_plus(cfg.hidden_size, 0.05), cfg.rms_eps)
         self.post_norm = RMSNorm(wi.ones_plus(cfg.hidden_size, 0.05), cfg.rms_eps)
-        self.attn = (KDAAttention if self.kind == "kda" else MLAAttention)(cfg, wi, tp, tp_rank)
+        if self.kind == "dsa":
+            from .dsv4 import DSAAttention
+
+            self.attn = DSAAttention(cfg, wi, tp, tp_rank, idx)
+        else:
+            self.attn = (KDAAttention if self.kind == "kda" else MLAAttention)(cfg, wi, tp, tp_rank)
         mt = cfg.mlp_types[idx]
         if mt == "moe":
             self.mlp = MoE(cfg, wi, tp, tp_rank)
@@ -598,3 +605,10 @@ class HybridForCausalLM(nn.Module):
     def mla_layer_ids(self):
         """Sparse-MLA layers of this stage (global indices)."""
         return [i for i, t in enumerate(self.cfg.layer_types) if t == "mla" and self.layer_start <= i < self.layer_end]
+
+    def dsa_layer_ids(self):
+        """DeepSeek-V4.1 attention layers of this stage (global indices)."""
+        return [i for i, t in enumerate(self.cfg.layer_types) if t == "dsa" and self.layer_start <= i < self.layer_end]
+
+    def layer(self, idx: int) -> "DecoderLayer":
+        return self.layers[idx - self.layer_start]

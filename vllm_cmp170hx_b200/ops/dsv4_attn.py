@@ -1,12 +1,11 @@
 """DeepSeek-V4.1 attention core: window + compressed KV, indexer top-k, sparse attention with sinks.
 
-`DSv4AttnCore` holds one layer's caches for up to `max_seqs` sequences and runs a step over any
-mix of prefill chunks and decode tokens.  B200 layout: every row a query can attend -- the
-sliding-window rows and the compressed group rows -- lives in ONE bf16 pool [max_seqs * R, 512]
-(per sequence a window ring of `window + max_chunk` rows, then one row per group), so the attention
-is a single gather over pool row ids and runs on the tcgen05 block-sparse attention kernel
-(csrc/mla_attn.cu, 512-wide rows, per-head sink in the softmax denominator).  The ring is wider than
-the window by the largest chunk, so no row a query of the chunk needs is overwritten by the chunk.
+`DSv4AttnCore` holds one layer's caches and runs a step over any mix of prefill chunks and decode
+tokens.  B200 layout: every row a query can attend -- the compressed group rows (paged on the
+engine's token blocks), the sliding-window rings and this step's own window rows -- lives in ONE
+bf16 pool, so the attention is a single gather over pool row ids and runs on the tcgen05
+block-sparse attention kernel (csrc/mla_attn.cu, 512-wide rows, per-head sink in the softmax
+denominator).
 
 Rounding points and selection rules are the reference's (oracle/dsv4_attn.py states them; the
 reference's layer is vllm_sm80/models/deepseek_v41/ops/sm80_attn_core.py:783 prepare_layer and
@@ -62,95 +61,140 @@ def attend(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sink: torch.T
 
 
 class DSv4AttnCore:
-    def __init__(self, spec: DSv4AttnSpec, max_seqs: int, max_len: int, max_chunk: int, freqs: torch.Tensor,
-                 sink: torch.Tensor, comp_norm: torch.Tensor | None = None, wk: torch.Tensor | None = None,
-                 k_norm: torch.Tensor | None = None, device="cpu"):
+    """One layer's caches and step.  Pool rows: [groups | rings | step scratch]:
+
+    * groups (and index keys): one row per closed group, paged like the engine's token blocks --
+      group g of sequence s at block_table[s, g // 64] * 64 + g % 64 (g <= position, so the block is
+      always allocated);
+    * rings: `window` (+ the speculative width) rows per sequence slot, position p at row p % ring;
+    * scratch: this step's window rows in token order, which the step's queries read for positions
+      inside the step (the ring keeps earlier positions); after the attention the last `ring`
+      positions of each sequence move into its ring.
+    """
+
+    def __init__(self, spec: DSv4AttnSpec, num_slots: int, group_rows: int, max_step_tokens: int,
+                 freqs: torch.Tensor, sink: torch.Tensor, comp_norm: torch.Tensor | None = None,
+                 wk: torch.Tensor | None = None, k_norm: torch.Tensor | None = None, device="cpu",
+                 carry_rows: int = 2, ring_extra: int = 0):
         self.spec, self.device = spec, torch.device(device)
-        self.max_chunk = max_chunk
-        self.ring = spec.window + max_chunk
-        self.groups = max_len // spec.ratio if spec.ratio else 0
-        self.R = self.ring + self.groups
         d = spec.head_dim
-        self.pool = torch.zeros(max_seqs * self.R, d, dtype=torch.bfloat16, device=self.device)
-        self.idxk = torch.zeros(max_seqs, max(self.groups, 1), spec.index_dim, dtype=torch.bfloat16,
-                                device=self.device)
-        self.prev = torch.zeros(max_seqs, 2 * d, dtype=torch.float32, device=self.device)  # open ratio-2 group
+        # ring rows per slot: the window plus the positions a speculative verify step may write past
+        # the accepted ones (without them a rejected draft would evict a row the window still needs)
+        self.ring = spec.window + ring_extra
+        self.G0, self.W0 = 0, group_rows
+        self.S0 = group_rows + num_slots * self.ring
+        self.max_step = max_step_tokens
+        self.pool = torch.zeros(self.S0 + max_step_tokens, d, dtype=torch.bfloat16, device=self.device)
+        self.idxk = torch.zeros(max(group_rows, 1), spec.index_dim, dtype=torch.bfloat16, device=self.device)
+        # ratio 2: the raw fp32 [kv | score] rows of each slot's last `carry_rows` positions (a step
+        # that starts on a group's second token pools it with the row before; speculative verify steps
+        # need as many rows as their width + 1, since rejected positions are written too)
+        self.carry = max(2, carry_rows)
+        self.prev = torch.zeros(num_slots, self.carry, 2 * d, dtype=torch.float32, device=self.device)
         self.freqs = freqs.float().to(self.device)
         self.sink = sink.float().to(self.device)
         self.comp_norm, self.wk, self.k_norm = comp_norm, wk, k_norm
 
-    # ------------------------------------------------------------------ cache writes
-    def _write(self, seq: torch.Tensor, pos: torch.Tensor, kv: torch.Tensor, kv_score: torch.Tensor | None):
+    def _group_rows(self, block_table: torch.Tensor, seq: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+        return block_table[seq.long(), (g // 64).long()].long() * 64 + g.long() % 64
+
+    # ------------------------------------------------------------------ compressed groups
+    def _write_groups(self, seq, slot, pos, kv, kv_score, block_table):
         sp = self.spec
-        base = seq.long() * self.R
-        self.pool[base + pos.long() % self.ring] = ref.window_rows(kv, pos, self.freqs)
-        if not sp.ratio:
-            return
         if sp.ratio == 1:
             closes = torch.ones_like(pos, dtype=torch.bool)
             latent = ref.rms_norm(kv, self.comp_norm, sp.eps)
         else:
             closes = (pos + 1) % 2 == 0
-            # the group's first row: the previous token of this chunk, or the sequence's open row
+            # the group's first row: the previous token of this step, or the sequence's open row
             same = torch.zeros_like(closes)
             same[1:] = (seq[1:] == seq[:-1]) & (pos[1:] == pos[:-1] + 1)
-            prev = torch.where(same[:, None], torch.roll(kv_score, 1, 0), self.prev[seq.long()])
+            tslot = slot[seq.long()].long()
+            carried = self.prev[tslot, (pos - 1) % self.carry]
+            prev = torch.where(same[:, None], torch.roll(kv_score, 1, 0), carried)
             latent = ref.pool_pair(prev, kv_score, self.comp_norm, sp.eps)
-            # a sequence whose chunk ends on a group's first token keeps that row for the next step
-            last = torch.ones_like(closes)
-            last[:-1] = seq[1:] != seq[:-1]
-            keep = last & ~closes
-            self.prev[seq[keep].long()] = kv_score[keep].float()
+            # the last `carry` positions of each sequence into its carry ring (distinct rows)
+            seq_l = seq.long()
+            last_pos = torch.zeros(int(seq_l.max()) + 1, dtype=torch.long, device=pos.device)
+            last_pos.scatter_reduce_(0, seq_l, pos, reduce="amax", include_self=False)
+            keep = pos > last_pos[seq_l] - self.carry
+            self.prev[tslot[keep], pos[keep] % self.carry] = kv_score[keep].float()
         g = torch.div(pos + 1, sp.ratio, rounding_mode="floor") - 1
         gpos = pos + 1 - sp.ratio
         c = closes.nonzero().flatten()
         if c.numel() == 0:
             return
-        sc, gc = seq[c].long(), g[c].long()
-        self.pool[sc * self.R + self.ring + gc] = ref.compressed_rows(latent[c], gpos[c], self.freqs)
+        rows = self._group_rows(block_table, seq[c], g[c])
+        self.pool[self.G0 + rows] = ref.compressed_rows(latent[c], gpos[c], self.freqs)
         k = latent[c].float() @ self.wk.float().t()
-        self.idxk[sc, gc] = ref.index_key_rows(k.to(torch.bfloat16), self.k_norm, self.freqs, gpos[c], sp.eps)
+        self.idxk[rows] = ref.index_key_rows(k.to(torch.bfloat16), self.k_norm, self.freqs, gpos[c], sp.eps)
 
     # ------------------------------------------------------------------ one step
-    def step(self, seq: torch.Tensor, pos: torch.Tensor, q: torch.Tensor, kv: torch.Tensor,
-             kv_score: torch.Tensor | None = None, index_q: torch.Tensor | None = None,
-             index_w: torch.Tensor | None = None, candidates_in: torch.Tensor | None = None,
-             candidates_out: list | None = None) -> torch.Tensor:
-        """Tokens of this step (each sequence's tokens consecutive and in position order, at most
-        `max_chunk` per sequence): seq [T], pos [T], q [T, h, 512] (pre-RoPE), kv [T, 512]
-        (kv_norm(wkv(x)), pre-RoPE), kv_score [T, 1024] fp32 (ratio 2), index_q [T, H_i, 128]
-        (pre-RoPE), index_w [T, H_i] (weights_proj(x)).  Returns the wo_a input [T, h, 512]."""
+    def step(self, seq: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, block_table: torch.Tensor,
+             q: torch.Tensor, kv: torch.Tensor, kv_score: torch.Tensor | None = None,
+             index_q: torch.Tensor | None = None, index_w: torch.Tensor | None = None,
+             candidates_in: torch.Tensor | None = None, candidates_out: list | None = None) -> torch.Tensor:
+        """Tokens of this step, each sequence's tokens consecutive and in position order: seq [T]
+        (row of block_table / slot), pos [T]; slot [S] ring slot of each sequence; q [T, h, 512]
+        (pre-RoPE), kv [T, 512] (kv_norm(wkv(x)), pre-RoPE), kv_score [T, 1024] fp32 (ratio 2),
+        index_q [T, H_i, 128] (pre-RoPE), index_w [T, H_i] (weights_proj(x)).  Returns the wo_a
+        input [T, h, 512]."""
         sp = self.spec
         T = pos.shape[0]
-        self._write(seq, pos, kv, kv_score)
-        # window rows of positions [p - window + 1, p]
-        back = torch.arange(sp.window, device=pos.device)
+        if T > self.max_step:
+            raise ValueError(f"{T} tokens in a step, the scratch holds {self.max_step}")
+        dev = pos.device
+        pos = pos.long()
+        seq_l = seq.long()
+        wrows = ref.window_rows(kv, pos, self.freqs)
+        self.pool[self.S0:self.S0 + T] = wrows
+        if sp.ratio:
+            self._write_groups(seq, slot, pos, kv, kv_score, block_table)
+        # first token and position of each token's sequence within this step
+        tix = torch.arange(T, device=dev)
+        new = torch.ones(T, dtype=torch.bool, device=dev)
+        new[1:] = seq_l[1:] != seq_l[:-1]
+        first = torch.cummax(torch.where(new, tix, 0), 0).values
+        p0 = pos[first]
+        # window rows of positions [p - window + 1, p]: this step's from the scratch, earlier ones
+        # from the sequence's ring
+        back = torch.arange(sp.window, device=dev)
         wpos = pos[:, None] - back[None]
-        widx = torch.where(wpos >= 0, seq[:, None].long() * self.R + wpos % self.ring, -1)
+        in_step = wpos >= p0[:, None]
+        ring = self.W0 + slot[seq_l].long()[:, None] * self.ring + wpos % self.ring
+        scratch = self.S0 + first[:, None] + (wpos - p0[:, None])
+        widx = torch.where(wpos < 0, -1, torch.where(in_step, scratch, ring))
         idx = [widx]
         if sp.ratio:
             n_vis = torch.div(pos + 1, sp.ratio, rounding_mode="floor")
             qi = ref.index_query(index_q, pos, self.freqs)
             wi = (index_w.float() * (sp.index_dim ** -0.5 * sp.index_heads ** -0.5)).to(torch.bfloat16)
-            sel = torch.full((T, sp.index_topk), -1, dtype=torch.long, device=pos.device)
+            sel = torch.full((T, sp.index_topk), -1, dtype=torch.long, device=dev)
             cands = []
-            for s in torch.unique(seq).tolist():
-                rows = (seq == s).nonzero().flatten()
+            for s in torch.unique(seq_l).tolist():
+                rows = (seq_l == s).nonzero().flatten()
                 N = max(int(n_vis[rows].max()), 1)
-                scores = ref.index_scores(qi[rows], wi[rows], self.idxk[s, :N], n_vis[rows], sp.index_heads_per_rank)
+                gr = self._group_rows(block_table, torch.full((N,), s, device=dev), torch.arange(N, device=dev))
+                scores = ref.index_scores(qi[rows], wi[rows], self.idxk[gr], n_vis[rows], sp.index_heads_per_rank)
                 if sp.candidate_blocks and candidates_in is None:
                     cands.append((rows, ref.candidate_blocks(scores, n_vis[rows], sp.candidate_blocks,
                                                              sp.candidate_block)))
                 elif candidates_in is not None:
                     scores = ref.mask_to_candidates(scores, candidates_in[rows], sp.candidate_block)
                 top = ref.topk_canonical(scores, n_vis[rows], sp.index_topk).long()
-                sel[rows] = torch.where(top >= 0, s * self.R + self.ring + top, -1)
+                sel[rows] = torch.where(top >= 0, self.G0 + gr[top.clamp_min(0)], -1)
             if candidates_out is not None and cands:
-                out = torch.full((T, sp.candidate_blocks), -1, dtype=torch.int32, device=pos.device)
+                out = torch.full((T, sp.candidate_blocks), -1, dtype=torch.int32, device=dev)
                 for rows, c in cands:
                     out[rows] = c
                 candidates_out.append(out)
             idx.append(sel)
         qr = ref.rope(q, pos, self.freqs)
         o = attend(qr, self.pool, torch.cat(idx, 1), self.sink, sp.head_dim ** -0.5)
+        # the last `ring` positions of each sequence into its ring (distinct ring rows)
+        last_pos = torch.zeros(int(seq_l.max()) + 1, dtype=torch.long, device=dev)
+        last_pos.scatter_reduce_(0, seq_l, pos, reduce="amax", include_self=False)
+        keep = pos > last_pos[seq_l] - self.ring
+        ring_rows = self.W0 + slot[seq_l].long() * self.ring + pos % self.ring
+        self.pool[ring_rows[keep]] = wrows[keep]
         return ref.output_qdq(o, pos, self.freqs, sp.out_groups)
