@@ -23,6 +23,9 @@ def _cfg(tp, fmt, pp=1):
     fmt = fmt[:-3] if hc else fmt
     ep = fmt.endswith("_ep")
     fmt = fmt[:-3] if ep else fmt
+    method = "mtp"
+    if fmt == "exl3_dflash":  # DFlash block drafter (auxiliary hidden states cross the pipeline hop)
+        fmt, method, k = "exl3", "dflash", 2
     if fmt == "dsv4":  # DeepSeek-V4.1 attention (window + compressed groups + sinks), delayed mHC, EXL3
         m = tiny_dsv4(layers=3, experts=4, hidden=256, vocab=512)
     elif fmt == "deepseek_mtp":  # Marlin experts, fp8 attention projections, MTP speculative decoding
@@ -38,7 +41,7 @@ def _cfg(tp, fmt, pp=1):
     return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp, expert_parallel=ep,
                                                          pipeline_parallel_size=pp),
                         scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256,
-                                                  num_speculative_tokens=k),
+                                                  num_speculative_tokens=k, spec_method=method),
                         cache=CacheConfig(num_blocks=32), device="cpu", enforce_eager=True)
 
 
@@ -97,7 +100,8 @@ def _pp_worker(rank, world, port, fmt, tp, path):
     pstate.destroy()
 
 
-@pytest.mark.parametrize("fmt,tp", [("exl3", 1), ("deepseek_mtp", 1), ("deepseek_mtp", 2), ("exl3_hc", 1)])
+@pytest.mark.parametrize("fmt,tp", [("exl3", 1), ("deepseek_mtp", 1), ("deepseek_mtp", 2), ("exl3_hc", 1),
+                                    ("exl3_dflash", 1)])
 def test_pp2_matches_pp1(fmt, tp):
     """Two pipeline stages (packed p2p hops, micro-batches, token / draft broadcast from the last
     stage) generate the same tokens as one stage; deepseek_mtp adds MTP speculative decoding, exl3_hc

@@ -69,6 +69,13 @@ class ModelRunner:
         self.spec = None
         self._pending = None
         self._pp_hidden: list = []
+        if cfg.scheduler.num_speculative_tokens > 0 and cfg.scheduler.spec_method == "dflash":
+            # every stage keeps the DFlash drafter's auxiliary hidden states of its layers; they travel
+            # to the last stage with the pipeline hop
+            from ..models.dflash import DFlashConfig
+
+            dc = DFlashConfig(num_layers=cfg.scheduler.dflash_layers).resolve(cfg.model)
+            self.model.aux_layer_ids = tuple(dc.aux_layer_ids)
         if cfg.scheduler.num_speculative_tokens > 0 and self.st.is_last_pp:
             from .spec_decode import SpecDecoder
 
@@ -325,16 +332,21 @@ class ModelRunner:
                 dist.recv(buf, src=st.pp_peer(st.pp_rank - 1), group=grp)
                 res = m(None, ctx, hybrid.hc_unpack(buf, self.mcfg, h["T"]))
             else:
-                buf = torch.empty(2, h["T"], H, dtype=torch.bfloat16, device=self.device)
+                # hidden, residual and the auxiliary hidden states of earlier stages' drafter layers
+                n_aux = sum(1 for i in m.aux_layer_ids if i < m.layer_start)
+                buf = torch.empty(2 + n_aux, h["T"], H, dtype=torch.bfloat16, device=self.device)
                 dist.recv(buf, src=st.pp_peer(st.pp_rank - 1), group=grp)
                 res = m(None, ctx, (buf[0], buf[1]))
+                if m.aux_layer_ids:
+                    m.aux_hidden = list(buf[2:]) + m.aux_hidden
             if not m.last:
-                packed = hybrid.hc_pack(res, self.mcfg) if hc else torch.stack(list(res))
+                packed = hybrid.hc_pack(res, self.mcfg) if hc else torch.stack(list(res) + list(m.aux_hidden))
                 sends.append((dist.isend(packed, dst=st.pp_peer(st.pp_rank + 1), group=grp), packed))
             elif self.spec is not None:
                 rows = self._to_dev(h["sample_rows"])
                 verify.update(self._verify_mb(mb, res, rows))
-                self._pp_hidden.append((mb, res))  # the MTP head catches up over every position
+                # the drafter catches up over every position (MTP: final hidden; DFlash: aux states)
+                self._pp_hidden.append((mb, res, list(m.aux_hidden)))
             else:
                 rows = self._to_dev(h["sample_rows"])
                 toks.append(self._sample_hidden(res, rows, self._sample_temps(mb, h), self.cfg.seed))
@@ -437,9 +449,10 @@ class ModelRunner:
 
             drafts = None
             if self.spec is not None:
-                for mb, hidden in self._pp_hidden:
+                for mb, hidden, aux in self._pp_hidden:
+                    self.model.aux_hidden = aux
                     self.spec.propose(mb, hidden, self._pp_accepted(mb))
-                drafts = {s.req.request_id: list(s.req.draft_token_ids) for mb, _ in self._pp_hidden
+                drafts = {s.req.request_id: list(s.req.draft_token_ids) for mb, _, _ in self._pp_hidden
                           for s in mb.reqs}
             self._pp_hidden = []
             obj = [drafts]

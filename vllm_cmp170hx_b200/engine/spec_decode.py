@@ -84,8 +84,8 @@ class SpecDecoder:
         if self.method == "dflash":
             from ..models.dflash import DFlashConfig, DFlashDrafter
 
-            if runner.st.pp_size > 1 or cfg.model.hc_mult:
-                raise NotImplementedError("the DFlash drafter runs without pipeline stages and hyper-connections")
+            if cfg.model.hc_mult:
+                raise NotImplementedError("the DFlash drafter reads plain residual streams (no hyper-connections)")
             dc = DFlashConfig(num_layers=cfg.scheduler.dflash_layers)
             self.dflash = DFlashDrafter(cfg.model, dc, runner.model, runner.device, cfg.seed, init_mode)
             runner.model.aux_layer_ids = tuple(self.dflash.dc.aux_layer_ids)
