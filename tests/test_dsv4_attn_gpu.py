@@ -45,9 +45,9 @@ def test_core_on_cuda_matches_host(ratio):
              comp_norm=(1 + 0.1 * torch.randn(d, generator=g)).bfloat16(),
              wk=(torch.randn(128, d, generator=g) * d ** -0.5).bfloat16(),
              k_norm=(1 + 0.1 * torch.randn(128, generator=g)).bfloat16())
-    cores = {dev: DSv4AttnCore(spec, num_slots=2, group_rows=8 * 64, max_step_tokens=320, device=dev,
+    cores = {dev: DSv4AttnCore(spec, num_slots=2, group_rows=10 * 64, max_step_tokens=320, device=dev,
                                **{k: v.to(dev) for k, v in w.items()}) for dev in ("cpu", "cuda")}
-    bt = torch.tensor([[0, 2, 4, 6], [1, 3, 5, 7]])
+    bt = torch.tensor([[0, 2, 4, 6, 8], [1, 3, 5, 7, 9]])  # 300 positions: up to 300 groups at ratio 1
     n = 300
     inp = dict(q=torch.randn(2, n, 16, d, generator=g).bfloat16(), kv=torch.randn(2, n, d, generator=g).bfloat16(),
                ks=torch.randn(2, n, 2 * d, generator=g), iq=torch.randn(2, n, 8, 128, generator=g).bfloat16(),
