@@ -15,6 +15,15 @@
 //              inserts them (evicting the least recently used way of the set)
 //              and writes every requested row into a caller buffer (pinned, so
 //              the copy to the device that follows is asynchronous).
+//              `enqueue` runs the same fetch as a host function on a CUDA
+//              stream (cudaLaunchHostFunc): the step's ids are copied to
+//              pinned memory, the fetch runs when the stream reaches it, the
+//              rows' copy to the device and their dequant follow on the
+//              stream, and the host thread never waits.  A job made with
+//              `fixed_job` keeps its buffers and row count, so a lookup built
+//              from it can be captured in a CUDA graph and replayed (each
+//              replay fetches the ids of that replay).
+#include <cuda_runtime.h>
 #include <fcntl.h>
 #include <torch/extension.h>
 #include <unistd.h>
@@ -183,6 +192,10 @@ class RowCache {
     data_.resize((size_t)slots * reader_->row_bytes());
   }
 
+  ~RowCache() {
+    for (Job* j : fixed_jobs_) delete j;
+  }
+
   // Writes rows `ids` into out [n, row_bytes] (uint8, host); returns the failed-row mask.  A negative
   // id (a row the caller does not need, e.g. another rank's) is written as zeros and is not read.
   torch::Tensor fetch(const torch::Tensor& ids, torch::Tensor& out) {
@@ -190,11 +203,69 @@ class RowCache {
     TORCH_CHECK(out.scalar_type() == at::kByte && !out.is_cuda() && out.is_contiguous() && out.size(0) == ids.size(0) &&
                     out.size(1) == reader_->row_bytes(),
                 "out: host uint8 [n, row_bytes]");
-    const int64_t n = ids.size(0), rb = reader_->row_bytes();
-    const int64_t* id = ids.data_ptr<int64_t>();
-    uint8_t* o = out.data_ptr<uint8_t>();
-    auto failed = torch::zeros({n}, torch::dtype(torch::kUInt8));
-    uint8_t* f = failed.data_ptr<uint8_t>();
+    auto failed = torch::zeros({ids.size(0)}, torch::dtype(torch::kUInt8));
+    fetch_raw(ids.data_ptr<int64_t>(), ids.size(0), out.data_ptr<uint8_t>(), failed.data_ptr<uint8_t>());
+    return failed;
+  }
+
+  // ---------------------------------------------------------------- stream-ordered fetch
+  struct Job {
+    RowCache* cache;
+    const int64_t* ids;
+    int64_t n;
+    uint8_t* out;
+    uint8_t* failed;
+    bool one_shot;
+  };
+
+  static void CUDART_CB run_job(void* arg) {
+    Job* j = static_cast<Job*>(arg);
+    try {
+      j->cache->fetch_raw(j->ids, j->n, j->out, j->failed);
+    } catch (...) {  // never unwind into the driver: every row of the call fails instead
+      std::memset(j->failed, 1, (size_t)j->n);
+      ++j->cache->host_errors_;
+    }
+    if (j->one_shot) delete j;
+  }
+
+  // Queue fetch(ids[0:n]) -> out / failed (all pinned host memory, addresses as integers) as a host
+  // function on `stream`.  The buffers must stay untouched until the stream has passed the call.
+  void enqueue(int64_t stream, int64_t ids, int64_t n, int64_t out, int64_t failed) {
+    Job* j = new Job{this, reinterpret_cast<const int64_t*>(ids), n, reinterpret_cast<uint8_t*>(out),
+                     reinterpret_cast<uint8_t*>(failed), true};
+    const cudaError_t e = cudaLaunchHostFunc(reinterpret_cast<cudaStream_t>(stream), &RowCache::run_job, j);
+    if (e != cudaSuccess) {
+      delete j;
+      TORCH_CHECK(false, "RowCache.enqueue: ", cudaGetErrorString(e));
+    }
+  }
+
+  // A job with fixed buffers and row count that lives as long as the cache (for graph capture).
+  int64_t fixed_job(int64_t ids, int64_t n, int64_t out, int64_t failed) {
+    Job* j = new Job{this, reinterpret_cast<const int64_t*>(ids), n, reinterpret_cast<uint8_t*>(out),
+                     reinterpret_cast<uint8_t*>(failed), false};
+    std::lock_guard<std::mutex> g(mu_);
+    fixed_jobs_.push_back(j);
+    return (int64_t)(fixed_jobs_.size() - 1);
+  }
+
+  void enqueue_job(int64_t stream, int64_t job) {
+    Job* j;
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      TORCH_CHECK(job >= 0 && job < (int64_t)fixed_jobs_.size(), "RowCache.enqueue_job: unknown job");
+      j = fixed_jobs_[job];
+    }
+    const cudaError_t e = cudaLaunchHostFunc(reinterpret_cast<cudaStream_t>(stream), &RowCache::run_job, j);
+    TORCH_CHECK(e == cudaSuccess, "RowCache.enqueue_job: ", cudaGetErrorString(e));
+  }
+
+  int64_t host_errors() const { return host_errors_.load(); }
+
+  void fetch_raw(const int64_t* id, int64_t n, uint8_t* o, uint8_t* f) {
+    const int64_t rb = reader_->row_bytes();
+    std::memset(f, 0, (size_t)n);
     std::vector<int64_t> miss_rows;
     std::vector<int64_t> miss_idx;
     std::lock_guard<std::mutex> g(mu_);
@@ -230,7 +301,6 @@ class RowCache {
         ++misses_;
       }
     }
-    return failed;
   }
 
   std::vector<int64_t> stats() const { return {hits_, misses_}; }
@@ -263,6 +333,8 @@ class RowCache {
   uint64_t clock_ = 0;
   int64_t hits_ = 0, misses_ = 0;
   std::mutex mu_;
+  std::vector<Job*> fixed_jobs_;
+  std::atomic<int64_t> host_errors_{0};
 };
 
 void register_row_store(pybind11::module_& m) {
@@ -299,7 +371,12 @@ void register_row_store(pybind11::module_& m) {
              py::gil_scoped_release nogil;
              return c.fetch(ids, out);
            })
-      .def("stats", &RowCache::stats);
+      .def("stats", &RowCache::stats)
+      .def("enqueue", &RowCache::enqueue, py::arg("stream"), py::arg("ids"), py::arg("n"), py::arg("out"),
+           py::arg("failed"))
+      .def("fixed_job", &RowCache::fixed_job, py::arg("ids"), py::arg("n"), py::arg("out"), py::arg("failed"))
+      .def("enqueue_job", &RowCache::enqueue_job, py::arg("stream"), py::arg("job"))
+      .def("host_errors", &RowCache::host_errors);
 }
 
 }  // namespace b200

@@ -64,6 +64,8 @@ class RowTable:
         self.cache = C.RowCache(self.reader, cache_rows, ways)
         self.device = torch.device(device) if device is not None else None
         self._pinned = None
+        self._copied = None  # the last host->device copy out of the pinned buffer
+        self._st = None  # staging of the stream-ordered lookup
 
     def _host(self, n: int) -> torch.Tensor:
         if self._pinned is None or self._pinned.shape[0] < n:
@@ -74,6 +76,9 @@ class RowTable:
     def lookup(self, ids: torch.Tensor) -> torch.Tensor:
         """bf16 [n, dim] rows of `ids`; rows whose read failed are NaN."""
         ids = ids.reshape(-1).to("cpu", torch.int64)
+        if self._copied is not None:
+            self._copied.synchronize()  # the previous lookup's copy still reads the pinned rows
+            self._copied = None
         host = self._host(ids.numel())
         failed = self.cache.fetch(ids, host)
         if self.device is None or self.device.type != "cuda":
@@ -82,6 +87,47 @@ class RowTable:
             return out.to(torch.bfloat16)
         raw = host.to(self.device, non_blocking=True)
         fl = failed.to(self.device, non_blocking=True)
+        self._copied = torch.cuda.Event()
+        self._copied.record()
         out = torch.empty(ids.numel(), self.dim, dtype=torch.bfloat16, device=self.device)
         _ext.ops().dequant_rows(raw, self.dim, fl, out)
+        return out
+
+    def _staging(self, cap: int) -> dict:
+        if self._st is None or self._st["cap"] < cap:
+            if self._st is not None and self._st["jobs"]:
+                raise RuntimeError("the staging of captured lookups cannot grow; make the first lookup the largest")
+            dev = self.device
+            self._st = dict(cap=cap, jobs={},
+                            ids_h=torch.empty(cap, dtype=torch.int64, pin_memory=True),
+                            rows_h=torch.empty(cap, self.row_bytes, dtype=torch.uint8, pin_memory=True),
+                            fail_h=torch.empty(cap, dtype=torch.uint8, pin_memory=True),
+                            rows_d=torch.empty(cap, self.row_bytes, dtype=torch.uint8, device=dev),
+                            fail_d=torch.empty(cap, dtype=torch.uint8, device=dev))
+        return self._st
+
+    def lookup_async(self, ids: torch.Tensor, fixed: bool = False) -> torch.Tensor:
+        """bf16 [n, dim] rows of the device ids [n] queued on the current stream with no host wait: the
+        ids' copy to pinned memory, the cache fetch as a host function (the reference's host-function
+        readers, csrc/exl3/ple_read.cpp:179 run_queued, csrc/exl3/engram_fetch.cpp:454 execute_fixed),
+        the rows' copy to the device and the dequant.  Calls share one staging and must stay on one
+        stream.  fixed=True binds a job to this row count and the staging, so the lookup can be
+        captured in a CUDA graph (each replay fetches that replay's ids); run it once outside capture
+        first, with the largest count, so the staging exists."""
+        n = ids.numel()
+        st = self._staging(max(n, 64))
+        stream = torch.cuda.current_stream(self.device)
+        st["ids_h"][:n].copy_(ids.reshape(-1).to(torch.int64), non_blocking=True)
+        args = (st["ids_h"].data_ptr(), n, st["rows_h"].data_ptr(), st["fail_h"].data_ptr())
+        if fixed:
+            job = st["jobs"].get(n)
+            if job is None:
+                job = st["jobs"][n] = self.cache.fixed_job(*args)
+            self.cache.enqueue_job(stream.cuda_stream, job)
+        else:
+            self.cache.enqueue(stream.cuda_stream, *args)
+        st["rows_d"][:n].copy_(st["rows_h"][:n], non_blocking=True)
+        st["fail_d"][:n].copy_(st["fail_h"][:n], non_blocking=True)
+        out = torch.empty(n, self.dim, dtype=torch.bfloat16, device=self.device)
+        _ext.ops().dequant_rows(st["rows_d"][:n], self.dim, st["fail_d"][:n], out)
         return out
