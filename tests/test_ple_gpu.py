@@ -52,3 +52,44 @@ def test_ple_table_lookup_on_gpu(tmp_path):
                                2012, 4).view(37, -1)
         assert not failed.any()
         assert torch.equal(rows.cpu(), exp), step
+
+
+def test_ple_lookup_async_matches_sync_and_replays(tmp_path):
+    """The host-function PLE lookup (no host wait) equals the synchronous one, keeps failed rows
+    NaN for the caller's mask, and replays in a CUDA graph with each replay's ids."""
+    from vllm_cmp170hx_b200.storage.ple import PleTable
+
+    t = fple.random_table(heads=2, vocab=300, dim=128, bits=4, padding=6)
+    path = os.path.join(tmp_path, "p.safetensors")
+    fple.write_table(path, "p", t, 4)
+    tab = PleTable(path, "p", 100, 550, device="cuda", threads=4)  # this rank owns rows [100, 550)
+    g = torch.Generator().manual_seed(3)
+    for step in range(3):
+        ids = torch.stack([torch.randint(0, 300, (50,), generator=g), torch.randint(300, 606, (50,), generator=g)], 1)
+        flat = ids.reshape(-1)
+        exp = fple.decode_rows(t["trellis"][flat], flat, t["head_bias"], t["head_offsets"], t["head_vocab_sizes"],
+                               100, 550, 4).view(50, -1)
+        got = tab.lookup_async(ids.cuda()).cpu()
+        assert torch.equal(got, exp), step
+    tab.reader.fail_rows_for_test([101])
+    ids = torch.tensor([[101, 400], [5, 301]])
+    rows, bad = PleTable.mask_failed(tab.lookup_async(ids.cuda()), 2)
+    assert bad.cpu().tolist() == [True, False] and (rows[0] == 0).all()
+    ids_dev = torch.full((16, 2), 200, dtype=torch.int64, device="cuda")
+    tab.lookup_async(ids_dev, fixed=True)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            out = tab.lookup_async(ids_dev, fixed=True)
+    for rep in range(2):
+        ids = torch.stack([torch.randint(150, 300, (16,), generator=g), torch.randint(300, 540, (16,), generator=g)], 1)
+        ids_dev.copy_(ids)
+        graph.replay()
+        torch.cuda.synchronize()
+        flat = ids.reshape(-1)
+        exp = fple.decode_rows(t["trellis"][flat], flat, t["head_bias"], t["head_offsets"], t["head_vocab_sizes"],
+                               100, 550, 4).view(16, -1)
+        assert torch.equal(out.cpu(), exp), rep
+    del graph

@@ -108,6 +108,63 @@ class PleTable:
         out = out.reshape(T, H * self.dim).masked_fill(bad[:, None], 0)
         return out, bad
 
+    def lookup_async(self, ids: torch.Tensor, fixed: bool = False) -> torch.Tensor:
+        """Device ids [T, heads] -> bf16 [T, heads*dim] queued on the current stream with no host wait
+        (the reference's host reader enqueued on the PLE stream, vllm_sm80/models/qwen4_exp/
+        exl3_ple.py:829): the owned-id mask on the device, the ids' copy to pinned memory, the cache
+        fetch as a host function, the rows' copy and the decode.  Failed reads come back as NaN rows
+        (the caller masks them, e.g. with `mask_failed`).  fixed=True binds a job to this row count
+        (CUDA-graph capture; run once outside capture first, with the largest count).  No tensor
+        parallel sum here: the caller all-reduces the rows."""
+        T, H = ids.shape
+        n = T * H
+        flat = ids.reshape(-1).to(torch.int64)
+        offs, vocab = self.head_offsets, self.head_vocab
+        h = torch.searchsorted(offs, flat, right=True) - 1
+        hc = h.clamp_min(0)
+        own = (h >= 0) & (flat - offs[hc] < vocab[hc]) & (flat >= self.owner_lo) & (flat < self.owner_hi)
+        want = torch.where(own, flat, torch.full_like(flat, -1))
+        st = self._staging(max(n, 64))
+        stream = torch.cuda.current_stream(self.device)
+        st["ids_h"][:n].copy_(want, non_blocking=True)
+        args = (st["ids_h"].data_ptr(), n, st["rows_h"].data_ptr(), st["fail_h"].data_ptr())
+        if fixed:
+            job = st["jobs"].get(n)
+            if job is None:
+                job = st["jobs"][n] = self.cache.fixed_job(*args)
+            self.cache.enqueue_job(stream.cuda_stream, job)
+        else:
+            self.cache.enqueue(stream.cuda_stream, *args)
+        rows = st["rows_d"][:n]
+        rows.copy_(st["rows_h"][:n], non_blocking=True)
+        st["fail_d"][:n].copy_(st["fail_h"][:n], non_blocking=True)
+        out = torch.empty(n, self.dim, dtype=torch.bfloat16, device=self.device)
+        _ext.ops().ple_decode(rows.view(torch.int16), flat, self.head_bias, self.head_offsets, self.head_vocab,
+                              self.owner_lo, self.owner_hi, self.bits, st["fail_d"][:n], out)
+        return out.view(T, H * self.dim)
+
+    @staticmethod
+    def mask_failed(rows: torch.Tensor, heads: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Zero the tokens with a NaN row: (rows, failed [T]) without a host sync."""
+        T = rows.shape[0]
+        bad = rows.view(T, heads, -1)[..., 0].isnan().any(-1)
+        return rows.masked_fill(bad[:, None], 0), bad
+
+    def _staging(self, cap: int) -> dict:
+        st = getattr(self, "_st", None)
+        if st is None or st["cap"] < cap:
+            if st is not None and st["jobs"]:
+                raise RuntimeError("the staging of captured lookups cannot grow; make the first lookup the largest")
+            rb = self.layout.row_bytes
+            dev = self.device
+            st = self._st = dict(cap=cap, jobs={},
+                                 ids_h=torch.empty(cap, dtype=torch.int64, pin_memory=True),
+                                 rows_h=torch.empty(cap, rb, dtype=torch.uint8, pin_memory=True),
+                                 fail_h=torch.empty(cap, dtype=torch.uint8, pin_memory=True),
+                                 rows_d=torch.empty(cap, rb, dtype=torch.uint8, device=dev),
+                                 fail_d=torch.empty(cap, dtype=torch.uint8, device=dev))
+        return st
+
     def stats(self) -> dict:
         r = self.reader.stats()
         h = self.cache.stats()
