@@ -63,6 +63,8 @@ _declare("VLLM_B200_MOE_DETERMINISTIC_ALIGN", _bool, True, "counting-sort expert
 _declare("VLLM_B200_FAIR_PREFILL_SHORT_BYPASS", int, 0, "prompts up to this length skip the partial-prefill cap")
 _declare("VLLM_B200_ADAPTIVE_K", str, "", "adaptive draft count policy ('' off, 'by_load', 'accept')")
 _declare("VLLM_B200_ADAPTIVE_DEPTH", str, "", "per-request verify depth policy file (dspark-depth-policy/1)")
+_declare("VLLM_B200_OVERRIDE", str, "", "override sidecar manifest restoring plain tensors at source precision")
+_declare("VLLM_B200_OVERRIDE_SHA256", str, "", "pinned sha256 of the override manifest")
 # --- storage-backed embeddings ------------------------------------------------------------------
 _declare("VLLM_B200_PLE_READ_RETRIES", int, 3, "retries of a failed PLE/Engram row read (1 ms doubling backoff)")
 _declare("VLLM_B200_ROW_CACHE_GIB", float, 0.0, "host LRU cache of table rows read from storage")
@@ -83,6 +85,8 @@ _declare("VLLM_B200_HOT_SWAP", str, "", "dev: swap implementation pairs between 
 ALIASES = {
     "VLLM_SM80_ALLREDUCE": "VLLM_B200_ALLREDUCE",
     "VLLM_DSPARK_ADAPTIVE_DEPTH": "VLLM_B200_ADAPTIVE_DEPTH",
+    "VLLM_EXL3_OVERRIDE": "VLLM_B200_OVERRIDE",
+    "VLLM_EXL3_OVERRIDE_SHA256": "VLLM_B200_OVERRIDE_SHA256",
     "VLLM_SM80_LIGHT_TIMING": "VLLM_B200_LIGHT_TIMING",
     "VLLM_SM80_EXECUTION_TRACE": "VLLM_B200_EXECUTION_TRACE",
     "VLLM_SM80_SERIAL_TRACE_EXPORT": "VLLM_B200_SERIAL_TRACE_EXPORT",

@@ -41,13 +41,22 @@ class MissingTensor(KeyError):
     pass
 
 
-def open_dir(path: str) -> Mapping[str, torch.Tensor]:
-    """All tensors of the ``*.safetensors`` files of a directory, read lazily by name."""
+def open_dir(path: str, readahead: bool = False) -> Mapping[str, torch.Tensor]:
+    """All tensors of the ``*.safetensors`` files of a directory, read lazily by name.  readahead:
+    page the shards in on a background thread meanwhile.  With ``VLLM_B200_OVERRIDE`` (a sidecar
+    manifest) and ``VLLM_B200_OVERRIDE_SHA256`` set, the manifest's tensors come from its sidecar
+    (checkpoint_override.apply_override)."""
     from safetensors import safe_open
+
+    from . import envs
+    from .checkpoint_override import Readahead, apply_override
 
     handles = {}
     index = {}
-    for f in sorted(glob.glob(os.path.join(path, "*.safetensors"))):
+    files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
+    if readahead:
+        Readahead(files).__enter__()  # daemon thread; nothing waits for it
+    for f in files:
         h = safe_open(f, framework="pt")
         handles[f] = h
         for k in h.keys():
@@ -65,7 +74,11 @@ def open_dir(path: str) -> Mapping[str, torch.Tensor]:
         def __len__(self):
             return len(index)
 
-    return _Lazy()
+    lazy = _Lazy()
+    manifest = envs.get("VLLM_B200_OVERRIDE")
+    if manifest:
+        lazy, _names = apply_override(lazy, manifest, envs.get("VLLM_B200_OVERRIDE_SHA256"))
+    return lazy
 
 
 def _get(t: Mapping, name: str) -> torch.Tensor:
