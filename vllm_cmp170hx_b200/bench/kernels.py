@@ -213,20 +213,43 @@ def bench_mla_decode(a):
 
 def bench_attn(a):
     """The sparse-attention kernel alone: --tokens queries of --heads heads, each attending to --topk
-    gathered latent rows of a --ctx-row cache (random rows, so every gather is a separate line)."""
+    gathered rows of a --ctx-row cache (random rows, so every gather is a separate line).  --dim 576:
+    MLA latent + RoPE rows; 512: DeepSeek-V4.1 rows (K = V) with per-head sinks (--sink)."""
     from ..ops import mla as mla_ops
 
-    T, nh, cnt = a.tokens, a.heads, min(a.topk, a.ctx)
+    T, nh, cnt, D = a.tokens, a.heads, min(a.topk, a.ctx), a.dim
     g = torch.Generator(device="cuda").manual_seed(0)
-    q = (torch.randn(T, nh, 576, device="cuda", generator=g) * 0.3).to(torch.bfloat16)
-    cache = torch.randn(a.ctx, 576, device="cuda", generator=g).to(torch.bfloat16)
+    q = (torch.randn(T, nh, D, device="cuda", generator=g) * 0.3).to(torch.bfloat16)
+    cache = torch.randn(a.ctx, D, device="cuda", generator=g).to(torch.bfloat16)
     idx = torch.stack([torch.randperm(a.ctx, device="cuda", generator=g)[:a.topk] for _ in range(T)]).int()
     counts = torch.full((T,), cnt, dtype=torch.int32, device="cuda")
     splits = a.splits or mla_ops.pick_splits(T, nh, a.topk)
-    us = time_us(lambda: mla_ops.sparse_attention(q, cache, idx, counts, 576 ** -0.5, splits), a.iters)
-    nbytes = T * cnt * 576 * 2 + T * nh * (576 + 512) * 2
-    flops = 2.0 * T * nh * cnt * (576 + 512)
-    return _report("attn", us, nbytes, flops, tokens=T, heads=nh, count=cnt, splits=splits)
+    out = torch.empty(T, nh, 512, dtype=torch.bfloat16, device="cuda")
+    sink = torch.randn(nh, device="cuda", generator=g) if a.sink else None
+    status = _ext.status_word(q.device)
+
+    def call():
+        _ext.ops().mla_sparse_attention(q, cache, idx, counts, D ** -0.5, splits, out, None, status, sink)
+
+    us = time_us(call, a.iters)
+    nbytes = T * cnt * D * 2 + T * nh * (D + 512) * 2
+    flops = 2.0 * T * nh * cnt * (D + 512)
+    return _report("attn", us, nbytes, flops, tokens=T, heads=nh, count=cnt, splits=splits, dim=D)
+
+
+def bench_ple_decode(a):
+    """EXL3 PLE row decode: --tokens rows of --dim channels at --bits bits, 4 heads."""
+    from ..formats import ple as fple
+
+    n, dim, bits = a.tokens, a.dim, a.bits
+    t = fple.random_table(heads=4, vocab=max(n, 64), dim=dim, bits=bits)
+    rows = t["trellis"][:n].cuda()
+    ids = torch.arange(n, device="cuda")
+    args = [t[k].cuda() for k in ("head_bias", "head_offsets", "head_vocab_sizes")]
+    out = torch.empty(n, dim, dtype=torch.bfloat16, device="cuda")
+    us = time_us(lambda: _ext.ops().ple_decode(rows, ids, *args, 0, 1 << 40, bits, None, out), a.iters)
+    nbytes = rows.numel() * 2 + out.numel() * 2
+    return _report("ple_decode", us, nbytes, rows=n, dim=dim, bits=bits)
 
 
 def bench_kda_decode(a):
@@ -244,7 +267,8 @@ def bench_kda_decode(a):
 
 
 OPS = {"gemm": bench_gemm, "exl3_moe": bench_exl3_moe, "marlin_moe": bench_marlin_moe, "fp8_linear": bench_fp8_linear,
-       "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode, "attn": bench_attn}
+       "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode, "attn": bench_attn,
+       "ple_decode": bench_ple_decode}
 
 
 def main(argv=None):
@@ -261,6 +285,10 @@ def main(argv=None):
     ap.add_argument("--ep", action="store_true", help="exl3_moe: experts split whole (expert parallel)")
     ap.add_argument("--topk", type=int, default=2048, help="attn: gathered rows per query")
     ap.add_argument("--splits", type=int, default=0, help="attn: position splits (0: the launcher's choice)")
+    ap.add_argument("--dim", type=int, default=576, help="attn: row width (576 MLA, 512 DeepSeek-V4.1); "
+                                                         "ple_decode: channels")
+    ap.add_argument("--sink", action="store_true", help="attn: per-head softmax sinks")
+    ap.add_argument("--bits", type=int, default=4, help="ple_decode: bits per channel")
     ap.add_argument("--profile", action="store_true", help="print a per-kernel table of one call (torch profiler)")
     ap.add_argument("--graph", action="store_true", help="time --iters calls replayed from one CUDA graph")
     a = ap.parse_args(argv)
