@@ -266,9 +266,35 @@ def bench_kda_decode(a):
     return _report("kda_decode", us, nbytes, seqs=a.tokens, heads=H)
 
 
+def bench_mhc(a):
+    """One mHC boundary (post + Sinkhorn coefficients + collapse + RMSNorm): --tokens tokens, 4
+    streams of --dim hidden."""
+    from ..ops import mhc as mhc_ops
+
+    T, n, d = a.tokens, 4, a.dim
+    g = torch.Generator(device="cuda").manual_seed(0)
+    N = 2 * n + n * n
+    x = torch.randn(T, d, device="cuda", generator=g).bfloat16()
+    H = torch.randn(T, n, d, device="cuda", generator=g).bfloat16()
+    post = torch.rand(T, n, device="cuda", generator=g)
+    comb = torch.rand(T, n, n, device="cuda", generator=g)
+    fn = torch.randn(N, n * d, device="cuda", generator=g) * (n * d) ** -0.5
+    scale = torch.ones(3, device="cuda")
+    base = torch.zeros(N, device="cuda")
+    w = torch.ones(d, device="cuda", dtype=torch.bfloat16)
+
+    def call():
+        mhc_ops.post_pre(x, H, post, comb, fn, scale, base, w, rms_eps=1e-6, eps=1e-6, post_mult=2.0, iters=20,
+                         norm_eps=1e-6)
+
+    us = time_us(call, a.iters)
+    nbytes = T * d * 2 + 2 * T * n * d * 2 + N * n * d * 4 + T * d * 2
+    return _report("mhc", us, nbytes, tokens=T, dim=d)
+
+
 OPS = {"gemm": bench_gemm, "exl3_moe": bench_exl3_moe, "marlin_moe": bench_marlin_moe, "fp8_linear": bench_fp8_linear,
        "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode, "attn": bench_attn,
-       "ple_decode": bench_ple_decode}
+       "ple_decode": bench_ple_decode, "mhc": bench_mhc}
 
 
 def main(argv=None):
