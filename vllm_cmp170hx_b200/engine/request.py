@@ -29,7 +29,10 @@ class Status(enum.Enum):
 
     @property
     def finished(self) -> bool:
-        return self.value.startswith("finished")
+        return self in _FINISHED
+
+
+_FINISHED = frozenset(s for s in Status if s.value.startswith("finished"))
 
 
 _ids = itertools.count()
@@ -60,6 +63,20 @@ class Request:
     @property
     def all_token_ids(self) -> list[int]:
         return self.prompt_token_ids + self.output_token_ids
+
+    def token_at(self, i: int) -> int:
+        """Token i of prompt + output without building the concatenation."""
+        n = len(self.prompt_token_ids)
+        return self.prompt_token_ids[i] if i < n else self.output_token_ids[i - n]
+
+    def tokens(self, a: int, b: int) -> list[int]:
+        """Tokens [a, b) of prompt + output without building the whole concatenation."""
+        n = len(self.prompt_token_ids)
+        if b <= n:
+            return self.prompt_token_ids[a:b]
+        if a >= n:
+            return self.output_token_ids[a - n:b - n]
+        return self.prompt_token_ids[a:] + self.output_token_ids[:b - n]
 
     @property
     def num_tokens(self) -> int:

@@ -141,10 +141,58 @@ class ModelRunner:
         self.graphs_ok = not dsa_ids
 
     # ------------------------------------------------------------------ inputs
+    def _bt_row(self, r) -> np.ndarray:
+        """The request's block-table row, kept on the request and extended as blocks are appended.  A
+        preemption gives the request a new block list (the cached row holds the old list, so its
+        identity cannot be reused), which rebuilds the row."""
+        row = getattr(r, "_bt_row", None)
+        ids = r.block_ids
+        n = len(ids)
+        if row is None or r._bt_list is not ids or n < r._bt_len:
+            row = np.zeros(self.max_blocks_per_seq, dtype=np.int32)
+            row[:n] = ids
+            r._bt_row, r._bt_list, r._bt_len = row, ids, n
+        elif n > r._bt_len:
+            row[r._bt_len:n] = ids[r._bt_len:]
+            r._bt_len = n
+        return row
+
+    def _host_inputs_decode(self, out: SchedulerOutput, Sp: int):
+        """_host_inputs of a step where every request computes one token (no drafts), vectorised."""
+        reqs = out.reqs
+        S = len(reqs)
+        a = np.fromiter((s.start for s in reqs), dtype=np.int64, count=S)
+        blk = np.fromiter((s.req.block_ids[s.start // 64] for s in reqs), dtype=np.int64, count=S)
+        ids = np.zeros(Sp, dtype=np.int64)
+        ids[:S] = np.fromiter((s.req.token_at(s.start) for s in reqs), dtype=np.int64, count=S)
+        pos = np.zeros(Sp, dtype=np.int32)
+        pos[:S] = a
+        slots = np.full(Sp, -1, dtype=np.int64)
+        slots[:S] = blk * 64 + a % 64
+        tseq = np.arange(Sp, dtype=np.int32)
+        tseq[S:] = 0
+        ctx = np.ones(Sp, dtype=np.int32)
+        ctx[:S] = a + 1
+        cu = np.arange(Sp + 1, dtype=np.int32)
+        kslot = np.zeros(Sp, dtype=np.int32)
+        kslot[:S] = np.fromiter((max(s.req.kda_slot, 0) for s in reqs), dtype=np.int32, count=S)
+        hinit = np.zeros(Sp, dtype=np.int32)
+        hinit[:S] = a > 0
+        bt = np.zeros((Sp, self.max_blocks_per_seq), dtype=np.int32)
+        if S:
+            bt[:S] = np.stack([self._bt_row(s.req) for s in reqs])
+        temps = np.zeros(Sp, dtype=np.float32)
+        temps[:S] = np.fromiter((s.req.params.temperature for s in reqs), dtype=np.float32, count=S)
+        sample_rows = np.fromiter((i for i, s in enumerate(reqs) if s.sample), dtype=np.int64)
+        return dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
+                    temps=temps, sample_rows=sample_rows, max_ctx=int(a.max()) + 1 if S else 1, T=Sp, S=Sp)
+
     def _host_inputs(self, out: SchedulerOutput, pad_to: int | None = None):
         reqs = out.reqs
         S = len(reqs)
         T = out.num_tokens
+        if T == S and all(s.num_new == 1 and s.num_draft == 0 for s in reqs) and not self._check_indices:
+            return self._host_inputs_decode(out, pad_to or S)
         Sp = pad_to or S
         Tp = T + (Sp - S)  # decode padding: one token per padded sequence
         ids = np.zeros(Tp, dtype=np.int64)
@@ -162,10 +210,9 @@ class ModelRunner:
         max_ctx = 1
         for i, s in enumerate(reqs):
             r = s.req
-            toks = r.all_token_ids
             n = s.num_new
             a = s.start
-            seq_tokens = toks[a:a + n - s.num_draft] + list(r.draft_token_ids[: s.num_draft])
+            seq_tokens = r.tokens(a, a + n - s.num_draft) + list(r.draft_token_ids[: s.num_draft])
             ids[t:t + n] = seq_tokens
             p = np.arange(a, a + n, dtype=np.int32)
             pos[t:t + n] = p
@@ -177,7 +224,7 @@ class ModelRunner:
             cu[i + 1] = cu[i] + n
             kslot[i] = max(r.kda_slot, 0)
             hinit[i] = 1 if a > 0 else 0
-            bt[i, : len(r.block_ids)] = r.block_ids
+            bt[i] = self._bt_row(r)
             temps[i] = r.params.temperature
             if s.sample:
                 if s.num_draft:

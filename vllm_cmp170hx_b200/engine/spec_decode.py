@@ -220,8 +220,7 @@ class SpecDecoder:
             if s.num_draft:
                 toks = accepted.get(req.request_id, [])
             else:
-                known = req.all_token_ids
-                toks = known[s.start + 1: s.start + s.num_new + 1]
+                toks = req.tokens(s.start + 1, min(s.start + s.num_new + 1, req.num_tokens))
             m = min(len(toks), n_rows)
             if m == 0:
                 continue
@@ -326,7 +325,7 @@ class SpecDecoder:
             p = np.arange(last[a] + 1)
             cs[a, : last[a] + 1] = b[p // 64] * 64 + p % 64
         ctx_slots = r._to_dev(cs)
-        bonus = torch.tensor([q.all_token_ids[q.num_computed_tokens] for q in areqs], device=dev)
+        bonus = torch.tensor([q.token_at(q.num_computed_tokens) for q in areqs], device=dev)
         h = d(bonus, torch.tensor(last, device=dev), ctx_slots, ctx_slots >= 0, self.dcaches, self.k)
         temps_l = [q.params.temperature for q in areqs]
         temps = torch.tensor(temps_l, dtype=torch.float32, device=dev) if any(v > 0 for v in temps_l) else None
