@@ -73,9 +73,13 @@ class DeviceStepError(RuntimeError):
 
 def check_status(device: torch.device, clear: bool = True) -> None:
     """Raise DeviceStepError if a kernel on `device` reported an error (host sync)."""
-    w = status_word(device)
-    v = int(w.item())
+    raise_status(device, int(status_word(device).item()), clear)
+
+
+def raise_status(device: torch.device, v: int, clear: bool = True) -> None:
+    """Raise DeviceStepError for a status value `v` already read from `device`'s word."""
     if v:
+        w = status_word(device)
         if clear:
             w.zero_()
         names = [msg for bit, msg in ERROR_BITS.items() if v & bit]

@@ -54,6 +54,8 @@ class ModelRunner:
         self._alloc_caches()
         self.step_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.graphs: dict[int, tuple] = {}
+        self._packed: dict[int, tuple] = {}
+        self._status_h = torch.zeros(1, dtype=torch.int32, pin_memory=torch.cuda.is_available())
         self.graph_pool = None
         self.last_stats = StepStats()
         self.time_device = False  # record CUDA events around each step's device work
@@ -303,7 +305,7 @@ class ModelRunner:
                 self._capture(B)
             g, bufs, ids_out = self.graphs[B]
             h = self._host_inputs(out, pad_to=B)
-            _, _, nbytes = self._context(h, bufs, self.cfg.scheduler.max_model_len)
+            nbytes = self._stage_graph_inputs(B, h)
             ev = self._ev_start()
             g.replay()
             self._ev_end(ev)
@@ -317,6 +319,9 @@ class ModelRunner:
             tokens = self._forward_sample(dev["ids"], ctx, rows, temps_rows, self.cfg.seed)
             self._ev_end(ev)
         self.step_counter += 1
+        if self.device.type == "cuda":
+            # the status word rides on the tokens' read-back: copied first, valid once they arrive
+            self._status_h.copy_(_ext.status_word(self.device), non_blocking=True)
         host = tokens.to("cpu", non_blocking=False).tolist()
         if self._events is not None:
             stats.device_ms = self._events[0].elapsed_time(self._events[1])
@@ -325,7 +330,7 @@ class ModelRunner:
         stats.d2h_bytes = tokens.numel() * tokens.element_size()
         self.last_stats = stats
         if self.device.type == "cuda":
-            _ext.check_status(self.device)
+            _ext.raise_status(self.device, int(self._status_h[0]))
         return self._split_tokens(out, sanitize(host, self.mcfg.vocab_size))
 
     _events = None
@@ -572,16 +577,28 @@ class ModelRunner:
     def _capture(self, B: int):
         dev = self.device
         mml = self.cfg.scheduler.max_model_len
-        bufs = dict(ids=torch.zeros(B, dtype=torch.int64, device=dev), pos=torch.zeros(B, dtype=torch.int32, device=dev),
-                    slots=torch.full((B,), -1, dtype=torch.int64, device=dev),
-                    tseq=torch.arange(B, dtype=torch.int32, device=dev),
-                    ctx=torch.ones(B, dtype=torch.int32, device=dev),
-                    cu=torch.arange(B + 1, dtype=torch.int32, device=dev),
-                    kslot=torch.zeros(B, dtype=torch.int32, device=dev),
-                    hinit=torch.zeros(B, dtype=torch.int32, device=dev),
-                    bt=torch.zeros(B, self.max_blocks_per_seq, dtype=torch.int32, device=dev),
-                    temps=torch.zeros(B, dtype=torch.float32, device=dev),
-                    scores=torch.empty(B, mml, dtype=torch.float32, device=dev))
+        # the per-step inputs are views of one device buffer, filled by one copy from one pinned
+        # host buffer of the same layout (fields 16-byte aligned)
+        specs = [("ids", (B,), torch.int64), ("pos", (B,), torch.int32), ("slots", (B,), torch.int64),
+                 ("tseq", (B,), torch.int32), ("ctx", (B,), torch.int32), ("cu", (B + 1,), torch.int32),
+                 ("kslot", (B,), torch.int32), ("hinit", (B,), torch.int32),
+                 ("bt", (B, self.max_blocks_per_seq), torch.int32), ("temps", (B,), torch.float32)]
+        offs, off = {}, 0
+        for k, shape, dt in specs:
+            offs[k] = off
+            off += (math.prod(shape) * torch.empty((), dtype=dt).element_size() + 15) // 16 * 16
+        host = torch.zeros(off, dtype=torch.uint8, pin_memory=True)
+        devbuf = torch.zeros(off, dtype=torch.uint8, device=dev)
+        bufs, hviews = {}, {}
+        for k, shape, dt in specs:
+            nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+            bufs[k] = devbuf[offs[k]:offs[k] + nb].view(dt).view(shape)
+            hviews[k] = host[offs[k]:offs[k] + nb].view(dt).view(shape).numpy()
+        bufs["slots"].fill_(-1)
+        bufs["tseq"].copy_(torch.arange(B, dtype=torch.int32))
+        bufs["ctx"].fill_(1)
+        bufs["cu"].copy_(torch.arange(B + 1, dtype=torch.int32))
+        bufs["scores"] = torch.empty(B, mml, dtype=torch.float32, device=dev)
         ctx = StepContext(positions=bufs["pos"], num_tokens=B, slot_mapping=bufs["slots"], token_seq=bufs["tseq"],
                           ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
                           kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
@@ -600,6 +617,16 @@ class ModelRunner:
             ids_out = self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed)
         torch.cuda.synchronize(dev)
         self.graphs[B] = (g, bufs, ids_out)
+        self._packed[B] = (host, devbuf, hviews)
+
+    def _stage_graph_inputs(self, B: int, h: dict) -> int:
+        """Write the step's inputs into the graph's pinned host buffer and copy it to the device in one
+        transfer (the previous step's copy has completed: every step reads its tokens back)."""
+        host, devbuf, hviews = self._packed[B]
+        for k, v in hviews.items():
+            np.copyto(v, h[k])
+        devbuf.copy_(host, non_blocking=True)
+        return host.numel()
 
     def capture_graphs(self) -> dict[int, int]:
         """Capture the decode graph of every configured batch size up front and return the device
@@ -659,4 +686,5 @@ class ModelRunner:
 
     def release_graphs(self):
         self.graphs.clear()
+        self._packed.clear()
         self.graph_pool = None
