@@ -38,11 +38,11 @@ def test_stream_ordered_lookup_matches_sync(tmp_path):
     t = tables.RowTable(path, 700, 256, cache_rows=256, ways=4, threads=4, device="cuda")
     g = torch.Generator().manual_seed(5)
     for step in range(4):
-        ids = torch.randint(-1, 700, (300,), generator=g)
+        ids = torch.randint(-1, 600, (300,), generator=g)  # rows 600.. stay out of the host cache
         y = t.lookup_async(ids.cuda()).float().cpu()
         assert torch.equal(y, _ref_rows(x, ids)), step
-    t.reader.fail_rows_for_test([13])
-    ids = torch.tensor([13, 5, 699])
+    t.reader.fail_rows_for_test([650])  # never read before, so the read (and its retries) fails
+    ids = torch.tensor([650, 5, 699])
     y = t.lookup_async(ids.cuda()).float().cpu()
     assert torch.isnan(y[0]).all() and torch.equal(y[1:], _ref_rows(x, ids)[1:])
     assert t.cache.host_errors() == 0
