@@ -41,10 +41,12 @@ struct ItemIn {
 template <bool FULL>
 __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
   pdl_prologue();
-  // Persistent: CTA c runs the (sequence, head) items c, c + grid, ...  The next item's 64 KiB
-  // state is bulk-copied into the other half of a shared double buffer while this item computes,
-  // and each item's final state is written straight from registers, so state reads and writes
-  // stream at the rate of the memory system instead of one load -> compute -> store per CTA.
+  // Persistent: CTA c runs the (sequence, head) items c, c + grid, ...  An item's 64 KiB state is
+  // bulk-copied into one half of a shared double buffer and moved into registers at the item's
+  // start; the half is then free, so the copy of the item two ahead is issued into it at once and
+  // two state copies are in flight while the item computes.  Each item's final state is written
+  // straight from registers, so state reads and writes stream at the rate of the memory system
+  // instead of one load -> compute -> store per CTA.
   extern __shared__ __align__(128) float sbuf[];  // [2][D * D]
   __shared__ __align__(8) uint64_t fullb[2];
   const int tid = threadIdx.x;
@@ -77,6 +79,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
   }
   __syncthreads();
   if (tid == 0 && (int)blockIdx.x < items) prefetch(blockIdx.x, 0);
+  if (tid == 0 && (int)(blockIdx.x + gridDim.x) < items) prefetch(blockIdx.x + gridDim.x, 1);
 
   // per-thread inputs of an item's first token (FULL): this thread's pre-conv channel value
   // (q/k/v threads) or gate pre-activation (gate threads), its conv taps and window, beta, the
@@ -134,11 +137,6 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
   const bool has_init = has_init_of(seq);
   const bool verify = p.verify != nullptr && p.verify[seq] != 0 && p.rec != nullptr;
   const int buf = local & 1;
-  // the other buffer was read by the previous item (and a barrier followed): refill it
-  if (tid == 0 && item + (int)gridDim.x < items) {
-    fence_proxy_async_smem();
-    prefetch(item + gridDim.x, buf ^ 1);
-  }
   const bool has_next = item + (int)gridDim.x < items;
   const Meta next_meta = has_next ? load_meta(item + gridDim.x) : Meta{0, 0, 0, 0};
   const bool landed = mbar_wait(&fullb[buf], (local >> 1) & 1, nullptr);
@@ -159,7 +157,11 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
       st[gi][j][3] = v.w;
     }
   }
-  __syncthreads();  // every thread has its state: the buffer may be refilled next item
+  __syncthreads();  // every thread has its state in registers: the buffer is free
+  if (tid == 0 && item + 2 * (int)gridDim.x < items) {
+    fence_proxy_async_smem();  // the generic-proxy reads above before the async-proxy refill
+    prefetch(item + 2 * gridDim.x, buf);
+  }
 
   // conv window of this thread's channel (FULL mode, threads 0..383); the item's first-token
   // inputs arrived in `in` (loaded while the previous item computed)
