@@ -73,4 +73,5 @@ def test_http_endpoints(client):
     r = client.post("/v1/messages", json={"system": "be brief", "messages": [{"role": "user", "content": "hi"}],
                                           "max_tokens": 2}).json()
     assert r["type"] == "message" and r["usage"]["output_tokens"] == 2
-    assert "b200_requests_total" in client.get("/metrics").text
+    text = client.get("/metrics").text
+    assert "b200_requests_total" in text and "b200_engine_steps_total" in text

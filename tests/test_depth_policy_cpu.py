@@ -108,3 +108,20 @@ def test_greedy_spec_under_depth_policy_matches_plain(tmp_path, bias, cut):
         assert st["proposed"] == 0 and st["depth_cut"] > 0
     else:
         assert st["proposed"] > 0
+
+
+def test_metrics_lines_report_spec_stats_and_k_histogram():
+    from vllm_cmp170hx_b200.engine.llm_engine import LLMEngine, metrics_lines
+
+    pstate.set_state(pstate.ParallelState())
+    cfg = _cfg(3)
+    cfg.scheduler.adaptive_k = "by_load"
+    model = HybridForCausalLM(cfg.model, "cpu", seed=3)
+    eng = LLMEngine(cfg, model)
+    eng.add_request([5, 6, 7, 8], SamplingParams(max_tokens=6))
+    while eng.has_unfinished() if hasattr(eng, "has_unfinished") else eng.requests:
+        eng.step()
+    model.aux_layer_ids = ()
+    text = "\n".join(metrics_lines(eng))
+    assert "b200_spec_draft_tokens_total" in text and 'b200_spec_method{method="dflash"} 1' in text
+    assert "b200_adaptive_k_steps{k=" in text

@@ -135,6 +135,9 @@ def build_app(engine: AsyncEngine, tokenizer, model_name: str):
                 v = sorted(vals)
                 lines.append(f'b200_{name}{{quantile="0.5"}} {v[len(v) // 2]}')
                 lines.append(f"b200_{name}_count {len(v)}")
+        from ..engine.llm_engine import metrics_lines
+
+        lines += metrics_lines(engine.spmd.engine)
         return PlainTextResponse("\n".join(lines) + "\n")
 
     @app.post("/v1/completions")

@@ -61,6 +61,7 @@ class LLMEngine:
                                               mode if mode in ("by_load", "accept") else "by_load")
         self.requests: dict[str, Request] = {}
         self.num_steps = 0
+        self.k_hist: dict[int, int] = {}  # draft count chosen per step (adaptive k) -> steps
         self.eos_token_id: int | None = None
 
     def _diagnostics(self, st) -> None:
@@ -151,6 +152,8 @@ class LLMEngine:
                 self.adaptive_k.observe(st["proposed"] - self._k_seen[0], st["accepted"] - self._k_seen[1])
                 self._k_seen = (st["proposed"], st["accepted"])
             self.scheduler.draft_cap = self.adaptive_k.choose(len(self.scheduler.running))
+            k = self.scheduler.draft_cap
+            self.k_hist[k] = self.k_hist.get(k, 0) + 1
         out = self.scheduler.schedule()
         if not out.reqs:
             return []
@@ -170,6 +173,26 @@ class LLMEngine:
             if r.status.finished:
                 self.requests.pop(r.request_id, None)
         return res
+
+
+def metrics_lines(engine: "LLMEngine") -> list[str]:
+    """Prometheus text lines of the engine's counters: steps, speculative decoding (drafts proposed /
+    accepted, acceptance rate, drafts the verify-depth policy cut), the adaptive draft count chosen per
+    step as a histogram, and the last step's device time."""
+    lines = [f"b200_engine_steps_total {engine.num_steps}"]
+    spec = getattr(engine.runner, "spec", None)
+    if spec is not None:
+        st = spec.stats
+        lines += [f"b200_spec_draft_tokens_total {st['proposed']}", f"b200_spec_accepted_tokens_total {st['accepted']}",
+                  f"b200_spec_acceptance_rate {spec.acceptance_rate():.6f}",
+                  f"b200_spec_depth_cut_tokens_total {st.get('depth_cut', 0)}",
+                  f'b200_spec_method{{method="{spec.method}"}} 1']
+    for k in sorted(engine.k_hist):
+        lines.append(f'b200_adaptive_k_steps{{k="{k}"}} {engine.k_hist[k]}')
+    last = getattr(engine.runner, "last_stats", None)
+    if last is not None and getattr(last, "device_ms", None):
+        lines.append(f"b200_last_step_device_ms {last.device_ms:.4f}")
+    return lines
 
 
 class LLM:
