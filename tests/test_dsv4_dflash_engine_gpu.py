@@ -17,16 +17,27 @@ pytestmark = pytest.mark.gpu
 PROMPTS = [[(5 * i + 3 * j) % 500 for j in range(n)] for i, n in enumerate([9, 40, 71, 150])]
 
 
-def test_dsv4_model_generates_on_gpu():
+def test_dsv4_model_generates_on_gpu_graph_equals_eager():
+    """Decode steps of the DeepSeek-V4.1 layers run from CUDA graphs (the indexer's score width is a
+    host bound, so no step reads the device) and emit the eager path's tokens."""
     pstate.set_state(pstate.ParallelState())
     m = tiny_dsv4(layers=3)
-    cfg = EngineConfig(model=m, scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=512),
-                       cache=CacheConfig(num_blocks=40), device="cuda")
+
+    def cfg(eager):
+        return EngineConfig(model=m, scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=64,
+                                                               max_model_len=512),
+                            cache=CacheConfig(num_blocks=40), device="cuda", enforce_eager=eager)
+
     model = HybridForCausalLM(m, "cuda", seed=5)
-    outs = LLM(cfg, model).generate(PROMPTS, SamplingParams(max_tokens=6))
+    eager = LLM(cfg(True), model).generate(PROMPTS, SamplingParams(max_tokens=6))
+    llm = LLM(cfg(False), model)
+    graph = llm.generate(PROMPTS, SamplingParams(max_tokens=6))
     torch.cuda.synchronize()
-    assert all(len(o.output_token_ids) == 6 for o in outs)
-    assert all(0 <= t < m.vocab_size for o in outs for t in o.output_token_ids)
+    assert all(len(o.output_token_ids) == 6 for o in graph)
+    assert all(0 <= t < m.vocab_size for o in graph for t in o.output_token_ids)
+    assert llm.engine.runner.graphs, "no decode graph was captured"
+    assert [o.output_token_ids for o in graph] == [o.output_token_ids for o in eager]
+    llm.engine.runner.release_graphs()
 
 
 def test_dflash_spec_matches_plain_on_gpu():

@@ -139,8 +139,7 @@ class ModelRunner:
                                                            sc.num_speculative_tokens, self.device)
         self.block_pool = make_block_pool(nb, 1)
         self.slot_pool = SlotPool(self.num_slots, 1) if (kda_ids or dsa_ids) else None
-        # layers that read host values inside the forward cannot be captured in decode graphs
-        self.graphs_ok = not dsa_ids
+        self.graphs_ok = True
 
     # ------------------------------------------------------------------ inputs
     def _bt_row(self, r) -> np.ndarray:
@@ -602,7 +601,7 @@ class ModelRunner:
         ctx = StepContext(positions=bufs["pos"], num_tokens=B, slot_mapping=bufs["slots"], token_seq=bufs["tseq"],
                           ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
                           kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
-                          kda_states=self.kda_states, scores_buf=bufs["scores"])
+                          kda_states=self.kda_states, scores_buf=bufs["scores"], dsa_cores=self.dsa_cores)
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):

@@ -10,8 +10,9 @@ row-parallel wo_b (summed over the tensor-parallel group) give the layer output.
 
 Heads, sinks and wo_a groups are split over tensor-parallel ranks; the indexer is replicated (it
 is small) and rounds its head sums in the reference's rank groups (`index_rank_groups`), so every
-rank selects the same rows.  The core reads host values (per-sequence score widths), so a model
-with these layers runs its steps eagerly (no decode graphs).
+rank selects the same rows.  The indexer's score width is the step's host bound on visible groups
+(`StepContext.max_ctx`), so a step reads no device value on the host and decode steps run from CUDA
+graphs like the other layer types.
 """
 
 from __future__ import annotations
@@ -91,6 +92,7 @@ class DSAAttention(nn.Module):
         ks = self.wkv_c(x, out_dtype=torch.float32) if self.ratio == 2 else None
         iq = self.idx_q(qr).view(T, a.index_n_heads, a.index_head_dim) if self.ratio else None
         iw = self.idx_w(x) if self.ratio else None
-        o = core.step(ctx.token_seq, ctx.positions, ctx.kda_slots, ctx.block_table, q, kv, ks, iq, iw)
+        ng = max(1, ctx.max_ctx // self.ratio) if self.ratio else None  # host bound: no device read
+        o = core.step(ctx.token_seq, ctx.positions, ctx.kda_slots, ctx.block_table, q, kv, ks, iq, iw, max_groups=ng)
         y = self.wo_a(o.reshape(T, self.G, (self.H // self.G) * a.head_dim))
         return self.wo_b.forward_reduced(y)

@@ -84,13 +84,17 @@ class DSv4AttnCore:
         self.G0, self.W0 = 0, group_rows
         self.S0 = group_rows + num_slots * self.ring
         self.max_step = max_step_tokens
-        self.pool = torch.zeros(self.S0 + max_step_tokens, d, dtype=torch.bfloat16, device=self.device)
-        self.idxk = torch.zeros(max(group_rows, 1), spec.index_dim, dtype=torch.bfloat16, device=self.device)
+        # one dummy row past the scratch (pool) and past the groups (index keys): masked writes of
+        # tokens that write nothing land there, so no step needs a data-dependent shape
+        self.dummy = self.S0 + max_step_tokens
+        self.pool = torch.zeros(self.dummy + 1, d, dtype=torch.bfloat16, device=self.device)
+        self.kdummy = max(group_rows, 1)
+        self.idxk = torch.zeros(self.kdummy + 1, spec.index_dim, dtype=torch.bfloat16, device=self.device)
         # ratio 2: the raw fp32 [kv | score] rows of each slot's last `carry_rows` positions (a step
         # that starts on a group's second token pools it with the row before; speculative verify steps
         # need as many rows as their width + 1, since rejected positions are written too)
         self.carry = max(2, carry_rows)
-        self.prev = torch.zeros(num_slots, self.carry, 2 * d, dtype=torch.float32, device=self.device)
+        self.prev = torch.zeros(num_slots + 1, self.carry, 2 * d, dtype=torch.float32, device=self.device)
         self.freqs = freqs.float().to(self.device)
         self.sink = sink.float().to(self.device)
         self.comp_norm, self.wk, self.k_norm = comp_norm, wk, k_norm
@@ -113,32 +117,39 @@ class DSv4AttnCore:
             carried = self.prev[tslot, (pos - 1) % self.carry]
             prev = torch.where(same[:, None], torch.roll(kv_score, 1, 0), carried)
             latent = ref.pool_pair(prev, kv_score, self.comp_norm, sp.eps)
-            # the last `carry` positions of each sequence into its carry ring (distinct rows)
-            seq_l = seq.long()
-            last_pos = torch.zeros(int(seq_l.max()) + 1, dtype=torch.long, device=pos.device)
-            last_pos.scatter_reduce_(0, seq_l, pos, reduce="amax", include_self=False)
-            keep = pos > last_pos[seq_l] - self.carry
-            self.prev[tslot[keep], pos[keep] % self.carry] = kv_score[keep].float()
-        g = torch.div(pos + 1, sp.ratio, rounding_mode="floor") - 1
+            # the last `carry` positions of each sequence into its carry ring (distinct rows; the
+            # others into the dummy slot)
+            keep = pos > self._last_pos(seq, pos, slot.shape[0]) - self.carry
+            dslot = self.prev.shape[0] - 1
+            self.prev[torch.where(keep, tslot, dslot), torch.where(keep, pos % self.carry, 0)] = kv_score.float()
+        g = (torch.div(pos + 1, sp.ratio, rounding_mode="floor") - 1).clamp_min(0)
         gpos = pos + 1 - sp.ratio
-        c = closes.nonzero().flatten()
-        if c.numel() == 0:
-            return
-        rows = self._group_rows(block_table, seq[c], g[c])
-        self.pool[self.G0 + rows] = ref.compressed_rows(latent[c], gpos[c], self.freqs)
-        k = latent[c].float() @ self.wk.float().t()
-        self.idxk[rows] = ref.index_key_rows(k.to(torch.bfloat16), self.k_norm, self.freqs, gpos[c], sp.eps)
+        rows = self._group_rows(block_table, seq, g)
+        self.pool[torch.where(closes, self.G0 + rows, self.dummy)] = ref.compressed_rows(latent, gpos, self.freqs)
+        k = latent.float() @ self.wk.float().t()
+        self.idxk[torch.where(closes, rows, self.kdummy)] = ref.index_key_rows(k.to(torch.bfloat16), self.k_norm,
+                                                                               self.freqs, gpos, sp.eps)
+
+    @staticmethod
+    def _last_pos(seq: torch.Tensor, pos: torch.Tensor, S: int) -> torch.Tensor:
+        """Per token, the last position its sequence reaches in this step."""
+        last = torch.full((S,), -1, dtype=torch.long, device=pos.device)
+        last.scatter_reduce_(0, seq.long(), pos.long(), reduce="amax", include_self=True)
+        return last[seq.long()]
 
     # ------------------------------------------------------------------ one step
     def step(self, seq: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, block_table: torch.Tensor,
              q: torch.Tensor, kv: torch.Tensor, kv_score: torch.Tensor | None = None,
              index_q: torch.Tensor | None = None, index_w: torch.Tensor | None = None,
-             candidates_in: torch.Tensor | None = None, candidates_out: list | None = None) -> torch.Tensor:
+             candidates_in: torch.Tensor | None = None, candidates_out: list | None = None,
+             max_groups: int | None = None) -> torch.Tensor:
         """Tokens of this step, each sequence's tokens consecutive and in position order: seq [T]
         (row of block_table / slot), pos [T]; slot [S] ring slot of each sequence; q [T, h, 512]
         (pre-RoPE), kv [T, 512] (kv_norm(wkv(x)), pre-RoPE), kv_score [T, 1024] fp32 (ratio 2),
-        index_q [T, H_i, 128] (pre-RoPE), index_w [T, H_i] (weights_proj(x)).  Returns the wo_a
-        input [T, h, 512]."""
+        index_q [T, H_i, 128] (pre-RoPE), index_w [T, H_i] (weights_proj(x)); max_groups: a host
+        bound on any token's visible groups (the indexer's score width; None reads it from the
+        device).  With max_groups given the step reads no device value on the host (graph
+        capturable).  Returns the wo_a input [T, h, 512]."""
         sp = self.spec
         T = pos.shape[0]
         if T > self.max_step:
@@ -169,32 +180,30 @@ class DSv4AttnCore:
             n_vis = torch.div(pos + 1, sp.ratio, rounding_mode="floor")
             qi = ref.index_query(index_q, pos, self.freqs)
             wi = (index_w.float() * (sp.index_dim ** -0.5 * sp.index_heads ** -0.5)).to(torch.bfloat16)
-            sel = torch.full((T, sp.index_topk), -1, dtype=torch.long, device=dev)
-            cands = []
-            for s in torch.unique(seq_l).tolist():
-                rows = (seq_l == s).nonzero().flatten()
-                N = max(int(n_vis[rows].max()), 1)
-                gr = self._group_rows(block_table, torch.full((N,), s, device=dev), torch.arange(N, device=dev))
-                scores = ref.index_scores(qi[rows], wi[rows], self.idxk[gr], n_vis[rows], sp.index_heads_per_rank)
+            N = max(1, max_groups if max_groups is not None else int(n_vis.max()))
+            # every query scores the groups of its own sequence, in row chunks of bounded size
+            per_row = N * (sp.index_heads * 4 + sp.index_dim * 2 + 16)
+            rc = max(1, (256 << 20) // per_row)
+            gi = torch.arange(N, device=dev)
+            sels, cbs = [], []
+            for r0 in range(0, T, rc):
+                r = slice(r0, min(T, r0 + rc))
+                gr = block_table[seq_l[r]][:, gi // 64].long() * 64 + gi % 64  # [rows, N] group rows
+                scores = ref.index_scores_rows(qi[r], wi[r], self.idxk[gr], n_vis[r], sp.index_heads_per_rank)
                 if sp.candidate_blocks and candidates_in is None:
-                    cands.append((rows, ref.candidate_blocks(scores, n_vis[rows], sp.candidate_blocks,
-                                                             sp.candidate_block)))
+                    cbs.append(ref.candidate_blocks(scores, n_vis[r], sp.candidate_blocks, sp.candidate_block))
                 elif candidates_in is not None:
-                    scores = ref.mask_to_candidates(scores, candidates_in[rows], sp.candidate_block)
-                top = ref.topk_canonical(scores, n_vis[rows], sp.index_topk).long()
-                sel[rows] = torch.where(top >= 0, self.G0 + gr[top.clamp_min(0)], -1)
-            if candidates_out is not None and cands:
-                out = torch.full((T, sp.candidate_blocks), -1, dtype=torch.int32, device=dev)
-                for rows, c in cands:
-                    out[rows] = c
-                candidates_out.append(out)
-            idx.append(sel)
+                    scores = ref.mask_to_candidates(scores, candidates_in[r], sp.candidate_block)
+                top = ref.topk_canonical(scores, n_vis[r], sp.index_topk).long()
+                sels.append(torch.where(top >= 0, self.G0 + gr.gather(1, top.clamp_min(0)), -1))
+            if candidates_out is not None and cbs:
+                candidates_out.append(torch.cat(cbs))
+            idx.append(torch.cat(sels))
         qr = ref.rope(q, pos, self.freqs)
         o = attend(qr, self.pool, torch.cat(idx, 1), self.sink, sp.head_dim ** -0.5)
-        # the last `ring` positions of each sequence into its ring (distinct ring rows)
-        last_pos = torch.zeros(int(seq_l.max()) + 1, dtype=torch.long, device=dev)
-        last_pos.scatter_reduce_(0, seq_l, pos, reduce="amax", include_self=False)
-        keep = pos > last_pos[seq_l] - self.ring
+        # the last `ring` positions of each sequence into its ring (distinct ring rows; the others
+        # into the dummy row)
+        keep = pos > self._last_pos(seq_l, pos, slot.shape[0]) - self.ring
         ring_rows = self.W0 + slot[seq_l].long() * self.ring + pos % self.ring
-        self.pool[ring_rows[keep]] = wrows[keep]
+        self.pool[torch.where(keep, ring_rows, self.dummy)] = wrows
         return ref.output_qdq(o, pos, self.freqs, sp.out_groups)

@@ -137,8 +137,14 @@ def index_query(q: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor) -
 def index_scores(q: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_vis: torch.Tensor,
                  heads_per_rank: int) -> torch.Tensor:
     """q [n, H, D] bf16, w [n, H] bf16, keys [N, D] -> [n, N] fp32 (bf16 values), -inf past n_vis."""
+    return index_scores_rows(q, w, keys.unsqueeze(0).expand(q.shape[0], -1, -1), n_vis, heads_per_rank)
+
+
+def index_scores_rows(q: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_vis: torch.Tensor,
+                      heads_per_rank: int) -> torch.Tensor:
+    """index_scores with each query's own keys [n, N, D] (queries of different sequences)."""
     bf = torch.bfloat16
-    s = torch.einsum("nhd,kd->nhk", q.float(), keys.float()).to(bf).float().clamp_min(0)
+    s = torch.einsum("nhd,nkd->nhk", q.float(), keys.float()).to(bf).float().clamp_min(0)
     s = (s * w.float().unsqueeze(-1)).to(bf).float()
     total = None
     for r0 in range(0, s.shape[1], heads_per_rank):
@@ -147,7 +153,7 @@ def index_scores(q: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_vis: to
             part = part + s[:, h]
         part = part.to(bf).float()
         total = part if total is None else (total + part).to(bf).float()
-    cols = torch.arange(keys.shape[0], device=q.device)
+    cols = torch.arange(keys.shape[1], device=q.device)
     return torch.where(cols[None] < n_vis[:, None], total, float("-inf"))
 
 
