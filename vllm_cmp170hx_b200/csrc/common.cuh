@@ -8,6 +8,7 @@
 // that runs out records an error code in a device word the host reads, and
 // the caller unwinds (it never traps).
 #pragma once
+#include <cstdlib>
 #include <utility>
 
 #include <cuda.h>
@@ -101,6 +102,17 @@ B200_DEVICE void pdl_prologue() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Whether launches may overlap their predecessor (programmatic dependent launch).  VLLM_B200_NO_PDL=1
+// turns it off for diagnosis: a profiler then charges each kernel its own time only, not the time it
+// spent launched early and waiting for its predecessor.  griddepcontrol.wait returns at once then.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("VLLM_B200_NO_PDL");
+    return !(v != nullptr && v[0] == '1');
+  }();
+  return on;
+}
+
 template <typename... Params, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                               Args&&... args) {
@@ -111,7 +123,7 @@ inline cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, si
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);

@@ -740,7 +740,7 @@ cudaError_t launch_csk(const void* A, int64_t lda, int rows_a, const void* B, in
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);

@@ -64,6 +64,7 @@ _declare("VLLM_B200_FAIR_PREFILL_SHORT_BYPASS", int, 0, "prompts up to this leng
 _declare("VLLM_B200_ADAPTIVE_K", str, "", "adaptive draft count policy ('' off, 'by_load', 'accept')")
 _declare("VLLM_B200_ADAPTIVE_DEPTH", str, "", "per-request verify depth policy file (dspark-depth-policy/1)")
 _declare("VLLM_B200_OVERRIDE", str, "", "override sidecar manifest restoring plain tensors at source precision")
+_declare("VLLM_B200_NO_PDL", bool, False, "launch kernels without programmatic dependent launch (profiling: each kernel charged its own time)")
 _declare("VLLM_B200_OVERRIDE_SHA256", str, "", "pinned sha256 of the override manifest")
 # --- storage-backed embeddings ------------------------------------------------------------------
 _declare("VLLM_B200_PLE_READ_RETRIES", int, 3, "retries of a failed PLE/Engram row read (1 ms doubling backoff)")
