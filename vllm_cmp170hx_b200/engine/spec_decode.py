@@ -319,12 +319,12 @@ class SpecDecoder:
         A = len(areqs)
         last = [q.num_computed_tokens - 1 for q in areqs]
         C = max(last) + 1
-        cs = np.full((A, C), -1, dtype=np.int64)
-        for a, q in enumerate(areqs):
-            b = np.asarray(q.block_ids, dtype=np.int64)
-            p = np.arange(last[a] + 1)
-            cs[a, : last[a] + 1] = b[p // 64] * 64 + p % 64
-        ctx_slots = r._to_dev(cs)
+        # context slots from the block-table rows on the device (no per-position host work)
+        bt = r._to_dev(np.stack([r._bt_row(q) for q in areqs])).long()
+        p = torch.arange(C, device=dev)
+        lt = torch.tensor(last, device=dev)
+        cs = bt[:, (p // 64).clamp(max=bt.shape[1] - 1)] * 64 + p % 64
+        ctx_slots = torch.where(p[None] <= lt[:, None], cs, -1)
         bonus = torch.tensor([q.token_at(q.num_computed_tokens) for q in areqs], device=dev)
         h = d(bonus, torch.tensor(last, device=dev), ctx_slots, ctx_slots >= 0, self.dcaches, self.k)
         temps_l = [q.params.temperature for q in areqs]
