@@ -39,7 +39,7 @@ def test_topk(mode):
     assert torch.allclose(w.cpu(), w_r, rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("T,E,k", [(4, 16, 4), (64, 32, 8), (300, 8, 2)])
+@pytest.mark.parametrize("T,E,k", [(4, 16, 4), (64, 32, 8), (300, 8, 2), (512, 16, 8), (1024, 8, 4)])
 def test_exl3_moe(T, E, k):
     g = torch.Generator().manual_seed(T + E)
     H, I = 256, 384
