@@ -125,3 +125,41 @@ def test_metrics_lines_report_spec_stats_and_k_histogram():
     text = "\n".join(metrics_lines(eng))
     assert "b200_spec_draft_tokens_total" in text and 'b200_spec_method{method="dflash"} 1' in text
     assert "b200_adaptive_k_steps{k=" in text
+
+
+def _stats_worker(rank, world, port, path):
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(9)
+        full = torch.randn(5, 1000, generator=g) * 4
+        shard = full[:, rank * 500:(rank + 1) * 500]
+
+        def ar(x, op):
+            dist.all_reduce(x, op=op)
+            return x
+
+        st = logit_stats(shard, ar)
+        if rank == 0:
+            torch.save((st, logit_stats(full)), path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_logit_stats_over_vocab_shards(tmp_path):
+    """Top-1 probability and entropy from two vocab shards (max, normaliser and sum p*logit
+    all-reduced) equal the full-vocabulary values."""
+    import os
+
+    import torch.multiprocessing as mp
+
+    path = str(tmp_path / "st.pt")
+    mp.start_processes(_stats_worker, args=(2, 29900 + os.getpid() % 90, path), nprocs=2, join=True,
+                       start_method="spawn")
+    sharded, full = torch.load(path)
+    assert torch.allclose(sharded, full, rtol=1e-5, atol=1e-6)

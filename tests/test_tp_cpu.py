@@ -101,7 +101,7 @@ def _pp_worker(rank, world, port, fmt, tp, path):
 
 
 @pytest.mark.parametrize("fmt,tp", [("exl3", 1), ("deepseek_mtp", 1), ("deepseek_mtp", 2), ("exl3_hc", 1),
-                                    ("exl3_dflash", 1)])
+                                    ("exl3_dflash", 1), ("dsv4", 1)])
 def test_pp2_matches_pp1(fmt, tp):
     """Two pipeline stages (packed p2p hops, micro-batches, token / draft broadcast from the last
     stage) generate the same tokens as one stage; deepseek_mtp adds MTP speculative decoding, exl3_hc
