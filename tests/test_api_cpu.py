@@ -75,3 +75,15 @@ def test_http_endpoints(client):
     assert r["type"] == "message" and r["usage"]["output_tokens"] == 2
     text = client.get("/metrics").text
     assert "b200_requests_total" in text and "b200_engine_steps_total" in text
+
+
+def test_server_command_line_reaches_engine_config():
+    from vllm_cmp170hx_b200.api.server import engine_config, parse_args
+
+    args = parse_args(["--model", "tiny", "--device", "cpu", "--num-speculative-tokens", "3", "--spec-method", "dflash",
+                       "--dflash-layers", "2", "--depth-policy", "/tmp/p.json", "--adaptive-k", "accept",
+                       "--max-num-seqs", "8"])
+    cfg = engine_config(args)
+    sc = cfg.scheduler
+    assert (sc.num_speculative_tokens, sc.spec_method, sc.dflash_layers, sc.depth_policy, sc.adaptive_k,
+            sc.max_num_seqs) == (3, "dflash", 2, "/tmp/p.json", "accept", 8)

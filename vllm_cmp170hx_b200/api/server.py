@@ -236,7 +236,7 @@ def build_app(engine: AsyncEngine, tokenizer, model_name: str):
     return app
 
 
-def main(argv=None):
+def parse_args(argv=None) -> argparse.Namespace:
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="tiny")
     ap.add_argument("--tokenizer", default=None)
@@ -251,18 +251,23 @@ def main(argv=None):
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--pp", type=int, default=1, help="pipeline-parallel stages")
     ap.add_argument("--enable-expert-parallel", action="store_true", help="routed experts split whole over TP")
-    ap.add_argument("--num-speculative-tokens", type=int, default=0, help="MTP draft tokens per step")
+    ap.add_argument("--num-speculative-tokens", type=int, default=0, help="draft tokens per step")
+    ap.add_argument("--spec-method", choices=["mtp", "dflash"], default="mtp", help="drafter")
+    ap.add_argument("--dflash-layers", type=int, default=1, help="DFlash drafter depth")
+    ap.add_argument("--depth-policy", default="", help="dspark-depth-policy/1 file: per-request verify depth")
+    ap.add_argument("--adaptive-k", default="", choices=["", "by_load", "accept"], help="adaptive draft count")
     ap.add_argument("--enforce-eager", action="store_true", help="no CUDA graphs")
     ap.add_argument("--nccl-collectives", action="store_true", help="TP collectives on NCCL (baseline path)")
     ap.add_argument("--no-warmup", action="store_true")
-    args = ap.parse_args(argv)
+    return ap.parse_args(argv)
 
-    from ..parallel import state as pstate
+
+def engine_config(args: argparse.Namespace) -> EngineConfig:
+    """The engine configuration the server's command line describes."""
     from ..registry import resolve
 
-    st = pstate.init(tp_size=args.tp, pp_size=args.pp, device=args.device)
     mcfg, _ckpt = resolve(args.model)
-    cfg = EngineConfig(model=mcfg,
+    return EngineConfig(model=mcfg,
                        parallel=ParallelConfig(tensor_parallel_size=args.tp, pipeline_parallel_size=args.pp,
                                                expert_parallel=args.enable_expert_parallel,
                                                fused_comm=not args.nccl_collectives),
@@ -271,8 +276,19 @@ def main(argv=None):
                                                  max_model_len=args.max_model_len,
                                                  prefill_chunk_with_decodes=args.prefill_chunk_with_decodes,
                                                  max_num_partial_prefills=args.max_num_partial_prefills,
-                                                 num_speculative_tokens=args.num_speculative_tokens),
+                                                 num_speculative_tokens=args.num_speculative_tokens,
+                                                 spec_method=args.spec_method, dflash_layers=args.dflash_layers,
+                                                 depth_policy=args.depth_policy, adaptive_k=args.adaptive_k),
                        cache=CacheConfig(), device=args.device, enforce_eager=args.enforce_eager)
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    from ..parallel import state as pstate
+
+    st = pstate.init(tp_size=args.tp, pp_size=args.pp, device=args.device)
+    cfg = engine_config(args)
+    mcfg = cfg.model
     engine = LLMEngine(cfg)
     if st.tp_size > 1 and not args.nccl_collectives:
         from ..parallel import symm
