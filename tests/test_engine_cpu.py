@@ -75,3 +75,38 @@ def test_warmup_leaves_pools_free(model):
     assert eng.runner.block_pool.num_free() == free
     out = eng.step()  # nothing scheduled
     assert out == [] and not eng.has_unfinished()
+
+
+def test_decode_step_inputs_fast_path_equals_general_path():
+    """The vectorised decode-step input builder gives the general builder's arrays (with padding)."""
+    import numpy as np
+
+    from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, SchedulerConfig, tiny
+    from vllm_cmp170hx_b200.engine.llm_engine import LLMEngine
+    from vllm_cmp170hx_b200.engine.request import SamplingParams
+    from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    cfg = EngineConfig(model=tiny(layers=2, experts=4, hidden=256),
+                       scheduler=SchedulerConfig(max_num_seqs=8, max_num_batched_tokens=512, max_model_len=512),
+                       cache=CacheConfig(num_blocks=64), device="cpu", enforce_eager=True)
+    eng = LLMEngine(cfg, HybridForCausalLM(cfg.model, "cpu", seed=0))
+    for i, n in enumerate([5, 70, 130]):
+        eng.add_request([(3 * i + j) % 400 + 1 for j in range(n)],
+                        SamplingParams(max_tokens=20, temperature=0.5 * (i % 2)))
+    for _ in range(3):
+        eng.step()
+    out = eng.scheduler.schedule()
+    r = eng.runner
+    assert out.decode_only and all(s.num_new == 1 for s in out.reqs)
+    for pad in (None, 8):
+        fast = r._host_inputs(out, pad_to=pad)
+        r._check_indices = True  # forces the general builder
+        try:
+            gen = r._host_inputs(out, pad_to=pad)
+        finally:
+            r._check_indices = False
+        for k in ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps", "sample_rows"):
+            assert np.array_equal(fast[k], gen[k]), (pad, k, fast[k], gen[k])
+        assert (fast["max_ctx"], fast["T"], fast["S"]) == (gen["max_ctx"], gen["T"], gen["S"])
