@@ -112,7 +112,8 @@ def _run(spec, w, seqs, chunks, device="cpu", candidates=None):
         if candidates is not None:
             cin = torch.stack([candidates[s][p] for s, p in zip(seq, pos)]).to(device)
         cout = []
-        o = core.step(seq_t.to(device), pos_t.to(device), slot, bt, pick("q"), pick("kv"), pick("ks"), pick("iq"),
+        ks = pick("ks") if spec.ratio == 2 else None  # ratio 1 compresses the attention's kv row here
+        o = core.step(seq_t.to(device), pos_t.to(device), slot, bt, pick("q"), pick("kv"), ks, pick("iq"),
                       pick("iw"),
                       candidates_in=cin, candidates_out=cout if spec.candidate_blocks else None)
         for i, (s, p) in enumerate(zip(seq, pos)):

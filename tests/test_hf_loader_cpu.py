@@ -10,13 +10,17 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny, tiny_deepseek
+from vllm_cmp170hx_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny, tiny_deepseek,
+                                       tiny_dsv4)
 
 PROMPTS = [[(7 * i + 3 * j) % 500 for j in range(6 + 11 * i)] for i in range(3)]
 
 
 def _cfg(kind, tp=1):
-    if kind == "deepseek":
+    if kind == "dsv4":
+        m = tiny_dsv4(layers=3, experts=4, hidden=256, vocab=512)
+        m.moe.expert_format = "bf16"
+    elif kind == "deepseek":
         m = tiny_deepseek(layers=2, experts=4, hidden=256, vocab=512)
         m.mla.num_heads = 4
         m.moe.expert_format = "bf16"
@@ -36,7 +40,7 @@ def _gen(cfg, model):
     return [o.output_token_ids for o in LLM(cfg, model).generate(PROMPTS, SamplingParams(max_tokens=4))]
 
 
-@pytest.mark.parametrize("kind", ["hybrid", "deepseek"])
+@pytest.mark.parametrize("kind", ["hybrid", "deepseek", "dsv4"])
 def test_export_then_load_by_upstream_names(kind, tmp_path):
     from safetensors.torch import save_file
 
@@ -49,7 +53,11 @@ def test_export_then_load_by_upstream_names(kind, tmp_path):
     src = HybridForCausalLM(cfg.model, "cpu", seed=1)
     ref = _gen(cfg, src)
     tensors = hf_loader.export_hf(src)
-    assert "model.layers.0.self_attn." + ("q_proj.weight" if kind == "hybrid" else "q_a_proj.weight") in tensors
+    first = {"hybrid": "self_attn.q_proj.weight", "deepseek": "self_attn.q_a_proj.weight", "dsv4": "attn.wq_a.weight"}
+    assert "model.layers.0." + first[kind] in tensors
+    if kind == "dsv4":
+        assert "model.layers.0.hc_attn_fn" in tensors and "model.hc_head_fn" in tensors
+        assert "model.layers.1.attn.compressor.wgate.weight" in tensors  # the ratio-2 layer
     save_file({k: v.contiguous() for k, v in tensors.items()}, str(tmp_path / "model.safetensors"))
     dst = HybridForCausalLM(cfg.model, "cpu", seed=2)
     assert _gen(cfg, dst) != ref
@@ -77,7 +85,7 @@ def _worker(rank, world, port, path, kind, out):
     pstate.destroy()
 
 
-@pytest.mark.parametrize("kind", ["hybrid", "deepseek"])
+@pytest.mark.parametrize("kind", ["hybrid", "deepseek", "dsv4"])
 def test_tp2_load_matches_tp1(kind, tmp_path):
     from safetensors.torch import save_file
 

@@ -158,6 +158,39 @@ def _load_mla(a, t, p, tp, r):
         _set(a.idx_k_ln_b, _get(t, p + "indexer.k_norm.bias"))
 
 
+def _load_dsa(a, t, p, tp, r):
+    """DeepSeek-V4.1 attention under `attn.` (the reference's module names, models/deepseek_v41/
+    sm80_attention.py:197-252): heads of wq_b and attn_sink and the wo_a groups cut by rank, wo_b by
+    its input columns; the compressor and the indexer replicated."""
+    _set_linear(a.wq_a, _dense(t, p + "wq_a"))
+    _set(a.q_norm.weight, _get(t, p + "q_norm.weight"))
+    _set_linear(a.wq_b, _rows(_dense(t, p + "wq_b"), tp, r))
+    _set_linear(a.wkv, _dense(t, p + "wkv"))
+    _set(a.kv_norm.weight, _get(t, p + "kv_norm.weight"))
+    _set(a.sink, _rows(_get(t, p + "attn_sink").float(), tp, r))
+    G, og, ig = a.wo_a.weight.shape
+    _set(a.wo_a.weight, _rows(_dense(t, p + "wo_a").view(G * tp, og, ig), tp, r))
+    _set_linear(a.wo_b, _cols(_dense(t, p + "wo_b"), tp, r))
+    if a.ratio:
+        _set(a.comp_norm, _get(t, p + "compressor.norm.weight"))
+        w = _dense(t, p + "compressor.wkv")
+        if a.ratio == 2:
+            w = torch.cat([w, _dense(t, p + "compressor.wgate")], 0)
+        _set_linear(a.wkv_c, w)
+        _set_linear(a.idx_q, _dense(t, p + "indexer.wq_b"))
+        _set_linear(a.idx_w, _dense(t, p + "indexer.weights_proj"))
+        _set(a.wk, _dense(t, p + "indexer.wk"))
+        _set(a.k_norm, _get(t, p + "indexer.k_norm.weight"))
+
+
+def _load_hc(hc, t, p):
+    """One mHC boundary: `{p}_fn`, `{p}_scale`, `{p}_base` (the reference's hc_attn_* / hc_ffn_*
+    names, models/deepseek_v41/sm80_model.py:159-161)."""
+    _set(hc.fn, _get(t, p + "_fn"))
+    _set(hc.scale, _get(t, p + "_scale"))
+    _set(hc.base, _get(t, p + "_base"))
+
+
 def _load_dense_mlp(mlp, t, p, tp, r):
     g, u = (_rows(_dense(t, p + n), tp, r) for n in ("gate_proj", "up_proj"))
     _set_linear(mlp.gate_up, torch.cat([g, u], 0))
@@ -234,11 +267,20 @@ def load_hf(model, tensors: Mapping[str, torch.Tensor] | str) -> None:
         _set(model.norm.weight, _get(t, "model.norm.weight"))
     if model.lm_head is not None:
         _set_linear(model.lm_head, _rows(_dense(t, "lm_head"), tp, r))
+    if getattr(model, "hc_head", None) is not None:
+        _load_hc(model.hc_head, t, "model.hc_head")
     for layer in model.layers:
         p = f"model.layers.{layer.idx}."
         _set(layer.input_norm.weight, _get(t, p + "input_layernorm.weight"))
         _set(layer.post_norm.weight, _get(t, p + "post_attention_layernorm.weight"))
-        (_load_kda if layer.kind == "kda" else _load_mla)(layer.attn, t, p + "self_attn.", tp, r)
+        if layer.kind == "dsa":
+            _load_dsa(layer.attn, t, p + "attn.", tp, r)
+        else:
+            (_load_kda if layer.kind == "kda" else _load_mla)(layer.attn, t, p + "self_attn.", tp, r)
+        if getattr(layer, "hc_attn", None) is not None:
+            _load_hc(layer.hc_attn, t, p + "hc_attn")
+            if layer.hc_mlp is not None:
+                _load_hc(layer.hc_mlp, t, p + "hc_ffn")
         if layer.mlp is None:
             continue
         if hasattr(layer.mlp, "gate_up"):
@@ -274,6 +316,10 @@ def export_hf(model) -> dict[str, torch.Tensor]:
             out[name + ".weight"] = lin.weight.detach()
 
     out["model.embed_tokens.weight"] = model.embed.detach()
+    if getattr(model, "hc_head", None) is not None:
+        h = model.hc_head
+        out["model.hc_head_fn"], out["model.hc_head_scale"], out["model.hc_head_base"] = (
+            h.fn.detach(), h.scale.detach(), h.base.detach())
     out["model.norm.weight"] = model.norm.weight.detach()
     out["lm_head.weight"] = dense(model.lm_head)
     for layer in model.layers:
@@ -282,7 +328,33 @@ def export_hf(model) -> dict[str, torch.Tensor]:
         out[p + "post_attention_layernorm.weight"] = layer.post_norm.weight.detach()
         a = layer.attn
         q = p + "self_attn."
-        if layer.kind == "kda":
+        for hc, n in ((getattr(layer, "hc_attn", None), "hc_attn"), (getattr(layer, "hc_mlp", None), "hc_ffn")):
+            if hc is not None:
+                out[p + n + "_fn"], out[p + n + "_scale"], out[p + n + "_base"] = (
+                    hc.fn.detach(), hc.scale.detach(), hc.base.detach())
+        if layer.kind == "dsa":
+            q = p + "attn."
+            out[q + "wq_a.weight"] = dense(a.wq_a)
+            out[q + "q_norm.weight"] = a.q_norm.weight.detach()
+            out[q + "wq_b.weight"] = dense(a.wq_b)
+            out[q + "wkv.weight"] = dense(a.wkv)
+            out[q + "kv_norm.weight"] = a.kv_norm.weight.detach()
+            out[q + "attn_sink"] = a.sink.detach()
+            out[q + "wo_a.weight"] = a.wo_a.weight.detach().reshape(-1, a.wo_a.weight.shape[-1])
+            out[q + "wo_b.weight"] = dense(a.wo_b)
+            if a.ratio:
+                out[q + "compressor.norm.weight"] = a.comp_norm.detach()
+                w = dense(a.wkv_c)
+                if a.ratio == 2:
+                    out[q + "compressor.wkv.weight"], out[q + "compressor.wgate.weight"] = (
+                        x.contiguous() for x in w.chunk(2, 0))
+                else:
+                    out[q + "compressor.wkv.weight"] = w
+                out[q + "indexer.wq_b.weight"] = dense(a.idx_q)
+                out[q + "indexer.weights_proj.weight"] = dense(a.idx_w)
+                out[q + "indexer.wk.weight"] = a.wk.detach()
+                out[q + "indexer.k_norm.weight"] = a.k_norm.detach()
+        elif layer.kind == "kda":
             H, D = a.H, a.D
             w = dense(a.in_proj)
             s = [H * D, H * D, H * D, D, D, H]

@@ -59,8 +59,8 @@ class DSAAttention(nn.Module):
         self.comp_norm = self.wk = self.k_norm = self.wkv_c = self.idx_q = self.idx_w = None
         if self.ratio:
             self.comp_norm = nn.Parameter(wi.ones_plus(d, 0.05), requires_grad=False)
-            if self.ratio == 2:
-                self.wkv_c = Linear(wi.normal((2 * d, hid), sd))  # compressor [kv | gate score]
+            # the compressor's own projection: [kv | gate score] (ratio 2) or kv (ratio 1)
+            self.wkv_c = Linear(wi.normal(((2 if self.ratio == 2 else 1) * d, hid), sd))
             self.idx_q = Linear(wi.normal((a.index_n_heads * a.index_head_dim, ql), default_std(ql)))
             self.idx_w = Linear(wi.normal((a.index_n_heads, hid), sd))
             self.wk = nn.Parameter(wi.normal((a.index_head_dim, d), default_std(d)), requires_grad=False)
@@ -89,7 +89,11 @@ class DSAAttention(nn.Module):
         qr = self.q_norm(self.wq_a(x))
         q = self.wq_b(qr).view(T, self.H, a.head_dim)
         kv = self.kv_norm(self.wkv(x))
-        ks = self.wkv_c(x, out_dtype=torch.float32) if self.ratio == 2 else None
+        ks = None
+        if self.ratio == 2:
+            ks = self.wkv_c(x, out_dtype=torch.float32)
+        elif self.ratio == 1:
+            ks = self.wkv_c(x)  # bf16 row, normalised by the core
         iq = self.idx_q(qr).view(T, a.index_n_heads, a.index_head_dim) if self.ratio else None
         iw = self.idx_w(x) if self.ratio else None
         ng = max(1, ctx.max_ctx // self.ratio) if self.ratio else None  # host bound: no device read

@@ -106,8 +106,9 @@ class DSv4AttnCore:
     def _write_groups(self, seq, slot, pos, kv, kv_score, block_table):
         sp = self.spec
         if sp.ratio == 1:
+            # the compressor's own bf16 row when given (kv_score), else the attention's kv row
             closes = torch.ones_like(pos, dtype=torch.bool)
-            latent = ref.rms_norm(kv, self.comp_norm, sp.eps)
+            latent = ref.rms_norm(kv_score if kv_score is not None else kv, self.comp_norm, sp.eps)
         else:
             closes = (pos + 1) % 2 == 0
             # the group's first row: the previous token of this step, or the sequence's open row
@@ -145,7 +146,7 @@ class DSv4AttnCore:
              max_groups: int | None = None) -> torch.Tensor:
         """Tokens of this step, each sequence's tokens consecutive and in position order: seq [T]
         (row of block_table / slot), pos [T]; slot [S] ring slot of each sequence; q [T, h, 512]
-        (pre-RoPE), kv [T, 512] (kv_norm(wkv(x)), pre-RoPE), kv_score [T, 1024] fp32 (ratio 2),
+        (pre-RoPE), kv [T, 512] (kv_norm(wkv(x)), pre-RoPE), kv_score [T, 1024] fp32 (ratio 2; at ratio 1 an optional bf16 [T, 512]),
         index_q [T, H_i, 128] (pre-RoPE), index_w [T, H_i] (weights_proj(x)); max_groups: a host
         bound on any token's visible groups (the indexer's score width; None reads it from the
         device).  With max_groups given the step reads no device value on the host (graph
