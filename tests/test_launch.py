@@ -30,3 +30,13 @@ def test_receipt_hashes_inputs(tmp_path):
     argv, env = launch.command(cfg)
     rec = launch.receipt(cfg, files, argv, env)
     assert len(rec["inputs"]) == 3 and all(len(h) == 64 for h in rec["inputs"].values())
+
+
+def test_dflash_overlay_reaches_the_server_command():
+    from vllm_cmp170hx_b200.api.server import engine_config, parse_args
+
+    cfg, _files = launch.resolve(SETTINGS, "tp1", ["dflash"], ["engine.device=\"cpu\""])
+    argv, _env = launch.command(cfg)
+    server = argv[argv.index("vllm_cmp170hx_b200.api.server") + 1:]
+    sc = engine_config(parse_args(server)).scheduler
+    assert (sc.num_speculative_tokens, sc.spec_method, sc.adaptive_k) == (3, "dflash", "by_load")
