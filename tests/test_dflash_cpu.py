@@ -86,6 +86,8 @@ def test_block_forward_over_paged_context_matches_dense():
         cs[a, :n] = torch.tensor(b)[p // 64] * 64 + p % 64
     k = 3
     h = d(torch.tensor([11, 22]), torch.tensor(lens) - 1, cs, cs >= 0, caches, k)
+    d.gather_bytes = 1  # one request per group: the same rows
+    assert torch.equal(d(torch.tensor([11, 22]), torch.tensor(lens) - 1, cs, cs >= 0, caches, k), h)
     for a in range(2):
         exp = _dense_block(d, target, states[a], [11, 22][a], k)
         err = ((h[a].float() - exp).norm() / exp.norm()).item()

@@ -144,8 +144,21 @@ class DFlashDrafter(nn.Module):
             kc[slots[keep]] = k[keep]
             vc[slots[keep]] = v[keep]
 
+    # bound on the context keys / values one block forward gathers (requests are split into groups)
+    gather_bytes = 256 << 20
+
     def forward(self, bonus: torch.Tensor, last_pos: torch.Tensor, ctx_slots: torch.Tensor, ctx_valid: torch.Tensor,
                 caches: list[tuple[torch.Tensor, torch.Tensor]], k: int) -> torch.Tensor:
+        A, C = ctx_slots.shape
+        per_req = C * self.dc.num_kv_heads * self.dc.head_dim * 2 * 2 * 2  # K and V, gathered and repeated
+        step = max(1, self.gather_bytes // max(1, per_req))
+        if A <= step:
+            return self._forward(bonus, last_pos, ctx_slots, ctx_valid, caches, k)
+        return torch.cat([self._forward(bonus[i:i + step], last_pos[i:i + step], ctx_slots[i:i + step],
+                                        ctx_valid[i:i + step], caches, k) for i in range(0, A, step)])
+
+    def _forward(self, bonus: torch.Tensor, last_pos: torch.Tensor, ctx_slots: torch.Tensor, ctx_valid: torch.Tensor,
+                 caches: list[tuple[torch.Tensor, torch.Tensor]], k: int) -> torch.Tensor:
         """bonus [A] (the token after the last verified position), last_pos [A]; ctx_slots [A, C]
         cache slots of the context positions (ctx_valid marks the real ones).  Returns the normed
         hidden states [A, k, H] of the k mask rows."""
