@@ -46,6 +46,8 @@ MODEL_DESC = {
 
 
 def reference_unavailable(args, reason: str) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:  # one line per job (rank 0), as the product arm
+        return
     print(json.dumps({"impl": "reference", "unavailable": reason, "metric": METRIC, "n_gpus": args.gpus}))
 
 
@@ -144,9 +146,21 @@ def main():
         if not os.path.isdir(os.path.join(ref, "vllm_sm80")):
             reference_unavailable(args, "reference not installed under baseline/_ref")
             return
-        reference_unavailable(args, "the reference is a vLLM plugin whose model classes subclass upstream vLLM packages "
-                                    "(vllm/models/glm5next, deepseek_v41, qwen4_exp, model-runner V2) that the image's "
-                                    "vLLM 0.22 does not ship, and its native kernels build for sm_80 only")
+        # the reference's own entry to the config-3 model: its GLM-5.3 model class (a vLLM plugin class)
+        sys.path.insert(0, ref)
+        mod = "vllm_sm80.models.glm5next.sm80_model" if args.config == 3 else "vllm_sm80.models.deepseek_v41.sm80_model"
+        try:
+            import importlib
+
+            importlib.import_module(mod)
+        except Exception as e:  # noqa: BLE001 -- whatever stops the reference is the reason
+            reference_unavailable(args, f"import {mod} fails ({type(e).__name__}: {str(e)[:120]}): the reference "
+                                        "is a vLLM plugin whose model classes subclass upstream vLLM packages "
+                                        "(vllm/models/glm5next, deepseek_v41, qwen4_exp, model-runner V2) that the "
+                                        "image's vLLM 0.22 does not ship, and its native kernels build for sm_80 only")
+            return
+        reference_unavailable(args, "the reference imports but has no sm_100 kernels (its extensions build for "
+                                    "sm_80 only)")
         return
 
     import torch

@@ -62,7 +62,7 @@ def test_override_refusals(tmp_path):
     open(bad, "w").write(json.dumps(raw))
     import hashlib
 
-    with pytest.raises(ValueError, match="sha256 mismatch"):
+    with pytest.raises(ValueError, match="do not hash to the manifest"):
         apply_override(tensors, bad, hashlib.sha256(open(bad, "rb").read()).hexdigest())
     raw = json.loads(open(path).read())
     raw["tensors"][0]["name"] = "a.trellis"

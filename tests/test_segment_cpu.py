@@ -103,3 +103,16 @@ def test_row_table_reads_a_held_file(tmp_path):
     finally:
         if proc.poll() is None:
             proc.kill()
+
+
+def test_manifest_hash_is_the_protocol_digest():
+    """The digest is sha256 of the canonical JSON document {label, files: [{name, size, sha256}]}
+    (sorted keys, no whitespace): clients of either holder compute the same value."""
+    import hashlib
+
+    from vllm_cmp170hx_b200.storage.segment import manifest_hash
+
+    files = [{"name": "a.bin", "size": 3, "sha256": "ab" * 32}, {"name": "b.bin", "size": 0, "sha256": "cd" * 32}]
+    text = ('{"files":[{"name":"a.bin","sha256":"' + "ab" * 32 + '","size":3},{"name":"b.bin","sha256":"'
+            + "cd" * 32 + '","size":0}],"label":"L"}')
+    assert manifest_hash("L", files) == hashlib.sha256(text.encode()).hexdigest()

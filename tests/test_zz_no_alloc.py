@@ -5,9 +5,12 @@ its split-K scratch is a fixed area compiled into the library instead of
 memory taken from PyTorch's allocator.  This test loads the extension as a
 plain shared library, calls the symbol twice in a row with fresh inputs and
 checks each result against the ordinary op (torch.ops.b200.gemm_bf16_out)
-with the same tolerance as the other GEMM tests.  It also checks that a shape
-needing more scratch than the fixed maximum is refused with the documented
-code.  (This file is named so pytest collects it last.)
+with the same tolerance as the other GEMM tests, reads the kernel's status
+word back through `b200_gemm_bf16_noalloc_status` (0 = no device-side
+error), and checks that the second call changes neither PyTorch's allocator
+counters nor the device's free memory.  It also checks that a shape needing
+more scratch than the fixed maximum is refused with the documented code.
+(This file is named so pytest collects it last.)
 """
 
 import ctypes
@@ -29,6 +32,19 @@ def _entry():
     f.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
                   ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
     return f
+
+
+def _status():
+    from vllm_cmp170hx_b200 import _C
+
+    lib = ctypes.CDLL(_C.__file__)
+    g = lib.b200_gemm_bf16_noalloc_status
+    g.restype = ctypes.c_int
+    g.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_void_p]
+    word = ctypes.c_uint32(0xFFFFFFFF)
+    rc = g(ctypes.byref(word), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, rc
+    return word.value
 
 
 def _call(f, x, w, y, splits=0):
@@ -59,10 +75,19 @@ def test_noalloc_matches_existing_entry_point_twice(M, N, K, splits):
         w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / K ** 0.5
         expected = ops.gemm(x, w)
         y = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        allocs = torch.cuda.memory_stats().get("allocation.all.allocated", 0)
+        free0 = torch.cuda.mem_get_info()[0]
         rc = _call(f, x, w, y, splits)
         torch.cuda.synchronize()
         assert rc == 0, (call, rc)
+        assert _status() == 0, call
+        if call == 1:  # the first call may load the kernel's module; the second allocates nothing
+            assert torch.cuda.memory_stats().get("allocation.all.allocated", 0) == allocs
+            assert torch.cuda.mem_get_info()[0] > free0 - (2 << 20)
         assert _rel_err(y, expected) < 1e-2, (call, _rel_err(y, expected))
+        err = (y.float() - expected.float()).abs().max().item()
+        assert err <= 2e-2 * expected.float().abs().max().item() + 1e-3, (call, err)
 
 
 def test_noalloc_refuses_more_scratch_than_its_maximum():

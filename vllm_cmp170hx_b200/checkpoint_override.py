@@ -74,40 +74,40 @@ def apply_override(tensors: Mapping[str, torch.Tensor], manifest_path: str, sha2
     from safetensors import safe_open
 
     if not sha256:
-        raise ValueError("an override manifest needs its pinned sha256")
+        raise ValueError("apply_override: pass the expected sha256 of the manifest file (no digest was given)")
     with open(manifest_path, "rb") as f:
         raw = f.read()
     digest = hashlib.sha256(raw).hexdigest()
     if digest != sha256.lower():
-        raise ValueError(f"override manifest sha256 {digest} differs from the pinned {sha256}")
+        raise ValueError(f"{manifest_path}: file digest {digest} is not the expected {sha256.lower()}")
     spec = json.loads(raw)
     if spec.get("format") != FORMAT:
-        raise ValueError(f"unsupported override manifest format {spec.get('format')!r}")
+        raise ValueError(f"{manifest_path}: format {spec.get('format')!r} is not {FORMAT!r}")
     entries = spec["tensors"]
     names = [e["name"] for e in entries]
     side_path = os.path.join(os.path.dirname(manifest_path), spec["sidecar"])
     with safe_open(side_path, framework="pt") as h:
         side = {k: h.get_tensor(k) for k in h.keys()}
     if len(set(names)) != len(names) or set(names) != set(side):
-        raise ValueError("the override sidecar and its manifest list different tensors")
+        raise ValueError(f"{side_path}: its tensor names {sorted(side)} do not equal the manifest's {sorted(set(names))} (or a name repeats)")
     for e in entries:
         n, shape = e["name"], tuple(e["shape"])
         if n not in tensors:
-            raise ValueError(f"override tensor {n} is not in the checkpoint")
+            raise ValueError(f"{n}: listed for replacement but the checkpoint has no tensor of that name")
         if n.endswith(PACKED_SUFFIXES):
-            raise ValueError(f"override tensor {n} is a packed EXL3 part")
+            raise ValueError(f"{n}: a packed EXL3 part (trellis / scales) cannot be replaced by a plain tensor")
         ex = tensors[n]
         if _DT[ex.dtype] != e["export_dtype"] or tuple(ex.shape) != shape:
-            raise ValueError(f"checkpoint tensor {n} differs from the override manifest")
+            raise ValueError(f"{n}: the checkpoint holds {_DT[ex.dtype]} {tuple(ex.shape)}, the manifest expects {e['export_dtype']} {shape}")
         if e.get("cast_check") != {"export_dtype": e["export_dtype"], "equal": True, "compared_elems": math.prod(shape)}:
-            raise ValueError(f"override tensor {n} has no passing cast check")
+            raise ValueError(f"{n}: the manifest records no successful cast check over all {math.prod(shape)} elements")
         src = side[n]
         if _DT[src.dtype] != e["source_dtype"] or tuple(src.shape) != shape:
-            raise ValueError(f"override sidecar tensor {n} differs from its manifest")
+            raise ValueError(f"{n}: the sidecar holds {_DT[src.dtype]} {tuple(src.shape)}, the manifest lists {e['source_dtype']} {shape}")
         if hashlib.sha256(_bytes(src)).hexdigest() != e["sha256"]:
-            raise ValueError(f"override tensor {n}: sha256 mismatch")
+            raise ValueError(f"{n}: the sidecar bytes do not hash to the manifest's sha256")
         if not torch.equal(src.to(ex.dtype).view(torch.uint8), ex.contiguous().view(torch.uint8)):
-            raise ValueError(f"checkpoint tensor {n} is not the sidecar tensor cast to {ex.dtype}")
+            raise ValueError(f"{n}: casting the sidecar tensor to {ex.dtype} does not give the checkpoint's bytes")
     return _Overlay(tensors, {n: side[n] for n in names}), names
 
 

@@ -74,6 +74,11 @@ class DSAConfig:
     o_lora_rank: int = 1024
     rope_theta: float = 10000.0
 
+    def __post_init__(self):
+        bad = sorted({r for r in self.compress_ratios if r not in (0, 1, 2)})
+        if bad:
+            raise ValueError(f"DSAConfig.compress_ratios: ratios {bad} are not supported (0, 1 or 2)")
+
 
 @dataclass
 class MoEConfig:

@@ -1044,3 +1044,18 @@ extern "C" int b200_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w,
   }
   return (int)e;
 }
+
+extern "C" int b200_gemm_bf16_noalloc_status(uint32_t* out, cudaStream_t stream) {
+  using namespace b200;
+  if (out == nullptr) return B200_NOALLOC_BAD_ARGS;
+  noalloc::DeviceScratch s;
+  cudaError_t e = noalloc::scratch_for_current_device(&s);
+  if (e != cudaSuccess) return (int)e;
+  uint32_t v = 0;
+  e = cudaMemcpyAsync(&v, s.status, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return (int)e;
+  *out = v;
+  return 0;
+}

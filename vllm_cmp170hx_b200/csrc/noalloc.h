@@ -27,10 +27,19 @@
 //   * All calls share the same scratch, which keeps the last call's contents.
 //     Calls that overlap on the GPU (different streams, or several host
 //     threads without ordering) race on it: serialise them on one stream.
-//   * Return value: 0 on success; B200_NOALLOC_TOO_LARGE (-1) when the chosen
-//     split-K needs more than B200_NOALLOC_SCRATCH_FLOATS partial values
-//     (splits * M * N); B200_NOALLOC_BAD_ARGS (-2) for invalid arguments;
-//     otherwise the cudaError_t of the CUDA call that failed.
+//   * Return value: 0 when the work was enqueued on `stream` (it has not run
+//     yet); B200_NOALLOC_TOO_LARGE (-1) when the chosen split-K needs more
+//     than B200_NOALLOC_SCRATCH_FLOATS partial values (splits * M * N);
+//     B200_NOALLOC_BAD_ARGS (-2) for invalid arguments; otherwise the
+//     cudaError_t of the CUDA call that failed.
+//   * Errors found while the kernel runs (a pipeline wait that gave up, bit
+//     0x1; an index out of range, 0x4; a tensor-memory allocation that did not
+//     return, 0x8) do not show in the return value: the kernel ORs them into
+//     the status word of the fixed area, which each call clears before its
+//     kernel.  b200_gemm_bf16_noalloc_status() waits for `stream` and copies
+//     that word out; when it is not 0, C holds partial results.  Like the
+//     scratch, the word is shared by every call on the device: read it after
+//     the call it should describe and before the next one.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -47,6 +56,12 @@ extern "C" {
 // splits: 0 lets the library choose (as the ordinary op does), > 0 forces it.
 int b200_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M,
                            int N, int K, int splits, cudaStream_t stream);
+
+// Waits until all work queued on `stream` so far has finished, then stores
+// the current device's status word in *out (0: the last call's kernel ran
+// without error).  Allocates nothing.  Returns 0, B200_NOALLOC_BAD_ARGS for a
+// null `out`, or the cudaError_t of the failed copy or wait.
+int b200_gemm_bf16_noalloc_status(uint32_t* out, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -174,7 +174,7 @@ def _load_dsa(a, t, p, tp, r):
     if a.ratio:
         _set(a.comp_norm, _get(t, p + "compressor.norm.weight"))
         w = _dense(t, p + "compressor.wkv")
-        if a.ratio == 2:
+        if a.ratio > 1:  # the compressor pools groups by gate scores: [wkv | wgate]
             w = torch.cat([w, _dense(t, p + "compressor.wgate")], 0)
         _set_linear(a.wkv_c, w)
         _set_linear(a.idx_q, _dense(t, p + "indexer.wq_b"))
@@ -345,7 +345,7 @@ def export_hf(model) -> dict[str, torch.Tensor]:
             if a.ratio:
                 out[q + "compressor.norm.weight"] = a.comp_norm.detach()
                 w = dense(a.wkv_c)
-                if a.ratio == 2:
+                if a.ratio > 1:
                     out[q + "compressor.wkv.weight"], out[q + "compressor.wgate.weight"] = (
                         x.contiguous() for x in w.chunk(2, 0))
                 else:

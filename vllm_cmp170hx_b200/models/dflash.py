@@ -97,11 +97,11 @@ class DFlashLayer(nn.Module):
         K = torch.cat([ctx_k, k.view(A, B, self.nkv, self.hd)], 1)  # [A, C + B, nkv, hd]
         V = torch.cat([ctx_v, v.view(A, B, self.nkv, self.hd)], 1)
         valid = torch.cat([ctx_valid, torch.ones(A, B, dtype=torch.bool, device=x.device)], 1)
-        rep = self.nh // self.nkv
         qh = q.view(A, B, self.nh, self.hd).transpose(1, 2)  # [A, nh, B, hd]
-        Kh = K.transpose(1, 2).repeat_interleave(rep, 1)  # [A, nh, C + B, hd]
-        Vh = V.transpose(1, 2).repeat_interleave(rep, 1)
-        o = F.scaled_dot_product_attention(qh, Kh, Vh, attn_mask=valid[:, None, None, :])
+        Kh = K.transpose(1, 2)  # [A, nkv, C + B, hd]: query head h reads key / value head h // (nh / nkv)
+        Vh = V.transpose(1, 2)
+        o = F.scaled_dot_product_attention(qh, Kh, Vh, attn_mask=valid[:, None, None, :],
+                                           enable_gqa=self.nh != self.nkv)
         o = o.transpose(1, 2).reshape(A * B, self.nh * self.hd).to(x.dtype)
         a = ops.gemm(o, self.o_proj.weight)
         h = self.post_norm(a, residual)  # residual += a (in place), h = norm(residual)
@@ -150,7 +150,9 @@ class DFlashDrafter(nn.Module):
     def forward(self, bonus: torch.Tensor, last_pos: torch.Tensor, ctx_slots: torch.Tensor, ctx_valid: torch.Tensor,
                 caches: list[tuple[torch.Tensor, torch.Tensor]], k: int) -> torch.Tensor:
         A, C = ctx_slots.shape
-        per_req = C * self.dc.num_kv_heads * self.dc.head_dim * 2 * 2 * 2  # K and V, gathered and repeated
+        # K and V (bf16) of the context plus the block rows, gathered once and joined once (the
+        # attention reads the key / value heads in place, no per-query-head copies)
+        per_req = (C + k + 1) * self.dc.num_kv_heads * self.dc.head_dim * 2 * 2 * 2
         step = max(1, self.gather_bytes // max(1, per_req))
         if A <= step:
             return self._forward(bonus, last_pos, ctx_slots, ctx_valid, caches, k)

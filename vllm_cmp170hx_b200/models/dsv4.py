@@ -29,7 +29,11 @@ def dsa_ratio(cfg: ModelConfig, idx: int) -> int:
     """Compression ratio of global layer idx (its position among the "dsa" layers)."""
     k = cfg.layer_types[:idx].count("dsa")
     r = cfg.dsa.compress_ratios
-    return r[k % len(r)] if r else 1
+    ratio = r[k % len(r)] if r else 1
+    if ratio not in (0, 1, 2):
+        # the compressor, its caches and the checkpoint names exist for ratios 0 (window only), 1 and 2
+        raise ValueError(f"DeepSeek-V4.1 layer {idx}: compression ratio {ratio} is not supported (0, 1 or 2)")
+    return ratio
 
 
 class DSAAttention(nn.Module):

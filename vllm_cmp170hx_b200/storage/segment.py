@@ -57,17 +57,20 @@ class SegmentError(RuntimeError):
 
 
 def file_identity(path: str) -> dict:
-    """What a client and the holder agree a file is: name, device, inode, size, mtime."""
-    st = os.stat(path)
-    return {"name": os.path.basename(path), "dev": st.st_dev, "ino": st.st_ino, "size": st.st_size,
-            "mtime_ns": st.st_mtime_ns}
+    """What a client and the holder agree a file is: its resolved path, device, inode, size and
+    modification time (the identity fields of the protocol)."""
+    real = os.path.realpath(path)
+    st = os.stat(real)
+    return {"path": real, "dev": st.st_dev, "ino": st.st_ino, "size": st.st_size, "mtime_ns": st.st_mtime_ns}
 
 
 def manifest_hash(label: str, files: list[dict]) -> str:
-    h = hashlib.sha256(label.encode())
-    for f in files:
-        h.update(f"{f['name']}\0{f['size']}\0{f['sha256']}\0".encode())
-    return h.hexdigest()
+    """The manifest digest of the protocol: sha256 over the canonical JSON text (keys sorted, no
+    whitespace) of ``{"label": label, "files": [{"name", "size", "sha256"}, ...]}`` with the files in
+    holding order, so a client of either holder computes the same value."""
+    listed = [{k: f[k] for k in ("name", "size", "sha256")} for f in files]
+    canonical = json.dumps({"files": listed, "label": label}, sort_keys=True, separators=(",", ":"))
+    return hashlib.sha256(canonical.encode()).hexdigest()
 
 
 def _send(sock: socket.socket, obj: dict, fds: list[int] | None = None) -> None:
@@ -133,7 +136,7 @@ class Holder:
         before = file_identity(hf.path)
         hf.identity = before
         size = before["size"]
-        fd = os.memfd_create("table:" + before["name"], os.MFD_CLOEXEC | getattr(os, "MFD_ALLOW_SEALING", 2))
+        fd = os.memfd_create("table:" + os.path.basename(before["path"]), os.MFD_CLOEXEC | getattr(os, "MFD_ALLOW_SEALING", 2))
         os.ftruncate(fd, size)
         h = hashlib.sha256()
         with open(hf.path, "rb", buffering=0) as src:
@@ -170,7 +173,7 @@ class Holder:
 
     # ------------------------------------------------------------------ answers
     def manifest(self) -> str:
-        return manifest_hash(self.label, [{"name": f.identity.get("name", os.path.basename(f.path)),
+        return manifest_hash(self.label, [{"name": os.path.basename(f.path),
                                            "size": f.identity.get("size", 0), "sha256": f.sha256}
                                           for f in self.files])
 
@@ -183,14 +186,14 @@ class Holder:
 
     def _attach_answer(self, msg: dict) -> tuple[dict, list[int]]:
         want = msg.get("files", [])
-        by_name = {f.identity["name"]: f for f in self.files}
+        by_path = {f.identity["path"]: f for f in self.files}
         fds, names = [], []
         for ident in want:
-            f = by_name.get(ident.get("name"))
+            f = by_path.get(ident.get("path"))
             if f is None or {k: ident.get(k) for k in f.identity} != f.identity:
-                return {"ok": False, "error": f"not held (or changed): {ident.get('name')}"}, []
+                return {"ok": False, "error": f"not held (or changed): {ident.get('path')}"}, []
             fds.append(f.fd)
-            names.append(f.identity["name"])
+            names.append(f.identity["path"])
         return {"ok": True, "files": names, "manifest": self.manifest()}, fds
 
     # ------------------------------------------------------------------ serve
@@ -305,7 +308,7 @@ class Attachment:
             raise SegmentError(answer.get("error", "attach refused"))
         self.manifest = answer["manifest"]
         self.fds = {os.path.basename(p): fd for p, fd in zip(paths, fds)}
-        self.sizes = {i["name"]: i["size"] for i in idents}
+        self.sizes = {os.path.basename(i["path"]): i["size"] for i in idents}
 
     def fd_path(self, path: str) -> str:
         return f"/proc/self/fd/{self.fds[os.path.basename(path)]}"
