@@ -12,16 +12,16 @@ from vllm_cmp170hx_b200.ops.dsv4_attn import DSv4AttnCore, DSv4AttnSpec
 
 def test_qdq_grids():
     x = torch.tensor([[0.0, 0.3, -1.1, 2.6, 5.0, -6.0, 100.0, 7e-3] * 4])
-    y = ref.qdq_fp4(x, 32, "e8m0")
+    y = ref.fp4_qdq(x, 32, "pow2")
     s = 32.0  # the smallest power of two >= 100 / 6
     grid = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6])
     q = (y / s).abs().flatten()
     assert all(bool((grid == v).any()) for v in q), q
-    y8 = ref.qdq_fp8(x, 32)
-    assert torch.equal(y8, ref.qdq_fp8(y8, 32))  # values on the grid stay put
+    y8 = ref.fp8_qdq(x, 32)
+    assert torch.equal(y8, ref.fp8_qdq(y8, 32))  # values on the grid stay put
     assert ((y8 - x).abs() <= x.abs() * 2 ** -3 + 2 ** -9 * 2 ** -2).all()
     # e4m3 block scales: s = e4m3(amax / 6)
-    z = ref.qdq_fp4(torch.full((1, 16), 0.75), 16, "e4m3")
+    z = ref.fp4_qdq(torch.full((1, 16), 0.75), 16, "e4m3")
     assert torch.allclose(z, torch.full((1, 16), 0.75))
 
 
@@ -53,7 +53,7 @@ def _scratch(spec, w, inp, p, cand=None):
     for b in range(spec.window):
         j = p - b
         ok = j >= 0
-        rows.append(ref.window_rows(inp["kv"][max(j, 0)][None], torch.tensor([max(j, 0)]), fr)[0])
+        rows.append(ref.window_kv(inp["kv"][max(j, 0)][None], torch.tensor([max(j, 0)]), fr)[0])
         valid.append(ok)
     n_vis = (p + 1) // spec.ratio
     sel = torch.full((spec.index_topk,), -1)
@@ -64,28 +64,28 @@ def _scratch(spec, w, inp, p, cand=None):
             if spec.ratio == 1:
                 lat.append(ref.rms_norm(inp["kv"][gi][None], w["comp_norm"], spec.eps)[0])
             else:
-                lat.append(ref.pool_pair(inp["ks"][2 * gi][None], inp["ks"][2 * gi + 1][None], w["comp_norm"],
+                lat.append(ref.pooled_pair(inp["ks"][2 * gi][None], inp["ks"][2 * gi + 1][None], w["comp_norm"],
                                          spec.eps)[0])
             gpos.append(gi * spec.ratio)
         lat, gpos = torch.stack(lat), torch.tensor(gpos)
-        comp = ref.compressed_rows(lat, gpos, fr)
-        keys = ref.index_key_rows((lat.float() @ w["wk"].float().t()).bfloat16(), w["k_norm"], fr, gpos, spec.eps)
-        qi = ref.index_query(inp["iq"][p][None], pos, fr)
+        comp = ref.compressed_kv(lat, gpos, fr)
+        keys = ref.index_key((lat.float() @ w["wk"].float().t()).bfloat16(), w["k_norm"], gpos, fr, spec.eps)
+        qi = ref.index_q(inp["iq"][p][None], pos, fr)
         wi = (inp["iw"][p][None].float() * (spec.index_dim ** -0.5 * spec.index_heads ** -0.5)).bfloat16()
-        sc = ref.index_scores(qi, wi, keys, torch.tensor([n_vis]), spec.index_heads_per_rank)
+        sc = ref.indexer_scores(qi, wi, keys[None], torch.tensor([n_vis]), spec.index_heads_per_rank)
         if cand is not None:
-            sc = ref.mask_to_candidates(sc, cand[None], spec.candidate_block)
-        sel = ref.topk_canonical(sc, torch.tensor([n_vis]), spec.index_topk)[0]
-        cb = ref.candidate_blocks(sc, torch.tensor([n_vis]), spec.candidate_blocks, spec.candidate_block)[0] \
+            sc = ref.restrict_to_blocks(sc, cand[None], spec.candidate_block)
+        sel = ref.select_topk(sc, torch.tensor([n_vis]), spec.index_topk)[0]
+        cb = ref.pick_blocks(sc, torch.tensor([n_vis]), spec.candidate_blocks, spec.candidate_block)[0] \
             if spec.candidate_blocks else None
     else:
         cb = torch.full((spec.candidate_blocks,), -1, dtype=torch.int32) if spec.candidate_blocks else None
     for s in sel.tolist():
         rows.append(comp[s] if s >= 0 else torch.zeros(spec.head_dim, dtype=torch.bfloat16))
         valid.append(s >= 0)
-    qr = ref.rope(inp["q"][p][None], pos, fr)
-    o = ref.sparse_attention(qr, torch.stack(rows)[None], torch.tensor(valid)[None], w["sink"], spec.head_dim ** -0.5)
-    return ref.output_qdq(o, pos, fr, spec.out_groups)[0], cb
+    qr = ref.rotate(inp["q"][p][None], pos, fr)
+    o = ref.attend_with_sink(qr, torch.stack(rows)[None], torch.tensor(valid)[None], w["sink"], spec.head_dim ** -0.5)
+    return ref.finish_output(o, pos, fr)[0], cb
 
 
 def _run(spec, w, seqs, chunks, device="cpu", candidates=None):
@@ -156,3 +156,78 @@ def test_candidate_blocks_two_levels():
         for p in range(len(seqs[s]["kv"])):
             exp, _ = _scratch(user, w, seqs[s], p, cand=cands[s][p])
             assert torch.equal(outs[s][p], exp), (s, p)
+
+
+def test_e2m1_nearest_ties_to_even_code():
+    """Every magnitude on a fine grid (thresholds included) goes to the nearest E2M1 value; on a tie
+    the value with the even code (0, 1, 2, 4) wins."""
+    grid = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+    xs = torch.arange(0, 6.0001, 1 / 64)
+    got = ref.e2m1(torch.cat([xs, -xs]))
+    for i, x in enumerate(xs.tolist()):
+        d = [abs(x - g) for g in grid]
+        best = min(d)
+        cands = [c for c, v in enumerate(d) if v == best]
+        code = cands[0] if len(cands) == 1 else [c for c in cands if c % 2 == 0][0]
+        assert got[i].item() == grid[code], x
+        assert got[len(xs) + i].item() == -grid[code], x
+
+
+def test_selection_against_sorted_pairs():
+    """select_topk / pick_blocks against a plain sort of (-score, column) pairs, with repeated scores,
+    signed zeros and -FLT_MAX entries."""
+    g = torch.Generator().manual_seed(7)
+    n, N, k = 6, 40, 9
+    scores = torch.randint(-3, 4, (n, N), generator=g).float()
+    scores[scores == 0] = torch.tensor(-0.0)
+    scores[:, ::7] = 0.0
+    scores[1, 3:20] = ref.NEG_FLT_MAX
+    n_vis = torch.tensor([40, 5, 9, 1, 0, 23])
+    scores = torch.where(torch.arange(N)[None] < n_vis[:, None], scores, float("-inf"))
+    got = ref.select_topk(scores, n_vis, k)
+    for i in range(n):
+        pairs = sorted((-scores[i, c].item(), c) for c in range(int(n_vis[i])))
+        want = sorted(c for _, c in pairs[:k])
+        assert got[i].tolist() == want + [-1] * (k - len(want)), i
+    blk = 4
+    got_b = ref.pick_blocks(scores, n_vis, 3, blk)
+    for i in range(n):
+        nv = int(n_vis[i])
+        nb = -(-nv // blk)
+        best = [max(scores[i, b * blk:min(N, b * blk + blk)].tolist()) for b in range(nb)]
+        if nv:
+            best[(nv - 1) // blk] = float("inf")
+        pairs = sorted((-(v + 0.0), b) for b, v in enumerate(best))
+        want = sorted(b for _, b in pairs[:3])
+        assert got_b[i].tolist() == want + [-1] * (3 - len(want)), i
+
+
+def test_indexer_score_rounding_chain():
+    """indexer_scores against a scalar evaluation of the stated rounding chain."""
+    import numpy as np
+
+    g = torch.Generator().manual_seed(3)
+    H, D, N, hpg = 8, 16, 5, 4
+    q = torch.randn(2, H, D, generator=g).bfloat16()
+    w = torch.randn(2, H, generator=g).bfloat16()
+    keys = torch.randn(2, N, D, generator=g).bfloat16()
+    got = ref.indexer_scores(q, w, keys, torch.tensor([N, 3]), hpg)
+
+    def bf(x):
+        return float(torch.tensor(x, dtype=torch.float32).bfloat16().float())
+
+    for i in range(2):
+        for c in range(N):
+            if c >= [N, 3][i]:
+                assert got[i, c].item() == float("-inf")
+                continue
+            total = None
+            for r in range(H // hpg):
+                acc = np.float32(0)
+                for h in range(r * hpg, (r + 1) * hpg):
+                    dot = float(np.dot(q[i, h].float().double().numpy(), keys[i, c].float().double().numpy()))
+                    t = bf(float(np.float32(w[i, h].float().item()) * np.float32(max(bf(dot), 0.0))))
+                    acc = np.float32(acc + np.float32(t)) if h > r * hpg else np.float32(t)
+                part = bf(float(acc))
+                total = part if total is None else bf(float(np.float32(total) + np.float32(part)))
+            assert got[i, c].item() == total, (i, c)

@@ -28,7 +28,7 @@ def test_sink_attention_matches_oracle(T, h, splits):
     idx[-1, 200:] = -1
     sink = torch.randn(h, generator=g) * 2
     scale = 512 ** -0.5
-    exp = ref.sparse_attention(q, pool[idx.clamp_min(0)], idx >= 0, sink, scale)
+    exp = ref.attend_with_sink(q, pool[idx.clamp_min(0)], idx >= 0, sink, scale)
     got = attend(q.cuda(), pool.cuda(), idx.cuda(), sink.cuda(), scale, splits=splits).cpu()
     assert _rel(got, exp) < 1e-2, _rel(got, exp)
     empty = (idx < 0).all(1)

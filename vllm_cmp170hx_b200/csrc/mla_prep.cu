@@ -202,7 +202,7 @@ __global__ void index_q_prep_kernel(const __nv_bfloat16* __restrict__ q, int64_t
 // ----------------------------------------------------------------------------- top-k
 // Order-preserving uint32 key of a float (larger float -> larger key).
 __device__ __forceinline__ uint32_t fkey(float f) {
-  const uint32_t u = __float_as_uint(f);
+  const uint32_t u = f == 0.f ? 0u : __float_as_uint(f);  // -0 and +0 are the same score (a tie)
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 

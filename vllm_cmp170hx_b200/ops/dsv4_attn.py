@@ -45,7 +45,7 @@ def attend(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sink: torch.T
     """q [T, h, 512] bf16 over pool rows idx [T, R] (int, -1 = none; K = V = the row) with a per-head
     sink [h] fp32 -> [T, h, 512] bf16."""
     if not q.is_cuda:
-        return ref.sparse_attention(q, pool[idx.clamp_min(0).long()], idx >= 0, sink, scale)
+        return ref.attend_with_sink(q, pool[idx.clamp_min(0).long()], idx >= 0, sink, scale)
     from .mla import pick_splits
 
     # valid rows first (stable), then the per-token count: the kernel reads the first `count`
@@ -117,7 +117,7 @@ class DSv4AttnCore:
             tslot = slot[seq.long()].long()
             carried = self.prev[tslot, (pos - 1) % self.carry]
             prev = torch.where(same[:, None], torch.roll(kv_score, 1, 0), carried)
-            latent = ref.pool_pair(prev, kv_score, self.comp_norm, sp.eps)
+            latent = ref.pooled_pair(prev, kv_score, self.comp_norm, sp.eps)
             # the last `carry` positions of each sequence into its carry ring (distinct rows; the
             # others into the dummy slot)
             keep = pos > self._last_pos(seq, pos, slot.shape[0]) - self.carry
@@ -126,10 +126,10 @@ class DSv4AttnCore:
         g = (torch.div(pos + 1, sp.ratio, rounding_mode="floor") - 1).clamp_min(0)
         gpos = pos + 1 - sp.ratio
         rows = self._group_rows(block_table, seq, g)
-        self.pool[torch.where(closes, self.G0 + rows, self.dummy)] = ref.compressed_rows(latent, gpos, self.freqs)
+        self.pool[torch.where(closes, self.G0 + rows, self.dummy)] = ref.compressed_kv(latent, gpos, self.freqs)
         k = latent.float() @ self.wk.float().t()
-        self.idxk[torch.where(closes, rows, self.kdummy)] = ref.index_key_rows(k.to(torch.bfloat16), self.k_norm,
-                                                                               self.freqs, gpos, sp.eps)
+        self.idxk[torch.where(closes, rows, self.kdummy)] = ref.index_key(k.to(torch.bfloat16), self.k_norm, gpos,
+                                                                          self.freqs, sp.eps)
 
     @staticmethod
     def _last_pos(seq: torch.Tensor, pos: torch.Tensor, S: int) -> torch.Tensor:
@@ -158,7 +158,7 @@ class DSv4AttnCore:
         dev = pos.device
         pos = pos.long()
         seq_l = seq.long()
-        wrows = ref.window_rows(kv, pos, self.freqs)
+        wrows = ref.window_kv(kv, pos, self.freqs)
         self.pool[self.S0:self.S0 + T] = wrows
         if sp.ratio:
             self._write_groups(seq, slot, pos, kv, kv_score, block_table)
@@ -179,7 +179,7 @@ class DSv4AttnCore:
         idx = [widx]
         if sp.ratio:
             n_vis = torch.div(pos + 1, sp.ratio, rounding_mode="floor")
-            qi = ref.index_query(index_q, pos, self.freqs)
+            qi = ref.index_q(index_q, pos, self.freqs)
             wi = (index_w.float() * (sp.index_dim ** -0.5 * sp.index_heads ** -0.5)).to(torch.bfloat16)
             N = max(1, max_groups if max_groups is not None else int(n_vis.max()))
             # every query scores the groups of its own sequence, in row chunks of bounded size
@@ -190,21 +190,21 @@ class DSv4AttnCore:
             for r0 in range(0, T, rc):
                 r = slice(r0, min(T, r0 + rc))
                 gr = block_table[seq_l[r]][:, gi // 64].long() * 64 + gi % 64  # [rows, N] group rows
-                scores = ref.index_scores_rows(qi[r], wi[r], self.idxk[gr], n_vis[r], sp.index_heads_per_rank)
+                scores = ref.indexer_scores(qi[r], wi[r], self.idxk[gr], n_vis[r], sp.index_heads_per_rank)
                 if sp.candidate_blocks and candidates_in is None:
-                    cbs.append(ref.candidate_blocks(scores, n_vis[r], sp.candidate_blocks, sp.candidate_block))
+                    cbs.append(ref.pick_blocks(scores, n_vis[r], sp.candidate_blocks, sp.candidate_block))
                 elif candidates_in is not None:
-                    scores = ref.mask_to_candidates(scores, candidates_in[r], sp.candidate_block)
-                top = ref.topk_canonical(scores, n_vis[r], sp.index_topk).long()
+                    scores = ref.restrict_to_blocks(scores, candidates_in[r], sp.candidate_block)
+                top = ref.select_topk(scores, n_vis[r], sp.index_topk).long()
                 sels.append(torch.where(top >= 0, self.G0 + gr.gather(1, top.clamp_min(0)), -1))
             if candidates_out is not None and cbs:
                 candidates_out.append(torch.cat(cbs))
             idx.append(torch.cat(sels))
-        qr = ref.rope(q, pos, self.freqs)
+        qr = ref.rotate(q, pos, self.freqs)
         o = attend(qr, self.pool, torch.cat(idx, 1), self.sink, sp.head_dim ** -0.5)
         # the last `ring` positions of each sequence into its ring (distinct ring rows; the others
         # into the dummy row)
         keep = pos > self._last_pos(seq_l, pos, slot.shape[0]) - self.ring
         ring_rows = self.W0 + slot[seq_l].long() * self.ring + pos % self.ring
         self.pool[torch.where(keep, ring_rows, self.dummy)] = wrows
-        return ref.output_qdq(o, pos, self.freqs, sp.out_groups)
+        return ref.finish_output(o, pos, self.freqs)

@@ -1,224 +1,264 @@
-"""fp32 definition of the DeepSeek-V4.1 attention core, per token.
+"""Host definition of the DeepSeek-V4.1 attention core (the fp32 model of what the CUDA path computes).
 
-For a query at absolute position p the attended rows are
+The contract, stated for one query token at absolute position ``p`` of a sequence:
 
-* the window: the layer's rows of positions [max(0, p - window + 1), p], each RoPE'd at its
-  position and then FP8 (blocks of 32, power-of-two scales) quantize-dequantized;
-* the compressed rows: n_vis = (p + 1) // ratio groups of `ratio` consecutive positions are closed;
-  group g's row is the RMS-normalised latent of the group (ratio 1: the token's own row; ratio 2:
-  the pair pooled by an fp32 softmax over its gate scores), RoPE'd at the group's first position
-  and FP4 (blocks of 16, E4M3 scales) quantize-dequantized.  When n_vis exceeds the indexer's
-  top-k only the top-k best groups are attended.
+Rows it may attend (every row is 512 wide and serves as both key and value; the last 64 dims carry RoPE):
 
-The indexer scores group g for the query as sum over index heads of
-bf16(bf16(relu(bf16(q_h . k_g))) * w_h), the heads summed in fp32 per tensor-parallel rank group and
-rounded to bf16, the groups added in rank order (the all-reduce); index keys are
-FP4(RoPE(RMSNorm(wk(latent)))) with power-of-two scales per 32, the index query likewise.  The
-selection is canonical (score descending, position ascending on ties, then sorted ascending).  A
-second level may restrict the choice to candidate blocks picked by another layer's indexer (the
-block holding the newest visible group always in); visible groups outside them score -FLT_MAX.
+* window rows: the layer's ``kv`` rows of positions ``max(0, p - window + 1) .. p``, each rotated by its
+  own position and then rounded onto the FP8 grid (E4M3 codes, one power-of-two scale per 32 values);
+* compressed rows: once ``ratio`` consecutive positions are complete they form a group.  At ratio 1 a
+  group is the RMS-normalised compressor row of its token; at ratio 2 the two tokens' fp32 compressor rows
+  ``[kv | score]`` are pooled with weights softmax(score) (per channel) and the pooled row is rounded to
+  bf16 and RMS-normalised.  The group row is rotated by the group's first position and rounded onto the
+  FP4 grid (E2M1 codes, one E4M3 scale per 16 values).  ``(p + 1) // ratio`` groups are visible.
 
-Attention is MQA over rows that serve as both K and V (512 dims, RoPE on the last 64): fp32 scores
-times head_dim^-0.5, softmax whose denominator also holds exp(sink_h), probabilities rounded to bf16
-before they weight the rows; a query with no row gets zeros.  The output gets the inverse RoPE on
-its tail and an FP8 quantize-dequantize per output group (the wo_a input).
+Indexer: index keys are FP4 (E2M1, power-of-two scale per 32) of the rotated, RMS-normalised
+``wk(latent)``; the index query is likewise FP4 of the rotated query.  The score of group ``g`` is
+built from per-head terms ``t_h = bf16(w_h * relu(bf16(q_h . k_g)))``; the heads of each tensor-parallel
+rank group are added in head order in fp32 and the sum rounded to bf16, and the rank groups' sums are
+added in rank order with a bf16 rounding after each addition (the all-reduce).  The chosen groups are
+the ``min(topk, visible)`` best by (score descending, group ascending), listed in ascending group
+order.  A second level may first restrict the candidates to blocks of ``block`` groups chosen by another
+layer's indexer; groups outside those blocks then score -FLT_MAX (not -inf: they stay selectable when
+too few candidates exist).  The blocks a source layer publishes are the ``topk_blocks`` best by their
+best group's score (block of the newest visible group always in), ascending.
 
-This is an independent statement of the math the reference implements in
-vllm_sm80/models/deepseek_v41/ops/sm80_attn_core.py (window_kv :262, compress_rows :294,
-index_key_rows :371, compressed_kv :384, index_query :433, combine_head_scores :450,
-topk_canonical :523, select_candidate_blocks :569, mask_to_candidates :598, sparse_attention_torch
-:678, output_qdq :736) and its quantize-dequantize definitions (ops/sm80_act_quant.py:1-32).
+Attention: MQA with fp32 logits ``q . row * 512^-0.5``; softmax weights ``e_r = exp(l_r - max_r l_r)``
+whose denominator also holds ``exp(sink_h - max_r l_r)``; the rows are weighted by the bf16-rounded
+``e_r`` and divided by the fp32 denominator; a query without any row gets zeros.  The output's tail is
+rotated back (inverse RoPE) and rounded onto the FP8 grid per 32 values (the input of ``wo_a``).
+
+Grids and scales (blocks along the last dim):
+
+* FP8: ``s = 2^ceil(log2(max(amax, 1e-4) * fl32(1/448)))``, ``y = e4m3(x / s) * s``;
+* FP4 with power-of-two scales: ``s = 2^ceil(log2(max(amax, 6 * 2^-126) * fl32(1/6)))``;
+* FP4 with E4M3 scales: ``s = e4m3(max(amax, 6 * 2^-9) / 6)``;
+* FP4 values: ``e2m1(clamp(x / s, -6, 6)) * s`` with E2M1 rounding to nearest, ties to the even code.
+
+The model these rounding points define is the reference's (vllm_sm80/models/deepseek_v41/ops/
+sm80_attn_core.py: window rows :262, compressed rows :294-384, indexer :433-470, selection :523-610,
+attention :678, output :736; FP8 / FP4 grids ops/sm80_act_quant.py:1-32).  The code below is written
+from that statement: rotations in fp64 from fp32 angles, scales from ``frexp``, E2M1 by rounding
+thresholds, and selections by one sortable 64-bit key per candidate.
 """
 
 from __future__ import annotations
 
 import torch
 
-FLT_MAX = torch.finfo(torch.float32).max
-_FP8_MAX = 448.0
-_FP4_MAX = 6.0
-_INV_FP8 = float(torch.tensor(1.0 / 448.0, dtype=torch.float32))
-_INV_FP4 = float(torch.tensor(1.0 / 6.0, dtype=torch.float32))
+NEG_FLT_MAX = -torch.finfo(torch.float32).max
+E4M3_MAX = 448.0
+E2M1_MAX = 6.0
+# the reciprocals the scale rules multiply by, as fp32 numbers
+RECIP_E4M3_MAX = float(torch.tensor(1.0 / E4M3_MAX, dtype=torch.float32))
+RECIP_E2M1_MAX = float(torch.tensor(1.0 / E2M1_MAX, dtype=torch.float32))
 
 
-# ---------------------------------------------------------------------------- quantize-dequantize
-def _pow2_at_least(a: torch.Tensor) -> torch.Tensor:
-    """The smallest power of two >= a, for positive normal fp32 a (from its exponent bits)."""
-    b = a.float().contiguous().view(torch.int32)
-    e = ((b >> 23) & 0xFF) + ((b & 0x7FFFFF) != 0).to(torch.int32)
-    return (e << 23).view(torch.float32)
+# ---------------------------------------------------------------------------- number grids
+def pow2_ceil(a: torch.Tensor) -> torch.Tensor:
+    """2^ceil(log2 a) for positive normal fp32 a: frexp gives a = m 2^e with m in [0.5, 1); a is itself
+    a power of two exactly when m == 0.5."""
+    m, e = torch.frexp(a.float())
+    return torch.ldexp(torch.ones_like(m), e - (m == 0.5).to(e.dtype))
 
 
-def _round_e2m1(v: torch.Tensor) -> torch.Tensor:
-    """fp32 onto {0, .5, 1, 1.5, 2, 3, 4, 6} (signed), nearest with ties to even; |v| <= 6."""
-    a = v.abs()
-    step = torch.where(a < 2, 0.5, torch.where(a < 4, 1.0, 2.0))
-    return torch.copysign(torch.round(a / step) * step, v)
+def e4m3(v: torch.Tensor) -> torch.Tensor:
+    """Nearest E4M3 value (saturating at +-448), as fp32."""
+    return v.float().clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).float()
 
 
-def _round_e4m3(v: torch.Tensor) -> torch.Tensor:
-    return v.clamp(-_FP8_MAX, _FP8_MAX).to(torch.float8_e4m3fn).float()
+# E2M1 magnitudes and the rounding thresholds between neighbours; a magnitude exactly on a threshold
+# goes to the neighbour with the even code (0, 1, 2, 4 have even codes; 0.5, 1.5, 3, 6 odd)
+_E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+_E2M1_THRESHOLDS = ((0.25, False), (0.75, True), (1.25, False), (1.75, True), (2.5, False), (3.5, True), (5.0, False))
 
 
-def qdq_fp8(x: torch.Tensor, block: int = 32) -> torch.Tensor:
-    """Per `block` values of the last dim: s = pow2 >= max(absmax, 1e-4) / 448, y = e4m3(x / s) s."""
-    shp = x.shape
-    b = x.float().reshape(*shp[:-1], shp[-1] // block, block)
-    s = _pow2_at_least(b.abs().amax(-1, keepdim=True).clamp_min(1e-4) * _INV_FP8)
-    return (_round_e4m3(b / s) * s).reshape(shp).to(x.dtype)
+def e2m1(v: torch.Tensor) -> torch.Tensor:
+    """Nearest E2M1 value of v (|v| <= 6), ties to the even code, as fp32."""
+    a = v.float().abs()
+    code = torch.zeros_like(a, dtype=torch.int64)
+    for t, tie_up in _E2M1_THRESHOLDS:
+        code += (a >= t if tie_up else a > t).to(torch.int64)
+    mag = torch.tensor(_E2M1, dtype=torch.float32, device=v.device)[code]
+    return torch.where(v < 0, -mag, mag)
 
 
-def qdq_fp4(x: torch.Tensor, block: int, scale: str = "e8m0") -> torch.Tensor:
-    """Per `block` values: e8m0 s = pow2 >= max(absmax, 6 * 2^-126) / 6; e4m3 s = e4m3(max(absmax,
-    6 * 2^-9) / 6) (saturating); y = e2m1(clamp(x / s, -6, 6)) s."""
-    shp = x.shape
-    b = x.float().reshape(*shp[:-1], shp[-1] // block, block)
+def _blocks(x: torch.Tensor, block: int) -> torch.Tensor:
+    return x.float().unflatten(-1, (x.shape[-1] // block, block))
+
+
+def fp8_qdq(x: torch.Tensor, block: int = 32) -> torch.Tensor:
+    """x rounded onto the FP8 grid with one power-of-two scale per `block` values (x's dtype)."""
+    b = _blocks(x, block)
+    s = pow2_ceil(b.abs().amax(-1, keepdim=True).clamp_min(1e-4) * RECIP_E4M3_MAX)
+    return (e4m3(b / s) * s).flatten(-2).to(x.dtype)
+
+
+def fp4_qdq(x: torch.Tensor, block: int, scale: str = "pow2") -> torch.Tensor:
+    """x rounded onto the FP4 grid with one scale per `block` values: `pow2` (E8M0) or `e4m3` scales."""
+    b = _blocks(x, block)
     amax = b.abs().amax(-1, keepdim=True)
-    if scale == "e8m0":
-        s = _pow2_at_least(amax.clamp_min(6 * 2.0 ** -126) * _INV_FP4)
+    if scale == "pow2":
+        s = pow2_ceil(amax.clamp_min(E2M1_MAX * 2.0 ** -126) * RECIP_E2M1_MAX)
     elif scale == "e4m3":
-        s = _round_e4m3(amax.clamp_min(6 * 2.0 ** -9) / _FP4_MAX)
+        s = e4m3(amax.clamp_min(E2M1_MAX * 2.0 ** -9) / E2M1_MAX)
     else:
-        raise ValueError(scale)
-    return (_round_e2m1((b / s).clamp(-_FP4_MAX, _FP4_MAX)) * s).reshape(shp).to(x.dtype)
+        raise ValueError(f"unknown FP4 scale kind {scale!r}")
+    return (e2m1((b / s).clamp(-E2M1_MAX, E2M1_MAX)) * s).flatten(-2).to(x.dtype)
 
 
-# ---------------------------------------------------------------------------- elementwise
+# ---------------------------------------------------------------------------- row transforms
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     xf = x.float()
-    xf = xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
-    return (w.float() * xf).to(x.dtype)
+    inv = (xf.square().mean(-1, keepdim=True) + eps).rsqrt()
+    return (xf * inv * w.float()).to(x.dtype)
 
 
-def rope(x: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor, inverse: bool = False) -> torch.Tensor:
-    """Rotate the last 2 len(freqs) dims of x [T, ..., D] (adjacent pairs as complex numbers) by
-    position * freq (fp32 angles, complex64 product), one rounding to x's dtype."""
-    rd = 2 * freqs.numel()
-    ang = positions.float().unsqueeze(-1) * freqs.float()
-    cis = torch.polar(torch.ones_like(ang), ang)
+def rotate(x: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor, inverse: bool = False) -> torch.Tensor:
+    """RoPE on the last 2 len(freqs) dims of x [T, ..., D]: dims (2i, 2i + 1) of that tail turn by the
+    fp32 angle position * freqs[i] (clockwise when `inverse`), evaluated in fp64 and rounded once to
+    x's dtype."""
+    n = freqs.numel()
+    ang = (positions.float()[:, None] * freqs.float()[None]).double()  # fp32 product, then exact
+    c, s = torch.cos(ang).float().double(), torch.sin(ang).float().double()  # fp32 cos / sin
     if inverse:
-        cis = cis.conj()
-    cis = cis.view((positions.shape[0],) + (1,) * (x.dim() - 2) + (rd // 2,))
-    tail = torch.view_as_complex(x[..., -rd:].float().reshape(*x.shape[:-1], rd // 2, 2).contiguous())
-    out = x.clone()
-    out[..., -rd:] = torch.view_as_real(tail * cis).flatten(-2).to(x.dtype)
-    return out
+        s = -s
+    shape = (positions.shape[0],) + (1,) * (x.dim() - 2) + (n,)
+    c, s = c.view(shape), s.view(shape)
+    tail = x[..., -2 * n:].double().unflatten(-1, (n, 2))
+    re, im = tail[..., 0], tail[..., 1]
+    turned = torch.stack((re * c - im * s, re * s + im * c), -1).flatten(-2)
+    return torch.cat((x[..., :-2 * n], turned.to(x.dtype)), -1)
 
 
-# ---------------------------------------------------------------------------- KV rows
-def window_rows(kv: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-    """Cached window rows of kv [T, 512] (bf16, pre-RoPE)."""
-    return qdq_fp8(rope(kv, positions, freqs), 32)
+def window_kv(kv: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """The cached window row of each token: its kv row [T, 512] rotated by its position, FP8 per 32."""
+    return fp8_qdq(rotate(kv, positions, freqs), 32)
 
 
-def pool_pair(prev: torch.Tensor, cur: torch.Tensor, norm_w: torch.Tensor, eps: float) -> torch.Tensor:
-    """Ratio-2 group latent from the group's two fp32 [kv | score] rows [n, 2 d]."""
-    d = prev.shape[-1] // 2
-    kv = torch.stack((prev[..., :d], cur[..., :d]), -2)
-    sc = torch.stack((prev[..., d:], cur[..., d:]), -2)
-    pooled = (kv * sc.softmax(-2)).sum(-2)
+def pooled_pair(first: torch.Tensor, second: torch.Tensor, norm_w: torch.Tensor, eps: float) -> torch.Tensor:
+    """Ratio-2 group latent from its two tokens' fp32 [kv | score] rows [n, 2 d]: per channel the kv
+    values weighted by softmax over the two scores, rounded to bf16, RMS-normalised."""
+    d = first.shape[-1] // 2
+    a, b = first[..., d:].float(), second[..., d:].float()
+    top = torch.maximum(a, b)
+    ea, eb = torch.exp(a - top), torch.exp(b - top)
+    pooled = (first[..., :d].float() * ea + second[..., :d].float() * eb) / (ea + eb)
     return rms_norm(pooled.to(torch.bfloat16), norm_w, eps)
 
 
-def compressed_rows(latent: torch.Tensor, group_pos: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-    return qdq_fp4(rope(latent, group_pos, freqs), 16, "e4m3")
+def compressed_kv(latent: torch.Tensor, group_pos: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """A closed group's attention row: its latent rotated by the group's first position, FP4 with
+    E4M3 scales per 16."""
+    return fp4_qdq(rotate(latent, group_pos, freqs), 16, "e4m3")
 
 
-def index_key_rows(k: torch.Tensor, k_norm: torch.Tensor, freqs: torch.Tensor, group_pos: torch.Tensor,
-                   eps: float) -> torch.Tensor:
-    return qdq_fp4(rope(rms_norm(k, k_norm, eps), group_pos, freqs), 32, "e8m0")
+def index_key(k: torch.Tensor, k_norm: torch.Tensor, group_pos: torch.Tensor, freqs: torch.Tensor,
+              eps: float) -> torch.Tensor:
+    """A closed group's index key: RMS-normalised wk(latent), rotated, FP4 with power-of-two scales per 32."""
+    return fp4_qdq(rotate(rms_norm(k, k_norm, eps), group_pos, freqs), 32, "pow2")
 
 
-def index_query(q: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-    return qdq_fp4(rope(q, positions, freqs), 32, "e8m0")
+def index_q(q: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """The index query [T, H, 128]: rotated, FP4 with power-of-two scales per 32."""
+    return fp4_qdq(rotate(q, positions, freqs), 32, "pow2")
+
+
+def finish_output(o: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """The per-head attention output [T, h, 512] as wo_a reads it: tail rotated back, FP8 per 32 (the
+    32-value blocks never straddle two heads, so the qdq grouping of heads does not matter)."""
+    return fp8_qdq(rotate(o, positions, freqs, inverse=True), 32)
 
 
 # ---------------------------------------------------------------------------- indexer
-def index_scores(q: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_vis: torch.Tensor,
-                 heads_per_rank: int) -> torch.Tensor:
-    """q [n, H, D] bf16, w [n, H] bf16, keys [N, D] -> [n, N] fp32 (bf16 values), -inf past n_vis."""
-    return index_scores_rows(q, w, keys.unsqueeze(0).expand(q.shape[0], -1, -1), n_vis, heads_per_rank)
+def _bf16(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).float()
 
 
-def index_scores_rows(q: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_vis: torch.Tensor,
-                      heads_per_rank: int) -> torch.Tensor:
-    """index_scores with each query's own keys [n, N, D] (queries of different sequences)."""
-    bf = torch.bfloat16
-    s = torch.einsum("nhd,nkd->nhk", q.float(), keys.float()).to(bf).float().clamp_min(0)
-    s = (s * w.float().unsqueeze(-1)).to(bf).float()
-    total = None
-    for r0 in range(0, s.shape[1], heads_per_rank):
-        part = s[:, r0]
-        for h in range(r0 + 1, r0 + heads_per_rank):
-            part = part + s[:, h]
-        part = part.to(bf).float()
-        total = part if total is None else (total + part).to(bf).float()
-    cols = torch.arange(keys.shape[1], device=q.device)
-    return torch.where(cols[None] < n_vis[:, None], total, float("-inf"))
+def indexer_scores(qi: torch.Tensor, wi: torch.Tensor, keys: torch.Tensor, n_vis: torch.Tensor,
+                   heads_per_group: int) -> torch.Tensor:
+    """Scores [n, N] (fp32 holding bf16 values; -inf past each query's n_vis) of query i against its
+    own keys[i] [N, D]: qi [n, H, D], wi [n, H] (bf16), heads in rank groups of `heads_per_group`."""
+    n, H, _ = qi.shape
+    N = keys.shape[1]
+    terms = _bf16(torch.relu(_bf16(torch.matmul(qi.float(), keys.float().transpose(1, 2)))) * wi.float()[..., None])
+    groups = terms.view(n, H // heads_per_group, heads_per_group, N)
+    acc = groups[:, :, 0]
+    for j in range(1, heads_per_group):  # head order inside every rank group at once, fp32
+        acc = acc + groups[:, :, j]
+    per_rank = _bf16(acc)  # [n, R, N]
+    total = per_rank[:, 0]
+    for r in range(1, per_rank.shape[1]):  # the all-reduce: rank order, bf16 after each addition
+        total = _bf16(total + per_rank[:, r])
+    visible = torch.arange(N, device=qi.device)[None] < n_vis[:, None]
+    return total.masked_fill(~visible, float("-inf"))
 
 
-def topk_canonical(scores: torch.Tensor, n_vis: torch.Tensor, k: int) -> torch.Tensor:
-    """min(k, n_vis) best columns per row (score desc, index asc), sorted ascending, -1 padded."""
-    n, N = scores.shape
-    dev = scores.device
-    out = torch.full((n, k), -1, dtype=torch.int32, device=dev)
+def _order_keys(scores: torch.Tensor) -> torch.Tensor:
+    """int64 keys whose ascending order is (score descending, column ascending)."""
+    # + 0.0 turns -0.0 into +0.0: the two zeros are one score (a tie broken by column)
+    bits = (scores.float() + 0.0).contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    # fp32 bit patterns -> unsigned integers that grow with the value (negatives reversed)
+    ordered = torch.where(bits >= 0x80000000, 0xFFFFFFFF - bits, bits | 0x80000000)
+    col = torch.arange(scores.shape[-1], device=scores.device, dtype=torch.int64)
+    return ((0xFFFFFFFF - ordered) << 31) | col  # columns < 2^31
+
+
+def _best_ascending(keys: torch.Tensor, count: torch.Tensor, k: int) -> torch.Tensor:
+    """Per row the columns of the min(k, count) smallest keys, ascending, -1 padded to k."""
+    n, N = keys.shape
+    out = torch.full((n, k), -1, dtype=torch.int32, device=keys.device)
     w = min(k, N)
     if n == 0 or w == 0:
         return out
-    cols = torch.arange(N, device=dev)
-    sc = torch.where(cols[None] < n_vis[:, None], scores, float("-inf"))
-    order = torch.sort(sc, dim=-1, descending=True, stable=True).indices[:, :w]
-    keep = torch.arange(w, device=dev)[None] < n_vis[:, None]
-    picked = torch.sort(torch.where(keep, order, N), -1).values
-    out[:, :w] = torch.where(picked == N, -1, picked).to(torch.int32)
+    cols = torch.topk(keys, w, dim=-1, largest=False, sorted=True).values & 0x7FFFFFFF
+    taken = torch.arange(w, device=keys.device)[None] < count[:, None]
+    cols = torch.sort(torch.where(taken, cols, N), -1).values
+    out[:, :w] = torch.where(cols == N, -1, cols).to(torch.int32)
     return out
 
 
-def candidate_blocks(scores: torch.Tensor, n_vis: torch.Tensor, topk_blocks: int, block: int) -> torch.Tensor:
-    """Blocks of `block` groups scored by their best group; the block of the newest visible group
-    pinned in; the best `topk_blocks` reachable blocks, sorted ascending, -1 padded."""
-    n, N = scores.shape
-    pad = -N % block
-    b = torch.nn.functional.pad(scores, (0, pad), value=float("-inf")).reshape(n, -1, block).amax(-1)
-    nb = b.shape[1]
-    last = torch.div(n_vis - 1, block, rounding_mode="floor")
-    b = b.masked_fill(torch.arange(nb, device=scores.device)[None] == last[:, None], float("inf"))
-    out = torch.full((n, topk_blocks), -1, dtype=torch.int32, device=scores.device)
-    w = min(topk_blocks, nb)
-    if n == 0 or w == 0:
-        return out
-    top = torch.sort(b, dim=-1, descending=True, stable=True)
-    ids = torch.where(top.values[:, :w] > float("-inf"), top.indices[:, :w], nb)
-    ids = torch.sort(ids, -1).values
-    out[:, :w] = torch.where(ids == nb, -1, ids).to(torch.int32)
-    return out
+def select_topk(scores: torch.Tensor, n_vis: torch.Tensor, k: int) -> torch.Tensor:
+    """The chosen groups per query: the min(k, n_vis) best visible columns, ascending, -1 padded."""
+    keys = _order_keys(scores)
+    N = scores.shape[-1]
+    visible = torch.arange(N, device=scores.device)[None] < n_vis[:, None]
+    keys = torch.where(visible, keys, torch.iinfo(torch.int64).max)
+    return _best_ascending(keys, n_vis.clamp(0, N), k)
 
 
-def mask_to_candidates(scores: torch.Tensor, cands: torch.Tensor, block: int) -> torch.Tensor:
+def pick_blocks(scores: torch.Tensor, n_vis: torch.Tensor, topk_blocks: int, block: int) -> torch.Tensor:
+    """Blocks of `block` groups ranked by their best score (the newest visible group's block first),
+    the best `topk_blocks` among blocks holding a visible group, ascending, -1 padded."""
     n, N = scores.shape
     nb = -(-N // block)
-    keep = torch.zeros(n, nb + 1, dtype=torch.bool, device=scores.device)
-    ids = torch.where((cands >= 0) & (cands < nb), cands, nb).long()
-    keep.scatter_(1, ids, True)
-    keep = keep[:, :nb].repeat_interleave(block, 1)[:, :N]
-    return torch.where(keep | (scores == float("-inf")), scores, -FLT_MAX)
+    padded = torch.full((n, nb * block), float("-inf"), device=scores.device)
+    padded[:, :N] = scores
+    best = padded.view(n, nb, block).amax(-1)
+    newest = torch.div(n_vis - 1, block, rounding_mode="floor")
+    best = torch.where(torch.arange(nb, device=scores.device)[None] == newest[:, None], float("inf"), best)
+    reachable = torch.div(n_vis + block - 1, block, rounding_mode="floor")
+    keys = torch.where(torch.arange(nb, device=scores.device)[None] < reachable[:, None], _order_keys(best),
+                       torch.iinfo(torch.int64).max)
+    return _best_ascending(keys, reachable, topk_blocks)
+
+
+def restrict_to_blocks(scores: torch.Tensor, blocks: torch.Tensor, block: int) -> torch.Tensor:
+    """Scores with every visible group outside the listed blocks (-1 = none) set to -FLT_MAX."""
+    col_block = torch.arange(scores.shape[-1], device=scores.device) // block
+    member = (blocks.long()[:, :, None] == col_block[None, None, :]).any(1)
+    return torch.where(member | torch.isneginf(scores), scores, NEG_FLT_MAX)
 
 
 # ---------------------------------------------------------------------------- attention
-def sparse_attention(q: torch.Tensor, rows: torch.Tensor, valid: torch.Tensor, sink: torch.Tensor,
+def attend_with_sink(q: torch.Tensor, rows: torch.Tensor, valid: torch.Tensor, sink: torch.Tensor,
                      scale: float) -> torch.Tensor:
-    """q [n, h, d], rows [n, R, d] (K = V), valid [n, R] -> [n, h, d] bf16."""
-    s = torch.einsum("nhd,nrd->nhr", q.float(), rows.float()) * scale
-    s = s.masked_fill(~valid[:, None, :], float("-inf"))
-    m = s.amax(-1, keepdim=True)
-    m = torch.where(torch.isfinite(m), m, torch.full_like(m, -1e30))
-    p = torch.exp(s - m)
-    den = p.sum(-1) + torch.exp(sink[None, :].float() - m.squeeze(-1))
-    o = torch.einsum("nhr,nrd->nhd", p.to(torch.bfloat16).float(), rows.float())
-    return (o / den.unsqueeze(-1)).to(torch.bfloat16)
-
-
-def output_qdq(o: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor, n_groups: int) -> torch.Tensor:
-    n, h, d = o.shape
-    o = rope(o, positions, freqs, inverse=True)
-    return qdq_fp8(o.reshape(n, n_groups, (h // n_groups) * d), 32).reshape(n, h, d)
+    """q [n, h, d] over rows [n, R, d] (K = V; valid [n, R]) with a per-head sink [h] -> [n, h, d] bf16."""
+    logits = torch.matmul(q.float(), rows.float().transpose(1, 2)) * scale  # [n, h, R]
+    logits = logits.masked_fill(~valid[:, None, :], float("-inf"))
+    has = valid.any(-1)
+    top = torch.where(has[:, None], logits.amax(-1), 0.0)  # [n, h]; any finite value without rows
+    e = torch.exp(logits - top[..., None])
+    den = e.sum(-1) + torch.exp(sink.float()[None] - top)
+    out = torch.matmul(_bf16(e), rows.float()) / den[..., None]
+    return torch.where(has[:, None, None], out, 0.0).to(torch.bfloat16)
