@@ -127,6 +127,8 @@ def main():
     ap.add_argument("--prefill-chunk", type=int, default=16384)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
+    ap.add_argument("--no-sp", action="store_true", help="expert parallel with replicated tokens and all-reduces "
+                                                        "instead of the sequence-parallel layout")
     ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
     ap.add_argument("--eager", action="store_true", help="no CUDA graphs (debugging)")
     ap.add_argument("--ep", action="store_true", help="(default for N > 1) routed experts split whole over the "
@@ -188,7 +190,7 @@ def main():
     total_len = args.prompt + args.output + 64
     cfg = EngineConfig(model=model_cfg,
                        parallel=ParallelConfig(tensor_parallel_size=args.gpus, fused_comm=not args.nccl_baseline,
-                                               expert_parallel=args.ep),
+                                               expert_parallel=args.ep, sequence_parallel=not args.no_sp),
                        scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
                                                  max_model_len=total_len, max_num_partial_prefills=args.batch),
                        cache=CacheConfig(num_blocks=args.batch * ((total_len + 63) // 64) + 1),
@@ -203,6 +205,12 @@ def main():
             fused = symm.enable_for_engine(engine)
         except ImportError:
             fused = False
+    from vllm_cmp170hx_b200.parallel import comm as pcomm
+
+    spt = pcomm._FUSED["sp"]
+    layout = ("sequence-parallel (all-gather + reduce-scatter around attention, dispatch / combine around the "
+              "experts)" if spt is not None else "replicated tokens (all-reduce)")
+    transport = ("fused NVLink peer-store kernels" if (fused and (spt is None or spt.fused)) else "NCCL")
     torch.cuda.synchronize()
     t_load = time.time() - t0
     g = torch.Generator().manual_seed(args.seed)
@@ -270,7 +278,7 @@ def main():
                        "global_batch": args.batch, "seq_len": args.prompt, "output_len": args.output,
                        "parallelism": (f"ep{args.gpus}+attn-tp{args.gpus}" if args.ep and args.gpus > 1
                                        else f"tp{args.gpus}"),
-                       "collectives": "fused symmetric-memory kernels" if fused else ("none" if args.gpus == 1 else "nccl"),
+                       "collectives": ("none" if args.gpus == 1 else f"{transport}; {layout}"),
                        "l2": "no flush: each step streams the expert weights (GBs per GPU) >> 126 MB L2"},
             "p50_tpot_ms": round(statistics.median(e2e_ms), 3),
             "clocks": clocks,

@@ -1,0 +1,229 @@
+"""Sequence-parallel collectives on 2+ GPUs (this package's kernels over NVLink peer memory):
+
+* all-gather into the next GEMM, reduce-scatter out of a GEMM, router top-k + dispatch to the experts'
+  ranks and the combine back, each against a float reference of the same data movement, over several
+  calls of different sizes (call numbers, flags);
+* the tiny expert-parallel hybrid model generating the same greedy tokens at TP=2 (sequence-parallel
+  layout on the fused kernels, decode steps replayed from CUDA graphs) as on one GPU.
+
+Every wait in the kernels is bounded; NVLS is off (plain peer stores only)."""
+
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
+
+
+def _rms(x, w, eps=1e-6):
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps) * w.float()).to(torch.bfloat16)
+
+
+def _kernel_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from vllm_cmp170hx_b200 import _ext, ops
+    from vllm_cmp170hx_b200.parallel import comm
+    from vllm_cmp170hx_b200.parallel import state as pstate
+    from vllm_cmp170hx_b200.parallel.sp import FusedSP, scope
+
+    try:
+        st = pstate.init(tp_size=world, timeout_s=60)
+        H, K, E, k = 512, 384, 8 * world, 4
+        sp = FusedSP(st.tp_group, st.tp_cpu_group, st.device, H, k, max_tokens=256, timeout_s=5.0)
+        errs = []
+
+        def step(it, T):
+            Tr = sp.begin(T)
+            g = torch.Generator().manual_seed(1000 * it)
+            xs = torch.randn(T, H, generator=g).to(torch.bfloat16)
+            wn = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+            Wq = [(torch.randn(K, H, generator=g) * H ** -0.5).to(torch.bfloat16) for _ in range(world)]
+            Wo = [(torch.randn(H, K, generator=g) * K ** -0.5).to(torch.bfloat16) for _ in range(world)]
+            logits = torch.randn(T, E, generator=g)
+            add = torch.randn(T, H, generator=g).to(torch.bfloat16)
+            dev = st.device
+            mine = slice(rank * Tr, (rank + 1) * Tr)
+            res = torch.empty(Tr, H, dtype=torch.bfloat16, device=dev)
+            # 1. residual <- x, norm, all-gather; the projection GEMM waits for the gather itself
+            sp.norm("local", res, wn.to(dev), 1e-6, x=xs[mine].to(dev).contiguous(), ag=True)
+            with scope(sp):
+                a = ops.gemm(sp.gathered(), Wq[rank].to(dev))
+            h_all = _rms(xs, wn)
+            errs.append(_rel(a.cpu(), h_all.float() @ Wq[rank].float().t()))
+            # 2. row-parallel output, reduce-scattered; the norm sums the pushed rows into the residual
+            with scope(sp):
+                assert comm.gemm_all_reduce(a, Wo[rank].to(dev), None) is None
+            h = torch.empty_like(res)
+            sp.norm("rs", res, wn.to(dev), 1e-6, out=h)
+            a_ref = [(h_all.float() @ Wq[r].float().t()).to(torch.bfloat16) for r in range(world)]
+            o_ref = sum(ar.float() @ Wo[r].float().t() for r, ar in enumerate(a_ref)).to(torch.bfloat16)
+            r_ref = (xs.float() + o_ref.float()).to(torch.bfloat16)
+            errs.append(_rel(res.cpu(), r_ref[mine]))
+            # 3. route + dispatch, received rows, combine back (partial = rows scaled by picked experts)
+            sp.route_dispatch(logits[mine].to(dev).contiguous(), h, k, 0, None, 1.0, True, E // world)
+            x_r, ids_r, w_r = sp.dispatch_recv()
+            TK = T * k
+            i32 = dict(dtype=torch.int32, device=dev)
+            sp.build_assignments(ids_r, w_r, None, E, 16, torch.empty(TK, **i32),
+                                 torch.empty(TK, dtype=torch.float32, device=dev), torch.empty(TK, **i32),
+                                 torch.empty(E + TK, 4, **i32), torch.empty(1, **i32), torch.empty(E + 1, **i32))
+            scale = (ids_r.float() + 1) * w_r * (ids_r >= 0).float()
+            partial = x_r.float() * scale.sum(1, keepdim=True)
+            sp.combine_partial(partial)
+            sp.norm("comb", res, wn.to(dev), 1e-6, add=add[mine].to(dev).contiguous(), out=h)
+            torch.cuda.synchronize()
+            # reference: router over all tokens, every pick's (e + 1) w summed
+            p = torch.softmax(logits, -1)
+            top = torch.topk(p, k, -1)
+            wts = top.values / top.values.sum(-1, keepdim=True)
+            h_ref = _rms(r_ref, wn)
+            moe = (h_ref.float() * ((top.indices.float() + 1) * wts).sum(1, keepdim=True)).to(torch.bfloat16)
+            # the kernel sums bf16 partials of the ranks plus `add` in fp32, then rounds once
+            r2 = (r_ref.float() + (moe.float() + add.float()).to(torch.bfloat16).float()).to(torch.bfloat16)
+            errs.append(_rel(res.cpu(), r2[mine]))
+
+        for it, T in enumerate([8 * world, 16 * world, 2 * world, 32 * world]):
+            step(it, T)
+        _ext.check_status(st.device)
+        q.put((rank, errs))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, repr(e) + traceback.format_exc()))
+    finally:
+        pstate.destroy()
+
+
+def _run(target, world, port, timeout=600):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=timeout) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
+def test_sp_collectives_match_reference():
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    world = min(world, 8)
+    res = _run(_kernel_worker, world, 28100 + os.getpid() % 400)
+    for r in range(world):
+        assert not isinstance(res[r], str), res[r]
+        assert max(res[r]) < 3e-2, res[r]
+
+
+PROMPTS = [[(11 * i + 3 * j) % 900 for j in range(20 + 7 * i)] for i in range(8)]
+
+
+def _cfg(tp):
+    from vllm_cmp170hx_b200.config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, tiny
+
+    m = tiny(layers=4, experts=8, hidden=256, expert_format="exl3")
+    m.moe.intermediate = 256
+    m.moe.shared_intermediate = 256
+    return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp, expert_parallel=tp > 1),
+                        scheduler=SchedulerConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=256),
+                        cache=CacheConfig(num_blocks=64), device="cuda", cuda_graph_batch_sizes=[2, 4, 8])
+
+
+def _generate(tp, fused):
+    """Greedy tokens, and the full-vocabulary logits of the first three steps (gathered over the vocab
+    shards) of the tiny expert-parallel model."""
+    import torch.distributed as dist
+
+    from vllm_cmp170hx_b200.engine.llm_engine import LLM
+    from vllm_cmp170hx_b200.engine.request import SamplingParams
+    from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+    from vllm_cmp170hx_b200.parallel import comm
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    cfg = _cfg(tp)
+    pstate.get().expert_parallel = cfg.parallel.expert_parallel
+    model = HybridForCausalLM(cfg.model, "cuda", seed=5, init_mode="sliced")
+    seen = []
+    orig = model.compute_logits
+
+    def recording(hidden):
+        out = orig(hidden)
+        if len(seen) < 3:
+            full = out
+            if tp > 1:
+                parts = [torch.empty_like(out) for _ in range(tp)]
+                dist.all_gather(parts, out.contiguous(), group=pstate.get().tp_group)
+                full = torch.cat(parts, -1)
+            seen.append(full.float().cpu())
+        return out
+
+    model.compute_logits = recording
+    llm = LLM(cfg, model)
+    if fused and tp > 1:
+        from vllm_cmp170hx_b200.parallel import symm
+
+        assert symm.enable_for_engine(llm.engine)
+        assert comm._FUSED["sp"] is not None and comm._FUSED["sp"].fused
+    outs = llm.generate(PROMPTS, SamplingParams(max_tokens=6))
+    return [o.output_token_ids for o in outs], seen
+
+
+def _engine_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from vllm_cmp170hx_b200 import _ext
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    try:
+        st = pstate.init(tp_size=world, timeout_s=60)
+        toks = _generate(world, True)
+        _ext.check_status(st.device)
+        q.put((rank, toks))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, repr(e) + traceback.format_exc()))
+    finally:
+        pstate.destroy()
+
+
+def test_sp_engine_tp2_matches_one_gpu():
+    """The first three steps' logits (a 256-token and a 100-token prefill chunk and a decode step, all in
+    the sequence-parallel layout at TP=2) agree with one GPU's to bf16 rounding of the partial sums, and
+    greedy decoding gives the same tokens except where two logits are that close."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 or more GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_single, args=(q,))
+    p.start()
+    ref = q.get(timeout=600)
+    p.join(timeout=60)
+    assert not isinstance(ref, str), ref
+    res = _run(_engine_worker, 2, 27700 + os.getpid() % 400)
+    assert not isinstance(res[0], str), res[0]
+    toks, logits = res[0]
+    ref_toks, ref_logits = ref
+    assert len(logits) == len(ref_logits) == 3
+    for a, b in zip(logits, ref_logits):
+        assert a.shape == b.shape
+        assert _rel(a, b) < 5e-2, _rel(a, b)
+    same = sum(x == y for x, y in zip(toks, ref_toks))
+    assert same >= len(ref_toks) - 2, (toks, ref_toks)
+
+
+def _single(q):
+    try:
+        q.put(_generate(1, False))
+    except Exception as e:  # noqa: BLE001
+        q.put(repr(e))

@@ -133,3 +133,58 @@ def test_emulated_tp_runs_per_rank_shapes(fmt):
         assert st.emulated and pstate.get().tp_size == 2
     finally:
         pstate.set_state(pstate.ParallelState())
+
+
+def _sp_worker(rank, world, port, fmt, path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from vllm_cmp170hx_b200.engine.llm_engine import LLM
+    from vllm_cmp170hx_b200.engine.request import SamplingParams
+    from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.init(tp_size=world, device="cpu", timeout_s=120)
+    cfg = _cfg(world, fmt)
+    pstate.get().expert_parallel = True
+    model = HybridForCausalLM(cfg.model, "cpu", seed=5, init_mode="sliced")
+    calls = {"sp": 0}
+    orig = HybridForCausalLM._forward_sp
+
+    def counted(self, *a, **k):
+        calls["sp"] += 1
+        return orig(self, *a, **k)
+
+    HybridForCausalLM._forward_sp = counted
+    outs = LLM(cfg, model).generate(SP_PROMPTS, SamplingParams(max_tokens=4))
+    if rank == 0:
+        with open(path, "w") as f:
+            json.dump({"toks": [o.output_token_ids for o in outs], "sp_steps": calls["sp"]}, f)
+    pstate.destroy()
+
+
+SP_PROMPTS = [[(7 * i + 5 * j) % 500 for j in range(6 + 3 * i)] for i in range(4)]
+
+
+@pytest.mark.parametrize("fmt", ["exl3_ep", "bf16_ep"])
+def test_sequence_parallel_ep_matches_tp1(fmt):
+    """Expert parallel at TP=2 in the sequence-parallel layout (token-sharded residual stream: all-gather
+    before attention, reduce-scatter after it, dispatch to the experts' ranks and combine back), over
+    torch.distributed on gloo: the same greedy tokens as one rank, with the layout actually taken by
+    the steps whose token count divides over the ranks."""
+    from vllm_cmp170hx_b200.engine.llm_engine import LLM
+    from vllm_cmp170hx_b200.engine.request import SamplingParams
+    from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    cfg = _cfg(1, fmt)
+    model = HybridForCausalLM(cfg.model, "cpu", seed=5, init_mode="sliced")
+    ref = [o.output_token_ids for o in LLM(cfg, model).generate(SP_PROMPTS, SamplingParams(max_tokens=4))]
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.json")
+        port = 27300 + os.getpid() % 1000
+        mp.start_processes(_sp_worker, args=(2, port, fmt, path), nprocs=2, join=True, start_method="spawn")
+        with open(path) as f:
+            got = json.load(f)
+    assert got["sp_steps"] >= 3, got
+    assert got["toks"] == ref

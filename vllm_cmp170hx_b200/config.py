@@ -266,6 +266,9 @@ class ParallelConfig:
     pipeline_parallel_size: int = 1
     expert_parallel: bool = False  # experts split whole across ranks (else TP-split experts)
     fused_comm: bool = True  # product path: fused GEMM+collective kernels; False = NCCL baseline
+    # with expert parallelism: steps whose tokens divide over the group keep the residual stream sharded
+    # by tokens (all-gather / reduce-scatter around attention, dispatch / combine around the experts)
+    sequence_parallel: bool = True
 
     @property
     def world_size(self) -> int:

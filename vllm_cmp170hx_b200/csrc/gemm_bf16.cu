@@ -24,6 +24,7 @@
 #include <algorithm>
 
 #include "launch.h"
+#include "sp_sync.cuh"
 #include "tma_host.h"
 
 namespace b200 {
@@ -69,7 +70,47 @@ struct Params {
   int64_t flag_off, data_off, tile_bytes;
   uint32_t* epochs;  // [gridDim.x] per-CTA call counters (this rank)
   uint64_t timeout_ns;
+  // Sequence-parallel collectives (sp_sync.cuh): 1 = reduce-scatter, every output token row pushed to
+  // its owner rank (token / sp_rows) at row (rank, token % sp_rows) of the area at sp_rs_off, C unused;
+  // 2 = all-gather, the activation operand (B when act_is_b, else A) is read only after every rank's
+  // all-gather flag arrived; the weight tiles of the first stages stream meanwhile.
+  int sp_mode;
+  SpSync sp;
+  int64_t sp_rs_off;
+  int sp_rows;
+  int act_is_b;
 };
+
+// Destination of output row `tok` (a token), columns from `feat`, in the reduce-scatter mode.
+__device__ __forceinline__ __nv_bfloat16* rs_dst(const Params& p, int tok, int feat, int feats) {
+  const int owner = tok / p.sp_rows;
+  const int lt = tok - owner * p.sp_rows;
+  return reinterpret_cast<__nv_bfloat16*>(p.sp.peers[owner] + p.sp_rs_off) +
+         (size_t)(p.sp.rank * p.sp_rows + lt) * feats + feat;
+}
+
+// All-gather mode of the producer: loads of the activation operand of the first stages wait here until
+// every rank's flag arrived.  `pend` holds (stage, k block, m tile, n tile) of deferred loads.
+struct AgGate {
+  bool open;
+  uint32_t e;
+  int n;
+  int pend[8][4];
+};
+
+__device__ __forceinline__ void ag_release(AgGate& g, const Params& p, const CUtensorMap* act_map, uint8_t* smem_act,
+                                           int act_bytes, uint64_t* full, int act_rows) {
+  if (!g.open) return;
+  for (int src = 0; src < p.sp.world; ++src) sp_wait_flag(p.sp, kSpAllGather, g.e, src);
+  asm volatile("fence.proxy.async.global;" ::: "memory");  // peer stores (generic) -> TMA reads (async)
+  for (int i = 0; i < g.n; ++i) {
+    const int st = g.pend[i][0], kb = g.pend[i][1];
+    const int row0 = p.act_is_b ? g.pend[i][3] * act_rows : g.pend[i][2] * act_rows;
+    tma_load_2d(smem_act + st * act_bytes, act_map, &full[st], kb * BK, row0);
+  }
+  g.n = 0;
+  g.open = false;
+}
 
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* ptr, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
@@ -107,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* s_epoch = tmem_slot + 2;
+  uint32_t* s_ag_epoch = tmem_slot + 3;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -144,8 +186,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // bf16 output, transposed: staged in smem, written as 16-byte runs of features (a token's row)
+  const bool rs = p.sp_mode == 1;
   const bool staged_out = C_::OUT_BYTES > 0 && p.transpose_out && !p.ar && p.splits == 1 && p.Cf == nullptr &&
-                          (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 && (p.ldc & 7) == 0;
+                          (rs || ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0 && (p.ldc & 7) == 0));
 
   const int tiles_mn = p.m_tiles * p.n_tiles;
   const int total = tiles_mn * p.splits;
@@ -158,6 +201,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
+      // the call number is read after the programmatic-launch wait (the previous kernel has completed);
+      // thread 0 reads it back from shared memory for the arrival at the end of the kernel
+      AgGate gate;
+      gate.open = p.sp_mode == 2;
+      gate.e = gate.open ? sp_recv_epoch(p.sp, kSpAllGather) : 0u;
+      gate.n = 0;
+      if (gate.open) *s_ag_epoch = gate.e;
+      const CUtensorMap* act_map = p.act_is_b ? &tma_b : &tma_a;
+      uint8_t* act_smem = p.act_is_b ? smem_b : smem_a;
+      const int act_bytes = p.act_is_b ? C_::B_BYTES : C_::A_BYTES;
+      const int act_rows = p.act_is_b ? BN : BM;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const int split = t / tiles_mn;
         const int mn = t % tiles_mn;
@@ -171,8 +225,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
-          tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
-          tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+          if (gate.open) {
+            // weights now, the activation tile once the all-gather landed
+            if (p.act_is_b)
+              tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
+            else
+              tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+            gate.pend[gate.n][0] = stage;
+            gate.pend[gate.n][1] = kb;
+            gate.pend[gate.n][2] = mt;
+            gate.pend[gate.n][3] = nt;
+            if (++gate.n == S || gate.n == 8) ag_release(gate, p, act_map, act_smem, act_bytes, full, act_rows);
+          } else {
+            tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
+            tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+          }
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -180,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      ag_release(gate, p, act_map, act_smem, act_bytes, full, act_rows);  // fewer k blocks than stages
       if (!ok) {
         *abort_flag = 1;
         // Drain: the most recent load of every stage must land before exit.
@@ -287,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col = nt * BN + n, f0 = mt * BM + g * 8;
             if (col >= p.N || f0 >= p.M) continue;
             const uint8_t* src = smem_out + n * (BM * 2) + g * 16;
-            __nv_bfloat16* dst = p.C + (size_t)col * p.ldc + f0;
+            __nv_bfloat16* dst = rs ? rs_dst(p, col, f0, p.M) : p.C + (size_t)col * p.ldc + f0;
             if (f0 + 8 <= p.M) {
               *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
             } else {
@@ -357,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (col < p.N) p.C[(size_t)col * p.ldc + row] = __float2bfloat16(__uint_as_float(r[j]) + bias);
             }
           } else {
-            __nv_bfloat16* dst = p.C + (size_t)row * p.ldc + col0;
+            __nv_bfloat16* dst = rs ? rs_dst(p, row, col0, p.N) : p.C + (size_t)row * p.ldc + col0;
             if (col0 + 16 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) && p.bias == nullptr) {
               uint4 v0, v1;
               v0.x = pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1]));
@@ -445,9 +513,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (rs) __threadfence_system();  // this CTA's pushed rows before the arrival below
   tc_fence_before();
   __syncthreads();
   if (p.ar && threadIdx.x == 0) p.epochs[blockIdx.x] = *s_epoch;
+  if (threadIdx.x == 0) {
+    if (rs) sp_push_arrive(p.sp, kSpReduceScatter, gridDim.x);
+    if (p.sp_mode == 2) sp_recv_arrive(p.sp, kSpAllGather, gridDim.x, *s_ag_epoch);
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C_::TMEM_COLS);
@@ -498,10 +571,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = bars + 2 * S + 3;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* s_ag_epoch = tmem_slot + 2;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int splits = p.splits;
+  const bool rs = p.sp_mode == 1;
   const uint32_t rank = cluster_ctarank();
   const int mn = blockIdx.x / splits;
   const int mt = mn % p.m_tiles, nt = mn / p.m_tiles;
@@ -549,20 +624,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued = 0;
       bool ok = true;
+      // the call number is read after the programmatic-launch wait (the previous kernel has completed);
+      // thread 0 reads it back from shared memory for the arrival at the end of the kernel
+      AgGate gate;
+      gate.open = p.sp_mode == 2;
+      gate.e = gate.open ? sp_recv_epoch(p.sp, kSpAllGather) : 0u;
+      gate.n = 0;
+      if (gate.open) *s_ag_epoch = gate.e;
+      const CUtensorMap* act_map = p.act_is_b ? &tma_b : &tma_a;
+      uint8_t* act_smem = p.act_is_b ? smem_b : smem_a;
+      const int act_bytes = p.act_is_b ? C_::B_BYTES : C_::A_BYTES;
+      const int act_rows = p.act_is_b ? BN : BM;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
-        tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
-        tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+        if (gate.open) {
+          if (p.act_is_b)
+            tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
+          else
+            tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+          gate.pend[gate.n][0] = stage;
+          gate.pend[gate.n][1] = kb;
+          gate.pend[gate.n][2] = mt;
+          gate.pend[gate.n][3] = nt;
+          if (++gate.n == S) ag_release(gate, p, act_map, act_smem, act_bytes, full, act_rows);
+        } else {
+          tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
+          tma_load_2d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN);
+        }
         ++issued;
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
         }
       }
+      ag_release(gate, p, act_map, act_smem, act_bytes, full, act_rows);
       if (!ok) {
         *abort_flag = 1;
         const uint32_t n = issued < (uint32_t)S ? issued : (uint32_t)S;
@@ -653,7 +752,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nrow = min(4, min(r1 - (r0 + g * 4), p.M - grow0));
         if (p.bias)
           for (int k = 0; k < nrow; ++k) acc[k] += __bfloat162float(p.transpose_out ? p.bias[grow0 + k] : p.bias[col]);
-        if (p.transpose_out && p.Cf == nullptr && nrow == 4 && ((reinterpret_cast<uintptr_t>(p.C) & 7) == 0) &&
+        if (rs && p.transpose_out) {
+          // token `col`, features grow0.. of its owner's reduce-scatter row (p.M features)
+          __nv_bfloat16* d = rs_dst(p, col, grow0, p.M);
+          if (nrow == 4) {
+            uint2 v;
+            v.x = pack_bf16x2(acc[0], acc[1]);
+            v.y = pack_bf16x2(acc[2], acc[3]);
+            *reinterpret_cast<uint2*>(d) = v;
+          } else {
+            for (int k = 0; k < nrow; ++k) d[k] = __float2bfloat16(acc[k]);
+          }
+        } else if (rs) {
+          for (int k = 0; k < nrow; ++k) *rs_dst(p, grow0 + k, col, p.N) = __float2bfloat16(acc[k]);
+        } else if (p.transpose_out && p.Cf == nullptr && nrow == 4 && ((reinterpret_cast<uintptr_t>(p.C) & 7) == 0) &&
             (p.ldc & 3) == 0) {
           uint2 v;
           v.x = pack_bf16x2(acc[0], acc[1]);
@@ -672,10 +784,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // this CTA's parked groups must be read out before its shared memory goes away
     if (et == 0) bulk_wait_read_all();
+    if (rs) __threadfence_system();
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) {
+    if (rs) sp_push_arrive(p.sp, kSpReduceScatter, gridDim.x);
+    if (p.sp_mode == 2) sp_recv_arrive(p.sp, kSpAllGather, gridDim.x, *s_ag_epoch);
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C_::TMEM_COLS);
@@ -833,7 +950,7 @@ int gemm_bf16_splits(int M, int N, int K, int splits_req) {
   return (kb_total + per - 1) / per;
 }
 
-cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
+static cudaError_t gemm_bf16_impl(const GemmArgs& a, const GemmSpArgs* sp, cudaStream_t stream) {
   using namespace gemm;
   if (a.M == 0 || a.N == 0) return cudaSuccess;
   if (a.K % 8 != 0) return cudaErrorInvalidValue;
@@ -856,7 +973,16 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.m_tiles = (Ma + BM - 1) / BM;
   p.n_tiles = (Nb + bn - 1) / bn;
   const int kb_total = (a.K + BK - 1) / BK;
-  const int splits = gemm_bf16_splits(a.M, a.N, a.K, a.splits);
+  int splits = gemm_bf16_splits(a.M, a.N, a.K, a.splits);
+  if (sp != nullptr) {
+    // the reduce-scatter pushes finished output rows: no fp32 partial pass (cluster split-K is fine)
+    if (sp->mode == 1 && (splits > kMaxClusterSplits || (splits > 1 && (bn > 128 || a.M > 128)))) splits = 1;
+    p.sp_mode = sp->mode;
+    p.sp = sp->sp;
+    p.sp_rs_off = sp->rs_off;
+    p.sp_rows = sp->rows_per_rank;
+    p.act_is_b = swap ? 1 : 0;
+  }
   p.k_blocks_per_split = (kb_total + splits - 1) / splits;
   p.splits = splits;
   p.C = a.out_f32 ? nullptr : reinterpret_cast<__nv_bfloat16*>(a.c);
@@ -887,12 +1013,23 @@ cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     default: e = launch<256>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid); break;
   }
   if (e != cudaSuccess || splits == 1) return e;
-  // partial is [splits, M, N] in output orientation.
+  // partial is [splits, M, N] in output orientation (never in the reduce-scatter mode).
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>(((int64_t)a.M * a.N + threads - 1) / threads, (int64_t)sms * 8);
   launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(threads), 0, stream, p.partial, p.C, p.Cf, a.M, a.N, (int)a.ldc, splits,
                                                        reinterpret_cast<const __nv_bfloat16*>(a.bias), 0);
   return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) { return gemm_bf16_impl(a, nullptr, stream); }
+
+cudaError_t gemm_bf16_sp(const GemmSpArgs& a, cudaStream_t stream) {
+  const SpSync& s = a.sp;
+  if (a.mode < 1 || a.mode > 2 || s.peers == nullptr || s.state == nullptr || s.world < 1 || s.world > kSpMaxRanks ||
+      (a.mode == 1 && (a.rows_per_rank < 1 || a.g.M != a.rows_per_rank * s.world || a.g.bias != nullptr ||
+                       a.g.out_f32 || a.g.N % 8)))
+    return cudaErrorInvalidValue;
+  return gemm_bf16_impl(a.g, &a, stream);
 }
 
 cudaError_t gemm_bf16_allreduce(const GemmArArgs& a, cudaStream_t stream) {

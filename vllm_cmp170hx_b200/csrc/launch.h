@@ -12,6 +12,75 @@ namespace b200 {
 
 int device_sm_count();
 
+// ---------------------------------------------------------------- sequence-parallel collectives
+// Flag protocol: sp_sync.cuh.  Channels of the symmetric buffer's flag area flags[channel][src].
+enum SpChannel : int { kSpAllGather = 0, kSpReduceScatter = 1, kSpDispatch = 2, kSpCombine = 3, kSpChannels = 4 };
+constexpr int kSpMaxRanks = 32;
+constexpr int64_t kSpFlagBytes = 4096;  // flags[kSpChannels][kSpMaxRanks] uint32, padded
+
+struct SpSync {
+  const uint64_t* peers;  // [world] base address of every rank's symmetric buffer (this rank's included)
+  int rank, world;
+  uint32_t* state;        // [kSpChannels * 4] local: pushes, push arrivals, receives, receive arrivals
+  uint32_t* status;       // error word (kErrPeerTimeout)
+  uint64_t timeout_ns;
+};
+
+// sp_comm.cu.  Receive areas (byte offsets into every rank's symmetric buffer; row r of a [world * Tr]
+// area is token r % Tr of source rank r / Tr):
+//   all-gather [world * Tr, H] bf16, reduce-scatter [world * Tr, H] bf16, dispatch rows [world * Tr, H]
+//   bf16 + ids [world * Tr, k] int32 + weights [world * Tr, k] fp32, combine [world * Tr, H] bf16.
+struct SpNormArgs {
+  SpSync s;
+  int src;                       // 0: rows x (the residual starts as x), 1: reduce-scatter area, 2: combine area
+  const __nv_bfloat16* x;        // src 0: [Tr, ld_x]
+  int64_t ld_x;
+  const __nv_bfloat16* add;      // src 2: added to the combined rows (shared expert output [Tr, H]) or null
+  const uint32_t* dmask;         // src 2: [Tr] ranks that pushed a combine row for the token (bit per rank)
+  int64_t rs_off, comb_off, ag_off;
+  __nv_bfloat16* residual;       // [Tr, H]: src 0 writes x, else residual += reduced rows
+  const __nv_bfloat16* w;        // RMSNorm weight [H]
+  float eps;
+  __nv_bfloat16* out;            // normalised rows [Tr, ld_out] or null
+  int64_t ld_out;
+  int ag;                        // 1: push the normalised rows into every rank's all-gather area
+  int Tr, H;
+};
+cudaError_t sp_residual_norm(const SpNormArgs& a, cudaStream_t stream);
+
+struct SpDispatchArgs {
+  SpSync s;
+  const float* logits;           // [Tr, E] router logits
+  const __nv_bfloat16* h;        // [Tr, ld_h] the MoE input rows
+  int64_t ld_h;
+  int E, k, mode, renorm;
+  const float* bias;
+  float scale;
+  int e_per_rank;                // experts [d * e_per_rank, (d + 1) * e_per_rank) live on rank d
+  int64_t rows_off, ids_off, w_off;
+  uint32_t* dmask;               // [Tr] out: ranks this rank pushed each token to
+  int* ids_local;                // [Tr, k] out (optional): the picks, for diagnostics and tests
+  float* w_local;
+  int Tr, H;
+};
+cudaError_t sp_route_dispatch(const SpDispatchArgs& a, cudaStream_t stream);
+
+struct SpCombineArgs {
+  SpSync s;
+  const float* y;                // [assignments, ld_y] expert outputs
+  int64_t ld_y;
+  const int* slot_of;            // [world * Tr, k] assignment row of (received row, j), -1: none here
+  const float* sorted_weight;    // [assignments]
+  int k;
+  int64_t comb_off;              // area the rows go to (the combine area, or the reduce-scatter area)
+  int Tr, H;
+  int channel;                   // kSpCombine, or kSpReduceScatter for a row-parallel output already computed
+};
+cudaError_t sp_combine_push(const SpCombineArgs& a, cudaStream_t stream);
+
+// Waits for every source's latest push on `channel` (for consumers that are not a fused kernel).
+cudaError_t sp_wait(const SpSync& s, int channel, cudaStream_t stream);
+
 // ---------------------------------------------------------------- gemm_bf16.cu
 // C[M, N] = X[M, K] . W[N, K]^T (+ bias[N]); bf16 in/out, fp32 accumulate.
 // `partial` (fp32, >= splits * M * N elements) is required when splits > 1;
@@ -36,6 +105,20 @@ int gemm_bf16_splits(int M, int N, int K, int splits_req);
 // Whether a launch with this many splits needs the fp32 partial scratch (cluster-reduced splits do not).
 bool gemm_bf16_uses_partial(int M, int splits);
 cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream);
+
+// The same GEMM fused with a sequence-parallel collective (gemm_bf16.cu):
+//   mode 1 (reduce-scatter): row t of the output (a token) is pushed into rank t / rows_per_rank's
+//          reduce-scatter area at row (this rank, t % rows_per_rank); C is not written;
+//   mode 2 (all-gather): x is this rank's all-gather area; the kernel streams its first weight tiles
+//          while it waits for every rank's push, then reads x.
+struct GemmSpArgs {
+  GemmArgs g;
+  int mode;
+  SpSync sp;
+  int64_t rs_off;
+  int rows_per_rank;
+};
+cudaError_t gemm_bf16_sp(const GemmSpArgs& a, cudaStream_t stream);
 
 // GEMM fused with the tensor-parallel all-reduce over symmetric peer buffers (gemm_bf16.cu).
 struct GemmArArgs {
@@ -107,7 +190,7 @@ cudaError_t moe_topk(const float* logits, int T, int E, int k, int mode, const f
 cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, int k, const int* expert_map,
                                   int E_map, int E_local, int tile_rows, int* sorted_token, float* sorted_weight, int* slot_of,
                                   int4* items, int* num_items, int* expert_offsets, int max_items,
-                                  cudaStream_t stream);
+                                  cudaStream_t stream, const SpSync* sp = nullptr);
 
 // ---------------------------------------------------------------- exl3.cu
 struct Exl3GemmArgs {

@@ -111,6 +111,32 @@ void dequant_gemm_op(int64_t format, int64_t nmat, const at::Tensor& w0, const c
 void gather_rows_op(const at::Tensor& x, const c10::optional<at::Tensor>& src, at::Tensor& out,
                     int64_t rows);  // dequant_gemm.cu
 
+// sp_ops.cpp: sequence-parallel collectives (state = int32 [16] call counters, peers = int64 [world])
+void sp_residual_norm_op(const at::Tensor& peers, int64_t rank, at::Tensor& state, at::Tensor& status,
+                         double timeout_s, int64_t src, const c10::optional<at::Tensor>& x,
+                         const c10::optional<at::Tensor>& add, const c10::optional<at::Tensor>& dmask,
+                         int64_t rs_off, int64_t comb_off, int64_t ag_off, at::Tensor& residual, const at::Tensor& w,
+                         double eps, const c10::optional<at::Tensor>& out, bool ag);
+void sp_route_dispatch_op(const at::Tensor& peers, int64_t rank, at::Tensor& state, at::Tensor& status,
+                          double timeout_s, const at::Tensor& logits, const at::Tensor& h, int64_t k, int64_t mode,
+                          const c10::optional<at::Tensor>& bias, double scale, bool renorm, int64_t e_per_rank,
+                          int64_t rows_off, int64_t ids_off, int64_t w_off, at::Tensor& dmask,
+                          const c10::optional<at::Tensor>& ids_local, const c10::optional<at::Tensor>& w_local);
+void sp_combine_push_op(const at::Tensor& peers, int64_t rank, at::Tensor& state, at::Tensor& status, double timeout_s,
+                        const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
+                        int64_t comb_off, int64_t Tr, int64_t H, int64_t channel);
+void sp_wait_op(const at::Tensor& peers, int64_t rank, at::Tensor& state, at::Tensor& status, double timeout_s,
+                int64_t channel);
+void gemm_sp_op(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& out, at::Tensor& status,
+                int64_t splits, const at::Tensor& peers, int64_t rank, at::Tensor& state, double timeout_s, int64_t mode,
+                int64_t rs_off, int64_t rows_per_rank);
+void moe_build_assignments_sp_op(const at::Tensor& ids, const at::Tensor& weights,
+                                 const c10::optional<at::Tensor>& expert_map, int64_t E_local, int64_t tile_rows,
+                                 at::Tensor& sorted_token, at::Tensor& sorted_weight, at::Tensor& slot_of,
+                                 at::Tensor& items, at::Tensor& num_items, at::Tensor& expert_offsets,
+                                 const at::Tensor& peers, int64_t rank, at::Tensor& state, at::Tensor& status,
+                                 double timeout_s);
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -178,7 +204,22 @@ void register_host_bindings(pybind11::module_& m);
   X("timing_open_row(Tensor(a!) ring, Tensor(b!) cursor, Tensor(c!) step_counter) -> ()")               \
   X("combine_allreduce(Tensor y, Tensor slot_of, Tensor sorted_weight, int k, Tensor? add, Tensor(a!) out, " \
     "Tensor peers, int rank, int world, int flag_off, int data_off, int slot_bytes, Tensor(b!) epochs, "    \
-    "Tensor(c!) status, float timeout_s) -> ()")
+    "Tensor(c!) status, float timeout_s) -> ()")                                                           \
+  X("sp_residual_norm(Tensor peers, int rank, Tensor(a!) state, Tensor(b!) status, float timeout_s, int src, " \
+    "Tensor? x, Tensor? add, Tensor? dmask, int rs_off, int comb_off, int ag_off, Tensor(c!) residual, "     \
+    "Tensor w, float eps, Tensor(d!)? out, bool ag) -> ()")                                                \
+  X("sp_route_dispatch(Tensor peers, int rank, Tensor(a!) state, Tensor(b!) status, float timeout_s, "      \
+    "Tensor logits, Tensor h, int k, int mode, Tensor? bias, float scale, bool renorm, int e_per_rank, "     \
+    "int rows_off, int ids_off, int w_off, Tensor(c!) dmask, Tensor(d!)? ids_local, Tensor(e!)? w_local) -> ()") \
+  X("sp_combine_push(Tensor peers, int rank, Tensor(a!) state, Tensor(b!) status, float timeout_s, Tensor y, " \
+    "Tensor slot_of, Tensor sorted_weight, int k, int comb_off, int Tr, int H, int channel=3) -> ()")                      \
+  X("sp_wait(Tensor peers, int rank, Tensor(a!) state, Tensor(b!) status, float timeout_s, int channel) -> ()") \
+  X("gemm_sp(Tensor x, Tensor w, Tensor(a!)? out, Tensor(b!) status, int splits, Tensor peers, int rank, "  \
+    "Tensor(c!) state, float timeout_s, int mode, int rs_off, int rows_per_rank) -> ()")                   \
+  X("moe_build_assignments_sp(Tensor ids, Tensor weights, Tensor? expert_map, int E_local, int tile_rows, " \
+    "Tensor(a!) sorted_token, Tensor(b!) sorted_weight, Tensor(c!) slot_of, Tensor(d!) items, "             \
+    "Tensor(e!) num_items, Tensor(f!) expert_offsets, Tensor peers, int rank, Tensor(g!) state, "           \
+    "Tensor(h!) status, float timeout_s) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -211,4 +252,10 @@ void register_host_bindings(pybind11::module_& m);
   X("timing_stamp", b200::timing_stamp_op)            \
   X("dequant_rows", b200::dequant_rows_op)            \
   X("ple_decode", b200::ple_decode_op)                \
-  X("timing_open_row", b200::timing_open_row_op)
+  X("timing_open_row", b200::timing_open_row_op)      \
+  X("sp_residual_norm", b200::sp_residual_norm_op)    \
+  X("sp_route_dispatch", b200::sp_route_dispatch_op)  \
+  X("sp_combine_push", b200::sp_combine_push_op)      \
+  X("sp_wait", b200::sp_wait_op)                      \
+  X("gemm_sp", b200::gemm_sp_op)                      \
+  X("moe_build_assignments_sp", b200::moe_build_assignments_sp_op)

@@ -15,11 +15,12 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "route_topk.cuh"
+#include "sp_sync.cuh"
 
 namespace b200 {
-namespace {
 
-constexpr int kMaxExpertsPerLane = 16;  // E <= 512
+namespace {
 
 __global__ void topk_kernel(const float* __restrict__ logits, int T, int E, int k, int mode,
                             const float* __restrict__ bias, float scale, int renorm, int* __restrict__ ids,
@@ -28,94 +29,12 @@ __global__ void topk_kernel(const float* __restrict__ logits, int T, int E, int 
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= T) return;
-  const float* row = logits + (size_t)warp * E;
-  float score[kMaxExpertsPerLane];  // value used for the weight
-  float key[kMaxExpertsPerLane];    // value used for selection
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-    const int e = lane + 32 * i;
-    float l = e < E ? row[e] : -INFINITY;
-    score[i] = l;
-    mx = fmaxf(mx, l);
-  }
-  float denom = 1.f;
-  if (mode == 0) {
-    mx = warp_max(mx);
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-      const int e = lane + 32 * i;
-      score[i] = e < E ? __expf(score[i] - mx) : 0.f;
-      s += score[i];
-    }
-    denom = warp_sum(s);
-  }
-#pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-    const int e = lane + 32 * i;
-    if (e >= E) {
-      key[i] = -INFINITY;
-      continue;
-    }
-    if (mode == 0) {
-      score[i] = score[i] / denom;
-      key[i] = score[i];
-    } else if (mode == 1) {
-      score[i] = sigmoidf_(score[i]);
-      key[i] = score[i] + (bias ? bias[e] : 0.f);
-    } else {
-      const float l = score[i];
-      const float sp = l > 20.f ? l : log1pf(__expf(l));
-      score[i] = sqrtf(sp);
-      key[i] = score[i] + (bias ? bias[e] : 0.f);
-    }
-    // a NaN key (a failed row) ranks below every real score but stays selectable, so every row
-    // gets k distinct valid expert ids (its weights carry the NaN on to the output row)
-    if (key[i] != key[i]) key[i] = -FLT_MAX;
-  }
-  float picked_sum = 0.f;
-  float my_w = 0.f;
-  int my_id = 0;
-  for (int j = 0; j < k; ++j) {
-    float best = -INFINITY;
-    int best_e = 0x7fffffff;
-    float best_s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-      const int e = lane + 32 * i;
-      if (key[i] > best || (key[i] == best && e < best_e)) {
-        best = key[i];
-        best_e = e;
-        best_s = score[i];
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
-      const float os = __shfl_xor_sync(0xffffffffu, best_s, o);
-      if (ob > best || (ob == best && oe < best_e)) {
-        best = ob;
-        best_e = oe;
-        best_s = os;
-      }
-    }
-    // remove the pick
-#pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i)
-      if (lane + 32 * i == best_e) key[i] = -INFINITY;
-    picked_sum += best_s;
-    if (lane == j) {
-      my_w = best_s;
-      my_id = best_e;
-    }
-  }
+  int id;
+  float w;
+  route_topk_warp(logits + (size_t)warp * E, E, k, mode, bias, scale, renorm, &id, &w);
   if (lane < k) {
-    float w = my_w;
-    if (renorm) w = mode == 2 ? w / (picked_sum + 1e-20f) : w / picked_sum;
-    ids[(size_t)warp * k + lane] = my_id;
-    weights[(size_t)warp * k + lane] = w * scale;
+    ids[(size_t)warp * k + lane] = id;
+    weights[(size_t)warp * k + lane] = w;
   }
 }
 
@@ -132,9 +51,19 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     const int* __restrict__ ids, const float* __restrict__ weights, int TK, int k, const int* __restrict__ expert_map,
     int E_map, int E_local, int tile_rows, int* __restrict__ sorted_token, float* __restrict__ sorted_weight,
     int* __restrict__ slot_of, int4* __restrict__ items, int* __restrict__ num_items, int* __restrict__ expert_offsets,
-    int max_items) {
+    int max_items, SpSync sp, int sp_wait) {
   pdl_prologue();
   extern __shared__ int sm[];
+  // sequence-parallel dispatch: ids / weights are the receive area the ranks pushed into; wait for
+  // every source's push of this call first (loads below bypass L1)
+  // (a source that never arrives is recorded in the status word; the stale ids are still in range)
+  __shared__ uint32_t s_epoch;
+  if (sp_wait) {
+    if (threadIdx.x == 0) s_epoch = sp_recv_epoch(sp, kSpDispatch);
+    __syncthreads();
+    if (threadIdx.x < sp.world) sp_wait_flag(sp, kSpDispatch, s_epoch, threadIdx.x);
+    __syncthreads();
+  }
   int* counts = sm;                         // [E_local]
   int* base = sm + E_local;                 // [E_local]  running base during placement
   int* warp_counts = sm + 2 * E_local;      // [32][E_local]
@@ -143,7 +72,7 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
   __syncthreads();
   // pass 1: counts
   for (int a = tid; a < TK; a += blockDim.x) {
-    int e = ids[a];
+    int e = __ldcg(ids + a);
     e = (e >= 0 && e < E_map) ? (expert_map ? expert_map[e] : e) : -1;
     if (e >= 0 && e < E_local) atomicAdd(&counts[e], 1);
   }
@@ -174,7 +103,7 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     const int a = c0 + tid;
     int e = -1;
     if (a < TK) {
-      e = ids[a];
+      e = __ldcg(ids + a);
       e = (e >= 0 && e < E_map) ? (expert_map ? expert_map[e] : e) : -1;
       if (e >= E_local) e = -1;
     }
@@ -189,7 +118,7 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
       for (int w = 0; w < warp; ++w) before += warp_counts[w * E_local + e];
       const int row = base[e] + before + rank_in_warp;
       sorted_token[row] = a / k;
-      sorted_weight[row] = weights[a];
+      sorted_weight[row] = __ldcg(weights + a);
       slot_of[a] = row;
     } else if (a < TK) {
       slot_of[a] = -1;
@@ -241,6 +170,7 @@ __global__ void __launch_bounds__(kBuildThreads) build_assignments_kernel(
     int n = base[e];
     for (int r = r0; r < r1 && n < max_items; r += tile_rows) items[n++] = make_int4(e, r, min(tile_rows, r1 - r), 0);
   }
+  if (sp_wait && threadIdx.x == 0) sp_recv_arrive(sp, kSpDispatch, 1, s_epoch);
 }
 
 }  // namespace
@@ -258,7 +188,7 @@ cudaError_t moe_topk(const float* logits, int T, int E, int k, int mode, const f
 cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, int k, const int* expert_map,
                                   int E_map, int E_local, int tile_rows, int* sorted_token, float* sorted_weight, int* slot_of,
                                   int4* items, int* num_items, int* expert_offsets, int max_items,
-                                  cudaStream_t stream) {
+                                  cudaStream_t stream, const SpSync* sp) {
   const size_t smem = sizeof(int) * (2 * E_local + 32 * E_local);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(build_assignments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -267,7 +197,8 @@ cudaError_t moe_build_assignments(const int* ids, const float* weights, int T, i
   launch_pdl(build_assignments_kernel, dim3(1), dim3(kBuildThreads), smem, stream, ids, weights, T * k, k, expert_map,
                                                                expert_map ? E_map : E_local, E_local,
                                                                tile_rows, sorted_token, sorted_weight, slot_of, items,
-                                                               num_items, expert_offsets, max_items);
+                                                               num_items, expert_offsets, max_items,
+                                                               sp ? *sp : SpSync{}, sp ? 1 : 0);
   return cudaGetLastError();
 }
 

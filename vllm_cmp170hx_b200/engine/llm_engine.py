@@ -45,6 +45,7 @@ class LLMEngine:
             st = pstate.init(cfg.parallel.tensor_parallel_size, cfg.parallel.pipeline_parallel_size)
         st.expert_parallel = bool(cfg.parallel.expert_parallel)
         self.runner = ModelRunner(cfg, model)
+        self._setup_sequence_parallel(st)
         self.scheduler = Scheduler(cfg.scheduler, cfg.cache, self.runner.block_pool, self.runner.slot_pool)
         self._diagnostics(st)
         self.adaptive_k = None
@@ -63,6 +64,19 @@ class LLMEngine:
         self.num_steps = 0
         self.k_hist: dict[int, int] = {}  # draft count chosen per step (adaptive k) -> steps
         self.eos_token_id: int | None = None
+
+    def _setup_sequence_parallel(self, st) -> None:
+        """Expert-parallel groups run steps in the sequence-parallel layout (parallel/sp.py) over
+        torch.distributed until a fused transport replaces it (parallel/symm.py)."""
+        from ..parallel import comm
+        from ..parallel.sp import TorchSP
+
+        comm.enable_sp(None)
+        p = self.cfg.parallel
+        model = self.runner.model
+        if (st.tp_size > 1 and not st.emulated and p.expert_parallel and p.sequence_parallel
+                and hasattr(model, "supports_sp") and model.supports_sp()):
+            comm.enable_sp(TorchSP(st.tp_group, model.cfg.hidden_size, model.cfg.moe.top_k))
 
     def _diagnostics(self, st) -> None:
         from .. import envs

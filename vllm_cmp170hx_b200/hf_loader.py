@@ -239,7 +239,8 @@ def _load_moe(moe, t, p, tp, r):
     else:
         raise NotImplementedError("Marlin-packed experts load from this package's own checkpoints")
     if moe.shared is not None:
-        _load_dense_mlp(moe.shared, t, p + "shared_experts.", tp, r)
+        rep = getattr(moe, "shared_replicated", False)  # expert parallel: the whole shared expert on every rank
+        _load_dense_mlp(moe.shared, t, p + "shared_experts.", 1 if rep else tp, 0 if rep else r)
 
 
 def _cut_exl3(m: "fx.Exl3Matrix", which: str, tp: int, r: int) -> "fx.Exl3Matrix":

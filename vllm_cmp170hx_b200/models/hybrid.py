@@ -32,6 +32,7 @@ from ..ops import moe as moe_ops
 from ..oracle import mla as mla_ref
 from ..parallel import comm
 from ..parallel import state as pstate
+from ..parallel.sp import scope as sp_scope
 from .layers import Linear, RMSNorm, WeightInit, default_std
 
 
@@ -286,7 +287,7 @@ class BF16Experts(nn.Module):
         out = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32, device=x.device)
         for e in range(self.gate_up.shape[0]):
             ge = e if self.expert_map is None else int((self.expert_map == e).nonzero()[0, 0])
-            mask = ids == ge
+            mask = ids == ge  # masked ids (-1, experts of other ranks) match no expert
             rows = mask.any(-1).nonzero()[:, 0]
             if rows.numel() == 0:
                 continue
@@ -331,8 +332,13 @@ class MoE(nn.Module):
             assert mc.intermediate % tp == 0
             self.experts = self._experts(mc, hid, mc.intermediate // tp, wi, tp, tp_rank, 0, mc.num_experts)
         self.shared = None
+        # with expert parallelism the shared expert is replicated (whole on every rank): the
+        # sequence-parallel layout runs it on each rank's own tokens; steps on the all-reduce path let
+        # rank 0 add it
+        self.shared_replicated = ep
         if mc.num_shared:
-            self.shared = DenseMLP(hid, mc.shared_intermediate * mc.num_shared, wi, tp, tp_rank, mc.swiglu_limit)
+            st_tp, st_rank = (1, 0) if ep else (tp, tp_rank)
+            self.shared = DenseMLP(hid, mc.shared_intermediate * mc.num_shared, wi, st_tp, st_rank, mc.swiglu_limit)
 
     @staticmethod
     def _experts(mc, hid, inter_local, wi, tp, tp_rank, first: int, count: int):
@@ -366,7 +372,9 @@ class MoE(nn.Module):
         logits = self.gate(x, out_dtype=torch.float32)
         ids, w = moe_ops.topk(logits, self.mc.top_k, self.mc.router_mode, self.e_bias, self.mc.routed_scaling,
                               self.mc.renormalize)
-        shared = self.shared(x) if self.shared is not None else None
+        shared = None
+        if self.shared is not None and not (self.shared_replicated and reduce and pstate.get().tp_rank != 0):
+            shared = self.shared(x)
         if isinstance(self.experts, moe_ops.Exl3Experts):
             return moe_ops.exl3_moe(x, ids, w, self.experts, add=shared, reduce=reduce)
         from ..ops.dequant import MarlinExperts, marlin_moe
@@ -374,6 +382,35 @@ class MoE(nn.Module):
         if isinstance(self.experts, MarlinExperts):
             return marlin_moe(x, ids, w, self.experts, add=shared, reduce=reduce)
         return self.experts(x, ids, w, add=shared, reduce=reduce)
+
+
+    def forward_sp(self, h: torch.Tensor, sp) -> torch.Tensor | None:
+        """Sequence-parallel form (expert parallel): h [Tr, H] this rank's tokens.  Routes them, sends each
+        row to the ranks holding its experts, runs this rank's experts on the rows it received and sends
+        the weighted sums back to the owners (summed by the next residual norm).  Returns the shared
+        expert's output of the local tokens (added by that norm) or None."""
+        mc = self.mc
+        logits = self.gate(h, out_dtype=torch.float32)
+        sp.route_dispatch(logits, h, mc.top_k, mc.router_mode, self.e_bias, mc.routed_scaling, mc.renormalize,
+                          mc.num_experts // sp.world)
+        # the shared expert runs while the dispatched rows travel
+        shared = self.shared(h) if self.shared is not None else None
+        x_r, ids_r, w_r = sp.dispatch_recv()
+        if sp.fused and isinstance(self.experts, moe_ops.Exl3Experts):
+            y, slot_of, sw = moe_ops.exl3_moe_rows(x_r, ids_r, w_r, self.experts, build=sp.build_assignments)
+            sp.combine_push(y, slot_of, sw, mc.top_k)
+            return shared
+        if isinstance(self.experts, moe_ops.Exl3Experts):
+            partial = moe_ops.exl3_moe(x_r, ids_r, w_r, self.experts, out_f32=True)
+        else:
+            from ..ops.dequant import MarlinExperts, marlin_moe
+
+            if isinstance(self.experts, MarlinExperts):
+                partial = marlin_moe(x_r, ids_r, w_r, self.experts, out_f32=True)
+            else:
+                partial = self.experts(x_r, ids_r, w_r)
+        sp.combine_partial(partial)
+        return shared
 
 
 # ============================================================================ model
@@ -484,6 +521,31 @@ class DecoderLayer(nn.Module):
             state.x = self.mlp(h, reduce=True)
         return state
 
+    def forward_sp(self, sp, residual: torch.Tensor, pending: tuple, ctx: StepContext) -> tuple:
+        """Sequence-parallel layer (the step's tokens sharded over the group, parallel/sp.py).
+        `pending` is how the layer input reaches this rank's residual rows: ("local", x) for the
+        embeddings, ("rs", None) for a reduce-scattered projection, ("comb", shared_out) for a combined
+        MoE output.  Returns the pending form of this layer's output."""
+        src, arg = pending
+        sp.norm(src, residual, self.input_norm.weight, self.input_norm.eps, x=arg if src == "local" else None,
+                add=arg if src == "comb" else None, ag=True)
+        with sp_scope(sp):
+            # the attention's first read of the gathered rows is its input GEMM, which waits for the
+            # all-gather itself when it is a bf16 projection; otherwise wait before the attention
+            first = getattr(self.attn, "in_proj", None) or getattr(self.attn, "wq_a", None)
+            self.attn(sp.gathered(wait=not isinstance(first, Linear)), ctx, self.idx)
+        if self.mlp is None:
+            return ("rs", None)
+        if isinstance(self.mlp, MoE):
+            h = torch.empty_like(residual)
+            sp.norm("rs", residual, self.post_norm.weight, self.post_norm.eps, out=h)
+            return ("comb", self.mlp.forward_sp(h, sp))
+        # dense MLP, tensor parallel: all-gather in, reduce-scatter out
+        sp.norm("rs", residual, self.post_norm.weight, self.post_norm.eps, ag=True)
+        with sp_scope(sp):
+            self.mlp(sp.gathered(), reduce=True)
+        return ("rs", None)
+
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None, ctx: StepContext):
         if residual is None:
             residual = x
@@ -566,6 +628,9 @@ class HybridForCausalLM(nn.Module):
             if not self.last:
                 return state
             return self.hc_head(state, self.norm, self.cfg)[1]
+        sp = comm.sp_for(input_ids.shape[0], self) if self.first and self.last else None
+        if sp is not None:
+            return self._forward_sp(input_ids, ctx, sp)
         if self.first:
             x, residual = self.embed[input_ids], None
         else:
@@ -580,6 +645,27 @@ class HybridForCausalLM(nn.Module):
         if self.last:
             return self.norm(x, residual)
         return x, residual
+
+    def supports_sp(self) -> bool:
+        """Whether the sequence-parallel layout covers this model: one pipeline stage, no
+        hyper-connections, no auxiliary hidden states (block drafter), MoE layers (or dense MLPs)."""
+        return (self.first and self.last and not self.cfg.hc_mult and not self.aux_layer_ids
+                and all(t in ("kda", "mla", "dsa") for t in self.cfg.layer_types)
+                and any(isinstance(layer.mlp, MoE) for layer in self.layers))
+
+    def _forward_sp(self, input_ids: torch.Tensor, ctx: StepContext, sp) -> torch.Tensor:
+        """The whole stack with the step's tokens sharded over the tensor-parallel group; returns the
+        final normed hidden states of all T tokens (all-gathered for the vocab-parallel head)."""
+        T = input_ids.shape[0]
+        Tr = sp.begin(T)
+        x = self.embed[sp.local_slice(input_ids)]
+        residual = torch.empty(Tr, self.cfg.hidden_size, dtype=torch.bfloat16, device=x.device)
+        pending = ("local", x)
+        for layer in self.layers:
+            pending = layer.forward_sp(sp, residual, pending, ctx)
+        src, arg = pending
+        sp.norm(src, residual, self.norm.weight, self.norm.eps, add=arg if src == "comb" else None, ag=True)
+        return sp.gathered(wait=True)
 
     def kda_recover(self, ctx: StepContext, keep: torch.Tensor) -> None:
         """After a speculative verify step: advance every verified sequence's KDA state and conv

@@ -41,6 +41,8 @@ class WeightInit:
     def normal(self, shape, std: float, shard: tuple[int, int, int] | None = None, dtype=None) -> torch.Tensor:
         """shard = (dim, rank, size): keep this rank's contiguous part along dim."""
         dtype = dtype or self.dtype
+        if shard is not None and shard[2] == 1:
+            shard = None  # a split over one rank is the whole (replicated) tensor
         if self.mode == "sliced" or self.device.type == "cpu":
             t = torch.randn(*shape, generator=self._gen("cpu")) * std
             if shard is not None:

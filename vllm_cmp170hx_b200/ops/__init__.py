@@ -35,6 +35,15 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
     if out is None:
         out = torch.empty(*lead, w.shape[0], dtype=out_dtype, device=x.device)
     o2 = out.view(-1, w.shape[0])
+    from ..parallel import sp as _sp
+
+    spa = _sp.active()
+    if spa is not None and spa.fused and spa.take_pending(x2):
+        # x is the all-gather area of the sequence-parallel layout: the GEMM waits for it itself
+        if bias is not None:
+            raise ValueError("the all-gather GEMM takes no bias")
+        spa.gemm_ag(x2, w, o2)
+        return out
     _ext.ops().gemm_bf16_out(x2, w, bias, o2, _ext.status_word(x.device), splits)
     return out
 

@@ -54,6 +54,8 @@ def _moe_cpu(x, ids, w, ex: MarlinExperts) -> torch.Tensor:
     for t in range(x.shape[0]):
         for j in range(ids.shape[1]):
             e = int(ids[t, j])
+            if e < 0:  # an expert of another rank (masked id)
+                continue
             if ex.expert_map is not None:
                 e = int(ex.expert_map[e])
                 if e < 0:

@@ -118,6 +118,22 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
 
             return comm.tp_all_reduce(y.to(x.dtype))
         return y if out_f32 else y.to(x.dtype)
+    y, slot_of, sorted_weight = exl3_moe_rows(x, ids, weights, ex)
+    if reduce:
+        from ..parallel import comm
+
+        return comm.combine_all_reduce(y, slot_of, sorted_weight, k, add, T, H)
+    out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16, device=x.device)
+    _ext.ops().moe_combine(y, slot_of, sorted_weight, k, add, out)
+    return out
+
+
+def exl3_moe_rows(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3Experts, build=None):
+    """The expert half of `exl3_moe` on CUDA tensors: returns (y [T k, Hp] fp32 expert outputs in
+    expert-sorted rows, slot_of [T, k] row of each (token, pick) or -1, sorted_weight [T k]).
+    `build` replaces the assignment builder (the sequence-parallel one waits for the dispatch)."""
+    T, H = x.shape
+    k = ids.shape[1]
     ops = _ext.ops()
     dev = x.device
     E = ex.num_local
@@ -134,8 +150,8 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
     items = torch.empty(max_items, 4, **i32)
     num_items = torch.empty(1, **i32)
     offsets = torch.empty(E + 1, **i32)
-    ops.moe_build_assignments(ids.contiguous(), weights.float().contiguous(), ex.expert_map, E, tile, sorted_token,
-                              sorted_weight, slot_of, items, num_items, offsets)
+    (build or ops.moe_build_assignments)(ids.contiguous(), weights.float().contiguous(), ex.expert_map, E, tile,
+                                         sorted_token, sorted_weight, slot_of, items, num_items, offsets)
     xg = torch.empty(TK, Kh, dtype=torch.float16, device=dev)
     xu = torch.empty(TK, Kh, dtype=torch.float16, device=dev)
     # activation row sums (codebook 2 applies its affine step to the accumulator: a acc + b sum x)
@@ -151,13 +167,7 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
     y = torch.empty(TK, Hp, dtype=torch.float32, device=dev)
     ops.exl3_gemm(1, ex.down_trellis, None, ex.down_svh, None, None, ex.bits_x2, ex.codebook, h, None, tile, items,
                   num_items, max_items * (Hp // 128), y, 1, 0.0, st, hsum, None, I // 128, None)
-    if reduce:
-        from ..parallel import comm
-
-        return comm.combine_all_reduce(y, slot_of, sorted_weight, k, add, T, H)
-    out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16, device=dev)
-    ops.moe_combine(y, slot_of, sorted_weight, k, add, out)
-    return out
+    return y, slot_of, sorted_weight
 
 
 _DENSE_ITEMS: dict = {}

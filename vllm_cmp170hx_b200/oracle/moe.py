@@ -41,6 +41,8 @@ def exl3_experts(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, expe
     for t in range(T):
         for j in range(ids.shape[1]):
             e = int(ids[t, j])
+            if e < 0:  # an expert of another rank (masked id)
+                continue
             if emap is not None:
                 e = int(emap[e])
                 if e < 0:

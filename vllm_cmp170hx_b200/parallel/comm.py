@@ -21,7 +21,7 @@ import torch.distributed as dist
 
 from . import state as _state
 
-_FUSED = {"enabled": False, "symm": None, "fused": None}
+_FUSED = {"enabled": False, "symm": None, "fused": None, "sp": None}
 
 
 def enable_fused(symm, fused=None) -> None:
@@ -36,8 +36,31 @@ def fused_enabled() -> bool:
     return _FUSED["enabled"]
 
 
+def enable_sp(sp) -> None:
+    """Run expert-parallel steps that fit `sp` (a parallel.sp transport) in the sequence-parallel layout."""
+    _FUSED["sp"] = sp
+
+
+def sp_for(T: int, model):
+    """The sequence-parallel transport for a step of T tokens of `model`, or None (all-reduce layout)."""
+    sp = _FUSED["sp"]
+    if sp is None or not sp.fits(T):
+        return None
+    ok = getattr(model, "_sp_ok", None)
+    if ok is None:
+        ok = model.supports_sp()
+        model._sp_ok = ok
+    return sp if ok else None
+
+
 def tp_all_reduce(x: torch.Tensor) -> torch.Tensor:
+    from . import sp as _sp
+
     st = _state.get()
+    spa = _sp.active()
+    if spa is not None:  # a row-parallel output inside the sequence-parallel layout
+        spa.rs_tensor(x.reshape(-1, x.shape[-1]))
+        return None
     if st.tp_size == 1 or st.emulated:
         return x
     symm = _FUSED["symm"]
@@ -85,8 +108,15 @@ def gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None 
     kernel computes the GEMM tile, pushes it to every rank and sums the pushed tiles (gemm_bf16.cu);
     baseline: GEMM, then the all-reduce."""
     from .. import ops
+    from . import sp as _sp
 
     st = _state.get()
+    spa = _sp.active()
+    if spa is not None:  # sequence-parallel layout: reduce-scatter to the token owners instead
+        if bias is not None:
+            raise ValueError("sequence-parallel row-parallel projections take no bias")
+        spa.gemm_rs(x.reshape(-1, x.shape[-1]), w)
+        return None
     if st.tp_size == 1:
         return ops.gemm(x, w, bias)
     fc = _FUSED["fused"]

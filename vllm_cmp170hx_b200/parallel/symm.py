@@ -143,6 +143,15 @@ def _agree(ok: bool, cpu_group) -> bool:
     return bool(t.item())
 
 
+def sp_max_tokens(engine) -> int:
+    """Largest step the sequence-parallel buffers take: the decode graphs' batch (times the verify
+    width), at least 256 tokens; larger steps (prefill chunks) take the all-reduce layout."""
+    c = engine.cfg
+    per = 1 + max(0, c.scheduler.num_speculative_tokens)
+    graphs = max(c.cuda_graph_batch_sizes or [0])
+    return max(256, min(4096, max(graphs, c.scheduler.max_num_seqs) * per))
+
+
 def enable_for_engine(engine) -> bool:
     """Switch the engine's TP all-reduces to the symmetric-memory kernel when
     every rank can set it up; returns whether it is active."""
@@ -166,6 +175,22 @@ def enable_for_engine(engine) -> bool:
             log.warning("fused compute + all-reduce kernels unavailable on rank %d: %s", st.rank, e)
         fused_ok = _agree(fused_ok, st.tp_cpu_group)
     comm.enable_fused(symm if ok else None, fused if fused_ok else None)
+    model = engine.runner.model
+    p = engine.cfg.parallel
+    if (fused_ok and st.expert_parallel and p.sequence_parallel and hasattr(model, "supports_sp")
+            and model.supports_sp()):
+        from .sp import FusedSP
+
+        sp = None
+        try:
+            sp = FusedSP(st.tp_group, st.tp_cpu_group, st.device, model.cfg.hidden_size, model.cfg.moe.top_k,
+                         max_tokens=sp_max_tokens(engine))
+            sp_ok = True
+        except Exception as e:  # noqa: BLE001 -- any setup failure falls back on every rank
+            log.warning("sequence-parallel kernels unavailable on rank %d: %s", st.rank, e)
+            sp_ok = False
+        if _agree(sp_ok, st.tp_cpu_group):
+            comm.enable_sp(sp)
     if st.rank == 0:
         log.info("TP all-reduce: %s", "symmetric-memory one-shot kernel" if ok else "NCCL")
     return ok
