@@ -127,6 +127,10 @@ def main():
     ap.add_argument("--prefill-chunk", type=int, default=16384)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--nccl-baseline", action="store_true", help="TP collectives on NCCL only (baseline path)")
+    ap.add_argument("--synthetic-context", action="store_true",
+                    help="no prefill: every request starts decoding at position --prompt over cache rows and "
+                         "recurrent states filled with random values (N(0,1) KV rows), so long contexts and "
+                         "large batches are measurable")
     ap.add_argument("--no-sp", action="store_true", help="expert parallel with replicated tokens and all-reduces "
                                                         "instead of the sequence-parallel layout")
     ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
@@ -215,9 +219,12 @@ def main():
     t_load = time.time() - t0
     g = torch.Generator().manual_seed(args.seed)
     V = model_cfg.vocab_size
+    if args.synthetic_context:
+        engine.runner.fill_caches_random(args.seed)
     for i in range(args.batch):
         prompt = torch.randint(0, V, (args.prompt,), generator=g).tolist()
-        engine.add_request(prompt, SamplingParams(max_tokens=args.output, ignore_eos=True), f"bench-{i}")
+        engine.add_request(prompt, SamplingParams(max_tokens=args.output, ignore_eos=True), f"bench-{i}",
+                           synthetic_prefix=args.prompt - 1 if args.synthetic_context else 0)
     # prefill (untimed): until every request has its first token
     t1 = time.time()
     while any(r.num_computed_tokens < r.num_prompt_tokens for r in engine.scheduler.running) or engine.scheduler.waiting:
@@ -273,7 +280,9 @@ def main():
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_total_ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "impl": "ours",
-            "data": f"synthetic: random token ids, random-init weights of the config-{args.config} architecture",
+            "data": (f"synthetic: random token ids, random-init weights of the config-{args.config} architecture"
+                     + ("; context rows and recurrent states random (no prefill)" if args.synthetic_context
+                        else "; prompts prefilled through the engine")),
             "config": {"model": MODEL_DESC[args.config],
                        "global_batch": args.batch, "seq_len": args.prompt, "output_len": args.output,
                        "parallelism": (f"ep{args.gpus}+attn-tp{args.gpus}" if args.ep and args.gpus > 1

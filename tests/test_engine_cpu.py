@@ -110,3 +110,25 @@ def test_decode_step_inputs_fast_path_equals_general_path():
         for k in ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps", "sample_rows"):
             assert np.array_equal(fast[k], gen[k]), (pad, k, fast[k], gen[k])
         assert (fast["max_ctx"], fast["T"], fast["S"]) == (gen["max_ctx"], gen["T"], gen["S"])
+
+
+def test_synthetic_prefix_skips_prefill(model):
+    """A request with a synthetic prefix starts at that position: its first step computes the last
+    prompt token only, over the rows the caches hold (here filled with random values)."""
+    eng = LLMEngine(_cfg(max_tokens_per_step=256), model)
+    eng.runner.fill_caches_random(3)
+    ids = [eng.add_request([(5 * j) % 500 for j in range(100)], SamplingParams(max_tokens=3), synthetic_prefix=99)
+           for _ in range(2)]
+    out = eng.scheduler.schedule()
+    assert [s.num_new for s in out.reqs] == [1, 1] and all(s.start == 99 and s.sample for s in out.reqs)
+    eng.scheduler.waiting.extendleft(reversed([s.req for s in out.reqs]))  # undo: let step() schedule them
+    for s in out.reqs:
+        eng.scheduler.running.remove(s.req)
+        eng.scheduler._release(s.req)
+        s.req.num_computed_tokens = 0
+    done = {}
+    while eng.has_unfinished():
+        for o in eng.step():
+            if o.finished:
+                done[o.request_id] = o
+    assert sorted(done) == sorted(ids) and all(len(o.output_token_ids) == 3 for o in done.values())

@@ -164,7 +164,7 @@ def _generate(tp, fused):
                 parts = [torch.empty_like(out) for _ in range(tp)]
                 dist.all_gather(parts, out.contiguous(), group=pstate.get().tp_group)
                 full = torch.cat(parts, -1)
-            seen.append(full.float().cpu())
+            seen.append(full.float().cpu().numpy())  # by value through the result queue
         return out
 
     model.compute_logits = recording
@@ -216,6 +216,7 @@ def test_sp_engine_tp2_matches_one_gpu():
     ref_toks, ref_logits = ref
     assert len(logits) == len(ref_logits) == 3
     for a, b in zip(logits, ref_logits):
+        a, b = torch.from_numpy(a), torch.from_numpy(b)
         assert a.shape == b.shape
         assert _rel(a, b) < 5e-2, _rel(a, b)
     same = sum(x == y for x, y in zip(toks, ref_toks))

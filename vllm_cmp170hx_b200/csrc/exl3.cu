@@ -498,6 +498,82 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
         st_off[r][3] = row + 1024 + c1;
       }
     }
+    if constexpr (FAST) {
+      // Software-pipelined 4-bit path over this CTA's chunks (all its units, in order): the trellis
+      // words of chunk c + 1 are loaded while chunk c is decoded, so the warps do not all stall on
+      // shared-memory latency right after each barrier.  A raw stage is released as soon as its
+      // words are in registers (after their first use), the operand stage after its stores.
+      constexpr int NT = NMAT * kRowsPerWarp;
+      const int my_units = blockIdx.x < total ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+      const int nchunk = my_units * kchunks;
+      uint32_t cur[NT], nxt[NT];
+      bool ok = nchunk > 0;
+      if (ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&raw_full[rs], rphase, p.status, abort_flag));
+        if (ok) {
+          const uint32_t rw = smem_u32(raw + rs * pl.raw_bytes) + raw_lane_off;
+#pragma unroll
+          for (int i = 0; i < NT; ++i) cur[i] = lds32(rw + (i / kRowsPerWarp) * 32 * 128 + (i % kRowsPerWarp) * 8 * 128);
+        }
+      }
+      for (int c = 0; c < nchunk && ok; ++c) {
+        uint32_t prev[NT];
+#pragma unroll
+        for (int i = 0; i < NT; ++i) prev[i] = __shfl_sync(0xffffffffu, cur[i], (lane + 31) & 31);
+        // every lane's words of chunk c have reached registers: release the raw stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        if (++rs == rstages) {
+          rs = 0;
+          rphase ^= 1;
+        }
+        const bool more = c + 1 < nchunk;
+        if (more) {
+          if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&raw_full[rs], rphase, p.status, abort_flag))) {
+            ok = false;
+            break;
+          }
+          const uint32_t rw = smem_u32(raw + rs * pl.raw_bytes) + raw_lane_off;
+#pragma unroll
+          for (int i = 0; i < NT; ++i) nxt[i] = lds32(rw + (i / kRowsPerWarp) * 32 * 128 + (i % kRowsPerWarp) * 8 * 128);
+        }
+        uint32_t packed[NT][4];
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+          uint32_t st[8];
+          states_b8(prev[i], cur[i], st);
+          packed[i][0] = cb_pair<CB>(st[0], st[1]);
+          packed[i][1] = cb_pair<CB>(st[2], st[3]);
+          packed[i][2] = cb_pair<CB>(st[4], st[5]);
+          packed[i][3] = cb_pair<CB>(st[6], st[7]);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const uint32_t ab = smem_u32(a_tile(stage, 0));
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+          const int m = i / kRowsPerWarp, r = i % kRowsPerWarp;
+          const uint32_t mo = ab + m * A_BYTES;
+          sts32(mo + st_off[r][0], packed[i][0]);
+          sts32(mo + st_off[r][1], packed[i][1]);
+          sts32(mo + st_off[r][2], packed[i][2]);
+          sts32(mo + st_off[r][3], packed[i][3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[stage]);
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (more) {
+#pragma unroll
+          for (int i = 0; i < NT; ++i) cur[i] = nxt[i];
+        }
+      }
+    } else
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
       bool ok = true;
       for (int kc = 0; kc < kchunks; ++kc) {

@@ -145,9 +145,11 @@ class LLMEngine:
         return path
 
     def add_request(self, prompt_token_ids: list[int], params: SamplingParams | None = None,
-                    request_id: str | None = None) -> str:
+                    request_id: str | None = None, synthetic_prefix: int = 0) -> str:
+        """synthetic_prefix (benchmarks): that many leading prompt positions are taken as already
+        computed, their cache rows being whatever the caches hold (see ModelRunner.fill_caches_random)."""
         req = Request(list(prompt_token_ids), params or SamplingParams(), request_id or "",
-                      eos_token_id=self.eos_token_id)
+                      eos_token_id=self.eos_token_id, synthetic_prefix=synthetic_prefix)
         self.scheduler.add(req)
         self.requests[req.request_id] = req
         return req.request_id

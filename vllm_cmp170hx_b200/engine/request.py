@@ -55,6 +55,10 @@ class Request:
     token_times: list[float] = field(default_factory=list)
     # speculative decoding: draft tokens proposed for the next verify step
     draft_token_ids: list[int] = field(default_factory=list)
+    # benchmarks: the first `synthetic_prefix` prompt positions count as computed on admission (their
+    # cache rows and recurrent state are whatever the caches hold, e.g. random rows), so a long-context
+    # decode can be measured without prefilling it
+    synthetic_prefix: int = 0
 
     def __post_init__(self):
         if not self.request_id:

@@ -84,6 +84,22 @@ class ModelRunner:
             self.spec = SpecDecoder(self, cfg.scheduler.num_speculative_tokens)
 
     # ------------------------------------------------------------------ caches
+    @torch.no_grad()
+    def fill_caches_random(self, seed: int = 0, state_std: float = 0.1) -> None:
+        """Benchmarks of long-context decode without a prefill: every latent row ~N(0, 1), index keys
+        fp8 codes of N(0, 1) values with unit scales, recurrent KDA states ~N(0, state_std^2), conv windows
+        ~N(0, 1) (requests added with a synthetic prefix then attend to these rows)."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        for lat, idx_k, idx_s in self.mla_caches.values():
+            lat.normal_(generator=g)
+            idx_k.copy_(torch.randn(idx_k.shape, generator=g, device=self.device).to(torch.float8_e4m3fn)
+                        .view(torch.uint8))
+            idx_s.fill_(1.0)
+        for rec, conv in self.kda_states.values():
+            rec.normal_(generator=g).mul_(state_std)
+            conv.normal_(generator=g)
+
     def _alloc_caches(self):
         cfg = self.cfg
         m = self.model

@@ -166,6 +166,8 @@ class Scheduler:
             req = self.waiting[0]
             if partial >= self.cfg.max_num_partial_prefills and req.num_tokens > budget:
                 break
+            if req.synthetic_prefix and req.num_computed_tokens == 0:
+                req.num_computed_tokens = min(req.synthetic_prefix, req.num_prompt_tokens - 1)
             n = min(req.num_tokens - req.num_computed_tokens, budget, cap)
             upto = req.num_computed_tokens + n
             if upto >= req.num_tokens:
