@@ -34,6 +34,8 @@
 namespace b200 {
 namespace exl3 {
 
+// Decoder warps per CTA (a template parameter DW of the kernel): 16 decode 2 tile rows each of every
+// 4-row chunk, 8 decode all 4 rows of their tile column (twice the work per barrier round).
 constexpr int kDecodeWarps = 16;
 
 constexpr int BK = 64;                              // K per pipeline stage (4 tile rows)
@@ -387,20 +389,30 @@ inline Plan make_plan(int nmat, int tile_rows, int bits_x2) {
   return pl;
 }
 
-constexpr int kEpiWarp0 = kDecodeWarps;                // epilogue warps [kEpiWarp0, kEpiWarp0 + 4)
-constexpr int kRawWarp = kDecodeWarps + kEpiWarps;      // trellis producer (TMA)
-constexpr int kBWarp = kRawWarp + 1;                    // activation producer (TMA)
-constexpr int kMmaWarp = kRawWarp + 2;                  // TMEM owner + MMA issuer
-constexpr int kThreadsStaged = (kMmaWarp + 1) * 32;
+// Warp roles for DW decoder warps: decoders [0, DW), epilogue [DW, DW + 4), trellis producer, activation
+// producer, TMEM owner + MMA issuer.
+template <int DW>
+struct Roles {
+  static constexpr int kEpiWarp0 = DW;
+  static constexpr int kRawWarp = DW + kEpiWarps;
+  static constexpr int kBWarp = kRawWarp + 1;
+  static constexpr int kMmaWarp = kRawWarp + 2;
+  static constexpr int kThreads = (kMmaWarp + 1) * 32;
+};
 
 // NMAT = 2: gate/up pass (writes the rotated SwiGLU intermediate), 1: down / dense.
 // Trellis chunks (4 tile rows x 8 tile columns per matrix) arrive by TMA in
 // a ring `raw_stages` deep, so the decoder warps never wait on global memory.
-template <int NMAT, int CB, bool FAST>
-__global__ void __launch_bounds__(kThreadsStaged, 1)
+template <int NMAT, int CB, bool FAST, int DW>
+__global__ void __launch_bounds__(Roles<DW>::kThreads, 1)
     exl3_gemm_kernel(const __grid_constant__ CUtensorMap tma_b0, const __grid_constant__ CUtensorMap tma_b1,
                      const __grid_constant__ CUtensorMap tma_t0, const __grid_constant__ CUtensorMap tma_t1,
                      GemmParams p, Plan pl) {
+  constexpr int kDecodeWarps = DW;
+  constexpr int kEpiWarp0 = Roles<DW>::kEpiWarp0;
+  constexpr int kRawWarp = Roles<DW>::kRawWarp;
+  constexpr int kBWarp = Roles<DW>::kBWarp;
+  constexpr int kMmaWarp = Roles<DW>::kMmaWarp;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int tile_rows = p.tile_rows;
@@ -498,82 +510,6 @@ __global__ void __launch_bounds__(kThreadsStaged, 1)
         st_off[r][3] = row + 1024 + c1;
       }
     }
-    if constexpr (FAST) {
-      // Software-pipelined 4-bit path over this CTA's chunks (all its units, in order): the trellis
-      // words of chunk c + 1 are loaded while chunk c is decoded, so the warps do not all stall on
-      // shared-memory latency right after each barrier.  A raw stage is released as soon as its
-      // words are in registers (after their first use), the operand stage after its stores.
-      constexpr int NT = NMAT * kRowsPerWarp;
-      const int my_units = blockIdx.x < total ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-      const int nchunk = my_units * kchunks;
-      uint32_t cur[NT], nxt[NT];
-      bool ok = nchunk > 0;
-      if (ok) {
-        ok = __all_sync(0xffffffffu, mbar_wait_or_abort(&raw_full[rs], rphase, p.status, abort_flag));
-        if (ok) {
-          const uint32_t rw = smem_u32(raw + rs * pl.raw_bytes) + raw_lane_off;
-#pragma unroll
-          for (int i = 0; i < NT; ++i) cur[i] = lds32(rw + (i / kRowsPerWarp) * 32 * 128 + (i % kRowsPerWarp) * 8 * 128);
-        }
-      }
-      for (int c = 0; c < nchunk && ok; ++c) {
-        uint32_t prev[NT];
-#pragma unroll
-        for (int i = 0; i < NT; ++i) prev[i] = __shfl_sync(0xffffffffu, cur[i], (lane + 31) & 31);
-        // every lane's words of chunk c have reached registers: release the raw stage
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
-        if (++rs == rstages) {
-          rs = 0;
-          rphase ^= 1;
-        }
-        const bool more = c + 1 < nchunk;
-        if (more) {
-          if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&raw_full[rs], rphase, p.status, abort_flag))) {
-            ok = false;
-            break;
-          }
-          const uint32_t rw = smem_u32(raw + rs * pl.raw_bytes) + raw_lane_off;
-#pragma unroll
-          for (int i = 0; i < NT; ++i) nxt[i] = lds32(rw + (i / kRowsPerWarp) * 32 * 128 + (i % kRowsPerWarp) * 8 * 128);
-        }
-        uint32_t packed[NT][4];
-#pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          uint32_t st[8];
-          states_b8(prev[i], cur[i], st);
-          packed[i][0] = cb_pair<CB>(st[0], st[1]);
-          packed[i][1] = cb_pair<CB>(st[2], st[3]);
-          packed[i][2] = cb_pair<CB>(st[4], st[5]);
-          packed[i][3] = cb_pair<CB>(st[6], st[7]);
-        }
-        if (!__all_sync(0xffffffffu, mbar_wait_or_abort(&empty[stage], phase ^ 1, p.status, abort_flag))) {
-          ok = false;
-          break;
-        }
-        const uint32_t ab = smem_u32(a_tile(stage, 0));
-#pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          const int m = i / kRowsPerWarp, r = i % kRowsPerWarp;
-          const uint32_t mo = ab + m * A_BYTES;
-          sts32(mo + st_off[r][0], packed[i][0]);
-          sts32(mo + st_off[r][1], packed[i][1]);
-          sts32(mo + st_off[r][2], packed[i][2]);
-          sts32(mo + st_off[r][3], packed[i][3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[stage]);
-        if (++stage == stages) {
-          stage = 0;
-          phase ^= 1;
-        }
-        if (more) {
-#pragma unroll
-          for (int i = 0; i < NT; ++i) cur[i] = nxt[i];
-        }
-      }
-    } else
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
       bool ok = true;
       for (int kc = 0; kc < kchunks; ++kc) {
@@ -904,39 +840,63 @@ __global__ void input_rotate_kernel(const __nv_bfloat16* __restrict__ x, int64_t
 }
 
 // out[t, :] = sum_j w[t, j] * y[slot[t, j], :]  (+ add[t, :]), fp32 math, fixed j order.
-// grid (T, column blocks of 4 * blockDim); 4 consecutive columns per thread.
-__global__ void combine_kernel(const float* __restrict__ y, int64_t ld_y, const int* __restrict__ slot_of,
-                               const float* __restrict__ sorted_weight, int k, int H,
-                               const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out,
-                               int64_t ld_out, float* __restrict__ out_f32) {
+// Grid (token, 256-column block), 64 threads: the token's k slots and weights are read once into
+// shared memory (one round of loads), then each thread sums its 4 columns over the k rows with the k
+// row loads independent of each other (no load waits on another load's result); many small blocks
+// keep enough loads in flight per SM for the fp32 rows to stream at memory speed.
+constexpr int kCombineMaxK = 32;
+constexpr int kCombineThreads = 64;
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ y, int64_t ld_y,
+                                                      const int* __restrict__ slot_of,
+                                                      const float* __restrict__ sorted_weight, int k, int H,
+                                                      const __nv_bfloat16* __restrict__ add,
+                                                      __nv_bfloat16* __restrict__ out, int64_t ld_out,
+                                                      float* __restrict__ out_f32) {
   pdl_prologue();
+  __shared__ int s_slot[kCombineMaxK];
+  __shared__ float s_w[kCombineMaxK];
   const int t = blockIdx.x;
-  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
-  if (c >= H) return;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const bool vec = (c + 4 <= H) && (ld_y % 4 == 0);
-  for (int j = 0; j < k; ++j) {
-    const int s = slot_of[(int64_t)t * k + j];
-    if (s < 0) continue;
-    const float w = sorted_weight[s];
-    const float* row = y + (int64_t)s * ld_y + c;
-    if (vec) {
-      const float4 v = *reinterpret_cast<const float4*>(row);
-      acc[0] += w * v.x;
-      acc[1] += w * v.y;
-      acc[2] += w * v.z;
-      acc[3] += w * v.w;
-    } else {
-      for (int i = 0; i < 4 && c + i < H; ++i) acc[i] += w * row[i];
-    }
+  if (threadIdx.x < k) {
+    const int s = slot_of[(int64_t)t * k + threadIdx.x];
+    s_slot[threadIdx.x] = s;
+    s_w[threadIdx.x] = s >= 0 ? sorted_weight[s] : 0.f;
   }
-  for (int i = 0; i < 4 && c + i < H; ++i) {
-    float a = acc[i];
-    if (add) a += __bfloat162float(add[(int64_t)t * ld_out + c + i]);
-    if (out_f32)
-      out_f32[(int64_t)t * H + c + i] = a;
-    else
-      out[(int64_t)t * ld_out + c + i] = __float2bfloat16(a);
+  __syncthreads();
+  const bool vec = (ld_y % 4 == 0);
+  for (int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4; c < H; c += gridDim.y * blockDim.x * 4) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec && c + 4 <= H) {
+      for (int j0 = 0; j0 < k; j0 += 8) {  // 8 independent row loads in flight, then their sums in j order
+        float4 v[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int s = j0 + jj < k ? s_slot[j0 + jj] : -1;
+          v[jj] = s >= 0 ? *reinterpret_cast<const float4*>(y + (int64_t)s * ld_y + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const float w = j0 + jj < k ? s_w[j0 + jj] : 0.f;
+          acc[0] += w * v[jj].x;
+          acc[1] += w * v[jj].y;
+          acc[2] += w * v[jj].z;
+          acc[3] += w * v[jj].w;
+        }
+      }
+    } else {
+      for (int j = 0; j < k; ++j) {
+        const int s = s_slot[j];
+        if (s < 0) continue;
+        for (int i = 0; i < 4 && c + i < H; ++i) acc[i] += s_w[j] * y[(int64_t)s * ld_y + c + i];
+      }
+    }
+    for (int i = 0; i < 4 && c + i < H; ++i) {
+      float a = acc[i];
+      if (add) a += __bfloat162float(add[(int64_t)t * ld_out + c + i]);
+      if (out_f32)
+        out_f32[(int64_t)t * H + c + i] = a;
+      else
+        out[(int64_t)t * ld_out + c + i] = __float2bfloat16(a);
+    }
   }
 }
 
@@ -957,7 +917,7 @@ inline CUtensorMap make_trellis_map(const void* base, int E, int K, int N, int b
   return map;
 }
 
-template <int NMAT, int CB, bool FAST>
+template <int NMAT, int CB, bool FAST, int DW>
 cudaError_t launch_gemm(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, int E,
                         cudaStream_t stream, int grid) {
   const Plan pl = make_plan(NMAT, p.tile_rows, p.bits_x2);
@@ -971,23 +931,38 @@ cudaError_t launch_gemm(const GemmParams& p, const void* b0, const void* b1, int
                              : m0;
   CUtensorMap t0 = make_trellis_map(p.trellis[0], E, p.K, p.N, p.bits_x2);
   CUtensorMap t1 = NMAT == 2 ? make_trellis_map(p.trellis[1], E, p.K, p.N, p.bits_x2) : t0;
-  auto kern = exl3_gemm_kernel<NMAT, CB, FAST>;
+  auto kern = exl3_gemm_kernel<NMAT, CB, FAST, DW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
   if (e != cudaSuccess) return e;
-  launch_pdl(kern, dim3(grid), dim3(kThreadsStaged), pl.smem, stream, m0, m1, t0, t1, p, pl);
+  launch_pdl(kern, dim3(grid), dim3(Roles<DW>::kThreads), pl.smem, stream, m0, m1, t0, t1, p, pl);
   return cudaGetLastError();
+}
+
+// Decoder warps per CTA: VLLM_B200_EXL3_DECODERS (8 or 16) when set, else the pass's default.
+inline int decoder_warps(int nmat) {
+  static const int env = [] {
+    const char* v = std::getenv("VLLM_B200_EXL3_DECODERS");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (env == 8 || env == 16) return env;
+  (void)nmat;
+  return 16;
 }
 
 template <int NMAT>
 cudaError_t dispatch(const GemmParams& p, const void* b0, const void* b1, int64_t b_rows, int E, cudaStream_t s,
                      int grid) {
   const bool fast = p.bits_x2 == 8;
-  if (p.codebook == 1) {
-    return fast ? launch_gemm<NMAT, 1, true>(p, b0, b1, b_rows, E, s, grid)
-                : launch_gemm<NMAT, 1, false>(p, b0, b1, b_rows, E, s, grid);
+  if (fast && decoder_warps(NMAT) == 8) {
+    return p.codebook == 1 ? launch_gemm<NMAT, 1, true, 8>(p, b0, b1, b_rows, E, s, grid)
+                           : launch_gemm<NMAT, 2, true, 8>(p, b0, b1, b_rows, E, s, grid);
   }
-  return fast ? launch_gemm<NMAT, 2, true>(p, b0, b1, b_rows, E, s, grid)
-              : launch_gemm<NMAT, 2, false>(p, b0, b1, b_rows, E, s, grid);
+  if (p.codebook == 1) {
+    return fast ? launch_gemm<NMAT, 1, true, 16>(p, b0, b1, b_rows, E, s, grid)
+                : launch_gemm<NMAT, 1, false, 16>(p, b0, b1, b_rows, E, s, grid);
+  }
+  return fast ? launch_gemm<NMAT, 2, true, 16>(p, b0, b1, b_rows, E, s, grid)
+              : launch_gemm<NMAT, 2, false, 16>(p, b0, b1, b_rows, E, s, grid);
 }
 
 }  // namespace exl3
@@ -1047,8 +1022,10 @@ cudaError_t exl3_gemm(const Exl3GemmArgs& a, cudaStream_t stream) {
 cudaError_t moe_combine(const float* y, int64_t ld_y, const int* slot_of, const float* sorted_weight, int T, int k,
                         int H, const void* add, void* out, int64_t ld_out, float* out_f32, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  dim3 grid(T, (H + 4 * 128 - 1) / (4 * 128));
-  launch_pdl(exl3::combine_kernel, dim3(grid), dim3(128), 0, stream, y, ld_y, slot_of, sorted_weight, k, H,
+  if (k > exl3::kCombineMaxK) return cudaErrorInvalidValue;
+  const int cblocks = (H + 4 * exl3::kCombineThreads - 1) / (4 * exl3::kCombineThreads);
+  launch_pdl(exl3::combine_kernel, dim3(T, cblocks), dim3(exl3::kCombineThreads), 0, stream, y, ld_y, slot_of,
+             sorted_weight, k, H,
                                               reinterpret_cast<const __nv_bfloat16*>(add),
                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_f32);
   return cudaGetLastError();

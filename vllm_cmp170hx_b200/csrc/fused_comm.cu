@@ -62,20 +62,34 @@ __global__ void __launch_bounds__(kThreads) combine_allreduce_kernel(CombineArAr
     const int t = (int)(v / hv);
     const int c = (int)(v % hv) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < p.k; ++j) {
-      const int s = p.slot_of[(int64_t)t * p.k + j];
-      if (s < 0) continue;
-      const float w = p.sorted_weight[s];
-      const float4* row = reinterpret_cast<const float4*>(p.y + (int64_t)s * p.ld_y + c);
-      const float4 a = row[0], bb = row[1];
-      acc[0] += w * a.x;
-      acc[1] += w * a.y;
-      acc[2] += w * a.z;
-      acc[3] += w * a.w;
-      acc[4] += w * bb.x;
-      acc[5] += w * bb.y;
-      acc[6] += w * bb.z;
-      acc[7] += w * bb.w;
+    for (int j0 = 0; j0 < p.k; j0 += 4) {  // fixed slot order; the slot, weight and row loads of 4 at once
+      int s[4];
+      float w[4];
+      float4 a[4], bb[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) s[jj] = j0 + jj < p.k ? p.slot_of[(int64_t)t * p.k + j0 + jj] : -1;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        w[jj] = s[jj] >= 0 ? p.sorted_weight[s[jj]] : 0.f;
+        if (s[jj] >= 0) {
+          const float4* row = reinterpret_cast<const float4*>(p.y + (int64_t)s[jj] * p.ld_y + c);
+          a[jj] = row[0];
+          bb[jj] = row[1];
+        } else {
+          a[jj] = bb[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        acc[0] += w[jj] * a[jj].x;
+        acc[1] += w[jj] * a[jj].y;
+        acc[2] += w[jj] * a[jj].z;
+        acc[3] += w[jj] * a[jj].w;
+        acc[4] += w[jj] * bb[jj].x;
+        acc[5] += w[jj] * bb[jj].y;
+        acc[6] += w[jj] * bb[jj].z;
+        acc[7] += w[jj] * bb[jj].w;
+      }
     }
     if (p.add) {
       const uint4 a = *reinterpret_cast<const uint4*>(p.add + (int64_t)t * p.H + c);

@@ -79,6 +79,10 @@ struct Params {
   int64_t sp_rs_off;
   int sp_rows;
   int act_is_b;
+  // Batched GEMM (batch > 1, splits == 1): tile t covers matrix t / (m_tiles * n_tiles); the operand
+  // maps are 3-D (K, rows, batch) and C of matrix b starts c_bstride elements after matrix b - 1's.
+  int batch;
+  int64_t c_bstride;
 };
 
 // Destination of output row `tok` (a token), columns from `feat`, in the reduce-scatter mode.
@@ -191,7 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                           (rs || ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0 && (p.ldc & 7) == 0));
 
   const int tiles_mn = p.m_tiles * p.n_tiles;
-  const int total = tiles_mn * p.splits;
+  const bool batched = p.batch > 1;
+  const int total = tiles_mn * (batched ? p.batch : p.splits);
   const int kb_total = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
@@ -213,7 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int act_bytes = p.act_is_b ? C_::B_BYTES : C_::A_BYTES;
       const int act_rows = p.act_is_b ? BN : BM;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int split = t / tiles_mn;
+        const int split = batched ? 0 : t / tiles_mn;
+        const int bz = batched ? t / tiles_mn : 0;
         const int mn = t % tiles_mn;
         const int mt = mn % p.m_tiles;
         const int nt = mn / p.m_tiles;
@@ -225,7 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
-          if (gate.open) {
+          if (batched) {
+            tma_load_3d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM, bz);
+            tma_load_3d(smem_b + stage * C_::B_BYTES, &tma_b, &full[stage], kb * BK, nt * BN, bz);
+          } else if (gate.open) {
             // weights now, the activation tile once the all-gather landed
             if (p.act_is_b)
               tma_load_2d(smem_a + stage * C_::A_BYTES, &tma_a, &full[stage], kb * BK, mt * BM);
@@ -267,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int local = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
-        const int split = t / tiles_mn;
+        const int split = batched ? 0 : t / tiles_mn;
         const int kb0 = split * p.k_blocks_per_split;
         const int kb1 = min(kb_total, kb0 + p.k_blocks_per_split);
         const int acc = local & 1;
@@ -310,7 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
-      const int split = t / tiles_mn;
+      const int split = batched ? 0 : t / tiles_mn;
+      __nv_bfloat16* const Cb = batched ? p.C + (size_t)(t / tiles_mn) * p.c_bstride : p.C;
       const int mn = t % tiles_mn;
       const int mt = mn % p.m_tiles;
       const int nt = mn / p.m_tiles;
@@ -355,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col = nt * BN + n, f0 = mt * BM + g * 8;
             if (col >= p.N || f0 >= p.M) continue;
             const uint8_t* src = smem_out + n * (BM * 2) + g * 16;
-            __nv_bfloat16* dst = rs ? rs_dst(p, col, f0, p.M) : p.C + (size_t)col * p.ldc + f0;
+            __nv_bfloat16* dst = rs ? rs_dst(p, col, f0, p.M) : Cb + (size_t)col * p.ldc + f0;
             if (f0 + 8 <= p.M) {
               *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
             } else {
@@ -422,10 +432,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int col = col0 + j;
-              if (col < p.N) p.C[(size_t)col * p.ldc + row] = __float2bfloat16(__uint_as_float(r[j]) + bias);
+              if (col < p.N) Cb[(size_t)col * p.ldc + row] = __float2bfloat16(__uint_as_float(r[j]) + bias);
             }
           } else {
-            __nv_bfloat16* dst = rs ? rs_dst(p, row, col0, p.N) : p.C + (size_t)row * p.ldc + col0;
+            __nv_bfloat16* dst = rs ? rs_dst(p, row, col0, p.N) : Cb + (size_t)row * p.ldc + col0;
             if (col0 + 16 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) && p.bias == nullptr) {
               uint4 v0, v1;
               v0.x = pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1]));
@@ -833,6 +843,21 @@ cudaError_t launch(const void* A, int64_t lda, int rows_a, const void* B, int64_
 }
 
 template <int BN>
+cudaError_t launch_batched(const void* A, int64_t lda, int64_t a_bs, int rows_a, const void* B, int64_t ldb,
+                           int64_t b_bs, int rows_b, int K, const Params& p, cudaStream_t stream, int grid) {
+  using C_ = Cfg<BN>;
+  CUtensorMap ta = make_tma_3d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_a, K, p.batch, lda, a_bs, BM, BK,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tma_3d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_b, K, p.batch, ldb, b_bs, BN, BK,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kern = gemm_bf16_tn_kernel<BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  launch_pdl(kern, dim3(grid), dim3(kThreads), C_::SMEM_BYTES, stream, ta, tb, p);
+  return cudaGetLastError();
+}
+
+template <int BN>
 cudaError_t launch_csk(const void* A, int64_t lda, int rows_a, const void* B, int64_t ldb, int rows_b, int K,
                        const Params& p, cudaStream_t stream) {
   using C_ = Cfg<BN>;
@@ -1022,6 +1047,42 @@ static cudaError_t gemm_bf16_impl(const GemmArgs& a, const GemmSpArgs* sp, cudaS
 }
 
 cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream) { return gemm_bf16_impl(a, nullptr, stream); }
+
+cudaError_t gemm_bf16_batched(const GemmBatchedArgs& a, cudaStream_t stream) {
+  using namespace gemm;
+  if (a.M == 0 || a.N == 0 || a.batch == 0) return cudaSuccess;
+  if (a.K % 8 != 0 || a.batch < 1) return cudaErrorInvalidValue;
+  const bool swap = a.M <= 128;
+  const void* A = swap ? a.w : a.x;
+  const void* B = swap ? a.x : a.w;
+  const int64_t lda = swap ? a.ldw : a.ldx, a_bs = swap ? a.w_bstride : a.x_bstride;
+  const int64_t ldb = swap ? a.ldx : a.ldw, b_bs = swap ? a.x_bstride : a.w_bstride;
+  const int Ma = swap ? a.N : a.M;
+  const int Nb = swap ? a.M : a.N;
+  const int bn = swap ? (Nb <= 16 ? 16 : Nb <= 32 ? 32 : Nb <= 64 ? 64 : 128) : 256;
+  Params p{};
+  p.M = Ma;
+  p.N = Nb;
+  p.K = a.K;
+  p.ldc = (int)a.ldc;
+  p.transpose_out = swap ? 1 : 0;
+  p.m_tiles = (Ma + BM - 1) / BM;
+  p.n_tiles = (Nb + bn - 1) / bn;
+  p.k_blocks_per_split = (a.K + BK - 1) / BK;
+  p.splits = 1;
+  p.C = reinterpret_cast<__nv_bfloat16*>(a.c);
+  p.status = a.status;
+  p.batch = a.batch;
+  p.c_bstride = a.c_bstride;
+  const int grid = std::min(p.m_tiles * p.n_tiles * a.batch, device_sm_count());
+  switch (bn) {
+    case 16: return launch_batched<16>(A, lda, a_bs, Ma, B, ldb, b_bs, Nb, a.K, p, stream, grid);
+    case 32: return launch_batched<32>(A, lda, a_bs, Ma, B, ldb, b_bs, Nb, a.K, p, stream, grid);
+    case 64: return launch_batched<64>(A, lda, a_bs, Ma, B, ldb, b_bs, Nb, a.K, p, stream, grid);
+    case 128: return launch_batched<128>(A, lda, a_bs, Ma, B, ldb, b_bs, Nb, a.K, p, stream, grid);
+    default: return launch_batched<256>(A, lda, a_bs, Ma, B, ldb, b_bs, Nb, a.K, p, stream, grid);
+  }
+}
 
 cudaError_t gemm_bf16_sp(const GemmSpArgs& a, cudaStream_t stream) {
   const SpSync& s = a.sp;

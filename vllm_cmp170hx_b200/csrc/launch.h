@@ -32,7 +32,8 @@ struct SpSync {
 //   bf16 + ids [world * Tr, k] int32 + weights [world * Tr, k] fp32, combine [world * Tr, H] bf16.
 struct SpNormArgs {
   SpSync s;
-  int src;                       // 0: rows x (the residual starts as x), 1: reduce-scatter area, 2: combine area
+  int src;                       // 0: rows x (the residual starts as x), 1: reduce-scatter area, 2: combine area,
+                                 // 3: rows x computed on this rank (added to the residual)
   const __nv_bfloat16* x;        // src 0: [Tr, ld_x]
   int64_t ld_x;
   const __nv_bfloat16* add;      // src 2: added to the combined rows (shared expert output [Tr, H]) or null
@@ -105,6 +106,20 @@ int gemm_bf16_splits(int M, int N, int K, int splits_req);
 // Whether a launch with this many splits needs the fp32 partial scratch (cluster-reduced splits do not).
 bool gemm_bf16_uses_partial(int M, int splits);
 cudaError_t gemm_bf16(const GemmArgs& a, cudaStream_t stream);
+
+// Batched: C[b] = X[b] . W[b]^T for b < batch (strides in elements; per-head projections such as the
+// MLA absorb / up-projection), bf16 out, no split-K.
+struct GemmBatchedArgs {
+  const void* x;
+  int64_t ldx, x_bstride;
+  const void* w;
+  int64_t ldw, w_bstride;
+  void* c;
+  int64_t ldc, c_bstride;
+  int M, N, K, batch;
+  uint32_t* status;
+};
+cudaError_t gemm_bf16_batched(const GemmBatchedArgs& a, cudaStream_t stream);
 
 // The same GEMM fused with a sequence-parallel collective (gemm_bf16.cu):
 //   mode 1 (reduce-scatter): row t of the output (a token) is pushed into rank t / rows_per_rank's
@@ -312,7 +327,8 @@ cudaError_t mhc_post_pre(const MhcArgs& a, cudaStream_t stream);
 
 // ---------------------------------------------------------------- mla_prep.cu / mla_attn.cu
 cudaError_t rope_apply(void* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
-                       const int* positions, const float* cos_sin, int interleaved, int T, cudaStream_t stream);
+                       const int* positions, const float* cos_sin, int interleaved, int T, cudaStream_t stream,
+                       void* y = nullptr, int64_t y_ld_tok = 0, int64_t y_ld_head = 0, int y_offset = 0);
 cudaError_t mla_latent_cache_write(const void* kv, int64_t ld_kv, const void* norm_w, float eps, const int* positions,
                                    const float* cos_sin, int interleaved, const int64_t* slots, void* cache, int T,
                                    cudaStream_t stream);

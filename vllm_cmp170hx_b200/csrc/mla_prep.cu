@@ -23,12 +23,13 @@ __device__ __forceinline__ void rot(float& a, float& b, float c, float s) {
   b = x2 * c + x1 * s;
 }
 
-// In place RoPE on rot_dim dims at `offset` of every head of every token.
+// RoPE on rot_dim dims at `offset` of every head of every token, in place or (y != null) into dims
+// y_offset.. of y (e.g. the rope tail of the MLA query rows, next to the absorbed part).
 // cos_sin: [max_pos, rot_dim] fp32 = [cos(rot_dim/2) | sin(rot_dim/2)].
 // interleaved: pairs (2i, 2i+1); else NeoX pairs (i, i + rot_dim/2).
 __global__ void rope_kernel(__nv_bfloat16* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
                             const int* __restrict__ positions, const float* __restrict__ cos_sin, int interleaved,
-                            int T) {
+                            int T, __nv_bfloat16* y, int64_t y_ld_tok, int64_t y_ld_head, int y_offset) {
   pdl_prologue();
   const int half = rot_dim / 2;
   const int64_t total = (int64_t)T * nheads * half;
@@ -43,8 +44,9 @@ __global__ void rope_kernel(__nv_bfloat16* x, int64_t ld_tok, int64_t ld_head, i
     const int i2 = interleaved ? 2 * j + 1 : j + half;
     float a = __bfloat162float(p[i1]), b = __bfloat162float(p[i2]);
     rot(a, b, c, s);
-    p[i1] = __float2bfloat16(a);
-    p[i2] = __float2bfloat16(b);
+    __nv_bfloat16* o = y ? y + t * y_ld_tok + h * y_ld_head + y_offset : p;
+    o[i1] = __float2bfloat16(a);
+    o[i2] = __float2bfloat16(b);
   }
 }
 
@@ -434,13 +436,15 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restr
 }  // namespace mla
 
 cudaError_t rope_apply(void* x, int64_t ld_tok, int64_t ld_head, int nheads, int offset, int rot_dim,
-                       const int* positions, const float* cos_sin, int interleaved, int T, cudaStream_t stream) {
+                       const int* positions, const float* cos_sin, int interleaved, int T, cudaStream_t stream,
+                       void* y, int64_t y_ld_tok, int64_t y_ld_head, int y_offset) {
   if (T == 0) return cudaSuccess;
   const int64_t total = (int64_t)T * nheads * (rot_dim / 2);
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
   launch_pdl(mla::rope_kernel, dim3(blocks), dim3(threads), 0, stream, reinterpret_cast<__nv_bfloat16*>(x), ld_tok, ld_head, nheads,
-                                                   offset, rot_dim, positions, cos_sin, interleaved, T);
+                                                   offset, rot_dim, positions, cos_sin, interleaved, T,
+                                                   reinterpret_cast<__nv_bfloat16*>(y), y_ld_tok, y_ld_head, y_offset);
   return cudaGetLastError();
 }
 

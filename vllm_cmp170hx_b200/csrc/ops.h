@@ -55,7 +55,7 @@ void kda_core_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& 
                  at::Tensor& out);  // kda.cu
 
 void rope_op(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin, int64_t offset, int64_t rot_dim,
-             bool interleaved);  // mla_prep.cu
+             bool interleaved, const c10::optional<at::Tensor>& out, int64_t out_offset);  // mla_prep.cu
 void mla_latent_cache_write_op(const at::Tensor& kv, const at::Tensor& norm_w, double eps, const at::Tensor& positions,
                                const at::Tensor& cos_sin, bool interleaved, const at::Tensor& slots,
                                at::Tensor& cache);  // mla_prep.cu
@@ -137,6 +137,8 @@ void moe_build_assignments_sp_op(const at::Tensor& ids, const at::Tensor& weight
                                  const at::Tensor& peers, int64_t rank, at::Tensor& state, at::Tensor& status,
                                  double timeout_s);
 
+void gemm_batched_op(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const at::Tensor& status);
+
 // Host (non-op) bindings: C++ runtime pieces exposed through pybind11.
 void register_host_bindings(pybind11::module_& m);
 
@@ -172,7 +174,8 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor qkv, Tensor(b!)? conv_state) -> ()")                                                          \
   X("kda_core(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor q, Tensor k, Tensor v, "      \
     "Tensor g, Tensor beta, Tensor(a!) state, Tensor(b!) out) -> ()")                                     \
-  X("rope(Tensor(a!) x, Tensor positions, Tensor cos_sin, int offset, int rot_dim, bool interleaved) -> ()") \
+  X("rope(Tensor(a!) x, Tensor positions, Tensor cos_sin, int offset, int rot_dim, bool interleaved, "        \
+    "Tensor(b!)? out=None, int out_offset=0) -> ()")                                                      \
   X("mla_latent_cache_write(Tensor kv, Tensor norm_w, float eps, Tensor positions, Tensor cos_sin, "        \
     "bool interleaved, Tensor slots, Tensor(a!) cache) -> ()")                                            \
   X("mla_index_k_write(Tensor k, Tensor? ln_w, Tensor? ln_b, float eps, Tensor positions, Tensor cos_sin, " \
@@ -219,7 +222,8 @@ void register_host_bindings(pybind11::module_& m);
   X("moe_build_assignments_sp(Tensor ids, Tensor weights, Tensor? expert_map, int E_local, int tile_rows, " \
     "Tensor(a!) sorted_token, Tensor(b!) sorted_weight, Tensor(c!) slot_of, Tensor(d!) items, "             \
     "Tensor(e!) num_items, Tensor(f!) expert_offsets, Tensor peers, int rank, Tensor(g!) state, "           \
-    "Tensor(h!) status, float timeout_s) -> ()")
+    "Tensor(h!) status, float timeout_s) -> ()")                                                      \
+  X("gemm_batched(Tensor x, Tensor w, Tensor(a!) out, Tensor(b!) status) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -258,4 +262,5 @@ void register_host_bindings(pybind11::module_& m);
   X("sp_combine_push", b200::sp_combine_push_op)      \
   X("sp_wait", b200::sp_wait_op)                      \
   X("gemm_sp", b200::gemm_sp_op)                      \
-  X("moe_build_assignments_sp", b200::moe_build_assignments_sp_op)
+  X("moe_build_assignments_sp", b200::moe_build_assignments_sp_op) \
+  X("gemm_batched", b200::gemm_batched_op)

@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(kThreads) residual_norm_kernel(SpNormArgs a) {
   const int nvec = a.H / 8;
   const int ch = a.src == 1 ? kSpReduceScatter : kSpCombine;
   const int world = a.s.world, rank = a.s.rank;
-  if (a.src != 0) {
+  const bool recv = a.src == 1 || a.src == 2;
+  if (recv) {
     if (tid == 0) s_e = sp_recv_epoch(a.s, ch);
     __syncthreads();
     if (tid < world) sp_wait_flag(a.s, ch, s_e, tid);
@@ -96,14 +97,19 @@ __global__ void __launch_bounds__(kThreads) residual_norm_kernel(SpNormArgs a) {
       for (int j = 0; j < 8; ++j) vals[i][j] = 0.f;
       add8(vals[i], x);
     } else {
-      // the pushed rows of this token, summed in rank order (fp32), rounded like the unfused op's output
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int r = 0; r < world; ++r) {
-        if (a.src == 2 && !((dm >> r) & 1u)) continue;
-        add8(acc, sp_ld_cg_v4(mine + area + ((int64_t)(r * a.Tr + t) * nvec + v) * 16));
+      uint4 y;
+      if (a.src == 3) {  // rows computed on this rank
+        y = reinterpret_cast<const uint4*>(a.x + (int64_t)t * a.ld_x)[v];
+      } else {
+        // the pushed rows of this token, summed in rank order (fp32), rounded like the unfused op's output
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < world; ++r) {
+          if (a.src == 2 && !((dm >> r) & 1u)) continue;
+          add8(acc, sp_ld_cg_v4(mine + area + ((int64_t)(r * a.Tr + t) * nvec + v) * 16));
+        }
+        if (a.src == 2 && a.add) add8(acc, reinterpret_cast<const uint4*>(a.add + (int64_t)t * a.H)[v]);
+        y = pack8(acc);
       }
-      if (a.src == 2 && a.add) add8(acc, reinterpret_cast<const uint4*>(a.add + (int64_t)t * a.H)[v]);
-      const uint4 y = pack8(acc);
       const uint4 r0 = *res;
       float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       add8(sum, y);
@@ -138,7 +144,7 @@ __global__ void __launch_bounds__(kThreads) residual_norm_kernel(SpNormArgs a) {
   __syncthreads();
   if (tid == 0) {
     if (a.ag) sp_push_arrive(a.s, kSpAllGather, gridDim.x);
-    if (a.src != 0) sp_recv_arrive(a.s, ch, gridDim.x, s_e);
+    if (recv) sp_recv_arrive(a.s, ch, gridDim.x, s_e);
   }
 }
 
@@ -187,6 +193,7 @@ __global__ void __launch_bounds__(kThreads) route_dispatch_kernel(SpDispatchArgs
 __global__ void __launch_bounds__(kThreads) combine_push_kernel(SpCombineArgs a) {
   pdl_prologue();
   __shared__ int s_slot[32];
+  __shared__ float s_w[32];
   __shared__ int s_any;
   const int world = a.s.world, rank = a.s.rank;
   const int R = world * a.Tr, nvec = a.H / 8;
@@ -196,6 +203,7 @@ __global__ void __launch_bounds__(kThreads) combine_push_kernel(SpCombineArgs a)
     if (threadIdx.x < a.k) {
       const int s = a.slot_of[(int64_t)row * a.k + threadIdx.x];
       s_slot[threadIdx.x] = s;
+      s_w[threadIdx.x] = s >= 0 ? a.sorted_weight[s] : 0.f;
       if (s >= 0) s_any = 1;
     }
     __syncthreads();
@@ -204,20 +212,31 @@ __global__ void __launch_bounds__(kThreads) combine_push_kernel(SpCombineArgs a)
       uint4* dst = reinterpret_cast<uint4*>(a.s.peers[src] + a.comb_off) + (int64_t)(rank * a.Tr + t) * nvec;
       for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int j = 0; j < a.k; ++j) {  // fixed slot order
-          const int s = s_slot[j];
-          if (s < 0) continue;
-          const float wt = a.sorted_weight[s];
-          const float4* yr = reinterpret_cast<const float4*>(a.y + (int64_t)s * a.ld_y + v * 8);
-          const float4 p = yr[0], q = yr[1];
-          acc[0] += wt * p.x;
-          acc[1] += wt * p.y;
-          acc[2] += wt * p.z;
-          acc[3] += wt * p.w;
-          acc[4] += wt * q.x;
-          acc[5] += wt * q.y;
-          acc[6] += wt * q.z;
-          acc[7] += wt * q.w;
+        for (int j0 = 0; j0 < a.k; j0 += 4) {  // fixed slot order; 4 rows' loads in flight at once
+          float4 p[4], q[4];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int s = j0 + jj < a.k ? s_slot[j0 + jj] : -1;
+            if (s >= 0) {
+              const float4* yr = reinterpret_cast<const float4*>(a.y + (int64_t)s * a.ld_y + v * 8);
+              p[jj] = yr[0];
+              q[jj] = yr[1];
+            } else {
+              p[jj] = q[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const float wt = j0 + jj < a.k ? s_w[j0 + jj] : 0.f;
+            acc[0] += wt * p[jj].x;
+            acc[1] += wt * p[jj].y;
+            acc[2] += wt * p[jj].z;
+            acc[3] += wt * p[jj].w;
+            acc[4] += wt * q[jj].x;
+            acc[5] += wt * q[jj].y;
+            acc[6] += wt * q[jj].z;
+            acc[7] += wt * q[jj].w;
+          }
         }
         dst[v] = pack8(acc);
       }
@@ -247,8 +266,8 @@ static bool sp_ok(const SpSync& s) {
 }
 
 cudaError_t sp_residual_norm(const SpNormArgs& a, cudaStream_t stream) {
-  if (!sp_ok(a.s) || a.H % 8 || a.H > spc::kThreads * spc::kMaxVec * 8 || a.Tr < 1 || a.src < 0 || a.src > 2 ||
-      (a.src == 0 && a.x == nullptr) || (a.src == 2 && a.dmask == nullptr) || a.residual == nullptr)
+  if (!sp_ok(a.s) || a.H % 8 || a.H > spc::kThreads * spc::kMaxVec * 8 || a.Tr < 1 || a.src < 0 || a.src > 3 ||
+      ((a.src == 0 || a.src == 3) && a.x == nullptr) || (a.src == 2 && a.dmask == nullptr) || a.residual == nullptr)
     return cudaErrorInvalidValue;
   launch_pdl(spc::residual_norm_kernel, dim3(a.Tr), dim3(spc::kThreads), 0, stream, a);
   return cudaGetLastError();

@@ -227,4 +227,37 @@ void moe_build_assignments_sp_op(const at::Tensor& ids, const at::Tensor& weight
       (int)items.size(0), sp_stream(), &s));
 }
 
+// out[b] = x[b] . w[b]^T over a batch of matrices (3-D views with unit inner stride; any outer strides
+// that are multiples of 8 elements).
+void gemm_batched_op(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const at::Tensor& status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16,
+              "gemm_batched: bf16 tensors");
+  TORCH_CHECK(x.dim() == 3 && w.dim() == 3 && out.dim() == 3, "gemm_batched: [B, M, K] x [B, N, K] -> [B, M, N]");
+  const int64_t B = x.size(0), M = x.size(1), K = x.size(2), N = w.size(1);
+  TORCH_CHECK(w.size(0) == B && w.size(2) == K && out.size(0) == B && out.size(1) == M && out.size(2) == N,
+              "gemm_batched: shapes");
+  TORCH_CHECK(x.stride(2) == 1 && w.stride(2) == 1 && out.stride(2) == 1, "gemm_batched: unit inner stride");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && x.stride(1) % 8 == 0 && w.stride(0) % 8 == 0 && w.stride(1) % 8 == 0 &&
+                  out.stride(0) % 8 == 0 && out.stride(1) % 8 == 0,
+              "gemm_batched: strides must be multiples of 8 elements");
+  c10::cuda::CUDAGuard g(x.device());
+  GemmBatchedArgs a{};
+  a.x = x.data_ptr();
+  a.ldx = x.stride(1);
+  a.x_bstride = x.stride(0);
+  a.w = w.data_ptr();
+  a.ldw = w.stride(1);
+  a.w_bstride = w.stride(0);
+  a.c = out.data_ptr();
+  a.ldc = out.stride(1);
+  a.c_bstride = out.stride(0);
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.batch = (int)B;
+  a.status = reinterpret_cast<uint32_t*>(status.data_ptr<int>());
+  B200_SP_LAUNCH(gemm_bf16_batched(a, sp_stream()));
+}
+
 }  // namespace b200

@@ -46,4 +46,25 @@ inline CUtensorMap make_tma_2d(const void* base, CUtensorMapDataType dtype, size
   return map;
 }
 
+// 3-D tiled map over a batch of row-major matrices [batch][rows, cols] (strides in elements); box =
+// [1, box_rows, box_cols].
+inline CUtensorMap make_tma_3d(const void* base, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
+                               uint64_t batch, uint64_t row_stride_elems, uint64_t batch_stride_elems,
+                               uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
+  if ((row_stride_elems * esz) % 16 != 0 || (batch_stride_elems * esz) % 16 != 0)
+    throw std::runtime_error("TMA strides must be multiples of 16 bytes");
+  if ((box_cols * esz) % 16 != 0) throw std::runtime_error("TMA box inner extent must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t gdim[3] = {cols, rows, batch};
+  cuuint64_t gstride[2] = {row_stride_elems * esz, batch_stride_elems * esz};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = tensor_map_encoder()(&map, dtype, 3, const_cast<void*>(base), gdim, gstride, box, estride,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3-D) failed: " + std::to_string((int)r));
+  return map;
+}
+
 }  // namespace b200

@@ -356,7 +356,7 @@ void kda_core_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& 
 namespace b200 {
 
 void rope_op(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_sin, int64_t offset, int64_t rot_dim,
-             bool interleaved) {
+             bool interleaved, const c10::optional<at::Tensor>& out, int64_t out_offset) {
   B200_CHECK_CUDA(x);
   B200_CHECK_DTYPE(x, at::kBFloat16);
   TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "rope: x [T, heads, dim] with contiguous dim");
@@ -364,9 +364,15 @@ void rope_op(at::Tensor& x, const at::Tensor& positions, const at::Tensor& cos_s
               "rope: positions int32, cos_sin fp32 [max_pos, rot_dim]");
   TORCH_CHECK(offset + rot_dim <= x.size(2) && rot_dim % 2 == 0, "rope: range");
   c10::cuda::CUDAGuard g(x.device());
+  if (out.has_value()) {
+    TORCH_CHECK(out->scalar_type() == at::kBFloat16 && out->dim() == 3 && out->stride(2) == 1 &&
+                    out->size(0) == x.size(0) && out->size(1) == x.size(1) && out_offset + rot_dim <= out->size(2),
+                "rope: out [T, heads, >= out_offset + rot_dim]");
+  }
   B200_LAUNCH(rope_apply(x.data_ptr(), x.stride(0), x.stride(1), x.size(1), (int)offset, (int)rot_dim,
                          positions.data_ptr<int>(), cos_sin.data_ptr<float>(), interleaved ? 1 : 0, x.size(0),
-                         cur_stream()));
+                         cur_stream(), out.has_value() ? out->data_ptr() : nullptr,
+                         out.has_value() ? out->stride(0) : 0, out.has_value() ? out->stride(1) : 0, (int)out_offset));
 }
 
 void mla_latent_cache_write_op(const at::Tensor& kv, const at::Tensor& norm_w, double eps, const at::Tensor& positions,

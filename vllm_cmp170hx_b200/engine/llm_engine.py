@@ -44,6 +44,11 @@ class LLMEngine:
         if st.tp_size != cfg.parallel.tensor_parallel_size:
             st = pstate.init(cfg.parallel.tensor_parallel_size, cfg.parallel.pipeline_parallel_size)
         st.expert_parallel = bool(cfg.parallel.expert_parallel)
+        from .. import envs
+
+        if not envs.get("VLLM_B200_CUDA_GRAPHS"):
+            cfg.enforce_eager = True
+        envs.log_gate("CUDA graphs for decode steps", not cfg.enforce_eager)
         self.runner = ModelRunner(cfg, model)
         self._setup_sequence_parallel(st)
         self.scheduler = Scheduler(cfg.scheduler, cfg.cache, self.runner.block_pool, self.runner.slot_pool)
@@ -68,13 +73,17 @@ class LLMEngine:
     def _setup_sequence_parallel(self, st) -> None:
         """Expert-parallel groups run steps in the sequence-parallel layout (parallel/sp.py) over
         torch.distributed until a fused transport replaces it (parallel/symm.py)."""
+        from .. import envs
         from ..parallel import comm
         from ..parallel.sp import TorchSP
 
         comm.enable_sp(None)
         p = self.cfg.parallel
         model = self.runner.model
-        if (st.tp_size > 1 and not st.emulated and p.expert_parallel and p.sequence_parallel
+        mode = envs.get("VLLM_B200_EP_DISPATCH")
+        if mode not in ("symm", "nccl", "off"):
+            raise ValueError(f"VLLM_B200_EP_DISPATCH={mode!r}: 'symm', 'nccl' or 'off'")
+        if (st.tp_size > 1 and not st.emulated and p.expert_parallel and p.sequence_parallel and mode != "off"
                 and hasattr(model, "supports_sp") and model.supports_sp()):
             comm.enable_sp(TorchSP(st.tp_group, model.cfg.hidden_size, model.cfg.moe.top_k))
 

@@ -61,6 +61,11 @@ class Scheduler:
         self.finished: list[Request] = []
         # speculative decoding: KV blocks reserved past a sampling step for the drafter's own cache writes
         self.lookahead = max(0, sched.num_speculative_tokens - 1)
+        from .. import envs
+
+        # prompts up to this length are never held back by the partial-prefill cap (the reference's
+        # VLLM_FAIR_PREFILL_SHORT_BYPASS): they finish in one chunk and cost the decodes little
+        self.short_bypass = envs.get("VLLM_B200_FAIR_PREFILL_SHORT_BYPASS")
         self.draft_cap = sched.num_speculative_tokens  # drafts verified per request this step (adaptive k)
 
     # ------------------------------------------------------------------ API
@@ -130,7 +135,7 @@ class Scheduler:
             remaining = req.num_tokens - req.num_computed_tokens
             if remaining > 1 or (req.num_computed_tokens == 0):
                 # still in prefill (the last prompt token is computed together with sampling)
-                if partial >= self.cfg.max_num_partial_prefills:
+                if partial >= self.cfg.max_num_partial_prefills and req.num_prompt_tokens > self.short_bypass:
                     i += 1
                     continue
                 n = min(remaining, budget, cap)
@@ -164,7 +169,8 @@ class Scheduler:
         # admit waiting requests
         while self.waiting and budget > 0 and len(self.running) < self.cfg.max_num_seqs:
             req = self.waiting[0]
-            if partial >= self.cfg.max_num_partial_prefills and req.num_tokens > budget:
+            if (partial >= self.cfg.max_num_partial_prefills and req.num_tokens > budget
+                    and req.num_prompt_tokens > self.short_bypass):
                 break
             if req.synthetic_prefix and req.num_computed_tokens == 0:
                 req.num_computed_tokens = min(req.synthetic_prefix, req.num_prompt_tokens - 1)

@@ -43,22 +43,24 @@ def _declare(name: str, typ, default, doc: str) -> None:
 
 
 # --- collectives --------------------------------------------------------------------------------
-_declare("VLLM_B200_ALLREDUCE", str, "symm", "TP all-reduce transport: 'symm' (own NVLink peer-memory kernel) or 'nccl'")
-_declare("VLLM_B200_ALLREDUCE_MAX_BYTES", int, 16 << 20, "largest message the symmetric-memory all-reduce takes")
+_declare("VLLM_B200_ALLREDUCE", str, "symm", "TP all-reduce transport: 'symm' (own NVLink peer-memory kernels, "
+         "read by parallel/symm.py) or 'nccl'")
+_declare("VLLM_B200_ALLREDUCE_MAX_BYTES", int, 0, "largest message the symmetric-memory all-reduce takes (0: the "
+         "tuning table's allreduce/symm_max_bytes)")
 _declare("VLLM_B200_ALLREDUCE_WAIT_S", float, 10.0, "bounded wait of the peer-memory kernels before they report")
-_declare("VLLM_B200_FUSED_GEMM_AR", _bool, True, "row-parallel GEMM fused with the all-reduce (tile push)")
-_declare("VLLM_B200_EP_DISPATCH", str, "symm", "expert-parallel dispatch/combine: 'symm' or 'nccl'")
-_declare("VLLM_B200_PP_PACKED_HOP", _bool, True, "pipeline boundary tensors packed into one send/recv")
-_declare("VLLM_B200_PP_HOP_NO_METADATA", _bool, False, "skip the per-hop metadata message after the handshake")
+_declare("VLLM_B200_FUSED_GEMM_AR", _bool, True, "row-parallel GEMM and MoE combine fused with the all-reduce "
+         "(replicated-token layout)")
+_declare("VLLM_B200_EP_DISPATCH", str, "symm", "expert-parallel steps: 'symm' (sequence-parallel layout on the fused "
+         "peer-store kernels), 'nccl' (the same layout on torch.distributed) or 'off' (replicated tokens)")
 # --- kernels ------------------------------------------------------------------------------------
-_declare("VLLM_B200_CUDA_GRAPHS", _bool, True, "capture decode steps in CUDA graphs")
+_declare("VLLM_B200_CUDA_GRAPHS", _bool, True, "capture decode steps in CUDA graphs (0: every step eager)")
 _declare("VLLM_B200_GEMM_SPLITK", int, 0, "force the split-K factor of the bf16 GEMM (0 = shape-chosen)")
-_declare("VLLM_B200_EXL3_TILE_ROWS", int, 0, "rows per EXL3 expert work item (0 = batch-chosen)")
+_declare("VLLM_B200_EXL3_TILE_ROWS", int, 0, "rows per EXL3 expert work item, 16 / 32 / 64 / 128 (0 = batch-chosen)")
+_declare("VLLM_B200_EXL3_DECODERS", int, 0, "decoder warps of the EXL3 GEMM, 8 or 16 (0 = the build's default; read "
+         "by csrc/exl3.cu)")
 _declare("VLLM_B200_SPARSE_MLA_SPLITS", int, 0, "position splits of the sparse-MLA attention (0 = auto)")
-_declare("VLLM_B200_KDA_PREFILL", str, "recurrent", "KDA prefill kernel: 'recurrent' (token loop) or 'chunked'")
-_declare("VLLM_B200_SHARD_ARGMAX", _bool, True, "greedy sampling by per-shard winners (no logits gather)")
-_declare("VLLM_B200_TOPK_CANONICAL_TIES", _bool, True, "indexer top-k: lowest position wins ties")
-_declare("VLLM_B200_MOE_DETERMINISTIC_ALIGN", _bool, True, "counting-sort expert assignment (deterministic)")
+_declare("VLLM_B200_MLA_DP", _bool, True, "with expert parallelism, sparse-MLA layers hold all heads and attend "
+         "data-parallel (each rank its own tokens) in the sequence-parallel layout")
 # --- scheduling ---------------------------------------------------------------------------------
 _declare("VLLM_B200_FAIR_PREFILL_SHORT_BYPASS", int, 0, "prompts up to this length skip the partial-prefill cap")
 _declare("VLLM_B200_ADAPTIVE_K", str, "", "adaptive draft count policy ('' off, 'by_load', 'accept')")
@@ -68,7 +70,8 @@ _declare("VLLM_B200_NO_PDL", bool, False, "launch kernels without programmatic d
 _declare("VLLM_B200_OVERRIDE_SHA256", str, "", "pinned sha256 of the override manifest")
 # --- storage-backed embeddings ------------------------------------------------------------------
 _declare("VLLM_B200_PLE_READ_RETRIES", int, 3, "retries of a failed PLE/Engram row read (1 ms doubling backoff)")
-_declare("VLLM_B200_ROW_CACHE_GIB", float, 0.0, "host LRU cache of table rows read from storage")
+_declare("VLLM_B200_ROW_CACHE_GIB", float, 0.0, "host LRU cache of table rows read from storage (0 = the table's "
+         "own row count)")
 # --- diagnostics --------------------------------------------------------------------------------
 _declare("VLLM_B200_LIGHT_TIMING", str, "", "device-timed per-scope profiler (JSON spec or '1')")
 _declare("VLLM_B200_EXECUTION_TRACE", _bool, False, "record a torch execution trace beside profiler traces")
@@ -78,7 +81,6 @@ _declare("VLLM_B200_MEM_ATTRIBUTION", _bool, False, "log resident bytes per modu
 _declare("VLLM_B200_STATE_INDEX_CHECK", _bool, False, "range-check state/cache indices on the host before launch")
 _declare("VLLM_B200_KV_PLAN_LOG", _bool, False, "log the KV/state memory plan")
 _declare("VLLM_B200_TUNING_FILE", str, "", "per-card tuning table to use instead of the device's own")
-_declare("VLLM_B200_TOOL_CHOICE_NONE_MASK", _bool, False, "mask tool-call start tokens when tool_choice='none'")
 _declare("VLLM_B200_DEV_AB_SWITCH", str, "", "dev: capture both arms of a switch and flip between steps")
 _declare("VLLM_B200_HOT_SWAP", str, "", "dev: swap implementation pairs between steps")
 
@@ -96,16 +98,19 @@ ALIASES = {
     "VLLM_STATE_INDEX_CHECK": "VLLM_B200_STATE_INDEX_CHECK",
     "VLLM_KV_PLAN_LOG": "VLLM_B200_KV_PLAN_LOG",
     "VLLM_SM80_TUNING_FILE": "VLLM_B200_TUNING_FILE",
-    "VLLM_SM80_SHARD_ARGMAX": "VLLM_B200_SHARD_ARGMAX",
     "VLLM_FAIR_PREFILL_SHORT_BYPASS": "VLLM_B200_FAIR_PREFILL_SHORT_BYPASS",
-    "VLLM_PP_PACKED_HOP": "VLLM_B200_PP_PACKED_HOP",
-    "VLLM_PP_HOP_NO_METADATA": "VLLM_B200_PP_HOP_NO_METADATA",
-    "VLLM_TOOL_CHOICE_NONE_MASK": "VLLM_B200_TOOL_CHOICE_NONE_MASK",
     "VLLM_DEV_AB_SWITCH": "VLLM_B200_DEV_AB_SWITCH",
     "VLLM_HOT_SWAP": "VLLM_B200_HOT_SWAP",
     "VLLM_EXL3_PLE_READ_RETRIES": "VLLM_B200_PLE_READ_RETRIES",
-    "VLLM_SM80_TOPK_CANONICAL_TIES": "VLLM_B200_TOPK_CANONICAL_TIES",
-    "VLLM_MOE_DETERMINISTIC_ALIGN": "VLLM_B200_MOE_DETERMINISTIC_ALIGN",
+}
+
+# reference switches whose behaviour is always on here (no switch): accepted, warned about
+ALWAYS_ON = {
+    "VLLM_SM80_SHARD_ARGMAX": "greedy sampling always combines per-vocab-shard winners (no logits gather)",
+    "VLLM_PP_PACKED_HOP": "pipeline boundary tensors always travel as one packed message",
+    "VLLM_PP_HOP_NO_METADATA": "pipeline hops never send per-hop metadata (shapes follow from the step)",
+    "VLLM_SM80_TOPK_CANONICAL_TIES": "the indexer top-k always breaks ties by the lowest position",
+    "VLLM_MOE_DETERMINISTIC_ALIGN": "the expert assignment is always a deterministic counting sort",
 }
 
 # reference switches of sm_80-only code paths: accepted, ignored, warned about
@@ -156,6 +161,8 @@ def check_environment() -> list[str]:
             msgs.append(f"unknown variable {k} (not declared in vllm_cmp170hx_b200.envs)")
         elif any(k.startswith(p) for p in RETIRED_PREFIXES):
             msgs.append(f"{k} switches an sm_80-only code path of the reference; it has no effect here")
+        elif k in ALWAYS_ON:
+            msgs.append(f"{k} has no effect here: {ALWAYS_ON[k]}")
     for m in msgs:
         _warn_once(m, m)
     return msgs

@@ -142,6 +142,8 @@ def _load_kda(a, t, p, tp, r):
 
 def _load_mla(a, t, p, tp, r):
     m = a.m
+    if getattr(a, "full_heads", False):  # every head on every rank (data-parallel attention)
+        tp, r = 1, 0
     w = torch.cat([_dense(t, p + "q_a_proj"), _dense(t, p + "kv_a_proj_with_mqa"), _dense(t, p + "indexer.wk"),
                    _dense(t, p + "indexer.weights_proj")], 0)
     _set_linear(a.in_proj, w)
@@ -149,7 +151,7 @@ def _load_mla(a, t, p, tp, r):
     _set(a.kv_a_norm_w, _get(t, p + "kv_a_layernorm.weight"))
     _set_linear(a.q_b, _rows(_dense(t, p + "q_b_proj"), tp, r))
     kvb = _rows(_dense(t, p + "kv_b_proj").view(m.num_heads, a.dn + a.dv, a.kvl), tp, r)
-    _set(a.w_uk, kvb[:, :a.dn])
+    _set(a.w_uk_t, kvb[:, :a.dn].transpose(1, 2))
     _set(a.w_uv_t, kvb[:, a.dn:])
     _set_linear(a.o_proj, _cols(_dense(t, p + "o_proj"), tp, r))
     _set_linear(a.idx_q, _dense(t, p + "indexer.wq_b"))
@@ -380,7 +382,7 @@ def export_hf(model) -> dict[str, torch.Tensor]:
             out[q + "q_a_layernorm.weight"] = a.q_a_norm.weight.detach()
             out[q + "kv_a_layernorm.weight"] = a.kv_a_norm_w.detach()
             put(q + "q_b_proj", a.q_b)
-            out[q + "kv_b_proj.weight"] = torch.cat([a.w_uk.detach(), a.w_uv_t.detach()], 1).reshape(-1, a.kvl)
+            out[q + "kv_b_proj.weight"] = torch.cat([a.w_uk_t.detach().transpose(1, 2), a.w_uv_t.detach()], 1).reshape(-1, a.kvl)
             put(q + "o_proj", a.o_proj)
             put(q + "indexer.wq_b", a.idx_q)
             out[q + "indexer.k_norm.weight"] = a.idx_k_ln_w.detach()

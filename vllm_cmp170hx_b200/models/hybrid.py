@@ -142,6 +142,17 @@ class MLAAttention(nn.Module):
         assert m.num_heads % tp == 0
         self.H = m.num_heads // tp
         self.eps = cfg.rms_eps
+        from .. import envs
+
+        # With expert parallelism every rank holds all heads (bf16 projections): steps in the
+        # sequence-parallel layout attend data-parallel (each rank its own tokens, all heads, no
+        # collective), steps in the replicated layout use this rank's head slice [h0, h0 + H).
+        self.full_heads = (tp > 1 and pstate.get().expert_parallel and m.attn_weight_format != "fp8_block"
+                           and envs.get("VLLM_B200_MLA_DP"))
+        self.H_all = m.num_heads if self.full_heads else self.H
+        self.h0 = tp_rank * self.H if self.full_heads else 0
+        if self.full_heads:
+            tp, tp_rank = 1, 0
         sd = default_std(hid)
         ql, kvl = m.q_lora_rank, m.kv_lora_rank
         self.ql, self.kvl = ql, kvl
@@ -161,9 +172,10 @@ class MLAAttention(nn.Module):
         self.q_a_norm = RMSNorm(wi.ones_plus(ql, 0.05), cfg.rms_eps)
         self.kv_a_norm_w = nn.Parameter(wi.ones_plus(kvl, 0.05), requires_grad=False)
         self.q_b = Proj(wi.normal((m.num_heads * (dn + dr), ql), default_std(ql), (0, tp_rank, tp)))
-        # kv_b: [H*(dn + dv), kvl] -> absorbed per-head W_UK [H, dn, kvl], W_UV [H, kvl, dv]
+        # kv_b: [H*(dn + dv), kvl] -> per-head W_UK (stored transposed, [H, kvl, dn]: the absorb GEMM's
+        # K-major operand) and W_UV ([H, dv, kvl]: the up-projection's)
         kvb = wi.normal((m.num_heads, dn + dv, kvl), default_std(kvl), (0, tp_rank, tp))
-        self.w_uk = nn.Parameter(kvb[:, :dn, :].contiguous(), requires_grad=False)  # [H, dn, kvl]
+        self.w_uk_t = nn.Parameter(kvb[:, :dn, :].transpose(1, 2).contiguous(), requires_grad=False)
         self.w_uv_t = nn.Parameter(kvb[:, dn:, :].contiguous(), requires_grad=False)  # [H, dv, kvl]
         self.o_proj = Proj(wi.normal((hid, m.num_heads * dv), default_std(m.num_heads * dv), (1, tp_rank, tp)))
         # indexer
@@ -197,15 +209,58 @@ class MLAAttention(nn.Module):
         q8, wq = mla_ops.index_q_prep(iq, pos, self.cos_sin, m.rope_interleave, w_idx, self.idx_wscale)
         indices, counts = mla_ops.indexer_topk(q8, wq, idx_k, idx_s, ctx.ctx_lens, ctx.token_seq, ctx.block_table, 64,
                                                m.index_topk, ctx.max_ctx, ctx.scores_buf)
-        # queries: rope part, absorbed nope part
-        q = self.q_b(q_lat).view(T, self.H, self.dn + dr)
-        mla_ops.rope_(q, pos, self.cos_sin, self.dn, dr, m.rope_interleave)
-        qf = torch.empty(T, self.H, kvl + dr, dtype=torch.bfloat16, device=x.device)
-        torch.bmm(q[:, :, : self.dn].transpose(0, 1), self.w_uk, out=qf[:, :, :kvl].transpose(0, 1))
-        qf[:, :, kvl:] = q[:, :, self.dn:]
+        o = self._heads(q_lat, pos, indices, counts, latent, self.h0, self.H)
+        if self.full_heads:  # this rank's head slice of the whole o_proj, summed over the group
+            return comm.gemm_all_reduce(o, self.o_proj.weight[:, self.h0 * self.dv:(self.h0 + self.H) * self.dv])
+        return self.o_proj.forward_reduced(o)
+
+    def _heads(self, q_lat, pos, indices, counts, latent, h0: int, H: int) -> torch.Tensor:
+        """Heads [h0, h0 + H) of the queries q_lat [n, q_lora]: q_b, RoPE, W_UK absorb, latent attention
+        over the selected rows, W_UV up-projection -> the o_proj input [n, H * dv]."""
+        m, kvl, dr, dn = self.m, self.kvl, self.dr, self.dn
+        n = q_lat.shape[0]
+        if self.full_heads:  # the heads' rows of the whole q_b
+            q = ops.gemm(q_lat, self.q_b.weight[h0 * (dn + dr):(h0 + H) * (dn + dr)]).view(n, H, dn + dr)
+        else:
+            q = self.q_b(q_lat).view(n, H, dn + dr)
+        qf = torch.empty(n, H, kvl + dr, dtype=torch.bfloat16, device=q_lat.device)
+        # rope part rotated straight into the query rows; absorbed nope part: per head q_nope W_UK
+        # (tcgen05 batched GEMM writing the first kvl dims of the same rows)
+        mla_ops.rope_into(q, pos, self.cos_sin, dn, dr, m.rope_interleave, qf, kvl)
+        ops.bmm(q[:, :, :dn].transpose(0, 1), self.w_uk_t[h0:h0 + H], out=qf[:, :, :kvl].transpose(0, 1))
         o_lat = mla_ops.sparse_attention(qf, latent, indices, counts, self.sm_scale)
-        o = torch.bmm(o_lat.transpose(0, 1), self.w_uv_t.transpose(1, 2))  # [H, T, dv]
-        return self.o_proj.forward_reduced(o.transpose(0, 1).reshape(T, self.H * self.dv))
+        # per-head up-projection W_UV, written head-interleaved as the o_proj input [n, H * dv]
+        o = torch.empty(n, H * self.dv, dtype=torch.bfloat16, device=q_lat.device)
+        ops.bmm(o_lat.transpose(0, 1), self.w_uv_t[h0:h0 + H], out=o.view(n, H, self.dv).transpose(0, 1))
+        return o
+
+    def forward_dp(self, x: torch.Tensor, ctx: StepContext, layer_idx: int, sp) -> torch.Tensor:
+        """Data-parallel attention of the sequence-parallel layout: x [T, hidden] all tokens (gathered);
+        every rank writes all tokens' cache rows (the caches stay replicated) and attends its own tokens
+        [rank Tr, (rank + 1) Tr) with all heads.  Returns the o_proj output of those tokens [Tr, hidden],
+        complete (no collective)."""
+        latent, idx_k, idx_s = ctx.mla_caches[layer_idx]
+        m = self.m
+        proj = self.in_proj(x)
+        ql, kvl, dr = self.ql, self.kvl, self.dr
+        kv = proj[:, ql: ql + kvl + dr]
+        k_idx = proj[:, ql + kvl + dr: ql + kvl + dr + m.index_head_dim]
+        pos = ctx.positions
+        mla_ops.latent_cache_write(kv, self.kv_a_norm_w, self.eps, pos, self.cos_sin, m.rope_interleave,
+                                   ctx.slot_mapping, latent)
+        mla_ops.index_k_write(k_idx, self.idx_k_ln_w, self.idx_k_ln_b, 1e-6, pos, self.cos_sin, m.rope_interleave,
+                              ctx.slot_mapping, idx_k, idx_s)
+        loc = slice(sp.rank * sp.Tr, (sp.rank + 1) * sp.Tr)
+        Tr = sp.Tr
+        q_lat = self.q_a_norm(proj[loc, :ql].contiguous())
+        w_idx = proj[loc, ql + kvl + dr + m.index_head_dim:]
+        pos_l = pos[loc]
+        iq = self.idx_q(q_lat).view(Tr, m.index_n_heads, m.index_head_dim)
+        q8, wq = mla_ops.index_q_prep(iq, pos_l, self.cos_sin, m.rope_interleave, w_idx, self.idx_wscale)
+        indices, counts = mla_ops.indexer_topk(q8, wq, idx_k, idx_s, ctx.ctx_lens[loc], ctx.token_seq[loc],
+                                               ctx.block_table, 64, m.index_topk, ctx.max_ctx, ctx.scores_buf)
+        o = self._heads(q_lat, pos_l, indices, counts, latent, 0, self.H_all)
+        return ops.gemm(o, self.o_proj.weight)
 
 
 # ============================================================================ MLPs
@@ -525,10 +580,18 @@ class DecoderLayer(nn.Module):
         """Sequence-parallel layer (the step's tokens sharded over the group, parallel/sp.py).
         `pending` is how the layer input reaches this rank's residual rows: ("local", x) for the
         embeddings, ("rs", None) for a reduce-scattered projection, ("comb", shared_out) for a combined
-        MoE output.  Returns the pending form of this layer's output."""
-        src, arg = pending
-        sp.norm(src, residual, self.input_norm.weight, self.input_norm.eps, x=arg if src == "local" else None,
-                add=arg if src == "comb" else None, ag=True)
+        MoE output, ("add", a) for rows computed on this rank.  Returns the pending form of this
+        layer's output."""
+        sp.apply(pending, residual, self.input_norm.weight, self.input_norm.eps, ag=True)
+        if isinstance(self.attn, MLAAttention) and self.attn.full_heads:
+            # data-parallel attention: this rank's tokens, all heads, output complete on this rank
+            a = self.attn.forward_dp(sp.gathered(), ctx, self.idx, sp)
+            if self.mlp is None:
+                return ("add", a)
+            h = torch.empty_like(residual)
+            sp.norm("add", residual, self.post_norm.weight, self.post_norm.eps, x=a, out=h,
+                    ag=not isinstance(self.mlp, MoE))
+            return self._mlp_sp(sp, residual, h)
         with sp_scope(sp):
             # the attention's first read of the gathered rows is its input GEMM, which waits for the
             # all-gather itself when it is a bf16 projection; otherwise wait before the attention
@@ -536,12 +599,16 @@ class DecoderLayer(nn.Module):
             self.attn(sp.gathered(wait=not isinstance(first, Linear)), ctx, self.idx)
         if self.mlp is None:
             return ("rs", None)
+        h = torch.empty_like(residual)
+        sp.norm("rs", residual, self.post_norm.weight, self.post_norm.eps, out=h, ag=not isinstance(self.mlp, MoE))
+        return self._mlp_sp(sp, residual, h)
+
+    def _mlp_sp(self, sp, residual: torch.Tensor, h: torch.Tensor) -> tuple:
+        """The MLP half of a sequence-parallel layer; h [Tr, hidden] the post-attention norm of this
+        rank's tokens (also all-gathered when the MLP is a dense tensor-parallel one)."""
         if isinstance(self.mlp, MoE):
-            h = torch.empty_like(residual)
-            sp.norm("rs", residual, self.post_norm.weight, self.post_norm.eps, out=h)
             return ("comb", self.mlp.forward_sp(h, sp))
-        # dense MLP, tensor parallel: all-gather in, reduce-scatter out
-        sp.norm("rs", residual, self.post_norm.weight, self.post_norm.eps, ag=True)
+        # dense MLP, tensor parallel: all-gather in (pushed by the norm), reduce-scatter out
         with sp_scope(sp):
             self.mlp(sp.gathered(), reduce=True)
         return ("rs", None)
@@ -553,8 +620,7 @@ class DecoderLayer(nn.Module):
         else:
             h = self.input_norm(x, residual)
         a = self.attn(h, ctx, self.idx)  # row-parallel o_proj: already summed over the TP group
-        if self.mlp is None:
-            residual = residual + a
+        if self.mlp is None:  # the next layer's fused norm adds the attention output
             return a, residual
         h = self.post_norm(a, residual)
         return self.mlp(h, reduce=True), residual
@@ -663,8 +729,7 @@ class HybridForCausalLM(nn.Module):
         pending = ("local", x)
         for layer in self.layers:
             pending = layer.forward_sp(sp, residual, pending, ctx)
-        src, arg = pending
-        sp.norm(src, residual, self.norm.weight, self.norm.eps, add=arg if src == "comb" else None, ag=True)
+        sp.apply(pending, residual, self.norm.weight, self.norm.eps, ag=True)
         return sp.gathered(wait=True)
 
     def kda_recover(self, ctx: StepContext, keep: torch.Tensor) -> None:

@@ -44,7 +44,23 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
             raise ValueError("the all-gather GEMM takes no bias")
         spa.gemm_ag(x2, w, o2)
         return out
+    if splits == 0:
+        from .. import envs
+
+        splits = envs.get("VLLM_B200_GEMM_SPLITK")
     _ext.ops().gemm_bf16_out(x2, w, bias, o2, _ext.status_word(x.device), splits)
+    return out
+
+
+def bmm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[b] = x[b] @ w[b]^T for x [B, M, K], w [B, N, K] (bf16, fp32 accumulate; any strides with a unit
+    inner one, e.g. per-head slices of a [T, H, D] tensor transposed to [H, T, D])."""
+    if out is None:
+        out = torch.empty(x.shape[0], x.shape[1], w.shape[1], dtype=torch.bfloat16, device=x.device)
+    if not _native(x):
+        out.copy_(torch.bmm(x.float(), w.float().transpose(1, 2)).to(out.dtype))
+        return out
+    _ext.ops().gemm_batched(x, w, out, _ext.status_word(x.device))
     return out
 
 

@@ -18,6 +18,18 @@ def rope_(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, offse
     return x
 
 
+def rope_into(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, offset: int, rot_dim: int,
+              interleaved: bool, out: torch.Tensor, out_offset: int) -> torch.Tensor:
+    """out[:, :, out_offset:out_offset + rot_dim] = RoPE of x[:, :, offset:offset + rot_dim] (one kernel:
+    the MLA query's rope dims go straight next to its absorbed part)."""
+    if not x.is_cuda:
+        y = _ref.rope(x, positions, cos_sin, offset, rot_dim, interleaved)
+        out[:, :, out_offset:out_offset + rot_dim] = y[:, :, offset:offset + rot_dim]
+        return out
+    _ext.ops().rope(x, positions, cos_sin, offset, rot_dim, interleaved, out, out_offset)
+    return out
+
+
 def latent_cache_write(kv, norm_w, eps, positions, cos_sin, interleaved, slots, cache):
     if not kv.is_cuda:
         rows = _ref.latent_row(kv, norm_w, eps, positions, cos_sin, interleaved)
@@ -87,9 +99,17 @@ def pick_splits(T: int, nh: int, topk: int = 2048, num_sms: int = 148, max_parti
                 block_us: float = 2.0, merge_bytes_per_us: float = 5e6) -> int:
     """Position splits of the block attention kernel (blocks of 128 positions): the count with the
     least estimated time = waves x blocks per CTA x the time of one block on one SM, plus the merge
-    pass over the fp32 partial outputs (written and read once) when split."""
+    pass over the fp32 partial outputs (written and read once) when split.  VLLM_B200_SPARSE_MLA_SPLITS
+    forces the count."""
+    from .. import envs
+
+    forced = envs.get("VLLM_B200_SPARSE_MLA_SPLITS")
+    if forced > 0:
+        return min(forced, max(1, (topk + 127) // 128))
+    from ..tuning_table import lookup
+
     base = T * ((nh + 127) // 128) * 2  # CTAs per split: tokens x head groups x latent halves
-    nblk = max(1, (topk + 127) // 128)
+    nblk = max(1, min((topk + 127) // 128, lookup("sparse_mla", "max_splits", {}, 8)))
     best, best_cost = 1, None
     for s in range(1, nblk + 1):
         part = s * T * nh * 512 * 4

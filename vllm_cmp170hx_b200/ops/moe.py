@@ -88,10 +88,19 @@ def topk(logits: torch.Tensor, k: int, mode: int = 0, bias: torch.Tensor | None 
 
 
 def pick_tile_rows(T: int, k: int, E_local: int) -> int:
+    from .. import envs
+
+    forced = envs.get("VLLM_B200_EXL3_TILE_ROWS")
+    if forced:
+        if forced not in (16, 32, 64, 128):
+            raise ValueError(f"VLLM_B200_EXL3_TILE_ROWS={forced}: 16, 32, 64 or 128")
+        return forced
+    from ..tuning_table import lookup
+
     avg = max(1, T * k // max(1, E_local))
-    for t in (16, 32, 64):
-        if avg <= t // 2:
-            return t
+    for max_avg, tile in lookup("exl3_moe", "tile_rows_by_avg_rows", {}, ((8, 16), (16, 32), (32, 64))):
+        if avg <= max_avg:
+            return tile
     return 128
 
 

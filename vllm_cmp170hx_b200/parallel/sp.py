@@ -65,6 +65,13 @@ class _Base:
     def local_slice(self, t: torch.Tensor) -> torch.Tensor:
         return t[self.rank * self.Tr:(self.rank + 1) * self.Tr]
 
+    def apply(self, pending: tuple, residual: torch.Tensor, w: torch.Tensor, eps: float, ag: bool = False,
+              out: torch.Tensor | None = None):
+        """The residual update a layer left pending (see DecoderLayer.forward_sp), then the norm."""
+        src, arg = pending
+        return self.norm(src, residual, w, eps, x=arg if src in ("local", "add") else None,
+                         add=arg if src == "comb" else None, ag=ag, out=out)
+
 
 class TorchSP(_Base):
     """The layout over torch.distributed collectives of the tensor-parallel group."""
@@ -97,6 +104,8 @@ class TorchSP(_Base):
              add: torch.Tensor | None = None, ag: bool = False, out: torch.Tensor | None = None):
         if src == "local":
             residual.copy_(x)
+        elif src == "add":
+            residual.copy_(_bf16_add(residual, x))
         else:
             y = self._rs if src == "rs" else self._comb
             if src == "comb" and add is not None:
@@ -194,7 +203,7 @@ class FusedSP(_Base):
     # ---------------------------------------------------------------- residual + norm (+ all-gather)
     def norm(self, src: str, residual: torch.Tensor, w: torch.Tensor, eps: float, x: torch.Tensor | None = None,
              add: torch.Tensor | None = None, ag: bool = False, out: torch.Tensor | None = None):
-        code = {"local": 0, "rs": 1, "comb": 2}[src]
+        code = {"local": 0, "rs": 1, "comb": 2, "add": 3}[src]
         _ext.ops().sp_residual_norm(*self._sync(), code, x, add, self.dmask if code == 2 else None, self.rs_off,
                                     self.comb_off, self.ag_off, residual, w, float(eps), out, ag)
         if ag:

@@ -147,29 +147,43 @@ def sp_max_tokens(engine) -> int:
     """Largest step the sequence-parallel buffers take: the decode graphs' batch (times the verify
     width), at least 256 tokens; larger steps (prefill chunks) take the all-reduce layout."""
     c = engine.cfg
+    from ..tuning_table import lookup
+
     per = 1 + max(0, c.scheduler.num_speculative_tokens)
     graphs = max(c.cuda_graph_batch_sizes or [0])
-    return max(256, min(4096, max(graphs, c.scheduler.max_num_seqs) * per))
+    return max(lookup("sp", "min_max_tokens", {}, 256), min(4096, max(graphs, c.scheduler.max_num_seqs) * per))
 
 
 def enable_for_engine(engine) -> bool:
     """Switch the engine's TP all-reduces to the symmetric-memory kernel when
     every rank can set it up; returns whether it is active."""
+    from .. import envs
+
     st = pstate.get()
     if st.tp_size == 1 or st.device.type != "cuda":
         return False
+    transport = envs.get("VLLM_B200_ALLREDUCE")
+    if transport not in ("symm", "nccl"):
+        raise ValueError(f"VLLM_B200_ALLREDUCE={transport!r}: 'symm' or 'nccl'")
+    envs.log_gate("symmetric-memory collectives", transport == "symm", "VLLM_B200_ALLREDUCE=nccl")
+    if transport == "nccl":
+        return False
+    wait_s = envs.get("VLLM_B200_ALLREDUCE_WAIT_S")
     symm = fused = None
     try:
-        symm = SymmComm(st.tp_group, st.tp_cpu_group, st.device)
+        from ..tuning_table import lookup
+
+        max_bytes = envs.get("VLLM_B200_ALLREDUCE_MAX_BYTES") or lookup("allreduce", "symm_max_bytes", {}, 16 << 20)
+        symm = SymmComm(st.tp_group, st.tp_cpu_group, st.device, max_bytes=max_bytes, timeout_s=wait_s)
         ok = True
     except Exception as e:  # noqa: BLE001 -- any setup failure falls back on every rank
         log.warning("symmetric-memory all-reduce unavailable on rank %d: %s", st.rank, e)
         ok = False
     ok = _agree(ok, st.tp_cpu_group)
     fused_ok = False
-    if ok and engine.cfg.parallel.fused_comm:
+    if ok and engine.cfg.parallel.fused_comm and envs.get("VLLM_B200_FUSED_GEMM_AR"):
         try:
-            fused = FusedComm(st.tp_group, st.tp_cpu_group, st.device)
+            fused = FusedComm(st.tp_group, st.tp_cpu_group, st.device, timeout_s=wait_s)
             fused_ok = True
         except Exception as e:  # noqa: BLE001
             log.warning("fused compute + all-reduce kernels unavailable on rank %d: %s", st.rank, e)
@@ -177,14 +191,14 @@ def enable_for_engine(engine) -> bool:
     comm.enable_fused(symm if ok else None, fused if fused_ok else None)
     model = engine.runner.model
     p = engine.cfg.parallel
-    if (fused_ok and st.expert_parallel and p.sequence_parallel and hasattr(model, "supports_sp")
-            and model.supports_sp()):
+    if (ok and p.fused_comm and st.expert_parallel and p.sequence_parallel
+            and envs.get("VLLM_B200_EP_DISPATCH") == "symm" and hasattr(model, "supports_sp") and model.supports_sp()):
         from .sp import FusedSP
 
         sp = None
         try:
             sp = FusedSP(st.tp_group, st.tp_cpu_group, st.device, model.cfg.hidden_size, model.cfg.moe.top_k,
-                         max_tokens=sp_max_tokens(engine))
+                         max_tokens=sp_max_tokens(engine), timeout_s=wait_s)
             sp_ok = True
         except Exception as e:  # noqa: BLE001 -- any setup failure falls back on every rank
             log.warning("sequence-parallel kernels unavailable on rank %d: %s", st.rank, e)

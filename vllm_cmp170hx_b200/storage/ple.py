@@ -30,7 +30,7 @@ from ..formats import ple as fple
 
 class PleTable:
     def __init__(self, path: str, prefix: str, owner_lo: int = 0, owner_hi: int | None = None, *,
-                 cache_rows: int = 1 << 16, ways: int = 8, threads: int = 8, retries: int = 3,
+                 cache_rows: int | None = None, ways: int = 8, threads: int = 8, retries: int | None = None,
                  o_direct: bool = False, device=None, group=None):
         self.layout = lay = fple.read_layout(path, prefix)
         owner_hi = lay.rows if owner_hi is None else owner_hi
@@ -50,6 +50,9 @@ class PleTable:
         self.layer_multipliers = aux["layer_multipliers"]
         self._offs_cpu, self._vocab_cpu = aux["head_offsets"], aux["head_vocab_sizes"]
         C = _ext.load()
+        from .tables import storage_defaults
+
+        cache_rows, retries = storage_defaults(lay.row_bytes, cache_rows, retries)
         self.reader = C.RowReader(path, lay.row_bytes, lay.rows, threads, retries, o_direct, lay.base)
         self.cache = C.RowCache(self.reader, cache_rows, ways)
         self._pinned = None

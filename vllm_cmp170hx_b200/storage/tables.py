@@ -54,12 +54,28 @@ def write_table(path: str, x: torch.Tensor) -> None:
     quantize_rows(x).tofile(path)
 
 
+def storage_defaults(row_bytes: int, cache_rows: int | None, retries: int | None) -> tuple[int, int]:
+    """Host-cache rows and read retries of a storage-backed table: the arguments when given, else
+    VLLM_B200_ROW_CACHE_GIB worth of rows (0: 65536 rows) and VLLM_B200_PLE_READ_RETRIES."""
+    from .. import envs
+
+    if cache_rows is None:
+        gib = envs.get("VLLM_B200_ROW_CACHE_GIB")
+        cache_rows = max(1024, int(gib * (1 << 30)) // max(1, row_bytes)) if gib > 0 else 1 << 16
+    if retries is None:
+        retries = envs.get("VLLM_B200_PLE_READ_RETRIES")
+    return cache_rows, retries
+
+
 class RowTable:
-    def __init__(self, path: str, num_rows: int, dim: int, cache_rows: int = 1 << 16, ways: int = 8,
-                 threads: int = 8, retries: int = 3, o_direct: bool = False, device=None):
+    def __init__(self, path: str, num_rows: int, dim: int, cache_rows: int | None = None, ways: int = 8,
+                 threads: int = 8, retries: int | None = None, o_direct: bool = False, device=None):
+        """cache_rows / retries default to VLLM_B200_ROW_CACHE_GIB (as rows; 0: 65536 rows) and
+        VLLM_B200_PLE_READ_RETRIES."""
         C = _ext.load()
         self.dim = dim
         self.row_bytes = row_bytes(dim)
+        cache_rows, retries = storage_defaults(self.row_bytes, cache_rows, retries)
         self.reader = C.RowReader(path, self.row_bytes, num_rows, threads, retries, o_direct)
         self.cache = C.RowCache(self.reader, cache_rows, ways)
         self.device = torch.device(device) if device is not None else None

@@ -49,6 +49,11 @@ def card_file(device_name: str) -> Path:
     return TABLE_DIR / (re.sub(r"[^a-z0-9]+", "-", device_name.lower()).strip("-") + ".toml")
 
 
+def _frozen(v):
+    """Array values as (nested) tuples: rows are hashable and their values immutable."""
+    return tuple(_frozen(x) for x in v) if isinstance(v, list) else v
+
+
 def parse(text: str, source: str = "<table>") -> list[Row]:
     d = tomllib.loads(text)
     if d.get("schema") != SCHEMA:
@@ -60,7 +65,7 @@ def parse(text: str, source: str = "<table>") -> list[Row]:
     for i, r in enumerate(d.get("row", [])):
         if set(r) != {"op", "param", "key", "value", "evidence"}:
             raise TuningTableError(f"{source}: row {i} must have exactly op, param, key, value, evidence")
-        rows.append(Row(r["op"], r["param"], tuple(sorted(r["key"].items())), r["value"], r["evidence"]))
+        rows.append(Row(r["op"], r["param"], tuple(sorted(r["key"].items())), _frozen(r["value"]), r["evidence"]))
     return rows
 
 
