@@ -132,3 +132,35 @@ def test_synthetic_prefix_skips_prefill(model):
             if o.finished:
                 done[o.request_id] = o
     assert sorted(done) == sorted(ids) and all(len(o.output_token_ids) == 3 for o in done.values())
+
+
+def _mla_cfg(prefix_caching):
+    from vllm_cmp170hx_b200.config import tiny_deepseek
+
+    m = tiny_deepseek(layers=2, experts=4, hidden=256, vocab=512)
+    m.mla.attn_weight_format = "bf16"
+    return EngineConfig(model=m, scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=512,
+                                                           max_model_len=512),
+                        cache=CacheConfig(num_blocks=32, enable_prefix_caching=prefix_caching), device="cpu",
+                        enforce_eager=True)
+
+
+def test_prefix_caching_reuses_blocks_and_keeps_outputs():
+    """A second request sharing a 2-block prefix with a finished one starts after the cached blocks and
+    generates what it generates without the cache."""
+    pstate.set_state(pstate.ParallelState())
+    base = [(13 * j) % 500 for j in range(150)]
+    prompts = [base + [1, 2, 3], base[:140] + [7, 8]]
+    p = SamplingParams(max_tokens=3)
+    model = HybridForCausalLM(_mla_cfg(False).model, "cpu", seed=2, init_mode="sliced")
+    ref = [o.output_token_ids for o in LLM(_mla_cfg(False), model).generate(prompts, p)]
+    eng = LLMEngine(_mla_cfg(True), model)
+    outs = []
+    for prompt in prompts:  # one after the other: the second sees the first's registered blocks
+        eng.add_request(prompt, p)
+        while eng.has_unfinished():
+            for o in eng.step():
+                if o.finished:
+                    outs.append(o.output_token_ids)
+    assert outs == ref
+    assert eng.scheduler.prefix_hits == 128  # two full 64-token blocks of the shared prefix

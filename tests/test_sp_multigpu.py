@@ -139,7 +139,7 @@ def _cfg(tp):
                         cache=CacheConfig(num_blocks=64), device="cuda", cuda_graph_batch_sizes=[2, 4, 8])
 
 
-def _generate(tp, fused):
+def _generate(tp, fused, expect_sp=None):
     """Greedy tokens, and the full-vocabulary logits of the first three steps (gathered over the vocab
     shards) of the tiny expert-parallel model."""
     import torch.distributed as dist
@@ -173,20 +173,27 @@ def _generate(tp, fused):
         from vllm_cmp170hx_b200.parallel import symm
 
         assert symm.enable_for_engine(llm.engine)
-        assert comm._FUSED["sp"] is not None and comm._FUSED["sp"].fused
+        sp = comm._FUSED["sp"]
+        if expect_sp == "fused":
+            assert sp is not None and sp.fused
+        elif expect_sp == "torch":
+            assert sp is not None and not sp.fused
+        elif expect_sp == "none":
+            assert sp is None
     outs = llm.generate(PROMPTS, SamplingParams(max_tokens=6))
     return [o.output_token_ids for o in outs], seen
 
 
-def _engine_worker(rank, world, port, q):
+def _engine_worker(rank, world, port, q, env):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0", **env)
     from vllm_cmp170hx_b200 import _ext
     from vllm_cmp170hx_b200.parallel import state as pstate
 
     try:
         st = pstate.init(tp_size=world, timeout_s=60)
-        toks = _generate(world, True)
+        expect = {"symm": "fused", "nccl": "torch", "off": "none"}[env["VLLM_B200_EP_DISPATCH"]]
+        toks = _generate(world, True, expect)
         _ext.check_status(st.device)
         q.put((rank, toks))
     except Exception as e:  # noqa: BLE001
@@ -197,30 +204,54 @@ def _engine_worker(rank, world, port, q):
         pstate.destroy()
 
 
-def test_sp_engine_tp2_matches_one_gpu():
-    """The first three steps' logits (a 256-token and a 100-token prefill chunk and a decode step, all in
-    the sequence-parallel layout at TP=2) agree with one GPU's to bf16 rounding of the partial sums, and
-    greedy decoding gives the same tokens except where two logits are that close."""
+_REF = {}
+
+
+def _reference():
+    if "ref" not in _REF:
+        ctx = mp.get_context("spawn")
+        q = ctx.Queue()
+        p = ctx.Process(target=_single, args=(q,))
+        p.start()
+        _REF["ref"] = q.get(timeout=600)
+        p.join(timeout=60)
+    return _REF["ref"]
+
+
+@pytest.mark.parametrize("dispatch,mla_dp", [("symm", "1"), ("symm", "0"), ("nccl", "1"), ("off", "1")])
+def test_sp_engine_tp2_matches_one_gpu(dispatch, mla_dp):
+    """The first three steps' logits (a 256-token and a 100-token prefill chunk and a decode step) at TP=2
+    agree with one GPU's to bf16 rounding of the partial sums, and greedy decoding gives the same tokens
+    except where two logits are that close: the sequence-parallel layout on the fused kernels or on
+    torch.distributed, with the MLA layers data-parallel or head-parallel, and the replicated layout."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 or more GPUs")
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    p = ctx.Process(target=_single, args=(q,))
-    p.start()
-    ref = q.get(timeout=600)
-    p.join(timeout=60)
+    ref = _reference()
     assert not isinstance(ref, str), ref
-    res = _run(_engine_worker, 2, 27700 + os.getpid() % 400)
+    env = {"VLLM_B200_EP_DISPATCH": dispatch, "VLLM_B200_MLA_DP": mla_dp}
+    res = _run_env(env)
     assert not isinstance(res[0], str), res[0]
     toks, logits = res[0]
     ref_toks, ref_logits = ref
     assert len(logits) == len(ref_logits) == 3
-    for a, b in zip(logits, ref_logits):
-        a, b = torch.from_numpy(a), torch.from_numpy(b)
-        assert a.shape == b.shape
-        assert _rel(a, b) < 5e-2, _rel(a, b)
+    errs = [_rel(torch.from_numpy(a), torch.from_numpy(b)) for a, b in zip(logits, ref_logits)]
+    assert max(errs) < 5e-2, errs
     same = sum(x == y for x, y in zip(toks, ref_toks))
     assert same >= len(ref_toks) - 2, (toks, ref_toks)
+
+
+def _run_env(env):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 27700 + os.getpid() % 300 + 13 * len(_REF)
+    _REF["n"] = _REF.get("n", 0) + 1
+    procs = [ctx.Process(target=_engine_worker, args=(r, 2, port + _REF["n"], q, env)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    return res
 
 
 def _single(q):

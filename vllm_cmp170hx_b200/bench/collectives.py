@@ -54,14 +54,17 @@ def _graph_time_us(fn, iters: int) -> float:
             fn()
     g.replay()
     torch.cuda.synchronize()
-    dist.barrier()
+    multi = dist.is_initialized()
+    if multi:
+        dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     g.replay()
     b.record()
     torch.cuda.synchronize()
     t = torch.tensor([a.elapsed_time(b) * 1e3 / iters], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if multi:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
     del g
     return float(t.item())
 
@@ -70,6 +73,8 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=128)
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--profile", action="store_true",
+                    help="rank 0 prints a per-kernel table of five eager calls of each path (guidance only)")
     a = ap.parse_args(argv)
     st = pstate.init(tp_size=int(os.environ.get("WORLD_SIZE", "1")), timeout_s=120)
     N, r = st.tp_size, st.tp_rank
@@ -167,6 +172,21 @@ def main(argv=None):
         "combine": (combine, dests * row, 0, 2.0 * TK * H),
     }
     for name, (mk, nv_bytes, hbm_bytes, flops) in paths.items():
+        if a.profile:
+            from torch.profiler import ProfilerActivity, profile
+
+            for tag, sp in (("fused", fsp), ("nccl", tsp)):
+                f = mk(sp)
+                f()
+                torch.cuda.synchronize()
+                with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                    for _ in range(5):
+                        f()
+                    torch.cuda.synchronize()
+                if r == 0:
+                    print(f"== {name} ({tag}), 5 calls", flush=True)
+                    print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=12, max_name_column_width=60),
+                          flush=True)
         t_f = _graph_time_us(mk(fsp), a.iters)
         t_n = _graph_time_us(mk(tsp), a.iters)
         roof_us = max(flops / (peaks["bf16_tflops"] * 1e12), hbm_bytes / (peaks["hbm_gbs"] * 1e9),

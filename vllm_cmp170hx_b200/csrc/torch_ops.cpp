@@ -433,6 +433,9 @@ void mla_indexer_scores_op(const at::Tensor& q8, const at::Tensor& w, const at::
   TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2, "indexer: block_table int32 [S, n]");
   c10::cuda::CUDAGuard g(q8.device());
   const int T = q8.size(0);
+  TORCH_CHECK(scores.size(0) >= T && ctx_lens.numel() >= T && w.numel() >= (int64_t)T * 64 &&
+                  (!token_seq.has_value() || token_seq->numel() >= T),
+              "indexer: scores / ctx_lens / token_seq / w must cover the ", T, " tokens of q8");
   B200_LAUNCH(mla_indexer_scores(q8.data_ptr(), w.data_ptr<float>(), T, k_cache.data_ptr(), k_cache.numel() / 128,
                                  k_scale.data_ptr<float>(), ctx_lens.data_ptr<int>(),
                                  token_seq.has_value() ? token_seq->data_ptr<int>() : nullptr,
@@ -446,11 +449,17 @@ void mla_topk_op(const at::Tensor& scores, const at::Tensor& ctx_lens, int64_t k
   B200_CHECK_CUDA(scores);
   TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.stride(1) == 1, "topk: scores fp32");
   TORCH_CHECK(out_idx.scalar_type() == at::kInt && out_idx.is_contiguous() && out_idx.size(1) == k, "topk: out");
+  // the tokens are out_idx's rows; the scores buffer may hold more rows (a graph's shared buffer)
+  const int64_t T = out_idx.size(0);
+  TORCH_CHECK(scores.size(0) >= T && ctx_lens.numel() >= T && out_count.numel() >= T &&
+                  (!token_seq.has_value() || token_seq->numel() >= T),
+              "topk: scores / ctx_lens / token_seq / out_count must cover the ", T, " tokens of out_idx");
+  TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && out_count.scalar_type() == at::kInt, "topk: int32 lengths");
   c10::cuda::CUDAGuard g(scores.device());
   B200_LAUNCH(mla_topk(scores.data_ptr<float>(), scores.stride(0), ctx_lens.data_ptr<int>(), (int)k,
                        token_seq.has_value() ? token_seq->data_ptr<int>() : nullptr, block_table.data_ptr<int>(),
                        block_table.stride(0), (int)block_size, out_idx.data_ptr<int>(), out_count.data_ptr<int>(),
-                       scores.size(0), cur_stream()));
+                       (int)T, cur_stream()));
 }
 
 void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& indices,
@@ -470,7 +479,10 @@ void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const
                 "sparse attn: sink fp32 [nh]");
   TORCH_CHECK(indices.scalar_type() == at::kInt && indices.is_contiguous() && indices.size(0) == q.size(0),
               "sparse attn: indices [T, topk] int32");
-  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(-1) == 512, "sparse attn: out");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(-1) == 512 &&
+                  out.numel() >= q.size(0) * q.size(1) * 512,
+              "sparse attn: out [T, nh, 512]");
+  TORCH_CHECK(counts.scalar_type() == at::kInt && counts.numel() >= q.size(0), "sparse attn: counts int32 [T]");
   c10::cuda::CUDAGuard g(q.device());
   const int T = q.size(0), nh = q.size(1);
   at::Tensor part_o, part_ml;

@@ -59,6 +59,11 @@ class Request:
     # cache rows and recurrent state are whatever the caches hold, e.g. random rows), so a long-context
     # decode can be measured without prefilling it
     synthetic_prefix: int = 0
+    # prefix caching: hashes of the prompt's full blocks (chained) and how many of this request's blocks
+    # are registered in the block pool's hash table
+    block_hashes: list[int] = field(default_factory=list)
+    num_cached_blocks: int = 0
+    num_prefix_hit_tokens: int = 0
 
     def __post_init__(self):
         if not self.request_id:

@@ -50,12 +50,28 @@ class SchedulerOutput:
         return bool(self.reqs) and all(s.num_new == 1 + s.num_draft and s.start > 0 for s in self.reqs)
 
 
+def block_hashes(tokens: list[int], block_size: int) -> list[int]:
+    """Chained hashes of the full blocks of `tokens`: block i's hash covers every token up to its end,
+    so equal hashes mean equal prefixes (ints only: the same on every rank and every run)."""
+    out, h = [], 0x9E3779B97F4A7C15
+    for i in range(len(tokens) // block_size):
+        h = hash((h, tuple(tokens[i * block_size:(i + 1) * block_size]))) & 0x7FFFFFFFFFFFFFFF
+        out.append(h)
+    return out
+
+
 class Scheduler:
     def __init__(self, sched: SchedulerConfig, cache: CacheConfig, block_pool, slot_pool=None):
         self.cfg = sched
         self.block_size = cache.block_size
         self.blocks = block_pool
         self.slots = slot_pool
+        # Prefix caching: a full block of computed prompt tokens is registered under its chained hash
+        # once the step that computed it succeeded; a later request whose prompt starts with the same
+        # blocks takes them (reference counted) and starts computing after them.  Models with
+        # recurrent state (KDA / DeepSeek-V4.1 rings) keep no per-block state, so it is off for them.
+        self.prefix_caching = bool(cache.enable_prefix_caching) and slot_pool is None
+        self.prefix_hits = 0  # tokens taken from the cache (metrics)
         self.waiting: collections.deque[Request] = collections.deque()
         self.running: list[Request] = []
         self.finished: list[Request] = []
@@ -106,11 +122,41 @@ class Scheduler:
 
     def _release(self, req: Request) -> None:
         if req.block_ids:
-            self.blocks.free(req.block_ids)
+            self.blocks.free(req.block_ids)  # registered blocks stay findable until reallocated (LRU)
             req.block_ids = []
+        req.num_cached_blocks = 0
         if self.slots is not None and req.kda_slot > 0:
             self.slots.free(req.kda_slot)
         req.kda_slot = -1
+
+    def _take_cached_prefix(self, req: Request) -> None:
+        """Reuse the longest run of cached leading blocks of the prompt (at least the last prompt token
+        is always computed, it is sampled from)."""
+        if not req.block_hashes:
+            req.block_hashes = block_hashes(req.prompt_token_ids, self.block_size)
+        hits = []
+        usable = (req.num_prompt_tokens - 1) // self.block_size
+        for h in req.block_hashes[:usable]:
+            b = int(self.blocks.lookup(h))
+            if b < 0:
+                break
+            hits.append(b)
+        for b in hits:
+            self.blocks.touch(b)
+        req.block_ids = hits
+        req.num_cached_blocks = len(hits)
+        req.num_computed_tokens = len(hits) * self.block_size
+        req.num_prefix_hit_tokens = req.num_computed_tokens
+        self.prefix_hits += req.num_computed_tokens
+
+    def _register_blocks(self, req: Request) -> None:
+        """Register the prompt blocks this request has fully computed under their hashes."""
+        if not req.block_hashes:
+            req.block_hashes = block_hashes(req.prompt_token_ids, self.block_size)
+        full = min(req.num_computed_tokens // self.block_size, len(req.block_hashes), len(req.block_ids))
+        for j in range(req.num_cached_blocks, full):
+            self.blocks.cache_block(req.block_ids[j], req.block_hashes[j])
+        req.num_cached_blocks = max(req.num_cached_blocks, full)
 
     def _preempt(self, victim: Request, out: SchedulerOutput) -> None:
         self.running.remove(victim)
@@ -174,6 +220,8 @@ class Scheduler:
                 break
             if req.synthetic_prefix and req.num_computed_tokens == 0:
                 req.num_computed_tokens = min(req.synthetic_prefix, req.num_prompt_tokens - 1)
+            elif self.prefix_caching and req.num_computed_tokens == 0 and not req.block_ids:
+                self._take_cached_prefix(req)
             n = min(req.num_tokens - req.num_computed_tokens, budget, cap)
             upto = req.num_computed_tokens + n
             if upto >= req.num_tokens:
@@ -207,7 +255,8 @@ class Scheduler:
                 continue
             toks = sampled.get(req.request_id, [])
             if FAILED_TOKEN in toks:
-                # no valid token from this step (poisoned inputs): finish with an error, drop the step
+                # no valid token from this step (poisoned inputs): finish with an error, drop the step;
+                # the blocks it computed are never registered for prefix reuse
                 req.status = Status.FINISHED_ERROR
                 req.draft_token_ids = []
                 done.append(req)
@@ -218,6 +267,8 @@ class Scheduler:
                 req.num_computed_tokens = s.start + 1 + accepted
             else:
                 req.num_computed_tokens = s.start + s.num_new
+            if self.prefix_caching:
+                self._register_blocks(req)
             req.draft_token_ids = []
             for t in toks:
                 req.output_token_ids.append(int(t))
