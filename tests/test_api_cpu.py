@@ -87,3 +87,66 @@ def test_server_command_line_reaches_engine_config():
     sc = cfg.scheduler
     assert (sc.num_speculative_tokens, sc.spec_method, sc.dflash_layers, sc.depth_policy, sc.adaptive_k,
             sc.max_num_seqs) == (3, "dflash", 2, "/tmp/p.json", "accept", 8)
+
+
+class _ScriptedEngine:
+    """Stands in for the engine: records each request's sampling params and replies with a fixed
+    text (byte tokens of the ByteTokenizer)."""
+
+    def __init__(self, tok, text):
+        self.tok, self.text, self.params = tok, text, []
+
+    async def generate(self, ids, params):
+        from types import SimpleNamespace
+
+        self.params.append(params)
+        out_ids = self.tok.encode(self.text)
+        half = len(out_ids) // 2
+        yield SimpleNamespace(new_token_ids=out_ids[:half], output_token_ids=out_ids[:half], finished=False,
+                              finish_reason=None)
+        yield SimpleNamespace(new_token_ids=out_ids[half:], output_token_ids=out_ids, finished=True,
+                              finish_reason="stop")
+
+
+@pytest.mark.parametrize("stream", [False, True])
+def test_glm_parser_and_tool_choice_none_mask(monkeypatch, stream):
+    from fastapi.testclient import TestClient
+
+    from vllm_cmp170hx_b200 import envs
+    from vllm_cmp170hx_b200.api.server import build_app
+    from vllm_cmp170hx_b200.api.tokenizer import ByteTokenizer
+
+    tok = ByteTokenizer(512)
+    tok.special_ids = dict(tok.special_ids, **{"<tool_call>": 2})
+    text = ("<think>look it up</think>On it.<tool_call>get_weather<arg_key>city</arg_key>"
+            "<arg_value>Oslo</arg_value></tool_call>")
+    eng = _ScriptedEngine(tok, text)
+    tools = [{"type": "function", "function": {"name": "get_weather", "parameters": {
+        "type": "object", "properties": {"city": {"type": "string"}}}}}]
+    monkeypatch.setenv("VLLM_B200_TOOL_CHOICE_NONE_MASK", "1")
+    envs._cache.clear()
+    try:
+        with TestClient(build_app(eng, tok, "glm", parser="glm47")) as c:
+            body = {"messages": [{"role": "user", "content": "weather?"}], "tools": tools, "stream": stream}
+            if stream:
+                with c.stream("POST", "/v1/chat/completions", json=body) as s:
+                    chunks = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: {")]
+                deltas = [ch["choices"][0]["delta"] for ch in chunks]
+                content = "".join(d.get("content", "") for d in deltas)
+                reasoning = "".join(d.get("reasoning_content", "") for d in deltas)
+                calls = [tc for d in deltas for tc in d.get("tool_calls", [])]
+                fin = chunks[-1]["choices"][0]["finish_reason"]
+            else:
+                m = c.post("/v1/chat/completions", json=body).json()["choices"][0]
+                content, reasoning = m["message"]["content"], m["message"]["reasoning_content"]
+                calls, fin = m["message"]["tool_calls"], m["finish_reason"]
+            assert (content, reasoning, fin) == ("On it.", "look it up", "tool_calls")
+            assert [(t["function"]["name"], json.loads(t["function"]["arguments"])) for t in calls] == \
+                [("get_weather", {"city": "Oslo"})]
+            assert eng.params[-1].bad_token_ids == []
+            # tool_choice="none": the opener is banned and the markup is not parsed as a call
+            r = c.post("/v1/chat/completions", json=dict(body, tool_choice="none", stream=False)).json()
+            assert eng.params[-1].bad_token_ids == [2]
+            assert "tool_calls" not in r["choices"][0]["message"]
+    finally:
+        envs._cache.clear()

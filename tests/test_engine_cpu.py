@@ -164,3 +164,20 @@ def test_prefix_caching_reuses_blocks_and_keeps_outputs():
                     outs.append(o.output_token_ids)
     assert outs == ref
     assert eng.scheduler.prefix_hits == 128  # two full 64-token blocks of the shared prefix
+
+
+def test_banned_tokens_are_never_sampled(model):
+    """A request's bad_token_ids (the decode mask of a tool_choice="none" request) never win: with the
+    greedy tokens of a first run banned, every step picks another token."""
+    prompts = [[(5 * i + 3 * j) % 500 for j in range(12 + 5 * i)] for i in range(3)]
+    free = LLM(_cfg(), model).generate(prompts, SamplingParams(max_tokens=1))
+    firsts = [o.output_token_ids[0] for o in free]
+    banned = [LLM(_cfg(), model).generate([p], SamplingParams(max_tokens=4, bad_token_ids=[t]))[0]
+              for p, t in zip(prompts, firsts)]
+    for o, t in zip(banned, firsts):
+        assert t not in o.output_token_ids
+    # the other requests of a batch are not affected
+    mixed = LLM(_cfg(), model).generate(prompts, [SamplingParams(max_tokens=1, bad_token_ids=[firsts[0]]),
+                                                  SamplingParams(max_tokens=1), SamplingParams(max_tokens=1)])
+    assert mixed[0].output_token_ids[0] != firsts[0]
+    assert [o.output_token_ids[0] for o in mixed[1:]] == firsts[1:]

@@ -50,3 +50,31 @@ def test_graph_decode_matches_eager():
     graph = LLM(_cfg("cuda", eager=False), model).generate(prompts, p)
     for a, b in zip(eager, graph):
         assert a.output_token_ids == b.output_token_ids
+
+
+def test_banned_tokens_in_kernel_and_graph():
+    """The sampling kernel skips each row's banned ids (against the CPU reference of the same rule), and
+    a graph-captured decode step applies them from its input buffer."""
+    from vllm_cmp170hx_b200.ops import sampling as sampling_ops
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    logits = torch.randn(6, 1000, device="cuda", generator=g).bfloat16()
+    top = logits.float().argmax(-1)
+    bans = torch.full((6, 4), -1, dtype=torch.int32, device="cuda")
+    bans[:, 0] = top.int()
+    bans[1, 1] = logits[1].float().topk(2).indices[1].int()
+    for off in (0, 500):  # the vocab shard's offset
+        val, idx = sampling_ops.sample_local(logits, None, 0, None, off, bans + off * (bans >= 0))
+        v_ref, i_ref = sampling_ops.sample_local(logits.cpu(), None, 0, None, off, (bans + off * (bans >= 0)).cpu())
+        assert idx.cpu().tolist() == i_ref.tolist()
+        assert all(int(i) - off != int(t) for i, t in zip(idx.cpu(), top.cpu()))
+    pstate.set_state(pstate.ParallelState())
+    model = HybridForCausalLM(_cfg("cuda").model, "cuda", seed=4, init_mode="local")
+    prompts = [list(range(10, 10 + n)) for n in (7, 66)]
+    free = LLM(_cfg("cuda", eager=False), model).generate(prompts, SamplingParams(max_tokens=4))
+    ban = free[0].output_token_ids[2]
+    ps = [SamplingParams(max_tokens=4, bad_token_ids=[ban]), SamplingParams(max_tokens=4)]
+    for eager in (True, False):
+        out = LLM(_cfg("cuda", eager=eager), model).generate(prompts, ps)
+        assert ban not in out[0].output_token_ids
+        assert out[1].output_token_ids == free[1].output_token_ids

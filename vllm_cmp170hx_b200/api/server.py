@@ -111,11 +111,22 @@ def _params(body: dict, default_max: int = 16) -> SamplingParams:
                           seed=body.get("seed"))
 
 
-def build_app(engine: AsyncEngine, tokenizer, model_name: str):
+def _think_open_in_prompt(tokenizer, ids: list[int]) -> bool:
+    """Whether the chat template opened the reasoning block at the end of the prompt."""
+    try:
+        return tokenizer.decode(ids[-4:]).rstrip().endswith(parsers.THINK_OPEN)
+    except Exception:  # noqa: BLE001 - a tokenizer without decode of special tokens
+        return False
+
+
+def build_app(engine: AsyncEngine, tokenizer, model_name: str, parser: str | None = None):
+    """The HTTP app.  ``parser`` names the reasoning / tool-call markup of the served model
+    (``api/parsers.PARSERS``: generic, glm45, glm47, ling3, deepseek_v41)."""
     from fastapi import FastAPI
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
     app = FastAPI(title="vllm_cmp170hx_b200")
+    family = parsers.get_family(parser)
 
     @app.get("/health")
     async def health():
@@ -173,23 +184,27 @@ def build_app(engine: AsyncEngine, tokenizer, model_name: str):
         messages = body.get("messages", [])
         ids = tokenizer.apply_chat_template(messages)
         params = _params(body)
-        tools_on = bool(body.get("tools")) and body.get("tool_choice", "auto") != "none"
+        params.bad_token_ids = parsers.tool_choice_none_bans(family, body, tokenizer)
+        tools, tool_choice = body.get("tools"), body.get("tool_choice", "auto")
+        think_open = _think_open_in_prompt(tokenizer, ids)
         cid = "chatcmpl-" + uuid.uuid4().hex[:24]
         if body.get("stream"):
             async def gen():
-                sp = parsers.StreamingParser(tools=tools_on)
+                sp = parsers.StreamParser(family, tools, tool_choice, think_open_in_prompt=think_open)
+                ncalls = 0
                 async for out in engine.generate(ids, params):
-                    r, c = sp.feed(tokenizer.decode(out.new_token_ids or []))
+                    r, c, calls = sp.feed(tokenizer.decode(out.new_token_ids or []))
                     if out.finished:
-                        r2, c2 = sp.finish()
-                        r, c = r + r2, c + c2
+                        r2, c2, calls2 = sp.finish()
+                        r, c, calls = r + r2, c + c2, calls + calls2
                     delta = {}
                     if r:
                         delta["reasoning_content"] = r
                     if c:
                         delta["content"] = c
-                    if out.finished and sp.calls:
-                        delta["tool_calls"] = [dict(t.to_openai(), index=i) for i, t in enumerate(sp.calls)]
+                    if calls:  # each call goes out whole, in the chunk where its closer arrived
+                        delta["tool_calls"] = [dict(t.to_openai(), index=ncalls + i) for i, t in enumerate(calls)]
+                        ncalls += len(calls)
                     fin = ("tool_calls" if sp.calls else out.finish_reason) if out.finished else None
                     chunk = {"id": cid, "object": "chat.completion.chunk", "model": model_name,
                              "choices": [{"index": 0, "delta": delta, "finish_reason": fin}]}
@@ -200,18 +215,15 @@ def build_app(engine: AsyncEngine, tokenizer, model_name: str):
         async for out in engine.generate(ids, params):
             last = out
         text = tokenizer.decode(last.output_token_ids)
-        reasoning, content = parsers.split_reasoning(text)
-        calls = []
-        if tools_on:
-            calls, content = parsers.parse_tool_calls(content)
-        msg = {"role": "assistant", "content": content or None}
-        if reasoning:
-            msg["reasoning_content"] = reasoning
-        if calls:
-            msg["tool_calls"] = [c.to_openai() for c in calls]
+        p = parsers.parse(text, family, tools, tool_choice, think_open_in_prompt=think_open)
+        msg = {"role": "assistant", "content": p.content or None}
+        if p.reasoning:
+            msg["reasoning_content"] = p.reasoning
+        if p.calls:
+            msg["tool_calls"] = [c.to_openai() for c in p.calls]
         return JSONResponse({"id": cid, "object": "chat.completion", "model": model_name,
                              "choices": [{"index": 0, "message": msg,
-                                          "finish_reason": "tool_calls" if calls else last.finish_reason}],
+                                          "finish_reason": "tool_calls" if p.calls else last.finish_reason}],
                              "usage": {"prompt_tokens": len(ids), "completion_tokens": len(last.output_token_ids),
                                        "total_tokens": len(ids) + len(last.output_token_ids)}})
 
@@ -259,6 +271,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--enforce-eager", action="store_true", help="no CUDA graphs")
     ap.add_argument("--nccl-collectives", action="store_true", help="TP collectives on NCCL (baseline path)")
     ap.add_argument("--no-warmup", action="store_true")
+    ap.add_argument("--tool-call-parser", "--reasoning-parser", dest="parser", default=None,
+                    choices=sorted(parsers.PARSERS),
+                    help="reasoning / tool-call markup of the served model (glm45, glm47, ling3, deepseek_v41)")
     return ap.parse_args(argv)
 
 
@@ -304,7 +319,12 @@ def main(argv=None):
         return
     import uvicorn
 
-    app = build_app(AsyncEngine(spmd), tok, args.model)
+    if args.parser in ("glm45", "glm47", "ling3"):
+        from .. import envs
+
+        envs.log_gate("tool_choice=none decode mask", bool(envs.get("VLLM_B200_TOOL_CHOICE_NONE_MASK")),
+                      "VLLM_B200_TOOL_CHOICE_NONE_MASK")
+    app = build_app(AsyncEngine(spmd), tok, args.model, parser=args.parser)
     uvicorn.run(app, host=args.host, port=args.port, log_level="info")
 
 

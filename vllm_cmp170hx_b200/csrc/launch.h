@@ -354,8 +354,8 @@ cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const vo
 
 // ---------------------------------------------------------------- sampling.cu
 cudaError_t sample_rows(const void* logits, int dtype, int64_t ld, int rows, int V, const float* temperature,
-                        uint64_t seed, const int64_t* step, int vocab_offset, float* out_val, int* out_idx,
-                        cudaStream_t stream);
+                        uint64_t seed, const int64_t* step, int vocab_offset, const int* bans, int nbans,
+                        float* out_val, int* out_idx, cudaStream_t stream);
 cudaError_t sample_combine(const float* vals, const int* idx, int R, int rows, int64_t* out, cudaStream_t stream);
 
 // ---------------------------------------------------------------- comm.cu

@@ -79,7 +79,7 @@ void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const
 
 void sample_rows_op(const at::Tensor& logits, const c10::optional<at::Tensor>& temperature, int64_t seed,
                     const c10::optional<at::Tensor>& step, int64_t vocab_offset, at::Tensor& out_val,
-                    at::Tensor& out_idx);  // sampling.cu
+                    at::Tensor& out_idx, const c10::optional<at::Tensor>& bans);  // sampling.cu
 void sample_combine_op(const at::Tensor& vals, const at::Tensor& idx, at::Tensor& out);  // sampling.cu
 
 void symm_all_reduce_op(const at::Tensor& in, at::Tensor& out, const at::Tensor& peers, int64_t rank, int64_t world,
@@ -189,7 +189,7 @@ void register_host_bindings(pybind11::module_& m);
   X("mla_sparse_attention(Tensor q, Tensor cache, Tensor indices, Tensor counts, float sm_scale, int splits, " \
     "Tensor(a!) out, Tensor(b!)? lse, Tensor(c!) status, Tensor? sink=None) -> ()")                      \
   X("sample_rows(Tensor logits, Tensor? temperature, int seed, Tensor? step, int vocab_offset, "          \
-    "Tensor(a!) out_val, Tensor(b!) out_idx) -> ()")                                                     \
+    "Tensor(a!) out_val, Tensor(b!) out_idx, Tensor? bans=None) -> ()")                                  \
   X("sample_combine(Tensor vals, Tensor idx, Tensor(a!) out) -> ()")                                     \
   X("symm_all_reduce(Tensor input, Tensor(a!) out, Tensor peers, int rank, int world, int data_off, "     \
     "int half_bytes, Tensor(b!) epochs, Tensor(c!) status, float timeout_s) -> ()")                       \

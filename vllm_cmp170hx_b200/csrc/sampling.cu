@@ -9,6 +9,9 @@
 //   (seed, step, row, i) so replays and ranks are reproducible; T <= 0 rows
 //   fall back to argmax.  Top-k / top-p restriction is applied before this by
 //   masking logits to -inf.
+// * banned tokens: up to kMaxBans global token ids per row (-1 = none) never
+//   win (the decode mask of a request, e.g. a parser's tool-call opener under
+//   tool_choice="none"); a graph-captured step reads them from its input buffer.
 #include "common.cuh"
 #include "launch.h"
 
@@ -16,6 +19,7 @@ namespace b200 {
 namespace {
 
 constexpr int kThreads = 1024;
+constexpr int kMaxBans = 4;
 
 __device__ __forceinline__ void better(float& v, int& i, float ov, int oi) {
   if (ov > v || (ov == v && oi < i)) {
@@ -37,11 +41,15 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) sample_kernel(const T* __restrict__ logits, int64_t ld, int V,
                                                           const float* __restrict__ temperature, uint64_t seed,
                                                           const int64_t* __restrict__ step, int vocab_offset,
+                                                          const int* __restrict__ bans, int nbans,
                                                           float* __restrict__ out_val, int* __restrict__ out_idx) {
   pdl_prologue();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int row = blockIdx.x;
+  int ban[kMaxBans];
+#pragma unroll
+  for (int b = 0; b < kMaxBans; ++b) ban[b] = (bans != nullptr && b < nbans) ? bans[(int64_t)row * nbans + b] - vocab_offset : -1;
   const T* x = logits + (int64_t)row * ld;
   const float temp = temperature ? temperature[row] : 0.f;
   const bool greedy = !(temp > 0.f);
@@ -52,6 +60,10 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const T* __restrict__ 
   int bi = 0x7fffffff;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     float v = to_float<T>(x[i]);
+    bool banned = false;
+#pragma unroll
+    for (int b = 0; b < kMaxBans; ++b) banned |= (ban[b] == i);
+    if (banned) continue;
     if (!greedy) {
       const float u = uniform01(base + (uint64_t)(vocab_offset + i) * 0xC2B2AE3D27D4EB4Full);
       v = v * inv_t - __logf(-__logf(u));
@@ -101,16 +113,17 @@ __global__ void combine_kernel(const float* __restrict__ vals, const int* __rest
 }  // namespace
 
 cudaError_t sample_rows(const void* logits, int dtype /*0 bf16, 1 fp32*/, int64_t ld, int rows, int V,
-                        const float* temperature, uint64_t seed, const int64_t* step, int vocab_offset, float* out_val,
-                        int* out_idx, cudaStream_t stream) {
+                        const float* temperature, uint64_t seed, const int64_t* step, int vocab_offset,
+                        const int* bans, int nbans, float* out_val, int* out_idx, cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
+  if (nbans < 0 || nbans > kMaxBans) return cudaErrorInvalidValue;
   if (dtype == 0)
     launch_pdl(sample_kernel<__nv_bfloat16>, dim3(rows), dim3(kThreads), 0, stream, reinterpret_cast<const __nv_bfloat16*>(logits), ld, V,
-                                                                temperature, seed, step, vocab_offset, out_val,
-                                                                out_idx);
+                                                                temperature, seed, step, vocab_offset, bans, nbans,
+                                                                out_val, out_idx);
   else
     launch_pdl(sample_kernel<float>, dim3(rows), dim3(kThreads), 0, stream, reinterpret_cast<const float*>(logits), ld, V, temperature,
-                                                        seed, step, vocab_offset, out_val, out_idx);
+                                                        seed, step, vocab_offset, bans, nbans, out_val, out_idx);
   return cudaGetLastError();
 }
 

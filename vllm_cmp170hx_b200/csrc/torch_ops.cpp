@@ -505,19 +505,27 @@ namespace b200 {
 
 void sample_rows_op(const at::Tensor& logits, const c10::optional<at::Tensor>& temperature, int64_t seed,
                     const c10::optional<at::Tensor>& step, int64_t vocab_offset, at::Tensor& out_val,
-                    at::Tensor& out_idx) {
+                    at::Tensor& out_idx, const c10::optional<at::Tensor>& bans) {
   B200_CHECK_CUDA(logits);
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: logits [rows, V]");
   TORCH_CHECK(logits.scalar_type() == at::kBFloat16 || logits.scalar_type() == at::kFloat, "sample: bf16/fp32");
   TORCH_CHECK(out_val.scalar_type() == at::kFloat && out_idx.scalar_type() == at::kInt, "sample: outputs");
   if (temperature.has_value()) TORCH_CHECK(temperature->scalar_type() == at::kFloat, "sample: temperature fp32");
   if (step.has_value()) TORCH_CHECK(step->scalar_type() == at::kLong, "sample: step int64");
+  if (temperature.has_value()) TORCH_CHECK(temperature->numel() >= logits.size(0), "sample: temperature rows");
+  if (bans.has_value())
+    TORCH_CHECK(bans->scalar_type() == at::kInt && bans->dim() == 2 && bans->is_contiguous() &&
+                    bans->size(0) >= logits.size(0) && bans->size(1) <= 4,
+                "sample: bans [rows, <= 4] int32 contiguous");
+  TORCH_CHECK(out_val.numel() >= logits.size(0) && out_idx.numel() >= logits.size(0), "sample: output rows");
   c10::cuda::CUDAGuard g(logits.device());
   B200_LAUNCH(sample_rows(logits.data_ptr(), logits.scalar_type() == at::kFloat ? 1 : 0, logits.stride(0),
                           logits.size(0), logits.size(1),
                           temperature.has_value() ? temperature->data_ptr<float>() : nullptr, (uint64_t)seed,
                           step.has_value() ? step->data_ptr<int64_t>() : nullptr, (int)vocab_offset,
-                          out_val.data_ptr<float>(), out_idx.data_ptr<int>(), cur_stream()));
+                          bans.has_value() ? bans->data_ptr<int>() : nullptr,
+                          bans.has_value() ? (int)bans->size(1) : 0, out_val.data_ptr<float>(),
+                          out_idx.data_ptr<int>(), cur_stream()));
 }
 
 void sample_combine_op(const at::Tensor& vals, const at::Tensor& idx, at::Tensor& out) {

@@ -16,6 +16,8 @@ class SamplingParams:
     stop_token_ids: list[int] = field(default_factory=list)
     ignore_eos: bool = False
     seed: int | None = None
+    # tokens that are never sampled (at most 4; e.g. a parser's tool-call opener under tool_choice="none")
+    bad_token_ids: list[int] = field(default_factory=list)
 
 
 class Status(enum.Enum):

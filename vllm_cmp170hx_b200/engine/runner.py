@@ -202,7 +202,18 @@ class ModelRunner:
         temps[:S] = np.fromiter((s.req.params.temperature for s in reqs), dtype=np.float32, count=S)
         sample_rows = np.fromiter((i for i, s in enumerate(reqs) if s.sample), dtype=np.int64)
         return dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
-                    temps=temps, sample_rows=sample_rows, max_ctx=int(a.max()) + 1 if S else 1, T=Sp, S=Sp)
+                    temps=temps, bans=self._bans_rows(reqs, Sp), sample_rows=sample_rows,
+                    max_ctx=int(a.max()) + 1 if S else 1, T=Sp, S=Sp)
+
+    @staticmethod
+    def _bans_rows(reqs, rows: int) -> np.ndarray:
+        """[rows, MAX_BANS] banned token ids of each sequence's sampled row (-1 = none)."""
+        bans = np.full((rows, sampling_ops.MAX_BANS), -1, dtype=np.int32)
+        for i, s in enumerate(reqs):
+            b = s.req.params.bad_token_ids
+            if b:
+                bans[i, :len(b)] = b[:sampling_ops.MAX_BANS]
+        return bans
 
     def _host_inputs(self, out: SchedulerOutput, pad_to: int | None = None):
         reqs = out.reqs
@@ -252,7 +263,8 @@ class ModelRunner:
         for i in range(S, Sp):  # decode padding rows
             cu[i + 1] = cu[i] + 1
         h = dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
-                 temps=temps, sample_rows=np.asarray(sample_rows, dtype=np.int64), max_ctx=max_ctx, T=Tp, S=Sp)
+                 temps=temps, bans=self._bans_rows(reqs, Sp), sample_rows=np.asarray(sample_rows, dtype=np.int64),
+                 max_ctx=max_ctx, T=Tp, S=Sp)
         if self._check_indices:
             from ..utils.state_check import check_step
 
@@ -287,15 +299,15 @@ class ModelRunner:
         return dev, ctx, nbytes
 
     # ------------------------------------------------------------------ forward + sample
-    def _forward_sample(self, ids, ctx, sample_rows, temps, seed):
+    def _forward_sample(self, ids, ctx, sample_rows, temps, seed, bans=None):
         if self.timer is not None:
             self.timer.open_row()
-        return self._sample_hidden(self.model(ids, ctx), sample_rows, temps, seed)
+        return self._sample_hidden(self.model(ids, ctx), sample_rows, temps, seed, bans)
 
-    def _sample_hidden(self, hidden, sample_rows, temps, seed):
+    def _sample_hidden(self, hidden, sample_rows, temps, seed, bans=None):
         hs = hidden if sample_rows is None else hidden.index_select(0, sample_rows)
         logits = self.model.compute_logits(hs)
-        val, idx = sampling_ops.sample_local(logits, temps, seed, self.step_counter, self.model.vocab_offset)
+        val, idx = sampling_ops.sample_local(logits, temps, seed, self.step_counter, self.model.vocab_offset, bans)
         if self.st.tp_size > 1:
             vals = comm.tp_all_gather(val[None], dim=0)
             idxs = comm.tp_all_gather(idx[None], dim=0)
@@ -330,8 +342,9 @@ class ModelRunner:
             dev, ctx, nbytes = self._context(h)
             rows = self._to_dev(h["sample_rows"])
             temps_rows = self._sample_temps(out, h)
+            bans = self._sample_bans(out)
             ev = self._ev_start()
-            tokens = self._forward_sample(dev["ids"], ctx, rows, temps_rows, self.cfg.seed)
+            tokens = self._forward_sample(dev["ids"], ctx, rows, temps_rows, self.cfg.seed, bans)
             self._ev_end(ev)
         self.step_counter += 1
         if self.device.type == "cuda":
@@ -416,7 +429,8 @@ class ModelRunner:
                 self._pp_hidden.append((mb, res, list(m.aux_hidden)))
             else:
                 rows = self._to_dev(h["sample_rows"])
-                toks.append(self._sample_hidden(res, rows, self._sample_temps(mb, h), self.cfg.seed))
+                toks.append(self._sample_hidden(res, rows, self._sample_temps(mb, h), self.cfg.seed,
+                                                self._sample_bans(mb)))
         for w, _ in sends:
             w.wait()
         self.step_counter += 1
@@ -554,6 +568,14 @@ class ModelRunner:
             ev[1].record()
             self._events = ev
 
+    def _sample_bans(self, out):
+        """[sampled rows, MAX_BANS] banned token ids on the device, or None when no request bans any."""
+        if not any(s.req.params.bad_token_ids for s in out.reqs if s.sample):
+            return None
+        rows = [s for s in out.reqs if s.sample]
+        assert all(s.num_draft == 0 for s in rows), "banned tokens with speculative decoding"
+        return self._to_dev(self._bans_rows(rows, len(rows)))
+
     def _sample_temps(self, out, h):
         temps = []
         for s in out.reqs:
@@ -597,7 +619,8 @@ class ModelRunner:
         specs = [("ids", (B,), torch.int64), ("pos", (B,), torch.int32), ("slots", (B,), torch.int64),
                  ("tseq", (B,), torch.int32), ("ctx", (B,), torch.int32), ("cu", (B + 1,), torch.int32),
                  ("kslot", (B,), torch.int32), ("hinit", (B,), torch.int32),
-                 ("bt", (B, self.max_blocks_per_seq), torch.int32), ("temps", (B,), torch.float32)]
+                 ("bt", (B, self.max_blocks_per_seq), torch.int32), ("temps", (B,), torch.float32),
+                 ("bans", (B, sampling_ops.MAX_BANS), torch.int32)]
         offs, off = {}, 0
         for k, shape, dt in specs:
             offs[k] = off
@@ -613,6 +636,7 @@ class ModelRunner:
         bufs["tseq"].copy_(torch.arange(B, dtype=torch.int32))
         bufs["ctx"].fill_(1)
         bufs["cu"].copy_(torch.arange(B + 1, dtype=torch.int32))
+        bufs["bans"].fill_(-1)
         bufs["scores"] = torch.empty(B, mml, dtype=torch.float32, device=dev)
         ctx = StepContext(positions=bufs["pos"], num_tokens=B, slot_mapping=bufs["slots"], token_seq=bufs["tseq"],
                           ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
@@ -622,14 +646,14 @@ class ModelRunner:
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
             for _ in range(2):
-                self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed)
+                self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed, bufs["bans"])
         torch.cuda.current_stream(dev).wait_stream(s)
         torch.cuda.synchronize(dev)
         g = torch.cuda.CUDAGraph()
         if self.graph_pool is None:
             self.graph_pool = torch.cuda.graph_pool_handle()
         with torch.cuda.graph(g, pool=self.graph_pool):
-            ids_out = self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed)
+            ids_out = self._forward_sample(bufs["ids"], ctx, None, bufs["temps"], self.cfg.seed, bufs["bans"])
         torch.cuda.synchronize(dev)
         self.graphs[B] = (g, bufs, ids_out)
         self._packed[B] = (host, devbuf, hviews)

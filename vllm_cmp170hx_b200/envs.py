@@ -68,6 +68,9 @@ _declare("VLLM_B200_ADAPTIVE_DEPTH", str, "", "per-request verify depth policy f
 _declare("VLLM_B200_OVERRIDE", str, "", "override sidecar manifest restoring plain tensors at source precision")
 _declare("VLLM_B200_NO_PDL", bool, False, "launch kernels without programmatic dependent launch (profiling: each kernel charged its own time)")
 _declare("VLLM_B200_OVERRIDE_SHA256", str, "", "pinned sha256 of the override manifest")
+# --- serving --------------------------------------------------------------------------------------
+_declare("VLLM_B200_TOOL_CHOICE_NONE_MASK", _bool, False, "with tool_choice='none', parsers that have one (glm45, "
+         "glm47, ling3) ban their tool-call opener token at decode time (read by api/parsers.py)")
 # --- storage-backed embeddings ------------------------------------------------------------------
 _declare("VLLM_B200_PLE_READ_RETRIES", int, 3, "retries of a failed PLE/Engram row read (1 ms doubling backoff)")
 _declare("VLLM_B200_ROW_CACHE_GIB", float, 0.0, "host LRU cache of table rows read from storage (0 = the table's "
@@ -101,6 +104,7 @@ ALIASES = {
     "VLLM_FAIR_PREFILL_SHORT_BYPASS": "VLLM_B200_FAIR_PREFILL_SHORT_BYPASS",
     "VLLM_DEV_AB_SWITCH": "VLLM_B200_DEV_AB_SWITCH",
     "VLLM_HOT_SWAP": "VLLM_B200_HOT_SWAP",
+    "VLLM_TOOL_CHOICE_NONE_MASK": "VLLM_B200_TOOL_CHOICE_NONE_MASK",
     "VLLM_EXL3_PLE_READ_RETRIES": "VLLM_B200_PLE_READ_RETRIES",
 }
 
