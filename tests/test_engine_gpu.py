@@ -64,8 +64,9 @@ def test_banned_tokens_in_kernel_and_graph():
     bans[:, 0] = top.int()
     bans[1, 1] = logits[1].float().topk(2).indices[1].int()
     for off in (0, 500):  # the vocab shard's offset
-        val, idx = sampling_ops.sample_local(logits, None, 0, None, off, bans + off * (bans >= 0))
-        v_ref, i_ref = sampling_ops.sample_local(logits.cpu(), None, 0, None, off, (bans + off * (bans >= 0)).cpu())
+        shard_bans = torch.where(bans >= 0, bans + off, bans).int().contiguous()
+        val, idx = sampling_ops.sample_local(logits, None, 0, None, off, shard_bans)
+        v_ref, i_ref = sampling_ops.sample_local(logits.cpu(), None, 0, None, off, shard_bans.cpu())
         assert idx.cpu().tolist() == i_ref.tolist()
         assert all(int(i) - off != int(t) for i, t in zip(idx.cpu(), top.cpu()))
     pstate.set_state(pstate.ParallelState())

@@ -134,3 +134,27 @@ def test_sparse_attention(nh, count, splits, qscale):
         o_r, lse_r = ref.sparse_attention(q[t].cpu(), rows, scale)
         assert _rel(out[t].cpu(), o_r) < 2e-2, (t, _rel(out[t].cpu(), o_r))
         assert (lse[t].cpu() - lse_r).abs().max() < 2e-2
+
+
+@pytest.mark.parametrize("H", [1, 2, 3])
+@pytest.mark.parametrize("n", [8, 64, 256])
+def test_batched_head_gemms(H, n):
+    """The MLA absorb and up-projection GEMMs on per-head views (`ops.bmm`: [H, n, K] slices of [n, H, D]
+    tensors, outputs written into slices of wider rows) against fp32 per-head matmuls; one head (a
+    rank's share of a small model) takes the 2-D path."""
+    from vllm_cmp170hx_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(H * 1000 + n)
+    q = torch.randn(n, H, 192, device="cuda", generator=g).bfloat16()
+    w_uk_t = (torch.randn(H + 1, 512, 128, device="cuda", generator=g) * 0.1).bfloat16()
+    qf = torch.zeros(n, H, 576, dtype=torch.bfloat16, device="cuda")
+    ops.bmm(q[:, :, :128].transpose(0, 1), w_uk_t[1:1 + H], out=qf[:, :, :512].transpose(0, 1))
+    ref = torch.einsum("nhk,hjk->nhj", q[:, :, :128].float(), w_uk_t[1:1 + H].float())
+    assert ((qf[:, :, :512].float() - ref).norm() / ref.norm()).item() < 1e-2
+    assert qf[:, :, 512:].abs().max().item() == 0  # the rope columns of the rows are untouched
+    o_lat = torch.randn(n, H, 512, device="cuda", generator=g).bfloat16()
+    w_uv = (torch.randn(H, 128, 512, device="cuda", generator=g) * 0.05).bfloat16()
+    o = torch.empty(n, H * 128, dtype=torch.bfloat16, device="cuda")
+    ops.bmm(o_lat.transpose(0, 1), w_uv, out=o.view(n, H, 128).transpose(0, 1))
+    ref2 = torch.einsum("nhk,hjk->nhj", o_lat.float(), w_uv.float()).reshape(n, H * 128)
+    assert ((o.float() - ref2).norm() / ref2.norm()).item() < 1e-2

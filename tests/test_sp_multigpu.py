@@ -136,7 +136,8 @@ def _cfg(tp):
     m.moe.shared_intermediate = 256
     return EngineConfig(model=m, parallel=ParallelConfig(tensor_parallel_size=tp, expert_parallel=tp > 1),
                         scheduler=SchedulerConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=256),
-                        cache=CacheConfig(num_blocks=64), device="cuda", cuda_graph_batch_sizes=[2, 4, 8])
+                        cache=CacheConfig(num_blocks=64), device="cuda", cuda_graph_batch_sizes=[2, 4, 8],
+                        enforce_eager=os.environ.get("SP_TEST_EAGER") == "1")
 
 
 def _generate(tp, fused, expect_sp=None):
@@ -218,8 +219,9 @@ def _reference():
     return _REF["ref"]
 
 
-@pytest.mark.parametrize("dispatch,mla_dp", [("symm", "1"), ("symm", "0"), ("nccl", "1"), ("off", "1")])
-def test_sp_engine_tp2_matches_one_gpu(dispatch, mla_dp):
+@pytest.mark.parametrize("dispatch,mla_dp,eager", [("symm", "1", "0"), ("symm", "1", "1"), ("symm", "0", "0"),
+                                                  ("nccl", "1", "0"), ("off", "1", "0")])
+def test_sp_engine_tp2_matches_one_gpu(dispatch, mla_dp, eager):
     """The first three steps' logits (a 256-token prefill chunk, then the rest of the prompts with the
     first decodes, then a decode step) at TP=2 agree with one GPU's to bf16 rounding of the partial
     sums, and greedy decoding gives the same tokens except where two logits are that close: the
@@ -238,7 +240,7 @@ def test_sp_engine_tp2_matches_one_gpu(dispatch, mla_dp):
         pytest.skip("needs 2 or more GPUs")
     ref = _reference()
     assert not isinstance(ref, str), ref
-    env = {"VLLM_B200_EP_DISPATCH": dispatch, "VLLM_B200_MLA_DP": mla_dp}
+    env = {"VLLM_B200_EP_DISPATCH": dispatch, "VLLM_B200_MLA_DP": mla_dp, "SP_TEST_EAGER": eager}
     res = _run_env(env)
     assert not isinstance(res[0], str), res[0]
     toks, logits = res[0]

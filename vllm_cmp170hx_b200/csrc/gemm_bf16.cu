@@ -846,6 +846,7 @@ template <int BN>
 cudaError_t launch_batched(const void* A, int64_t lda, int64_t a_bs, int rows_a, const void* B, int64_t ldb,
                            int64_t b_bs, int rows_b, int K, const Params& p, cudaStream_t stream, int grid) {
   using C_ = Cfg<BN>;
+  if (p.batch < 2) return cudaErrorInvalidValue;  // the kernel loads through the 3-D maps only for batch > 1
   CUtensorMap ta = make_tma_3d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_a, K, p.batch, lda, a_bs, BM, BK,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tb = make_tma_3d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_b, K, p.batch, ldb, b_bs, BN, BK,
@@ -1075,6 +1076,17 @@ cudaError_t gemm_bf16_batched(const GemmBatchedArgs& a, cudaStream_t stream) {
   p.batch = a.batch;
   p.c_bstride = a.c_bstride;
   const int grid = std::min(p.m_tiles * p.n_tiles * a.batch, device_sm_count());
+  if (a.batch == 1) {
+    // one matrix: the plain kernel path with 2-D maps (the kernel issues 3-D loads only for batch > 1,
+    // and a 2-D load through a 3-D map is an illegal instruction)
+    switch (bn) {
+      case 16: return launch<16>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid);
+      case 32: return launch<32>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid);
+      case 64: return launch<64>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid);
+      case 128: return launch<128>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid);
+      default: return launch<256>(A, lda, Ma, B, ldb, Nb, a.K, p, stream, grid);
+    }
+  }
   switch (bn) {
     case 16: return launch_batched<16>(A, lda, a_bs, Ma, B, ldb, b_bs, Nb, a.K, p, stream, grid);
     case 32: return launch_batched<32>(A, lda, a_bs, Ma, B, ldb, b_bs, Nb, a.K, p, stream, grid);
