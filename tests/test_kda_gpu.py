@@ -131,3 +131,76 @@ def test_verify_records_and_recover_match_prefix():
                             -5.0, norm_w, st_ref)
         assert torch.equal(st, st_ref), n
         assert torch.equal(cv, cv_ref), n
+
+
+def _layer_inputs(lens, H, seed, state_scale=0.05):
+    g = torch.Generator().manual_seed(seed)
+    HD = H * 128
+    T = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32)
+    qkv = torch.randn(T, 3 * HD, generator=g).to(torch.bfloat16)
+    g_raw = (torch.randn(T, HD, generator=g) * 2).to(torch.bfloat16)
+    beta_raw = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    g2 = torch.randn(T, HD, generator=g).to(torch.bfloat16)
+    conv_w = (torch.randn(3 * HD, 4, generator=g) * 0.5).to(torch.bfloat16)
+    a_log = torch.randn(H, generator=g) * 0.5
+    g_bias = torch.randn(HD, generator=g) * 0.1
+    norm_w = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    S = len(lens)
+    state = torch.randn(S + 1, H, 128, 128, generator=g) * state_scale
+    conv_state = torch.randn(S + 1, 3 * HD, 3, generator=g).to(torch.bfloat16)
+    idx = torch.randperm(S + 1, generator=g)[:S].to(torch.int32)
+    has_init = (torch.arange(S) % 2).to(torch.int32)
+    return dict(cu=cu, qkv=qkv, g_raw=g_raw, beta_raw=beta_raw, g2=g2, conv_w=conv_w, a_log=a_log, g_bias=g_bias,
+                norm_w=norm_w, state=state, conv_state=conv_state, idx=idx, has_init=has_init)
+
+
+def _run_gpu(x, mode, monkeypatch):
+    from vllm_cmp170hx_b200 import envs
+    from vllm_cmp170hx_b200.ops import kda as kda_ops
+
+    monkeypatch.setenv("VLLM_B200_KDA_PREFILL", mode)
+    envs._cache.clear()
+    st, cs = x["state"].cuda(), x["conv_state"].cuda()
+    c = {k: v.cuda() for k, v in x.items() if k not in ("state", "conv_state")}
+    out = kda_ops.kda_forward(c["qkv"], c["g_raw"], c["beta_raw"], c["g2"], c["cu"], c["idx"], c["has_init"], cs,
+                              c["conv_w"], None, c["a_log"], c["g_bias"], -5.0, c["norm_w"], st)
+    torch.cuda.synchronize()
+    _ext.check_status(torch.device("cuda", 0))
+    envs._cache.clear()
+    return out.cpu().float(), st.cpu(), cs.cpu()
+
+
+@pytest.mark.parametrize("lens", [[64], [100, 3, 200, 1, 130], [64, 65, 127, 128, 129], [300]])
+def test_chunked_prefill_matches_recurrence(lens, monkeypatch):
+    """The chunked tensor-core prefill (sequences of >= 64 tokens; shorter ones stay on the recurrence in
+    the same call) against the token recurrence: outputs, final states and conv windows, with fresh and
+    continuing sequences, partial last chunks and strong decays (gate pre-activations x2)."""
+    H = 4
+    x = _layer_inputs(lens, H, seed=len(lens) * 7 + sum(lens))
+    o_c, st_c, cs_c = _run_gpu(x, "chunked", monkeypatch)
+    o_r, st_r, cs_r = _run_gpu(x, "recurrent", monkeypatch)
+    cu = x["cu"].tolist()
+    for s in range(len(lens)):
+        a, b = cu[s], cu[s + 1]
+        rel = ((o_c[a:b] - o_r[a:b]).norm() / o_r[a:b].norm()).item()
+        assert rel < 2e-2, (s, lens[s], rel)
+        slot = int(x["idx"][s])
+        ds = (st_c[slot] - st_r[slot]).norm() / st_r[slot].norm()
+        assert ds < 1e-2, (s, lens[s], ds.item())
+        assert torch.equal(cs_c[slot], cs_r[slot]), s
+
+
+def test_chunked_prefill_matches_layer_oracle(monkeypatch):
+    """One long continuing sequence and one fresh one against the fp32 layer oracle."""
+    H = 2
+    x = _layer_inputs([150, 70], H, seed=11)
+    st_r, cs_r = x["state"].clone(), x["conv_state"].clone()
+    ref = kda.kda_layer(x["qkv"], x["g_raw"], x["beta_raw"], x["g2"], x["cu"], st_r, cs_r, x["idx"], x["has_init"],
+                        x["conv_w"], None, x["a_log"], x["g_bias"], -5.0, x["norm_w"])
+    o_c, st_c, cs_c = _run_gpu(x, "chunked", monkeypatch)
+    rel = ((o_c - ref).norm() / ref.norm()).item()
+    assert rel < 2e-2, rel
+    for s in range(2):
+        slot = int(x["idx"][s])
+        assert ((st_c[slot] - st_r[slot]).norm() / st_r[slot].norm()).item() < 1e-2

@@ -14,7 +14,7 @@ import functools
 import torch
 
 BUILD_HINT = "python setup.py build_ext --inplace   (from the repository root)"
-EXPECTED_BUILD_INFO = 100 * 1000 + 2
+EXPECTED_BUILD_INFO = 100 * 1000 + 3
 
 
 class ExtensionMissing(RuntimeError):

@@ -10,7 +10,7 @@
 namespace {
 int64_t build_info() {
   // 100 = sm_100a; bump the low digits when an op's ABI changes.
-  return 100 * 1000 + 2;
+  return 100 * 1000 + 3;
 }
 }  // namespace
 

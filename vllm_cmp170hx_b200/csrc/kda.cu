@@ -60,12 +60,16 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
   __shared__ __align__(16) float o_s[D];
   __shared__ float beta_s;
 
+  // sequences of at least skip_long tokens belong to the chunked kernel: no tokens, no state traffic here
+  auto skipped_of = [&](int seq) {
+    return p.skip_long > 0 && p.cu_seqlens[seq + 1] - p.cu_seqlens[seq] >= p.skip_long;
+  };
   auto has_init_of = [&](int seq) { return p.has_init ? (p.has_init[seq] != 0) : true; };
   // issue the state copy of `item` into buffer `b` (an empty transaction when it has no state)
   auto prefetch = [&](int item, int b) {
     const int sq = item / p.H, hh = item % p.H;
     const int sl = p.state_idx ? p.state_idx[sq] : sq;
-    if (has_init_of(sq)) {
+    if (has_init_of(sq) && !skipped_of(sq)) {
       mbar_arrive_expect_tx(&fullb[b], D * D * 4);
       bulk_load(sbuf + b * D * D, p.state + ((int64_t)sl * p.H + hh) * D * D, D * D * 4, &fullb[b]);
     } else {
@@ -91,7 +95,8 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
   };
   auto load_meta = [&](int it) {
     const int sq = it / p.H;
-    return Meta{p.cu_seqlens[sq], p.cu_seqlens[sq + 1], p.state_idx ? p.state_idx[sq] : sq,
+    return Meta{p.cu_seqlens[sq], skipped_of(sq) ? p.cu_seqlens[sq] : p.cu_seqlens[sq + 1],
+                p.state_idx ? p.state_idx[sq] : sq,
                 has_init_of(sq) ? 1 : 0};
   };
   auto load_inputs = [&](int it, const Meta& m) {
@@ -132,9 +137,10 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
   for (int item = blockIdx.x; item < items; item += gridDim.x, ++local) {
   const int seq = item / p.H;
   const int h = item % p.H;
-  const int t0 = p.cu_seqlens[seq], t1 = p.cu_seqlens[seq + 1];
+  const bool skipped = skipped_of(seq);
+  const int t0 = p.cu_seqlens[seq], t1 = skipped ? t0 : p.cu_seqlens[seq + 1];
   const int slot = p.state_idx ? p.state_idx[seq] : seq;
-  const bool has_init = has_init_of(seq);
+  const bool has_init = has_init_of(seq) && !skipped;
   const bool verify = p.verify != nullptr && p.verify[seq] != 0 && p.rec != nullptr;
   const int buf = local & 1;
   const bool has_next = item + (int)gridDim.x < items;
@@ -306,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
   }
   if (t0 == t1 && has_next) in = load_inputs(item + gridDim.x, next_meta);  // (no token ran)
   // ------------------------------------------------------------------ write back
-  if (verify) continue;  // kda_recover applies the accepted prefix later
+  if (verify || skipped) continue;  // kda_recover applies the accepted prefix later; or chunked
 #pragma unroll
   for (int gi = 0; gi < 2; ++gi) {
     const int row = warp * 8 + gi * 4 + rs;

@@ -283,8 +283,25 @@ struct KdaArgs {
   // then applies the accepted prefix
   const int* verify;  // [num_seqs] nullable
   float* rec;
+  int skip_long;  // > 0: sequences of at least this many tokens are left to the chunked kernel
 };
 cudaError_t kda_recurrent(const KdaArgs& a, cudaStream_t stream);
+
+// Chunked prefill (kda_chunk.cu): the sequences of at least `min_len` tokens run in chunks of 64 on the
+// tensor cores (the recurrence skips them when its `skip_long` is the same length).  `scratch` holds the
+// per-token prep outputs (kda_chunk_scratch_bytes); the fields after it are filled by the launcher.
+struct KdaChunkArgs {
+  KdaArgs k;
+  int T;
+  int min_len;
+  void* scratch;
+  size_t scratch_bytes;
+  uint32_t* status;
+  __nv_bfloat16 *qn, *kn, *vv;  // [T, H, 128]
+  float *gl, *beta;             // [T, H, 128] log2 decay, [T, H]
+};
+size_t kda_chunk_scratch_bytes(int T, int H);
+cudaError_t kda_chunked(const KdaChunkArgs& a, cudaStream_t stream);
 
 // Applies the first keep[s] recorded tokens of each verified sequence to its state, and moves its conv
 // window past them (the window is rebuilt from the step's pre-conv inputs).

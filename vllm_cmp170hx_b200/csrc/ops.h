@@ -40,7 +40,8 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                     const at::Tensor& a_log, const c10::optional<at::Tensor>& g_bias, double lower_bound,
                     const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
                     at::Tensor& state, at::Tensor& out, const c10::optional<at::Tensor>& verify,
-                    const c10::optional<at::Tensor>& rec);
+                    const c10::optional<at::Tensor>& rec, int64_t chunk_min_len,
+                    const c10::optional<at::Tensor>& chunk_scratch, const c10::optional<at::Tensor>& status);
 void mhc_post_pre_op(const c10::optional<at::Tensor>& x, const at::Tensor& H, const c10::optional<at::Tensor>& post,
                      const c10::optional<at::Tensor>& comb, const at::Tensor& fn, const at::Tensor& scale,
                      const at::Tensor& base, const at::Tensor& norm_w, const c10::optional<at::Tensor>& pre_mix,
@@ -166,7 +167,8 @@ void register_host_bindings(pybind11::module_& m);
   X("kda_forward(Tensor cu_seqlens, Tensor? state_idx, Tensor? has_init, Tensor qkv, Tensor g_raw, "        \
     "Tensor beta_raw, Tensor? g2, Tensor(a!) conv_state, Tensor? conv_w, Tensor? conv_b, Tensor a_log, "   \
     "Tensor? g_bias, float lower_bound, Tensor? norm_w, float eps, float l2_eps, float q_scale, "            \
-    "bool l2norm, Tensor(b!) state, Tensor(c!) out, Tensor? verify=None, Tensor(d!)? rec=None) -> ()")       \
+    "bool l2norm, Tensor(b!) state, Tensor(c!) out, Tensor? verify=None, Tensor(d!)? rec=None, "            \
+    "int chunk_min_len=0, Tensor(e!)? chunk_scratch=None, Tensor(f!)? status=None) -> ()")                  \
   X("mhc_post_pre(Tensor? x, Tensor H, Tensor? post, Tensor? comb, Tensor fn, Tensor scale, Tensor base, "   \
     "Tensor norm_w, Tensor? pre_mix, float rms_eps, float eps, float post_mult, int iters, float norm_eps, "  \
     "int mode, Tensor(a!) H_out, Tensor(b!) y, Tensor(c!) post_out, Tensor(d!) comb_out, Tensor(e!) pre_out) -> ()") \

@@ -266,7 +266,8 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                     const at::Tensor& a_log, const c10::optional<at::Tensor>& g_bias, double lower_bound,
                     const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
                     at::Tensor& state, at::Tensor& out, const c10::optional<at::Tensor>& verify,
-                    const c10::optional<at::Tensor>& rec) {
+                    const c10::optional<at::Tensor>& rec, int64_t chunk_min_len,
+                    const c10::optional<at::Tensor>& chunk_scratch, const c10::optional<at::Tensor>& status) {
   B200_CHECK_CUDA(qkv);
   B200_CHECK_DTYPE(qkv, at::kBFloat16);
   B200_CHECK_DTYPE(state, at::kFloat);
@@ -317,6 +318,30 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                 "kda verify: int32 flags [num_seqs] and fp32 records [T, H, 3, 128]");
     a.verify = verify->data_ptr<int>();
     a.rec = rec->data_ptr<float>();
+  }
+  if (chunk_min_len > 0) {
+    // sequences of at least chunk_min_len tokens in chunks of 64 on the tensor cores, the rest (and
+    // everything under speculative verify) through the recurrence
+    TORCH_CHECK(!verify.has_value(), "kda: chunked prefill does not record verify updates");
+    TORCH_CHECK(chunk_scratch.has_value() && chunk_scratch->is_cuda() && chunk_scratch->is_contiguous() &&
+                    (size_t)chunk_scratch->nbytes() >= kda_chunk_scratch_bytes((int)qkv.size(0), H),
+                "kda: chunk scratch of kda_chunk_scratch_bytes(T, H) bytes");
+    TORCH_CHECK(out.stride(0) >= H * 128 && out.stride(0) % 8 == 0 &&
+                    reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+                "kda: chunked output rows must be 16-byte aligned");
+    TORCH_CHECK(status.has_value() && status->scalar_type() == at::kInt, "kda: status word");
+    a.skip_long = (int)chunk_min_len;
+    B200_LAUNCH(kda_recurrent(a, cur_stream()));
+    KdaChunkArgs c{};
+    c.k = a;
+    c.k.skip_long = 0;
+    c.T = (int)qkv.size(0);
+    c.min_len = (int)chunk_min_len;
+    c.scratch = chunk_scratch->data_ptr();
+    c.scratch_bytes = chunk_scratch->nbytes();
+    c.status = reinterpret_cast<uint32_t*>(status->data_ptr<int>());
+    B200_LAUNCH(kda_chunked(c, cur_stream()));
+    return;
   }
   B200_LAUNCH(kda_recurrent(a, cur_stream()));
 }

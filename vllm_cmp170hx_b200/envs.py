@@ -58,6 +58,8 @@ _declare("VLLM_B200_GEMM_SPLITK", int, 0, "force the split-K factor of the bf16 
 _declare("VLLM_B200_EXL3_TILE_ROWS", int, 0, "rows per EXL3 expert work item, 16 / 32 / 64 / 128 (0 = batch-chosen)")
 _declare("VLLM_B200_EXL3_DECODERS", int, 0, "decoder warps of the EXL3 GEMM, 8 or 16 (0 = the build's default; read "
          "by csrc/exl3.cu)")
+_declare("VLLM_B200_KDA_PREFILL", str, "chunked", "KDA prefill: 'chunked' (sequences of >= 64 tokens in chunks of 64 "
+         "on the tensor cores, read by ops/kda.py) or 'recurrent' (token by token)")
 _declare("VLLM_B200_SPARSE_MLA_SPLITS", int, 0, "position splits of the sparse-MLA attention (0 = auto)")
 _declare("VLLM_B200_MLA_DP", _bool, True, "with expert parallelism, sparse-MLA layers hold all heads and attend "
          "data-parallel (each rank its own tokens) in the sequence-parallel layout")

@@ -45,11 +45,42 @@ def kda_forward(qkv, g_raw, beta_raw, g2, cu_seqlens, state_idx, has_init, conv_
         if records.rec is None or records.rec.numel() < T * H * 3 * 128:
             records.rec = torch.empty(max(T, 1), H, 3, 128, dtype=torch.float32, device=qkv.device)
         rec = records.rec
+    min_len, scratch = 0, None
+    S = cu_seqlens.numel() - 1
+    # a sequence can reach CHUNK_MIN_LEN tokens only if T - (S - 1) does (decode steps never launch it)
+    if verify is None and T - (S - 1) >= CHUNK_MIN_LEN and lower_bound >= -5.8 and _chunked_enabled():
+        # sequences of at least CHUNK_MIN_LEN tokens run in chunks of 64 on the tensor cores
+        min_len = CHUNK_MIN_LEN
+        scratch = _chunk_scratch(T, H, qkv.device)
     _ext.ops().kda_forward(cu_seqlens, state_idx, has_init, qkv, g_raw, beta_raw, g2, conv_state, conv_w, conv_b,
-                           a_log, g_bias, lower_bound, norm_w, eps, l2_eps, 128 ** -0.5, True, state, out, verify, rec)
+                           a_log, g_bias, lower_bound, norm_w, eps, l2_eps, 128 ** -0.5, True, state, out, verify, rec,
+                           min_len, scratch, _ext.status_word(qkv.device) if min_len else None)
     if verify is not None:
         records.inputs = (qkv, cu_seqlens, state_idx)
     return out
+
+
+CHUNK_MIN_LEN = 64
+
+
+def _chunked_enabled() -> bool:
+    from .. import envs
+
+    mode = envs.get("VLLM_B200_KDA_PREFILL")
+    if mode not in ("chunked", "recurrent"):
+        raise ValueError(f"VLLM_B200_KDA_PREFILL={mode!r}: 'chunked' or 'recurrent'")
+    return mode == "chunked"
+
+
+def chunk_scratch_bytes(T: int, H: int) -> int:
+    """Bytes of the chunked prefill's per-token inputs (q, k, v bf16 and the log2 decay fp32 per
+    channel, beta per head), as the kernel lays them out."""
+    n = T * H * 128
+    return n * 10 + T * H * 4 + 1280
+
+
+def _chunk_scratch(T: int, H: int, dev) -> torch.Tensor:
+    return torch.empty(chunk_scratch_bytes(T, H), dtype=torch.uint8, device=dev)
 
 
 def kda_recover(records: KdaRecords, keep: torch.Tensor, state: torch.Tensor, conv_state: torch.Tensor) -> None:
