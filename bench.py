@@ -42,6 +42,7 @@ MODEL_DESC = {
        "expert intermediate 1024, EXL3 4-bit experts, vocab 163840",
     4: "DeepSeek-style sparse-MLA MoE, 43 layers (3 dense FFN 12288), hidden 4096, 128 heads, 256 experts top-8 + 1 "
        "shared, expert intermediate 1536, Marlin int4 g128 experts, fp8 128x128 block-scaled attention, vocab 129280",
+    5: "config 4's model with a 1-layer MTP head drafting 3 tokens, rejection sampling at temperature 0.7",
 }
 
 
@@ -142,10 +143,22 @@ def main():
     ap.add_argument("--emulate-tp", type=int, default=0,
                     help="1 GPU standing in for rank 0 of a TP group of this size (collectives return local data): "
                          "prints the per-rank step time of the compute kernels only, never a bench line")
-    ap.add_argument("--config", type=int, default=3, choices=[3, 4],
+    ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5],
                     help="BASELINE config: 3 = hybrid KDA/MLA EXL3 MoE at TP=N (headline); "
-                         "4 = DeepSeek-style Marlin MoE, experts EP=N, attention TP=N")
+                         "4 = DeepSeek-style Marlin MoE, experts EP=N, attention TP=N; "
+                         "5 = config 4's model at PP2 x TP(N/2) with MTP speculative decoding (3 drafts, "
+                         "temperature 0.7), 512 requests with context lengths uniform in [512, 8192], output 1024 "
+                         "(synthetic context: decoding starts at each request's context length)")
     args = ap.parse_args()
+    if args.config == 5:
+        # the BASELINE workload of config 5 unless given explicitly
+        if "--batch" not in sys.argv:
+            args.batch = 512
+        if "--output" not in sys.argv:
+            args.output = 1024
+        if "--prompt" not in sys.argv:
+            args.prompt = 8192  # the longest context; each request draws its own in [512, 8192]
+        args.synthetic_context = True
 
     if args.impl == "reference":
         ref = os.path.join(ROOT, "baseline", "_ref")
@@ -186,18 +199,26 @@ def main():
         args.gpus = args.emulate_tp
         args.nccl_baseline = True  # no symmetric-memory kernels without peers
     else:
-        st = pstate.init(tp_size=args.gpus, pp_size=1, timeout_s=600)
+        pp = 2 if (args.config == 5 and args.gpus >= 2) else 1
+        st = pstate.init(tp_size=args.gpus // pp, pp_size=pp, timeout_s=600)
     # routed experts: whole experts per rank (EP) unless asked otherwise; attention stays tensor parallel
-    args.ep = args.config == 4 or args.ep or (args.gpus > 1 and not args.moe_tp)
+    args.ep = args.config in (4, 5) or args.ep or (args.gpus > 1 and not args.moe_tp)
     dev = st.device
     model_cfg = config3() if args.config == 3 else config4()
     total_len = args.prompt + args.output + 64
+    g_len = torch.Generator().manual_seed(args.seed + 1)
+    ctx_lens = ([int(x) for x in torch.randint(512, args.prompt + 1, (args.batch,), generator=g_len)]
+                if args.config == 5 else [args.prompt] * args.batch)
+    spec_k = 3 if args.config == 5 else 0
+    blocks = sum((L + args.output + 64 + 63) // 64 for L in ctx_lens) + 1
     cfg = EngineConfig(model=model_cfg,
-                       parallel=ParallelConfig(tensor_parallel_size=args.gpus, fused_comm=not args.nccl_baseline,
+                       parallel=ParallelConfig(tensor_parallel_size=st.tp_size, pipeline_parallel_size=st.pp_size,
+                                               fused_comm=not args.nccl_baseline,
                                                expert_parallel=args.ep, sequence_parallel=not args.no_sp),
                        scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
-                                                 max_model_len=total_len, max_num_partial_prefills=args.batch),
-                       cache=CacheConfig(num_blocks=args.batch * ((total_len + 63) // 64) + 1),
+                                                 max_model_len=total_len, max_num_partial_prefills=args.batch,
+                                                 num_speculative_tokens=spec_k, spec_method="mtp"),
+                       cache=CacheConfig(num_blocks=blocks),
                        seed=args.seed, device="cuda", enforce_eager=args.eager,
                        cuda_graph_batch_sizes=[args.batch])
     t0 = time.time()
@@ -221,10 +242,12 @@ def main():
     V = model_cfg.vocab_size
     if args.synthetic_context:
         engine.runner.fill_caches_random(args.seed)
+    temperature = 0.7 if args.config == 5 else 0.0
     for i in range(args.batch):
-        prompt = torch.randint(0, V, (args.prompt,), generator=g).tolist()
-        engine.add_request(prompt, SamplingParams(max_tokens=args.output, ignore_eos=True), f"bench-{i}",
-                           synthetic_prefix=args.prompt - 1 if args.synthetic_context else 0)
+        prompt = torch.randint(0, V, (ctx_lens[i],), generator=g).tolist()
+        engine.add_request(prompt, SamplingParams(max_tokens=args.output, ignore_eos=True, temperature=temperature,
+                                                  seed=args.seed + i), f"bench-{i}",
+                           synthetic_prefix=ctx_lens[i] - 1 if args.synthetic_context else 0)
     # prefill (untimed): until every request has its first token
     t1 = time.time()
     while any(r.num_computed_tokens < r.num_prompt_tokens for r in engine.scheduler.running) or engine.scheduler.waiting:
@@ -285,8 +308,12 @@ def main():
                         else "; prompts prefilled through the engine")),
             "config": {"model": MODEL_DESC[args.config],
                        "global_batch": args.batch, "seq_len": args.prompt, "output_len": args.output,
-                       "parallelism": (f"ep{args.gpus}+attn-tp{args.gpus}" if args.ep and args.gpus > 1
+                       "parallelism": (f"pp{st.pp_size}+tp{st.tp_size}" + (f"+ep{st.tp_size}" if args.ep else "")
+                                       if st.pp_size > 1 else
+                                       f"ep{args.gpus}+attn-tp{args.gpus}" if args.ep and args.gpus > 1
                                        else f"tp{args.gpus}"),
+                       **({"speculative": "MTP, 3 drafts, temperature 0.7",
+                           "context_lens": "uniform [512, %d]" % args.prompt} if args.config == 5 else {}),
                        "collectives": ("none" if args.gpus == 1 else f"{transport}; {layout}"),
                        "l2": "no flush: each step streams the expert weights (GBs per GPU) >> 126 MB L2"},
             "p50_tpot_ms": round(statistics.median(e2e_ms), 3),

@@ -9,6 +9,8 @@ ops:
   fp8_linear  fp8 128x128 block-scaled linear, --m --n --k
   mla_decode  config-2 sparse-MLA decode layer (128 heads, top-2048 of --ctx positions), --tokens = batch
   kda_decode  config-3 KDA layer decode step (32 heads x 128), --tokens = sequences
+  kda_prefill config-3 KDA layer core over --seqs prompts of --tokens tokens (32 heads x 128), the
+              chunked tensor-core path and the token recurrence (--mode chunked | recurrent)
   attn        the sparse-attention kernel alone, --tokens --heads --topk --ctx --splits
 
 Each op prints one JSON line: mean device time per call over --iters calls
@@ -266,6 +268,49 @@ def bench_kda_decode(a):
     return _report("kda_decode", us, nbytes, seqs=a.tokens, heads=H)
 
 
+def bench_kda_prefill(a):
+    """The KDA layer core (conv, gates, recurrence, gated norm) over a prefill batch of --seqs prompts of
+    --tokens tokens: the kernel time of `ops.kda.kda_forward` in the mode --mode.  FLOPs are those of the
+    chunked form (per 64-token chunk: the decayed key/query products, the state products, the inverse
+    application, the output and state updates, in bf16 MMA passes)."""
+    from .. import envs
+    from ..ops import kda as kda_ops
+
+    os.environ["VLLM_B200_KDA_PREFILL"] = a.mode
+    envs._cache.clear()
+    c = config3()
+    H, D = c.kda.num_heads, c.kda.head_dim
+    S, L = a.seqs, a.tokens
+    T = S * L
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn(T, 3 * H * D, device=dev, generator=g).bfloat16()
+    g_raw = torch.randn(T, H * D, device=dev, generator=g).bfloat16()
+    beta = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    g2 = torch.randn(T, H * D, device=dev, generator=g).bfloat16()
+    conv_w = (torch.randn(3 * H * D, 4, device=dev, generator=g) * 0.5).bfloat16()
+    a_log = torch.randn(H, device=dev, generator=g) * 0.5
+    norm_w = torch.ones(D, device=dev, dtype=torch.bfloat16)
+    state = torch.zeros(S + 1, H, D, D, device=dev)
+    conv = torch.zeros(S + 1, 3 * H * D, 3, device=dev, dtype=torch.bfloat16)
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+    idx = torch.arange(1, S + 1, dtype=torch.int32, device=dev)
+    init = torch.zeros(S, dtype=torch.int32, device=dev)
+    out = torch.empty(T, H * D, device=dev, dtype=torch.bfloat16)
+
+    def call():
+        kda_ops.kda_forward(qkv, g_raw, beta, g2, cu, idx, init, conv, conv_w, None, a_log, None, c.kda.lower_bound,
+                            norm_w, state, out=out)
+
+    us = time_us(call, a.iters)
+    chunks = S * H * ((L + 63) // 64)
+    flops = chunks * 2.0 * (128 * 160 * 128 + 2 * 128 * 128 * 128 + 3 * 128 * 128 * 64 + 2 * 128 * 128 * 64
+                            + 3 * 128 * 128 * 64)
+    nbytes = T * (3 * H * D * 2 + H * D * 2 * 2 + H * 2) + T * H * D * 2 + S * H * D * D * 4
+    return _report("kda_prefill", us, nbytes, flops, mode=a.mode, seqs=S, tokens=L, heads=H,
+                   us_per_token_head=round(us / (T * H), 5))
+
+
 def bench_mhc(a):
     """One mHC boundary (post + Sinkhorn coefficients + collapse + RMSNorm): --tokens tokens, 4
     streams of --dim hidden."""
@@ -293,7 +338,8 @@ def bench_mhc(a):
 
 
 OPS = {"gemm": bench_gemm, "exl3_moe": bench_exl3_moe, "marlin_moe": bench_marlin_moe, "fp8_linear": bench_fp8_linear,
-       "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode, "attn": bench_attn,
+       "mla_decode": bench_mla_decode, "kda_decode": bench_kda_decode, "kda_prefill": bench_kda_prefill,
+       "attn": bench_attn,
        "ple_decode": bench_ple_decode, "mhc": bench_mhc}
 
 
@@ -317,6 +363,8 @@ def main(argv=None):
     ap.add_argument("--bits", type=int, default=4, help="ple_decode: bits per channel")
     ap.add_argument("--profile", action="store_true", help="print a per-kernel table of one call (torch profiler)")
     ap.add_argument("--graph", action="store_true", help="time --iters calls replayed from one CUDA graph")
+    ap.add_argument("--seqs", type=int, default=8, help="kda_prefill: prompts")
+    ap.add_argument("--mode", default="chunked", choices=["chunked", "recurrent"], help="kda_prefill: path")
     a = ap.parse_args(argv)
     global _PROFILE, _GRAPH
     _PROFILE = a.profile

@@ -395,6 +395,7 @@ class ModelRunner:
         hc = bool(self.mcfg.hc_mult)
         grp = st.pp_group
         sends, toks, nbytes = [], [], 0
+        ev = self._ev_start()
         verify = {}
         mb_ctx = []
         for mb in self._micro_batches(out):
@@ -436,9 +437,7 @@ class ModelRunner:
         self.step_counter += 1
         last = st.pp_peer(st.pp_size - 1)
         if self._spec_enabled_elsewhere():
-            obj = [verify if m.last else None]
-            dist.broadcast_object_list(obj, src=last, group=st.pp_cpu_group)
-            res = obj[0]
+            res = self._pp_broadcast_lists(out, verify if m.last else None, self.cfg.scheduler.num_speculative_tokens + 1)
             self._pp_last_out, self._pp_last_res = out, res
             for mb, ctx in mb_ctx:
                 self._kda_recover(mb, ctx, res)
@@ -448,11 +447,36 @@ class ModelRunner:
             if n:
                 dist.broadcast(tokens, src=last, group=grp)
             res = self._split_tokens(out, sanitize(tokens.cpu().tolist(), self.mcfg.vocab_size))
+        self._ev_end(ev)
         self.last_stats = StepStats(num_tokens=out.num_tokens, graph=False, h2d_bytes=nbytes,
                                     d2h_bytes=8 * sum(len(v) for v in res.values()))
+        if self._events is not None:
+            self.last_stats.device_ms = self._events[0].elapsed_time(self._events[1])
+            self._events = None
         if self.device.type == "cuda":
             _ext.check_status(self.device)
         return res
+
+    def _pp_broadcast_lists(self, out: SchedulerOutput, lists: dict | None, width: int) -> dict[str, list[int]]:
+        """Token lists per request (accepted tokens of a verify step, or drafts) from the last pipeline
+        stage to every stage of this TP column, as one int64 device tensor [requests, 1 + width] (count,
+        tokens) in the step's request order, which every rank's scheduler shares: no pickled objects."""
+        import torch.distributed as dist
+
+        st = self.st
+        rids = [s.req.request_id for s in out.reqs]
+        buf = torch.full((len(rids), 1 + width), -1, dtype=torch.int64)
+        if lists is not None:
+            for i, rid in enumerate(rids):
+                v = lists.get(rid)
+                if v is not None:
+                    buf[i, 0] = len(v)
+                    buf[i, 1:1 + len(v)] = torch.tensor(v[:width], dtype=torch.int64)
+        dev = buf.to(self.device) if self.device.type == "cuda" else buf
+        dist.broadcast(dev, src=st.pp_peer(st.pp_size - 1), group=st.pp_group if self.device.type == "cuda"
+                       else st.pp_cpu_group)
+        host = dev.cpu().tolist()
+        return {rid: row[1:1 + row[0]] for rid, row in zip(rids, host) if row[0] >= 0}
 
     def _kda_verify_flags(self, out: SchedulerOutput, ctx) -> None:
         """Sequences verifying drafts through KDA layers record their updates instead of committing
@@ -536,11 +560,12 @@ class ModelRunner:
                 drafts = {s.req.request_id: list(s.req.draft_token_ids) for mb, _, _ in self._pp_hidden
                           for s in mb.reqs}
             self._pp_hidden = []
-            obj = [drafts]
-            dist.broadcast_object_list(obj, src=self.st.pp_peer(self.st.pp_size - 1), group=self.st.pp_cpu_group)
-            if self.spec is None and self._pp_last_out is not None:
+            if self._pp_last_out is None:
+                return
+            got = self._pp_broadcast_lists(self._pp_last_out, drafts, self.cfg.scheduler.num_speculative_tokens)
+            if self.spec is None:
                 for s in self._pp_last_out.reqs:
-                    d = obj[0].get(s.req.request_id)
+                    d = got.get(s.req.request_id)
                     if d is not None and not s.req.status.finished:
                         s.req.draft_token_ids = list(d)
             return
