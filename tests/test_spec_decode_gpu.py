@@ -67,6 +67,7 @@ def test_greedy_spec_matches_plain(model):
     got = [o.output_token_ids for o in llm.generate(PROMPTS, [SamplingParams(max_tokens=m) for m in MAX_TOKENS])]
     assert got == ref
     assert llm.engine.runner.spec.stats["proposed"] > 0
+    assert llm.engine.runner.spec_graphs, "uniform verify steps replay a captured graph"
 
 
 def test_planted_drafts_all_accepted(model, monkeypatch):
@@ -130,3 +131,6 @@ def test_hybrid_kda_spec_matches_plain(planted, monkeypatch):
     llm = LLM(_hybrid_cfg(k=3), m)
     got = [o.output_token_ids for o in llm.generate(PROMPTS, params)]
     assert got == ref
+    assert llm.engine.runner.spec_graphs, "uniform verify steps replay a captured graph"
+    eager = LLM(_hybrid_cfg(k=3, eager=True), m)
+    assert [o.output_token_ids for o in eager.generate(PROMPTS, params)] == ref

@@ -55,6 +55,7 @@ class ModelRunner:
         self.step_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.graphs: dict[int, tuple] = {}
         self._packed: dict[int, tuple] = {}
+        self.spec_graphs: dict[tuple, tuple] = {}
         self._status_h = torch.zeros(1, dtype=torch.int32, pin_memory=torch.cuda.is_available())
         self.graph_pool = None
         self.last_stats = StepStats()
@@ -510,7 +511,11 @@ class ModelRunner:
         return sanitize_dict(self.spec.verify(mb, logits, rows_of), self.mcfg.vocab_size)
 
     def _execute_spec(self, out: SchedulerOutput) -> dict[str, list[int]]:
-        """Eager target step with draft verification; the hidden states are kept for :meth:`propose`."""
+        """Target step with draft verification (a captured graph per batch size and draft count when the
+        step is uniform, else eager); the hidden states are kept for :meth:`propose`."""
+        k = self._spec_graph_k(out)
+        if k:
+            return self._execute_spec_graph(out, k)
         h = self._host_inputs(out)
         dev, ctx, nbytes = self._context(h)
         self._kda_verify_flags(out, ctx)
@@ -646,17 +651,7 @@ class ModelRunner:
                  ("kslot", (B,), torch.int32), ("hinit", (B,), torch.int32),
                  ("bt", (B, self.max_blocks_per_seq), torch.int32), ("temps", (B,), torch.float32),
                  ("bans", (B, sampling_ops.MAX_BANS), torch.int32)]
-        offs, off = {}, 0
-        for k, shape, dt in specs:
-            offs[k] = off
-            off += (math.prod(shape) * torch.empty((), dtype=dt).element_size() + 15) // 16 * 16
-        host = torch.zeros(off, dtype=torch.uint8, pin_memory=True)
-        devbuf = torch.zeros(off, dtype=torch.uint8, device=dev)
-        bufs, hviews = {}, {}
-        for k, shape, dt in specs:
-            nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
-            bufs[k] = devbuf[offs[k]:offs[k] + nb].view(dt).view(shape)
-            hviews[k] = host[offs[k]:offs[k] + nb].view(dt).view(shape).numpy()
+        bufs, host, devbuf, hviews = self._graph_buffers(specs)
         bufs["slots"].fill_(-1)
         bufs["tseq"].copy_(torch.arange(B, dtype=torch.int32))
         bufs["ctx"].fill_(1)
@@ -682,6 +677,135 @@ class ModelRunner:
         torch.cuda.synchronize(dev)
         self.graphs[B] = (g, bufs, ids_out)
         self._packed[B] = (host, devbuf, hviews)
+
+    def _graph_buffers(self, specs):
+        """Device views of one buffer for a graph's per-step inputs, filled by one copy from a pinned host
+        buffer of the same layout (fields 16-byte aligned): (device views, host, device, host views)."""
+        offs, off = {}, 0
+        for k, shape, dt in specs:
+            offs[k] = off
+            off += (math.prod(shape) * torch.empty((), dtype=dt).element_size() + 15) // 16 * 16
+        host = torch.zeros(off, dtype=torch.uint8, pin_memory=True)
+        devbuf = torch.zeros(off, dtype=torch.uint8, device=self.device)
+        bufs, hviews = {}, {}
+        for k, shape, dt in specs:
+            nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+            bufs[k] = devbuf[offs[k]:offs[k] + nb].view(dt).view(shape)
+            hviews[k] = host[offs[k]:offs[k] + nb].view(dt).view(shape).numpy()
+        return bufs, host, devbuf, hviews
+
+    # ------------------------------------------------------------------ speculative verify graphs
+    def _spec_graph_k(self, out: SchedulerOutput) -> int:
+        """The draft count k when this verify step replays a captured graph (one graph per batch size
+        and draft count, the reference's adaptive-k graphs, vllm_sm80/worker/adaptive_k_graphs.py:35-119):
+        every request verifies exactly k drafts from a non-empty context, one pipeline stage, graphs on.
+        0 otherwise (the eager path)."""
+        if (self.cfg.enforce_eager or not self.graphs_ok or self.device.type != "cuda" or self.st.pp_size > 1
+                or self.dsa_cores or not out.reqs or len(out.reqs) > max(self.cfg.cuda_graph_batch_sizes)):
+            return 0
+        k = out.reqs[0].num_draft
+        if k <= 0 or any(s.num_draft != k or s.num_new != k + 1 or not s.sample or s.start == 0 for s in out.reqs):
+            return 0
+        return k
+
+    def _host_inputs_spec(self, out: SchedulerOutput, Bp: int, k: int) -> dict:
+        """Inputs of a uniform verify step padded to Bp sequences of k + 1 tokens (padding: no cache rows
+        written, KDA updates only recorded)."""
+        reqs = out.reqs
+        n = k + 1
+        T = Bp * n
+        ids = np.zeros(T, dtype=np.int64)
+        pos = np.tile(np.arange(n, dtype=np.int32), Bp)
+        slots = np.full(T, -1, dtype=np.int64)
+        ctx = pos + 1
+        kslot = np.zeros(Bp, dtype=np.int32)
+        hinit = np.zeros(Bp, dtype=np.int32)
+        bt = np.zeros((Bp, self.max_blocks_per_seq), dtype=np.int32)
+        for i, s in enumerate(reqs):
+            r = s.req
+            a = s.start
+            ids[i * n:(i + 1) * n] = r.tokens(a, a + 1) + list(r.draft_token_ids[:k])
+            p = np.arange(a, a + n, dtype=np.int64)
+            pos[i * n:(i + 1) * n] = p
+            ctx[i * n:(i + 1) * n] = p + 1
+            b = np.asarray(r.block_ids, dtype=np.int64)
+            slots[i * n:(i + 1) * n] = b[p // 64] * 64 + p % 64
+            kslot[i] = max(r.kda_slot, 0)
+            hinit[i] = 1
+            bt[i] = self._bt_row(r)
+        return dict(ids=ids, pos=pos, slots=slots, ctx=ctx, kslot=kslot, hinit=hinit, bt=bt)
+
+    def _capture_spec(self, Bp: int, k: int) -> None:
+        dev = self.device
+        mml = self.cfg.scheduler.max_model_len
+        n = k + 1
+        T = Bp * n
+        specs = [("ids", (T,), torch.int64), ("pos", (T,), torch.int32), ("slots", (T,), torch.int64),
+                 ("ctx", (T,), torch.int32), ("kslot", (Bp,), torch.int32), ("hinit", (Bp,), torch.int32),
+                 ("bt", (Bp, self.max_blocks_per_seq), torch.int32)]
+        bufs, host, devbuf, hviews = self._graph_buffers(specs)
+        bufs["slots"].fill_(-1)
+        bufs["ctx"].fill_(1)
+        bufs["tseq"] = torch.arange(Bp, dtype=torch.int32, device=dev).repeat_interleave(n)
+        bufs["cu"] = torch.arange(0, T + 1, n, dtype=torch.int32, device=dev)
+        bufs["scores"] = torch.empty(T, mml, dtype=torch.float32, device=dev)
+        verify = torch.ones(Bp, dtype=torch.int32, device=dev) if self.model.kda_layer_ids() else None
+        ctx = StepContext(positions=bufs["pos"], num_tokens=T, slot_mapping=bufs["slots"], token_seq=bufs["tseq"],
+                          ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
+                          kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
+                          kda_states=self.kda_states, scores_buf=bufs["scores"], dsa_cores=self.dsa_cores,
+                          kda_verify=verify)
+
+        def fwd():
+            hidden = self.model(bufs["ids"], ctx)
+            return hidden, self.model.compute_logits(hidden)
+
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                fwd()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        if self.graph_pool is None:
+            self.graph_pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g, pool=self.graph_pool):
+            hidden, logits = fwd()
+        torch.cuda.synchronize(dev)
+        self.spec_graphs[(Bp, k)] = (g, bufs, ctx, hidden, logits, list(self.model.aux_hidden or []),
+                                     (host, devbuf, hviews))
+
+    def _execute_spec_graph(self, out: SchedulerOutput, k: int) -> dict[str, list[int]]:
+        Bp = next(b for b in sorted(self.cfg.cuda_graph_batch_sizes) if b >= len(out.reqs))
+        if (Bp, k) not in self.spec_graphs:
+            self._capture_spec(Bp, k)
+        g, bufs, ctx, hidden_all, logits_all, aux, (host, devbuf, hviews) = self.spec_graphs[(Bp, k)]
+        h = self._host_inputs_spec(out, Bp, k)
+        for name, v in hviews.items():
+            np.copyto(v, h[name])
+        devbuf.copy_(host, non_blocking=True)
+        ev = self._ev_start()
+        g.replay()
+        n, S = k + 1, len(out.reqs)
+        rows_of = {s.req.request_id: list(range(i * n, (i + 1) * n)) for i, s in enumerate(out.reqs)}
+        res = sanitize_dict(self.spec.verify(out, logits_all[:S * n], rows_of), self.mcfg.vocab_size)
+        if ctx.kda_verify is not None:
+            keep = np.zeros(Bp, dtype=np.int32)
+            keep[:S] = [max(1, len(res.get(s.req.request_id, []))) for s in out.reqs]
+            self.model.kda_recover(ctx, torch.from_numpy(keep))
+        self._ev_end(ev)
+        self.step_counter += 1
+        stats = StepStats(num_tokens=out.num_tokens, graph=True, h2d_bytes=host.numel(),
+                          d2h_bytes=8 * sum(len(v) for v in res.values()))
+        if self._events is not None:
+            stats.device_ms = self._events[0].elapsed_time(self._events[1])
+            self._events = None
+        self.last_stats = stats
+        self.model.aux_hidden = list(aux)
+        self._pending = (out, hidden_all[:S * n], res)
+        _ext.check_status(self.device)
+        return res
 
     def _stage_graph_inputs(self, B: int, h: dict) -> int:
         """Write the step's inputs into the graph's pinned host buffer and copy it to the device in one
@@ -751,4 +875,5 @@ class ModelRunner:
     def release_graphs(self):
         self.graphs.clear()
         self._packed.clear()
+        self.spec_graphs.clear()
         self.graph_pool = None
