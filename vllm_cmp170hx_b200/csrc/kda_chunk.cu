@@ -226,9 +226,18 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
   const uint32_t sbase = smem_u32(sm);
   uint32_t mma_phase = 0;
 
-  // one MMA group issued by thread 0 and waited on by everyone
+  // one MMA group issued by thread 0 and waited on by everyone, for at most two seconds (a group takes
+  // microseconds); on time-out the error is recorded and the CTA leaves its items
   auto mma_wait = [&]() -> bool {
-    const bool ok = mbar_wait(bar, mma_phase, a.status);
+    const uint64_t t_start = globaltimer();
+    bool ok = true;
+    while (!mbar_try_wait(bar, mma_phase)) {
+      if (globaltimer() - t_start > 2000000000ull) {
+        record_error(a.status, kErrMbarTimeout);
+        ok = false;
+        break;
+      }
+    }
     mma_phase ^= 1;
     if (!ok) *s_abort = 1;
     tc_fence_after();
@@ -426,22 +435,31 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
       }
       if (!mma_wait()) break;
       // ============================================================== P1: T, M and R
+      // A warp's 32 rows span two 16-row blocks (lanes 0..15: block bA, 16..31: bA + 1).  tcgen05.ld is
+      // warp-collective, so the warp loads the columns of both blocks (each when it has them) and every
+      // lane keeps its own block's.
+      float pb[16];
+      {
+        const int bA = 2 * (quarter & 1), bB = bA + 1;
+        uint32_t rA[16], rB[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) rA[i] = rB[i] = 0u;
+        if (cgrp <= bA) tmem_ld16(tl + p_col(bA) + cgrp * 16, rA);
+        if (cgrp <= bB) tmem_ld16(tl + p_col(bB) + cgrp * 16, rB);
+        tmem_wait_ld();
+        const bool upper = lane >= 16;
+        const bool have = cgrp <= (upper ? bB : bA);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pb[i] = have ? __uint_as_float(upper ? rB[i] : rA[i]) : 0.f;
+      }
       if (quarter < 2) {
         // rows t of L (lanes 0..63): T[t][s] = 1 (s = t), beta_t L[t][s] (s < t), 0 (s > t); columns
         // 16 cgrp .. 16 cgrp + 15 come from block b's P columns when cgrp <= b
-        const int t = quarter * 32 + lane, b = t >> 4;
+        const int t = quarter * 32 + lane;
         const float bt = s_beta[t];
         float x[16];
-        if (cgrp <= b) {
-          uint32_t r[16];
-          tmem_ld16(tl + p_col(b) + cgrp * 16, r);
-          tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = __uint_as_float(r[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = 0.f;
-        }
+        for (int i = 0; i < 16; ++i) x[i] = pb[i];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int s = cgrp * 16 + i;
@@ -452,18 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
           *reinterpret_cast<float4*>(s_t + t * 64 + cgrp * 16 + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
       } else {
         // rows t of M (lanes 64..127): M[t][s] for s <= t, as the K-major A operand (K = s)
-        const int t = (quarter - 2) * 32 + lane, b = t >> 4;
+        const int t = (quarter - 2) * 32 + lane;
         float x[16];
-        if (cgrp <= b) {
-          uint32_t r[16];
-          tmem_ld16(tl + p_col(b) + cgrp * 16, r);
-          tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = (cgrp * 16 + i <= t) ? __uint_as_float(r[i]) : 0.f;
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = 0.f;
-        }
+        for (int i = 0; i < 16; ++i) x[i] = (cgrp * 16 + i <= t) ? pb[i] : 0.f;
         float y[8];
 #pragma unroll
         for (int g8 = 0; g8 < 2; ++g8) {
