@@ -184,9 +184,10 @@ def test_chunked_prefill_matches_recurrence(lens, monkeypatch):
     for s in range(len(lens)):
         a, b = cu[s], cu[s + 1]
         rel = ((o_c[a:b] - o_r[a:b]).norm() / o_r[a:b].norm()).item()
-        assert rel < 2e-2, (s, lens[s], rel)
         slot = int(x["idx"][s])
         ds = (st_c[slot] - st_r[slot]).norm() / st_r[slot].norm()
+        print(f"chunked vs recurrence: len {lens[s]} out {rel:.2e} state {ds.item():.2e}")
+        assert rel < 2e-2, (s, lens[s], rel)
         assert ds < 1e-2, (s, lens[s], ds.item())
         assert torch.equal(cs_c[slot], cs_r[slot]), s
 
@@ -199,7 +200,10 @@ def test_chunked_prefill_matches_layer_oracle(monkeypatch):
     ref = kda.kda_layer(x["qkv"], x["g_raw"], x["beta_raw"], x["g2"], x["cu"], st_r, cs_r, x["idx"], x["has_init"],
                         x["conv_w"], None, x["a_log"], x["g_bias"], -5.0, x["norm_w"])
     o_c, st_c, cs_c = _run_gpu(x, "chunked", monkeypatch)
+    o_r = _run_gpu(x, "recurrent", monkeypatch)[0]
     rel = ((o_c - ref).norm() / ref.norm()).item()
+    rel_r = ((o_r - ref).norm() / ref.norm()).item()
+    print(f"vs layer oracle: chunked {rel:.2e} recurrent {rel_r:.2e}")
     assert rel < 2e-2, rel
     for s in range(2):
         slot = int(x["idx"][s])

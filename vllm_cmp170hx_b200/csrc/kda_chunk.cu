@@ -24,7 +24,7 @@
 //   P   = [K 2^(G-R) ; Q 2^(G-R)] [K 2^(R-G)]_b^T           -> L and M (four blocks, N = 16 .. 64)
 //   D2  = [Q 2^G ; K 2^G] S0^T                              (S0 as bf16 hi + lo: two passes)
 //   U   = T^-1 R,  R = diag(beta) (V - K 2^G S0^T)          (T^-1 hi + lo, R hi + lo: three passes)
-//   D2 += M U                                               (U hi + lo)
+//   D2 += M U                                               (M hi + lo, U hi + lo: three passes)
 //   S  += U^T (K 2^(G_C - G))                               (three hi/lo passes)
 // The state and the value-side operands keep about 16 mantissa bits through the hi/lo splits, the
 // decayed keys and queries are bf16.  T^-1 (unit lower triangular) comes from the four 16x16 diagonal
@@ -55,11 +55,13 @@ constexpr int OFF_GC = OFF_SMALL;               // [128] f32 chunk-end decay (lo
 constexpr int OFF_BETA = OFF_GC + 512;          // [64] f32
 constexpr int OFF_NSQ = OFF_BETA + 256;         // [4][64] f32 partial sums of squares of the output rows
 constexpr int OFF_W = OFF_NSQ + 1024;           // [3][16][16] f32 block-product scratch
-constexpr int OFF_BAR = OFF_W + 3 * 1024;       // mbarrier + tmem slot + flags
+constexpr int OFF_NW = OFF_W + 3 * 1024;        // [128] bf16 output norm weights
+constexpr int OFF_BAR = OFF_NW + 256;           // mbarrier + tmem slot + flags
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 // phase-2 aliases (after the first MMA group completed)
 constexpr int OFF_TM = OFF_A1;            // T fp32 [64][64]
-constexpr int OFF_A3 = OFF_A1 + 16384;    // M bf16 K-major [128 rows][64]: rows 64.. are stale A1 data
+constexpr int OFF_A3 = OFF_A1 + 16384;    // M hi, K-major [128 rows][64]: rows 64.. are stale (finite) data
+constexpr int OFF_A3L = OFF_B1 + 32768;   // M lo: rows 0..63 in the tail of B1, rows 64.. over the start of R hi
 constexpr int OFF_A5H = OFF_B1;           // T^-1 hi, K-major [128 rows][64]
 constexpr int OFF_A5L = OFF_B1 + 16384;   // T^-1 lo
 constexpr int OFF_RH = OFF_A2;            // R hi, MN-major [64 rows][128 values]
@@ -76,6 +78,19 @@ __host__ __device__ constexpr uint32_t p_col(int b) { return COL_P + (b == 0 ? 0
 
 // byte offset of (row r, 16-byte unit u) in a 128-byte-swizzled tile of 128-byte rows
 B200_DEVICE uint32_t swz(int r, int u) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((u ^ (r & 7)) << 4)); }
+
+// 2^x by the hardware's ex2.approx (relative error about 2^-22; flushes denormal results to zero, which
+// only affects factors below 2^-126 that multiply unit-size operands)
+B200_DEVICE float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// bring `bytes` (multiple of 16) at a 16-byte aligned global address into L2 ahead of use
+B200_DEVICE void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 B200_DEVICE uint4 pack8(const float (&x)[8]) {
   uint4 v;
@@ -161,7 +176,7 @@ __global__ void __launch_bounds__(256) kda_prep_kernel(KdaChunkArgs a) {
     qn *= rsqrtf(warp_sum(sq) + p.l2_eps);
     kn = rsqrtf(warp_sum(sk) + p.l2_eps);
   }
-  const int64_t row = ((int64_t)t * p.H + h) * D + lane * 4;
+  const int64_t row = ((int64_t)h * a.T + t) * D + lane * 4;  // head-major: a chunk's rows are contiguous
   uint2 vq, vk, vv;
   vq.x = pack_bf16x2(y[0][0] * qn, y[0][1] * qn);
   vq.y = pack_bf16x2(y[0][2] * qn, y[0][3] * qn);
@@ -181,7 +196,7 @@ __global__ void __launch_bounds__(256) kda_prep_kernel(KdaChunkArgs a) {
     gv[j] = p.lower_bound * sigmoidf_(ah * x) * kLog2e;
   }
   *reinterpret_cast<float4*>(a.gl + row) = make_float4(gv[0], gv[1], gv[2], gv[3]);
-  if (lane == 0) a.beta[(int64_t)t * p.H + h] = sigmoidf_(__bfloat162float(p.beta_raw[(int64_t)t * p.ld_beta + h]));
+  if (lane == 0) a.beta[(int64_t)h * a.T + t] = sigmoidf_(__bfloat162float(p.beta_raw[(int64_t)t * p.ld_beta + h]));
 }
 
 // ----------------------------------------------------------------------------------- chunk kernel
@@ -201,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
   float* s_w = reinterpret_cast<float*>(sm + OFF_W);
   float* s_t = reinterpret_cast<float*>(sm + OFF_TM);
   float* s_ti = reinterpret_cast<float*>(sm + OFF_TI);
+  __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(sm + OFF_NW);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + OFF_BAR + 12);
@@ -214,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
     *s_abort = 0;
     fence_barrier_init();
   }
+  if (tid < D) s_nw[tid] = p.norm_w ? p.norm_w[tid] : __float2bfloat16(1.f);
   if (warp == 0) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -281,8 +298,23 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
       tmem_wait_st();
     }
 
+    // the chunk's per-token inputs into L2 one chunk ahead (head-major rows are contiguous)
+    auto prefetch_chunk = [&](int r) {
+      if (tid == 0 && r < t1) {
+        const int m = min(C, t1 - r);
+        const int64_t row = (int64_t)h * a.T + r;
+        prefetch_l2(a.kn + row * D, (uint32_t)m * D * 2);
+        prefetch_l2(a.qn + row * D, (uint32_t)m * D * 2);
+        prefetch_l2(a.vv + row * D, (uint32_t)m * D * 2);
+        prefetch_l2(a.gl + row * D, (uint32_t)m * D * 4);
+      }
+      if (p.g2 && tid >= 32 && tid < 32 + C && r + tid - 32 < t1)  // the output gate rows (256 B each)
+        prefetch_l2(p.g2 + (int64_t)(r + tid - 32) * p.ld_g2 + h * D, D * 2);
+    };
+    prefetch_chunk(t0);
     for (int r0 = t0; r0 < t1 && !*s_abort; r0 += C) {
       const int n = min(C, t1 - r0);
+      prefetch_chunk(r0 + C);
       // ============================================================== P0: chunk operands
       // warp w: key channels 8w..8w+7; lane: rows lane and 32 + lane
       {
@@ -292,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
         for (int hf = 0; hf < 2; ++hf) {
           const int t = hf * 32 + lane;
           const bool valid = t < n;
-          const int64_t row = ((int64_t)(r0 + t) * p.H + h) * D + c0;
+          const int64_t row = ((int64_t)h * a.T + r0 + t) * D + c0;
           if (valid) {
             const float4 g0 = *reinterpret_cast<const float4*>(a.gl + row);
             const float4 g1 = *reinterpret_cast<const float4*>(a.gl + row + 4);
@@ -339,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
           // row operands (<= 1): K 2^(G - R_b), Q 2^(G - R_b)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float e = exp2f(G[hf][j] - Rb[j]);
+            const float e = ex2(G[hf][j] - Rb[j]);
             x[j] = kx[hf][j] * e;
             y[j] = qx[hf][j] * e;
           }
@@ -348,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
           // Q 2^G, K 2^G
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float e = exp2f(G[hf][j]);
+            const float e = ex2(G[hf][j]);
             x[j] = qx[hf][j] * e;
             y[j] = kx[hf][j] * e;
           }
@@ -359,12 +391,12 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
           for (int bb = 2 * hf; bb < 4; ++bb) {
             if (bb < b) continue;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) x[j] = kx[hf][j] * exp2f(R[bb][j] - G[hf][j]);
+            for (int j = 0; j < 8; ++j) x[j] = kx[hf][j] * ex2(R[bb][j] - G[hf][j]);
             sts128(sm, OFF_B1 + b1_off(bb) + kc * (16 * (bb + 1) * 128) + swz(t, u), pack8(x));
           }
           // K 2^(G_C - G), MN-major [token][key], hi / lo
 #pragma unroll
-          for (int j = 0; j < 8; ++j) x[j] = kx[hf][j] * exp2f(GCv[j] - G[hf][j]);
+          for (int j = 0; j < 8; ++j) x[j] = kx[hf][j] * ex2(GCv[j] - G[hf][j]);
           uint4 vh, vl;
           pack8_hilo(x, vh, vl);
           sts128(sm, OFF_KEH + kc * 8192 + swz(t, u), vh);
@@ -374,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             const int t = hf * 32 + lane;
-            s_beta[t] = t < n ? a.beta[(int64_t)(r0 + t) * p.H + h] : 0.f;
+            s_beta[t] = t < n ? a.beta[(int64_t)h * a.T + r0 + t] : 0.f;
           }
         }
       }
@@ -401,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
           }
           uint32_t w8[2][8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w8[i >> 3][i & 7] = __float_as_uint(x[i >> 3][i & 7] * exp2f(s_gc[col + i]));
+          for (int i = 0; i < 16; ++i) w8[i >> 3][i & 7] = __float_as_uint(x[i >> 3][i & 7] * ex2(s_gc[col + i]));
           tmem_st8(tl + COL_S + col, w8[0]);
           tmem_st8(tl + COL_S + col + 8, w8[1]);
         }
@@ -479,7 +511,10 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
         for (int g8 = 0; g8 < 2; ++g8) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) y[i] = x[g8 * 8 + i];
-          sts128(sm, OFF_A3 + swz(t, cgrp * 2 + g8), pack8(y));
+          uint4 vh, vl;
+          pack8_hilo(y, vh, vl);
+          sts128(sm, OFF_A3 + swz(t, cgrp * 2 + g8), vh);
+          sts128(sm, OFF_A3L + swz(t, cgrp * 2 + g8), vl);
         }
         // R[s][v] = beta_s (v_s - (K 2^G S0^T)[s][v]) for values 32 cgrp .. + 31, MN-major hi / lo
         const int s = t;
@@ -493,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
           tmem_wait_ld();
           float vin[16];
           if (valid) {
-            const __nv_bfloat16* src = a.vv + ((int64_t)(r0 + s) * p.H + h) * D + v0;
+            const __nv_bfloat16* src = a.vv + ((int64_t)h * a.T + r0 + s) * D + v0;
             float f8[8];
             bf16x8_to_f32(*reinterpret_cast<const uint4*>(src), f8);
 #pragma unroll
@@ -613,14 +648,14 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
       }
       sync_for_mma();
       if (tid == 0) {
-        // D2 += M U (U = hi + lo)
+        // D2 += M U: (hi, hi), (hi, lo), (lo, hi)
         const uint32_t idesc3 = make_idesc_f16(128, 128, 1, false, true);
 #pragma unroll
-        for (int pass = 0; pass < 2; ++pass)
+        for (int pass = 0; pass < 3; ++pass)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tbase + COL_D2, kdesc(sbase + OFF_A3 + kk * 32),
-                     mdesc(sbase + (pass ? OFF_UL : OFF_UH) + kk * 2048, 8192), idesc3, 1u);
+            umma_f16(tbase + COL_D2, kdesc(sbase + (pass == 2 ? OFF_A3L : OFF_A3) + kk * 32),
+                     mdesc(sbase + (pass == 1 ? OFF_UL : OFF_UH) + kk * 2048, 8192), idesc3, 1u);
         // S += U^T (K 2^(G_C - G)): (hi, hi), (hi, lo), (lo, hi); A = U MN-major, B MN-major
         const uint32_t idesc4 = make_idesc_f16(128, 128, 1, true, true);
 #pragma unroll
@@ -636,43 +671,51 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
       }
       if (!mma_wait()) break;
       // ============================================================== P4: output rows, gated RMSNorm
-      float o[32];
       const int t = quarter * 32 + lane;  // rows 0..63 in quarters 0, 1
       if (quarter < 2) {
-        uint32_t r[16];
-        tmem_ld16(tl + COL_D2 + cgrp * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(r[i]);
-        tmem_ld16(tl + COL_D2 + cgrp * 32 + 16, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[16 + i] = __uint_as_float(r[i]);
         float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ss += o[i] * o[i];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t r[16];
+          tmem_ld16(tl + COL_D2 + cgrp * 32 + half * 16, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) ss += __uint_as_float(r[i]) * __uint_as_float(r[i]);
+        }
         s_nsq[cgrp * 64 + t] = ss;
       }
       __syncthreads();
-      if (quarter < 2 && t < n) {
+      if (quarter < 2) {  // warp-uniform: the TMEM reads are warp-collective; rows past n are not stored
         const int64_t tok = r0 + t;
         float scale = 1.f;
         if (p.norm_w) scale = rsqrtf((s_nsq[t] + s_nsq[64 + t] + s_nsq[128 + t] + s_nsq[192 + t]) / D + p.eps);
         __nv_bfloat16* dst = p.out + tok * p.ld_out + h * D + cgrp * 32;
 #pragma unroll
-        for (int g8 = 0; g8 < 4; ++g8) {
-          float y[8];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t r[16];
+          tmem_ld16(tl + COL_D2 + cgrp * 32 + half * 16, r);
+          tmem_wait_ld();
+          if (t < n) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int v = cgrp * 32 + g8 * 8 + i;
-            float z = o[g8 * 8 + i];
-            if (p.norm_w) {
-              z *= scale * __bfloat162float(p.norm_w[v]);
-              if (p.g2) z *= sigmoidf_(__bfloat162float(p.g2[tok * p.ld_g2 + h * D + v]));
+            for (int g8 = 0; g8 < 2; ++g8) {
+              const int c8 = half * 16 + g8 * 8;  // first of these 8 values within the 32
+              float y[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(r[g8 * 8 + i]);
+              if (p.norm_w) {
+                float nw[8], gg[8];
+                bf16x8_to_f32(*reinterpret_cast<const uint4*>(s_nw + cgrp * 32 + c8), nw);
+                if (p.g2)  // the chunk's gate rows were prefetched into L2 at its start
+                  bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.g2 + tok * p.ld_g2 + h * D + cgrp * 32 + c8), gg);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  y[i] *= scale * nw[i];
+                  if (p.g2) y[i] *= sigmoidf_(gg[i]);
+                }
+              }
+              *reinterpret_cast<uint4*>(dst + c8) = pack8(y);
             }
-            y[i] = z;
           }
-          *reinterpret_cast<uint4*>(dst + g8 * 8) = pack8(y);
         }
       }
       // the next chunk's first barrier orders these TMEM reads before its MMAs

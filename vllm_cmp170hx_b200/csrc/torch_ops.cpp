@@ -329,6 +329,11 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
     TORCH_CHECK(out.stride(0) >= H * 128 && out.stride(0) % 8 == 0 &&
                     reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
                 "kda: chunked output rows must be 16-byte aligned");
+    TORCH_CHECK(!g2.has_value() || (g2->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(g2->data_ptr()) % 16 == 0),
+                "kda: chunked output gate rows must be 16-byte aligned");
+    TORCH_CHECK(!norm_w.has_value() || (norm_w->is_contiguous() &&
+                                        reinterpret_cast<uintptr_t>(norm_w->data_ptr()) % 16 == 0),
+                "kda: chunked norm weight must be contiguous and 16-byte aligned");
     TORCH_CHECK(status.has_value() && status->scalar_type() == at::kInt, "kda: status word");
     a.skip_long = (int)chunk_min_len;
     B200_LAUNCH(kda_recurrent(a, cur_stream()));
