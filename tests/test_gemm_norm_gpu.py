@@ -13,6 +13,18 @@ def _rel_err(y, r):
     return ((y.float() - r.float()).norm() / r.float().norm().clamp_min(1e-12)).item()
 
 
+def _tile_max_err(y, r, tm=128, tn=16):
+    """Worst tile of the output: max |y - r| over a tile against the tile's max |r| (a wrong tile in a
+    large matrix barely moves the global norm error)."""
+    y, r = y.float(), r.float()
+    worst = 0.0
+    for i in range(0, r.shape[0], tm):
+        for j in range(0, r.shape[1], tn):
+            d = (y[i:i + tm, j:j + tn] - r[i:i + tm, j:j + tn]).abs().max().item()
+            worst = max(worst, d / max(r[i:i + tm, j:j + tn].abs().max().item(), 1e-6))
+    return worst
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 2304, 2304), (7, 4096, 2304), (16, 256, 128), (33, 1000, 520),
                                    (128, 2304, 4096), (129, 512, 256), (300, 777, 1024), (1024, 2048, 2304)])
 def test_gemm_bf16(M, N, K):
@@ -24,6 +36,9 @@ def test_gemm_bf16(M, N, K):
     torch.cuda.synchronize()
     _ext.check_status(x.device)
     assert _rel_err(y, r) < 1e-2, (M, N, K, _rel_err(y, r))
+    # both tile orientations of the kernel (swapped for M <= 128: tokens along the tile's N)
+    assert _tile_max_err(y, r) < 3e-2, (M, N, K, _tile_max_err(y, r))
+    assert _tile_max_err(y, r, 16, 128) < 3e-2, (M, N, K)
 
 
 @pytest.mark.parametrize("splits", [1, 2, 5])
@@ -36,6 +51,7 @@ def test_gemm_bf16_splits_and_bias(splits):
     y = ops.gemm(x, w, b, splits=splits)
     r = x.float() @ w.float().t() + b.float()
     assert _rel_err(y, r) < 1e-2
+    assert _tile_max_err(y, r) < 3e-2
 
 
 def test_gemm_deterministic():
