@@ -79,3 +79,20 @@ def test_banned_tokens_in_kernel_and_graph():
         out = LLM(_cfg("cuda", eager=eager), model).generate(prompts, ps)
         assert ban not in out[0].output_token_ids
         assert out[1].output_token_ids == free[1].output_token_ids
+
+
+def test_kv_pool_sized_from_a_profiled_step():
+    """With num_blocks = 0 the runner measures one full prefill step's activation peak and sizes the KV
+    pool from the free memory left: the peak is positive, the pool covers every sequence, and the
+    engine generates with it."""
+    pstate.set_state(pstate.ParallelState())
+    cfg = EngineConfig(model=tiny(layers=4, experts=8), device="cuda", enforce_eager=False,
+                       scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=512, max_model_len=512),
+                       cache=CacheConfig(num_blocks=0, gpu_memory_utilization=0.5), cuda_graph_batch_sizes=[1, 2, 4])
+    model = HybridForCausalLM(cfg.model, "cuda", seed=4, init_mode="local")
+    llm = LLM(cfg, model)
+    r = llm.engine.runner
+    assert r.activation_peak > 0
+    assert r.num_blocks == cfg.scheduler.max_num_seqs * r.max_blocks_per_seq + 1
+    outs = llm.generate([list(range(10, 10 + n)) for n in (7, 130)], SamplingParams(max_tokens=4))
+    assert all(len(o.output_token_ids) == 4 for o in outs)

@@ -127,13 +127,64 @@ class ModelRunner:
                     k = sc.num_speculative_tokens
                     kda_bytes += n_dsa * (self.num_slots * ((a.window + k) * a.head_dim * 2 + (k + 2) * a.head_dim * 8)
                                           + max(sc.max_num_batched_tokens, sc.max_num_seqs) * a.head_dim * 2)
-                scratch = 6 << 30
+                scratch = self._activation_reserve()
+                free, _total = torch.cuda.mem_get_info(self.device)
                 avail = free * cfg.cache.gpu_memory_utilization - kda_bytes - scratch
                 nb = int(max(avail, 0) // per_block)
                 want = cfg.scheduler.max_num_seqs * self.max_blocks_per_seq + 1
                 nb = max(2, min(nb, want))
             else:
                 nb = cfg.scheduler.max_num_seqs * self.max_blocks_per_seq + 1
+        self._make_caches(nb)
+        self.graphs_ok = True
+
+    def _activation_reserve(self) -> int:
+        """Bytes a full prefill step allocates on top of the caches, measured: one forward of
+        max_num_batched_tokens prompt tokens (sequences of up to max_model_len tokens, no cache rows
+        written) over a cache of one sequence's blocks, the peak of the allocator minus its level before,
+        plus a quarter and 1 GiB for CUDA graphs and the drafter (the reference sizes its KV pool from
+        a profiling run the same way, vllm_sm80/kv_planning.py:48,503).  With pipeline parallelism (a
+        forward needs the other stages) a fixed 6 GiB."""
+        from .request import Request, SamplingParams
+        from .scheduler import ScheduledReq
+
+        sc = self.cfg.scheduler
+        if self.st.pp_size > 1 or self.device.type != "cuda":
+            return 6 << 30
+        self._make_caches(self.max_blocks_per_seq + 1)
+        T = max(sc.max_num_batched_tokens, 1)
+        L = max(1, min(sc.max_model_len - 1, T))
+        reqs, left = [], T
+        while left > 0 and len(reqs) < sc.max_num_seqs:
+            n = min(L, left)
+            r = Request([1] * n, SamplingParams(max_tokens=1), request_id=f"__profile_{len(reqs)}__")
+            r.block_ids = [0] * self.max_blocks_per_seq
+            r.kda_slot = 0
+            reqs.append(ScheduledReq(r, n, 0, True))
+            left -= n
+        out = SchedulerOutput(reqs=reqs)
+        torch.cuda.synchronize(self.device)
+        torch.cuda.reset_peak_memory_stats(self.device)
+        base = torch.cuda.memory_allocated(self.device)
+        with torch.inference_mode():
+            h = self._host_inputs(out)
+            h["slots"][:] = -1  # no cache rows written
+            dev, ctx, _ = self._context(h)
+            hidden = self.model(dev["ids"], ctx)
+            self.model.compute_logits(hidden.index_select(0, self._to_dev(h["sample_rows"])))
+        torch.cuda.synchronize(self.device)
+        peak = torch.cuda.max_memory_allocated(self.device) - base
+        del hidden, dev, ctx
+        self.mla_caches, self.kda_states, self.dsa_cores = {}, {}, {}
+        torch.cuda.empty_cache()
+        self.activation_peak = int(peak)
+        return int(peak * 1.25) + (1 << 30)
+
+    def _make_caches(self, nb: int) -> None:
+        cfg = self.cfg
+        m = self.model
+        kda_ids, mla_ids = m.kda_layer_ids(), m.mla_layer_ids()
+        rec_shape, conv_shape = m.kda_state_shapes()
         self.num_blocks = nb
         rows = nb * 64
         self.mla_caches = {}
@@ -156,7 +207,6 @@ class ModelRunner:
                                                            sc.num_speculative_tokens, self.device)
         self.block_pool = make_block_pool(nb, 1)
         self.slot_pool = SlotPool(self.num_slots, 1) if (kda_ids or dsa_ids) else None
-        self.graphs_ok = True
 
     # ------------------------------------------------------------------ inputs
     def _bt_row(self, r) -> np.ndarray:
