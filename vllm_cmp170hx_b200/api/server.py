@@ -258,7 +258,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--max-num-seqs", type=int, default=64)
     ap.add_argument("--max-model-len", type=int, default=8192)
     ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
-    ap.add_argument("--prefill-chunk-with-decodes", action="store_true", default=True)
+    ap.add_argument("--prefill-chunk-with-decodes", type=int, default=0,
+                    help="fair chunked prefill: the prefill-only token budget of a step while requests decode "
+                         "(0: off)")
     ap.add_argument("--max-num-partial-prefills", type=int, default=1)
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--pp", type=int, default=1, help="pipeline-parallel stages")

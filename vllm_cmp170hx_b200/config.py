@@ -280,7 +280,9 @@ class SchedulerConfig:
     max_num_seqs: int = 256
     max_num_batched_tokens: int = 8192
     max_model_len: int = 8192
-    prefill_chunk_with_decodes: bool = True  # fair chunked prefill: decodes ride along prefill chunks
+    # fair chunked prefill: while a running request decodes, prefill chunks of a step draw on a second
+    # budget of this many tokens (0: off), split evenly between up to max_num_partial_prefills prompts
+    prefill_chunk_with_decodes: int = 0
     max_num_partial_prefills: int = 1
     long_prefill_token_threshold: int = 0
     num_speculative_tokens: int = 0
@@ -288,6 +290,7 @@ class SchedulerConfig:
     spec_method: str = "mtp"  # drafter: 'mtp' (chained MTP head) or 'dflash' (block drafter)
     dflash_layers: int = 1  # DFlash drafter depth
     depth_policy: str = ""  # per-request verify depth policy file (dspark-depth-policy/1); "" off
+    pp_spread_decodes: bool = True  # pipeline micro-batches take equal shares of the decodes
 
 
 @dataclass

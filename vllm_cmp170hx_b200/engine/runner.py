@@ -416,9 +416,25 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ pipeline parallel
     def _micro_batches(self, out: SchedulerOutput) -> list[SchedulerOutput]:
-        """Split the step into up to pp_size micro-batches of consecutive requests with about equal
-        token counts, so stage s works on micro-batch i + 1 while stage s + 1 works on i."""
+        """Split the step into up to pp_size micro-batches, so stage s works on micro-batch i + 1 while
+        stage s + 1 works on i.  With decode spreading (the reference's PP decode cap,
+        vllm_sm80/sched/scheduler.py:329) every micro-batch takes an equal share of the decoding
+        requests and the prefill chunks fill in by token count, so no micro-batch holds all the decodes
+        behind a long chunk; otherwise consecutive requests with about equal token counts."""
         n = min(self.st.pp_size, len(out.reqs))
+        if self.cfg.scheduler.pp_spread_decodes and n > 1:
+            bins = [[] for _ in range(n)]
+            load = [0] * n
+            decodes = [s for s in out.reqs if s.num_new - s.num_draft == 1 and s.start > 0]
+            did = {id(s) for s in decodes}
+            for j, s in enumerate(decodes):
+                bins[j % n].append(s)
+                load[j % n] += s.num_new
+            for s in sorted((s for s in out.reqs if id(s) not in did), key=lambda s: -s.num_new):
+                j = min(range(n), key=lambda b: load[b])
+                bins[j].append(s)
+                load[j] += s.num_new
+            return [SchedulerOutput(reqs=b) for b in bins if b]
         total = out.num_tokens
         mbs, cur, acc = [], [], 0
         for s in out.reqs:
@@ -449,7 +465,9 @@ class ModelRunner:
         ev = self._ev_start()
         verify = {}
         mb_ctx = []
-        for mb in self._micro_batches(out):
+        mbs = self._micro_batches(out)
+        out = SchedulerOutput(reqs=[s for mb in mbs for s in mb.reqs], preempted=out.preempted)
+        for mb in mbs:
             h = self._host_inputs(mb)
             dev, ctx, nb = self._context(h)
             if self._spec_enabled_elsewhere():

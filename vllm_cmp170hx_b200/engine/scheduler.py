@@ -12,8 +12,15 @@ head with `num_computed_tokens = 0`).
 Fair chunked prefill (the reference's `--prefill-chunk-with-decodes`,
 `--max-num-partial-prefills`, vllm_sm80/sched/step.py:36 Sm80Step): at most
 `max_num_partial_prefills` requests are in a partial prefill at once and a
-request's chunk is capped at `long_prefill_token_threshold` when set, so
-decodes keep flowing while long prompts are chunked.
+request's chunk is capped at `long_prefill_token_threshold` when set.  With
+`prefill_chunk_with_decodes` > 0 and some running request decoding, prefill
+chunks also draw on a second, prefill-only budget of that many tokens, split
+evenly between the prompts that can advance this step (running chunks and
+admissible waiting prompts, up to `max_num_partial_prefills`); decode tokens
+never draw on it, so decodes keep their slot in every step while long prompts
+are chunked.  Prompts the short-prompt bypass exempts are neither capped nor
+charged.  (Requests are preempted only from the back of the running list,
+after the ones already scheduled this step, so no charge needs a refund.)
 """
 
 from __future__ import annotations
@@ -169,11 +176,30 @@ class Scheduler:
         out.preempted.append(victim)
 
     # ------------------------------------------------------------------ schedule
+    def _prefill_budget(self, budget: int) -> tuple[int, int]:
+        """This step's prefill-only budget and per-prompt chunk cap (both = budget when off or when no
+        running request decodes)."""
+        total = budget
+        if self.cfg.prefill_chunk_with_decodes > 0 and any(
+                r.num_tokens - r.num_computed_tokens <= 1 and r.num_computed_tokens > 0 for r in self.running):
+            total = min(total, self.cfg.prefill_chunk_with_decodes)
+        per = total
+        if self.cfg.prefill_chunk_with_decodes > 0 and self.cfg.max_num_partial_prefills > 0:
+            n = sum(1 for r in self.running
+                    if (r.num_tokens - r.num_computed_tokens > 1 or r.num_computed_tokens == 0)
+                    and r.num_prompt_tokens > self.short_bypass)
+            n += sum(1 for r in list(self.waiting)[: self.cfg.max_num_partial_prefills]
+                     if r.num_prompt_tokens > self.short_bypass)
+            n = min(max(n, 1), self.cfg.max_num_partial_prefills)
+            per = max(1, total // n)
+        return total, per
+
     def schedule(self) -> SchedulerOutput:
         out = SchedulerOutput()
         budget = self.cfg.max_num_batched_tokens
         partial = 0
         cap = self.cfg.long_prefill_token_threshold or budget
+        prefill_left, per_prompt = self._prefill_budget(budget)
         scheduled_ids = set()
         i = 0
         while i < len(self.running):
@@ -185,6 +211,8 @@ class Scheduler:
                     i += 1
                     continue
                 n = min(remaining, budget, cap)
+                if req.num_prompt_tokens > self.short_bypass:
+                    n = min(n, per_prompt, prefill_left)
                 drafts = 0
             else:
                 drafts = min(len(req.draft_token_ids), max(0, budget - 1), self.draft_cap)
@@ -208,6 +236,8 @@ class Scheduler:
             sample = req.num_computed_tokens + n >= req.num_tokens
             if not sample:
                 partial += 1
+            if drafts == 0 and n > 1 and req.num_prompt_tokens > self.short_bypass:
+                prefill_left -= n
             out.reqs.append(ScheduledReq(req, n, req.num_computed_tokens, sample, drafts))
             scheduled_ids.add(req.request_id)
             budget -= n
@@ -223,6 +253,11 @@ class Scheduler:
             elif self.prefix_caching and req.num_computed_tokens == 0 and not req.block_ids:
                 self._take_cached_prefix(req)
             n = min(req.num_tokens - req.num_computed_tokens, budget, cap)
+            charged = req.num_tokens - req.num_computed_tokens > 1 and req.num_prompt_tokens > self.short_bypass
+            if charged:
+                if prefill_left <= 0:
+                    break
+                n = min(n, per_prompt, prefill_left)
             upto = req.num_computed_tokens + n
             if upto >= req.num_tokens:
                 upto = min(upto + self.lookahead, self.cfg.max_model_len)
@@ -239,6 +274,8 @@ class Scheduler:
             sample = req.num_computed_tokens + n >= req.num_tokens
             if not sample:
                 partial += 1
+            if charged:
+                prefill_left -= n
             out.reqs.append(ScheduledReq(req, n, req.num_computed_tokens, sample, 0))
             budget -= n
         return out
