@@ -21,13 +21,15 @@
 // B200 layout: a persistent CTA of 16 warps per (sequence, head) item, the fp32 state resident in TMEM
 // for the whole sequence (128 lanes = value rows, 128 columns = key channels).  Per chunk, one thread
 // issues five tcgen05 MMA groups (bf16 operands in 128-byte-swizzled shared memory, fp32 accumulate):
-//   P   = [K 2^(G-R) ; Q 2^(G-R)] [K 2^(R-G)]_b^T           -> L and M (four blocks, N = 16 .. 64)
+//   P   = [K 2^(G-R) ; Q 2^(G-R)] [K 2^(R-G)]_b^T           -> L and M (four blocks, N = 16 .. 64; hi/lo
+//                                                           passes: three for L, two for M)
 //   D2  = [Q 2^G ; K 2^G] S0^T                              (S0 as bf16 hi + lo: two passes)
 //   U   = T^-1 R,  R = diag(beta) (V - K 2^G S0^T)          (T^-1 hi + lo, R hi + lo: three passes)
 //   D2 += M U                                               (M hi + lo, U hi + lo: three passes)
 //   S  += U^T (K 2^(G_C - G))                               (three hi/lo passes)
-// The state and the value-side operands keep about 16 mantissa bits through the hi/lo splits, the
-// decayed keys and queries are bf16.  T^-1 (unit lower triangular) comes from the four 16x16 diagonal
+// The key-key products (L: the delta rule's correction can cancel, so its errors are amplified), the
+// state and the value-side operands keep about 16 mantissa bits through the hi/lo splits; the decayed
+// queries and the keys of the state products are bf16.  T^-1 (unit lower triangular) comes from the four 16x16 diagonal
 // inverses by forward substitution and the off-diagonal blocks by block products, on the CUDA cores in
 // fp32.  A prep kernel computes the per-token inputs in parallel first (conv1d + SiLU, L2 norms, the
 // log2 decay, beta); the gated RMSNorm of the output runs in the chunk's epilogue.
@@ -42,15 +44,19 @@ constexpr int C = 64;
 constexpr int kThreads = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// shared memory (byte offsets from a 1024-aligned base)
-constexpr int OFF_A1 = 0;         // [K 2^(G-R) ; Q 2^(G-R)]: 128 rows x 128 K, two 64-wide K chunks of 16 KiB
-constexpr int OFF_B1 = 32768;     // [K 2^(R_b - G)] for b = 0..3: 16 (b + 1) rows each, two K chunks
-constexpr int OFF_A2 = 73728;     // [Q 2^G ; K 2^G]: 128 rows x 128 K
-constexpr int OFF_B2H = 106496;   // S0 hi: 128 value rows x 128 key K
-constexpr int OFF_B2L = 139264;   // S0 lo
-constexpr int OFF_KEH = 172032;   // K 2^(G_C - G) hi, MN-major: [64 tokens][128 keys] as two 64-key chunks
-constexpr int OFF_KEL = 188416;   // lo
-constexpr int OFF_SMALL = 204800;
+// shared memory (byte offsets from a 1024-aligned base).  Region X is reused three times per chunk:
+// the operands of the first MMA group, then S0 (hi / lo) for the second, then the phase-2 tiles.
+constexpr int OFF_A1H = 0;        // [K 2^(G-R) ; Q 2^(G-R)] hi: 128 rows x 128 K, two 64-wide K chunks of 16 KiB
+constexpr int OFF_A1L = 32768;    // lo of the K rows; rows 64..127 zero (M needs no lo part)
+constexpr int OFF_B1H = 65536;    // [K 2^(R_b - G)] hi for b = 0..3: 16 (b + 1) rows each, two K chunks
+constexpr int OFF_B1L = 106496;   // lo
+constexpr int REGION_X = 147456;
+constexpr int OFF_B2H = 0;        // (after the first group) S0 hi: 128 value rows x 128 key K
+constexpr int OFF_B2L = 32768;    // S0 lo
+constexpr int OFF_A2 = REGION_X;  // [Q 2^G ; K 2^G]: 128 rows x 128 K
+constexpr int OFF_KEH = OFF_A2 + 32768;   // K 2^(G_C - G) hi, MN-major: [64 tokens][128 keys] as two 64-key chunks
+constexpr int OFF_KEL = OFF_KEH + 16384;  // lo
+constexpr int OFF_SMALL = OFF_KEL + 16384;
 constexpr int OFF_GC = OFF_SMALL;               // [128] f32 chunk-end decay (log2)
 constexpr int OFF_BETA = OFF_GC + 512;          // [64] f32
 constexpr int OFF_NSQ = OFF_BETA + 256;         // [4][64] f32 partial sums of squares of the output rows
@@ -58,17 +64,18 @@ constexpr int OFF_W = OFF_NSQ + 1024;           // [3][16][16] f32 block-product
 constexpr int OFF_NW = OFF_W + 3 * 1024;        // [128] bf16 output norm weights
 constexpr int OFF_BAR = OFF_NW + 256;           // mbarrier + tmem slot + flags
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
-// phase-2 aliases (after the first MMA group completed)
-constexpr int OFF_TM = OFF_A1;            // T fp32 [64][64]
-constexpr int OFF_A3 = OFF_A1 + 16384;    // M hi, K-major [128 rows][64]: rows 64.. are stale (finite) data
-constexpr int OFF_A3L = OFF_B1 + 32768;   // M lo: rows 0..63 in the tail of B1, rows 64.. over the start of R hi
-constexpr int OFF_A5H = OFF_B1;           // T^-1 hi, K-major [128 rows][64]
-constexpr int OFF_A5L = OFF_B1 + 16384;   // T^-1 lo
-constexpr int OFF_RH = OFF_A2;            // R hi, MN-major [64 rows][128 values]
-constexpr int OFF_RL = OFF_A2 + 16384;    // R lo
-constexpr int OFF_UH = OFF_B2H;           // U hi, MN-major [64 rows][128 values]
-constexpr int OFF_UL = OFF_B2H + 16384;   // U lo
-constexpr int OFF_TI = OFF_B2L;           // T^-1 fp32 [64][64]
+// phase-2 tiles in region X (after the second group).  The rows 64.. of the 128-row A operands are read
+// by the MMAs but never used: they hold stale, finite data of the earlier phases.
+constexpr int OFF_TM = 0;                 // T fp32 [64][64]
+constexpr int OFF_TI = 16384;             // T^-1 fp32 [64][64]
+constexpr int OFF_A3 = 32768;             // M hi, K-major [128 rows][64]
+constexpr int OFF_A3L = 49152;            // M lo
+constexpr int OFF_A5H = 65536;            // T^-1 hi, K-major [128 rows][64]
+constexpr int OFF_A5L = 81920;            // T^-1 lo
+constexpr int OFF_RH = 98304;             // R hi, MN-major [64 rows][128 values]
+constexpr int OFF_RL = 114688;            // R lo
+constexpr int OFF_UH = 131072;            // U hi, MN-major [64 rows][128 values]
+constexpr int OFF_UL = OFF_A2;            // U lo (the second group's A operand is free by then)
 // B1 block b: rows 16 (b + 1), chunk stride rows * 128
 __host__ __device__ constexpr int b1_off(int b) { return b == 0 ? 0 : b == 1 ? 4096 : b == 2 ? 12288 : 24576; }
 
@@ -375,8 +382,14 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
             x[j] = kx[hf][j] * e;
             y[j] = qx[hf][j] * e;
           }
-          sts128(sm, OFF_A1 + kc * 16384 + swz(t, u), pack8(x));
-          sts128(sm, OFF_A1 + kc * 16384 + swz(64 + t, u), pack8(y));
+          {
+            uint4 vh, vl;
+            pack8_hilo(x, vh, vl);
+            sts128(sm, OFF_A1H + kc * 16384 + swz(t, u), vh);
+            sts128(sm, OFF_A1L + kc * 16384 + swz(t, u), vl);
+            sts128(sm, OFF_A1H + kc * 16384 + swz(64 + t, u), pack8(y));
+            sts128(sm, OFF_A1L + kc * 16384 + swz(64 + t, u), make_uint4(0, 0, 0, 0));
+          }
           // Q 2^G, K 2^G
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -392,7 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
             if (bb < b) continue;
 #pragma unroll
             for (int j = 0; j < 8; ++j) x[j] = kx[hf][j] * ex2(R[bb][j] - G[hf][j]);
-            sts128(sm, OFF_B1 + b1_off(bb) + kc * (16 * (bb + 1) * 128) + swz(t, u), pack8(x));
+            uint4 vh, vl;
+            pack8_hilo(x, vh, vl);
+            sts128(sm, OFF_B1H + b1_off(bb) + kc * (16 * (bb + 1) * 128) + swz(t, u), vh);
+            sts128(sm, OFF_B1L + b1_off(bb) + kc * (16 * (bb + 1) * 128) + swz(t, u), vl);
           }
           // K 2^(G_C - G), MN-major [token][key], hi / lo
 #pragma unroll
@@ -410,8 +426,30 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
           }
         }
       }
-      __syncthreads();  // s_gc
-      // ---- S0 hi / lo as the K-major B operand (row v, K = keys), then S *= 2^G_C in TMEM
+      sync_for_mma();  // the operands of the first group (and s_gc) are written
+      if (tid == 0) {
+        // P_b = [K 2^(G-R) ; Q 2^(G-R)] (K 2^(R_b - G))^T, b = 0..3: (hi, hi), (hi, lo), (lo, hi); the
+        // lo part of A holds only the key rows, so the M rows get two passes
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t idesc = make_idesc_f16(128, 16 * (b + 1), 1);
+#pragma unroll
+          for (int pass = 0; pass < 3; ++pass) {
+            const int ao = pass == 2 ? OFF_A1L : OFF_A1H;
+            const int bo = (pass == 1 ? OFF_B1L : OFF_B1H) + b1_off(b);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t da = kdesc(sbase + ao + (kk >> 2) * 16384 + (kk & 3) * 32);
+              const uint64_t db = kdesc(sbase + bo + (kk >> 2) * (16 * (b + 1) * 128) + (kk & 3) * 32);
+              umma_f16(tbase + p_col(b), da, db, idesc, (pass > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+        }
+        umma_commit(bar);
+      }
+      if (!mma_wait()) break;
+      // ---- S0 hi / lo as the K-major B operand (row v, K = keys) over the first group's operands,
+      // then S *= 2^G_C in TMEM
       {
         const int v = quarter * 32 + lane;
 #pragma unroll
@@ -441,17 +479,6 @@ __global__ void __launch_bounds__(kThreads, 1) kda_chunk_kernel(KdaChunkArgs a) 
       }
       sync_for_mma();
       if (tid == 0) {
-        // P_b = [K 2^(G-R) ; Q 2^(G-R)] (K 2^(R_b - G))^T, b = 0..3
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const uint32_t idesc = make_idesc_f16(128, 16 * (b + 1), 1);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t da = kdesc(sbase + OFF_A1 + (kk >> 2) * 16384 + (kk & 3) * 32);
-            const uint64_t db = kdesc(sbase + OFF_B1 + b1_off(b) + (kk >> 2) * (16 * (b + 1) * 128) + (kk & 3) * 32);
-            umma_f16(tbase + p_col(b), da, db, idesc, kk > 0 ? 1u : 0u);
-          }
-        }
         // D2 = [Q 2^G ; K 2^G] S0^T, S0 = hi + lo
         const uint32_t idesc2 = make_idesc_f16(128, 128, 1);
 #pragma unroll

@@ -584,8 +584,11 @@ class DecoderLayer(nn.Module):
         layer's output."""
         sp.apply(pending, residual, self.input_norm.weight, self.input_norm.eps, ag=True)
         if isinstance(self.attn, MLAAttention) and self.attn.full_heads:
-            # data-parallel attention: this rank's tokens, all heads, output complete on this rank
-            a = self.attn.forward_dp(sp.gathered(), ctx, self.idx, sp)
+            # data-parallel attention: this rank's tokens, all heads, output complete on this rank.  In
+            # the scope, its input GEMM is the all-gather area's first reader and waits for the peers'
+            # rows (it issues no row-parallel reduction)
+            with sp_scope(sp):
+                a = self.attn.forward_dp(sp.gathered(), ctx, self.idx, sp)
             if self.mlp is None:
                 return ("add", a)
             h = torch.empty_like(residual)
