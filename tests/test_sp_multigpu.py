@@ -220,7 +220,8 @@ def _reference():
 
 
 @pytest.mark.parametrize("dispatch,mla_dp,eager", [("symm", "1", "0"), ("symm", "1", "1"), ("symm", "0", "0"),
-                                                  ("nccl", "1", "0"), ("off", "1", "0")])
+                                                  ("symm", "0", "1"), ("nccl", "1", "0"), ("nccl", "1", "1"),
+                                                  ("off", "1", "0")])
 def test_sp_engine_tp2_matches_one_gpu(dispatch, mla_dp, eager):
     """The first three steps' logits (a 256-token prefill chunk, then the rest of the prompts with the
     first decodes, then a decode step) at TP=2 agree with one GPU's to bf16 rounding of the partial

@@ -51,6 +51,9 @@ class ModelRunner:
         self.block_size = cfg.cache.block_size
         assert self.block_size == 64, "the sparse-MLA kernels use 64-token blocks"
         self.max_blocks_per_seq = math.ceil(cfg.scheduler.max_model_len / self.block_size)
+        from .. import envs
+
+        self._check_indices = bool(envs.get("VLLM_B200_STATE_INDEX_CHECK"))
         self._alloc_caches()
         self.step_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.graphs: dict[int, tuple] = {}
@@ -67,7 +70,6 @@ class ModelRunner:
         if self.timer is not None:
             self.timer.attach(self.model)
         envs.log_gate("light timing", self.timer is not None)
-        self._check_indices = bool(envs.get("VLLM_B200_STATE_INDEX_CHECK"))
         envs.log_gate("state index check", self._check_indices)
         self.spec = None
         self._pending = None
