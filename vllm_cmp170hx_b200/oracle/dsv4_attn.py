@@ -74,12 +74,13 @@ _E2M1_THRESHOLDS = ((0.25, False), (0.75, True), (1.25, False), (1.75, True), (2
 
 
 def e2m1(v: torch.Tensor) -> torch.Tensor:
-    """Nearest E2M1 value of v (|v| <= 6), ties to the even code, as fp32."""
+    """Nearest E2M1 value of v (|v| <= 6), ties to the even code, as fp32.  The magnitude is the sum of
+    the steps between neighbouring grid values whose threshold v passes (no table tensor, so the
+    function runs inside CUDA-graph capture)."""
     a = v.float().abs()
-    code = torch.zeros_like(a, dtype=torch.int64)
-    for t, tie_up in _E2M1_THRESHOLDS:
-        code += (a >= t if tie_up else a > t).to(torch.int64)
-    mag = torch.tensor(_E2M1, dtype=torch.float32, device=v.device)[code]
+    mag = torch.zeros_like(a)
+    for (t, tie_up), lo, hi in zip(_E2M1_THRESHOLDS, _E2M1[:-1], _E2M1[1:]):
+        mag += (a >= t if tie_up else a > t).to(torch.float32) * (hi - lo)
     return torch.where(v < 0, -mag, mag)
 
 
