@@ -29,10 +29,37 @@ from dataclasses import dataclass, field
 
 @dataclass
 class KDAConfig:
+    """Linear-attention layers (layer type "kda"): Kimi delta attention (mode "kda": per-channel decay,
+    sigmoid output gate) or the gated delta net of Qwen3-Next-style models (mode "gdn": one decay per
+    head, SiLU output gate, num_k_heads query / key heads shared by num_heads // num_k_heads value heads)."""
     num_heads: int = 32
     head_dim: int = 128
     conv_kernel: int = 4
     lower_bound: float = -5.0
+    mode: str = "kda"
+    num_k_heads: int = 0  # gdn: query / key heads (0: num_heads)
+
+    def __post_init__(self):
+        if self.mode not in ("kda", "gdn"):
+            raise ValueError(f"KDAConfig.mode={self.mode!r}: 'kda' or 'gdn'")
+        nk = self.num_k_heads or self.num_heads
+        if self.num_heads % nk:
+            raise ValueError("KDAConfig: value heads must be a multiple of the query / key heads")
+
+
+@dataclass
+class GQAConfig:
+    """Gated grouped-query full attention (layer type "gqa", Qwen3-Next style): per query head
+    [q | sigmoid gate], per-head q / k RMSNorm, partial NeoX RoPE, head_dim 256."""
+    num_heads: int = 16
+    num_kv_heads: int = 2
+    head_dim: int = 256
+    rotary_dim: int = 64
+    rope_theta: float = 10000000.0
+
+    def __post_init__(self):
+        if self.head_dim != 256 or self.num_heads % self.num_kv_heads or self.rotary_dim % 2:
+            raise ValueError("GQAConfig: head_dim 256, query heads a multiple of key-value heads, even rotary dims")
 
 
 @dataclass
@@ -94,6 +121,13 @@ class MoEConfig:
     exl3_bits_x2: int = 8
     exl3_codebook: int = 2
     swiglu_limit: float = 0.0
+    # router logits precision: "float32" (the gate GEMM writes fp32 logits) or "bfloat16" (logits rounded
+    # to the model dtype before the top-k), the reference's `moe_router_dtype` switch
+    router_dtype: str = "float32"
+
+    def __post_init__(self):
+        if self.router_dtype not in ("float32", "bfloat16"):
+            raise ValueError(f"MoEConfig.router_dtype={self.router_dtype!r}: 'float32' or 'bfloat16'")
 
     @property
     def router_mode(self) -> int:
@@ -106,13 +140,24 @@ class ModelConfig:
     vocab_size: int = 163840
     hidden_size: int = 2304
     num_layers: int = 48
-    layer_types: list[str] = field(default_factory=list)  # "kda" | "mla" | "dsa" per layer
+    layer_types: list[str] = field(default_factory=list)  # "kda" | "mla" | "dsa" | "gqa" per layer
     mlp_types: list[str] = field(default_factory=list)  # "dense" | "moe" per layer
     dense_intermediate: int = 12288
     kda: KDAConfig = field(default_factory=KDAConfig)
     mla: MLAConfig = field(default_factory=MLAConfig)
     moe: MoEConfig = field(default_factory=MoEConfig)
     dsa: DSAConfig = field(default_factory=DSAConfig)
+    gqa: GQAConfig = field(default_factory=GQAConfig)
+    # per-layer n-gram embeddings (PLE) from an EXL3-coded table file: ple_heads hash heads of ple_dim
+    # channels (head h hashes the last ple_orders[h] tokens into its ple_vocab rows); the rows are
+    # projected to the hidden size and added to the token embedding.  ple_path "" draws a random table
+    # (synthetic runs).  0 heads: none.
+    ple_heads: int = 0
+    ple_dim: int = 256
+    ple_vocab: int = 4096
+    ple_bits: int = 4
+    ple_orders: list[int] = field(default_factory=list)
+    ple_path: str = ""
     rms_eps: float = 1e-5
     max_position: int = 1 << 20
     tie_embeddings: bool = False
@@ -151,7 +196,8 @@ class ModelConfig:
         mla = MLAConfig(**d.pop("mla", {}))
         moe = MoEConfig(**d.pop("moe", {}))
         dsa = DSAConfig(**d.pop("dsa", {}))
-        return ModelConfig(kda=kda, mla=mla, moe=moe, dsa=dsa, **d)
+        gqa = GQAConfig(**d.pop("gqa", {}))
+        return ModelConfig(kda=kda, mla=mla, moe=moe, dsa=dsa, gqa=gqa, **d)
 
 
 def config3() -> ModelConfig:
@@ -256,8 +302,49 @@ def tiny_dsv4(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: int =
     )
 
 
+def qwen38_flash_next() -> ModelConfig:
+    """Qwen3.8-Flash-Next-style linear / full hybrid (the reference's third served family, README.md:32-37,
+    vllm_sm80/models/qwen4_exp/): 48 layers at 3:1 gated-delta-net : gated full attention, hidden 2048,
+    linear attention 16 query / key heads and 32 value heads of 128, full attention 16 query / 2 key-value
+    heads of 256 with a 64-dim rotary part, 512 routed experts top-10 + 1 shared (intermediate 512), EXL3
+    4-bit experts, a compressed n-gram PLE table, one MTP layer."""
+    L = 48
+    return ModelConfig(
+        name="qwen-linear-full-hybrid-moe-48L-2048",
+        vocab_size=151936,
+        hidden_size=2048,
+        num_layers=L,
+        layer_types=["gqa" if i % 4 == 3 else "kda" for i in range(L)],
+        kda=KDAConfig(num_heads=32, head_dim=128, mode="gdn", num_k_heads=16),
+        gqa=GQAConfig(num_heads=16, num_kv_heads=2, head_dim=256, rotary_dim=64),
+        moe=MoEConfig(num_experts=512, top_k=10, intermediate=512, num_shared=1, shared_intermediate=512,
+                      router="softmax", expert_format="exl3", exl3_bits_x2=8, exl3_codebook=2),
+        rms_eps=1e-6,
+        ple_heads=4, ple_dim=256, ple_vocab=1 << 20, ple_orders=[2, 3, 2, 3],
+        num_mtp_layers=1,
+    )
+
+
+def tiny_qwen(layers: int = 4, experts: int = 8, hidden: int = 256, vocab: int = 512, ple: bool = True) -> ModelConfig:
+    """Small model of the Qwen3-Next-style family for tests."""
+    return ModelConfig(
+        name="tiny-qwen",
+        vocab_size=vocab,
+        hidden_size=hidden,
+        num_layers=layers,
+        layer_types=["gqa" if i % 4 == 3 else "kda" for i in range(layers)],
+        kda=KDAConfig(num_heads=4, head_dim=128, mode="gdn", num_k_heads=2),
+        gqa=GQAConfig(num_heads=4, num_kv_heads=2, head_dim=256, rotary_dim=64),
+        moe=MoEConfig(num_experts=experts, top_k=2, intermediate=128, num_shared=1, shared_intermediate=128,
+                      expert_format="exl3"),
+        max_position=4096,
+        ple_heads=2 if ple else 0, ple_dim=128, ple_vocab=1024, ple_orders=[2, 3],
+    )
+
+
 PRESETS = {"config3": config3, "config4": config4, "config2_layer": config2_layer, "tiny": tiny,
-           "tiny_deepseek": tiny_deepseek, "tiny_dsv4": tiny_dsv4}
+           "tiny_deepseek": tiny_deepseek, "tiny_dsv4": tiny_dsv4, "qwen38_flash_next": qwen38_flash_next,
+           "tiny_qwen": tiny_qwen}
 
 
 @dataclass

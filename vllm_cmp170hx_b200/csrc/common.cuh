@@ -451,6 +451,8 @@ template <>
 B200_DEVICE __half from_float<__half>(float v) { return __float2half(v); }
 
 B200_DEVICE float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// softplus with torch's default threshold (x above 20 returns x)
+B200_DEVICE float softplusf_(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 B200_DEVICE float siluf_(float x) { return x / (1.0f + __expf(-x)); }
 
 }  // namespace b200

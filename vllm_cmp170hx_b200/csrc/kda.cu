@@ -7,6 +7,9 @@
 // S <- S*e; u = (v - S k) * beta; S += u k^T; o = S q, and the gated RMSNorm
 // with sigmoid(g2)), oracle tests/kernels/test_ampere_pp_kda_prefill.py:228-248.
 //
+// The gated delta net of the Qwen3-Next-style linear-attention layers is the same recurrence with one
+// decay per head, exp(-exp(A_log) * softplus(a + dt_bias)), and a SiLU output gate (gate_mode 1).
+//
 // B200 layout: one CTA per (sequence, head), 16 warps; warp w owns value rows
 // 8w..8w+7 as two groups of four.  Lane = (row-in-group rs: 2 bits, column
 // group cg: 3 bits); a thread holds 16 key columns {32j + 4cg + i} of its row
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
         }
       }
     } else {
-      r.x = __bfloat162float(p.g_raw[(int64_t)tt * p.ld_g + hh * D + (tid - 3 * D)]);
+      r.x = __bfloat162float(p.g_raw[(int64_t)tt * p.ld_g + (p.gate_mode ? hh : hh * D + (tid - 3 * D))]);
       if (tid == 3 * D) r.beta = __bfloat162float(p.beta_raw[(int64_t)tt * p.ld_beta + hh]);
     }
     if (tid < D) {
@@ -200,9 +203,10 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
       const int cc = tid - 3 * D;  // 0..127
       float e;
       if (FULL) {
-        const float g = (first ? cur.x : __bfloat162float(p.g_raw[(int64_t)t * p.ld_g + h * D + cc])) +
-                        (p.g_bias ? p.g_bias[h * D + cc] : 0.f);
-        e = __expf(p.lower_bound * sigmoidf_(cur.a_h * g));
+        const int gi = p.gate_mode ? h : h * D + cc;
+        const float g = (first ? cur.x : __bfloat162float(p.g_raw[(int64_t)t * p.ld_g + gi])) +
+                        (p.g_bias ? p.g_bias[gi] : 0.f);
+        e = p.gate_mode ? __expf(-cur.a_h * softplusf_(g)) : __expf(p.lower_bound * sigmoidf_(cur.a_h * g));
       } else {
         e = __expf(p.g_f32[((int64_t)t * p.H + h) * D + cc]);
       }
@@ -301,7 +305,10 @@ __global__ void __launch_bounds__(kThreads, 1) kda_recurrent_kernel(KdaArgs p) {
         }
         ss = warp_sum(ss);
         float y = o * rsqrtf(ss / D + p.eps) * cur.nw;
-        if (p.g2) y *= sigmoidf_(first ? cur.g2 : __bfloat162float(p.g2[(int64_t)t * p.ld_g2 + h * D + tid]));
+        if (p.g2) {
+          const float z = first ? cur.g2 : __bfloat162float(p.g2[(int64_t)t * p.ld_g2 + h * D + tid]);
+          y *= p.gate_mode ? z * sigmoidf_(z) : sigmoidf_(z);
+        }
         p.out[(int64_t)t * p.ld_out + h * D + tid] = __float2bfloat16(y);
       } else if (p.out_f32) {
         p.out_f32[((int64_t)t * p.H + h) * D + tid] = o;

@@ -284,6 +284,10 @@ struct KdaArgs {
   const int* verify;  // [num_seqs] nullable
   float* rec;
   int skip_long;  // > 0: sequences of at least this many tokens are left to the chunked kernel
+  // 0: KDA gates (per-channel decay exp(lb * sigmoid(exp(A_log) * (g + bias))), output gate sigmoid(g2));
+  // 1: gated delta net (one decay per head exp(-exp(A_log) * softplus(a + dt_bias)) with g_raw [T, H] and
+  //    g_bias = dt_bias [H], output gate silu(g2))
+  int gate_mode;
 };
 cudaError_t kda_recurrent(const KdaArgs& a, cudaStream_t stream);
 
@@ -364,6 +368,31 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
                                cudaStream_t stream);
 // q [T, nh, dim] (dim 576: MLA latent + RoPE; 512: DeepSeek-V4.1 rows), cache rows of dim; V = the
 // first 512 dims.  sink: per-head logits added to the softmax denominator (null: none).
+// Gated grouped-query attention (gqa.cu); head_dim 256.
+struct GqaPrepArgs {
+  const __nv_bfloat16* proj;  // [T, ld_proj]: nh x [q | gate] (512 each), nkv x k (256), nkv x v (256)
+  int64_t ld_proj;
+  int nh, nkv, group;         // this rank's query heads, key-value heads, query heads per key-value head
+  const __nv_bfloat16* q_norm_w;  // [256]
+  const __nv_bfloat16* k_norm_w;  // [256]
+  float eps;
+  const int* positions;       // [T]
+  const float* cos_sin;       // [max_pos, rot_dim] fp32 (cos | sin)
+  int rot_dim;                // NeoX RoPE on the first rot_dim dims
+  const int64_t* slots;       // [T] cache position of each token (< 0: none)
+  __nv_bfloat16* q_out;       // [T * nkv, group, 512] query rows [q' | 0]
+  __nv_bfloat16* cache;       // [positions * nkv, 512] rows [k' | v]
+};
+cudaError_t gqa_prep(const GqaPrepArgs& a, int T, cudaStream_t stream);
+cudaError_t gqa_gate(const void* attn, const void* proj, int64_t ld_proj, int T, int nh, void* out, int64_t ld_out,
+                     cudaStream_t stream);
+// Dense causal attention of the query rows [Tq = T * kv_heads, group, 512] over the paged [K | V] rows
+// (mla_attn.cu's block kernel in its dense mode): out [Tq, group, 512], value half [256, 512) written.
+cudaError_t gqa_dense_attention(const void* q, int Tq, int group, const void* cache, const int* ctx_lens,
+                                const int* token_seq, const int* block_table, int64_t ld_bt, int kv_heads,
+                                float sm_scale, int splits, void* out, float* part_o, float* part_ml,
+                                uint32_t* status, cudaStream_t stream);
+
 cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const void* cache, const int* indices,
                                  const int* counts, int topk, float sm_scale, int splits, void* out, float* part_o,
                                  float* part_ml, float* lse, const float* sink, uint32_t* status,

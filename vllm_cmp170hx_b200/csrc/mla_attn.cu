@@ -211,7 +211,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 // merge split partials: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s
 __global__ void merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits, int T,
                              int nh, __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
-                             const float* __restrict__ sink) {
+                             const float* __restrict__ sink, int c_lo, int c_hi) {
   pdl_prologue();
   const int th = blockIdx.x;  // t * nh + h
   float M = -INFINITY;
@@ -225,7 +225,7 @@ __global__ void merge_kernel(const float* __restrict__ part_o, const float* __re
   // a sink adds exp(sink) to the denominator only (not to the returned log-sum-exp)
   if (sink != nullptr && M != -INFINITY) L += exp2f(sink[th % nh] * kLog2e - M);
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int c = threadIdx.x; c < 512; c += blockDim.x) {
+  for (int c = c_lo + threadIdx.x; c < c_hi; c += blockDim.x) {  // the output dims the splits computed
     float acc = 0.f;
     for (int s = 0; s < splits; ++s) {
       const float m = part_ml[((int64_t)s * T * nh + th) * 2];
@@ -297,6 +297,16 @@ struct Params {
   const float* sink;  // per-head softmax sink logit (natural-log units, already scaled), or null
   int T;
   uint32_t* status;
+  // -1: both latent halves (grid z = 2 x splits); 0 or 1: only that half of the output dims (grid z = splits)
+  int only_half;
+  // dense causal mode (grouped-query attention over paged [K | V] rows): when dense_ctx is set, query row
+  // t is (token t / kv_heads, key-value head t % kv_heads); it attends positions [0, dense_ctx[token]) of
+  // its sequence, whose rows are (block_table[seq][pos / 64] * 64 + pos % 64) * kv_heads + head
+  const int* dense_ctx;
+  const int* dense_seq;
+  const int* dense_bt;
+  int64_t dense_ld_bt;
+  int dense_kv_heads;
 };
 
 // byte offset of (row r, 16-byte chunk c) in a 128-byte-swizzled tile of 128-byte rows
@@ -347,10 +357,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int t = blockIdx.x;
   const int hg = blockIdx.y;
-  const int half = blockIdx.z & 1;
-  const int split = blockIdx.z >> 1;
+  const int half = p.only_half >= 0 ? p.only_half : (int)(blockIdx.z & 1);
+  const int split = p.only_half >= 0 ? (int)blockIdx.z : (int)(blockIdx.z >> 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int count = min(p.counts[t], p.topk);
+  const bool dense = p.dense_ctx != nullptr;
+  const int count = dense ? p.dense_ctx[t / p.dense_kv_heads] : min(p.counts[t], p.topk);
   const int nblk_all = (count + BP - 1) / BP;
   const int per = (nblk_all + p.splits - 1) / p.splits;
   const int blk0 = split * per;
@@ -423,10 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and lane l holds the cache row index of block row 4 l + gw.
     const int gw = warp - 1;
     const int sub = lane >> 3, ch = lane & 7;
-    const int* idx_g = p.indices + (int64_t)t * p.topk;
+    const int* idx_g = dense ? nullptr : p.indices + (int64_t)t * p.topk;
+    const int* bt_g = dense ? p.dense_bt + (int64_t)p.dense_seq[t / p.dense_kv_heads] * p.dense_ld_bt : nullptr;
+    const int kvh = dense ? t % p.dense_kv_heads : 0;
     auto fetch_idx = [&](int b) -> int {
       const int pos = (blk0 + b) * BP + lane * 4 + gw;
-      return pos < count ? idx_g[pos] : -1;
+      if (pos >= count) return -1;
+      return dense ? (bt_g[pos >> 6] * 64 + (pos & 63)) * p.dense_kv_heads + kvh : idx_g[pos];
     };
     int cur = nb > 0 ? fetch_idx(0) : -1;
     uint32_t ns = 0;
@@ -652,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 256; ++c) dst[c] = 0.f;
       }
     }
-    if (head < p.nh && half == 0) {
+    if (head < p.nh && half == (p.only_half >= 0 ? p.only_half : 0)) {
       if (p.splits > 1) {
         float* ml = p.part_ml + (((int64_t)split * p.T + t) * p.nh + head) * 2;
         ml[0] = nb > 0 ? m_run : -INFINITY;
@@ -701,7 +715,7 @@ cudaError_t launch_sparse_attention(const CUtensorMap& tq, const mla::attn4::Par
   using namespace mla::attn4;
   cudaError_t e = cudaFuncSetAttribute(sparse_attn_block_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid(T, (nh + 127) / 128, 2 * splits);
+  dim3 grid(T, (nh + 127) / 128, (p.only_half >= 0 ? 1 : 2) * splits);
   launch_pdl(sparse_attn_block_kernel<D>, dim3(grid), dim3(kThreads), SMEM, stream, tq, p);
   return cudaGetLastError();
 }
@@ -734,11 +748,48 @@ cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const vo
   p.sink = sink;
   p.T = T;
   p.status = status;
+  p.only_half = -1;
   cudaError_t e = dim == 512 ? launch_sparse_attention<512>(tq, p, T, nh, splits, stream)
                              : launch_sparse_attention<576>(tq, p, T, nh, splits, stream);
   if (e != cudaSuccess || splits == 1) return e;
   launch_pdl(mla::attn::merge_kernel, dim3(T * nh), dim3(128), 0, stream, part_o, part_ml, splits, T, nh,
-             reinterpret_cast<__nv_bfloat16*>(out), lse, sink);
+             reinterpret_cast<__nv_bfloat16*>(out), lse, sink, 0, 512);
+  return cudaGetLastError();
+}
+
+cudaError_t gqa_dense_attention(const void* q, int Tq, int group, const void* cache, const int* ctx_lens,
+                                const int* token_seq, const int* block_table, int64_t ld_bt, int kv_heads,
+                                float sm_scale, int splits, void* out, float* part_o, float* part_ml,
+                                uint32_t* status, cudaStream_t stream) {
+  using namespace mla::attn4;
+  if (Tq == 0) return cudaSuccess;
+  if (group < 1 || group > 128 || kv_heads < 1) return cudaErrorInvalidValue;
+  const int box_rows = (group + 7) / 8 * 8;
+  CUtensorMap tq = make_tma_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)Tq * group, 512, 512, box_rows, 64,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  Params p{};
+  p.q_box_rows = box_rows;
+  p.topk = 1 << 30;
+  p.nh = group;
+  p.cache = reinterpret_cast<const __nv_bfloat16*>(cache);
+  p.sm_scale_log2 = sm_scale * kLog2e;
+  p.splits = splits;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.part_o = part_o;
+  p.part_ml = part_ml;
+  p.T = Tq;
+  p.status = status;
+  p.only_half = 1;  // rows are [K (256) | V (256)]: the value dims are the upper half
+  p.dense_ctx = ctx_lens;
+  p.dense_seq = token_seq;
+  p.dense_bt = block_table;
+  p.dense_ld_bt = ld_bt;
+  p.dense_kv_heads = kv_heads;
+  cudaError_t e = launch_sparse_attention<512>(tq, p, Tq, group, splits, stream);
+  if (e != cudaSuccess || splits == 1) return e;
+  launch_pdl(mla::attn::merge_kernel, dim3(Tq * group), dim3(128), 0, stream, part_o, part_ml, splits, Tq, group,
+             reinterpret_cast<__nv_bfloat16*>(out), static_cast<float*>(nullptr), static_cast<const float*>(nullptr),
+             256, 512);
   return cudaGetLastError();
 }
 

@@ -33,6 +33,13 @@ void exl3_gemm_op(int64_t nmat, const at::Tensor& trellis0, const c10::optional<
 void moe_combine_op(const at::Tensor& y, const at::Tensor& slot_of, const at::Tensor& sorted_weight, int64_t k,
                     const c10::optional<at::Tensor>& add, at::Tensor& out);  // exl3.cu
 
+void gqa_prep_op(const at::Tensor& proj, int64_t nh, int64_t nkv, const at::Tensor& q_norm_w,
+                 const at::Tensor& k_norm_w, double eps, const at::Tensor& positions, const at::Tensor& cos_sin,
+                 const at::Tensor& slots, at::Tensor& q_out, at::Tensor& cache);
+void gqa_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& ctx_lens,
+                      const at::Tensor& token_seq, const at::Tensor& block_table, int64_t kv_heads, double sm_scale,
+                      int64_t splits, at::Tensor& out, const at::Tensor& status);
+void gqa_gate_op(const at::Tensor& attn, const at::Tensor& proj, int64_t nh, at::Tensor& out);
 void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
                     const c10::optional<at::Tensor>& has_init, const at::Tensor& qkv, const at::Tensor& g_raw,
                     const at::Tensor& beta_raw, const c10::optional<at::Tensor>& g2, at::Tensor& conv_state,
@@ -41,7 +48,8 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                     const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
                     at::Tensor& state, at::Tensor& out, const c10::optional<at::Tensor>& verify,
                     const c10::optional<at::Tensor>& rec, int64_t chunk_min_len,
-                    const c10::optional<at::Tensor>& chunk_scratch, const c10::optional<at::Tensor>& status);
+                    const c10::optional<at::Tensor>& chunk_scratch, const c10::optional<at::Tensor>& status,
+                    int64_t gate_mode);
 void mhc_post_pre_op(const c10::optional<at::Tensor>& x, const at::Tensor& H, const c10::optional<at::Tensor>& post,
                      const c10::optional<at::Tensor>& comb, const at::Tensor& fn, const at::Tensor& scale,
                      const at::Tensor& base, const at::Tensor& norm_w, const c10::optional<at::Tensor>& pre_mix,
@@ -168,7 +176,7 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor beta_raw, Tensor? g2, Tensor(a!) conv_state, Tensor? conv_w, Tensor? conv_b, Tensor a_log, "   \
     "Tensor? g_bias, float lower_bound, Tensor? norm_w, float eps, float l2_eps, float q_scale, "            \
     "bool l2norm, Tensor(b!) state, Tensor(c!) out, Tensor? verify=None, Tensor(d!)? rec=None, "            \
-    "int chunk_min_len=0, Tensor(e!)? chunk_scratch=None, Tensor(f!)? status=None) -> ()")                  \
+    "int chunk_min_len=0, Tensor(e!)? chunk_scratch=None, Tensor(f!)? status=None, int gate_mode=0) -> ()")                  \
   X("mhc_post_pre(Tensor? x, Tensor H, Tensor? post, Tensor? comb, Tensor fn, Tensor scale, Tensor base, "   \
     "Tensor norm_w, Tensor? pre_mix, float rms_eps, float eps, float post_mult, int iters, float norm_eps, "  \
     "int mode, Tensor(a!) H_out, Tensor(b!) y, Tensor(c!) post_out, Tensor(d!) comb_out, Tensor(e!) pre_out) -> ()") \
@@ -225,7 +233,12 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor(a!) sorted_token, Tensor(b!) sorted_weight, Tensor(c!) slot_of, Tensor(d!) items, "             \
     "Tensor(e!) num_items, Tensor(f!) expert_offsets, Tensor peers, int rank, Tensor(g!) state, "           \
     "Tensor(h!) status, float timeout_s) -> ()")                                                      \
-  X("gemm_batched(Tensor x, Tensor w, Tensor(a!) out, Tensor(b!) status) -> ()")
+  X("gemm_batched(Tensor x, Tensor w, Tensor(a!) out, Tensor(b!) status) -> ()")                       \
+  X("gqa_prep(Tensor proj, int nh, int nkv, Tensor q_norm_w, Tensor k_norm_w, float eps, Tensor positions, " \
+    "Tensor cos_sin, Tensor slots, Tensor(a!) q_out, Tensor(b!) cache) -> ()")                             \
+  X("gqa_attention(Tensor q, Tensor cache, Tensor ctx_lens, Tensor token_seq, Tensor block_table, "         \
+    "int kv_heads, float sm_scale, int splits, Tensor(a!) out, Tensor(b!) status) -> ()")                  \
+  X("gqa_gate(Tensor attn, Tensor proj, int nh, Tensor(a!) out) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -265,4 +278,7 @@ void register_host_bindings(pybind11::module_& m);
   X("sp_wait", b200::sp_wait_op)                      \
   X("gemm_sp", b200::gemm_sp_op)                      \
   X("moe_build_assignments_sp", b200::moe_build_assignments_sp_op) \
-  X("gemm_batched", b200::gemm_batched_op)
+  X("gemm_batched", b200::gemm_batched_op)            \
+  X("gqa_prep", b200::gqa_prep_op)                    \
+  X("gqa_attention", b200::gqa_attention_op)          \
+  X("gqa_gate", b200::gqa_gate_op)

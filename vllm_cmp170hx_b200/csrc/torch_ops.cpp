@@ -267,7 +267,8 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
                     const c10::optional<at::Tensor>& norm_w, double eps, double l2_eps, double q_scale, bool l2norm,
                     at::Tensor& state, at::Tensor& out, const c10::optional<at::Tensor>& verify,
                     const c10::optional<at::Tensor>& rec, int64_t chunk_min_len,
-                    const c10::optional<at::Tensor>& chunk_scratch, const c10::optional<at::Tensor>& status) {
+                    const c10::optional<at::Tensor>& chunk_scratch, const c10::optional<at::Tensor>& status,
+                    int64_t gate_mode) {
   B200_CHECK_CUDA(qkv);
   B200_CHECK_DTYPE(qkv, at::kBFloat16);
   B200_CHECK_DTYPE(state, at::kFloat);
@@ -280,7 +281,12 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
   TORCH_CHECK(conv_state.is_contiguous() && conv_state.size(1) == 3 * H * 128 && conv_state.size(2) == 3,
               "kda: conv_state [slots, 3*H*128, 3]");
   TORCH_CHECK(a_log.numel() == H, "kda: a_log [H]");
-  if (g_bias.has_value()) TORCH_CHECK(g_bias->scalar_type() == at::kFloat && g_bias->numel() == H * 128, "kda: g_bias");
+  TORCH_CHECK(gate_mode == 0 || gate_mode == 1, "kda: gate_mode 0 (KDA) or 1 (gated delta net)");
+  const int64_t gate_width = gate_mode ? H : H * 128;  // per channel (KDA) or per head (gated delta net)
+  TORCH_CHECK(g_raw.size(-1) >= gate_width, "kda: g_raw [T, H*128] (KDA) or [T, H] (gated delta net)");
+  if (g_bias.has_value())
+    TORCH_CHECK(g_bias->scalar_type() == at::kFloat && g_bias->numel() == gate_width, "kda: g_bias");
+  TORCH_CHECK(gate_mode == 0 || chunk_min_len == 0, "kda: the chunked prefill takes KDA gates only");
   c10::cuda::CUDAGuard g(qkv.device());
   KdaArgs a{};
   a.full = 1;
@@ -304,6 +310,7 @@ void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor
   a.a_log = a_log.data_ptr<float>();
   a.g_bias = g_bias.has_value() ? g_bias->data_ptr<float>() : nullptr;
   a.lower_bound = (float)lower_bound;
+  a.gate_mode = (int)gate_mode;
   a.norm_w = norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(norm_w->data_ptr()) : nullptr;
   a.eps = (float)eps;
   a.l2_eps = (float)l2_eps;
@@ -881,6 +888,99 @@ void mhc_post_pre_op(const c10::optional<at::Tensor>& x, const at::Tensor& H, co
   a.comb_out = comb_out.data_ptr<float>();
   a.pre_out = pre_out.data_ptr<float>();
   B200_LAUNCH(mhc_post_pre(a, cur_stream()));
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+// Gated grouped-query attention (gqa.cu + the dense mode of the block attention kernel).
+void gqa_prep_op(const at::Tensor& proj, int64_t nh, int64_t nkv, const at::Tensor& q_norm_w,
+                 const at::Tensor& k_norm_w, double eps, const at::Tensor& positions, const at::Tensor& cos_sin,
+                 const at::Tensor& slots, at::Tensor& q_out, at::Tensor& cache) {
+  B200_CHECK_CUDA(proj);
+  B200_CHECK_DTYPE(proj, at::kBFloat16);
+  TORCH_CHECK(proj.dim() == 2 && proj.stride(1) == 1 && proj.size(1) >= nh * 512 + nkv * 512,
+              "gqa prep: proj [T, nh*512 + nkv*512]");
+  TORCH_CHECK(nkv >= 1 && nh % nkv == 0, "gqa prep: query heads must be a multiple of key-value heads");
+  const int T = proj.size(0);
+  TORCH_CHECK(q_norm_w.scalar_type() == at::kBFloat16 && q_norm_w.numel() == 256 && q_norm_w.is_contiguous() &&
+                  k_norm_w.scalar_type() == at::kBFloat16 && k_norm_w.numel() == 256 && k_norm_w.is_contiguous(),
+              "gqa prep: q / k norm weights bf16 [256]");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() >= T, "gqa prep: positions int32 [T]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.dim() == 2,
+              "gqa prep: cos_sin fp32 [max_pos, rot_dim]");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && slots.numel() >= T, "gqa prep: slots int64 [T]");
+  TORCH_CHECK(q_out.scalar_type() == at::kBFloat16 && q_out.is_contiguous() && q_out.numel() >= (int64_t)T * nh * 512,
+              "gqa prep: q_out [T * nkv, group, 512]");
+  TORCH_CHECK(cache.scalar_type() == at::kBFloat16 && cache.is_contiguous() && cache.size(-1) == 512,
+              "gqa prep: cache rows [.., 512]");
+  c10::cuda::CUDAGuard g(proj.device());
+  GqaPrepArgs a{};
+  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
+  a.ld_proj = proj.stride(0);
+  a.nh = (int)nh;
+  a.nkv = (int)nkv;
+  a.group = (int)(nh / nkv);
+  a.q_norm_w = reinterpret_cast<const __nv_bfloat16*>(q_norm_w.data_ptr());
+  a.k_norm_w = reinterpret_cast<const __nv_bfloat16*>(k_norm_w.data_ptr());
+  a.eps = (float)eps;
+  a.positions = positions.data_ptr<int>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.rot_dim = (int)cos_sin.size(1);
+  a.slots = slots.data_ptr<int64_t>();
+  a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  a.cache = reinterpret_cast<__nv_bfloat16*>(cache.data_ptr());
+  B200_LAUNCH(gqa_prep(a, T, cur_stream()));
+}
+
+void gqa_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& ctx_lens,
+                      const at::Tensor& token_seq, const at::Tensor& block_table, int64_t kv_heads, double sm_scale,
+                      int64_t splits, at::Tensor& out, const at::Tensor& status) {
+  B200_CHECK_CUDA(q);
+  B200_CHECK_DTYPE(q, at::kBFloat16);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 512 && q.is_contiguous() && q.size(0) % kv_heads == 0,
+              "gqa attention: q [T * kv_heads, group, 512] contiguous");
+  TORCH_CHECK(cache.scalar_type() == at::kBFloat16 && cache.is_contiguous() && cache.size(-1) == 512,
+              "gqa attention: cache rows [.., 512]");
+  const int Tq = q.size(0), group = q.size(1);
+  const int T = Tq / kv_heads;
+  TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && ctx_lens.numel() >= T && token_seq.scalar_type() == at::kInt &&
+                  token_seq.numel() >= T,
+              "gqa attention: ctx_lens / token_seq int32 [T]");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2 && block_table.stride(1) == 1,
+              "gqa attention: block_table int32 [S, max_blocks]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() >= (int64_t)Tq * group * 512,
+              "gqa attention: out [T * kv_heads, group, 512]");
+  TORCH_CHECK(splits >= 1, "gqa attention: splits >= 1");
+  c10::cuda::CUDAGuard g(q.device());
+  at::Tensor part_o, part_ml;
+  if (splits > 1) {
+    part_o = at::empty({splits, Tq, group, 512}, q.options().dtype(at::kFloat));
+    part_ml = at::empty({splits, Tq, group, 2}, q.options().dtype(at::kFloat));
+  }
+  B200_LAUNCH(gqa_dense_attention(q.data_ptr(), Tq, group, cache.data_ptr(), ctx_lens.data_ptr<int>(),
+                                  token_seq.data_ptr<int>(), block_table.data_ptr<int>(), block_table.stride(0),
+                                  (int)kv_heads, (float)sm_scale, (int)splits, out.data_ptr(),
+                                  splits > 1 ? part_o.data_ptr<float>() : nullptr,
+                                  splits > 1 ? part_ml.data_ptr<float>() : nullptr, status_ptr(status), cur_stream()));
+}
+
+void gqa_gate_op(const at::Tensor& attn, const at::Tensor& proj, int64_t nh, at::Tensor& out) {
+  B200_CHECK_CUDA(attn);
+  TORCH_CHECK(attn.scalar_type() == at::kBFloat16 && attn.is_contiguous() && attn.size(-1) == 512,
+              "gqa gate: attention rows [T * nh, 512]");
+  TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.dim() == 2 && proj.stride(1) == 1 &&
+                  proj.size(1) >= nh * 512 && reinterpret_cast<uintptr_t>(proj.data_ptr()) % 16 == 0,
+              "gqa gate: proj [T, >= nh*512], 16-byte aligned");
+  const int T = proj.size(0);
+  TORCH_CHECK(attn.numel() >= (int64_t)T * nh * 512, "gqa gate: attention rows cover T * nh");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= T &&
+                  out.size(1) >= nh * 256 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "gqa gate: out [T, nh*256], 16-byte aligned");
+  c10::cuda::CUDAGuard g(attn.device());
+  B200_LAUNCH(gqa_gate(attn.data_ptr(), proj.data_ptr(), proj.stride(0), T, (int)nh, out.data_ptr(), out.stride(0),
+                       cur_stream()));
 }
 
 }  // namespace b200

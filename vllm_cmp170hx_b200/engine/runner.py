@@ -54,6 +54,9 @@ class ModelRunner:
         from .. import envs
 
         self._check_indices = bool(envs.get("VLLM_B200_STATE_INDEX_CHECK"))
+        if getattr(self.model, "ple", None) is not None:
+            sc = cfg.scheduler
+            self.model.ple.reserve(max(sc.max_num_batched_tokens, sc.max_num_seqs * (1 + sc.num_speculative_tokens)))
         self._alloc_caches()
         self.step_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.graphs: dict[int, tuple] = {}
@@ -117,8 +120,12 @@ class ModelRunner:
                 kda_bytes = len(kda_ids) * self.num_slots * (math.prod(rec_shape) * 4 + math.prod(conv_shape) * 2)
                 spec = cfg.scheduler.num_speculative_tokens > 0
                 mtp = spec and cfg.scheduler.spec_method == "mtp"
-                n_mla = len(mla_ids) + (1 if mtp else 0)  # + MTP layer
+                mtp_gqa = mtp and "mla" not in self.mcfg.layer_types and "gqa" in self.mcfg.layer_types
+                n_mla = len(mla_ids) + (1 if mtp and not mtp_gqa else 0)  # + MTP layer
                 per_block = max(1, n_mla) * 64 * (576 * 2 + 128 + 4)
+                n_gqa = len(m.gqa_layer_ids()) + (1 if mtp_gqa else 0)
+                if n_gqa:  # [k | v] rows of the local key-value heads
+                    per_block += n_gqa * 64 * m.gqa_kv_heads() * 512 * 2
                 if spec and not mtp:  # DFlash context keys / values (the drafter's default shape)
                     per_block += cfg.scheduler.dflash_layers * 64 * 2 * 4 * 128 * 2
                 n_dsa = len(m.dsa_layer_ids())
@@ -177,7 +184,7 @@ class ModelRunner:
         torch.cuda.synchronize(self.device)
         peak = torch.cuda.max_memory_allocated(self.device) - base
         del hidden, dev, ctx
-        self.mla_caches, self.kda_states, self.dsa_cores = {}, {}, {}
+        self.mla_caches, self.kda_states, self.dsa_cores, self.gqa_caches = {}, {}, {}, {}
         torch.cuda.empty_cache()
         self.activation_peak = int(peak)
         return int(peak * 1.25) + (1 << 30)
@@ -207,6 +214,10 @@ class ModelRunner:
         for i in dsa_ids:
             self.dsa_cores[i] = m.layer(i).attn.make_core(self.num_slots, rows, max_step,
                                                            sc.num_speculative_tokens, self.device)
+        self.gqa_caches = {}
+        for i in m.gqa_layer_ids():
+            self.gqa_caches[i] = torch.zeros(*m.layer(i).attn.cache_rows(rows), dtype=torch.bfloat16,
+                                             device=self.device)
         self.block_pool = make_block_pool(nb, 1)
         self.slot_pool = SlotPool(self.num_slots, 1) if (kda_ids or dsa_ids) else None
 
@@ -254,9 +265,13 @@ class ModelRunner:
         temps = np.zeros(Sp, dtype=np.float32)
         temps[:S] = np.fromiter((s.req.params.temperature for s in reqs), dtype=np.float32, count=S)
         sample_rows = np.fromiter((i for i, s in enumerate(reqs) if s.sample), dtype=np.int64)
-        return dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
-                    temps=temps, bans=self._bans_rows(reqs, Sp), sample_rows=sample_rows,
-                    max_ctx=int(a.max()) + 1 if S else 1, T=Sp, S=Sp)
+        h = dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
+                 temps=temps, bans=self._bans_rows(reqs, Sp), sample_rows=sample_rows,
+                 max_ctx=int(a.max()) + 1 if S else 1, T=Sp, S=Sp)
+        ple = self._ple_ids(((s.req, s.start, 1, 0) for s in reqs), Sp)
+        if ple is not None:
+            h["ple"] = ple
+        return h
 
     @staticmethod
     def _bans_rows(reqs, rows: int) -> np.ndarray:
@@ -267,6 +282,22 @@ class ModelRunner:
             if b:
                 bans[i, :len(b)] = b[:sampling_ops.MAX_BANS]
         return bans
+
+    def _ple_ids(self, items, rows: int) -> np.ndarray | None:
+        """n-gram embedding ids [rows, heads] of the step's tokens (models with a PLE table; None otherwise):
+        items = (request, first position, tokens, drafts among them) per scheduled sequence, in row order;
+        padding rows keep id 0."""
+        emb = getattr(self.model, "ple", None)
+        if emb is None:
+            return None
+        out = np.zeros((rows, emb.table.heads), dtype=np.int64)
+        t = 0
+        for r, a, n, nd in items:
+            w0 = max(0, a - emb.max_order + 1)
+            toks = r.tokens(w0, a + n - nd) + list(r.draft_token_ids[:nd])
+            out[t:t + n] = emb.ids_of(toks, np.arange(a - w0, a - w0 + n))
+            t += n
+        return out
 
     def _host_inputs(self, out: SchedulerOutput, pad_to: int | None = None):
         reqs = out.reqs
@@ -318,6 +349,9 @@ class ModelRunner:
         h = dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
                  temps=temps, bans=self._bans_rows(reqs, Sp), sample_rows=np.asarray(sample_rows, dtype=np.int64),
                  max_ctx=max_ctx, T=Tp, S=Sp)
+        ple = self._ple_ids(((s.req, s.start, s.num_new, s.num_draft) for s in reqs), Tp)
+        if ple is not None:
+            h["ple"] = ple
         if self._check_indices:
             from ..utils.state_check import check_step
 
@@ -340,15 +374,16 @@ class ModelRunner:
 
     def _context(self, h: dict, bufs: dict | None = None, max_ctx: int | None = None) -> tuple:
         b = bufs or {}
-        dev = {k: self._to_dev(h[k], b.get(k)) for k in ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit",
-                                                          "bt", "temps")}
+        keys = ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps") + (
+            ("ple",) if "ple" in h else ())
+        dev = {k: self._to_dev(h[k], b.get(k)) for k in keys}
         ctx = StepContext(positions=dev["pos"], num_tokens=h["T"], slot_mapping=dev["slots"], token_seq=dev["tseq"],
                           ctx_lens=dev["ctx"], block_table=dev["bt"], max_ctx=max_ctx or h["max_ctx"],
                           cu_seqlens=dev["cu"], kda_slots=dev["kslot"], has_init=dev["hinit"],
-                          dsa_cores=self.dsa_cores,
+                          dsa_cores=self.dsa_cores, gqa_caches=self.gqa_caches,
                           mla_caches=self.mla_caches, kda_states=self.kda_states,
-                          scores_buf=b.get("scores"))
-        nbytes = sum(h[k].nbytes for k in ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps"))
+                          scores_buf=b.get("scores"), ple_ids=dev.get("ple"))
+        nbytes = sum(h[k].nbytes for k in keys)
         return dev, ctx, nbytes
 
     # ------------------------------------------------------------------ forward + sample
@@ -721,6 +756,8 @@ class ModelRunner:
                  ("kslot", (B,), torch.int32), ("hinit", (B,), torch.int32),
                  ("bt", (B, self.max_blocks_per_seq), torch.int32), ("temps", (B,), torch.float32),
                  ("bans", (B, sampling_ops.MAX_BANS), torch.int32)]
+        if getattr(self.model, "ple", None) is not None:
+            specs.append(("ple", (B, self.model.ple.table.heads), torch.int64))
         bufs, host, devbuf, hviews = self._graph_buffers(specs)
         bufs["slots"].fill_(-1)
         bufs["tseq"].copy_(torch.arange(B, dtype=torch.int32))
@@ -731,7 +768,8 @@ class ModelRunner:
         ctx = StepContext(positions=bufs["pos"], num_tokens=B, slot_mapping=bufs["slots"], token_seq=bufs["tseq"],
                           ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
                           kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
-                          kda_states=self.kda_states, scores_buf=bufs["scores"], dsa_cores=self.dsa_cores)
+                          kda_states=self.kda_states, scores_buf=bufs["scores"], dsa_cores=self.dsa_cores,
+                          gqa_caches=self.gqa_caches, ple_ids=bufs.get("ple"))
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
@@ -803,7 +841,11 @@ class ModelRunner:
             kslot[i] = max(r.kda_slot, 0)
             hinit[i] = 1
             bt[i] = self._bt_row(r)
-        return dict(ids=ids, pos=pos, slots=slots, ctx=ctx, kslot=kslot, hinit=hinit, bt=bt)
+        h = dict(ids=ids, pos=pos, slots=slots, ctx=ctx, kslot=kslot, hinit=hinit, bt=bt)
+        ple = self._ple_ids(((s.req, s.start, n, k) for s in reqs), Bp * n)
+        if ple is not None:
+            h["ple"] = ple
+        return h
 
     def _capture_spec(self, Bp: int, k: int) -> None:
         dev = self.device
@@ -813,6 +855,8 @@ class ModelRunner:
         specs = [("ids", (T,), torch.int64), ("pos", (T,), torch.int32), ("slots", (T,), torch.int64),
                  ("ctx", (T,), torch.int32), ("kslot", (Bp,), torch.int32), ("hinit", (Bp,), torch.int32),
                  ("bt", (Bp, self.max_blocks_per_seq), torch.int32)]
+        if getattr(self.model, "ple", None) is not None:
+            specs.append(("ple", (T, self.model.ple.table.heads), torch.int64))
         bufs, host, devbuf, hviews = self._graph_buffers(specs)
         bufs["slots"].fill_(-1)
         bufs["ctx"].fill_(1)
@@ -824,7 +868,7 @@ class ModelRunner:
                           ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
                           kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
                           kda_states=self.kda_states, scores_buf=bufs["scores"], dsa_cores=self.dsa_cores,
-                          kda_verify=verify)
+                          gqa_caches=self.gqa_caches, ple_ids=bufs.get("ple"), kda_verify=verify)
 
         def fwd():
             hidden = self.model(bufs["ids"], ctx)

@@ -94,10 +94,14 @@ class SpecDecoder:
             from ..models.mtp import MTPHead
 
             self.mtp = MTPHead(cfg.model, runner.model, runner.device, cfg.seed, init_mode)
-            runner.mla_caches[self.mtp.layer_id] = (
-                torch.zeros(rows, 576, dtype=torch.bfloat16, device=runner.device),
-                torch.zeros(rows, 128, dtype=torch.uint8, device=runner.device),
-                torch.ones(rows, dtype=torch.float32, device=runner.device))
+            if self.mtp.kind == "gqa":
+                runner.gqa_caches[self.mtp.layer_id] = torch.zeros(
+                    *self.mtp.layer.attn.cache_rows(rows), dtype=torch.bfloat16, device=runner.device)
+            else:
+                runner.mla_caches[self.mtp.layer_id] = (
+                    torch.zeros(rows, 576, dtype=torch.bfloat16, device=runner.device),
+                    torch.zeros(rows, 128, dtype=torch.uint8, device=runner.device),
+                    torch.ones(rows, dtype=torch.float32, device=runner.device))
         else:
             raise ValueError(f"unknown speculative method {self.method!r}")
         self.depth = None
@@ -374,7 +378,8 @@ class SpecDecoder:
                            token_seq=t(ts, np.int32), ctx_lens=t(np.minimum(p + 1, cap), np.int32),
                            block_table=t(bt, np.int32), max_ctx=int(min(p.max() + 1, cap)),
                            cu_seqlens=t(cu, np.int32), kda_slots=t(np.zeros(S), np.int32),
-                           has_init=t(np.ones(S), np.int32), mla_caches=r.mla_caches, kda_states=r.kda_states)
+                           has_init=t(np.ones(S), np.int32), mla_caches=r.mla_caches, kda_states=r.kda_states,
+                           gqa_caches=r.gqa_caches)
 
     def acceptance_rate(self) -> float:
         return self.stats["accepted"] / max(1, self.stats["proposed"])

@@ -62,6 +62,10 @@ class StepContext:
     kda_records: dict = field(default_factory=dict)
     # DeepSeek-V4.1 attention layers: i -> DSv4AttnCore (caches; rings indexed by kda_slots)
     dsa_cores: dict = field(default_factory=dict)
+    # gated grouped-query attention layers: i -> paged [k | v] rows [positions * kv heads, 512] bf16
+    gqa_caches: dict = field(default_factory=dict)
+    # n-gram embedding ids of the step's tokens, int64 [T, heads] (models with a PLE table)
+    ple_ids: torch.Tensor | None = None
 
 
 def _fp8_proj(w: torch.Tensor):
@@ -551,6 +555,14 @@ class DecoderLayer(nn.Module):
             from .dsv4 import DSAAttention
 
             self.attn = DSAAttention(cfg, wi, tp, tp_rank, idx)
+        elif self.kind == "gqa":
+            from .qwen import GatedAttention
+
+            self.attn = GatedAttention(cfg, wi, tp, tp_rank)
+        elif self.kind == "kda" and cfg.kda.mode == "gdn":
+            from .qwen import GDNAttention
+
+            self.attn = GDNAttention(cfg, wi, tp, tp_rank)
         else:
             self.attn = (KDAAttention if self.kind == "kda" else MLAAttention)(cfg, wi, tp, tp_rank)
         mt = cfg.mlp_types[idx]
@@ -675,6 +687,12 @@ class HybridForCausalLM(nn.Module):
         # layers whose output the forward keeps in `aux_hidden` (set by a DFlash drafter)
         self.aux_layer_ids: tuple[int, ...] = ()
         self.aux_hidden: list[torch.Tensor] = []
+        # n-gram (PLE) embeddings added to the token embedding on the first stage
+        self.ple = None
+        if cfg.ple_heads and self.first:
+            from .qwen import NgramEmbedding
+
+            self.ple = NgramEmbedding(cfg, wi, device, seed)
         self.hc_head = None
         if cfg.hc_mult and (self.last or init_mode == "sliced"):
             # the final boundary: the last sublayer's post, then the head collapse + final norm
@@ -702,6 +720,8 @@ class HybridForCausalLM(nn.Module):
             return self._forward_sp(input_ids, ctx, sp)
         if self.first:
             x, residual = self.embed[input_ids], None
+            if self.ple is not None:
+                x = x + self.ple(ctx.ple_ids)
         else:
             x, residual = hidden_in
         aux = self.aux_layer_ids
@@ -718,7 +738,7 @@ class HybridForCausalLM(nn.Module):
     def supports_sp(self) -> bool:
         """Whether the sequence-parallel layout covers this model: one pipeline stage, no
         hyper-connections, no auxiliary hidden states (block drafter), MoE layers (or dense MLPs)."""
-        return (self.first and self.last and not self.cfg.hc_mult and not self.aux_layer_ids
+        return (self.first and self.last and not self.cfg.hc_mult and not self.aux_layer_ids and self.ple is None
                 and all(t in ("kda", "mla", "dsa") for t in self.cfg.layer_types)
                 and any(isinstance(layer.mlp, MoE) for layer in self.layers))
 
@@ -759,6 +779,15 @@ class HybridForCausalLM(nn.Module):
     def mla_layer_ids(self):
         """Sparse-MLA layers of this stage (global indices)."""
         return [i for i, t in enumerate(self.cfg.layer_types) if t == "mla" and self.layer_start <= i < self.layer_end]
+
+    def gqa_layer_ids(self):
+        """Gated grouped-query attention layers of this stage (global indices)."""
+        return [i for i, t in enumerate(self.cfg.layer_types) if t == "gqa" and self.layer_start <= i < self.layer_end]
+
+    def gqa_kv_heads(self) -> int:
+        """Key-value heads of this rank in a gated grouped-query attention layer."""
+        g, tp = self.cfg.gqa, pstate.get().tp_size
+        return g.num_kv_heads // tp if g.num_kv_heads % tp == 0 else 1
 
     def dsa_layer_ids(self):
         """DeepSeek-V4.1 attention layers of this stage (global indices)."""

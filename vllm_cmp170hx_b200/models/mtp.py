@@ -30,8 +30,11 @@ class MTPHead(nn.Module):
         # the MTP layer is an MLA layer with the model's MLP type of the last layer
         # (a plain residual inside the MTP layer even when the target widens its residual into
         # hyper-connection streams: the head consumes the target's final, collapsed hidden state)
+        # (models whose full attention is gated grouped-query attention -- the Qwen3-Next-style family --
+        # get an MTP layer of that kind instead, with its own paged [k | v] cache)
+        self.kind = "gqa" if ("gqa" in cfg.layer_types and "mla" not in cfg.layer_types) else "mla"
         mcfg = ModelConfig.from_dict({**_cfg_dict(cfg), "num_layers": cfg.num_layers + 1, "hc_mult": 0,
-                                      "layer_types": cfg.layer_types + ["mla"],
+                                      "layer_types": cfg.layer_types + [self.kind], "ple_heads": 0,
                                       "mlp_types": cfg.mlp_types + [cfg.mlp_types[-1]]})
         self.enorm = RMSNorm(wi.ones_plus(H, 0.05), cfg.rms_eps)
         self.hnorm = RMSNorm(wi.ones_plus(H, 0.05), cfg.rms_eps)

@@ -21,11 +21,16 @@ class KdaRecords:
 
 
 def kda_forward(qkv, g_raw, beta_raw, g2, cu_seqlens, state_idx, has_init, conv_state, conv_w, conv_b, a_log, g_bias,
-                lower_bound, norm_w, state, eps=1e-5, l2_eps=1e-6, out=None, verify=None, records=None):
+                lower_bound, norm_w, state, eps=1e-5, l2_eps=1e-6, out=None, verify=None, records=None, gate_mode=0):
     """Varlen batch of sequences (cu_seqlens int32 [S+1]); state [slots, H, 128, 128] fp32 and
     conv_state [slots, 3*H*128, 3] bf16 are read for sequences with has_init != 0 and
     written back -- except sequences flagged in `verify` (int32 [S]), whose state is left as it was
-    and whose updates go to `records` for :func:`kda_recover`.  Returns [T, H*128] bf16."""
+    and whose updates go to `records` for :func:`kda_recover`.  Returns [T, H*128] bf16.
+
+    gate_mode 0: KDA gates (g_raw [T, H*128], per-channel decay); 1: gated delta net (g_raw [T, H],
+    g_bias = dt_bias [H], one decay per head, SiLU output gate).  The chunked tensor-core prefill
+    takes KDA gates only (its block-local exponents need the KDA lower bound), so gated-delta-net
+    prefills run the recurrence."""
     T = qkv.shape[0]
     H = state.shape[1]
     if out is None:
@@ -35,9 +40,9 @@ def kda_forward(qkv, g_raw, beta_raw, g2, cu_seqlens, state_idx, has_init, conv_
             slots = state_idx.long()
             records.snapshot = (state[slots].clone(), conv_state[slots].clone(), verify.clone())
             records.inputs = (qkv, g_raw, beta_raw, g2, cu_seqlens, state_idx, conv_w, conv_b, a_log, g_bias,
-                              lower_bound, norm_w, eps, l2_eps)
+                              lower_bound, norm_w, eps, l2_eps, gate_mode)
         y = _ref.kda_layer(qkv, g_raw, beta_raw, g2, cu_seqlens, state, conv_state, state_idx, has_init, conv_w,
-                           conv_b, a_log, g_bias, lower_bound, norm_w, eps, l2_eps)
+                           conv_b, a_log, g_bias, lower_bound, norm_w, eps, l2_eps, gate_mode=gate_mode)
         out.copy_(y.to(out.dtype))
         return out
     rec = None
@@ -48,13 +53,13 @@ def kda_forward(qkv, g_raw, beta_raw, g2, cu_seqlens, state_idx, has_init, conv_
     min_len, scratch = 0, None
     S = cu_seqlens.numel() - 1
     # a sequence can reach CHUNK_MIN_LEN tokens only if T - (S - 1) does (decode steps never launch it)
-    if verify is None and T - (S - 1) >= CHUNK_MIN_LEN and lower_bound >= -5.8 and _chunked_enabled():
+    if verify is None and not gate_mode and T - (S - 1) >= CHUNK_MIN_LEN and lower_bound >= -5.8 and _chunked_enabled():
         # sequences of at least CHUNK_MIN_LEN tokens run in chunks of 64 on the tensor cores
         min_len = CHUNK_MIN_LEN
         scratch = _chunk_scratch(T, H, qkv.device)
     _ext.ops().kda_forward(cu_seqlens, state_idx, has_init, qkv, g_raw, beta_raw, g2, conv_state, conv_w, conv_b,
                            a_log, g_bias, lower_bound, norm_w, eps, l2_eps, 128 ** -0.5, True, state, out, verify, rec,
-                           min_len, scratch, _ext.status_word(qkv.device) if min_len else None)
+                           min_len, scratch, _ext.status_word(qkv.device) if min_len else None, gate_mode)
     if verify is not None:
         records.inputs = (qkv, cu_seqlens, state_idx)
     return out
@@ -93,7 +98,7 @@ def kda_recover(records: KdaRecords, keep: torch.Tensor, state: torch.Tensor, co
         return
     if records.snapshot is None:
         return
-    (qkv, g_raw, beta_raw, g2, cu, sidx, conv_w, conv_b, a_log, g_bias, lb, norm_w, eps, l2_eps) = records.inputs
+    (qkv, g_raw, beta_raw, g2, cu, sidx, conv_w, conv_b, a_log, g_bias, lb, norm_w, eps, l2_eps, gm) = records.inputs
     st0, cv0, verify = records.snapshot
     cu_l = cu.tolist()
     for s in range(len(cu_l) - 1):
@@ -107,4 +112,4 @@ def kda_recover(records: KdaRecords, keep: torch.Tensor, state: torch.Tensor, co
         one = torch.tensor([0, n], dtype=torch.int32)
         _ref.kda_layer(qkv[a:b], g_raw[a:b], beta_raw[a:b], None if g2 is None else g2[a:b], one, state, conv_state,
                        sidx[s:s + 1], torch.ones(1, dtype=torch.int32), conv_w, conv_b, a_log, g_bias, lb, norm_w,
-                       eps, l2_eps)
+                       eps, l2_eps, gate_mode=gm)

@@ -85,9 +85,13 @@ def conv_silu(x, w, b, state):
 
 
 def kda_layer(qkv, g_raw, beta_raw, g2, cu_seqlens, state, conv_state, state_idx, has_init, conv_w, conv_b, a_log,
-              g_bias, lower_bound, norm_w, eps=1e-5, l2_eps=1e-6, round_conv=True):
+              g_bias, lower_bound, norm_w, eps=1e-5, l2_eps=1e-6, round_conv=True, gate_mode=0):
     """Varlen GLM KDA layer core (fp32 math).  Shapes as the CUDA op
-    `kda_forward`.  Updates state / conv_state in place; returns out [T, H*D] fp32."""
+    `kda_forward`.  Updates state / conv_state in place; returns out [T, H*D] fp32.
+
+    gate_mode 1 is the gated delta net of Qwen3-Next-style linear attention: g_raw [T, H] and g_bias
+    [H] (dt_bias) give one log decay per head, -exp(A_log) * softplus(g + dt_bias), broadcast over the
+    key channels, and the output gate is silu(g2) instead of sigmoid(g2)."""
     H = state.shape[1]
     D = 128
     HD = H * D
@@ -110,8 +114,12 @@ def kda_layer(qkv, g_raw, beta_raw, g2, cu_seqlens, state, conv_state, state_idx
         q = q / torch.sqrt((q * q).sum(-1, keepdim=True) + l2_eps) * D ** -0.5
         k = k / torch.sqrt((k * k).sum(-1, keepdim=True) + l2_eps)
         a = torch.exp(a_log.float())[:, None]
-        x = g_raw[t0:t1].float().view(-1, H, D) + (g_bias.float().view(H, D) if g_bias is not None else 0)
-        g = lower_bound * torch.sigmoid(a * x)  # log decay
+        if gate_mode:
+            x = g_raw[t0:t1, :H].float() + (g_bias.float().view(H) if g_bias is not None else 0)
+            g = (-a[:, 0] * torch.nn.functional.softplus(x))[..., None].expand(-1, H, D)  # log decay per head
+        else:
+            x = g_raw[t0:t1].float().view(-1, H, D) + (g_bias.float().view(H, D) if g_bias is not None else 0)
+            g = lower_bound * torch.sigmoid(a * x)  # log decay
         beta = torch.sigmoid(beta_raw[t0:t1].float().view(-1, H))
         S0 = state[slot].float()[None] if init else None
         o, S = naive_recurrence(q[None], k[None], v[None], g[None], beta[None], S0)
@@ -120,6 +128,7 @@ def kda_layer(qkv, g_raw, beta_raw, g2, cu_seqlens, state, conv_state, state_idx
         if norm_w is not None:
             o = o * torch.rsqrt((o * o).mean(-1, keepdim=True) + eps) * norm_w.float()
             if g2 is not None:
-                o = o * torch.sigmoid(g2[t0:t1].float().view(-1, H, D))
+                z = g2[t0:t1].float().view(-1, H, D)
+                o = o * (torch.nn.functional.silu(z) if gate_mode else torch.sigmoid(z))
         out[t0:t1] = o.reshape(-1, HD)
     return out
