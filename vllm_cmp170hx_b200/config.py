@@ -158,6 +158,16 @@ class ModelConfig:
     ple_bits: int = 4
     ple_orders: list[int] = field(default_factory=list)
     ple_path: str = ""
+    # Engram n-gram memory (DeepSeek-V4.1 style): at each layer of engram_layers a gated block adds the
+    # projection of the token's retrieved rows to the attention output; rows come from one storage-backed
+    # table of engram_heads x engram_vocab rows of engram_dim e4m3 values with E8M0 block scales, head h
+    # hashing the last engram_orders[h] tokens.  engram_path "" draws a random table (synthetic runs).
+    engram_layers: list[int] = field(default_factory=list)
+    engram_heads: int = 4
+    engram_dim: int = 256
+    engram_vocab: int = 4096
+    engram_orders: list[int] = field(default_factory=list)
+    engram_path: str = ""
     rms_eps: float = 1e-5
     max_position: int = 1 << 20
     tie_embeddings: bool = False
@@ -280,9 +290,11 @@ def tiny_deepseek(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: i
     )
 
 
-def tiny_dsv4(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: int = 512) -> ModelConfig:
+def tiny_dsv4(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: int = 512,
+              engram: bool = False) -> ModelConfig:
     """Small DeepSeek-V4.1-style model: compressed sparse attention layers (window + ratio 1 / 2 /
-    window-only), sqrt-softplus routing, EXL3 experts, delayed hyper-connections."""
+    window-only), sqrt-softplus routing, EXL3 experts, delayed hyper-connections; with `engram` an
+    Engram memory block at layer 1."""
     ratios = [(1, 2, 0)[i % 3] for i in range(layers)]
     return ModelConfig(
         name="tiny-dsv4",
@@ -299,6 +311,8 @@ def tiny_dsv4(layers: int = 3, experts: int = 8, hidden: int = 256, vocab: int =
         max_position=4096,
         hc_mult=4,
         hc_delayed=True,
+        engram_layers=[1] if engram and layers > 1 else [],
+        engram_heads=2, engram_dim=256, engram_vocab=1024, engram_orders=[2, 3],
     )
 
 
@@ -400,6 +414,43 @@ class EngineConfig:
     cuda_graph_batch_sizes: list[int] = field(default_factory=lambda: [1, 2, 4, 8, 16, 32, 64, 128, 256])
 
 
+def _from_hf_qwen_next(hf: dict, c: dict) -> ModelConfig:
+    """Qwen3-Next-style config.json (`linear_num_key_heads`, `linear_num_value_heads`, `full_attention_interval`
+    or `layer_types` of 'linear_attention' / 'full_attention', `partial_rotary_factor`, `num_experts`; the
+    reference's precision switch `moe_router_dtype` and an optional PLE table)."""
+    n = int(c["num_hidden_layers"])
+    lt = c.get("layer_types")
+    if lt:
+        layer_types = ["kda" if t == "linear_attention" else "gqa" for t in lt]
+    else:
+        every = int(c.get("full_attention_interval", 4))
+        layer_types = ["gqa" if (i + 1) % every == 0 else "kda" for i in range(n)]
+    hd = int(c.get("head_dim", 256))
+    kda = KDAConfig(num_heads=int(c.get("linear_num_value_heads", 32)),
+                    head_dim=int(c.get("linear_value_head_dim", 128)),
+                    conv_kernel=int(c.get("linear_conv_kernel_dim", 4)), mode="gdn",
+                    num_k_heads=int(c.get("linear_num_key_heads", 16)))
+    gqa = GQAConfig(num_heads=int(c["num_attention_heads"]), num_kv_heads=int(c.get("num_key_value_heads", 2)),
+                    head_dim=hd, rotary_dim=int(hd * float(c.get("partial_rotary_factor", 0.25))),
+                    rope_theta=float(c.get("rope_theta", 10000000.0)))
+    moe = MoEConfig(num_experts=int(c.get("num_experts", 512)), top_k=int(c.get("num_experts_per_tok", 10)),
+                    intermediate=int(c.get("moe_intermediate_size", 512)),
+                    num_shared=1 if c.get("shared_expert_intermediate_size") else 0,
+                    shared_intermediate=int(c.get("shared_expert_intermediate_size") or 512),
+                    router="softmax", renormalize=bool(c.get("norm_topk_prob", True)),
+                    router_dtype="float32" if c.get("moe_router_dtype", "float32") == "float32" else "bfloat16")
+    ple = c.get("ple_config", {})
+    return ModelConfig(name=str(c.get("model_type", "qwen3_next")), vocab_size=int(c["vocab_size"]),
+                       hidden_size=int(c["hidden_size"]), num_layers=n, layer_types=layer_types,
+                       mlp_types=["moe"] * n, kda=kda, gqa=gqa, moe=moe, rms_eps=float(c.get("rms_norm_eps", 1e-6)),
+                       max_position=int(c.get("max_position_embeddings", 1 << 18)),
+                       tie_embeddings=bool(hf.get("tie_word_embeddings", False)),
+                       num_mtp_layers=int(c.get("num_nextn_predict_layers", c.get("mtp_num_hidden_layers", 0))),
+                       ple_heads=int(ple.get("heads", 0)), ple_dim=int(ple.get("dim", 256)),
+                       ple_vocab=int(ple.get("vocab", 4096)), ple_orders=list(ple.get("orders", [])),
+                       ple_path=str(ple.get("path", "")))
+
+
 def from_hf_config(hf: dict) -> ModelConfig:
     """ModelConfig from a Hugging Face style config.json of the supported
     families: GLM-5.x hybrid (`glm5_next[_text]`: linear_attn_config, layer_types
@@ -407,6 +458,8 @@ def from_hf_config(hf: dict) -> ModelConfig:
     tests/models/fixtures/native_checkpoint_configs/glm53_flash/config.json in the
     reference) and DeepSeek-V3.x-style sparse MLA MoE (`deepseek_v3[2]`)."""
     c = hf.get("text_config", hf)
+    if "linear_num_value_heads" in c or str(c.get("model_type", "")).startswith(("qwen3_next", "qwen4")):
+        return _from_hf_qwen_next(hf, c)
     n = int(c["num_hidden_layers"])
     lt = c.get("layer_types")
     if lt:

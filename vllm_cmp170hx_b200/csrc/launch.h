@@ -368,6 +368,10 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
                                cudaStream_t stream);
 // q [T, nh, dim] (dim 576: MLA latent + RoPE; 512: DeepSeek-V4.1 rows), cache rows of dim; V = the
 // first 512 dims.  sink: per-head logits added to the softmax denominator (null: none).
+// Engram gate (engram.cu): out[t] += sigmoid(<rmsnorm(h_t) w_h, rmsnorm(k_t) w_k> / sqrt(H)) v_t, kv = [k | v].
+cudaError_t engram_gate(const void* h, int64_t ld_h, const void* kv, int64_t ld_kv, const void* wh, const void* wk,
+                        float eps, int T, int H, void* out, int64_t ld_out, cudaStream_t stream);
+
 // Gated grouped-query attention (gqa.cu); head_dim 256.
 struct GqaPrepArgs {
   const __nv_bfloat16* proj;  // [T, ld_proj]: nh x [q | gate] (512 each), nkv x k (256), nkv x v (256)

@@ -40,6 +40,8 @@ void gqa_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Te
                       const at::Tensor& token_seq, const at::Tensor& block_table, int64_t kv_heads, double sm_scale,
                       int64_t splits, at::Tensor& out, const at::Tensor& status);
 void gqa_gate_op(const at::Tensor& attn, const at::Tensor& proj, int64_t nh, at::Tensor& out);
+void engram_gate_op(const at::Tensor& h, const at::Tensor& kv, const at::Tensor& wh, const at::Tensor& wk, double eps,
+                    at::Tensor& out);
 void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
                     const c10::optional<at::Tensor>& has_init, const at::Tensor& qkv, const at::Tensor& g_raw,
                     const at::Tensor& beta_raw, const c10::optional<at::Tensor>& g2, at::Tensor& conv_state,
@@ -238,7 +240,8 @@ void register_host_bindings(pybind11::module_& m);
     "Tensor cos_sin, Tensor slots, Tensor(a!) q_out, Tensor(b!) cache) -> ()")                             \
   X("gqa_attention(Tensor q, Tensor cache, Tensor ctx_lens, Tensor token_seq, Tensor block_table, "         \
     "int kv_heads, float sm_scale, int splits, Tensor(a!) out, Tensor(b!) status) -> ()")                  \
-  X("gqa_gate(Tensor attn, Tensor proj, int nh, Tensor(a!) out) -> ()")
+  X("gqa_gate(Tensor attn, Tensor proj, int nh, Tensor(a!) out) -> ()")                                   \
+  X("engram_gate(Tensor h, Tensor kv, Tensor wh, Tensor wk, float eps, Tensor(a!) out) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -281,4 +284,5 @@ void register_host_bindings(pybind11::module_& m);
   X("gemm_batched", b200::gemm_batched_op)            \
   X("gqa_prep", b200::gqa_prep_op)                    \
   X("gqa_attention", b200::gqa_attention_op)          \
-  X("gqa_gate", b200::gqa_gate_op)
+  X("gqa_gate", b200::gqa_gate_op)                    \
+  X("engram_gate", b200::engram_gate_op)

@@ -984,3 +984,26 @@ void gqa_gate_op(const at::Tensor& attn, const at::Tensor& proj, int64_t nh, at:
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void engram_gate_op(const at::Tensor& h, const at::Tensor& kv, const at::Tensor& wh, const at::Tensor& wk, double eps,
+                    at::Tensor& out) {
+  B200_CHECK_CUDA(h);
+  const int T = h.size(0), H = h.size(1);
+  auto rows_ok = [&](const at::Tensor& x, int64_t width) {
+    return x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(0) >= T && x.size(1) >= width &&
+           x.stride(1) == 1 && x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0;
+  };
+  TORCH_CHECK(rows_ok(h, H) && H % 8 == 0, "engram gate: h bf16 [T, H], H a multiple of 8, 16-byte rows");
+  TORCH_CHECK(rows_ok(kv, 2 * H), "engram gate: kv bf16 [T, 2H] = [k | v], 16-byte rows");
+  TORCH_CHECK(rows_ok(out, H), "engram gate: out bf16 [T, H], 16-byte rows");
+  TORCH_CHECK(wh.scalar_type() == at::kBFloat16 && wh.numel() == H && wh.is_contiguous() &&
+                  wk.scalar_type() == at::kBFloat16 && wk.numel() == H && wk.is_contiguous(),
+              "engram gate: norm weights bf16 [H]");
+  c10::cuda::CUDAGuard g(h.device());
+  B200_LAUNCH(engram_gate(h.data_ptr(), h.stride(0), kv.data_ptr(), kv.stride(0), wh.data_ptr(), wk.data_ptr(),
+                          (float)eps, T, H, out.data_ptr(), out.stride(0), cur_stream()));
+}
+
+}  // namespace b200

@@ -54,9 +54,9 @@ class ModelRunner:
         from .. import envs
 
         self._check_indices = bool(envs.get("VLLM_B200_STATE_INDEX_CHECK"))
-        if getattr(self.model, "ple", None) is not None:
+        for _name, src in self._ngram_sources():
             sc = cfg.scheduler
-            self.model.ple.reserve(max(sc.max_num_batched_tokens, sc.max_num_seqs * (1 + sc.num_speculative_tokens)))
+            src.reserve(max(sc.max_num_batched_tokens, sc.max_num_seqs * (1 + sc.num_speculative_tokens)))
         self._alloc_caches()
         self.step_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.graphs: dict[int, tuple] = {}
@@ -268,9 +268,7 @@ class ModelRunner:
         h = dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
                  temps=temps, bans=self._bans_rows(reqs, Sp), sample_rows=sample_rows,
                  max_ctx=int(a.max()) + 1 if S else 1, T=Sp, S=Sp)
-        ple = self._ple_ids(((s.req, s.start, 1, 0) for s in reqs), Sp)
-        if ple is not None:
-            h["ple"] = ple
+        self._add_ngram_ids(h, ((s.req, s.start, 1, 0) for s in reqs), Sp)
         return h
 
     @staticmethod
@@ -283,21 +281,33 @@ class ModelRunner:
                 bans[i, :len(b)] = b[:sampling_ops.MAX_BANS]
         return bans
 
-    def _ple_ids(self, items, rows: int) -> np.ndarray | None:
-        """n-gram embedding ids [rows, heads] of the step's tokens (models with a PLE table; None otherwise):
+    def _ngram_sources(self) -> list:
+        """(input name, source) of the model's n-gram tables: the PLE embedding ("ple") and the Engram
+        memory ("engram"); each source has `ids_of(tokens, positions)`, `max_order` and `heads`."""
+        out = []
+        if getattr(self.model, "ple", None) is not None:
+            out.append(("ple", self.model.ple))
+        if getattr(self.model, "engram", None) is not None:
+            out.append(("engram", self.model.engram))
+        return out
+
+    def _add_ngram_ids(self, h: dict, items, rows: int) -> None:
+        """n-gram ids [rows, heads] of the step's tokens for every n-gram table of the model, into h:
         items = (request, first position, tokens, drafts among them) per scheduled sequence, in row order;
         padding rows keep id 0."""
-        emb = getattr(self.model, "ple", None)
-        if emb is None:
-            return None
-        out = np.zeros((rows, emb.table.heads), dtype=np.int64)
-        t = 0
-        for r, a, n, nd in items:
-            w0 = max(0, a - emb.max_order + 1)
-            toks = r.tokens(w0, a + n - nd) + list(r.draft_token_ids[:nd])
-            out[t:t + n] = emb.ids_of(toks, np.arange(a - w0, a - w0 + n))
-            t += n
-        return out
+        srcs = self._ngram_sources()
+        if not srcs:
+            return
+        items = list(items)
+        for name, src in srcs:
+            out = np.zeros((rows, src.heads), dtype=np.int64)
+            t = 0
+            for r, a, n, nd in items:
+                w0 = max(0, a - src.max_order + 1)
+                toks = r.tokens(w0, a + n - nd) + list(r.draft_token_ids[:nd])
+                out[t:t + n] = src.ids_of(toks, np.arange(a - w0, a - w0 + n))
+                t += n
+            h[name] = out
 
     def _host_inputs(self, out: SchedulerOutput, pad_to: int | None = None):
         reqs = out.reqs
@@ -349,9 +359,7 @@ class ModelRunner:
         h = dict(ids=ids, pos=pos, slots=slots, tseq=tseq, ctx=ctx, cu=cu, kslot=kslot, hinit=hinit, bt=bt,
                  temps=temps, bans=self._bans_rows(reqs, Sp), sample_rows=np.asarray(sample_rows, dtype=np.int64),
                  max_ctx=max_ctx, T=Tp, S=Sp)
-        ple = self._ple_ids(((s.req, s.start, s.num_new, s.num_draft) for s in reqs), Tp)
-        if ple is not None:
-            h["ple"] = ple
+        self._add_ngram_ids(h, ((s.req, s.start, s.num_new, s.num_draft) for s in reqs), Tp)
         if self._check_indices:
             from ..utils.state_check import check_step
 
@@ -374,15 +382,16 @@ class ModelRunner:
 
     def _context(self, h: dict, bufs: dict | None = None, max_ctx: int | None = None) -> tuple:
         b = bufs or {}
-        keys = ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps") + (
-            ("ple",) if "ple" in h else ())
+        keys = ("ids", "pos", "slots", "tseq", "ctx", "cu", "kslot", "hinit", "bt", "temps") + tuple(
+            k for k in ("ple", "engram") if k in h)
         dev = {k: self._to_dev(h[k], b.get(k)) for k in keys}
         ctx = StepContext(positions=dev["pos"], num_tokens=h["T"], slot_mapping=dev["slots"], token_seq=dev["tseq"],
                           ctx_lens=dev["ctx"], block_table=dev["bt"], max_ctx=max_ctx or h["max_ctx"],
                           cu_seqlens=dev["cu"], kda_slots=dev["kslot"], has_init=dev["hinit"],
                           dsa_cores=self.dsa_cores, gqa_caches=self.gqa_caches,
                           mla_caches=self.mla_caches, kda_states=self.kda_states,
-                          scores_buf=b.get("scores"), ple_ids=dev.get("ple"))
+                          scores_buf=b.get("scores"), ple_ids=dev.get("ple"),
+                          engram_ids=dev.get("engram"))
         nbytes = sum(h[k].nbytes for k in keys)
         return dev, ctx, nbytes
 
@@ -756,8 +765,8 @@ class ModelRunner:
                  ("kslot", (B,), torch.int32), ("hinit", (B,), torch.int32),
                  ("bt", (B, self.max_blocks_per_seq), torch.int32), ("temps", (B,), torch.float32),
                  ("bans", (B, sampling_ops.MAX_BANS), torch.int32)]
-        if getattr(self.model, "ple", None) is not None:
-            specs.append(("ple", (B, self.model.ple.table.heads), torch.int64))
+        for name, src in self._ngram_sources():
+            specs.append((name, (B, src.heads), torch.int64))
         bufs, host, devbuf, hviews = self._graph_buffers(specs)
         bufs["slots"].fill_(-1)
         bufs["tseq"].copy_(torch.arange(B, dtype=torch.int32))
@@ -769,7 +778,8 @@ class ModelRunner:
                           ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
                           kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
                           kda_states=self.kda_states, scores_buf=bufs["scores"], dsa_cores=self.dsa_cores,
-                          gqa_caches=self.gqa_caches, ple_ids=bufs.get("ple"))
+                          gqa_caches=self.gqa_caches, ple_ids=bufs.get("ple"),
+                          engram_ids=bufs.get("engram"))
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
@@ -842,9 +852,7 @@ class ModelRunner:
             hinit[i] = 1
             bt[i] = self._bt_row(r)
         h = dict(ids=ids, pos=pos, slots=slots, ctx=ctx, kslot=kslot, hinit=hinit, bt=bt)
-        ple = self._ple_ids(((s.req, s.start, n, k) for s in reqs), Bp * n)
-        if ple is not None:
-            h["ple"] = ple
+        self._add_ngram_ids(h, ((s.req, s.start, n, k) for s in reqs), Bp * n)
         return h
 
     def _capture_spec(self, Bp: int, k: int) -> None:
@@ -855,8 +863,8 @@ class ModelRunner:
         specs = [("ids", (T,), torch.int64), ("pos", (T,), torch.int32), ("slots", (T,), torch.int64),
                  ("ctx", (T,), torch.int32), ("kslot", (Bp,), torch.int32), ("hinit", (Bp,), torch.int32),
                  ("bt", (Bp, self.max_blocks_per_seq), torch.int32)]
-        if getattr(self.model, "ple", None) is not None:
-            specs.append(("ple", (T, self.model.ple.table.heads), torch.int64))
+        for name, src in self._ngram_sources():
+            specs.append((name, (T, src.heads), torch.int64))
         bufs, host, devbuf, hviews = self._graph_buffers(specs)
         bufs["slots"].fill_(-1)
         bufs["ctx"].fill_(1)
@@ -868,7 +876,8 @@ class ModelRunner:
                           ctx_lens=bufs["ctx"], block_table=bufs["bt"], max_ctx=mml, cu_seqlens=bufs["cu"],
                           kda_slots=bufs["kslot"], has_init=bufs["hinit"], mla_caches=self.mla_caches,
                           kda_states=self.kda_states, scores_buf=bufs["scores"], dsa_cores=self.dsa_cores,
-                          gqa_caches=self.gqa_caches, ple_ids=bufs.get("ple"), kda_verify=verify)
+                          gqa_caches=self.gqa_caches, ple_ids=bufs.get("ple"),
+                          engram_ids=bufs.get("engram"), kda_verify=verify)
 
         def fwd():
             hidden = self.model(bufs["ids"], ctx)

@@ -66,6 +66,9 @@ class StepContext:
     gqa_caches: dict = field(default_factory=dict)
     # n-gram embedding ids of the step's tokens, int64 [T, heads] (models with a PLE table)
     ple_ids: torch.Tensor | None = None
+    # Engram memory ids of the step's tokens, int64 [T, heads], and the rows the stage looked up for them
+    engram_ids: torch.Tensor | None = None
+    engram_rows: torch.Tensor | None = None
 
 
 def _fp8_proj(w: torch.Tensor):
@@ -376,6 +379,9 @@ class MoE(nn.Module):
         hid = cfg.hidden_size
         ep = pstate.get().expert_parallel and tp > 1
         self.gate = Linear(wi.normal((mc.num_experts, hid), default_std(hid)))
+        # router logits precision (the reference's `moe_router_dtype` switch): fp32 from the GEMM, or
+        # rounded to bf16 by the GEMM's epilogue (the top-k reads them as fp32 either way)
+        self.router_out = torch.float32 if mc.router_dtype == "float32" else torch.bfloat16
         self.e_bias = None
         if mc.router != "softmax":
             self.e_bias = nn.Parameter(wi.uniform((mc.num_experts,), -0.05, 0.05), requires_grad=False)
@@ -428,7 +434,7 @@ class MoE(nn.Module):
 
     def forward(self, x: torch.Tensor, reduce: bool = False) -> torch.Tensor:
         """reduce: return the output summed over the tensor-parallel group."""
-        logits = self.gate(x, out_dtype=torch.float32)
+        logits = self.gate(x, out_dtype=self.router_out)
         ids, w = moe_ops.topk(logits, self.mc.top_k, self.mc.router_mode, self.e_bias, self.mc.routed_scaling,
                               self.mc.renormalize)
         shared = None
@@ -449,7 +455,7 @@ class MoE(nn.Module):
         the weighted sums back to the owners (summed by the next residual norm).  Returns the shared
         expert's output of the local tokens (added by that norm) or None."""
         mc = self.mc
-        logits = self.gate(h, out_dtype=torch.float32)
+        logits = self.gate(h, out_dtype=self.router_out).float()
         sp.route_dispatch(logits, h, mc.top_k, mc.router_mode, self.e_bias, mc.routed_scaling, mc.renormalize,
                           mc.num_experts // sp.world)
         # the shared expert runs while the dispatched rows travel
@@ -565,6 +571,11 @@ class DecoderLayer(nn.Module):
             self.attn = GDNAttention(cfg, wi, tp, tp_rank)
         else:
             self.attn = (KDAAttention if self.kind == "kda" else MLAAttention)(cfg, wi, tp, tp_rank)
+        self.engram = None
+        if idx in cfg.engram_layers:
+            from .engram import EngramBlock
+
+            self.engram = EngramBlock(cfg, wi)
         mt = cfg.mlp_types[idx]
         if mt == "moe":
             self.mlp = MoE(cfg, wi, tp, tp_rank)
@@ -582,6 +593,8 @@ class DecoderLayer(nn.Module):
         leaves its output pending for the next boundary's post."""
         state, h = self.hc_attn(state, self.input_norm, self.cfg)
         state.x = self.attn(h, ctx, self.idx)
+        if self.engram is not None:
+            self.engram.add_(state.x, h, ctx.engram_rows)
         if self.mlp is not None:
             # the attention output's post, then the MLP input, in one boundary op
             state, h = self.hc_mlp(state, self.post_norm, self.cfg)
@@ -635,6 +648,8 @@ class DecoderLayer(nn.Module):
         else:
             h = self.input_norm(x, residual)
         a = self.attn(h, ctx, self.idx)  # row-parallel o_proj: already summed over the TP group
+        if self.engram is not None:
+            self.engram.add_(a, h, ctx.engram_rows)
         if self.mlp is None:  # the next layer's fused norm adds the attention output
             return a, residual
         h = self.post_norm(a, residual)
@@ -693,6 +708,12 @@ class HybridForCausalLM(nn.Module):
             from .qwen import NgramEmbedding
 
             self.ple = NgramEmbedding(cfg, wi, device, seed)
+        # the Engram memory table (one lookup per step serves this stage's Engram layers)
+        self.engram = None
+        if any(self.layer_start <= i < self.layer_end for i in cfg.engram_layers):
+            from .engram import EngramMemory
+
+            self.engram = EngramMemory(cfg, device, seed)
         self.hc_head = None
         if cfg.hc_mult and (self.last or init_mode == "sliced"):
             # the final boundary: the last sublayer's post, then the head collapse + final norm
@@ -704,6 +725,8 @@ class HybridForCausalLM(nn.Module):
         """First stage: token ids; later stages: `hidden_in` = the previous stage's (hidden, residual),
         or its `HCState` with hyper-connections.  Returns the normed final hidden on the last stage,
         else what the next stage takes as `hidden_in`."""
+        if self.engram is not None:
+            ctx.engram_rows = self.engram.rows(ctx.engram_ids)
         if self.cfg.hc_mult:
             if self.first:
                 e = self.embed[input_ids]
@@ -739,6 +762,7 @@ class HybridForCausalLM(nn.Module):
         """Whether the sequence-parallel layout covers this model: one pipeline stage, no
         hyper-connections, no auxiliary hidden states (block drafter), MoE layers (or dense MLPs)."""
         return (self.first and self.last and not self.cfg.hc_mult and not self.aux_layer_ids and self.ple is None
+                and self.engram is None
                 and all(t in ("kda", "mla", "dsa") for t in self.cfg.layer_types)
                 and any(isinstance(layer.mlp, MoE) for layer in self.layers))
 

@@ -175,6 +175,7 @@ class NgramEmbedding(nn.Module):
         if len(self.orders) != cfg.ple_heads:
             raise ValueError("ple_orders needs one n-gram order per PLE head")
         self.max_order = max(self.orders)
+        self.heads = cfg.ple_heads
         self.offsets = np.asarray(self.table._offs_cpu, dtype=np.int64)
         self.vocab = np.asarray(self.table._vocab_cpu, dtype=np.int64)
         self.mult = np.asarray(self.table.layer_multipliers.tolist(), dtype=np.int64)

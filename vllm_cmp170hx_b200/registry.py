@@ -23,6 +23,10 @@ ARCHITECTURES = {
     "DeepseekV3ForCausalLM": "hybrid",
     "DeepseekV32ForCausalLM": "hybrid",
     "DeepseekV41ForCausalLM": "hybrid",
+    # Qwen3-Next-style linear / full hybrid (the reference's Qwen4Exp classes, sm80_model.py:72-121)
+    "Qwen3NextForCausalLM": "hybrid",
+    "Qwen4ExpForCausalLM": "hybrid",
+    "Qwen4ExpForConditionalGeneration": "hybrid",
 }
 
 HF_CONFIG_DEFAULTS = {
