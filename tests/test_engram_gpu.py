@@ -1,6 +1,6 @@
 """Engram memory on the GPU: the gate kernel against its fp32 definition, and the DeepSeek-V4.1-style
 model with an Engram layer in the engine (logits against the CPU oracle path, CUDA-graph decode equal to
-eager decode)."""
+eager decode with and without the Engram layer)."""
 
 import pytest
 import torch
@@ -38,7 +38,7 @@ def _cfg(device, eager=True):
                         cuda_graph_batch_sizes=[1, 2, 4])
 
 
-def test_engram_model_matches_cpu_and_graphs_match_eager():
+def test_engram_model_matches_cpu():
     pstate.set_state(pstate.ParallelState())
     prompts = [list(range(3, 3 + 90)), [5, 9, 11]]
     hs = {}
@@ -53,11 +53,35 @@ def test_engram_model_matches_cpu_and_graphs_match_eager():
         with torch.inference_mode():
             hidden = eng.runner.model(d["ids"], ctx)
             hs[dev] = eng.runner.model.compute_logits(hidden).float().cpu()
-    rel = ((hs["cuda"] - hs["cpu"]).norm() / hs["cpu"].norm()).item()
-    print(f"engram model logits rel {rel:.2e}")
-    assert rel < 5e-2, rel
-    p = SamplingParams(max_tokens=6)
-    long_prompts = [list(range(10, 10 + n)) for n in (7, 66, 130)]
-    eager = [o.output_token_ids for o in LLM(_cfg("cuda", eager=True), model).generate(long_prompts, p)]
-    graph = [o.output_token_ids for o in LLM(_cfg("cuda", eager=False), model).generate(long_prompts, p)]
+    # per-row relative error: a few rows may route a token to another expert on a near-tie of the
+    # router scores (bf16 model, different reduction orders), so the median row is what is bounded
+    row = (hs["cuda"] - hs["cpu"]).norm(dim=-1) / hs["cpu"].norm(dim=-1)
+    med = row.median().item()
+    print(f"engram model logits per-row rel: median {med:.2e}, max {row.max().item():.2e}")
+    assert med < 3e-2, med
+    # the lookup itself is exact: the same rows decode to the same bf16 values on both devices
+    ids = torch.randint(0, model.engram.heads * model.engram.vocab, (64, model.engram.heads))
+    cpu_mem = HybridForCausalLM(_cfg("cpu").model, "cpu", seed=3, init_mode="sliced").engram
+    assert torch.equal(model.engram.rows(ids.cuda()).cpu(), cpu_mem.rows(ids))
+
+
+@pytest.mark.parametrize("engram", [False, True])
+def test_dsv4_graph_decode_matches_eager(engram):
+    """Decode graphs pad the batch with tokens that carry sequence 0's index and no cache slot; they must
+    leave that sequence's compressed groups, window ring and carry rows alone (3 sequences in a graph of
+    4, the shortest inside the window)."""
+    pstate.set_state(pstate.ParallelState())
+    m = tiny_dsv4(layers=3, engram=engram)
+
+    def cfg(eager):
+        return EngineConfig(model=m, scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=512,
+                                                               max_model_len=512),
+                            cache=CacheConfig(num_blocks=32), device="cuda", enforce_eager=eager,
+                            cuda_graph_batch_sizes=[1, 2, 4])
+
+    model = HybridForCausalLM(m, "cuda", seed=3, init_mode="sliced")
+    p = SamplingParams(max_tokens=12)
+    prompts = [list(range(10, 10 + n)) for n in (7, 66, 130)]
+    eager = [o.output_token_ids for o in LLM(cfg(True), model).generate(prompts, p)]
+    graph = [o.output_token_ids for o in LLM(cfg(False), model).generate(prompts, p)]
     assert eager == graph

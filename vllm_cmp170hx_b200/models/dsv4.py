@@ -101,6 +101,9 @@ class DSAAttention(nn.Module):
         iq = self.idx_q(qr).view(T, a.index_n_heads, a.index_head_dim) if self.ratio else None
         iw = self.idx_w(x) if self.ratio else None
         ng = max(1, ctx.max_ctx // self.ratio) if self.ratio else None  # host bound: no device read
-        o = core.step(ctx.token_seq, ctx.positions, ctx.kda_slots, ctx.block_table, q, kv, ks, iq, iw, max_groups=ng)
+        # tokens without a cache slot (the padding of a CUDA-graph batch) write no group, ring or carry row
+        valid = ctx.slot_mapping >= 0 if ctx.slot_mapping is not None else None
+        o = core.step(ctx.token_seq, ctx.positions, ctx.kda_slots, ctx.block_table, q, kv, ks, iq, iw, max_groups=ng,
+                      valid=valid)
         y = self.wo_a(o.reshape(T, self.G, (self.H // self.G) * a.head_dim))
         return self.wo_b.forward_reduced(y)

@@ -103,7 +103,7 @@ class DSv4AttnCore:
         return block_table[seq.long(), (g // 64).long()].long() * 64 + g.long() % 64
 
     # ------------------------------------------------------------------ compressed groups
-    def _write_groups(self, seq, slot, pos, kv, kv_score, block_table):
+    def _write_groups(self, seq, slot, pos, kv, kv_score, block_table, valid=None):
         sp = self.spec
         if sp.ratio == 1:
             # the compressor's own bf16 row when given (kv_score), else the attention's kv row
@@ -121,8 +121,12 @@ class DSv4AttnCore:
             # the last `carry` positions of each sequence into its carry ring (distinct rows; the
             # others into the dummy slot)
             keep = pos > self._last_pos(seq, pos, slot.shape[0]) - self.carry
+            if valid is not None:
+                keep = keep & valid
             dslot = self.prev.shape[0] - 1
             self.prev[torch.where(keep, tslot, dslot), torch.where(keep, pos % self.carry, 0)] = kv_score.float()
+        if valid is not None:
+            closes = closes & valid
         g = (torch.div(pos + 1, sp.ratio, rounding_mode="floor") - 1).clamp_min(0)
         gpos = pos + 1 - sp.ratio
         rows = self._group_rows(block_table, seq, g)
@@ -143,14 +147,16 @@ class DSv4AttnCore:
              q: torch.Tensor, kv: torch.Tensor, kv_score: torch.Tensor | None = None,
              index_q: torch.Tensor | None = None, index_w: torch.Tensor | None = None,
              candidates_in: torch.Tensor | None = None, candidates_out: list | None = None,
-             max_groups: int | None = None) -> torch.Tensor:
+             max_groups: int | None = None, valid: torch.Tensor | None = None) -> torch.Tensor:
         """Tokens of this step, each sequence's tokens consecutive and in position order: seq [T]
         (row of block_table / slot), pos [T]; slot [S] ring slot of each sequence; q [T, h, 512]
         (pre-RoPE), kv [T, 512] (kv_norm(wkv(x)), pre-RoPE), kv_score [T, 1024] fp32 (ratio 2; at ratio 1 an optional bf16 [T, 512]),
         index_q [T, H_i, 128] (pre-RoPE), index_w [T, H_i] (weights_proj(x)); max_groups: a host
         bound on any token's visible groups (the indexer's score width; None reads it from the
         device).  With max_groups given the step reads no device value on the host (graph
-        capturable).  Returns the wo_a input [T, h, 512]."""
+        capturable).  valid [T] bool: tokens that write cache rows (padding tokens of a CUDA-graph batch
+        carry another sequence's index and must leave its groups, rings and carry rows alone); None: all.
+        Returns the wo_a input [T, h, 512]."""
         sp = self.spec
         T = pos.shape[0]
         if T > self.max_step:
@@ -161,7 +167,7 @@ class DSv4AttnCore:
         wrows = ref.window_kv(kv, pos, self.freqs)
         self.pool[self.S0:self.S0 + T] = wrows
         if sp.ratio:
-            self._write_groups(seq, slot, pos, kv, kv_score, block_table)
+            self._write_groups(seq, slot, pos, kv, kv_score, block_table, valid)
         # first token and position of each token's sequence within this step
         tix = torch.arange(T, device=dev)
         new = torch.ones(T, dtype=torch.bool, device=dev)
@@ -205,6 +211,8 @@ class DSv4AttnCore:
         # the last `ring` positions of each sequence into its ring (distinct ring rows; the others
         # into the dummy row)
         keep = pos > self._last_pos(seq_l, pos, slot.shape[0]) - self.ring
+        if valid is not None:
+            keep = keep & valid
         ring_rows = self.W0 + slot[seq_l].long() * self.ring + pos % self.ring
         self.pool[torch.where(keep, ring_rows, self.dummy)] = wrows
         return ref.finish_output(o, pos, self.freqs)
