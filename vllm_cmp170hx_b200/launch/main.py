@@ -13,8 +13,12 @@ resolver.py:433: defaults -> model -> layout -> variants/overlays -> --set):
 Every ``[env]`` name must be declared in vllm_cmp170hx_b200.envs (or be a
 reference alias); retired sm_80 switches are refused.  The result is
 printed as JSON (``--dry-run``) or exec'ed: ``torchrun`` when tp > 1.
-A receipt (resolved settings + sha256 of every input file) is written
-beside the command when ``--receipt PATH`` is given.
+A receipt (resolved settings + sha256 of every input file, the engine tree's
+commit and dirty state, the native extension's identity and the checkpoint's
+manifest digest) is written beside the command when ``--receipt PATH`` is
+given.  ``--require-clean`` refuses a dirty tree or a native build older than
+its sources; ``--checkpoint-manifest FILE`` refuses a checkpoint directory
+that is not complete and identical to the manifest (launch/provenance.py).
 """
 
 from __future__ import annotations
@@ -101,9 +105,35 @@ def command(cfg: dict) -> tuple[list[str], dict[str, str]]:
     return argv, env
 
 
-def receipt(cfg: dict, files: list[Path], argv: list[str], env: dict) -> dict:
+def receipt(cfg: dict, files: list[Path], argv: list[str], env: dict, checkpoint: dict | None = None) -> dict:
+    from . import provenance
+
     return {"settings": cfg, "argv": argv, "env": env,
-            "inputs": {str(f): hashlib.sha256(f.read_bytes()).hexdigest() for f in files if f.exists()}}
+            "inputs": {str(f): hashlib.sha256(f.read_bytes()).hexdigest() for f in files if f.exists()},
+            "tree": provenance.tree_state(), "native": provenance.native_identity(), "checkpoint": checkpoint}
+
+
+def check_launch(cfg: dict, require_clean: bool, manifest_path: Path | None) -> dict | None:
+    """Provenance gates before the exec: with `require_clean` a dirty tree or a stale native build is
+    refused; with a manifest the model directory must verify against it (its stamp is kept beside the
+    manifest).  Returns the checkpoint record for the receipt."""
+    from . import provenance
+
+    if require_clean:
+        t = provenance.tree_state()
+        if t["dirty"]:
+            raise LaunchError(f"the engine tree is dirty ({len(t['changed'])} changed files, e.g. {t['changed'][:3]})")
+        n = provenance.native_identity()
+        if n.get("path") is None or n.get("stale"):
+            raise LaunchError(f"the native extension is missing or older than its sources: {n}")
+    if manifest_path is None:
+        return None
+    manifest = json.loads(Path(manifest_path).read_text())
+    stamp = Path(str(manifest_path) + ".stamp.json")
+    status, problems = provenance.verify_checkpoint(Path(str(cfg["model"])), manifest, stamp)
+    if status != "verified":
+        raise LaunchError(f"checkpoint {cfg['model']} is {status}: {problems}")
+    return {"path": str(cfg["model"]), "manifest_sha256": manifest["manifest_sha256"], "status": status}
 
 
 def main(argv=None) -> None:
@@ -114,10 +144,13 @@ def main(argv=None) -> None:
     ap.add_argument("--set", action="append", default=[])
     ap.add_argument("--dry-run", action="store_true")
     ap.add_argument("--receipt", type=Path)
+    ap.add_argument("--require-clean", action="store_true", help="refuse a dirty tree or a stale native build")
+    ap.add_argument("--checkpoint-manifest", type=Path, help="verify the model directory against this manifest")
     a = ap.parse_args(argv)
     cfg, files = resolve(a.settings, a.layout, a.overlay, a.set)
     cmd, env = command(cfg)
-    rec = receipt(cfg, files, cmd, env)
+    ck = check_launch(cfg, a.require_clean, a.checkpoint_manifest)
+    rec = receipt(cfg, files, cmd, env, ck)
     if a.receipt:
         a.receipt.write_text(json.dumps(rec, indent=2, default=str))
     if a.dry_run:
