@@ -82,6 +82,16 @@ def test_kernel_capture_writes_calls(tmp_path, monkeypatch):
     assert {x["op"] for x in lines} == {"gemm", "rms_norm"} and len(lines) == 4
     rec = torch.load(d / lines[0]["file"])
     assert isinstance(rec["out"], torch.Tensor) and rec["args"]
+    # every saved call replays to its saved result (the CPU path is deterministic), also through the CLI
+    from vllm_cmp170hx_b200.utils import capture
+
+    assert all(capture.replay(str(d / x["file"])) == 0.0 for x in lines)
+    assert capture.main(["replay", str(d), "--tol", "0"]) == 0
+    # a corrupted result is reported
+    rec["out"] = rec["out"] + 1
+    torch.save(rec, d / lines[0]["file"])
+    assert capture.replay(str(d / lines[0]["file"])) > 0
+    assert capture.main(["replay", str(d), "--tol", "0"]) == 1
 
 
 def test_memory_attribution_and_kv_plan():

@@ -35,3 +35,30 @@ def test_light_timing_in_cuda_graphs(tmp_path, monkeypatch):
     summ = light_timing.summarize(path)
     assert set(summ) == {"L0", "L1", "L2", "L3"} and all(0 < v < 1e5 for v in summ.values())
     envs.reset_cache()
+
+
+def test_captured_gpu_calls_replay_on_the_oracle(tmp_path, monkeypatch):
+    """Kernel calls saved from an eager GPU step replay on the CPU oracle within bf16 tolerance."""
+    from vllm_cmp170hx_b200.utils import capture
+
+    pstate.set_state(pstate.ParallelState())
+    envs.reset_cache()
+    spec = tmp_path / "cap.toml"
+    spec.write_text(f'dir = "{tmp_path / "caps"}"\nops = ["gemm", "rms_norm"]\nmax_calls = 3\n')
+    monkeypatch.setenv("VLLM_B200_CAPTURE", str(spec))
+    cfg = EngineConfig(model=tiny(layers=4, experts=8), scheduler=SchedulerConfig(max_num_seqs=4, max_model_len=512),
+                       cache=CacheConfig(num_blocks=32), device="cuda", enforce_eager=True)
+    eng = LLMEngine(cfg)
+    try:
+        eng.add_request(list(range(5, 60)), SamplingParams(max_tokens=2))
+        while eng.has_unfinished():
+            eng.step()
+    finally:
+        eng.capture.uninstall()
+        envs.reset_cache()
+    d = tmp_path / "caps" / "rank0"
+    lines = [json.loads(x) for x in (d / "index.jsonl").read_text().splitlines()]
+    assert {x["op"] for x in lines} == {"gemm", "rms_norm"}
+    for x in lines:
+        rel = capture.replay(str(d / x["file"]), "cpu")
+        assert rel < 2e-2, (x, rel)

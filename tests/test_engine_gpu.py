@@ -96,3 +96,27 @@ def test_kv_pool_sized_from_a_profiled_step():
     assert r.num_blocks == cfg.scheduler.max_num_seqs * r.max_blocks_per_seq + 1
     outs = llm.generate([list(range(10, 10 + n)) for n in (7, 130)], SamplingParams(max_tokens=4))
     assert all(len(o.output_token_ids) == 4 for o in outs)
+
+
+def test_shared_expert_stream_matches_inline(monkeypatch):
+    """With the shared expert on a second stream (fork / join, also inside the decode graphs) the engine
+    emits the tokens of the inline order; graph capture reports kept and transient bytes."""
+    from vllm_cmp170hx_b200 import envs
+
+    pstate.set_state(pstate.ParallelState())
+    model = HybridForCausalLM(_cfg("cuda").model, "cuda", seed=6, init_mode="local")
+    prompts = [list(range(20, 20 + n)) for n in (5, 70, 129)]
+    p = SamplingParams(max_tokens=5)
+    base = [o.output_token_ids for o in LLM(_cfg("cuda", eager=False), model).generate(prompts, p)]
+    envs.reset_cache()
+    monkeypatch.setenv("VLLM_B200_SHARED_EXPERT_STREAM", "1")
+    try:
+        for eager in (True, False):
+            llm = LLM(_cfg("cuda", eager=eager), model)
+            assert [o.output_token_ids for o in llm.generate(prompts, p)] == base
+        eng = LLMEngine(_cfg("cuda", eager=False), model)
+        kept = eng.warmup()
+        assert set(kept) == {1, 2, 4} and all(v >= 0 for v in kept.values())
+        assert set(eng.runner.graph_transient) == {1, 2, 4}
+    finally:
+        envs.reset_cache()

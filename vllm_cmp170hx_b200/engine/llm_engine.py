@@ -118,8 +118,11 @@ class LLMEngine:
         self.runner.warmup()
         kept = self.runner.capture_graphs() if capture_graphs else {}
         if kept:
+            tr = self.runner.graph_transient
             logging.getLogger("vllm_cmp170hx_b200").info(
-                "CUDA graphs captured: %s", ", ".join(f"batch {b}: {v / 2**20:.1f} MiB" for b, v in kept.items()))
+                "CUDA graphs captured: %s", ", ".join(f"batch {b}: {v / 2**20:.1f} MiB kept, "
+                                                      f"{tr.get(b, 0) / 2**20:.1f} MiB transient"
+                                                      for b, v in kept.items()))
         return kept
 
     def profile(self, steps: int, out_dir: str) -> str:

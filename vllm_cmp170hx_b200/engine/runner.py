@@ -946,6 +946,7 @@ class ModelRunner:
         measures the same quantity to split its graph-memory budget
         (vllm_sm80/worker/cudagraph_mem.py:202-284)."""
         kept = {}
+        self.graph_transient = {}
         if self.device.type != "cuda" or self.cfg.enforce_eager or self.st.pp_size > 1 or not self.graphs_ok:
             return kept
         for B in sorted(self.cfg.cuda_graph_batch_sizes):
@@ -953,10 +954,18 @@ class ModelRunner:
                 continue
             torch.cuda.synchronize(self.device)
             before = torch.cuda.memory_reserved(self.device)
+            torch.cuda.reset_peak_memory_stats(self.device)
             self._capture(B)
             torch.cuda.synchronize(self.device)
             kept[B] = torch.cuda.memory_reserved(self.device) - before
+            # transient: what the capture (its eager warm-up runs included) allocated at its peak and freed
+            # again -- needed free while capturing, not kept afterwards (the reference splits the same two,
+            # vllm_sm80/worker/cudagraph_mem.py:202-284)
+            self.graph_transient[B] = max(0, torch.cuda.max_memory_allocated(self.device)
+                                          - torch.cuda.memory_allocated(self.device))
         return kept
+
+    graph_transient: dict = {}
 
     @torch.inference_mode()
     def warmup(self) -> None:

@@ -61,6 +61,8 @@ _declare("VLLM_B200_EXL3_DECODERS", int, 0, "decoder warps of the EXL3 GEMM, 8 o
 _declare("VLLM_B200_KDA_PREFILL", str, "chunked", "KDA prefill: 'chunked' (sequences of >= 64 tokens in chunks of 64 "
          "on the tensor cores, read by ops/kda.py) or 'recurrent' (token by token)")
 _declare("VLLM_B200_SPARSE_MLA_SPLITS", int, 0, "position splits of the sparse-MLA attention (0 = auto)")
+_declare("VLLM_B200_SHARED_EXPERT_STREAM", _bool, False, "MoE layers run the shared expert on a second CUDA stream "
+         "beside the routed experts' assignment and rotation, joined before the combine (read by models/hybrid.py)")
 _declare("VLLM_B200_MLA_DP", _bool, True, "with expert parallelism, sparse-MLA layers hold all heads and attend "
          "data-parallel (each rank its own tokens) in the sequence-parallel layout")
 # --- scheduling ---------------------------------------------------------------------------------

@@ -432,13 +432,37 @@ class MoE(nn.Module):
             ex = ex.select(first, count)
         return ex
 
+    _aux_streams: dict = {}
+
+    def _aux_stream(self, dev) -> torch.cuda.Stream:
+        s = MoE._aux_streams.get(dev)
+        if s is None:
+            s = MoE._aux_streams[dev] = torch.cuda.Stream(dev)
+        return s
+
     def forward(self, x: torch.Tensor, reduce: bool = False) -> torch.Tensor:
         """reduce: return the output summed over the tensor-parallel group."""
         logits = self.gate(x, out_dtype=self.router_out)
         ids, w = moe_ops.topk(logits, self.mc.top_k, self.mc.router_mode, self.e_bias, self.mc.routed_scaling,
                               self.mc.renormalize)
         shared = None
-        if self.shared is not None and not (self.shared_replicated and reduce and pstate.get().tp_rank != 0):
+        need_shared = self.shared is not None and not (self.shared_replicated and reduce and pstate.get().tp_rank != 0)
+        if need_shared and x.is_cuda and isinstance(self.experts, moe_ops.Exl3Experts) and _shared_stream_on():
+            # the shared expert on a second stream while this one builds the assignments, rotates the
+            # inputs and runs the routed experts; joined before the combine adds it (the reference's
+            # shared-expert aux-stream reorder, vllm_sm80/layers/moe/shared_experts.py:67).  Works under
+            # CUDA-graph capture (fork / join of the capturing stream).
+            cur = torch.cuda.current_stream(x.device)
+            aux = self._aux_stream(x.device)
+            aux.wait_stream(cur)
+            with torch.cuda.stream(aux):
+                shared = self.shared(x)
+            x.record_stream(aux)
+            y, slot_of, sw = moe_ops.exl3_moe_rows(x, ids, w, self.experts)
+            cur.wait_stream(aux)
+            shared.record_stream(cur)
+            return moe_ops.exl3_combine(y, slot_of, sw, ids.shape[1], shared, x.shape[0], x.shape[1], reduce)
+        if need_shared:
             shared = self.shared(x)
         if isinstance(self.experts, moe_ops.Exl3Experts):
             return moe_ops.exl3_moe(x, ids, w, self.experts, add=shared, reduce=reduce)
@@ -479,6 +503,12 @@ class MoE(nn.Module):
 
 
 # ============================================================================ model
+def _shared_stream_on() -> bool:
+    from .. import envs
+
+    return bool(envs.get("VLLM_B200_SHARED_EXPERT_STREAM"))
+
+
 class HyperConnection(nn.Module):
     """Coefficient parameters of one mHC boundary: fn [2n + n^2, n d], scale [3], base [2n + n^2]
     (fp32, replicated over tensor-parallel ranks)."""

@@ -128,11 +128,18 @@ def exl3_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, ex: Exl3
             return comm.tp_all_reduce(y.to(x.dtype))
         return y if out_f32 else y.to(x.dtype)
     y, slot_of, sorted_weight = exl3_moe_rows(x, ids, weights, ex)
+    return exl3_combine(y, slot_of, sorted_weight, k, add, T, H, reduce, out_f32)
+
+
+def exl3_combine(y, slot_of, sorted_weight, k: int, add, T: int, H: int, reduce: bool = False,
+                 out_f32: bool = False) -> torch.Tensor:
+    """The top-k weighted combine of `exl3_moe_rows`' expert outputs (+ add), fused with the all-reduce
+    when `reduce`."""
     if reduce:
         from ..parallel import comm
 
         return comm.combine_all_reduce(y, slot_of, sorted_weight, k, add, T, H)
-    out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16, device=x.device)
+    out = torch.empty(T, H, dtype=torch.float32 if out_f32 else torch.bfloat16, device=y.device)
     _ext.ops().moe_combine(y, slot_of, sorted_weight, k, add, out)
     return out
 
