@@ -136,6 +136,8 @@ def main():
                                                         "instead of the sequence-parallel layout")
     ap.add_argument("--profile", action="store_true", help="print rank 0's per-kernel times of one eager step")
     ap.add_argument("--eager", action="store_true", help="no CUDA graphs (debugging)")
+    ap.add_argument("--sync-scheduling", action="store_true", help="read every step's tokens back before "
+                    "scheduling the next (default: decode steps are scheduled and launched one step ahead)")
     ap.add_argument("--ep", action="store_true", help="(default for N > 1) routed experts split whole over the "
                                                       "ranks (EP=N)")
     ap.add_argument("--moe-tp", action="store_true", help="config 3 at N > 1: split every routed expert by "
@@ -217,7 +219,8 @@ def main():
                                                expert_parallel=args.ep, sequence_parallel=not args.no_sp),
                        scheduler=SchedulerConfig(max_num_seqs=args.batch, max_num_batched_tokens=args.prefill_chunk,
                                                  max_model_len=total_len, max_num_partial_prefills=args.batch,
-                                                 num_speculative_tokens=spec_k, spec_method="mtp"),
+                                                 num_speculative_tokens=spec_k, spec_method="mtp",
+                                                 async_scheduling=not args.sync_scheduling),
                        cache=CacheConfig(num_blocks=blocks),
                        seed=args.seed, device="cuda", enforce_eager=args.eager,
                        cuda_graph_batch_sizes=[args.batch])
@@ -254,10 +257,12 @@ def main():
         engine.step()
     torch.cuda.synchronize()
     t_prefill = time.time() - t1
+    # device timing on from the warm-up on: with asynchronous scheduling the first timed call finishes the
+    # step the last warm-up call launched
+    engine.runner.time_device = True
+    launches = count_own_kernels(engine, args.steps, table=args.profile and st.rank == 0)
     for _ in range(args.warmup):
         engine.step()
-    launches = count_own_kernels(engine, args.steps, table=args.profile and st.rank == 0)
-    engine.runner.time_device = True
     clk = sample_clocks_start(dev.index or 0) if st.rank == 0 else None
     if world > 1:
         dist.barrier()
@@ -267,10 +272,16 @@ def main():
     reqs = list(engine.requests.values())
     emitted0 = sum(len(r.output_token_ids) for r in reqs)
     t_start = time.perf_counter()
+    sync_each = engine.cfg.scheduler.async_scheduling is False
     for _ in range(args.steps):
         a = time.perf_counter()
         engine.step()
-        torch.cuda.synchronize()
+        if sync_each:
+            torch.cuda.synchronize()
+        # asynchronous scheduling: one call launches step n + 1 and returns step n's tokens, so the
+        # interval between returns is the per-token time; the synchronize before the loop has finished
+        # the step in flight from the warm-up, the one after it the step the last call launched, so the
+        # region holds exactly `steps` steps of device work and emits `steps` tokens per request
         e2e_ms.append((time.perf_counter() - a) * 1e3)
         s = engine.runner.last_stats
         dev_ms.append(s.device_ms)

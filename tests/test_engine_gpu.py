@@ -120,3 +120,31 @@ def test_shared_expert_stream_matches_inline(monkeypatch):
         assert set(eng.runner.graph_transient) == {1, 2, 4}
     finally:
         envs.reset_cache()
+
+
+def test_async_scheduling_matches_sync():
+    """Decode steps scheduled and launched one step ahead (input ids gathered on the device from the
+    previous graph's sampled tokens) emit the synchronous tokens, also when a stop token ends a request
+    while the next step is in flight and when requests arrive mid-run."""
+    pstate.set_state(pstate.ParallelState())
+    model = HybridForCausalLM(_cfg("cuda").model, "cuda", seed=8, init_mode="local")
+
+    def run(async_on, stop=None):
+        cfg = _cfg("cuda", eager=False)
+        cfg.scheduler.async_scheduling = async_on
+        eng = LLMEngine(cfg, model)
+        outs = {}
+        plan = {0: [("a", list(range(10, 50)), 12), ("b", list(range(60, 75)), 9)], 4: [("c", [3, 4, 5], 7)]}
+        for step in range(100):
+            for rid, prompt, n in plan.get(step, []):
+                eng.add_request(prompt, SamplingParams(max_tokens=n, stop_token_ids=[stop] if stop else []), rid)
+            for o in eng.step():
+                outs[o.request_id] = (o.output_token_ids, o.finish_reason)
+            if step > 4 and not eng.has_unfinished():
+                break
+        return outs
+
+    sync = run(False)
+    assert run(True) == sync
+    stop = sync["a"][0][5]
+    assert run(True, stop) == run(False, stop)

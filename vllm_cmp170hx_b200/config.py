@@ -392,6 +392,9 @@ class SchedulerConfig:
     dflash_layers: int = 1  # DFlash drafter depth
     depth_policy: str = ""  # per-request verify depth policy file (dspark-depth-policy/1); "" off
     pp_spread_decodes: bool = True  # pipeline micro-batches take equal shares of the decodes
+    # asynchronous scheduling of decode steps: the next step is scheduled and launched (its input tokens
+    # gathered on the device from the step in flight) before that step's tokens are read back
+    async_scheduling: bool = False
 
 
 @dataclass

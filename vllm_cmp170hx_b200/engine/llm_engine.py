@@ -27,6 +27,10 @@ from .runner import ModelRunner
 from .scheduler import Scheduler
 
 
+# an output slot whose token is still on the device (asynchronous scheduling)
+_PLACEHOLDER = -1
+
+
 @dataclass
 class RequestOutput:
     request_id: str
@@ -168,11 +172,122 @@ class LLMEngine:
 
     def abort_request(self, request_id: str) -> None:
         self.scheduler.abort(request_id)
+        self.requests.pop(request_id, None)
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_work()
+        return self.scheduler.has_work() or self._inflight is not None
+
+    _inflight = None  # asynchronous scheduling: (scheduler output, runner handle) of the step in flight
+
+    def _async_on(self) -> bool:
+        r = self.runner
+        return (self.cfg.scheduler.async_scheduling and r.st.pp_size == 1 and r.spec is None
+                and self.adaptive_k is None and not r._ngram_sources())
 
     def step(self) -> list[RequestOutput]:
+        if self._inflight is not None or self._async_on():
+            return self._step_async()
+        return self._step_sync()
+
+    # ------------------------------------------------------------------ asynchronous scheduling
+    def _step_async(self) -> list[RequestOutput]:
+        """Decode steps overlap the host: step N+1 is scheduled (its requests' step-N tokens taken as
+        placeholders) and launched -- its input ids gathered on the device from step N's sampled tokens --
+        before step N's tokens are read back and applied.  A request whose step-N token stops it has one
+        extra position computed in step N+1, which is discarded.  Steps that need the host to know every
+        token (admissions, prefill chunks, preemption victims coming back) run synchronously after the
+        step in flight is drained (the reference's async scheduler, vllm_sm80/sched/scheduler.py:439-444,
+        over upstream's placeholder scheduling)."""
+        sch, r = self.scheduler, self.runner
+        if self._inflight is None:
+            out = sch.schedule()
+            if not out.reqs:
+                return []
+            if not (self._async_on() and r.can_launch(out)):
+                return self._execute_sync(out)
+            self._inflight = (out, r.launch(out))
+            self.num_steps += 1
+            return []
+        out_n, h_n = self._inflight
+        self._inflight = None
+        nxt = self._schedule_ahead(out_n) if (self._async_on() and not sch.waiting) else None
+        h_next = r.launch(nxt, prev=(out_n, h_n)) if nxt is not None else None
+        res = self._finalize(out_n, h_n)
+        if h_next is not None:
+            self._inflight = (nxt, h_next)
+            self.num_steps += 1
+        return res
+
+    def _schedule_ahead(self, out_n):
+        """Schedule the step after `out_n` (in flight) with its tokens as placeholders; None when that
+        step could not be one launchable decode step."""
+        sch, r = self.scheduler, self.runner
+        live = [s for s in out_n.reqs if not s.req.status.finished]
+        if not live or len(sch.running) > max(self.cfg.cuda_graph_batch_sizes) or any(
+                s.num_new != 1 or not s.sample for s in live):
+            return None
+        for s in live:
+            req = s.req
+            req.output_token_ids.append(_PLACEHOLDER)
+            req.num_computed_tokens = s.start + 1
+            req.async_hold = (len(req.output_token_ids) >= req.params.max_tokens
+                              or req.num_tokens >= self.cfg.scheduler.max_model_len)
+        nxt = sch.schedule(admit=False)
+        if not nxt.reqs or not r.can_launch(nxt):
+            # nothing to run ahead: those requests are scheduled again after the drain, which fills their
+            # placeholders (blocks grown for them stay theirs)
+            return None
+        return nxt
+
+    def _finalize(self, out_n, h_n) -> list[RequestOutput]:
+        """Read back a launched step's tokens, put them in place of the placeholders (or append them),
+        check stops and retire finished requests; returns that step's outputs."""
+        from .failed_inputs import FAILED_TOKEN
+
+        sch = self.scheduler
+        sampled = self.runner.finish(out_n, h_n)
+        now = time.monotonic()
+        done, res = [], []
+        for s in out_n.reqs:
+            req = s.req
+            if req.status.finished:
+                continue  # stopped by its previous token: this step's position is discarded
+            toks = sampled.get(req.request_id, [])
+            i = s.start + 1 - req.num_prompt_tokens  # output index of this step's token
+            ahead = i < len(req.output_token_ids) and req.output_token_ids[i] == _PLACEHOLDER
+            req.async_hold = False
+            if not toks or FAILED_TOKEN in toks:
+                if ahead:
+                    del req.output_token_ids[i:]
+                req.status = Status.FINISHED_ERROR
+                done.append(req)
+            else:
+                if ahead:
+                    req.output_token_ids[i] = int(toks[0])
+                else:
+                    req.num_computed_tokens = s.start + 1
+                    req.output_token_ids.append(int(toks[0]))
+                if req.first_token_time is None:
+                    req.first_token_time = now
+                req.token_times.append(now)
+                if req.check_stop():
+                    done.append(req)
+            res.append(RequestOutput(req.request_id, req.prompt_token_ids, list(req.output_token_ids),
+                                     req.status.finished,
+                                     req.status.value.replace("finished_", "") if req.status.finished else None,
+                                     [] if req.status == Status.FINISHED_ERROR else [req.output_token_ids[-1]]))
+        for req in done:
+            if req in sch.running:
+                sch.running.remove(req)
+            elif req in sch.waiting:  # preempted while scheduling ahead
+                sch.waiting.remove(req)
+            sch._release(req)
+            sch.finished.append(req)
+            self.requests.pop(req.request_id, None)
+        return res
+
+    # ------------------------------------------------------------------ synchronous steps
+    def _step_sync(self) -> list[RequestOutput]:
         if self.adaptive_k is not None:
             spec = self.runner.spec
             if spec is not None:
@@ -185,6 +300,9 @@ class LLMEngine:
         out = self.scheduler.schedule()
         if not out.reqs:
             return []
+        return self._execute_sync(out)
+
+    def _execute_sync(self, out) -> list[RequestOutput]:
         before = {s.req.request_id: len(s.req.output_token_ids) for s in out.reqs}
         sampled = self.runner.execute(out)
         self.scheduler.update(out, sampled)

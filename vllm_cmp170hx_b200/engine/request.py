@@ -66,6 +66,9 @@ class Request:
     block_hashes: list[int] = field(default_factory=list)
     num_cached_blocks: int = 0
     num_prefix_hit_tokens: int = 0
+    # asynchronous scheduling: the request ends with the step in flight whatever its token (length
+    # limit), so the step scheduled ahead leaves it out
+    async_hold: bool = False
 
     def __post_init__(self):
         if not self.request_id:

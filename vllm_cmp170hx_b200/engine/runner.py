@@ -412,6 +412,18 @@ class ModelRunner:
         return idx.long()
 
     @torch.inference_mode()
+    def _graph_step(self, out: SchedulerOutput) -> bool:
+        return (not self.cfg.enforce_eager and self.graphs_ok and self.device.type == "cuda" and out.decode_only
+                and all(s.num_draft == 0 for s in out.reqs)
+                and len(out.reqs) <= max(self.cfg.cuda_graph_batch_sizes))
+
+    def can_launch(self, out: SchedulerOutput) -> bool:
+        """Whether `out` is a decode step that `launch` can queue without the host knowing its input
+        tokens (one pipeline stage, no speculative decoding, no n-gram tables hashed on the host)."""
+        return (bool(out.reqs) and self.st.pp_size == 1 and self.spec is None and out.decode_only
+                and all(s.num_draft == 0 for s in out.reqs) and not self._ngram_sources()
+                and len(out.reqs) <= max(self.cfg.cuda_graph_batch_sizes))
+
     def execute(self, out: SchedulerOutput) -> dict[str, list[int]]:
         if not out.reqs:
             return {}
@@ -419,43 +431,100 @@ class ModelRunner:
             return self._execute_pp(out)
         if self.spec is not None:
             return self._execute_spec(out)
-        use_graph = (not self.cfg.enforce_eager and self.graphs_ok and self.device.type == "cuda" and out.decode_only
-                     and all(s.num_draft == 0 for s in out.reqs)
-                     and len(out.reqs) <= max(self.cfg.cuda_graph_batch_sizes))
-        stats = StepStats(num_tokens=out.num_tokens, graph=use_graph)
-        if use_graph:
-            B = next(b for b in sorted(self.cfg.cuda_graph_batch_sizes) if b >= len(out.reqs))
-            if B not in self.graphs:
-                self._capture(B)
-            g, bufs, ids_out = self.graphs[B]
-            h = self._host_inputs(out, pad_to=B)
-            nbytes = self._stage_graph_inputs(B, h)
-            ev = self._ev_start()
-            g.replay()
-            self._ev_end(ev)
-            tokens = ids_out[: len(out.reqs)]
-        else:
-            h = self._host_inputs(out)
-            dev, ctx, nbytes = self._context(h)
-            rows = self._to_dev(h["sample_rows"])
-            temps_rows = self._sample_temps(out, h)
-            bans = self._sample_bans(out)
-            ev = self._ev_start()
-            tokens = self._forward_sample(dev["ids"], ctx, rows, temps_rows, self.cfg.seed, bans)
-            self._ev_end(ev)
+        if self._graph_step(out):
+            return self.finish(out, self.launch(out))
+        stats = StepStats(num_tokens=out.num_tokens, graph=False)
+        h = self._host_inputs(out)
+        dev, ctx, nbytes = self._context(h)
+        rows = self._to_dev(h["sample_rows"])
+        temps_rows = self._sample_temps(out, h)
+        bans = self._sample_bans(out)
+        ev = self._ev_start()
+        tokens = self._forward_sample(dev["ids"], ctx, rows, temps_rows, self.cfg.seed, bans)
+        self._ev_end(ev)
+        return self.finish(out, self._readback(tokens, stats, nbytes))
+
+    def launch(self, out: SchedulerOutput, prev: tuple | None = None) -> dict:
+        """Queue one decode step as a graph replay and the read-back of its tokens; returns the handle
+        `finish` completes.  prev = (the previous step's output, its handle): tokens the host does not
+        know yet (the previous step's, still in flight) are taken on the device from that step's sampled
+        tokens, request by request, before the replay (asynchronous scheduling).  Without graphs the step
+        runs eagerly the same way."""
+        if not self._graph_step(out):
+            return self._launch_eager(out, prev)
+        B = next(b for b in sorted(self.cfg.cuda_graph_batch_sizes) if b >= len(out.reqs))
+        if B not in self.graphs:
+            self._capture(B)
+        g, bufs, ids_out = self.graphs[B]
+        h = self._host_inputs(out, pad_to=B)
+        nbytes = self._stage_graph_inputs(B, h)
+        if prev is not None:
+            # the previous step's sampled tokens (that graph's output buffer, read before this replay
+            # overwrites it) gathered into this step's input ids
+            src_h = self._gather_rows(out, prev[0], B)
+            nbytes += src_h.nbytes
+            torch.index_select(prev[1]["tokens_dev"].to(bufs["ids"].dtype), 0, self._to_dev(src_h), out=bufs["ids"])
+        ev = self._ev_start()
+        g.replay()
+        self._ev_end(ev)
+        tokens = ids_out[: len(out.reqs)]
+        stats = StepStats(num_tokens=out.num_tokens, graph=True)
+        return self._readback(tokens, stats, nbytes, keep_dev=ids_out[:B])
+
+    @staticmethod
+    def _gather_rows(out: SchedulerOutput, prev_out: SchedulerOutput, rows: int) -> np.ndarray:
+        """Row of each of `out`'s requests in `prev_out` (0 for padding rows)."""
+        row_of = {s.req.request_id: i for i, s in enumerate(prev_out.reqs)}
+        src = np.zeros(rows, dtype=np.int64)
+        src[:len(out.reqs)] = [row_of.get(s.req.request_id, 0) for s in out.reqs]
+        return src
+
+    def _launch_eager(self, out: SchedulerOutput, prev: tuple | None) -> dict:
+        h = self._host_inputs(out)
+        dev, ctx, nbytes = self._context(h)
+        if prev is not None:
+            src = self._to_dev(self._gather_rows(out, prev[0], dev["ids"].shape[0]))
+            torch.index_select(prev[1]["tokens_dev"].to(dev["ids"].dtype), 0, src, out=dev["ids"])
+        rows = self._to_dev(h["sample_rows"])
+        ev = self._ev_start()
+        tokens = self._forward_sample(dev["ids"], ctx, rows, self._sample_temps(out, h), self.cfg.seed,
+                                      self._sample_bans(out))
+        self._ev_end(ev)
+        return self._readback(tokens, StepStats(num_tokens=out.num_tokens, graph=False), nbytes, keep_dev=tokens)
+
+    def _readback(self, tokens: torch.Tensor, stats: "StepStats", nbytes: int, keep_dev=None) -> dict:
+        """Queue the step's device-to-host token copy (and the status word's) without waiting."""
         self.step_counter += 1
+        hnd = {"stats": stats, "nbytes": nbytes, "out_bytes": tokens.numel() * tokens.element_size(),
+               "tokens_dev": keep_dev}
         if self.device.type == "cuda":
             # the status word rides on the tokens' read-back: copied first, valid once they arrive
-            self._status_h.copy_(_ext.status_word(self.device), non_blocking=True)
-        host = tokens.to("cpu", non_blocking=False).tolist()
-        if self._events is not None:
-            stats.device_ms = self._events[0].elapsed_time(self._events[1])
+            status = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            status.copy_(_ext.status_word(self.device), non_blocking=True)
+            host = torch.empty(tokens.shape, dtype=tokens.dtype, pin_memory=True)
+            host.copy_(tokens, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record()
+            hnd.update(status=status, host=host, done=done, events=self._events)
             self._events = None
-        stats.h2d_bytes = nbytes
-        stats.d2h_bytes = tokens.numel() * tokens.element_size()
+        else:
+            hnd.update(host=tokens, events=None)
+        return hnd
+
+    def finish(self, out: SchedulerOutput, hnd: dict) -> dict[str, list[int]]:
+        """Wait for a launched step's tokens and return them per request."""
+        if "done" in hnd:
+            hnd["done"].synchronize()
+        host = hnd["host"].tolist()
+        stats = hnd["stats"]
+        if hnd.get("events") is not None:
+            a, b = hnd["events"]
+            stats.device_ms = a.elapsed_time(b)
+        stats.h2d_bytes = hnd["nbytes"]
+        stats.d2h_bytes = hnd["out_bytes"]
         self.last_stats = stats
         if self.device.type == "cuda":
-            _ext.raise_status(self.device, int(self._status_h[0]))
+            _ext.raise_status(self.device, int(hnd["status"][0]))
         return self._split_tokens(out, sanitize(host, self.mcfg.vocab_size))
 
     _events = None

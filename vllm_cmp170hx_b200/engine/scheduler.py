@@ -194,7 +194,9 @@ class Scheduler:
             per = max(1, total // n)
         return total, per
 
-    def schedule(self) -> SchedulerOutput:
+    def schedule(self, admit: bool = True) -> SchedulerOutput:
+        """One step's work.  admit=False schedules only running requests (asynchronous scheduling ahead
+        of a step in flight, whose tokens are not known on the host yet)."""
         out = SchedulerOutput()
         budget = self.cfg.max_num_batched_tokens
         partial = 0
@@ -204,6 +206,9 @@ class Scheduler:
         i = 0
         while i < len(self.running):
             req = self.running[i]
+            if req.async_hold:
+                i += 1
+                continue
             remaining = req.num_tokens - req.num_computed_tokens
             if remaining > 1 or (req.num_computed_tokens == 0):
                 # still in prefill (the last prompt token is computed together with sampling)
@@ -243,7 +248,7 @@ class Scheduler:
             budget -= n
             i += 1
         # admit waiting requests
-        while self.waiting and budget > 0 and len(self.running) < self.cfg.max_num_seqs:
+        while admit and self.waiting and budget > 0 and len(self.running) < self.cfg.max_num_seqs:
             req = self.waiting[0]
             if (partial >= self.cfg.max_num_partial_prefills and req.num_tokens > budget
                     and req.num_prompt_tokens > self.short_bypass):
