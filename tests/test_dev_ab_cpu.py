@@ -33,3 +33,37 @@ def test_switch_flip_and_hot_swap():
     finally:
         hs.swap_out()
     assert got == ref
+
+
+@pytest.mark.parametrize("name", ["async_scheduling", "shared_expert_stream", "kda_prefill", "exl3_tile_rows",
+                                  "gemm_splitk", "prefix_caching", "fair_prefill", "router_dtype"])
+def test_every_switch_flips_between_steps(name, monkeypatch):
+    """Generation flips the switch every step; both arms leave greedy outputs as they are (the switches
+    whose arms change numerics are checked to reach their knob instead)."""
+    from vllm_cmp170hx_b200 import envs
+    from vllm_cmp170hx_b200.dev.ab import SWITCHES
+
+    pstate.set_state(pstate.ParallelState())
+    m = HybridForCausalLM(_cfg().model, "cpu", seed=4)
+    prompts = [list(range(3, 30)), list(range(40, 52))]
+    ref = [o.output_token_ids for o in LLM(_cfg(), m).generate(prompts, SamplingParams(max_tokens=5))]
+    for var in ("VLLM_B200_SHARED_EXPERT_STREAM", "VLLM_B200_KDA_PREFILL", "VLLM_B200_EXL3_TILE_ROWS",
+                "VLLM_B200_GEMM_SPLITK"):
+        monkeypatch.delenv(var, raising=False)  # restored after the test (the switch arms set them)
+    llm = LLM(_cfg(), m)
+    eng = llm.engine
+    ab = DevAB(eng, name)
+    for rid, p in zip("ab", prompts):
+        eng.add_request(p, SamplingParams(max_tokens=5), rid)
+    outs, flips = {}, 0
+    while eng.has_unfinished():
+        for o in eng.step():
+            outs[o.request_id] = o.output_token_ids
+        ab.flip()
+        flips += 1
+    envs.reset_cache()
+    assert flips >= 5 and SWITCHES[name].doc
+    if name == "router_dtype":
+        assert all(layer.router_out is not None for layer in m.modules() if hasattr(layer, "router_out"))
+    else:
+        assert [outs["a"], outs["b"]] == ref
