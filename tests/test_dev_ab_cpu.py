@@ -37,19 +37,34 @@ def test_switch_flip_and_hot_swap():
 
 @pytest.mark.parametrize("name", ["async_scheduling", "shared_expert_stream", "kda_prefill", "exl3_tile_rows",
                                   "gemm_splitk", "prefix_caching", "fair_prefill", "router_dtype"])
-def test_every_switch_flips_between_steps(name, monkeypatch):
+def test_every_switch_flips_between_steps(name):
     """Generation flips the switch every step; both arms leave greedy outputs as they are (the switches
     whose arms change numerics are checked to reach their knob instead)."""
     from vllm_cmp170hx_b200 import envs
-    from vllm_cmp170hx_b200.dev.ab import SWITCHES
 
     pstate.set_state(pstate.ParallelState())
     m = HybridForCausalLM(_cfg().model, "cpu", seed=4)
     prompts = [list(range(3, 30)), list(range(40, 52))]
     ref = [o.output_token_ids for o in LLM(_cfg(), m).generate(prompts, SamplingParams(max_tokens=5))]
-    for var in ("VLLM_B200_SHARED_EXPERT_STREAM", "VLLM_B200_KDA_PREFILL", "VLLM_B200_EXL3_TILE_ROWS",
-                "VLLM_B200_GEMM_SPLITK"):
-        monkeypatch.delenv(var, raising=False)  # restored after the test (the switch arms set them)
+    import os
+
+    names = ("VLLM_B200_SHARED_EXPERT_STREAM", "VLLM_B200_KDA_PREFILL", "VLLM_B200_EXL3_TILE_ROWS",
+             "VLLM_B200_GEMM_SPLITK")
+    saved = {v: os.environ.get(v) for v in names}  # the switch arms set them; put them back afterwards
+    try:
+        _flip_run(name, m, prompts, ref)
+    finally:
+        for v, val in saved.items():
+            if val is None:
+                os.environ.pop(v, None)
+            else:
+                os.environ[v] = val
+        envs.reset_cache()
+
+
+def _flip_run(name, m, prompts, ref):
+    from vllm_cmp170hx_b200.dev.ab import SWITCHES
+
     llm = LLM(_cfg(), m)
     eng = llm.engine
     ab = DevAB(eng, name)
@@ -61,7 +76,6 @@ def test_every_switch_flips_between_steps(name, monkeypatch):
             outs[o.request_id] = o.output_token_ids
         ab.flip()
         flips += 1
-    envs.reset_cache()
     assert flips >= 5 and SWITCHES[name].doc
     if name == "router_dtype":
         assert all(layer.router_out is not None for layer in m.modules() if hasattr(layer, "router_out"))
