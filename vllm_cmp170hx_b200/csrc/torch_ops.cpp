@@ -1,5 +1,6 @@
 // Torch glue of the `_C` extension: argument checks, stream/device guards and
 // scratch allocation around the plain launchers of launch.h.
+#include <ATen/MemoryOverlap.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -35,6 +36,8 @@ void gemm_bf16_out(const at::Tensor& x, const at::Tensor& w, const c10::optional
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "gemm_bf16: inner dims must be contiguous");
   TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == w.size(0), "gemm_bf16: bad out shape");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat, "gemm_bf16: out bf16 or fp32");
+  at::assert_no_partial_overlap(out, x);  // the output must not alias an operand
+  at::assert_no_partial_overlap(out, w);
   if (bias.has_value()) {
     B200_CHECK_DTYPE(*bias, at::kBFloat16);
     TORCH_CHECK(bias->numel() == w.size(0) && bias->is_contiguous(), "gemm_bf16: bad bias");
@@ -953,6 +956,8 @@ void gqa_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Te
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() >= (int64_t)Tq * group * 512,
               "gqa attention: out [T * kv_heads, group, 512]");
   TORCH_CHECK(splits >= 1, "gqa attention: splits >= 1");
+  at::assert_no_partial_overlap(out, q);
+  at::assert_no_partial_overlap(out, cache);
   c10::cuda::CUDAGuard g(q.device());
   at::Tensor part_o, part_ml;
   if (splits > 1) {
@@ -978,6 +983,8 @@ void gqa_gate_op(const at::Tensor& attn, const at::Tensor& proj, int64_t nh, at:
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= T &&
                   out.size(1) >= nh * 256 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
               "gqa gate: out [T, nh*256], 16-byte aligned");
+  at::assert_no_partial_overlap(out, attn);
+  at::assert_no_partial_overlap(out, proj);
   c10::cuda::CUDAGuard g(attn.device());
   B200_LAUNCH(gqa_gate(attn.data_ptr(), proj.data_ptr(), proj.stride(0), T, (int)nh, out.data_ptr(), out.stride(0),
                        cur_stream()));
@@ -1001,6 +1008,8 @@ void engram_gate_op(const at::Tensor& h, const at::Tensor& kv, const at::Tensor&
   TORCH_CHECK(wh.scalar_type() == at::kBFloat16 && wh.numel() == H && wh.is_contiguous() &&
                   wk.scalar_type() == at::kBFloat16 && wk.numel() == H && wk.is_contiguous(),
               "engram gate: norm weights bf16 [H]");
+  at::assert_no_partial_overlap(out, h);
+  at::assert_no_partial_overlap(out, kv);
   c10::cuda::CUDAGuard g(h.device());
   B200_LAUNCH(engram_gate(h.data_ptr(), h.stride(0), kv.data_ptr(), kv.stride(0), wh.data_ptr(), wk.data_ptr(),
                           (float)eps, T, H, out.data_ptr(), out.stride(0), cur_stream()));
