@@ -103,3 +103,61 @@ def test_tp2_load_matches_tp1(kind, tmp_path):
     mp.start_processes(_worker, args=(2, port, str(tmp_path), kind, out), nprocs=2, join=True, start_method="spawn")
     with open(out) as f:
         assert json.load(f) == ref
+
+
+def _fresh(cfg, seed):
+    from vllm_cmp170hx_b200.models.hybrid import HybridForCausalLM
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    return HybridForCausalLM(cfg, "cpu", seed=seed, init_mode="sliced")
+
+
+@pytest.mark.parametrize("which", ["qwen", "dsv4_engram"])
+def test_roundtrip_new_families_strict(which):
+    """The Qwen-style family (gated delta net under linear_attn with rows grouped per key head, gated
+    attention, shared_expert, PLE projection) and the Engram layers export under upstream names and load
+    back exactly, with every tensor consumed (strict inventory)."""
+    from vllm_cmp170hx_b200.config import tiny_dsv4, tiny_qwen
+    from vllm_cmp170hx_b200.hf_loader import export_hf, load_hf
+
+    cfg = tiny_qwen(layers=4) if which == "qwen" else tiny_dsv4(layers=3, engram=True)
+    a = _fresh(cfg, 1)
+    tensors = export_hf(a)
+    if which == "qwen":  # the upstream name of the singular shared expert
+        tensors = {k.replace("shared_experts.", "shared_expert."): v for k, v in tensors.items()}
+    b = _fresh(cfg, 2)
+    inv = load_hf(b, tensors, strict=True)
+    assert inv["unused"] == [] and inv["consumed"] == len(tensors)
+    for (n, x), (_, y) in zip(a.named_parameters(), b.named_parameters()):
+        assert torch.equal(x, y), n
+
+
+def test_unused_tensor_is_refused_and_hybrid_exl3_projection_decodes():
+    from vllm_cmp170hx_b200.config import tiny_qwen
+    from vllm_cmp170hx_b200.formats import exl3 as fx
+    from vllm_cmp170hx_b200.hf_loader import UnusedTensors, export_hf, load_hf
+
+    cfg = tiny_qwen(layers=4, ple=False)
+    a = _fresh(cfg, 1)
+    t = export_hf(a)
+    with pytest.raises(UnusedTensors):
+        load_hf(_fresh(cfg, 2), {**t, "model.layers.0.mystery.weight": torch.zeros(2)}, strict=True)
+    # hybrid checkpoint: layer 0's out projection stored as an EXL3 matrix, selected by a module rule
+    name = "model.layers.0.linear_attn.out_proj"
+    w = t.pop(name + ".weight")
+    m = fx.random_matrix(w.shape[1], w.shape[0], generator=torch.Generator().manual_seed(3))
+    for part in ("trellis", "suh", "svh"):
+        t[f"{name}.{part}"] = getattr(m, part)
+    rules = {"rules": [{"match": r"^model\.layers\.0\.linear_attn\.out_proj$", "method": "exl3"}],
+             "default": "unquantized"}
+    b = _fresh(cfg, 2)
+    inv = load_hf(b, t, strict=True, quantization_config={"module_quantization": rules, "codebook": "mul1"})
+    assert inv["unused"] == []
+    x = torch.randn(3, w.shape[1])
+    got = x @ b.layer(0).attn.o_proj.weight.float().t()
+    ref = fx.linear(x, m)
+    assert ((got - ref).norm() / ref.norm()).item() < 1e-2
+    # a module no rule covers, without a default, is refused
+    with pytest.raises(ValueError, match="no module_quantization rule"):
+        load_hf(_fresh(cfg, 2), t, quantization_config={"module_quantization": {"rules": rules["rules"]}})

@@ -16,6 +16,26 @@ Names follow the upstream model families the engine serves:
 * ``model.embed_tokens.weight``, ``model.norm.weight``, ``lm_head.weight``,
   ``model.layers.{i}.{input,post_attention}_layernorm.weight``.
 
+* Qwen3-Next-style layers: gated delta net under ``linear_attn.`` (``in_proj_qkvz`` grouped per key
+  head as [q | k | v of its value heads | z of its value heads], ``in_proj_ba`` grouped the same way
+  as [b | a], ``conv1d.weight`` over [q | k | v] channels, ``A_log``, ``dt_bias``, ``norm.weight``,
+  ``out_proj``); gated attention under ``self_attn.`` (``q_proj`` per head [q | gate], ``k_proj``,
+  ``v_proj``, ``q_norm``, ``k_norm``, ``o_proj``); ``mlp.shared_expert.*``;
+* Engram layers: ``model.layers.{i}.engram.{kv, h_norm, k_norm}``; the n-gram embedding
+  ``model.ple_proj.weight`` (the tables themselves are separate files).
+
+Hybrid checkpoints (the reference's EXL3 + another method per module, vllm_sm80/kernels/exl3/hybrid.py:85):
+``quantization_config.module_quantization = {"rules": [{"match": REGEX, "method": M}, ...], "default": M}``
+gives each projection's method by the first rule whose regex searches its name: ``"exl3"`` (the module is
+stored as ``{trellis, suh, svh}``) or ``"unquantized"`` / ``"fp8"`` (``weight`` [+ ``weight_scale_inv``]).
+Routed experts load in the model's expert format; any other EXL3-stored projection is decoded at load
+into the model's float weight (W = diag(suh) H W_trellis H diag(svh), exactly the EXL3 linear).  A module
+no rule names is refused when there is no default.
+
+Every load records which checkpoint tensors it consumed; ``load_hf(..., strict=True)`` refuses a
+checkpoint with tensors nothing read (``LoadInventory``), so a misnamed or extra tensor cannot be
+silently ignored.
+
 Tensor-parallel cuts match the model's own (heads of q/k/v/b/conv/A_log/dt_bias, rows of q_b and
 the per-head kv_b, columns of o_proj, intermediate columns of the experts in whole 128-column
 blocks for EXL3, the vocab rows of lm_head); expert parallel keeps this rank's whole experts.  The
@@ -39,6 +59,64 @@ from .parallel import state as pstate
 
 class MissingTensor(KeyError):
     pass
+
+
+class UnusedTensors(ValueError):
+    pass
+
+
+# tensors a checkpoint may carry that no module of the engine reads (derived buffers, drafter heads the
+# config does not enable)
+_IGNORED = (".rotary_emb.inv_freq", "mlp.shared_expert_gate.weight", "mtp.", "model.mtp")
+
+
+class _Tracked(Mapping):
+    """A tensor mapping that records the names read from it (the load inventory)."""
+
+    def __init__(self, base: Mapping, rules=None, codebook: int = 2):
+        self.base, self.used = base, set()
+        self.rules, self.codebook = rules, codebook
+
+    def __getitem__(self, k):
+        self.used.add(k)
+        return self.base[k]
+
+    def __contains__(self, k):
+        return k in self.base
+
+    def __iter__(self):
+        return iter(self.base)
+
+    def __len__(self):
+        return len(self.base)
+
+    def unused(self) -> list[str]:
+        return sorted(k for k in self.base if k not in self.used and not any(i in k for i in _IGNORED))
+
+
+def module_method(rules: dict | None, name: str) -> str | None:
+    """The method a hybrid checkpoint's rules give module `name` (first regex match, else the default);
+    None without rules.  Raises for a module no rule covers when there is no default."""
+    import re
+
+    if not rules:
+        return None
+    for r in rules.get("rules", []):
+        if re.search(r["match"], name):
+            return r["method"]
+    if "default" in rules:
+        return rules["default"]
+    raise ValueError(f"hybrid checkpoint: no module_quantization rule matches {name} and there is no default")
+
+
+def _exl3_dense(t: Mapping, name: str, codebook: int) -> torch.Tensor:
+    """The dense [out, in] fp32 weight of an EXL3-stored projection: the EXL3 linear applied to the
+    identity (diag(suh) H W H diag(svh), logical sizes from the stored vectors)."""
+    tr, suh, svh = _get(t, name + ".trellis"), _get(t, name + ".suh"), _get(t, name + ".svh")
+    bits_x2 = tr.shape[2] // 8
+    m = fx.Exl3Matrix(tr, suh, svh, bits_x2, codebook, suh.shape[0], svh.shape[0])
+    W = fx.decode_weight(tr, bits_x2, codebook).float()
+    return fx.linear(torch.eye(suh.shape[0]), m, W).t().contiguous()
 
 
 def open_dir(path: str, readahead: bool = False) -> Mapping[str, torch.Tensor]:
@@ -88,7 +166,12 @@ def _get(t: Mapping, name: str) -> torch.Tensor:
 
 
 def _dense(t: Mapping, name: str) -> torch.Tensor:
-    """A projection's weight as float: bf16 as stored, fp8 dequantised with its block scales."""
+    """A projection's weight as float: bf16 as stored, fp8 dequantised with its block scales, an EXL3-stored
+    module (hybrid checkpoints) decoded."""
+    rules = getattr(t, "rules", None)
+    method = module_method(rules, name) if rules else None
+    if method == "exl3" or (method is None and name + ".weight" not in t and name + ".trellis" in t):
+        return _exl3_dense(t, name, getattr(t, "codebook", 2))
     w = _get(t, name + ".weight")
     if w.dtype == torch.float8_e4m3fn:
         return f8.dequantize(w, _get(t, name + ".weight_scale_inv").float())
@@ -138,6 +221,64 @@ def _load_kda(a, t, p, tp, r):
     _set(a.g_bias, _rows(_get(t, p + "dt_bias").float().reshape(H * D), tp, r))
     _set(a.norm_w, _get(t, p + "o_norm.weight"))
     _set_linear(a.o_proj, _cols(_dense(t, p + "o_proj"), tp, r))
+
+
+def _gdn_groups(cfg_kda, Hv_local, tp, r):
+    """For this rank's value heads: (key head, index in its group) of each, and the group size."""
+    Hv = cfg_kda.num_heads
+    Hk = cfg_kda.num_k_heads or Hv
+    rep = Hv // Hk
+    heads = list(range(r * Hv_local, (r + 1) * Hv_local))
+    return [(j // rep, j % rep) for j in heads], rep, Hk
+
+
+def _load_gdn(a, t, p, tp, r, cfg):
+    """Gated delta net from Qwen3-Next names (rows grouped per key head)."""
+    D = a.D
+    grp, rep, Hk = _gdn_groups(cfg.kda, a.H, tp, r)
+    qkvz = _dense(t, p + "in_proj_qkvz").view(Hk, 2 * D + 2 * rep * D, -1)
+    ba = _dense(t, p + "in_proj_ba").view(Hk, 2 * rep, -1)
+    q = torch.cat([qkvz[h, :D] for h, _ in grp])
+    k = torch.cat([qkvz[h, D:2 * D] for h, _ in grp])
+    v = torch.cat([qkvz[h, 2 * D + i * D:2 * D + (i + 1) * D] for h, i in grp])
+    z = torch.cat([qkvz[h, 2 * D + rep * D + i * D:2 * D + rep * D + (i + 1) * D] for h, i in grp])
+    b = torch.stack([ba[h, i] for h, i in grp])
+    av = torch.stack([ba[h, rep + i] for h, i in grp])
+    w = torch.cat([q, k, v, z, b, av], 0)
+    pad = a.in_proj.weight.shape[0] - w.shape[0]
+    _set_linear(a.in_proj, torch.cat([w, w.new_zeros(pad, w.shape[1])], 0))
+    conv = _get(t, p + "conv1d.weight").float().reshape(-1, 4)
+    cq = torch.cat([conv[h * D:(h + 1) * D] for h, _ in grp])
+    ck = torch.cat([conv[Hk * D + h * D:Hk * D + (h + 1) * D] for h, _ in grp])
+    cv = torch.cat([conv[2 * Hk * D + (h * rep + i) * D:2 * Hk * D + (h * rep + i + 1) * D] for h, i in grp])
+    _set(a.conv_w, torch.cat([cq, ck, cv], 0))
+    _set(a.a_log, _rows(_get(t, p + "A_log").float(), tp, r))
+    _set(a.dt_bias, _rows(_get(t, p + "dt_bias").float(), tp, r))
+    _set(a.norm_w, _get(t, p + "norm.weight"))
+    _set_linear(a.o_proj, _cols(_dense(t, p + "out_proj"), tp, r))
+
+
+def _load_gqa(a, t, p, tp, r, cfg):
+    """Gated attention from Qwen3-Next names; key-value heads cut or replicated as the model keeps them."""
+    g = cfg.gqa
+    hd = g.head_dim
+    qg = _rows(_dense(t, p + "q_proj"), tp, r)
+    if g.num_kv_heads % tp == 0:
+        kv0 = r * (g.num_kv_heads // tp)
+    else:
+        kv0 = r // (tp // g.num_kv_heads)
+    k = _dense(t, p + "k_proj")[kv0 * hd:(kv0 + a.nkv) * hd]
+    v = _dense(t, p + "v_proj")[kv0 * hd:(kv0 + a.nkv) * hd]
+    _set_linear(a.in_proj, torch.cat([qg, k, v], 0))
+    _set(a.q_norm_w, _get(t, p + "q_norm.weight"))
+    _set(a.k_norm_w, _get(t, p + "k_norm.weight"))
+    _set_linear(a.o_proj, _cols(_dense(t, p + "o_proj"), tp, r))
+
+
+def _load_engram(e, t, p):
+    _set_linear(e.kv, _dense(t, p + "kv"))
+    _set(e.h_norm_w, _get(t, p + "h_norm.weight"))
+    _set(e.k_norm_w, _get(t, p + "k_norm.weight"))
 
 
 def _load_mla(a, t, p, tp, r):
@@ -242,7 +383,9 @@ def _load_moe(moe, t, p, tp, r):
         raise NotImplementedError("Marlin-packed experts load from this package's own checkpoints")
     if moe.shared is not None:
         rep = getattr(moe, "shared_replicated", False)  # expert parallel: the whole shared expert on every rank
-        _load_dense_mlp(moe.shared, t, p + "shared_experts.", 1 if rep else tp, 0 if rep else r)
+        sp = p + ("shared_expert." if p + "shared_expert.gate_proj.weight" in t
+                  or p + "shared_expert.gate_proj.trellis" in t else "shared_experts.")
+        _load_dense_mlp(moe.shared, t, sp, 1 if rep else tp, 0 if rep else r)
 
 
 def _cut_exl3(m: "fx.Exl3Matrix", which: str, tp: int, r: int) -> "fx.Exl3Matrix":
@@ -258,10 +401,18 @@ def _cut_exl3(m: "fx.Exl3Matrix", which: str, tp: int, r: int) -> "fx.Exl3Matrix
                          m.svh[r * n:(r + 1) * n].contiguous(), m.bits_x2, m.codebook, m.in_features, n)
 
 
-def load_hf(model, tensors: Mapping[str, torch.Tensor] | str) -> None:
+def load_hf(model, tensors: Mapping[str, torch.Tensor] | str, strict: bool = False,
+            quantization_config: dict | None = None) -> dict:
     """Fill a built HybridForCausalLM (this rank's stage and shards) from upstream-named tensors (a
-    mapping, or a directory of safetensors files)."""
+    mapping, or a directory of safetensors files).  Returns the load inventory {"consumed": n, "unused":
+    [names]}; with `strict` a checkpoint holding tensors nothing read is refused (UnusedTensors) -- on a
+    single-stage, single-rank load, where every tensor has a reader.  `quantization_config` is the
+    checkpoint's (hybrid `module_quantization` rules, EXL3 `codebook` marker)."""
     t = open_dir(tensors) if isinstance(tensors, str) else tensors
+    qc = quantization_config or {}
+    codebook = fx.MARKERS.get(qc.get("codebook", "mul1"), (2, 0))[0]
+    t = _Tracked(t, qc.get("module_quantization"), codebook)
+    cfg = model.cfg
     st = pstate.get()
     tp, r = st.tp_size, st.tp_rank
     if model.embed is not None:
@@ -278,8 +429,14 @@ def load_hf(model, tensors: Mapping[str, torch.Tensor] | str) -> None:
         _set(layer.post_norm.weight, _get(t, p + "post_attention_layernorm.weight"))
         if layer.kind == "dsa":
             _load_dsa(layer.attn, t, p + "attn.", tp, r)
+        elif layer.kind == "gqa":
+            _load_gqa(layer.attn, t, p + "self_attn.", tp, r, cfg)
+        elif layer.kind == "kda" and cfg.kda.mode == "gdn":
+            _load_gdn(layer.attn, t, p + "linear_attn.", tp, r, cfg)
         else:
             (_load_kda if layer.kind == "kda" else _load_mla)(layer.attn, t, p + "self_attn.", tp, r)
+        if getattr(layer, "engram", None) is not None:
+            _load_engram(layer.engram, t, p + "engram.")
         if getattr(layer, "hc_attn", None) is not None:
             _load_hc(layer.hc_attn, t, p + "hc_attn")
             if layer.hc_mlp is not None:
@@ -290,9 +447,15 @@ def load_hf(model, tensors: Mapping[str, torch.Tensor] | str) -> None:
             _load_dense_mlp(layer.mlp, t, p + "mlp.", tp, r)
         else:
             _load_moe(layer.mlp, t, p + "mlp.", tp, r)
+    if getattr(model, "ple", None) is not None:
+        _set_linear(model.ple.proj, _dense(t, "model.ple_proj"))
     from .checkpoint import drop_decoded_caches
 
     drop_decoded_caches(model)
+    unused = t.unused()
+    if strict and unused:
+        raise UnusedTensors(f"{len(unused)} checkpoint tensors have no reader, e.g. {unused[:5]}")
+    return {"consumed": len(t.used), "unused": unused}
 
 
 def export_hf(model) -> dict[str, torch.Tensor]:
@@ -325,6 +488,8 @@ def export_hf(model) -> dict[str, torch.Tensor]:
             h.fn.detach(), h.scale.detach(), h.base.detach())
     out["model.norm.weight"] = model.norm.weight.detach()
     out["lm_head.weight"] = dense(model.lm_head)
+    if getattr(model, "ple", None) is not None:
+        out["model.ple_proj.weight"] = dense(model.ple.proj)
     for layer in model.layers:
         p = f"model.layers.{layer.idx}."
         out[p + "input_layernorm.weight"] = layer.input_norm.weight.detach()
@@ -357,6 +522,38 @@ def export_hf(model) -> dict[str, torch.Tensor]:
                 out[q + "indexer.weights_proj.weight"] = dense(a.idx_w)
                 out[q + "indexer.wk.weight"] = a.wk.detach()
                 out[q + "indexer.k_norm.weight"] = a.k_norm.detach()
+        elif layer.kind == "gqa":
+            hd = model.cfg.gqa.head_dim
+            w = dense(a.in_proj)
+            nq = a.nh * 2 * hd
+            out[q + "q_proj.weight"] = w[:nq].contiguous()
+            out[q + "k_proj.weight"] = w[nq:nq + a.nkv * hd].contiguous()
+            out[q + "v_proj.weight"] = w[nq + a.nkv * hd:nq + 2 * a.nkv * hd].contiguous()
+            out[q + "q_norm.weight"] = a.q_norm_w.detach()
+            out[q + "k_norm.weight"] = a.k_norm_w.detach()
+            out[q + "o_proj.weight"] = dense(a.o_proj)
+        elif layer.kind == "kda" and model.cfg.kda.mode == "gdn":
+            q = p + "linear_attn."
+            H, D = a.H, a.D
+            grp, rep, Hk = _gdn_groups(model.cfg.kda, H, 1, 0)
+            w = dense(a.in_proj)
+            qs, ks, vs, zs = (w[i * H * D:(i + 1) * H * D].view(H, D, -1) for i in range(4))
+            bs, as_ = w[4 * H * D:4 * H * D + H], w[4 * H * D + H:4 * H * D + 2 * H]
+            rows, ba = [], []
+            for h in range(Hk):
+                js = [j for j, (hh, _) in enumerate(grp) if hh == h]
+                rows += [qs[js[0]], ks[js[0]]] + [vs[j] for j in js] + [zs[j] for j in js]
+                ba += [bs[j:j + 1] for j in js] + [as_[j:j + 1] for j in js]
+            out[q + "in_proj_qkvz.weight"] = torch.cat(rows, 0).contiguous()
+            out[q + "in_proj_ba.weight"] = torch.cat(ba, 0).contiguous()
+            conv = a.conv_w.detach().view(3, H, D, 4)
+            first = [next(j for j, (hh, _) in enumerate(grp) if hh == h) for h in range(Hk)]
+            out[q + "conv1d.weight"] = torch.cat([conv[0, first].reshape(-1, 4), conv[1, first].reshape(-1, 4),
+                                                  conv[2].reshape(-1, 4)], 0).unsqueeze(1).contiguous()
+            out[q + "A_log"] = a.a_log.detach()
+            out[q + "dt_bias"] = a.dt_bias.detach()
+            out[q + "norm.weight"] = a.norm_w.detach()
+            out[q + "out_proj.weight"] = dense(a.o_proj)
         elif layer.kind == "kda":
             H, D = a.H, a.D
             w = dense(a.in_proj)
@@ -387,6 +584,11 @@ def export_hf(model) -> dict[str, torch.Tensor]:
             put(q + "indexer.wq_b", a.idx_q)
             out[q + "indexer.k_norm.weight"] = a.idx_k_ln_w.detach()
             out[q + "indexer.k_norm.bias"] = a.idx_k_ln_b.detach()
+        if getattr(layer, "engram", None) is not None:
+            e = layer.engram
+            out[p + "engram.kv.weight"] = dense(e.kv)
+            out[p + "engram.h_norm.weight"] = e.h_norm_w.detach()
+            out[p + "engram.k_norm.weight"] = e.k_norm_w.detach()
         mlp = layer.mlp
         if mlp is None:
             continue
