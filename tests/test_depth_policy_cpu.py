@@ -163,3 +163,36 @@ def test_logit_stats_over_vocab_shards(tmp_path):
                        start_method="spawn")
     sharded, full = torch.load(path)
     assert torch.allclose(sharded, full, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("bias", [3.0, -20.0, 0.0])
+def test_row_mask_mode_keeps_the_verify_width_and_matches_plain(tmp_path, bias):
+    """depth_mode "mask": every request verifies all k drafts (one verify width, so the verify step's
+    CUDA graph applies) and the policy's cut only masks candidates; greedy output equals plain decoding."""
+    pstate.set_state(pstate.ParallelState())
+    path = tmp_path / "policy.json"
+    path.write_text(json.dumps({
+        "schema": "dspark-depth-policy/1", "max_depth": 3, "features": ["bias", "logit_conf", "logit_top1", "ent"],
+        "weights": [[bias, 0.1, 0.1, -0.01]] * 3,
+        "costs": {"1": {"0": 10, "1": 10.5, "2": 11, "3": 11.5}, "4": {"0": 10, "1": 11, "2": 12, "3": 13}}}))
+    prompts = [[(5 * i + 3 * j) % 500 for j in range(n)] for i, n in enumerate([9, 40, 71])]
+    model = HybridForCausalLM(_cfg(0).model, "cpu", seed=3)
+    plain = LLM(_cfg(0), model).generate(prompts, SamplingParams(max_tokens=8))
+    cfg = _cfg(3, str(path))
+    cfg.scheduler.depth_mode = "mask"
+    llm = LLM(cfg, model)
+    widths = []
+    orig = llm.engine.runner.execute
+
+    def spy(out):
+        widths.extend(s.num_draft for s in out.reqs if s.num_draft)
+        return orig(out)
+
+    llm.engine.runner.execute = spy
+    got = llm.generate(prompts, SamplingParams(max_tokens=8))
+    model.aux_layer_ids = ()
+    assert [o.output_token_ids for o in got] == [o.output_token_ids for o in plain]
+    # verify steps keep the full k-draft width (only the length limit near max_tokens narrows one)
+    assert widths and widths.count(3) >= len(widths) // 2
+    if bias < -10:  # all drafts masked: nothing is a candidate, yet the rows were verified
+        assert llm.engine.runner.spec.stats["accepted"] == 0

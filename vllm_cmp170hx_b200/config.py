@@ -391,6 +391,10 @@ class SchedulerConfig:
     spec_method: str = "mtp"  # drafter: 'mtp' (chained MTP head) or 'dflash' (block drafter)
     dflash_layers: int = 1  # DFlash drafter depth
     depth_policy: str = ""  # per-request verify depth policy file (dspark-depth-policy/1); "" off
+    # how the policy's cut applies: "unschedule" (drafts past the depth are not verified) or "mask" (every
+    # request verifies k drafts, those past its depth are masked rows: the verify step keeps one width and
+    # replays its CUDA graph)
+    depth_mode: str = "unschedule"
     pp_spread_decodes: bool = True  # pipeline micro-batches take equal shares of the decodes
     # asynchronous scheduling of decode steps: the next step is scheduled and launched (its input tokens
     # gathered on the device from the step in flight) before that step's tokens are read back

@@ -55,8 +55,11 @@ class Request:
     num_preemptions: int = 0
     first_token_time: float | None = None
     token_times: list[float] = field(default_factory=list)
-    # speculative decoding: draft tokens proposed for the next verify step
+    # speculative decoding: draft tokens proposed for the next verify step, and how many of them are live
+    # (the verify-depth policy's row mask: drafts past it are verified rows whose results are ignored,
+    # so every request keeps the same verify width; -1 = all live)
     draft_token_ids: list[int] = field(default_factory=list)
+    draft_live: int = -1
     # benchmarks: the first `synthetic_prefix` prompt positions count as computed on admission (their
     # cache rows and recurrent state are whatever the caches hold, e.g. random rows), so a long-context
     # decode can be measured without prefilling it

@@ -809,14 +809,15 @@ class ModelRunner:
                 # verify: accept drafts while they match the target's choice, then the bonus token
                 cand = host[k:k + s.num_new]
                 k += s.num_new
-                drafts = s.req.draft_token_ids[: s.num_draft]
+                live = s.num_draft if s.req.draft_live < 0 else min(s.num_draft, s.req.draft_live)
+                drafts = s.req.draft_token_ids[:live]
                 acc = []
                 for j, d in enumerate(drafts):
                     acc.append(cand[j])
                     if cand[j] != d:
                         break
                 else:
-                    acc.append(cand[s.num_draft])
+                    acc.append(cand[live])
                 res[s.req.request_id] = acc
             else:
                 res[s.req.request_id] = [host[k]]

@@ -172,6 +172,7 @@ class Scheduler:
         victim.num_preemptions += 1
         victim.status = Status.PREEMPTED
         victim.draft_token_ids = []
+        victim.draft_live = -1
         self.waiting.appendleft(victim)
         out.preempted.append(victim)
 
@@ -301,6 +302,7 @@ class Scheduler:
                 # the blocks it computed are never registered for prefix reuse
                 req.status = Status.FINISHED_ERROR
                 req.draft_token_ids = []
+                req.draft_live = -1
                 done.append(req)
                 continue
             if s.num_draft:
@@ -312,6 +314,7 @@ class Scheduler:
             if self.prefix_caching:
                 self._register_blocks(req)
             req.draft_token_ids = []
+            req.draft_live = -1
             for t in toks:
                 req.output_token_ids.append(int(t))
                 if req.first_token_time is None:

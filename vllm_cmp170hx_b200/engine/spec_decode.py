@@ -47,6 +47,11 @@ _SEED_VERIFY = 0x5BD1E995
 _SEED_DRAFT = 0x27D4EB2F
 
 
+def _live_drafts(req, num_draft: int) -> int:
+    """Drafts of a verify step that are candidates (the row mask's live depth, at most the scheduled)."""
+    return num_draft if req.draft_live < 0 else min(num_draft, req.draft_live)
+
+
 def _all_reduce(x: torch.Tensor, op=dist.ReduceOp.SUM) -> torch.Tensor:
     st = pstate.get()
     if st.tp_size > 1 and not st.emulated:
@@ -136,7 +141,7 @@ class SpecDecoder:
             for j, row in enumerate(rows):
                 trows.append(row)
                 ttemps.append(req.params.temperature)
-                d = req.draft_token_ids[j] if j < s.num_draft else -1
+                d = req.draft_token_ids[j] if j < _live_drafts(req, s.num_draft) else -1
                 tdraft.append(d)
                 tq.append((qs, j) if (d >= 0 and qs is not None) else None)
         host_stats = None
@@ -177,7 +182,9 @@ class SpecDecoder:
                 continue
             req = s.req
             rows = rows_of[req.request_id]
-            drafts = req.draft_token_ids[: s.num_draft]
+            # masked draft rows (past the request's live depth) were verified but are not candidates:
+            # the token at the first masked position is the target's own (greedy) or a draw from p
+            drafts = req.draft_token_ids[: _live_drafts(req, s.num_draft)]
             acc = []
             if req.params.temperature <= 0:
                 for j, dtok in enumerate(drafts):
@@ -271,11 +278,22 @@ class SpecDecoder:
             cur = self.mtp(tok, cur, ctx)
         live = self._live(A, stats, None)
         dh = torch.stack(drafts, dim=1).cpu().tolist()
-        for a, req in enumerate(areqs):
-            limit = max(0, min(self.k, live[a], req.params.max_tokens - len(req.output_token_ids) - 1))
-            req.draft_token_ids = [int(v) for v in dh[a][:limit]]
+        self._set_drafts(areqs, dh, live)
         for qi, a in enumerate(samp):
             self.q_store[areqs[a].request_id] = (qbuf, qi)
+
+    def _set_drafts(self, areqs, dh, live) -> None:
+        """Store each request's drafts: cut to its live depth, or (depth_mode "mask") all k with the live
+        depth recorded as the row mask."""
+        mask = self.runner.cfg.scheduler.depth_mode == "mask" and self.depth is not None
+        for a, req in enumerate(areqs):
+            room = max(0, req.params.max_tokens - len(req.output_token_ids) - 1)
+            if mask:
+                req.draft_token_ids = [int(v) for v in dh[a][:min(self.k, room)]]
+                req.draft_live = max(0, min(live[a], len(req.draft_token_ids)))
+            else:
+                req.draft_token_ids = [int(v) for v in dh[a][:max(0, min(self.k, live[a], room))]]
+                req.draft_live = -1
 
     def _live(self, A: int, stats: list, conf) -> list[int]:
         """Drafts worth verifying per request (all k without a depth policy)."""
@@ -347,9 +365,7 @@ class SpecDecoder:
                 qbuf[j] = e / ssum[:, None]
         live = self._live(A, stats, d.confidence(h) if (self.depth is not None and self.depth.uses_conf) else None)
         dh = torch.stack(drafts, dim=1).cpu().tolist()
-        for a, req in enumerate(areqs):
-            limit = max(0, min(self.k, live[a], req.params.max_tokens - len(req.output_token_ids) - 1))
-            req.draft_token_ids = [int(v) for v in dh[a][:limit]]
+        self._set_drafts(areqs, dh, live)
         for qi, a in enumerate(samp):
             self.q_store[areqs[a].request_id] = (qbuf, qi)
 
