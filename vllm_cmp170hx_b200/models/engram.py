@@ -74,6 +74,30 @@ class EngramMemory:
             out = self.table.lookup(ids)
         return out.view(T, self.heads * self.dim)
 
+    _streams: dict = {}
+
+    def prefetch(self, ids: torch.Tensor):
+        """Start the step's lookup on a side stream (the reference's Engram prefetch on its own stream,
+        vllm_sm80/models/deepseek_v41/sm80_engram_prefetch.py): the ids' copy out, the host fetch, the rows'
+        copy in and the dequant run beside the layers before the first Engram layer.  Returns (rows,
+        event); a consumer waits for the event before reading the rows.  On CPU: (rows, None)."""
+        if not ids.is_cuda:
+            return self.rows(ids), None
+        dev = ids.device
+        side = EngramMemory._streams.get(dev)
+        if side is None:
+            side = EngramMemory._streams[dev] = torch.cuda.Stream(dev)
+        cur = torch.cuda.current_stream(dev)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            rows = self.rows(ids)
+            ev = torch.cuda.Event()
+            ev.record(side)
+        if not torch.cuda.is_current_stream_capturing():  # graph buffers live as long as the graph
+            ids.record_stream(side)
+            rows.record_stream(cur)
+        return rows, ev
+
 
 class EngramBlock(nn.Module):
     def __init__(self, cfg: ModelConfig, wi: WeightInit):
@@ -85,8 +109,11 @@ class EngramBlock(nn.Module):
         self.k_norm_w = nn.Parameter(wi.ones_plus(H, 0.05), requires_grad=False)
         self.eps = cfg.rms_eps
 
-    def add_(self, a: torch.Tensor, h: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
-        """a += sigmoid(<rmsnorm(h) w_h, rmsnorm(k) w_k> / sqrt(H)) v, [k | v] = rows W^T; returns a."""
+    def add_(self, a: torch.Tensor, h: torch.Tensor, rows: torch.Tensor, ready=None) -> torch.Tensor:
+        """a += sigmoid(<rmsnorm(h) w_h, rmsnorm(k) w_k> / sqrt(H)) v, [k | v] = rows W^T; returns a.
+        ready: the prefetch's event (waited for on the current stream before the rows are read)."""
+        if ready is not None:
+            torch.cuda.current_stream(rows.device).wait_event(ready)
         kv = self.kv(rows)
         if a.is_cuda:
             _ext.ops().engram_gate(h, kv, self.h_norm_w, self.k_norm_w, self.eps, a)

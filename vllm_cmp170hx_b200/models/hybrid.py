@@ -69,6 +69,7 @@ class StepContext:
     # Engram memory ids of the step's tokens, int64 [T, heads], and the rows the stage looked up for them
     engram_ids: torch.Tensor | None = None
     engram_rows: torch.Tensor | None = None
+    engram_ready: object = None  # CUDA event of the side-stream lookup (None: rows ready in stream order)
 
 
 def _fp8_proj(w: torch.Tensor):
@@ -624,7 +625,7 @@ class DecoderLayer(nn.Module):
         state, h = self.hc_attn(state, self.input_norm, self.cfg)
         state.x = self.attn(h, ctx, self.idx)
         if self.engram is not None:
-            self.engram.add_(state.x, h, ctx.engram_rows)
+            self.engram.add_(state.x, h, ctx.engram_rows, ctx.engram_ready)
         if self.mlp is not None:
             # the attention output's post, then the MLP input, in one boundary op
             state, h = self.hc_mlp(state, self.post_norm, self.cfg)
@@ -679,7 +680,7 @@ class DecoderLayer(nn.Module):
             h = self.input_norm(x, residual)
         a = self.attn(h, ctx, self.idx)  # row-parallel o_proj: already summed over the TP group
         if self.engram is not None:
-            self.engram.add_(a, h, ctx.engram_rows)
+            self.engram.add_(a, h, ctx.engram_rows, ctx.engram_ready)
         if self.mlp is None:  # the next layer's fused norm adds the attention output
             return a, residual
         h = self.post_norm(a, residual)
@@ -756,7 +757,8 @@ class HybridForCausalLM(nn.Module):
         or its `HCState` with hyper-connections.  Returns the normed final hidden on the last stage,
         else what the next stage takes as `hidden_in`."""
         if self.engram is not None:
-            ctx.engram_rows = self.engram.rows(ctx.engram_ids)
+            # the lookup runs on a side stream beside the layers before the first Engram layer
+            ctx.engram_rows, ctx.engram_ready = self.engram.prefetch(ctx.engram_ids)
         if self.cfg.hc_mult:
             if self.first:
                 e = self.embed[input_ids]
