@@ -26,6 +26,7 @@
 // kernel with one "expert" whose rows are all tokens.
 #include "common.cuh"
 #include "launch.h"
+#include <cstdio>
 #include <stdexcept>
 #include <string>
 
@@ -938,14 +939,27 @@ cudaError_t launch_gemm(const GemmParams& p, const void* b0, const void* b1, int
   return cudaGetLastError();
 }
 
-// Decoder warps per CTA: VLLM_B200_EXL3_DECODERS (8 or 16) when set, else the pass's default.
-inline int decoder_warps(int nmat) {
-  static const int env = [] {
+// Decoder warps per CTA: VLLM_B200_EXL3_DECODERS when set -- "8" or "16" for both passes, or "G,D" for the
+// gate/up pass (two matrices) and the down pass (one) apart -- else the pass's default.
+struct DecoderChoice {
+  int down = 0, gate_up = 0;
+  DecoderChoice() {
     const char* v = std::getenv("VLLM_B200_EXL3_DECODERS");
-    return v ? std::atoi(v) : 0;
-  }();
-  if (env == 8 || env == 16) return env;
-  (void)nmat;
+    if (v == nullptr) return;
+    int g = 0, d = 0;
+    if (std::sscanf(v, "%d,%d", &g, &d) == 2) {
+      gate_up = g;
+      down = d;
+    } else {
+      gate_up = down = std::atoi(v);
+    }
+  }
+};
+
+inline int decoder_warps(int nmat) {
+  static const DecoderChoice choice;  // read once per process
+  const int w = nmat == 2 ? choice.gate_up : choice.down;
+  if (w == 8 || w == 16) return w;
   return 16;
 }
 

@@ -56,8 +56,8 @@ _declare("VLLM_B200_EP_DISPATCH", str, "symm", "expert-parallel steps: 'symm' (s
 _declare("VLLM_B200_CUDA_GRAPHS", _bool, True, "capture decode steps in CUDA graphs (0: every step eager)")
 _declare("VLLM_B200_GEMM_SPLITK", int, 0, "force the split-K factor of the bf16 GEMM (0 = shape-chosen)")
 _declare("VLLM_B200_EXL3_TILE_ROWS", int, 0, "rows per EXL3 expert work item, 16 / 32 / 64 / 128 (0 = batch-chosen)")
-_declare("VLLM_B200_EXL3_DECODERS", int, 0, "decoder warps of the EXL3 GEMM, 8 or 16 (0 = the build's default; read "
-         "by csrc/exl3.cu)")
+_declare("VLLM_B200_EXL3_DECODERS", str, "", "decoder warps of the EXL3 GEMM: '8' or '16' for both passes, or "
+         "'G,D' for the gate/up and the down pass ('' = the build's default; read by csrc/exl3.cu)")
 _declare("VLLM_B200_KDA_PREFILL", str, "chunked", "KDA prefill: 'chunked' (sequences of >= 64 tokens in chunks of 64 "
          "on the tensor cores, read by ops/kda.py) or 'recurrent' (token by token)")
 _declare("VLLM_B200_SPARSE_MLA_SPLITS", int, 0, "position splits of the sparse-MLA attention (0 = auto)")
