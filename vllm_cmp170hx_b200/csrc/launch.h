@@ -400,7 +400,7 @@ cudaError_t gqa_dense_attention(const void* q, int Tq, int group, const void* ca
 cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const void* cache, const int* indices,
                                  const int* counts, int topk, float sm_scale, int splits, void* out, float* part_o,
                                  float* part_ml, float* lse, const float* sink, uint32_t* status,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream, int only_half = -1);
 
 // ---------------------------------------------------------------- sampling.cu
 cudaError_t sample_rows(const void* logits, int dtype, int64_t ld, int rows, int V, const float* temperature,

@@ -724,10 +724,11 @@ cudaError_t launch_sparse_attention(const CUtensorMap& tq, const mla::attn4::Par
 cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const void* cache, const int* indices,
                                  const int* counts, int topk, float sm_scale, int splits, void* out, float* part_o,
                                  float* part_ml, float* lse, const float* sink, uint32_t* status,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, int only_half) {
   using namespace mla::attn4;
   if (T == 0) return cudaSuccess;
   if (dim != 512 && dim != 576) return cudaErrorInvalidValue;
+  if (only_half < -1 || only_half > 1) return cudaErrorInvalidValue;
   const int DIM = dim;
   const int box_rows = nh >= 128 ? 128 : (nh + 7) / 8 * 8;
   CUtensorMap tq = make_tma_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)T * nh, DIM, DIM, box_rows, 64,
@@ -748,12 +749,13 @@ cudaError_t mla_sparse_attention(const void* q, int T, int nh, int dim, const vo
   p.sink = sink;
   p.T = T;
   p.status = status;
-  p.only_half = -1;
+  p.only_half = only_half;
   cudaError_t e = dim == 512 ? launch_sparse_attention<512>(tq, p, T, nh, splits, stream)
                              : launch_sparse_attention<576>(tq, p, T, nh, splits, stream);
   if (e != cudaSuccess || splits == 1) return e;
+  const int c_lo = only_half == 1 ? 256 : 0, c_hi = only_half == 0 ? 256 : 512;
   launch_pdl(mla::attn::merge_kernel, dim3(T * nh), dim3(128), 0, stream, part_o, part_ml, splits, T, nh,
-             reinterpret_cast<__nv_bfloat16*>(out), lse, sink, 0, 512);
+             reinterpret_cast<__nv_bfloat16*>(out), lse, sink, c_lo, c_hi);
   return cudaGetLastError();
 }
 

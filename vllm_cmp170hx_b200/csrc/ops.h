@@ -86,7 +86,7 @@ void mla_topk_op(const at::Tensor& scores, const at::Tensor& ctx_lens, int64_t k
 void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& indices,
                              const at::Tensor& counts, double sm_scale, int64_t splits, at::Tensor& out,
                              const c10::optional<at::Tensor>& lse, const at::Tensor& status,
-                             const c10::optional<at::Tensor>& sink);  // mla_attn.cu
+                             const c10::optional<at::Tensor>& sink, int64_t only_half);  // mla_attn.cu
 
 void sample_rows_op(const at::Tensor& logits, const c10::optional<at::Tensor>& temperature, int64_t seed,
                     const c10::optional<at::Tensor>& step, int64_t vocab_offset, at::Tensor& out_val,
@@ -199,7 +199,7 @@ void register_host_bindings(pybind11::module_& m);
   X("mla_topk(Tensor scores, Tensor ctx_lens, int k, Tensor? token_seq, Tensor block_table, int block_size, " \
     "Tensor(a!) out_idx, Tensor(b!) out_count) -> ()")                                                    \
   X("mla_sparse_attention(Tensor q, Tensor cache, Tensor indices, Tensor counts, float sm_scale, int splits, " \
-    "Tensor(a!) out, Tensor(b!)? lse, Tensor(c!) status, Tensor? sink=None) -> ()")                      \
+    "Tensor(a!) out, Tensor(b!)? lse, Tensor(c!) status, Tensor? sink=None, int only_half=-1) -> ()")                      \
   X("sample_rows(Tensor logits, Tensor? temperature, int seed, Tensor? step, int vocab_offset, "          \
     "Tensor(a!) out_val, Tensor(b!) out_idx, Tensor? bans=None) -> ()")                                  \
   X("sample_combine(Tensor vals, Tensor idx, Tensor(a!) out) -> ()")                                     \

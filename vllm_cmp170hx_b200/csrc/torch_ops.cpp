@@ -505,7 +505,9 @@ void mla_topk_op(const at::Tensor& scores, const at::Tensor& ctx_lens, int64_t k
 void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Tensor& indices,
                              const at::Tensor& counts, double sm_scale, int64_t splits, at::Tensor& out,
                              const c10::optional<at::Tensor>& lse, const at::Tensor& status,
-                             const c10::optional<at::Tensor>& sink) {
+                             const c10::optional<at::Tensor>& sink, int64_t only_half) {
+  TORCH_CHECK(only_half >= -1 && only_half <= 1, "sparse attn: only_half -1 (both), 0 or 1");
+  TORCH_CHECK(only_half < 0 || !lse.has_value(), "sparse attn: the log-sum-exp comes with both halves");
   B200_CHECK_CUDA(q);
   B200_CHECK_DTYPE(q, at::kBFloat16);
   TORCH_CHECK(q.dim() == 3 && (q.size(2) == 576 || q.size(2) == 512) && q.is_contiguous(),
@@ -536,7 +538,7 @@ void mla_sparse_attention_op(const at::Tensor& q, const at::Tensor& cache, const
                                    splits > 1 ? part_ml.data_ptr<float>() : nullptr,
                                    lse.has_value() ? lse->data_ptr<float>() : nullptr,
                                    sink.has_value() ? sink->data_ptr<float>() : nullptr, status_ptr(status),
-                                   cur_stream()));
+                                   cur_stream(), (int)only_half));
 }
 
 }  // namespace b200

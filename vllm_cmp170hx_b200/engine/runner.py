@@ -126,8 +126,8 @@ class ModelRunner:
                 n_gqa = len(m.gqa_layer_ids()) + (1 if mtp_gqa else 0)
                 if n_gqa:  # [k | v] rows of the local key-value heads
                     per_block += n_gqa * 64 * m.gqa_kv_heads() * 512 * 2
-                if spec and not mtp:  # DFlash context keys / values (the drafter's default shape)
-                    per_block += cfg.scheduler.dflash_layers * 64 * 2 * 4 * 128 * 2
+                if spec and not mtp:  # DFlash [k | v | 0] rows of 512 per key-value head (the default 4 heads)
+                    per_block += cfg.scheduler.dflash_layers * 64 * 4 * 512 * 2
                 n_dsa = len(m.dsa_layer_ids())
                 if n_dsa:  # DeepSeek-V4.1 group rows + index keys, and the per-slot rings / step scratch
                     a = self.mcfg.dsa

@@ -94,7 +94,8 @@ class SpecDecoder:
             dc = DFlashConfig(num_layers=cfg.scheduler.dflash_layers)
             self.dflash = DFlashDrafter(cfg.model, dc, runner.model, runner.device, cfg.seed, init_mode)
             runner.model.aux_layer_ids = tuple(self.dflash.dc.aux_layer_ids)
-            self.dcaches = self.dflash.alloc_caches(rows, runner.device)
+            self.dcaches = self.dflash.alloc_caches(rows, runner.device,
+                                                    cfg.scheduler.max_num_seqs * (self.k + 1))
         elif self.method == "mtp":
             from ..models.mtp import MTPHead
 

@@ -1,5 +1,11 @@
 """DFlash block drafter: k draft tokens from one non-causal forward over a block of k + 1 queries.
 
+On the GPU the block attention runs on the package's tcgen05 block-sparse attention kernel: each draft
+layer keeps one 512-wide row per (position, key-value head), ``[k | v | 0]``, and a query row of the
+block (per key-value head, its query heads in one tile) attends to the row list [its request's context
+rows | the block's own rows], written into scratch rows of the same buffer; only the output half that
+holds v is computed (ops/mla.py ``only_half``).  On the CPU the same attention is evaluated densely.
+
 The target exposes the residual stream after a few of its layers (the auxiliary hidden states);
 their concatenation goes through `fc` into one context state per verified position.  Each draft
 layer projects a context state (after `hidden_norm`) to a key / value row -- k_norm per head and
@@ -58,6 +64,34 @@ def _rope(x: torch.Tensor, positions: torch.Tensor, theta: float) -> torch.Tenso
     return torch.cat([a * cos - b * sin, b * cos + a * sin], -1).to(x.dtype)
 
 
+class DFlashCache:
+    """One draft layer's context keys / values.  CUDA: rows [(slots + scratch) * nkv, 512] bf16 =
+    [k | v | 0] per (slot, key-value head), the scratch slots after the paged ones holding a forward's
+    block rows; CPU: k, v [slots, nkv, hd]."""
+
+    def __init__(self, slots: int, nkv: int, hd: int, device, scratch: int = 0):
+        self.nkv, self.hd = nkv, hd
+        self.fused = torch.device(device).type == "cuda"
+        if self.fused:
+            if not (hd <= 128 or hd == 256):
+                raise ValueError(f"DFlash head_dim {hd}: v must sit inside one 256-wide half of the rows "
+                                 "(head_dim <= 128 or 256)")
+            self.rows = torch.zeros((slots + scratch) * nkv, 512, dtype=torch.bfloat16, device=device)
+            self.scratch0, self.scratch = slots, scratch
+        else:
+            self.k = torch.zeros(slots, nkv, hd, dtype=torch.bfloat16, device=device)
+            self.v = torch.zeros(slots, nkv, hd, dtype=torch.bfloat16, device=device)
+
+    def write(self, slots: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+        if self.fused:
+            r = self.rows.view(-1, self.nkv, 512)
+            r[slots, :, :self.hd] = k.to(r.dtype)
+            r[slots, :, self.hd:2 * self.hd] = v.to(r.dtype)
+        else:
+            self.k[slots] = k
+            self.v[slots] = v
+
+
 class DFlashLayer(nn.Module):
     def __init__(self, H: int, dc: DFlashConfig, eps: float, wi: WeightInit):
         super().__init__()
@@ -71,18 +105,35 @@ class DFlashLayer(nn.Module):
         self.o_proj = Linear(wi.normal((H, nh * hd), default_std(nh * hd)))
         self.gate_up = Linear(wi.normal((2 * dc.intermediate, H), default_std(H)))
         self.down = Linear(wi.normal((H, dc.intermediate), default_std(dc.intermediate)))
+        # RoPE table of the GPU path (NeoX rotate-half over the whole head)
+        self.register_buffer("cos_sin", None, persistent=False)
+        self.max_position = 1 << 17
+
+    def _table(self, device) -> torch.Tensor:
+        if self.cos_sin is None:
+            from ..oracle.mla import rope_cos_sin
+
+            self.cos_sin = rope_cos_sin(self.max_position, self.hd, self.theta, device)
+        return self.cos_sin
+
+    def _rope(self, x: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda:
+            return _rope(x, positions, self.theta)
+        from ..ops import mla as mla_ops
+
+        return mla_ops.rope_(x.contiguous(), positions.to(torch.int32), self._table(x.device), 0, self.hd, False)
 
     def kv_rows(self, h: torch.Tensor, positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """Key / value rows [n, nkv, hd] of normed states h [n, H]."""
         kv = ops.gemm(h, self.qkv.weight[self.nh * self.hd:])
         k, v = kv.view(-1, 2, self.nkv, self.hd).unbind(1)
-        k = _rope(self.k_norm(k.reshape(-1, self.hd)).view(-1, self.nkv, self.hd), positions, self.theta)
+        k = self._rope(self.k_norm(k.reshape(-1, self.hd)).view(-1, self.nkv, self.hd), positions)
         return k, v.contiguous()
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None, positions: torch.Tensor,
-                ctx_k: torch.Tensor, ctx_v: torch.Tensor, ctx_valid: torch.Tensor):
-        """x [A * B, H] block rows of A requests (B = k + 1 each); ctx_k / ctx_v [A, C, nkv, hd] with
-        ctx_valid [A, C]."""
+                cache: DFlashCache, ctx_slots: torch.Tensor, ctx_valid: torch.Tensor):
+        """x [A * B, H] block rows of A requests (B = k + 1 each); ctx_slots [A, C] cache slots of the
+        context positions, ctx_valid [A, C] the real ones (a prefix of each row)."""
         if residual is None:
             residual, h = x, self.input_norm(x)
         else:
@@ -91,23 +142,59 @@ class DFlashLayer(nn.Module):
         B = x.shape[0] // A
         qkv = ops.gemm(h, self.qkv.weight)
         q, k, v = qkv.split([self.nh * self.hd, self.nkv * self.hd, self.nkv * self.hd], -1)
-        q = _rope(self.q_norm(q.reshape(-1, self.hd)).view(-1, self.nh, self.hd), positions, self.theta)
-        k = _rope(self.k_norm(k.reshape(-1, self.hd)).view(-1, self.nkv, self.hd), positions, self.theta)
+        qn = self.q_norm(q.reshape(-1, self.hd)).view(-1, self.nh, self.hd)
+        k = self._rope(self.k_norm(k.reshape(-1, self.hd)).view(-1, self.nkv, self.hd), positions)
         v = v.reshape(-1, self.nkv, self.hd)
+        if cache.fused:
+            o = self._attend_kernel(qn, k, v, positions, cache, ctx_slots, ctx_valid, A, B)
+        else:
+            o = self._attend_dense(qn, k, v, positions, cache, ctx_slots, ctx_valid, A, B)
+        a = ops.gemm(o.to(x.dtype), self.o_proj.weight)
+        h = self.post_norm(a, residual)  # residual += a (in place), h = norm(residual)
+        gu = ops.gemm(h, self.gate_up.weight)
+        return ops.gemm(ops.silu_mul(gu), self.down.weight), residual
+
+    def _attend_kernel(self, qn, k, v, positions, cache: DFlashCache, ctx_slots, ctx_valid, A: int, B: int):
+        """The block attention on the block-sparse attention kernel: the block's k / v go to scratch rows,
+        each (block row, key-value head) attends the row list [valid context rows | the block's rows]."""
+        from ..ops import mla as mla_ops
+
+        nkv, hd = self.nkv, self.hd
+        G = self.nh // nkv
+        dev = qn.device
+        if A * B > cache.scratch:
+            raise ValueError(f"DFlash block of {A * B} rows, the cache holds {cache.scratch} scratch rows")
+        blk = cache.scratch0 + torch.arange(A * B, device=dev)
+        cache.write(blk, k, v)
+        C = ctx_slots.shape[1]
+        n_valid = ctx_valid.sum(1)  # the valid context is a prefix of each row
+        lst = torch.full((A, C + B), -1, dtype=torch.int64, device=dev)
+        lst[:, :C] = torch.where(ctx_valid, ctx_slots.long(), -1)
+        lst.scatter_(1, n_valid[:, None] + torch.arange(B, device=dev)[None], blk.view(A, B))
+        j = torch.arange(nkv, device=dev)
+        rows = torch.where(lst[:, None, :] >= 0, lst[:, None, :] * nkv + j[None, :, None], -1)  # [A, nkv, C+B]
+        idx = rows[:, None].expand(A, B, nkv, C + B).reshape(A * B * nkv, C + B).to(torch.int32).contiguous()
+        counts = (n_valid + B).to(torch.int32).repeat_interleave(B * nkv)
+        qpad = torch.zeros(A * B * nkv, G, 512, dtype=torch.bfloat16, device=dev)
+        mla_ops.rope_into(qn.reshape(A * B * nkv, G, hd), positions.to(torch.int32).repeat_interleave(nkv),
+                          self._table(dev), 0, hd, False, qpad, 0)
+        half = 0 if hd <= 128 else 1
+        out = mla_ops.sparse_attention(qpad, cache.rows, idx, counts, hd ** -0.5, only_half=half)
+        return out[..., hd:2 * hd].reshape(A * B, self.nh * hd)
+
+    def _attend_dense(self, qn, k, v, positions, cache: DFlashCache, ctx_slots, ctx_valid, A: int, B: int):
+        sl = ctx_slots.clamp_min(0).long()
+        ctx_k, ctx_v = cache.k[sl], cache.v[sl]
+        q = _rope(qn, positions, self.theta)
         K = torch.cat([ctx_k, k.view(A, B, self.nkv, self.hd)], 1)  # [A, C + B, nkv, hd]
         V = torch.cat([ctx_v, v.view(A, B, self.nkv, self.hd)], 1)
-        valid = torch.cat([ctx_valid, torch.ones(A, B, dtype=torch.bool, device=x.device)], 1)
+        valid = torch.cat([ctx_valid, torch.ones(A, B, dtype=torch.bool, device=qn.device)], 1)
         qh = q.view(A, B, self.nh, self.hd).transpose(1, 2)  # [A, nh, B, hd]
         Kh = K.transpose(1, 2)  # [A, nkv, C + B, hd]: query head h reads key / value head h // (nh / nkv)
         Vh = V.transpose(1, 2)
-        o = F.scaled_dot_product_attention(qh, Kh, Vh, attn_mask=valid[:, None, None, :],
+        o = F.scaled_dot_product_attention(qh.float(), Kh.float(), Vh.float(), attn_mask=valid[:, None, None, :],
                                            enable_gqa=self.nh != self.nkv)
-        o = o.transpose(1, 2).reshape(A * B, self.nh * self.hd).to(x.dtype)
-        a = ops.gemm(o, self.o_proj.weight)
-        h = self.post_norm(a, residual)  # residual += a (in place), h = norm(residual)
-        gu = ops.gemm(h, self.gate_up.weight)
-        g, u = gu.chunk(2, -1)
-        return ops.gemm((F.silu(g.float()) * u.float()).to(x.dtype), self.down.weight), residual
+        return o.transpose(1, 2).reshape(A * B, self.nh * self.hd)
 
 
 class DFlashDrafter(nn.Module):
@@ -135,21 +222,22 @@ class DFlashDrafter(nn.Module):
         return ops.gemm(torch.cat(aux, -1), self.fc.weight)
 
     def store_context(self, states: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
-                      caches: list[tuple[torch.Tensor, torch.Tensor]]) -> None:
+                      caches: list[DFlashCache]) -> None:
         """Write each layer's key / value rows of the context states at `slots` (-1: none)."""
         h = self.hidden_norm(states)
         keep = slots >= 0
-        for layer, (kc, vc) in zip(self.layers, caches):
+        for layer, cache in zip(self.layers, caches):
             k, v = layer.kv_rows(h, positions)
-            kc[slots[keep]] = k[keep]
-            vc[slots[keep]] = v[keep]
+            cache.write(slots[keep], k[keep], v[keep])
 
     # bound on the context keys / values one block forward gathers (requests are split into groups)
     gather_bytes = 256 << 20
 
     def forward(self, bonus: torch.Tensor, last_pos: torch.Tensor, ctx_slots: torch.Tensor, ctx_valid: torch.Tensor,
-                caches: list[tuple[torch.Tensor, torch.Tensor]], k: int) -> torch.Tensor:
+                caches: list[DFlashCache], k: int) -> torch.Tensor:
         A, C = ctx_slots.shape
+        if caches and caches[0].fused:  # the attention kernel reads the rows in place: no gather, no groups
+            return self._forward(bonus, last_pos, ctx_slots, ctx_valid, caches, k)
         # K and V (bf16) of the context plus the block rows, gathered once and joined once (the
         # attention reads the key / value heads in place, no per-query-head copies)
         per_req = (C + k + 1) * self.dc.num_kv_heads * self.dc.head_dim * 2 * 2 * 2
@@ -160,7 +248,7 @@ class DFlashDrafter(nn.Module):
                                         ctx_valid[i:i + step], caches, k) for i in range(0, A, step)])
 
     def _forward(self, bonus: torch.Tensor, last_pos: torch.Tensor, ctx_slots: torch.Tensor, ctx_valid: torch.Tensor,
-                 caches: list[tuple[torch.Tensor, torch.Tensor]], k: int) -> torch.Tensor:
+                 caches: list[DFlashCache], k: int) -> torch.Tensor:
         """bonus [A] (the token after the last verified position), last_pos [A]; ctx_slots [A, C]
         cache slots of the context positions (ctx_valid marks the real ones).  Returns the normed
         hidden states [A, k, H] of the k mask rows."""
@@ -172,14 +260,13 @@ class DFlashDrafter(nn.Module):
         pos = (last_pos[:, None] + 1 + torch.arange(B, device=bonus.device)[None]).reshape(-1)
         x = t.embed[ids.reshape(-1)]
         residual = None
-        sl = ctx_slots.clamp_min(0).long()
-        for layer, (kc, vc) in zip(self.layers, caches):
-            x, residual = layer(x, residual, pos, kc[sl], vc[sl], ctx_valid)
+        for layer, cache in zip(self.layers, caches):
+            x, residual = layer(x, residual, pos, cache, ctx_slots, ctx_valid)
         h = self.norm(x, residual).view(A, B, -1)
         return h[:, 1:]
 
-    def alloc_caches(self, rows: int, device) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    def alloc_caches(self, rows: int, device, max_block_rows: int = 0) -> list[DFlashCache]:
+        """Per draft layer: the context rows of `rows` cache slots, plus (GPU) scratch rows for the largest
+        block forward (requests x (k + 1))."""
         dc = self.dc
-        return [(torch.zeros(rows, dc.num_kv_heads, dc.head_dim, dtype=torch.bfloat16, device=device),
-                 torch.zeros(rows, dc.num_kv_heads, dc.head_dim, dtype=torch.bfloat16, device=device))
-                for _ in self.layers]
+        return [DFlashCache(rows, dc.num_kv_heads, dc.head_dim, device, max_block_rows) for _ in self.layers]

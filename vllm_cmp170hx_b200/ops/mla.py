@@ -123,8 +123,9 @@ def pick_splits(T: int, nh: int, topk: int = 2048, num_sms: int = 148, max_parti
 
 
 def sparse_attention(q: torch.Tensor, cache: torch.Tensor, indices: torch.Tensor, counts: torch.Tensor,
-                     sm_scale: float, splits: int | None = None, want_lse: bool = False):
-    """q [T, nh, 576] (absorbed nope | rope) -> o_lat [T, nh, 512] bf16 (and lse [T, nh])."""
+                     sm_scale: float, splits: int | None = None, want_lse: bool = False, only_half: int = -1):
+    """q [T, nh, 576] (absorbed nope | rope) -> o_lat [T, nh, 512] bf16 (and lse [T, nh]).  only_half 0 / 1:
+    compute only that 256-wide half of the output (the other half is left unwritten)."""
     T, nh, _ = q.shape
     if not q.is_cuda:
         out = torch.zeros(T, nh, 512, dtype=torch.bfloat16)
@@ -142,5 +143,5 @@ def sparse_attention(q: torch.Tensor, cache: torch.Tensor, indices: torch.Tensor
     lse = torch.empty(T, nh, dtype=torch.float32, device=q.device) if want_lse else None
     s = splits if splits is not None else pick_splits(T, nh, indices.shape[1])
     _ext.ops().mla_sparse_attention(q.contiguous(), cache, indices, counts, sm_scale, s, out, lse,
-                                    _ext.status_word(q.device))
+                                    _ext.status_word(q.device), None, only_half)
     return (out, lse) if want_lse else out
