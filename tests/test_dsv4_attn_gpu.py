@@ -69,3 +69,44 @@ def test_core_on_cuda_matches_host(ratio):
         torch.cuda.synchronize()
         assert _rel(out["cuda"], out["cpu"]) < 2e-2, (c, _rel(out["cuda"], out["cpu"]))
         done += c
+
+
+@pytest.mark.parametrize("T,H,hpg,N", [(5, 4, 2, 40), (64, 32, 8, 700), (130, 64, 64, 129), (16, 16, 4, 1030)])
+def test_index_scores_kernel_matches_rounding_chain(T, H, hpg, N):
+    """csrc/dsv4_index.cu against the fp32 statement of the rounding chain (ref.indexer_scores) over the
+    same paged keys: almost every score is bit-equal (the fp32 dot products sum in another order, so a
+    bf16 rounding may land one ulp apart), and the canonical top-k picks nearly the same groups."""
+    from vllm_cmp170hx_b200 import _ext
+    from vllm_cmp170hx_b200.oracle import dsv4_attn as ref
+
+    g = torch.Generator().manual_seed(T + H + N)
+    nb = (N + 63) // 64
+    S = 3
+    bt = torch.randperm(S * nb + 5, generator=g)[:S * nb].view(S, nb).to(torch.int32)
+    keys = torch.randn((S * nb + 5) * 64, 128, generator=g).bfloat16()
+    q = torch.randn(T, H, 128, generator=g).bfloat16()
+    w = (torch.randn(T, H, generator=g) * 0.1).bfloat16()
+    seq = torch.randint(0, S, (T,), generator=g, dtype=torch.int32)
+    n_vis = torch.randint(1, N + 1, (T,), generator=g, dtype=torch.int32)
+    gi = torch.arange(N)
+    rows = bt[seq.long()][:, gi // 64].long() * 64 + gi % 64
+    want = ref.indexer_scores(q, w, keys[rows], n_vis.long(), hpg)
+    got = torch.empty(T, N, dtype=torch.float32, device="cuda")
+    ops = _ext.ops()
+    ops.dsv4_index_scores(q.cuda(), w.cuda(), keys.cuda(), bt.cuda(), seq.cuda(), n_vis.cuda(), hpg, got)
+    torch.cuda.synchronize()
+    got = got.cpu()
+    vis = gi[None] < n_vis[:, None]
+    assert torch.equal(torch.isinf(got), ~vis)
+    same = (got[vis] == want[vis]).float().mean().item()
+    scale = want[vis].abs().max().item()
+    print(f"dsv4 index scores: {same:.4f} bit-equal, max diff {(got[vis] - want[vis]).abs().max().item():.2e}")
+    assert same > 0.97 and (got[vis] - want[vis]).abs().max().item() <= 0.02 * scale
+    k = 16
+    top = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    cnt = torch.empty(T, dtype=torch.int32, device="cuda")
+    ops.mla_topk(want.cuda(), n_vis.cuda(), k, seq.cuda(), bt.cuda(), 64, top, cnt)
+    torch.cuda.synchronize()
+    sel = ref.select_topk(want, n_vis.long(), k)  # same scores: the same groups, ascending
+    rows_ref = torch.where(sel >= 0, rows.gather(1, sel.long().clamp_min(0)), -1)
+    assert torch.equal(top.cpu().long(), rows_ref)

@@ -368,6 +368,12 @@ cudaError_t mla_indexer_scores(const void* q8, const float* w, int T, const void
                                cudaStream_t stream);
 // q [T, nh, dim] (dim 576: MLA latent + RoPE; 512: DeepSeek-V4.1 rows), cache rows of dim; V = the
 // first 512 dims.  sink: per-head logits added to the softmax denominator (null: none).
+// DeepSeek-V4.1 indexer scores (dsv4_index.cu): q [T, H, 128], w [T, H] bf16, keys [rows, 128] bf16 paged by
+// the block table; scores [T, N] fp32 (-inf past n_vis).  H in {4, 8, 16, 32, 64}.
+cudaError_t dsv4_index_scores(const void* q, const void* w, const void* keys, const int* block_table, int64_t ld_bt,
+                              const int* seq, const int* n_vis, int T, int H, int heads_per_group, float* scores,
+                              int64_t ld_scores, int N, cudaStream_t stream);
+
 // Engram gate (engram.cu): out[t] += sigmoid(<rmsnorm(h_t) w_h, rmsnorm(k_t) w_k> / sqrt(H)) v_t, kv = [k | v].
 cudaError_t engram_gate(const void* h, int64_t ld_h, const void* kv, int64_t ld_kv, const void* wh, const void* wk,
                         float eps, int T, int H, void* out, int64_t ld_out, cudaStream_t stream);

@@ -40,6 +40,9 @@ void gqa_attention_op(const at::Tensor& q, const at::Tensor& cache, const at::Te
                       const at::Tensor& token_seq, const at::Tensor& block_table, int64_t kv_heads, double sm_scale,
                       int64_t splits, at::Tensor& out, const at::Tensor& status);
 void gqa_gate_op(const at::Tensor& attn, const at::Tensor& proj, int64_t nh, at::Tensor& out);
+void dsv4_index_scores_op(const at::Tensor& q, const at::Tensor& w, const at::Tensor& keys,
+                          const at::Tensor& block_table, const at::Tensor& seq, const at::Tensor& n_vis,
+                          int64_t heads_per_group, at::Tensor& scores);
 void engram_gate_op(const at::Tensor& h, const at::Tensor& kv, const at::Tensor& wh, const at::Tensor& wk, double eps,
                     at::Tensor& out);
 void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
@@ -241,7 +244,9 @@ void register_host_bindings(pybind11::module_& m);
   X("gqa_attention(Tensor q, Tensor cache, Tensor ctx_lens, Tensor token_seq, Tensor block_table, "         \
     "int kv_heads, float sm_scale, int splits, Tensor(a!) out, Tensor(b!) status) -> ()")                  \
   X("gqa_gate(Tensor attn, Tensor proj, int nh, Tensor(a!) out) -> ()")                                   \
-  X("engram_gate(Tensor h, Tensor kv, Tensor wh, Tensor wk, float eps, Tensor(a!) out) -> ()")
+  X("engram_gate(Tensor h, Tensor kv, Tensor wh, Tensor wk, float eps, Tensor(a!) out) -> ()")              \
+  X("dsv4_index_scores(Tensor q, Tensor w, Tensor keys, Tensor block_table, Tensor seq, Tensor n_vis, "     \
+    "int heads_per_group, Tensor(a!) scores) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -285,4 +290,5 @@ void register_host_bindings(pybind11::module_& m);
   X("gqa_prep", b200::gqa_prep_op)                    \
   X("gqa_attention", b200::gqa_attention_op)          \
   X("gqa_gate", b200::gqa_gate_op)                    \
-  X("engram_gate", b200::engram_gate_op)
+  X("engram_gate", b200::engram_gate_op)              \
+  X("dsv4_index_scores", b200::dsv4_index_scores_op)

@@ -1018,3 +1018,34 @@ void engram_gate_op(const at::Tensor& h, const at::Tensor& kv, const at::Tensor&
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void dsv4_index_scores_op(const at::Tensor& q, const at::Tensor& w, const at::Tensor& keys,
+                          const at::Tensor& block_table, const at::Tensor& seq, const at::Tensor& n_vis,
+                          int64_t heads_per_group, at::Tensor& scores) {
+  B200_CHECK_CUDA(q);
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(),
+              "dsv4 index scores: q bf16 [T, H, 128] contiguous");
+  const int T = q.size(0), H = q.size(1);
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.numel() >= (int64_t)T * H,
+              "dsv4 index scores: w bf16 [T, H]");
+  TORCH_CHECK(keys.scalar_type() == at::kBFloat16 && keys.is_contiguous() && keys.size(-1) == 128,
+              "dsv4 index scores: keys bf16 [rows, 128]");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2 && block_table.stride(1) == 1,
+              "dsv4 index scores: block_table int32 [S, blocks]");
+  TORCH_CHECK(seq.scalar_type() == at::kInt && seq.numel() >= T && n_vis.scalar_type() == at::kInt &&
+                  n_vis.numel() >= T,
+              "dsv4 index scores: seq / n_vis int32 [T]");
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.dim() == 2 && scores.size(0) >= T &&
+                  scores.stride(1) == 1,
+              "dsv4 index scores: scores fp32 [T, N]");
+  TORCH_CHECK(heads_per_group >= 1 && H % heads_per_group == 0, "dsv4 index scores: rank groups divide the heads");
+  c10::cuda::CUDAGuard g(q.device());
+  B200_LAUNCH(dsv4_index_scores(q.data_ptr(), w.data_ptr(), keys.data_ptr(), block_table.data_ptr<int>(),
+                                block_table.stride(0), seq.data_ptr<int>(), n_vis.data_ptr<int>(), T, H,
+                                (int)heads_per_group, scores.data_ptr<float>(), scores.stride(0),
+                                (int)scores.size(1), cur_stream()));
+}
+
+}  // namespace b200

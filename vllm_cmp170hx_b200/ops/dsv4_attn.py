@@ -9,8 +9,10 @@ denominator).
 
 Rounding points and selection rules are the reference's (oracle/dsv4_attn.py states them; the
 reference's layer is vllm_sm80/models/deepseek_v41/ops/sm80_attn_core.py:783 prepare_layer and
-:848 attend_layer).  Index scores, top-k and the qdq steps run as torch ops on the step's tensors;
-on CPU tensors everything runs on the oracle.
+:848 attend_layer).  On the GPU the index scores run on csrc/dsv4_index.cu (the same rounding chain over
+the paged group keys) and the selection on the canonical top-k kernel; the two-level candidate-block
+selection, the RoPE and the qdq steps run as torch ops on the step's tensors; on CPU tensors everything
+runs on the oracle.
 """
 
 from __future__ import annotations
@@ -188,12 +190,28 @@ class DSv4AttnCore:
             qi = ref.index_q(index_q, pos, self.freqs)
             wi = (index_w.float() * (sp.index_dim ** -0.5 * sp.index_heads ** -0.5)).to(torch.bfloat16)
             N = max(1, max_groups if max_groups is not None else int(n_vis.max()))
+            if q.is_cuda and not sp.candidate_blocks and candidates_in is None:
+                # the scores kernel (csrc/dsv4_index.cu: the rounding chain of ref.indexer_scores over the
+                # paged group keys) and the canonical top-k kernel, straight to group rows through the
+                # block table -- no gathered key tensor, no sorts
+                ops = _ext.ops()
+                scores = torch.empty(T, N, dtype=torch.float32, device=dev)
+                nv = n_vis.to(torch.int32)
+                sq = seq_l.to(torch.int32)
+                bt = block_table.to(torch.int32).contiguous()  # the engine's is int32 already
+                ops.dsv4_index_scores(qi.to(torch.bfloat16).contiguous(), wi.contiguous(), self.idxk, bt,
+                                      sq, nv, sp.index_heads_per_rank, scores)
+                top = torch.empty(T, sp.index_topk, dtype=torch.int32, device=dev)
+                cnt = torch.empty(T, dtype=torch.int32, device=dev)
+                ops.mla_topk(scores, nv, sp.index_topk, sq, bt, 64, top, cnt)
+                idx.append(torch.where(top >= 0, self.G0 + top.long(), -1))
+                N = 0  # nothing left for the host selection below
             # every query scores the groups of its own sequence, in row chunks of bounded size
-            per_row = N * (sp.index_heads * 4 + sp.index_dim * 2 + 16)
+            per_row = max(N, 1) * (sp.index_heads * 4 + sp.index_dim * 2 + 16)
             rc = max(1, (256 << 20) // per_row)
             gi = torch.arange(N, device=dev)
             sels, cbs = [], []
-            for r0 in range(0, T, rc):
+            for r0 in range(0, T if N else 0, rc):
                 r = slice(r0, min(T, r0 + rc))
                 gr = block_table[seq_l[r]][:, gi // 64].long() * 64 + gi % 64  # [rows, N] group rows
                 scores = ref.indexer_scores(qi[r], wi[r], self.idxk[gr], n_vis[r], sp.index_heads_per_rank)
@@ -205,7 +223,8 @@ class DSv4AttnCore:
                 sels.append(torch.where(top >= 0, self.G0 + gr.gather(1, top.clamp_min(0)), -1))
             if candidates_out is not None and cbs:
                 candidates_out.append(torch.cat(cbs))
-            idx.append(torch.cat(sels))
+            if sels:
+                idx.append(torch.cat(sels))
         qr = ref.rotate(q, pos, self.freqs)
         o = attend(qr, self.pool, torch.cat(idx, 1), self.sink, sp.head_dim ** -0.5)
         # the last `ring` positions of each sequence into its ring (distinct ring rows; the others
