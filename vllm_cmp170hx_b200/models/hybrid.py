@@ -202,7 +202,7 @@ class MLAAttention(nn.Module):
         m = self.m
         proj = self.in_proj(x)
         ql, kvl, dr = self.ql, self.kvl, self.dr
-        q_lat = self.q_a_norm(proj[:, :ql].contiguous())
+        q_lat = self.q_a_norm(proj[:, :ql])  # the norm reads the strided rows
         kv = proj[:, ql: ql + kvl + dr]
         k_idx = proj[:, ql + kvl + dr: ql + kvl + dr + m.index_head_dim]
         w_idx = proj[:, ql + kvl + dr + m.index_head_dim:]
@@ -260,7 +260,7 @@ class MLAAttention(nn.Module):
                               ctx.slot_mapping, idx_k, idx_s)
         loc = slice(sp.rank * sp.Tr, (sp.rank + 1) * sp.Tr)
         Tr = sp.Tr
-        q_lat = self.q_a_norm(proj[loc, :ql].contiguous())
+        q_lat = self.q_a_norm(proj[loc, :ql])  # the norm reads the strided rows
         w_idx = proj[loc, ql + kvl + dr + m.index_head_dim:]
         pos_l = pos[loc]
         iq = self.idx_q(q_lat).view(Tr, m.index_n_heads, m.index_head_dim)
