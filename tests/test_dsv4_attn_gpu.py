@@ -110,3 +110,30 @@ def test_index_scores_kernel_matches_rounding_chain(T, H, hpg, N):
     sel = ref.select_topk(want, n_vis.long(), k)  # same scores: the same groups, ascending
     rows_ref = torch.where(sel >= 0, rows.gather(1, sel.long().clamp_min(0)), -1)
     assert torch.equal(top.cpu().long(), rows_ref)
+
+
+@pytest.mark.parametrize("mode,D,heads,norm,inverse", [("fp8", 512, 1, False, False), ("fp8", 512, 8, False, True),
+                                                         ("fp4_e4m3", 512, 1, False, False),
+                                                         ("fp4_pow2", 128, 4, False, False),
+                                                         ("fp4_pow2", 128, 1, True, False),
+                                                         ("none", 512, 16, False, False)])
+def test_row_transform_kernel_matches_oracle(mode, D, heads, norm, inverse):
+    """csrc/dsv4_rot.cu (RMSNorm, RoPE turn in fp64 from fp32 angles, FP8 / FP4 qdq) against the oracle's
+    functions: bit-equal except, with the RMSNorm, where the two sums of squares round apart."""
+    from vllm_cmp170hx_b200.ops.dsv4_attn import rot_qdq
+
+    g = torch.Generator().manual_seed(D + heads)
+    T = 37
+    x = (torch.randn(T, heads, D, generator=g) * 3).bfloat16()
+    if heads == 1:
+        x = x[:, 0]
+    pos = torch.randint(-1, 70000, (T,), generator=g)
+    freqs = 1.0 / (10000.0 ** (torch.arange(32, dtype=torch.float32) / 32))
+    w = (1 + 0.1 * torch.randn(D, generator=g)).bfloat16() if norm else None
+    want = rot_qdq(x, pos, freqs, mode, inverse, w, 1e-6).float()
+    got = rot_qdq(x.cuda(), pos.cuda(), freqs.cuda(), mode, inverse, None if w is None else w.cuda(), 1e-6)
+    torch.cuda.synchronize()
+    got = got.cpu().float()
+    same = (got == want).float().mean().item()
+    print(f"dsv4 row transform {mode}: {same:.4f} bit-equal")
+    assert same > (0.99 if norm else 0.999), same

@@ -374,6 +374,13 @@ cudaError_t dsv4_index_scores(const void* q, const void* w, const void* keys, co
                               const int* seq, const int* n_vis, int T, int H, int heads_per_group, float* scores,
                               int64_t ld_scores, int N, cudaStream_t stream);
 
+// DeepSeek-V4.1 row transforms (dsv4_rot.cu): optional RMSNorm, RoPE turn of the last 2 n_pairs dims at
+// positions[row / heads] (inverse: the opposite turn), then mode 0 (none), 1 (FP8 per 32), 2 (FP4, E4M3 scales
+// per 16) or 3 (FP4, power-of-two scales per 32); rows of D <= 512 bf16 values, D a multiple of 32.
+cudaError_t dsv4_rot_qdq(const void* x, int64_t ld_x, void* out, int64_t ld_out, int rows, int D,
+                         const int64_t* positions, int heads, const float* freqs, int n_pairs, int inverse,
+                         const void* norm_w, float eps, int mode, cudaStream_t stream);
+
 // Engram gate (engram.cu): out[t] += sigmoid(<rmsnorm(h_t) w_h, rmsnorm(k_t) w_k> / sqrt(H)) v_t, kv = [k | v].
 cudaError_t engram_gate(const void* h, int64_t ld_h, const void* kv, int64_t ld_kv, const void* wh, const void* wk,
                         float eps, int T, int H, void* out, int64_t ld_out, cudaStream_t stream);

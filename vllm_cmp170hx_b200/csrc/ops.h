@@ -43,6 +43,9 @@ void gqa_gate_op(const at::Tensor& attn, const at::Tensor& proj, int64_t nh, at:
 void dsv4_index_scores_op(const at::Tensor& q, const at::Tensor& w, const at::Tensor& keys,
                           const at::Tensor& block_table, const at::Tensor& seq, const at::Tensor& n_vis,
                           int64_t heads_per_group, at::Tensor& scores);
+void dsv4_rot_qdq_op(const at::Tensor& x, at::Tensor& out, const at::Tensor& positions, int64_t heads,
+                     const at::Tensor& freqs, bool inverse, const c10::optional<at::Tensor>& norm_w, double eps,
+                     int64_t mode);
 void engram_gate_op(const at::Tensor& h, const at::Tensor& kv, const at::Tensor& wh, const at::Tensor& wk, double eps,
                     at::Tensor& out);
 void kda_forward_op(const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& state_idx,
@@ -246,7 +249,9 @@ void register_host_bindings(pybind11::module_& m);
   X("gqa_gate(Tensor attn, Tensor proj, int nh, Tensor(a!) out) -> ()")                                   \
   X("engram_gate(Tensor h, Tensor kv, Tensor wh, Tensor wk, float eps, Tensor(a!) out) -> ()")              \
   X("dsv4_index_scores(Tensor q, Tensor w, Tensor keys, Tensor block_table, Tensor seq, Tensor n_vis, "     \
-    "int heads_per_group, Tensor(a!) scores) -> ()")
+    "int heads_per_group, Tensor(a!) scores) -> ()")                                                        \
+  X("dsv4_rot_qdq(Tensor x, Tensor(a!) out, Tensor positions, int heads, Tensor freqs, bool inverse, "     \
+    "Tensor? norm_w, float eps, int mode) -> ()")
 
 #define B200_OP_IMPLS(X)                   \
   X("gemm_bf16_out", b200::gemm_bf16_out)  \
@@ -291,4 +296,5 @@ void register_host_bindings(pybind11::module_& m);
   X("gqa_attention", b200::gqa_attention_op)          \
   X("gqa_gate", b200::gqa_gate_op)                    \
   X("engram_gate", b200::engram_gate_op)              \
-  X("dsv4_index_scores", b200::dsv4_index_scores_op)
+  X("dsv4_index_scores", b200::dsv4_index_scores_op)  \
+  X("dsv4_rot_qdq", b200::dsv4_rot_qdq_op)

@@ -1049,3 +1049,31 @@ void dsv4_index_scores_op(const at::Tensor& q, const at::Tensor& w, const at::Te
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+void dsv4_rot_qdq_op(const at::Tensor& x, at::Tensor& out, const at::Tensor& positions, int64_t heads,
+                     const at::Tensor& freqs, bool inverse, const c10::optional<at::Tensor>& norm_w, double eps,
+                     int64_t mode) {
+  B200_CHECK_CUDA(x);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "dsv4 rot: x bf16 [rows, D]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.stride(1) == 1 &&
+                  out.sizes() == x.sizes(),
+              "dsv4 rot: out bf16 like x");
+  const int rows = x.size(0), D = x.size(1);
+  TORCH_CHECK(heads >= 1 && positions.scalar_type() == at::kLong && positions.numel() * heads >= rows,
+              "dsv4 rot: positions int64 [rows / heads]");
+  TORCH_CHECK(freqs.scalar_type() == at::kFloat && freqs.is_contiguous() && 2 * freqs.numel() <= D,
+              "dsv4 rot: freqs fp32 [pairs]");
+  if (norm_w.has_value())
+    TORCH_CHECK(norm_w->scalar_type() == at::kBFloat16 && norm_w->numel() == D && norm_w->is_contiguous(),
+                "dsv4 rot: norm weight bf16 [D]");
+  TORCH_CHECK(D % 32 == 0 && D <= 512 && mode >= 0 && mode <= 3, "dsv4 rot: D a multiple of 32 up to 512, mode 0-3");
+  c10::cuda::CUDAGuard g(x.device());
+  B200_LAUNCH(dsv4_rot_qdq(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), rows, D,
+                           positions.data_ptr<int64_t>(), (int)heads, freqs.data_ptr<float>(), (int)freqs.numel(),
+                           inverse ? 1 : 0, norm_w.has_value() ? norm_w->data_ptr() : nullptr, (float)eps, (int)mode,
+                           cur_stream()));
+}
+
+}  // namespace b200

@@ -11,7 +11,8 @@ Rounding points and selection rules are the reference's (oracle/dsv4_attn.py sta
 reference's layer is vllm_sm80/models/deepseek_v41/ops/sm80_attn_core.py:783 prepare_layer and
 :848 attend_layer).  On the GPU the index scores run on csrc/dsv4_index.cu (the same rounding chain over
 the paged group keys) and the selection on the canonical top-k kernel; the two-level candidate-block
-selection, the RoPE and the qdq steps run as torch ops on the step's tensors; on CPU tensors everything
+selection, the RoPE turns and the FP8 / FP4 qdq steps on csrc/dsv4_rot.cu (one pass per row); the
+ratio-2 pooling and the ring bookkeeping run as torch ops on the step's tensors; on CPU tensors everything
 runs on the oracle.
 """
 
@@ -23,6 +24,34 @@ import torch
 
 from .. import _ext
 from ..oracle import dsv4_attn as ref
+
+
+_ROT_MODES = {"none": 0, "fp8": 1, "fp4_e4m3": 2, "fp4_pow2": 3}
+
+
+def rot_qdq(x: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor, mode: str, inverse: bool = False,
+            norm_w: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
+    """The row transforms of the layer on x [T, D] or [T, heads, D] (bf16): optional RMSNorm, the RoPE turn of
+    the tail at each token's position, then the qdq `mode` ("none", "fp8" per 32, "fp4_e4m3" per 16,
+    "fp4_pow2" per 32).  CUDA: csrc/dsv4_rot.cu in one pass; CPU: the oracle's functions."""
+    if not x.is_cuda:
+        y = ref.rms_norm(x, norm_w, eps) if norm_w is not None else x
+        y = ref.rotate(y, positions, freqs, inverse=inverse)
+        if mode == "fp8":
+            return ref.fp8_qdq(y, 32)
+        if mode == "fp4_e4m3":
+            return ref.fp4_qdq(y, 16, "e4m3")
+        if mode == "fp4_pow2":
+            return ref.fp4_qdq(y, 32, "pow2")
+        return y
+    heads = x.shape[1] if x.dim() == 3 else 1
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    out = torch.empty(x2.shape, dtype=torch.bfloat16, device=x.device)
+    _ext.ops().dsv4_rot_qdq(x2.to(torch.bfloat16), out, positions.to(torch.int64).contiguous(), heads,
+                            freqs.float().contiguous(), inverse, norm_w, eps, _ROT_MODES[mode])
+    return out.view(x.shape)
 
 
 @dataclass
@@ -132,7 +161,14 @@ class DSv4AttnCore:
         g = (torch.div(pos + 1, sp.ratio, rounding_mode="floor") - 1).clamp_min(0)
         gpos = pos + 1 - sp.ratio
         rows = self._group_rows(block_table, seq, g)
-        self.pool[torch.where(closes, self.G0 + rows, self.dummy)] = ref.compressed_kv(latent, gpos, self.freqs)
+        self.pool[torch.where(closes, self.G0 + rows, self.dummy)] = rot_qdq(latent, gpos, self.freqs, "fp4_e4m3")
+        if latent.is_cuda:
+            from . import gemm
+
+            k = gemm(latent.to(torch.bfloat16), self.wk.to(torch.bfloat16))  # fp32 accumulate, bf16 out
+            self.idxk[torch.where(closes, rows, self.kdummy)] = rot_qdq(k, gpos, self.freqs, "fp4_pow2", False,
+                                                                         self.k_norm.to(torch.bfloat16), sp.eps)
+            return
         k = latent.float() @ self.wk.float().t()
         self.idxk[torch.where(closes, rows, self.kdummy)] = ref.index_key(k.to(torch.bfloat16), self.k_norm, gpos,
                                                                           self.freqs, sp.eps)
@@ -166,7 +202,7 @@ class DSv4AttnCore:
         dev = pos.device
         pos = pos.long()
         seq_l = seq.long()
-        wrows = ref.window_kv(kv, pos, self.freqs)
+        wrows = rot_qdq(kv, pos, self.freqs, "fp8")
         self.pool[self.S0:self.S0 + T] = wrows
         if sp.ratio:
             self._write_groups(seq, slot, pos, kv, kv_score, block_table, valid)
@@ -187,7 +223,7 @@ class DSv4AttnCore:
         idx = [widx]
         if sp.ratio:
             n_vis = torch.div(pos + 1, sp.ratio, rounding_mode="floor")
-            qi = ref.index_q(index_q, pos, self.freqs)
+            qi = rot_qdq(index_q, pos, self.freqs, "fp4_pow2")
             wi = (index_w.float() * (sp.index_dim ** -0.5 * sp.index_heads ** -0.5)).to(torch.bfloat16)
             N = max(1, max_groups if max_groups is not None else int(n_vis.max()))
             if q.is_cuda and not sp.candidate_blocks and candidates_in is None:
@@ -225,7 +261,7 @@ class DSv4AttnCore:
                 candidates_out.append(torch.cat(cbs))
             if sels:
                 idx.append(torch.cat(sels))
-        qr = ref.rotate(q, pos, self.freqs)
+        qr = rot_qdq(q, pos, self.freqs, "none")
         o = attend(qr, self.pool, torch.cat(idx, 1), self.sink, sp.head_dim ** -0.5)
         # the last `ring` positions of each sequence into its ring (distinct ring rows; the others
         # into the dummy row)
@@ -234,4 +270,4 @@ class DSv4AttnCore:
             keep = keep & valid
         ring_rows = self.W0 + slot[seq_l].long() * self.ring + pos % self.ring
         self.pool[torch.where(keep, ring_rows, self.dummy)] = wrows
-        return ref.finish_output(o, pos, self.freqs)
+        return rot_qdq(o, pos, self.freqs, "fp8", inverse=True)
