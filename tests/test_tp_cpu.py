@@ -87,16 +87,18 @@ def test_tp2_matches_tp1(fmt):
     assert got == ref
 
 
-def _pp_worker(rank, world, port, fmt, tp, path):
+def _pp_worker(rank, world, port, fmt, tp, path, env=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), **(env or {}))
     from vllm_cmp170hx_b200.parallel import state as pstate
 
     pstate.init(tp_size=tp, pp_size=world // tp, device="cpu", timeout_s=120)
     toks = _generate(tp, fmt, world // tp)
     if rank == 0:
+        from vllm_cmp170hx_b200.engine.runner import ModelRunner
+
         with open(path, "w") as f:
-            json.dump(toks, f)
+            json.dump({"tokens": toks, "split_events": ModelRunner.split_draft_events} if env else toks, f)
     pstate.destroy()
 
 
@@ -118,6 +120,25 @@ def test_pp2_matches_pp1(fmt, tp):
         with open(path) as f:
             got = json.load(f)
     assert got == ref
+
+
+@pytest.mark.parametrize("fmt", ["deepseek_mtp", "exl3_dflash"])
+def test_pp2_split_draft_event_matches_pp1(fmt):
+    """Split draft event: the last stage's drafts travel by an asynchronous broadcast that the first
+    stage waits for only before its next forward; the other stages schedule on draft counts alone.
+    Greedy outputs equal one stage's, and the asynchronous path ran."""
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    ref = _generate(1, fmt)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.json")
+        port = 29700 + os.getpid() % 1000
+        mp.start_processes(_pp_worker, args=(2, port, fmt, 1, path, {"VLLM_B200_PP_SPLIT_DRAFTS": "1"}), nprocs=2,
+                           join=True, start_method="spawn")
+        with open(path) as f:
+            got = json.load(f)
+    assert got["tokens"] == ref and got["split_events"] > 0
 
 
 @pytest.mark.parametrize("fmt", ["exl3", "deepseek_mtp"])

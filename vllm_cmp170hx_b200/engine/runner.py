@@ -590,6 +590,7 @@ class ModelRunner:
                 mb_ctx.append((mb, ctx))
             nbytes += nb
             if m.first:
+                self._apply_pp_drafts(mb, dev["ids"])
                 res = m(dev["ids"], ctx)
             elif hc:
                 # hyper-connection streams: the whole mHC state as one packed uint8 message
@@ -618,6 +619,9 @@ class ModelRunner:
                                                 self._sample_bans(mb)))
         for w, _ in sends:
             w.wait()
+        if self._pp_drafts is not None:  # taken by this step; the other stages retire the broadcast here
+            self._pp_drafts[2].wait()
+            self._pp_drafts = None
         self.step_counter += 1
         last = st.pp_peer(st.pp_size - 1)
         if self._spec_enabled_elsewhere():
@@ -750,6 +754,9 @@ class ModelRunner:
             self._pp_hidden = []
             if self._pp_last_out is None:
                 return
+            if self._split_drafts_on():
+                self._pp_drafts_async(self._pp_last_out, drafts)
+                return
             got = self._pp_broadcast_lists(self._pp_last_out, drafts, self.cfg.scheduler.num_speculative_tokens)
             if self.spec is None:
                 for s in self._pp_last_out.reqs:
@@ -765,6 +772,70 @@ class ModelRunner:
 
     _pp_last_out = None
     _pp_last_res: dict = {}
+    _pp_drafts = None  # split draft event: (request -> row, the broadcast int64 [requests, 1 + k], its work)
+    split_draft_events = 0  # asynchronous draft broadcasts this process issued (all runners)
+
+    def _split_drafts_on(self) -> bool:
+        """Split draft event (the reference's VLLM_PP_SPLIT_DRAFT_EVENT, vllm_sm80/worker/pp_handler.py:7-10,
+        applied in runner_hooks.py:148-160): usable when every stage can name each request's draft count
+        without the drafts (no verify-depth cut that depends on device features, no n-gram tables hashed
+        from the tokens on the host)."""
+        from .. import envs
+
+        pol = getattr(self.spec, "depth", None) if self.spec is not None else None
+        masked = self.cfg.scheduler.depth_mode == "mask" or (pol is None and not self.cfg.scheduler.depth_policy
+                                                            and not envs.get("VLLM_B200_ADAPTIVE_DEPTH"))
+        return bool(envs.get("VLLM_B200_PP_SPLIT_DRAFTS")) and masked and not self._ngram_sources()
+
+    def _pp_drafts_async(self, out: SchedulerOutput, drafts: dict | None) -> None:
+        """Send the last stage's drafts over the stage column without waiting; the other stages set each
+        continuing request's draft count now (placeholder ids) and the first stage takes the ids from the
+        broadcast right before its next forward."""
+        import torch.distributed as dist
+
+        st = self.st
+        k = self.cfg.scheduler.num_speculative_tokens
+        rids = [s.req.request_id for s in out.reqs]
+        buf = torch.full((len(rids), 1 + k), -1, dtype=torch.int64)
+        if drafts is not None:
+            for i, rid in enumerate(rids):
+                v = drafts.get(rid)
+                if v is not None:
+                    buf[i, 0] = len(v)
+                    buf[i, 1:1 + len(v)] = torch.tensor(v[:k], dtype=torch.int64)
+        dev = buf.to(self.device) if self.device.type == "cuda" else buf
+        work = dist.broadcast(dev, src=st.pp_peer(st.pp_size - 1), group=st.pp_group if self.device.type == "cuda"
+                              else st.pp_cpu_group, async_op=True)
+        self._pp_drafts = ({rid: i for i, rid in enumerate(rids)}, dev, work)
+        ModelRunner.split_draft_events += 1
+        if self.spec is None:
+            for s in out.reqs:
+                req = s.req
+                # the drafter's own count rule: requests that keep decoding draft min(k, room) tokens
+                if req.status.finished or req.num_computed_tokens != req.num_tokens - 1:
+                    continue
+                room = max(0, req.params.max_tokens - len(req.output_token_ids) - 1)
+                req.draft_token_ids = [-1] * max(0, min(k, room))
+
+    def _apply_pp_drafts(self, mb: SchedulerOutput, ids: torch.Tensor) -> None:
+        """First stage, split draft event: wait for the drafts' broadcast on the stream (as late as
+        possible) and put the ids into this micro-batch's input rows."""
+        if self._pp_drafts is None:
+            return
+        row_of, buf, work = self._pp_drafts
+        work.wait()
+        dst, src = [], []
+        t = 0
+        w = buf.shape[1]
+        for s in mb.reqs:
+            r = row_of.get(s.req.request_id)
+            if s.num_draft and r is not None:
+                for j in range(s.num_draft):  # drafts follow the request's first token of the step
+                    dst.append(t + 1 + j)
+                    src.append(r * w + 1 + j)
+            t += s.num_new
+        if dst:
+            ids[self._to_dev(np.asarray(dst, dtype=np.int64))] = buf.view(-1)[self._to_dev(np.asarray(src, dtype=np.int64))]
 
     def _pp_accepted(self, mb) -> dict:
         return {s.req.request_id: self._pp_last_res.get(s.req.request_id, []) for s in mb.reqs}

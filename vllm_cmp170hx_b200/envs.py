@@ -63,6 +63,9 @@ _declare("VLLM_B200_KDA_PREFILL", str, "chunked", "KDA prefill: 'chunked' (seque
 _declare("VLLM_B200_SPARSE_MLA_SPLITS", int, 0, "position splits of the sparse-MLA attention (0 = auto)")
 _declare("VLLM_B200_SHARED_EXPERT_STREAM", _bool, False, "MoE layers run the shared expert on a second CUDA stream "
          "beside the routed experts' assignment and rotation, joined before the combine (read by models/hybrid.py)")
+_declare("VLLM_B200_PP_SPLIT_DRAFTS", _bool, False, "pipeline parallel speculative decoding: the drafts reach the "
+         "other stages by an asynchronous broadcast waited for right before the first stage's forward, the draft "
+         "counts (known on every stage) schedule the step meanwhile (read by engine/runner.py)")
 _declare("VLLM_B200_MLA_DP", _bool, True, "with expert parallelism, sparse-MLA layers hold all heads and attend "
          "data-parallel (each rank its own tokens) in the sequence-parallel layout")
 # --- scheduling ---------------------------------------------------------------------------------
@@ -110,6 +113,7 @@ ALIASES = {
     "VLLM_HOT_SWAP": "VLLM_B200_HOT_SWAP",
     "VLLM_TOOL_CHOICE_NONE_MASK": "VLLM_B200_TOOL_CHOICE_NONE_MASK",
     "VLLM_EXL3_PLE_READ_RETRIES": "VLLM_B200_PLE_READ_RETRIES",
+    "VLLM_PP_SPLIT_DRAFT_EVENT": "VLLM_B200_PP_SPLIT_DRAFTS",
 }
 
 # reference switches whose behaviour is always on here (no switch): accepted, warned about
