@@ -98,7 +98,8 @@ def _pp_worker(rank, world, port, fmt, tp, path, env=None):
         from vllm_cmp170hx_b200.engine.runner import ModelRunner
 
         with open(path, "w") as f:
-            json.dump({"tokens": toks, "split_events": ModelRunner.split_draft_events} if env else toks, f)
+            json.dump({"tokens": toks, "split_events": ModelRunner.split_draft_events,
+                       "tail_steps": ModelRunner.draft_tail_steps} if env else toks, f)
     pstate.destroy()
 
 
@@ -139,6 +140,24 @@ def test_pp2_split_draft_event_matches_pp1(fmt):
         with open(path) as f:
             got = json.load(f)
     assert got["tokens"] == ref and got["split_events"] > 0
+
+
+def test_pp2_draft_tail_on_first_stage_matches_pp1():
+    """Pipeline draft tail: the last stage runs the DFlash block forward and sends its hidden states
+    to stage 0, which holds a copy of the lm_head shard, picks the drafts and roots their broadcast.
+    Greedy outputs equal one stage's, and the tail ran on stage 0."""
+    from vllm_cmp170hx_b200.parallel import state as pstate
+
+    pstate.set_state(pstate.ParallelState())
+    ref = _generate(1, "exl3_dflash")
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.json")
+        port = 30700 + os.getpid() % 1000
+        mp.start_processes(_pp_worker, args=(2, port, "exl3_dflash", 1, path, {"VLLM_B200_PP_DRAFT_TAIL_STAGE": "0"}),
+                           nprocs=2, join=True, start_method="spawn")
+        with open(path) as f:
+            got = json.load(f)
+    assert got["tokens"] == ref and got["tail_steps"] > 0
 
 
 @pytest.mark.parametrize("fmt", ["exl3", "deepseek_mtp"])

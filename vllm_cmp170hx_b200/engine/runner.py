@@ -645,10 +645,12 @@ class ModelRunner:
             _ext.check_status(self.device)
         return res
 
-    def _pp_broadcast_lists(self, out: SchedulerOutput, lists: dict | None, width: int) -> dict[str, list[int]]:
+    def _pp_broadcast_lists(self, out: SchedulerOutput, lists: dict | None, width: int,
+                            src_stage: int = -1) -> dict[str, list[int]]:
         """Token lists per request (accepted tokens of a verify step, or drafts) from the last pipeline
-        stage to every stage of this TP column, as one int64 device tensor [requests, 1 + width] (count,
-        tokens) in the step's request order, which every rank's scheduler shares: no pickled objects."""
+        stage (or ``src_stage``) to every stage of this TP column, as one int64 device tensor
+        [requests, 1 + width] (count, tokens) in the step's request order, which every rank's scheduler
+        shares: no pickled objects."""
         import torch.distributed as dist
 
         st = self.st
@@ -661,8 +663,8 @@ class ModelRunner:
                     buf[i, 0] = len(v)
                     buf[i, 1:1 + len(v)] = torch.tensor(v[:width], dtype=torch.int64)
         dev = buf.to(self.device) if self.device.type == "cuda" else buf
-        dist.broadcast(dev, src=st.pp_peer(st.pp_size - 1), group=st.pp_group if self.device.type == "cuda"
-                       else st.pp_cpu_group)
+        src = st.pp_size - 1 if src_stage < 0 else src_stage
+        dist.broadcast(dev, src=st.pp_peer(src), group=st.pp_group if self.device.type == "cuda" else st.pp_cpu_group)
         host = dev.cpu().tolist()
         return {rid: row[1:1 + row[0]] for rid, row in zip(rids, host) if row[0] >= 0}
 
@@ -745,6 +747,8 @@ class ModelRunner:
             import torch.distributed as dist
 
             drafts = None
+            if self._pp_last_out is not None and self._tail_step(self._pp_last_out):
+                return self._propose_tail()
             if self.spec is not None:
                 for mb, hidden, aux in self._pp_hidden:
                     self.model.aux_hidden = aux
@@ -786,6 +790,90 @@ class ModelRunner:
         masked = self.cfg.scheduler.depth_mode == "mask" or (pol is None and not self.cfg.scheduler.depth_policy
                                                             and not envs.get("VLLM_B200_ADAPTIVE_DEPTH"))
         return bool(envs.get("VLLM_B200_PP_SPLIT_DRAFTS")) and masked and not self._ngram_sources()
+
+    # ------------------------------------------------------------------ pipeline draft tail
+    _tail_head = None  # tail stage: the lm_head shard received from the last stage
+    _tail_sent = False  # last stage: the lm_head shard went to the tail stage
+    draft_tail_steps = 0  # steps whose drafts a tail stage picked (all runners of this process)
+
+    def _tail_stage(self) -> int:
+        """The stage computing the DFlash drafter's tail (the reference's VLLM_PP_DRAFT_TAIL_STAGE,
+        vllm_sm80/worker/pp_handler.py:11-14 and worker/pp_draft_tail.py), or -1.  The block drafter's
+        forward stays beside the target's last layers (it reads their auxiliary states); the tail --
+        the lm_head over k rows per request and the picks -- moves to a stage that is otherwise idle
+        while the last stage finishes, which roots the drafts' broadcast."""
+        from .. import envs
+
+        v = int(envs.get("VLLM_B200_PP_DRAFT_TAIL_STAGE"))
+        sch = self.cfg.scheduler
+        if (v < 0 or v >= self.st.pp_size - 1 or sch.spec_method != "dflash" or sch.depth_policy
+                or envs.get("VLLM_B200_ADAPTIVE_DEPTH") or self._ngram_sources()):
+            return -1
+        return v
+
+    def _tail_reqs(self, out: SchedulerOutput) -> list:
+        """The requests that keep decoding after the step (the drafter's rule, on every stage)."""
+        return [s.req for s in out.reqs if not s.req.status.finished
+                and s.req.num_computed_tokens == s.req.num_tokens - 1]
+
+    def _tail_step(self, out: SchedulerOutput) -> bool:
+        """The tail moves this step: a tail stage is set and every drafting request picks greedily (a
+        sampled draft's probabilities must stay beside the verifier on the last stage)."""
+        return self._tail_stage() >= 0 and all(q.params.temperature <= 0 for q in self._tail_reqs(out))
+
+    def _propose_tail(self) -> None:
+        """Last stage: the block forward per micro-batch, its hidden states [A, k, H] to the tail stage
+        (with the lm_head shard once, the first time).  Tail stage: the logits and greedy picks, then the
+        drafts' broadcast from there; every stage stores the drafts it receives."""
+        import torch.distributed as dist
+
+        st = self.st
+        out = self._pp_last_out
+        tail = self._tail_stage()
+        k = self.cfg.scheduler.num_speculative_tokens
+        grp = st.pp_group
+        areqs = self._tail_reqs(out)
+        H = self.mcfg.hidden_size
+        drafts = None
+        if self.spec is not None:  # last stage
+            parts = []
+            for mb, hidden, aux in self._pp_hidden:
+                self.model.aux_hidden = aux
+                got = self.spec.propose(mb, hidden, self._pp_accepted(mb), defer_tail=True)
+                if got is not None:
+                    parts.append(got[1])
+            self._pp_hidden = []
+            if not self._tail_sent:
+                dist.send(self.model.lm_head.weight.data.contiguous(), dst=st.pp_peer(tail), group=grp)
+                self._tail_sent = True
+            if areqs:
+                h = torch.cat(parts).contiguous()
+                assert h.shape == (len(areqs), k, H), "the drafter's requests differ from the stage's rule"
+                dist.send(h, dst=st.pp_peer(tail), group=grp)
+        elif st.pp_rank == tail:
+            if self._tail_head is None:
+                w = torch.empty(self.model.vocab_local, H, dtype=torch.bfloat16, device=self.device)
+                dist.recv(w, src=st.pp_peer(st.pp_size - 1), group=grp)
+                from ..models.layers import Linear
+
+                self._tail_head = Linear(w)
+            if areqs:
+                from .spec_decode import _SEED_DRAFT, _sample
+
+                h = torch.empty(len(areqs), k, H, dtype=torch.bfloat16, device=self.device)
+                dist.recv(h, src=st.pp_peer(st.pp_size - 1), group=grp)
+                picks = [_sample(self._tail_head(h[:, j].contiguous()), None, self.cfg.seed ^ (_SEED_DRAFT + j),
+                                 self.step_counter, self.model.vocab_offset) for j in range(k)]
+                dh = torch.stack(picks, dim=1).cpu().tolist()
+                drafts = {}
+                for a, req in enumerate(areqs):
+                    room = max(0, req.params.max_tokens - len(req.output_token_ids) - 1)
+                    drafts[req.request_id] = [int(v) for v in dh[a][:max(0, min(k, room))]]
+        got = self._pp_broadcast_lists(out, drafts, k, src_stage=tail)
+        ModelRunner.draft_tail_steps += 1
+        for req in areqs:
+            req.draft_token_ids = list(got.get(req.request_id, []))
+            req.draft_live = -1
 
     def _pp_drafts_async(self, out: SchedulerOutput, drafts: dict | None) -> None:
         """Send the last stage's drafts over the stage column without waiting; the other stages set each

@@ -213,14 +213,17 @@ class SpecDecoder:
         return res
 
     # ------------------------------------------------------------------ proposal
-    def propose(self, out, hidden: torch.Tensor, accepted: dict[str, list[int]]) -> None:
-        """Set ``draft_token_ids`` of the step's unfinished requests (call after the scheduler update)."""
+    def propose(self, out, hidden: torch.Tensor, accepted: dict[str, list[int]], defer_tail: bool = False):
+        """Set ``draft_token_ids`` of the step's unfinished requests (call after the scheduler update).
+        ``defer_tail`` (DFlash, pipeline draft tail): stop after the block forward and return the
+        requests that keep decoding with the block's hidden states [A, k, H], whose logits and picks
+        another stage computes."""
         r = self.runner
         dev = r.device
         for s in out.reqs:
             self.q_store.pop(s.req.request_id, None)
         if self.dflash is not None:
-            return self._propose_dflash(out, accepted)
+            return self._propose_dflash(out, accepted, defer_tail)
         ids, pos, hrows, tseq, reqs = [], [], [], [], []
         last = []
         t = 0
@@ -313,7 +316,7 @@ class SpecDecoder:
         b = req.block_ids
         return b[p // 64] * 64 + p % 64 if p // 64 < len(b) else -1
 
-    def _propose_dflash(self, out, accepted: dict[str, list[int]]) -> None:
+    def _propose_dflash(self, out, accepted: dict[str, list[int]], defer_tail: bool = False):
         """DFlash: store the context rows this step verified, then draft all k tokens of every
         request that keeps decoding with one block forward."""
         r = self.runner
@@ -350,6 +353,8 @@ class SpecDecoder:
         ctx_slots = torch.where(p[None] <= lt[:, None], cs, -1)
         bonus = torch.tensor([q.token_at(q.num_computed_tokens) for q in areqs], device=dev)
         h = d(bonus, torch.tensor(last, device=dev), ctx_slots, ctx_slots >= 0, self.dcaches, self.k)
+        if defer_tail:
+            return areqs, h
         temps_l = [q.params.temperature for q in areqs]
         temps = torch.tensor(temps_l, dtype=torch.float32, device=dev) if any(v > 0 for v in temps_l) else None
         samp = [i for i, v in enumerate(temps_l) if v > 0]

@@ -66,6 +66,9 @@ _declare("VLLM_B200_SHARED_EXPERT_STREAM", _bool, False, "MoE layers run the sha
 _declare("VLLM_B200_PP_SPLIT_DRAFTS", _bool, False, "pipeline parallel speculative decoding: the drafts reach the "
          "other stages by an asynchronous broadcast waited for right before the first stage's forward, the draft "
          "counts (known on every stage) schedule the step meanwhile (read by engine/runner.py)")
+_declare("VLLM_B200_PP_DRAFT_TAIL_STAGE", int, -1, "pipeline parallel DFlash drafting: the stage (below the last) "
+         "that computes the drafter's tail -- the lm_head over the block's hidden states and the greedy picks -- and "
+         "roots the drafts' broadcast; -1 keeps it on the last stage (read by engine/runner.py)")
 _declare("VLLM_B200_MLA_DP", _bool, True, "with expert parallelism, sparse-MLA layers hold all heads and attend "
          "data-parallel (each rank its own tokens) in the sequence-parallel layout")
 # --- scheduling ---------------------------------------------------------------------------------
@@ -114,6 +117,7 @@ ALIASES = {
     "VLLM_TOOL_CHOICE_NONE_MASK": "VLLM_B200_TOOL_CHOICE_NONE_MASK",
     "VLLM_EXL3_PLE_READ_RETRIES": "VLLM_B200_PLE_READ_RETRIES",
     "VLLM_PP_SPLIT_DRAFT_EVENT": "VLLM_B200_PP_SPLIT_DRAFTS",
+    "VLLM_PP_DRAFT_TAIL_STAGE": "VLLM_B200_PP_DRAFT_TAIL_STAGE",
 }
 
 # reference switches whose behaviour is always on here (no switch): accepted, warned about
