@@ -27,6 +27,7 @@ except ImportError:  # pragma: no cover
     Request = object
 
 from ..config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig
+from ..engine.depth_hint import certain_output
 from ..engine.llm_engine import LLMEngine
 from ..engine.request import SamplingParams
 from ..engine.spmd import Control, SPMDEngine
@@ -185,6 +186,7 @@ def build_app(engine: AsyncEngine, tokenizer, model_name: str, parser: str | Non
         ids = tokenizer.apply_chat_template(messages)
         params = _params(body)
         params.bad_token_ids = parsers.tool_choice_none_bans(family, body, tokenizer)
+        params.certain_output = certain_output(body)
         tools, tool_choice = body.get("tools"), body.get("tool_choice", "auto")
         think_open = _think_open_in_prompt(tokenizer, ids)
         cid = "chatcmpl-" + uuid.uuid4().hex[:24]

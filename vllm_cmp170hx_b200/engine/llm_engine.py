@@ -69,6 +69,12 @@ class LLMEngine:
 
             self.adaptive_k = AdaptiveKPolicy(cfg.scheduler.num_speculative_tokens,
                                               mode if mode in ("by_load", "accept") else "by_load")
+        self.depth_hint = None
+        if cfg.scheduler.num_speculative_tokens > 0:
+            from .. import envs
+            from .depth_hint import DepthHint
+
+            self.depth_hint = DepthHint.parse(envs.get("VLLM_B200_DEPTH_HINT"))
         self.requests: dict[str, Request] = {}
         self.num_steps = 0
         self.k_hist: dict[int, int] = {}  # draft count chosen per step (adaptive k) -> steps
@@ -297,6 +303,11 @@ class LLMEngine:
             self.scheduler.draft_cap = self.adaptive_k.choose(len(self.scheduler.running))
             k = self.scheduler.draft_cap
             self.k_hist[k] = self.k_hist.get(k, 0) + 1
+        if self.depth_hint is not None:
+            sch = self.scheduler
+            cap = sch.draft_cap if self.adaptive_k is not None else self.cfg.scheduler.num_speculative_tokens
+            decoding = [r for r in sch.running if r.num_computed_tokens == r.num_tokens - 1]
+            sch.draft_cap = self.depth_hint.select(decoding, len(sch.running) + len(sch.waiting), cap)
         out = self.scheduler.schedule()
         if not out.reqs:
             return []
@@ -305,6 +316,11 @@ class LLMEngine:
     def _execute_sync(self, out) -> list[RequestOutput]:
         before = {s.req.request_id: len(s.req.output_token_ids) for s in out.reqs}
         sampled = self.runner.execute(out)
+        if self.depth_hint is not None:
+            for s in out.reqs:
+                if s.num_draft:
+                    self.depth_hint.observe(s.req.request_id, s.num_draft,
+                                            max(0, len(sampled.get(s.req.request_id, [])) - 1))
         self.scheduler.update(out, sampled)
         self.runner.propose()
         self.num_steps += 1
@@ -318,6 +334,8 @@ class LLMEngine:
                                          r.status.value.replace("finished_", "") if r.status.finished else None, new))
             if r.status.finished:
                 self.requests.pop(r.request_id, None)
+                if self.depth_hint is not None:
+                    self.depth_hint.forget(r.request_id)
         return res
 
 

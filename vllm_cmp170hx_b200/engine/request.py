@@ -18,6 +18,8 @@ class SamplingParams:
     seed: int | None = None
     # tokens that are never sampled (at most 4; e.g. a parser's tool-call opener under tool_choice="none")
     bad_token_ids: list[int] = field(default_factory=list)
+    # the output is a tool call or JSON by the request's own fields (a verify-width hint; chat endpoint)
+    certain_output: bool = False
 
 
 class Status(enum.Enum):

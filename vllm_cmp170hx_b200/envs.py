@@ -75,6 +75,8 @@ _declare("VLLM_B200_MLA_DP", _bool, True, "with expert parallelism, sparse-MLA l
 _declare("VLLM_B200_FAIR_PREFILL_SHORT_BYPASS", int, 0, "prompts up to this length skip the partial-prefill cap")
 _declare("VLLM_B200_ADAPTIVE_K", str, "", "adaptive draft count policy ('' off, 'by_load', 'accept')")
 _declare("VLLM_B200_ADAPTIVE_DEPTH", str, "", "per-request verify depth policy file (dspark-depth-policy/1)")
+_declare("VLLM_B200_DEPTH_HINT", str, "", "verify width per step from the requests' last rounds: 'full=W,..;base=W,..' "
+         "indexed by the requests held (read by engine/llm_engine.py)")
 _declare("VLLM_B200_OVERRIDE", str, "", "override sidecar manifest restoring plain tensors at source precision")
 _declare("VLLM_B200_NO_PDL", bool, False, "launch kernels without programmatic dependent launch (profiling: each kernel charged its own time)")
 _declare("VLLM_B200_OVERRIDE_SHA256", str, "", "pinned sha256 of the override manifest")
@@ -101,6 +103,7 @@ _declare("VLLM_B200_HOT_SWAP", str, "", "dev: swap implementation pairs between 
 ALIASES = {
     "VLLM_SM80_ALLREDUCE": "VLLM_B200_ALLREDUCE",
     "VLLM_DSPARK_ADAPTIVE_DEPTH": "VLLM_B200_ADAPTIVE_DEPTH",
+    "VLLM_DSPARK_DEPTH_HINT": "VLLM_B200_DEPTH_HINT",
     "VLLM_EXL3_OVERRIDE": "VLLM_B200_OVERRIDE",
     "VLLM_EXL3_OVERRIDE_SHA256": "VLLM_B200_OVERRIDE_SHA256",
     "VLLM_SM80_LIGHT_TIMING": "VLLM_B200_LIGHT_TIMING",
