@@ -196,3 +196,81 @@ def test_row_mask_mode_keeps_the_verify_width_and_matches_plain(tmp_path, bias):
     assert widths and widths.count(3) >= len(widths) // 2
     if bias < -10:  # all drafts masked: nothing is a candidate, yet the rows were verified
         assert llm.engine.runner.spec.stats["accepted"] == 0
+
+
+def _hw_raw(**block):
+    hw = {"estimate": "stale", "lag_rounds": 1, "k_choices": [1, 2, 3], "fallback_k": 2, "batch_sizes": [2, 3],
+          "t0_ms": {"2": 10.0, "3": 12.0}, "cum_ms": {"2": [0, 1, 2, 3], "3": [0, 1.5, 3, 4.5]},
+          "s": {"2": {"1": 1.0, "2": 0.5, "3": 0.5}, "3": {"1": 1.0, "2": 1.0, "3": 1.0}}}
+    hw.update(block)
+    return {"tau": {"2": 0.3, "3": 0.3}, "host_width": hw}
+
+
+def _hw_brute(hw, q_rows, b, cap):
+    """The objective evaluated term by term, over the K of k_choices at most cap."""
+    best = None
+    for K in [k for k in hw.k_choices if k <= cap]:
+        E, gap = 0.0, 0.0
+        for q in q_rows:
+            d = max([k for k in range(1, K + 1) if math.prod(q[:k]) >= hw.tau[b]], default=0)
+            E += 1 + sum(math.prod(q[:i]) for i in range(1, d + 1))
+            gap += hw.cum[b][K] - hw.cum[b][d]
+        score = E / (hw.t0[b] + b * hw.cum[b][K] - (1 - hw.share[b][K]) * gap)
+        if best is None or score > best[0] + 1e-12:
+            best = (score, K)
+    return best[1]
+
+
+def test_host_width_block_parse_and_choice():
+    """The policy's host_width block: validation, the K its objective picks (checked against the
+    objective evaluated term by term), the fallback for a request without an earlier round, ties to
+    the smaller K, and batch sizes outside the block keeping their width."""
+    pol = _pol(**_hw_raw())
+    hw = pol.host_width
+    assert hw is not None and hw.k_choices == (1, 2, 3) and hw.lag == 1
+    for bad in ({"estimate": "fresh"}, {"lag_rounds": 0}, {"fallback_k": 5}, {"batch_sizes": [1, 2]},
+                {"cum_ms": {"2": [0, 1, 2], "3": [0, 1, 2, 3]}}, {"cum_ms": {"2": [0, 2, 1, 3], "3": [0, 1, 2, 3]}},
+                {"s": {"2": {"1": 1.0}, "3": {"1": 1.0, "2": 1.0, "3": 1.0}}}, {"t0_ms": {"2": 0, "3": 1}}):
+        with pytest.raises(ValueError):
+            _pol(**_hw_raw(**bad))
+    gen = torch.Generator().manual_seed(0)
+    for _ in range(40):
+        b = 2 + int(torch.randint(0, 2, (1,), generator=gen))
+        q = torch.rand(b, 3, generator=gen).tolist()
+        for cap in (3, 2):
+            assert hw.choose(q, b, cap) == _hw_brute(hw, q, b, cap)
+    assert hw.choose([[0.9, 0.9, 0.9], None], 2, 3) == 2  # fallback_k
+    assert hw.choose([[0.9, 0.9, 0.9]] * 4, 4, 3) is None  # b outside the block
+    # every draft below tau: d = 0 for all K, E = 1; the cost grows with K unless shares cancel it
+    assert hw.choose([[0.01] * 3] * 3, 3, 3) == 1
+
+
+def test_host_width_in_the_engine_matches_plain(tmp_path):
+    """A policy with a host_width block steers decode steps of two or three requests by their p_i
+    rows of the round before; greedy outputs stay those of plain decoding."""
+    pstate.set_state(pstate.ParallelState())
+    path = tmp_path / "policy.json"
+    raw = {"schema": "dspark-depth-policy/1", "max_depth": 3, "features": ["bias", "logit_conf"],
+           "weights": [[1.0, 0.2]] * 3,
+           "costs": {"1": {"0": 10, "1": 10.5, "2": 11, "3": 11.5}, "4": {"0": 10, "1": 11, "2": 12, "3": 13}}}
+    raw.update(_hw_raw())
+    path.write_text(json.dumps(raw))
+    prompts = [[(5 * i + 3 * j) % 500 for j in range(n)] for i, n in enumerate([9, 40, 71])]
+    model = HybridForCausalLM(_cfg(0).model, "cpu", seed=3)
+    plain = LLM(_cfg(0), model).generate(prompts, SamplingParams(max_tokens=10))
+    llm = LLM(_cfg(3, str(path)), model)
+    eng = llm.engine
+    caps = []
+    orig = eng._host_width
+
+    def host_width():
+        orig()
+        caps.append(eng.scheduler.draft_cap)
+
+    eng._host_width = host_width
+    got = llm.generate(prompts, SamplingParams(max_tokens=10))
+    model.aux_layer_ids = ()
+    assert [o.output_token_ids for o in got] == [o.output_token_ids for o in plain]
+    spec = eng.runner.spec
+    assert spec.depth.host_width is not None and caps and all(1 <= c <= 3 for c in caps)
+    assert not spec.p_rounds  # finished requests' rows are dropped

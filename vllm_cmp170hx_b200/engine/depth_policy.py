@@ -32,6 +32,7 @@ output equals the unmasked output truncated at `live`.
 from __future__ import annotations
 
 import json
+import math
 from dataclasses import dataclass
 
 import torch
@@ -54,6 +55,120 @@ def _interp(table: dict[int, float], b: int) -> float:
     raise AssertionError
 
 
+@dataclass(frozen=True)
+class HostWidth:
+    """The policy's optional ``host_width`` block: the verify width K of a decode step of b requests
+    (b in ``batch_sizes``), chosen on the host from each request's p_i of its verify round
+    ``lag_rounds`` back (the reference's DSpark host width, vllm_sm80/spec_decode/dspark_host_width.py:
+    1-31; same block format so policy files load unchanged).  K in ``k_choices`` maximises
+
+        sum_r E(q_r, d_r(K)) / T(b, K | d)
+        d_r(K)      = the largest k <= K with prod_{j <= k} q_rj >= tau[b]   (0 if none)
+        E(q, d)     = 1 + sum_{i <= d} prod_{j <= i} q_j
+        T(b, K | d) = t0_ms[b] + b cum_ms[b][K] - (1 - s[b][K]) sum_r (cum_ms[b][K] - cum_ms[b][d_r])
+
+    ties to the smaller K; ``fallback_k`` when a request has no such round."""
+
+    batch_sizes: frozenset
+    lag: int
+    fallback_k: int
+    k_choices: tuple  # ascending
+    t0: dict
+    cum: dict  # b -> (cum_ms at k = 0 .. max K)
+    share: dict  # b -> {K: s}
+    tau: dict
+
+    @staticmethod
+    def parse(raw: dict, where: str = "policy") -> "HostWidth":
+        block = raw.get("host_width")
+        if not isinstance(block, dict):
+            raise ValueError(f"{where}: host_width must be an object")
+        if block.get("estimate") != "stale":
+            raise ValueError(f"{where}: host_width estimate must be 'stale' (p_i of an earlier round)")
+
+        def ints(name):
+            v = block.get(name)
+            if (not isinstance(v, list) or not v or len(set(v)) != len(v)
+                    or any(not isinstance(x, int) or isinstance(x, bool) or x < 1 for x in v)):
+                raise ValueError(f"{where}: host_width {name} must be distinct positive integers: {v!r}")
+            return tuple(sorted(v))
+
+        def num(name, v):
+            try:
+                f = float(v)
+            except (TypeError, ValueError):
+                raise ValueError(f"{where}: host_width {name} is not a number: {v!r}") from None
+            if not math.isfinite(f):
+                raise ValueError(f"{where}: host_width {name} is not finite: {v!r}")
+            return f
+
+        lag = block.get("lag_rounds")
+        if not isinstance(lag, int) or isinstance(lag, bool) or lag < 1:
+            raise ValueError(f"{where}: host_width lag_rounds must be a positive integer: {lag!r}")
+        ks = ints("k_choices")
+        if block.get("fallback_k") not in ks:
+            raise ValueError(f"{where}: host_width fallback_k must be one of k_choices {list(ks)}")
+        sizes = ints("batch_sizes")
+        if sizes[0] < 2:
+            raise ValueError(f"{where}: host_width batch_sizes start at 2")
+        raw_tau = raw.get("tau")
+        if not isinstance(raw_tau, dict):
+            raise ValueError(f"{where}: host_width needs the policy's tau")
+        t0, cum, share, tau = {}, {}, {}, {}
+        for b in sizes:
+            key = str(b)
+            try:
+                t0_b, cum_b, s_b, tau_b = block["t0_ms"][key], block["cum_ms"][key], block["s"][key], raw_tau[key]
+            except (KeyError, TypeError):
+                raise ValueError(f"{where}: host_width needs t0_ms, cum_ms, s and tau at batch size {b}") from None
+            tau[b] = num(f"tau[{b}]", tau_b)
+            t0[b] = num(f"t0_ms[{b}]", t0_b)
+            if not 0.0 < tau[b] <= 1.0 or t0[b] <= 0.0:
+                raise ValueError(f"{where}: host_width tau[{b}] must be in (0, 1] and t0_ms[{b}] positive")
+            if not isinstance(cum_b, list) or len(cum_b) <= ks[-1]:
+                raise ValueError(f"{where}: host_width cum_ms[{b}] needs k = 0 .. {ks[-1]}")
+            row = tuple(num(f"cum_ms[{b}]", v) for v in cum_b)
+            if row[0] != 0.0 or any(x > y for x, y in zip(row, row[1:])):
+                raise ValueError(f"{where}: host_width cum_ms[{b}] must start at 0 and not decrease")
+            cum[b] = row
+            if not isinstance(s_b, dict) or any(str(k) not in s_b for k in ks):
+                raise ValueError(f"{where}: host_width s[{b}] needs a share for every K of k_choices")
+            share[b] = {k: num(f"s[{b}][{k}]", s_b[str(k)]) for k in ks}
+            if any(not 0.0 <= v <= 1.0 for v in share[b].values()):
+                raise ValueError(f"{where}: host_width s[{b}] shares must be in [0, 1]")
+        return HostWidth(frozenset(sizes), lag, block["fallback_k"], ks, t0, cum, share, tau)
+
+    def choose(self, q_rows: list, b: int, cap: int) -> int | None:
+        """The step's K (at most ``cap``) from each request's p_i row, ``fallback_k`` when a row is
+        missing; None when b is not a batch size of the block (the width stays as it is)."""
+        if b not in self.batch_sizes:
+            return None
+        ks = [k for k in self.k_choices if k <= cap] or [self.k_choices[0]]
+        if any(q is None or len(q) < ks[-1] for q in q_rows):
+            return min(self.fallback_k, cap)
+        tau, cum = self.tau[b], self.cum[b]
+        best, best_k = -1.0, ks[0]
+        for K in ks:
+            e_sum, gap = 0.0, 0.0
+            for q in q_rows:
+                prod, d, e = 1.0, 0, 1.0
+                for j in range(K):
+                    prod *= q[j]
+                    if prod >= tau:
+                        d = j + 1
+                pp = 1.0
+                for j in range(d):
+                    pp *= q[j]
+                    e += pp
+                e_sum += e
+                gap += cum[K] - cum[d]
+            t = self.t0[b] + b * cum[K] - (1.0 - self.share[b][K]) * gap
+            score = e_sum / t
+            if score > best + 1e-12:  # ties keep the smaller K
+                best, best_k = score, K
+        return best_k
+
+
 @dataclass
 class DepthPolicy:
     weights: torch.Tensor  # [max_depth, len(FEATURES)] fp32, unlisted features 0
@@ -61,6 +176,7 @@ class DepthPolicy:
     tau: dict[int, float]
     uses_conf: bool
     uses_stats: bool
+    host_width: HostWidth | None = None
 
     @property
     def max_depth(self) -> int:
@@ -100,7 +216,8 @@ class DepthPolicy:
         if not costs:
             raise ValueError(f"{where}: costs must not be empty")
         tau = {int(k): float(v) for k, v in (raw.get("tau") or {}).items()}
-        return DepthPolicy(W, costs, tau, "logit_conf" in feats, bool({"logit_top1", "ent"} & set(feats)))
+        hw = HostWidth.parse(raw, where) if "host_width" in raw else None
+        return DepthPolicy(W, costs, tau, "logit_conf" in feats, bool({"logit_top1", "ent"} & set(feats)), hw)
 
     def cost_row(self, b: int, K: int) -> list[float]:
         """T_b(0..K), interpolated over batch sizes on the k every neighbour lists."""

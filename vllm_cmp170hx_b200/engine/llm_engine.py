@@ -308,10 +308,27 @@ class LLMEngine:
             cap = sch.draft_cap if self.adaptive_k is not None else self.cfg.scheduler.num_speculative_tokens
             decoding = [r for r in sch.running if r.num_computed_tokens == r.num_tokens - 1]
             sch.draft_cap = self.depth_hint.select(decoding, len(sch.running) + len(sch.waiting), cap)
+        self._host_width()
         out = self.scheduler.schedule()
         if not out.reqs:
             return []
         return self._execute_sync(out)
+
+    def _host_width(self) -> None:
+        """The depth policy's host width: a decode-only step of b requests (b in its batch sizes)
+        verifies the K its objective picks from each request's p_i of an earlier round."""
+        spec = self.runner.spec
+        hw = getattr(getattr(spec, "depth", None), "host_width", None) if spec is not None else None
+        if hw is None:
+            return
+        sch = self.scheduler
+        decoding = [r for r in sch.running if r.num_computed_tokens == r.num_tokens - 1]
+        if not decoding or len(decoding) != len(sch.running) or sch.waiting:
+            return  # steps with prefill rows keep the width the load gave
+        cap = (sch.draft_cap if (self.adaptive_k is not None or self.depth_hint is not None)
+               else self.cfg.scheduler.num_speculative_tokens)
+        K = hw.choose([spec.p_round(r.request_id, hw.lag) for r in decoding], len(decoding), cap)
+        sch.draft_cap = cap if K is None else K
 
     def _execute_sync(self, out) -> list[RequestOutput]:
         before = {s.req.request_id: len(s.req.output_token_ids) for s in out.reqs}
@@ -336,6 +353,8 @@ class LLMEngine:
                 self.requests.pop(r.request_id, None)
                 if self.depth_hint is not None:
                     self.depth_hint.forget(r.request_id)
+                if self.runner.spec is not None:
+                    self.runner.spec.p_rounds.pop(r.request_id, None)
         return res
 
 

@@ -122,6 +122,8 @@ class SpecDecoder:
         # draft distributions of sampled requests: rid -> (tensor [k, A, V_local], row a)
         self.q_store: dict[str, tuple[torch.Tensor, int]] = {}
         self.stats = {"proposed": 0, "accepted": 0, "steps": 0}
+        self._last_p = None
+        self.p_rounds: dict = {}  # request -> p_i rows of its latest drafted rounds (host width of the depth policy)
 
     # ------------------------------------------------------------------ verification
     def verify(self, out, logits: torch.Tensor, rows_of: dict[str, list[int]]) -> dict[str, list[int]]:
@@ -286,9 +288,22 @@ class SpecDecoder:
         for qi, a in enumerate(samp):
             self.q_store[areqs[a].request_id] = (qbuf, qi)
 
+    def p_round(self, request_id: str, lag: int):
+        """The p_i row of the request's verify round ``lag`` rounds before the one being scheduled
+        (whose drafts were the latest drafted), or None."""
+        rows = self.p_rounds.get(request_id)
+        return rows[-1 - lag] if rows is not None and len(rows) > lag else None
+
     def _set_drafts(self, areqs, dh, live) -> None:
         """Store each request's drafts: cut to its live depth, or (depth_mode "mask") all k with the live
         depth recorded as the row mask."""
+        if self._last_p is not None:
+            from collections import deque
+
+            keep = self.depth.host_width.lag + 1
+            for a, req in enumerate(areqs):
+                self.p_rounds.setdefault(req.request_id, deque(maxlen=keep)).append(self._last_p[a])
+            self._last_p = None
         mask = self.runner.cfg.scheduler.depth_mode == "mask" and self.depth is not None
         for a, req in enumerate(areqs):
             room = max(0, req.params.max_tokens - len(req.output_token_ids) - 1)
@@ -308,7 +323,10 @@ class SpecDecoder:
         K = min(self.k, self.depth.max_depth)
         st = torch.stack(stats, 1)[:, :K] if stats else None
         feats = draft_features(A, K, st, conf[:, :K] if conf is not None else None, self.runner.device)
-        live = self.depth.live(self.depth.accept_probs(feats), A)
+        p = self.depth.accept_probs(feats)
+        live = self.depth.live(p, A)
+        if self.depth.host_width is not None:
+            self._last_p = p.double().cpu().tolist()  # host copy: live() above read p on the host already
         self.stats["depth_cut"] = self.stats.get("depth_cut", 0) + sum(self.k - v for v in live)
         return live
 
